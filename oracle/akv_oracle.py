@@ -1,0 +1,374 @@
+"""CPU oracle for the AKV warm-tier hot path.  TEST INFRASTRUCTURE ONLY.
+
+This module is a numpy restatement of the reference package ``akv`` (v1.4.0)
+arithmetic for the warm tier.  It exists so that the CUDA path can be checked
+against the reference's algorithm on the same seeded inputs.  Only the test
+suite, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline / reference
+arm may import it; the product path (``akv`` package) never does.
+
+Parity is pinned: every function here is checked against golden vectors that
+``tests/golden/make_golden.py`` produced by calling the reference package
+itself (``tests/test_oracle_golden.py``).
+
+FP16 semantics.  The reference runs its quantiser on FP16 tensors with torch
+CPU elementwise ops.  Each op widens both operands to fp32, computes, and
+rounds the result back to fp16 (round-to-nearest-even).  For + - * / the
+double rounding fp32 -> fp16 is innocuous (24 >= 2*11 + 2), so each op equals
+the correctly rounded fp16 op.  ``_h`` below applies that rounding.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+F16 = np.float16
+F32 = np.float32
+
+
+def _h(x) -> np.ndarray:
+    """Round an fp32 array to fp16 (RNE), like torch's per-op Half result.
+
+    Overflow to +-inf is the expected IEEE result (e.g. 65504 - (-65504))."""
+    with np.errstate(over="ignore", invalid="ignore"):
+        return np.asarray(x, dtype=F32).astype(F16)
+
+
+def _f(x) -> np.ndarray:
+    return np.asarray(x).astype(F32)
+
+
+# ---------------------------------------------------------------------------
+# Bit packing — reference akv/bitpack.py
+# ---------------------------------------------------------------------------
+
+def pack_uint4(codes: np.ndarray) -> np.ndarray:
+    """akv/bitpack.py:13-19 — even index -> high nibble, odd -> low nibble."""
+    c = np.asarray(codes).astype(np.uint8)
+    if c.shape[-1] % 2:
+        c = np.concatenate([c, np.zeros(c.shape[:-1] + (1,), np.uint8)], -1)
+    return (((c[..., 0::2] & 0x0F) << 4) | (c[..., 1::2] & 0x0F)).astype(np.uint8)
+
+
+def unpack_uint4(packed: np.ndarray, orig_dim: int) -> np.ndarray:
+    """akv/bitpack.py:22-30."""
+    p = np.asarray(packed).astype(np.uint8)
+    out = np.empty(p.shape[:-1] + (orig_dim,), np.uint8)
+    out[..., 0::2] = ((p >> 4) & 0x0F)[..., : orig_dim // 2 + orig_dim % 2]
+    out[..., 1::2] = (p & 0x0F)[..., : orig_dim // 2]
+    return out
+
+
+def pack_uint3(codes: np.ndarray) -> np.ndarray:
+    """akv/bitpack.py:35-51 — 8 codes -> 24-bit word c0<<21|..|c7 -> 3 bytes big-endian."""
+    c = np.asarray(codes).astype(np.int64) & 0x07
+    if c.shape[-1] % 8:
+        pad = 8 - c.shape[-1] % 8
+        c = np.concatenate([c, np.zeros(c.shape[:-1] + (pad,), np.int64)], -1)
+    g = c.reshape(c.shape[:-1] + (-1, 8))
+    word = np.zeros(g.shape[:-1], np.int64)
+    for j in range(8):
+        word |= g[..., j] << (21 - 3 * j)
+    out = np.stack([(word >> 16) & 0xFF, (word >> 8) & 0xFF, word & 0xFF], -1)
+    return out.reshape(c.shape[:-1] + (-1,)).astype(np.uint8)
+
+
+def unpack_uint3(packed: np.ndarray, orig_dim: int) -> np.ndarray:
+    """akv/bitpack.py:54-68."""
+    p = np.asarray(packed).astype(np.int64)
+    k = p.shape[-1] // 3
+    p = p.reshape(p.shape[:-1] + (k, 3))
+    word = (p[..., 0] << 16) | (p[..., 1] << 8) | p[..., 2]
+    out = np.stack([(word >> (21 - 3 * j)) & 0x7 for j in range(8)], -1)
+    return out.reshape(out.shape[:-2] + (k * 8,))[..., :orig_dim].astype(np.uint8)
+
+
+def pack_uint2(codes: np.ndarray) -> np.ndarray:
+    """akv/bitpack.py:73-79 — 4 codes per byte, first code in the top bits."""
+    c = np.asarray(codes).astype(np.uint8)
+    if c.shape[-1] % 4:
+        pad = 4 - c.shape[-1] % 4
+        c = np.concatenate([c, np.zeros(c.shape[:-1] + (pad,), np.uint8)], -1)
+    c = c & 0x03
+    return ((c[..., 0::4] << 6) | (c[..., 1::4] << 4) | (c[..., 2::4] << 2) | c[..., 3::4]).astype(np.uint8)
+
+
+def unpack_uint2(packed: np.ndarray, orig_dim: int) -> np.ndarray:
+    """akv/bitpack.py:82-90 (orig_dim must be the padded width's multiple of 4)."""
+    p = np.asarray(packed).astype(np.uint8)
+    out = np.empty(p.shape[:-1] + (orig_dim,), np.uint8)
+    out[..., 0::4] = (p >> 6) & 0x03
+    out[..., 1::4] = (p >> 4) & 0x03
+    out[..., 2::4] = (p >> 2) & 0x03
+    out[..., 3::4] = p & 0x03
+    return out
+
+
+def pack(codes: np.ndarray, bits: int) -> np.ndarray:
+    """akv/bitpack.py:95-103."""
+    if bits == 4:
+        return pack_uint4(codes)
+    if bits == 3:
+        return pack_uint3(codes)
+    if bits == 2:
+        return pack_uint2(codes)
+    return np.asarray(codes)
+
+
+def unpack(packed: np.ndarray, bits: int, orig_dim: int) -> np.ndarray:
+    """akv/bitpack.py:106-114."""
+    if bits == 4:
+        return unpack_uint4(packed, orig_dim)
+    if bits == 3:
+        return unpack_uint3(packed, orig_dim)
+    if bits == 2:
+        return unpack_uint2(packed, orig_dim)
+    return np.asarray(packed)
+
+
+def packed_width(dim: int, bits: int) -> int:
+    """Bytes per row after packing (right-padded to the pack group)."""
+    if bits == 4:
+        return (dim + 1) // 2
+    if bits == 3:
+        return (dim + 7) // 8 * 3
+    if bits == 2:
+        return (dim + 3) // 4
+    return dim
+
+
+# ---------------------------------------------------------------------------
+# Block-affine quantiser — reference akv/affine_quantizer.py
+# ---------------------------------------------------------------------------
+
+def _outlier_select(x16: np.ndarray, fraction: float):
+    """affine_quantizer.py:75-85 (keys) / :143-151 (values).
+
+    Channel score = L2 norm over tokens (fp32) per (head, channel), then the
+    mean over heads; top-n channels, largest first.  torch's CPU ``topk`` does
+    not promise an order for equal scores; this restatement takes the lower
+    channel index first.
+    """
+    D = x16.shape[-1]
+    n = max(1, int(D * fraction))
+    xf = _f(x16)
+    norms = np.sqrt(np.sum(xf * xf, axis=1, dtype=F32)).astype(F32)  # (H, D)
+    score = (np.sum(norms, axis=0, dtype=F32) / F32(norms.shape[0])).astype(F32)
+    idx = np.argsort(-score, kind="stable")[:n]
+    data = x16[..., idx].astype(F16)
+    x16 = x16.copy()
+    x16[..., idx] = F16(0.0)
+    return x16, idx.astype(np.int64), data
+
+
+def _affine_codes(x16: np.ndarray, lo: np.ndarray, hi: np.ndarray, bits: int):
+    """affine_quantizer.py:91-95 / :157-161, op by op in fp16.
+
+    ``clamp(min=1e-8)`` is a no-op on fp16: 1e-8 is below fp16's smallest
+    subnormal, so a zero range keeps scale == 0.  0/0 then gives NaN, which
+    ``.to(uint8)`` turns into 0 on x86; x/0 for x > 0 gives inf -> clamp -> maxval.
+    """
+    maxval = (1 << bits) - 1
+    with np.errstate(over="ignore", invalid="ignore"):
+        scale = _h(_f(hi) - _f(lo))
+    scale = _h(_f(scale) / F32(maxval))
+    zero = lo.astype(F16)
+    diff = _h(_f(x16) - _f(zero))
+    with np.errstate(divide="ignore", invalid="ignore"):
+        ratio = _h(_f(diff) / _f(scale))
+    r = np.rint(_f(ratio))
+    r = np.where(np.isnan(r), F32(0.0), np.clip(r, 0, maxval))
+    return r.astype(np.uint8), scale, zero
+
+
+def quantize_keys(k: np.ndarray, bits: int, outlier_fraction: float = 0.0, packed: bool = True) -> dict:
+    """affine_quantizer.py:63-110 — per-(head, channel) min/max over the tokens of the call.
+
+    k: (H, N, D) fp16.  Returns the reference's dict layout.
+    """
+    k16 = np.asarray(k).astype(F16)
+    out = {}
+    if outlier_fraction > 0:
+        k16, idx, data = _outlier_select(k16, outlier_fraction)
+        out["outlier_idx"] = idx
+        out["outlier_data"] = data
+    lo = k16.min(axis=1, keepdims=True)
+    hi = k16.max(axis=1, keepdims=True)
+    codes, scale, zero = _affine_codes(k16, lo, hi, bits)
+    out.update(scale=scale, zero=zero, orig_dim=codes.shape[-1], bits=bits)
+    out["codes"] = pack(codes, bits) if packed else codes
+    return out
+
+
+def quantize_values(v: np.ndarray, bits: int, outlier_fraction: float = 0.0, packed: bool = True) -> dict:
+    """affine_quantizer.py:131-176 — per-(head, token) min/max over channels."""
+    v16 = np.asarray(v).astype(F16)
+    out = {}
+    if outlier_fraction > 0:
+        v16, idx, data = _outlier_select(v16, outlier_fraction)
+        out["outlier_idx"] = idx
+        out["outlier_data"] = data
+    lo = v16.min(axis=2, keepdims=True)
+    hi = v16.max(axis=2, keepdims=True)
+    codes, scale, zero = _affine_codes(v16, lo, hi, bits)
+    out.update(scale=scale, zero=zero, orig_dim=codes.shape[-1], bits=bits)
+    out["codes"] = pack(codes, bits) if packed else codes
+    return out
+
+
+def _dequant(q: dict) -> np.ndarray:
+    """affine_quantizer.py:112-124 / :178-189 — fp16 multiply, then fp16 add (no FMA)."""
+    codes = q["codes"]
+    if q["bits"] in (2, 3, 4):
+        codes = unpack(codes, q["bits"], q["orig_dim"])
+    c = _f(codes.astype(F16))
+    with np.errstate(invalid="ignore", over="ignore"):  # 0 * inf -> NaN, as in torch
+        out = _h(_h(c * _f(q["scale"])).astype(F32) + _f(q["zero"]))
+    if "outlier_idx" in q:
+        out[..., q["outlier_idx"]] = q["outlier_data"]
+    return out
+
+
+dequantize_keys = _dequant
+dequantize_values = _dequant
+
+
+def measure_packed_bytes(q: dict, bits: int) -> int:
+    """akv/packed_layout.py:501-543 — packed codes + scale + zero bytes.
+
+    Outlier side-store bytes are NOT counted by the reference.
+    """
+    total = int(np.asarray(q["codes"]).nbytes)
+    for key in ("scale", "zero"):
+        if key in q:
+            total += int(np.asarray(q[key]).nbytes)
+    return total
+
+
+def quantize_groups(x: np.ndarray, bits: int, group: int, is_key: bool,
+                    outlier_fraction: float = 0.0) -> list:
+    """Per batch row, per ``group``-token slice: one reference quantiser call each.
+
+    The reference's ``AKVLayer`` quantises one demote event per call and
+    breaks for batch > 1 (``drop_in.py:334``: ``squeeze(0)`` is a no-op), so
+    the oracle for a (B, H, N, D) warm tier is one call per batch row and per
+    token group.  Returns ``out[b][j]`` = the dict of group j of row b.
+    """
+    x = np.asarray(x).astype(F16)
+    B, H, N, D = x.shape
+    fn = quantize_keys if is_key else quantize_values
+    res = []
+    for b in range(B):
+        row = []
+        for j in range(0, N, group):
+            row.append(fn(x[b, :, j:j + group], bits, outlier_fraction))
+        res.append(row)
+    return res
+
+
+def dequantize_groups(groups: list) -> np.ndarray:
+    """Inverse of ``quantize_groups``: (B, H, N, D) fp16."""
+    rows = []
+    for row in groups:
+        rows.append(np.concatenate([_dequant(g) for g in row], axis=1))
+    return np.stack(rows, 0)
+
+
+# ---------------------------------------------------------------------------
+# Attention — reference akv/fused_attention.py:324-366
+# ---------------------------------------------------------------------------
+
+def decode_attention(q: np.ndarray, keys: np.ndarray, values: np.ndarray,
+                     sm_scale: float | None = None, return_lse: bool = False):
+    """softmax(q.K^T * sm_scale).V in fp32 (fused_attention.py:362-366).
+
+    q: (B, Hq, D); keys/values: (B, Hkv, N, D) fp16 (already dequantised warm
+    tokens concatenated with the FP16 hot window — order does not matter for a
+    single decode query).  Query head h reads KV head h // (Hq // Hkv), the
+    HF ``repeat_kv`` mapping.  Returns fp32 (B, Hq, D) (and the natural-log LSE
+    of the scaled logits when asked).
+    """
+    q = _f(q)
+    B, Hq, D = q.shape
+    Hkv = keys.shape[1]
+    g = Hq // Hkv
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    kf = _f(keys)
+    vf = _f(values)
+    out = np.zeros((B, Hq, D), F32)
+    lse = np.zeros((B, Hq), F32)
+    for b in range(B):
+        for h in range(Hq):
+            kv = h // g
+            s = (kf[b, kv] @ q[b, h]).astype(F32) * F32(sm_scale)
+            if s.size == 0:
+                continue
+            m = s.max()
+            p = np.exp(s - m)
+            l = p.sum(dtype=F32)
+            out[b, h] = (p / l) @ vf[b, kv]
+            lse[b, h] = m + np.log(l)
+    return (out, lse) if return_lse else out
+
+
+def int4_group_dequant(packed: np.ndarray, scales: np.ndarray, zeros: np.ndarray,
+                       head_dim: int, group_size: int) -> np.ndarray:
+    """fused_attention.py:293-317 — INT4 (H, N, D/2) per-token per-D-group affine.
+
+    fp32 ``c * s + z`` (two roundings), then one rounding to fp16.
+    """
+    p = np.asarray(packed).astype(np.uint8)
+    H, N, _ = p.shape
+    c = np.empty((H, N, head_dim), F32)
+    c[..., 0::2] = ((p >> 4) & 0x0F).astype(F32)
+    c[..., 1::2] = (p & 0x0F).astype(F32)
+    gi = np.arange(head_dim) // group_size
+    s = _f(scales)[:, :, gi]
+    z = _f(zeros)[:, :, gi]
+    return _h((c * s).astype(F32) + z)
+
+
+# ---------------------------------------------------------------------------
+# Importance update and demote selection
+# ---------------------------------------------------------------------------
+
+def importance_update(attn: np.ndarray, scores: np.ndarray, decay: float) -> np.ndarray:
+    """triton_ops.py:604-650 (CPU branch): scores*decay + sum_M mean_{B,H} attn.
+
+    Two roundings (``mul_`` then ``add_``); the importance vector is truncated
+    or zero-padded to len(scores) (:627-633).
+    """
+    a = _f(attn)
+    B, H, M, N = a.shape
+    avg = (np.sum(a, axis=(0, 1), dtype=F32) / F32(B * H)).astype(F32)
+    imp = np.sum(avg, axis=0, dtype=F32).astype(F32)
+    n = scores.shape[0]
+    if imp.shape[0] > n:
+        imp = imp[:n]
+    elif imp.shape[0] < n:
+        imp = np.concatenate([imp, np.zeros(n - imp.shape[0], F32)])
+    return ((_f(scores) * F32(decay)).astype(F32) + imp).astype(F32)
+
+
+def select_demote(scores: np.ndarray, n_demote: int, hot_budget: int,
+                  protect_initial: int = 4) -> np.ndarray:
+    """drop_in.py:392-413 — bottom-k of scores with protected ends, sorted ascending.
+
+    The first ``protect_initial`` and the last ``min(16, hot_budget // 4)``
+    positions get +inf.  For equal scores this restatement takes the lower
+    index first (torch's CPU topk leaves that order unspecified).
+    """
+    s = _f(scores).copy()
+    n = s.shape[0]
+    protect_recent = min(16, hot_budget // 4)
+    s[:protect_initial] = np.inf
+    s[max(0, n - protect_recent):] = np.inf
+    order = np.argsort(s, kind="stable")[:n_demote]
+    return np.sort(order).astype(np.int64)
+
+
+def recency_decay(scores: np.ndarray, n_new: int, decay: float = 0.3) -> np.ndarray:
+    """drop_in.py:376-390 — old scores * decay, new tokens at 1.0."""
+    s = (_f(scores) * F32(decay)).astype(F32)
+    return np.concatenate([s, np.ones(n_new, F32)])

@@ -1,0 +1,259 @@
+"""Generate golden vectors by running the reference ``akv`` package (CPU).
+
+Run in a container where the reference source is available:
+
+    python tests/golden/make_golden.py /path/to/reference
+
+It imports the reference package from that path, feeds it seeded inputs and
+stores inputs + outputs as ``.npz`` fixtures next to this script.  The
+fixtures pin the numpy oracle (``oracle/akv_oracle.py``) in
+``tests/test_oracle_golden.py``; nothing at test or bench time imports the
+reference itself.
+"""
+from __future__ import annotations
+
+import math
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _import_reference(path: str):
+    sys.path.insert(0, path)
+    import akv  # noqa: F401  (the reference package)
+    from akv import bitpack
+    from akv.affine_quantizer import AffineQuantizer, AffineQuantConfig
+    from akv import fused_attention, triton_ops, packed_layout
+    from akv.drop_in import AKVLayer
+    assert os.path.abspath(akv.__file__).startswith(os.path.abspath(path)), akv.__file__
+    return dict(bitpack=bitpack, AffineQuantizer=AffineQuantizer, AffineQuantConfig=AffineQuantConfig,
+                fused_attention=fused_attention, triton_ops=triton_ops,
+                packed_layout=packed_layout, AKVLayer=AKVLayer)
+
+
+def rope(x, positions, base=10000.0):
+    """Half-split rotary embedding (the recipe of the reference's
+    ``_diag_quant_rope.py``: base 10000, rotate the two halves of D)."""
+    import torch
+    D = x.shape[-1]
+    half = D // 2
+    inv = 1.0 / (base ** (torch.arange(0, half, dtype=torch.float32) / half))
+    ang = positions.float()[:, None] * inv[None, :]
+    cos, sin = ang.cos(), ang.sin()
+    xf = x.float()
+    x1, x2 = xf[..., :half], xf[..., half:]
+    return torch.cat([x1 * cos - x2 * sin, x1 * sin + x2 * cos], -1).to(x.dtype)
+
+
+def make_kv(gen, H, N, D, outlier_ch=(), outlier_scale=12.0, use_rope=False, start=0):
+    import torch
+    x = torch.randn(H, N, D, generator=gen, dtype=torch.float32)
+    for c in outlier_ch:
+        x[..., c] *= outlier_scale
+    x = x.half()
+    if use_rope:
+        x = rope(x, torch.arange(start, start + N))
+    return x
+
+
+def main(ref_path: str):
+    import torch
+    torch.set_num_threads(1)
+    R = _import_reference(ref_path)
+    bp = R["bitpack"]
+
+    # ---------------- bitpack ----------------
+    out = {}
+    g = torch.Generator().manual_seed(1)
+    for bits in (2, 3, 4):
+        for D in (8, 32, 64, 128, 256):
+            codes = torch.randint(0, 1 << bits, (2, 5, D), generator=g, dtype=torch.uint8)
+            packed = bp.pack(codes, bits)
+            out[f"b{bits}_d{D}_codes"] = codes.numpy()
+            out[f"b{bits}_d{D}_packed"] = packed.numpy()
+            out[f"b{bits}_d{D}_unpacked"] = bp.unpack(packed, bits, D).numpy()
+    # odd widths: the reference right-pads with zeros
+    for bits, D in ((4, 7), (3, 13), (2, 10)):
+        codes = torch.randint(0, 1 << bits, (3, D), generator=g, dtype=torch.uint8)
+        out[f"b{bits}_d{D}_codes"] = codes.numpy()
+        out[f"b{bits}_d{D}_packed"] = bp.pack(codes, bits).numpy()
+    np.savez_compressed(os.path.join(HERE, "bitpack.npz"), **out)
+
+    # ---------------- affine quantiser ----------------
+    AQ, AQC = R["AffineQuantizer"], R["AffineQuantConfig"]
+    cases = []
+    g = torch.Generator().manual_seed(2)
+    # full bits x outlier-fraction matrix on small shapes, a few combos on larger ones
+    combos = [(b, f) for b in (2, 3, 4) for f in (0.0, 0.01, 0.05)]
+    shapes = [((2, 32, 128), combos), ((1, 1, 128), combos), ((2, 7, 64), combos),
+              ((4, 32, 32), combos), ((3, 5, 16), combos),
+              ((8, 32, 128), [(3, 0.01), (4, 0.0)]), ((2, 64, 128), [(2, 0.05)])]
+    for (H, N, D), cmb in shapes:
+        for bits, frac in cmb:
+            ch = [int(torch.randint(0, D, (1,), generator=g))]
+            k = make_kv(g, H, N, D, outlier_ch=ch, use_rope=(D >= 64))
+            v = make_kv(g, H, N, D, outlier_ch=[int(torch.randint(0, D, (1,), generator=g))])
+            cases.append((f"H{H}_N{N}_D{D}_b{bits}_f{frac}", k, v, bits, bits, frac))
+    # asymmetric K/V bits (k4v2, k4v3)
+    for kb, vb in ((4, 2), (4, 3)):
+        k = make_kv(g, 8, 32, 128, outlier_ch=[5], use_rope=True)
+        v = make_kv(g, 8, 32, 128)
+        cases.append((f"asym_k{kb}v{vb}", k, v, kb, vb, 0.01))
+    # edge cases: constant channel / constant token, zeros, large, subnormal, ties
+    k = make_kv(g, 2, 32, 64)
+    k[:, :, 3] = 1.5            # constant channel -> scale 0 for K
+    k[0, :, 10] = 0.0           # zero channel
+    k[1, 4, :] = 65504.0        # fp16 max in one token
+    k[1, 5, :] = -65504.0
+    v = make_kv(g, 2, 32, 64)
+    v[0, 3, :] = 0.25           # constant token -> scale 0 for V
+    v[1, 7, :] = 6e-8           # subnormal token
+    v[1, 8, :2] = torch.tensor([6e-8, 0.0], dtype=torch.float16)
+    for bits in (2, 3, 4):
+        cases.append((f"edge_b{bits}", k.clone(), v.clone(), bits, bits, 0.0))
+        cases.append((f"edge_out_b{bits}", k.clone(), v.clone(), bits, bits, 0.05))
+    # tiny range -> scale underflows to zero while (x - zero) > 0
+    k = torch.zeros(1, 4, 16, dtype=torch.float16)
+    k[0, 1, :] = 6e-8
+    k[0, 2, :] = 1.2e-7
+    v = k.transpose(1, 2).contiguous().clone()[:, :4, :4].repeat(1, 1, 4)
+    for bits in (2, 3, 4):
+        cases.append((f"tiny_b{bits}", k.clone(), v.clone(), bits, bits, 0.0))
+
+    out = {}
+    names = []
+    for name, k, v, kb, vb, frac in cases:
+        qz = AQ(AQC(key_bits=kb, value_bits=vb, outlier_fraction=frac))
+        qk = qz.quantize_keys(k.clone())
+        qv = qz.quantize_values(v.clone())
+        dk = qz.dequantize_keys(qk)
+        dv = qz.dequantize_values(qv)
+        pl = R["packed_layout"]
+        names.append(name)
+        out[f"{name}/k"] = k.numpy()
+        out[f"{name}/v"] = v.numpy()
+        out[f"{name}/meta"] = np.array([kb, vb, frac], np.float64)
+        for tag, q, d in (("qk", qk, dk), ("qv", qv, dv)):
+            for key in ("codes", "scale", "zero"):
+                out[f"{name}/{tag}_{key}"] = q[key].numpy()
+            if "outlier_idx" in q:
+                out[f"{name}/{tag}_outlier_idx"] = q["outlier_idx"].numpy()
+                out[f"{name}/{tag}_outlier_data"] = q["outlier_data"].numpy()
+            out[f"{name}/{tag}_deq"] = d.numpy()
+            out[f"{name}/{tag}_bytes"] = np.array(
+                pl.measure_packed_bytes(q, kb if tag == "qk" else vb), np.int64)
+    out["names"] = np.array(names)
+    np.savez_compressed(os.path.join(HERE, "affine.npz"), **out)
+
+    # ---------------- config-1 slice: 32-token groups ----------------
+    # BASELINE config 1 shapes (B1, 2 KV heads, D128, 3-bit), first 8 groups.
+    g = torch.Generator().manual_seed(0)
+    H, N, D = 2, 256, 128
+    kout = list(range(0, D, 100))  # one planted outlier channel at D=128
+    k = make_kv(g, H, N, D, outlier_ch=kout, use_rope=True)
+    v = make_kv(g, H, N, D)
+    qz = AQ(AQC(key_bits=3, value_bits=3))
+    out = {"k": k.numpy(), "v": v.numpy()}
+    for j in range(N // 32):
+        qk = qz.quantize_keys(k[:, j * 32:(j + 1) * 32].clone())
+        qv = qz.quantize_values(v[:, j * 32:(j + 1) * 32].clone())
+        for key in ("codes", "scale", "zero"):
+            out[f"g{j}/qk_{key}"] = qk[key].numpy()
+            out[f"g{j}/qv_{key}"] = qv[key].numpy()
+    np.savez_compressed(os.path.join(HERE, "config1_groups.npz"), **out)
+
+    # ---------------- attention ----------------
+    fa = R["fused_attention"]
+    out = {}
+    g = torch.Generator().manual_seed(3)
+    # (a) plain fp32 attention over hot FP16 (MHA, the reference's
+    #     mixed_precision_decode_attention with no warm tier)
+    for (B, H, N, D) in ((1, 4, 64, 64), (2, 2, 100, 128)):
+        q = torch.randn(B, H, 1, D, generator=g).half()
+        kk = torch.randn(B, H, N, D, generator=g).half()
+        vv = torch.randn(B, H, N, D, generator=g).half()
+        o = fa.mixed_precision_decode_attention(q, kk, vv)
+        tag = f"hot_B{B}_H{H}_N{N}_D{D}"
+        out[f"{tag}/q"], out[f"{tag}/k"], out[f"{tag}/v"] = q.numpy(), kk.numpy(), vv.numpy()
+        out[f"{tag}/out"] = o.numpy()
+    # (b) mixed hot + INT4 per-token-group warm (reference layout of
+    #     fused_attention.py:324-366), group_size 32 and 128
+    for gs in (32, 128):
+        B, H, Nh, Nw, D = 2, 4, 16, 48, 64
+        q = torch.randn(B, H, 1, D, generator=g).half()
+        hk = torch.randn(B, H, Nh, D, generator=g).half()
+        hv = torch.randn(B, H, Nh, D, generator=g).half()
+        G = D // gs if D >= gs else 1
+        wkp = torch.randint(0, 256, (H, Nw, D // 2), generator=g, dtype=torch.uint8)
+        wvp = torch.randint(0, 256, (H, Nw, D // 2), generator=g, dtype=torch.uint8)
+        wks = (torch.rand(H, Nw, G, generator=g) * 0.3 + 0.01).half()
+        wkz = (torch.randn(H, Nw, G, generator=g)).half()
+        wvs = (torch.rand(H, Nw, G, generator=g) * 0.3 + 0.01).half()
+        wvz = (torch.randn(H, Nw, G, generator=g)).half()
+        o = fa.mixed_precision_decode_attention(q, hk, hv, wkp, wks, wkz, wvp, wvs, wvz, group_size=gs)
+        o2 = fa.fused_int4_decode_attention(q, wkp, wks, wkz, wvp, wvs, wvz, group_size=gs)
+        o3 = fa.fused_int4_decode_attention(q, wkp, wks, wkz, wvp, wvs, wvz, group_size=gs,
+                                            memory_limit_mb=0.0)  # tiled online-softmax branch
+        tag = f"int4_gs{gs}"
+        for nm, t in (("q", q), ("hk", hk), ("hv", hv), ("wkp", wkp), ("wvp", wvp), ("wks", wks),
+                      ("wkz", wkz), ("wvs", wvs), ("wvz", wvz), ("mixed", o), ("int4", o2), ("int4_tiled", o3)):
+            out[f"{tag}/{nm}"] = t.numpy()
+        out[f"{tag}/deq_k"] = fa._dequant_int4_tile(wkp, wks, wkz, D, gs).numpy()
+    # (c) affine warm (AffineQuantizer) + hot, GQA, evaluated the way the
+    #     reference HF path does: dequantise, concatenate, fp32 attention
+    B, Hq, Hkv, Nh, Nw, D = 1, 12, 2, 64, 96, 128
+    q = torch.randn(B, Hq, 1, D, generator=g).half()
+    hk = make_kv(g, Hkv, Nh, D).unsqueeze(0)
+    hv = make_kv(g, Hkv, Nh, D).unsqueeze(0)
+    wk = make_kv(g, Hkv, Nw, D, outlier_ch=[7], use_rope=True).unsqueeze(0)
+    wv = make_kv(g, Hkv, Nw, D).unsqueeze(0)
+    qz = AQ(AQC(key_bits=3, value_bits=3))
+    dk = torch.cat([qz.dequantize_keys(qz.quantize_keys(wk[0, :, j:j + 32].clone()))
+                    for j in range(0, Nw, 32)], 1).unsqueeze(0)
+    dv = torch.cat([qz.dequantize_values(qz.quantize_values(wv[0, :, j:j + 32].clone()))
+                    for j in range(0, Nw, 32)], 1).unsqueeze(0)
+    keys = torch.cat([dk, hk], 2).repeat_interleave(Hq // Hkv, 1)
+    vals = torch.cat([dv, hv], 2).repeat_interleave(Hq // Hkv, 1)
+    o = fa.mixed_precision_decode_attention(q, keys, vals)
+    for nm, t in (("q", q), ("hk", hk), ("hv", hv), ("wk", wk), ("wv", wv), ("out", o)):
+        out[f"affine_gqa/{nm}"] = t.numpy()
+    np.savez_compressed(os.path.join(HERE, "attention.npz"), **out)
+
+    # ---------------- importance update + demote selection ----------------
+    to = R["triton_ops"]
+    out = {}
+    g = torch.Generator().manual_seed(4)
+    for (B, H, M, N, decay) in ((1, 4, 1, 64, 0.95), (2, 8, 3, 257, 0.9), (8, 8, 1, 512, 0.9)):
+        attn = torch.rand(B, H, M, N, generator=g)
+        attn = attn / attn.sum(-1, keepdim=True)
+        scores = torch.rand(N, generator=g)
+        s_in = scores.clone()
+        s_out = to.fused_importance_update(attn, scores, decay=decay)
+        tag = f"imp_B{B}_H{H}_M{M}_N{N}"
+        out[f"{tag}/attn"], out[f"{tag}/scores_in"] = attn.numpy(), s_in.numpy()
+        out[f"{tag}/scores_out"] = s_out.numpy()
+        out[f"{tag}/decay"] = np.array(decay)
+    # zero attention: pure decay (tests/test_triton_ops.py:169-174 of the reference)
+    s = torch.ones(32)
+    out["imp_zero/scores_out"] = to.fused_importance_update(torch.zeros(1, 1, 1, 32), s, decay=0.5).numpy()
+
+    AKVLayer = R["AKVLayer"]
+    for (hot_len, budget, n_dem, seed) in ((600, 512, 88, 5), (160, 128, 32, 6), (1024, 256, 768, 7), (64, 16, 40, 8)):
+        gg = torch.Generator().manual_seed(seed)
+        scores = torch.randperm(hot_len * 4, generator=gg)[:hot_len].float() / (hot_len * 4)  # tie-free
+        layer = AKVLayer(hot_budget=budget)
+        layer._importance = scores.clone()
+        idx = layer._select_demote_indices(n_dem, hot_len)
+        tag = f"sel_n{hot_len}_b{budget}_k{n_dem}"
+        out[f"{tag}/scores"] = scores.numpy()
+        out[f"{tag}/idx"] = idx.numpy()
+        out[f"{tag}/meta"] = np.array([hot_len, budget, n_dem])
+    np.savez_compressed(os.path.join(HERE, "importance.npz"), **out)
+    print("golden fixtures written to", HERE)
+
+
+if __name__ == "__main__":
+    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
