@@ -1,0 +1,126 @@
+"""ctypes binding of libakv_sm100.so (the C ABI in include/akv_b200.h).
+
+The library is built in-tree by ``adaptive-kv-memory_b200/build.py`` into
+``akv/_lib/libakv_sm100.so``.  There is no fallback: if the library is
+missing, every warm-tier op raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import POINTER, c_float, c_int, c_int32, c_int64, c_size_t, c_void_p, c_char_p
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "libakv_sm100.so")
+
+AKV_OK = 0
+BLOCK_TOKENS = 32
+ERRORS = {
+    -1: "AKV_ERR_SHAPE", -2: "AKV_ERR_BITS", -3: "AKV_ERR_ALIGN", -4: "AKV_ERR_UNSUPPORTED",
+    -5: "AKV_ERR_LAUNCH", -6: "AKV_ERR_TIMEOUT", -7: "AKV_ERR_NULL", -8: "AKV_ERR_WORKSPACE",
+}
+
+
+class View(ctypes.Structure):
+    """akv_view: addr(b, h, blk, slot) = ptr + b*sb + h*sh + blk*sblk + slot*sslot (bytes)."""
+    _fields_ = [("ptr", c_void_p), ("sb", c_int64), ("sh", c_int64), ("sblk", c_int64), ("sslot", c_int64)]
+
+
+class QDest(ctypes.Structure):
+    """akv_qdest: where one quantiser call writes (or one dequantiser call reads)."""
+    _fields_ = [(n, View) for n in ("codes", "scale", "zero", "out_data", "out_idx", "mask")]
+
+
+class WarmLayout(ctypes.Structure):
+    """akv_warm_layout: byte offsets inside one 32-token warm block record."""
+    _fields_ = [(n, c_int32) for n in ("head_dim", "key_bits", "value_bits", "n_outlier", "kc", "vc", "ks",
+                                        "kz", "vs", "vz", "ko", "vo", "ki", "vi", "mask", "bytes")]
+
+    def as_dict(self) -> dict:
+        return {n: getattr(self, n) for n, _ in self._fields_}
+
+
+# name -> (restype, argtypes); must list every function declared in akv_b200.h
+SIGNATURES = {
+    "akv_strerror": (c_char_p, [c_int]),
+    "akv_abi_version": (c_int, []),
+    "akv_warm_layout_init": (c_int, [c_int, c_int, c_int, c_int, POINTER(WarmLayout)]),
+    "akv_pack_codes": (c_int, [c_void_p, c_int64, c_int, c_int, c_void_p, c_void_p]),
+    "akv_unpack_codes": (c_int, [c_void_p, c_int64, c_int, c_int, c_void_p, c_void_p]),
+    "akv_quantize": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64,
+                             c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
+                             POINTER(QDest), c_void_p, c_void_p]),
+    "akv_dequantize": (c_int, [POINTER(QDest), c_void_p, c_int64, c_int, c_int, c_int, c_int, c_int, c_int,
+                               c_int, c_void_p, c_int64, c_int64, c_int64, c_void_p]),
+    "akv_decode_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int, c_int]),
+    "akv_mixed_decode": (c_int, [c_void_p, c_int64, c_int64,
+                                 c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int, c_void_p,
+                                 c_void_p, c_int64, c_int64, POINTER(WarmLayout), c_int, c_void_p,
+                                 c_int, c_int, c_int, c_int, c_float,
+                                 c_void_p, c_int64, c_int64, c_void_p,
+                                 c_void_p, c_size_t, c_void_p, c_void_p]),
+    "akv_lse_combine": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_int64, c_void_p, c_void_p]),
+    "akv_importance_update": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int, c_float, c_void_p]),
+    "akv_select_workspace_bytes": (c_size_t, [c_int]),
+    "akv_select_bottomk": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "akv_gather_rows": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int, c_int, c_int, c_int64,
+                                c_void_p, c_int64, c_int64, c_int64, c_void_p]),
+    "akv_cold_copy": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int64, c_int, c_void_p, c_void_p]),
+}
+
+_lib = None
+
+
+def lib_path() -> str:
+    return LIB_PATH
+
+
+def load():
+    """Load the library (once) and bind every ABI symbol.  Raises if absent."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(
+            f"akv: native library not found at {LIB_PATH}; build it with "
+            "`python adaptive-kv-memory_b200/build.py` (no CPU fallback exists)")
+    import torch  # noqa: F401  (makes torch's libcudart visible to the loader first)
+    lib = ctypes.CDLL(LIB_PATH)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def strerror(rc: int) -> str:
+    return load().akv_strerror(rc).decode()
+
+
+def check(rc: int, what: str) -> None:
+    if rc != AKV_OK:
+        raise RuntimeError(f"{what} failed: {ERRORS.get(rc, rc)} ({strerror(rc)})")
+
+
+def ptr(t) -> int | None:
+    """Device/host address of a tensor (None for None)."""
+    return None if t is None else t.data_ptr()
+
+
+def stream_of(t) -> int:
+    """The current torch stream handle for the tensor's device (as an int)."""
+    import torch
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def require_cuda(*tensors) -> None:
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("akv: warm-tier ops run on CUDA tensors only (no CPU fallback)")
+
+
+def warm_layout(head_dim: int, key_bits: int, value_bits: int, n_outlier: int) -> WarmLayout:
+    L = WarmLayout()
+    check(load().akv_warm_layout_init(head_dim, key_bits, value_bits, n_outlier, ctypes.byref(L)),
+          "akv_warm_layout_init")
+    return L

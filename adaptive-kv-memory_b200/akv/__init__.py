@@ -1,0 +1,20 @@
+"""akv — B200-native warm tier of Adaptive KV Memory.
+
+Block-affine quantise + bit-pack, packed warm block records, mixed-tier
+(FP16 hot + packed warm) split-K decode attention, importance update and
+demote/promote, behind the reference package's Python API.  Every op runs in
+the sm_100a library ``akv/_lib/libakv_sm100.so``; there is no CPU fallback.
+"""
+from . import _C
+from .affine_quantizer import AffineQuantConfig, AffineQuantizer
+from .bitpack import pack, unpack, packed_bytes
+from .fused_attention import mixed_precision_decode_attention, mixed_tier_decode_attention
+from .packed_layout import WarmArena, measure_packed_bytes
+
+__version__ = "0.1.0"
+
+__all__ = [
+    "AffineQuantConfig", "AffineQuantizer", "WarmArena", "measure_packed_bytes",
+    "mixed_tier_decode_attention", "mixed_precision_decode_attention",
+    "pack", "unpack", "packed_bytes",
+]

@@ -1,0 +1,162 @@
+"""Packed warm-tier storage and byte accounting.
+
+``measure_packed_bytes`` keeps the reference's accounting
+(akv/packed_layout.py:501-543): packed codes + scale + zero bytes, outlier
+side-store not counted.
+
+``WarmArena`` is the packed warm tier of one layer.  Tokens live in 32-token
+block records (layout in include/akv_b200.h, ``akv_warm_layout``), one run of
+records per (batch row, KV head), preallocated for ``max_blocks`` blocks.  A
+record carries exactly what one reference quantiser call returns for those
+tokens, so the arena is the source of truth for attention (read in place by
+``akv_mixed_decode``), promotion (``akv_dequantize``) and the cold tier
+(byte-for-byte copies of records).
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _C
+from .affine_quantizer import n_outliers
+from .bitpack import packed_width
+
+BLOCK = _C.BLOCK_TOKENS
+
+
+def measure_packed_bytes(qdata: dict, bits: int) -> int:
+    """Bytes a quantiser call's output occupies (reference packed_layout.py:501-543)."""
+    if "codes" not in qdata:
+        return 0
+    codes = qdata["codes"]
+    if "bits" in qdata:
+        total = codes.element_size() * codes.numel()
+    else:
+        D = codes.shape[-1]
+        rows = codes.numel() // D if D else 0
+        total = rows * packed_width(D, bits) if bits in (2, 3, 4) else codes.element_size() * codes.numel()
+    for key in ("group_mean", "group_std", "scale", "zero"):
+        t = qdata.get(key)
+        if isinstance(t, torch.Tensor):
+            total += t.element_size() * t.numel()
+    return int(total)
+
+
+class WarmArena:
+    """Packed warm tier: (B, H, max_blocks) block records in one uint8 buffer."""
+
+    def __init__(self, batch: int, heads: int, head_dim: int, key_bits: int, value_bits: int,
+                 outlier_fraction: float = 0.0, max_blocks: int = 64, device="cuda"):
+        self.B, self.H, self.D = batch, heads, head_dim
+        self.key_bits, self.value_bits = key_bits, value_bits
+        self.n_out = n_outliers(head_dim, outlier_fraction)
+        self.layout = _C.warm_layout(head_dim, key_bits, value_bits, self.n_out)
+        self.rec = self.layout.bytes
+        self.max_blocks = max_blocks
+        self.buf = torch.zeros(batch, heads, max_blocks, self.rec, dtype=torch.uint8, device=device)
+        self.n_blocks = 0
+
+    # -------------------------------------------------------------- views
+    @property
+    def device(self):
+        return self.buf.device
+
+    def _base(self, blk0: int) -> int:
+        return self.buf.data_ptr() + blk0 * self.rec
+
+    def dest(self, is_key: bool, blk0: int = 0) -> _C.QDest:
+        """QDest addressing K (or V) fields of the records starting at block blk0."""
+        L, rec = self.layout, self.rec
+        sb, sh = self.H * self.max_blocks * rec, self.max_blocks * rec
+        base = self._base(blk0)
+        d = _C.QDest()
+        n = self.n_out
+        if is_key:
+            d.codes = _C.View(base + L.kc, sb, sh, rec, packed_width(self.D, self.key_bits))
+            d.scale = _C.View(base + L.ks, sb, sh, rec, 0)
+            d.zero = _C.View(base + L.kz, sb, sh, rec, 0)
+            if n:
+                d.out_data = _C.View(base + L.ko, sb, sh, rec, 2 * n)
+                d.out_idx = _C.View(base + L.ki, sb, sh, rec, 0)
+        else:
+            d.codes = _C.View(base + L.vc, sb, sh, rec, packed_width(self.D, self.value_bits))
+            d.scale = _C.View(base + L.vs, sb, sh, rec, 2)
+            d.zero = _C.View(base + L.vz, sb, sh, rec, 2)
+            if n:
+                d.out_data = _C.View(base + L.vo, sb, sh, rec, 2 * n)
+                d.out_idx = _C.View(base + L.vi, sb, sh, rec, 0)
+        d.mask = _C.View(base + L.mask, sb, sh, rec, 0)
+        return d
+
+    # -------------------------------------------------------------- writes
+    def append(self, k: torch.Tensor, v: torch.Tensor, group: int = BLOCK, tok_idx: torch.Tensor | None = None,
+               status: torch.Tensor | None = None) -> int:
+        """Quantise (B, H, N, D) fp16 K/V (optionally gathered by ``tok_idx``) into new blocks.
+
+        ``group`` tokens share one K scale (32 = one block; N = one reference
+        call over the whole event).  Returns the first block index written.
+        """
+        _C.require_cuda(k, v)
+        B, H, N, D = (k.shape if tok_idx is None else (k.shape[0], k.shape[1], tok_idx.shape[-1], k.shape[3]))
+        if (B, H, D) != (self.B, self.H, self.D):
+            raise ValueError("K/V shape does not match the arena")
+        nblk = (N + BLOCK - 1) // BLOCK
+        if self.n_blocks + nblk > self.max_blocks:
+            raise RuntimeError(f"warm arena full ({self.n_blocks}+{nblk} > {self.max_blocks} blocks)")
+        blk0 = self.n_blocks
+        lib = _C.load()
+        st = _C.stream_of(k)
+        ti = None if tok_idx is None else tok_idx.contiguous()
+        tsb = 0 if ti is None or ti.dim() == 1 else ti.stride(0)
+        sp = None if status is None else status.data_ptr()
+        for x, is_key, bits in ((k, True, self.key_bits), (v, False, self.value_bits)):
+            if x.stride(-1) != 1:
+                x = x.contiguous()
+            dest = self.dest(is_key, blk0)
+            rc = lib.akv_quantize(x.data_ptr(), x.stride(0), x.stride(1), x.stride(2),
+                                  None if ti is None else ti.data_ptr(), tsb,
+                                  B, H, N, D, bits, int(is_key), min(group, N), self.n_out,
+                                  ctypes.byref(dest), sp, st)
+            _C.check(rc, "akv_quantize")
+        self.n_blocks += nblk
+        return blk0
+
+    def dequantize(self, tok_idx: torch.Tensor | None = None, n_tokens: int | None = None) -> tuple:
+        """FP16 (B, H, N, D) K and V of warm token slots (``tok_idx`` = slot = blk*32 + s)."""
+        lib = _C.load()
+        N = tok_idx.shape[-1] if tok_idx is not None else (n_tokens if n_tokens is not None
+                                                            else self.n_blocks * BLOCK)
+        outs = []
+        for is_key, bits in ((True, self.key_bits), (False, self.value_bits)):
+            out = torch.empty(self.B, self.H, N, self.D, dtype=torch.float16, device=self.device)
+            src = self.dest(is_key, 0)
+            rc = lib.akv_dequantize(ctypes.byref(src), None if tok_idx is None else tok_idx.data_ptr(),
+                                    0 if tok_idx is None or tok_idx.dim() == 1 else tok_idx.stride(0),
+                                    self.B, self.H, N, self.D, bits, int(is_key), self.n_out,
+                                    out.data_ptr(), out.stride(0), out.stride(1), out.stride(2),
+                                    _C.stream_of(self.buf))
+            _C.check(rc, "akv_dequantize")
+            outs.append(out)
+        return tuple(outs)
+
+    def masks(self) -> torch.Tensor:
+        """(B, H, n_blocks) int64 valid-slot masks (host-side bookkeeping / tests)."""
+        L = self.layout
+        m = self.buf[:, :, : self.n_blocks, L.mask:L.mask + 4].contiguous().view(torch.int32)
+        return m[..., 0].to(torch.int64) & 0xFFFFFFFF
+
+    def clear_slots(self, blk: torch.Tensor, slot_mask: torch.Tensor) -> None:
+        """Drop tokens from the warm tier by clearing their mask bits (promotion)."""
+        L = self.layout
+        m = self.buf[:, :, :, L.mask:L.mask + 4].view(torch.int32)[..., 0]
+        m[:, :, blk] &= ~slot_mask.to(torch.int32)
+
+    def packed_bytes(self) -> int:
+        """Bytes a reference quantiser would report for the stored blocks (codes+scale+zero)."""
+        D, H, B = self.D, self.H, self.B
+        per_tok = packed_width(D, self.key_bits) + packed_width(D, self.value_bits) + 4
+        return B * H * (self.n_blocks * BLOCK * per_tok + self.n_blocks * 4 * D)
+
+    def resident_bytes(self) -> int:
+        return self.buf.numel()

@@ -1,0 +1,100 @@
+"""Tier management on the GPU: importance update, demote selection, row
+gather/compaction and cold-tier (pinned host) copies.
+
+  fused_importance_update   reference akv/triton_ops.py:604-650
+  select_demote_indices     reference akv/drop_in.py:392-413
+  select_bottomk            reference akv/vmm.py:221-242 (bottom-k, protected ends)
+  gather_rows               reference akv/drop_in.py:684-685, :739-751 (gather / keep-mask)
+  cold_copy_blocks /        reference akv/async_migration.py:303-349, with pinned host
+  cold_restore_blocks       memory and a side stream (the reference declares
+                            pin_memory but never uses it, :102)
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _C
+
+
+def fused_importance_update(attention_weights: torch.Tensor, scores: torch.Tensor,
+                            decay: float = 0.95) -> torch.Tensor:
+    """scores = scores*decay + sum_M mean_{B,H} attn, in place (two roundings, no FMA)."""
+    _C.require_cuda(attention_weights, scores)
+    a = attention_weights
+    if a.dtype != torch.float32:
+        a = a.float()
+    a = a.contiguous()
+    if scores.dtype != torch.float32 or not scores.is_contiguous():
+        raise TypeError("scores must be a contiguous fp32 tensor (updated in place)")
+    B, H, M, Na = a.shape
+    _C.check(_C.load().akv_importance_update(a.data_ptr(), B, H, M, Na, scores.data_ptr(), scores.shape[0],
+                                             float(decay), _C.stream_of(scores)), "akv_importance_update")
+    return scores
+
+
+def select_bottomk(scores: torch.Tensor, k: int, protect_first: int = 4, protect_last: int = 16) -> torch.Tensor:
+    """Ascending int64 indices of the k lowest scores, protected ends excluded; ties lowest index first."""
+    _C.require_cuda(scores)
+    s = scores.float().contiguous()
+    n = s.shape[0]
+    out = torch.empty(k, dtype=torch.int64, device=s.device)
+    if k == 0:
+        return out
+    _C.check(_C.load().akv_select_bottomk(s.data_ptr(), n, k, protect_first, protect_last, out.data_ptr(),
+                                          None, 0, _C.stream_of(s)), "akv_select_bottomk")
+    return out
+
+
+def select_demote_indices(scores: torch.Tensor, n_demote: int, hot_budget: int,
+                          protect_initial: int = 4) -> torch.Tensor:
+    """AKVLayer demote choice: first 4 and last min(16, budget//4) positions are never demoted."""
+    return select_bottomk(scores, n_demote, protect_initial, min(16, hot_budget // 4))
+
+
+def gather_rows(x: torch.Tensor, idx: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """out[b, h, i] = x[b, h, idx[i]] for (B, H, N, D) tensors (rows of D elements)."""
+    _C.require_cuda(x, idx)
+    B, H, N, D = x.shape
+    n = idx.shape[0]
+    if out is None:
+        out = torch.empty(B, H, n, D, dtype=x.dtype, device=x.device)
+    es = x.element_size()
+    if x.stride(-1) != 1 or out.stride(-1) != 1:
+        raise ValueError("rows must be contiguous")
+    i64 = idx.to(torch.int64).contiguous()
+    _C.check(_C.load().akv_gather_rows(x.data_ptr(), x.stride(0) * es, x.stride(1) * es, x.stride(2) * es,
+                                       i64.data_ptr(), n, B, H, D * es,
+                                       out.data_ptr(), out.stride(0) * es, out.stride(1) * es, out.stride(2) * es,
+                                       _C.stream_of(x)), "akv_gather_rows")
+    return out
+
+
+def cold_copy_blocks(arena_buf: torch.Tensor, blk0: int, nblk: int, host: torch.Tensor,
+                     stream: torch.cuda.Stream | None = None) -> torch.cuda.Event:
+    """Copy warm records [blk0, blk0+nblk) of every (b, h) to a pinned host buffer (B, H, nblk, rec)."""
+    B, H, maxb, rec = arena_buf.shape
+    if not host.is_pinned():
+        raise ValueError("cold tier buffers must be pinned host memory")
+    st = stream or torch.cuda.current_stream(arena_buf.device)
+    st.wait_stream(torch.cuda.current_stream(arena_buf.device))
+    src = arena_buf.data_ptr() + blk0 * rec
+    _C.check(_C.load().akv_cold_copy(host.data_ptr(), nblk * rec, src, maxb * rec, nblk * rec, B * H, 0,
+                                     st.cuda_stream, None), "akv_cold_copy")
+    ev = torch.cuda.Event()
+    ev.record(st)
+    return ev
+
+
+def cold_restore_blocks(host: torch.Tensor, arena_buf: torch.Tensor, blk0: int,
+                        stream: torch.cuda.Stream | None = None) -> torch.cuda.Event:
+    """Copy pinned host records (B, H, nblk, rec) back into arena blocks [blk0, blk0+nblk)."""
+    B, H, maxb, rec = arena_buf.shape
+    nblk = host.shape[2]
+    st = stream or torch.cuda.current_stream(arena_buf.device)
+    st.wait_stream(torch.cuda.current_stream(arena_buf.device))
+    dst = arena_buf.data_ptr() + blk0 * rec
+    _C.check(_C.load().akv_cold_copy(dst, maxb * rec, host.data_ptr(), nblk * rec, nblk * rec, B * H, 1,
+                                     st.cuda_stream, None), "akv_cold_copy")
+    ev = torch.cuda.Event()
+    ev.record(st)
+    return ev

@@ -1,0 +1,73 @@
+"""Build libakv_sm100.so (sm_100a) in-tree with nvcc.
+
+    python adaptive-kv-memory_b200/build.py [--verbose]
+
+Sources: csrc/*.cu; public header: include/akv_b200.h at the repo root.
+Output:  akv/_lib/libakv_sm100.so next to the Python package, so the built
+library travels with the source tree.  No --use_fast_math: the quantiser
+relies on IEEE-rounded division and fp16 conversions.
+"""
+from __future__ import annotations
+
+import os
+import shutil
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+CSRC = os.path.join(HERE, "csrc")
+INCLUDE = os.path.join(ROOT, "include")
+OUT_DIR = os.path.join(HERE, "akv", "_lib")
+LIB = os.path.join(OUT_DIR, "libakv_sm100.so")
+SOURCES = ["quant_pack.cu", "decode_attn.cu", "tiering.cu"]
+
+
+def nvcc() -> str:
+    for cand in (shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if cand and os.path.exists(cand):
+            return cand
+    raise RuntimeError("nvcc not found")
+
+
+def flags(verbose: bool = False) -> list:
+    f = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
+         "-Xcompiler", "-fPIC", "-I", INCLUDE, "-I", CSRC, "--expt-relaxed-constexpr"]
+    if verbose:
+        f += ["-Xptxas", "-v"]
+    return f
+
+
+def build(verbose: bool = False, force: bool = False) -> str:
+    os.makedirs(OUT_DIR, exist_ok=True)
+    srcs = [os.path.join(CSRC, s) for s in SOURCES]
+    deps = srcs + [os.path.join(CSRC, "common.cuh"), os.path.join(INCLUDE, "akv_b200.h")]
+    if not force and os.path.exists(LIB):
+        lib_t = os.path.getmtime(LIB)
+        if all(os.path.getmtime(d) <= lib_t for d in deps):
+            return LIB
+    objs = []
+    for s in srcs:
+        o = os.path.join(OUT_DIR, os.path.basename(s) + ".o")
+        cmd = [nvcc(), "-c", s, "-o", o] + flags(verbose)
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if verbose or r.returncode:
+            sys.stderr.write(r.stdout + r.stderr)
+        if r.returncode:
+            raise RuntimeError(f"nvcc failed on {s}")
+        objs.append(o)
+    tmp = LIB + ".tmp"
+    cmd = [nvcc(), "-shared", "-o", tmp] + objs + ["-gencode", "arch=compute_100a,code=sm_100a",
+                                                 "-Xcompiler", "-fPIC", "-lcudart"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode:
+        sys.stderr.write(r.stdout + r.stderr)
+        raise RuntimeError("link failed")
+    os.replace(tmp, LIB)
+    for o in objs:
+        os.remove(o)
+    return LIB
+
+
+if __name__ == "__main__":
+    print(build(verbose="--verbose" in sys.argv, force=True))

@@ -1,0 +1,158 @@
+// Device helpers shared by the warm-tier kernels (sm_100a).
+//
+// Everything here is hand-written inline PTX / CUDA intrinsics:
+//   * mbarrier + cp.async.bulk (1-D TMA) for streaming warm records into SMEM,
+//   * mma.sync m16n8k16 (f16 x f16 -> f32) and movmatrix for the decode
+//     contraction,
+//   * the "1024 + code" fp16 bit trick that turns packed integer codes into
+//     exact fp16 values with one LOP3 and one HFMA2 per pair.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "akv_b200.h"
+
+#define AKV_DEV __device__ __forceinline__
+
+namespace akv {
+
+constexpr int kBlockTokens = 32;   // tokens per warm block record
+
+// Bounded spin limit for every mbarrier wait (each try_wait may itself
+// suspend the thread for a while).  A wait that runs out records
+// AKV_ERR_TIMEOUT in the status word and the kernel stops issuing work.
+constexpr uint32_t kSpinLimit = 1u << 22;
+
+// ---------------------------------------------------------------- status
+AKV_DEV void set_status(int* status, int code) {
+  if (status) atomicCAS(status, 0, code);
+}
+
+// ---------------------------------------------------------------- smem
+AKV_DEV uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---------------------------------------------------------------- mbarrier
+AKV_DEV void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+AKV_DEV void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+AKV_DEV void mbar_arrive(uint64_t* bar) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+AKV_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
+                   smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+AKV_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: returns false (and records a timeout) if the phase never completes.
+AKV_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int* status) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+  }
+  set_status(status, AKV_ERR_TIMEOUT);
+  return false;
+}
+
+// 1-D bulk TMA copy global -> shared, completion counted on an mbarrier.
+// dst/src 16-byte aligned, bytes a multiple of 16.  No multicast.
+AKV_DEV void tma_load_1d(void* dst_smem, const void* src_gmem, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst_smem)),
+      "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// ---------------------------------------------------------------- loads
+AKV_DEV uint4 ldg_nc_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+AKV_DEV uint4 lds_v4(const void* p) { return *reinterpret_cast<const uint4*>(p); }
+AKV_DEV uint2 lds_v2(const void* p) { return *reinterpret_cast<const uint2*>(p); }
+AKV_DEV uint32_t lds_u32(const void* p) { return *reinterpret_cast<const uint32_t*>(p); }
+
+// ---------------------------------------------------------------- bit tricks
+AKV_DEV uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) { return __byte_perm(a, b, sel); }
+
+// (x & mask) | 0x64006400 in one LOP3: each 16-bit half becomes the fp16
+// value 1024 + (x & mask_half) as long as the mask lies in bits 0..9.
+template <uint32_t MASK>
+AKV_DEV uint32_t lop_magic(uint32_t x) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(x), "n"(MASK), "n"(0x64006400u));
+  return r;
+}
+
+// Undo the magic offset exactly: (1024 + m*c)/m - 1024/m == c for power-of-two m.
+template <int MULT>
+AKV_DEV uint32_t fix_magic(uint32_t x) {
+  const __half2 inv = __float2half2_rn(1.0f / MULT);
+  const __half2 off = __float2half2_rn(-1024.0f / MULT);
+  __half2 h = *reinterpret_cast<__half2*>(&x);
+  h = __hfma2(h, inv, off);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+template <uint32_t MASK, int MULT>
+AKV_DEV uint32_t code_pair(uint32_t x) {
+  return fix_magic<MULT>(lop_magic<MASK>(x));
+}
+
+AKV_DEV uint32_t h2_as_u32(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+AKV_DEV __half2 u32_as_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+
+AKV_DEV uint32_t pack_h2(float lo, float hi) { return h2_as_u32(__floats2half2_rn(lo, hi)); }
+
+// ---------------------------------------------------------------- MMA
+// D = A(16x16, row) * B(16x8, col) + D, f16 inputs, f32 accumulate.
+AKV_DEV void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                       uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Transpose an 8x8 b16 matrix held in the m8n8 fragment layout.
+AKV_DEV uint32_t movmatrix_trans(uint32_t a) {
+  uint32_t d;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
+  return d;
+}
+
+AKV_DEV float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+}  // namespace akv

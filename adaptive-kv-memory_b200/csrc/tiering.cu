@@ -1,0 +1,270 @@
+// Tier-management kernels: importance update, demote selection (bottom-k),
+// row gather for demote/promote, and cold-tier copies; plus the ABI helpers.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace akv {
+
+// ---------------------------------------------------------------------------
+// importance update (akv/triton_ops.py:604-650, CPU branch semantics)
+//   imp[n]    = sum_m ( sum_{b,h} attn[b,h,m,n] / (B*H) )
+//   scores[n] = fl(fl(scores[n] * decay) + imp[n])
+// One thread per column n; the (b,h) sum runs in order, like a sequential
+// reduction of the reference's mean over dims (0, 1).
+// ---------------------------------------------------------------------------
+__global__ void importance_update_kernel(const float* __restrict__ attn, int B, int H, int M, int Na,
+                                         float* __restrict__ scores, int N, float decay) {
+  const int n = blockIdx.x * blockDim.x + threadIdx.x;
+  if (n >= N) return;
+  float imp = 0.f;
+  if (n < Na) {
+    const float inv = static_cast<float>(B * H);
+    for (int m = 0; m < M; ++m) {
+      float s = 0.f;
+      for (int bh = 0; bh < B * H; ++bh) s = __fadd_rn(s, attn[(static_cast<int64_t>(bh) * M + m) * Na + n]);
+      imp = __fadd_rn(imp, __fdiv_rn(s, inv));
+    }
+  }
+  scores[n] = __fadd_rn(__fmul_rn(scores[n], decay), imp);
+}
+
+// ---------------------------------------------------------------------------
+// bottom-k selection with protected ends (akv/drop_in.py:392-413)
+//
+// Scores map to order-preserving u32 keys; protected positions get the key
+// of +inf.  A single CTA finds the k-th smallest key by an 8-bit radix select
+// (4 passes of a 256-bin histogram), then a stable compaction emits, in
+// ascending index order, every position below the threshold key plus the
+// first (k - count_below) positions equal to it.
+// ---------------------------------------------------------------------------
+constexpr int kSelThreads = 1024;
+
+AKV_DEV uint32_t order_key(float f) {
+  uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+AKV_DEV uint32_t sel_key(const float* s, int i, int n, int pf, int pl) {
+  if (i < pf || i >= n - pl) return order_key(INFINITY);
+  return order_key(s[i]);
+}
+
+__global__ void __launch_bounds__(kSelThreads) select_bottomk_kernel(const float* __restrict__ scores, int n, int k,
+                                                                     int pf, int pl, int64_t* __restrict__ out) {
+  __shared__ uint32_t hist[256];
+  __shared__ uint32_t s_prefix, s_mask, s_remaining;
+  __shared__ uint32_t warp_cnt[kSelThreads / 32];
+  __shared__ uint32_t s_base_lt, s_base_eq;
+  const int tid = threadIdx.x;
+  if (tid == 0) {
+    s_prefix = 0;
+    s_mask = 0;
+    s_remaining = static_cast<uint32_t>(k);
+  }
+  __syncthreads();
+  // radix select of the k-th smallest key, most significant byte first
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int i = tid; i < 256; i += kSelThreads) hist[i] = 0;
+    __syncthreads();
+    const uint32_t prefix = s_prefix, mask = s_mask;
+    for (int i = tid; i < n; i += kSelThreads) {
+      const uint32_t key = sel_key(scores, i, n, pf, pl);
+      if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+    }
+    __syncthreads();
+    if (tid == 0) {
+      uint32_t rem = s_remaining, acc = 0;
+      int bin = 0;
+      for (; bin < 256; ++bin) {
+        if (acc + hist[bin] >= rem) break;
+        acc += hist[bin];
+      }
+      s_remaining = rem - acc;
+      s_prefix = prefix | (static_cast<uint32_t>(bin) << shift);
+      s_mask = mask | (255u << shift);
+    }
+    __syncthreads();
+  }
+  const uint32_t thr = s_prefix;       // key of the k-th smallest
+  const uint32_t take_eq = s_remaining;  // how many keys == thr to take (lowest indices first)
+  // stable compaction in index order, chunk by chunk
+  if (tid == 0) {
+    s_base_lt = 0;
+    s_base_eq = 0;
+  }
+  __syncthreads();
+  const int lane = tid & 31, wid = tid >> 5;
+  for (int base = 0; base < n; base += kSelThreads) {
+    const int i = base + tid;
+    uint32_t key = i < n ? sel_key(scores, i, n, pf, pl) : 0xffffffffu;
+    const bool lt = i < n && key < thr;
+    const bool eq = i < n && key == thr;
+    // ranks of `eq` entries in index order
+    const uint32_t beq = __ballot_sync(0xffffffffu, eq);
+    const uint32_t blt = __ballot_sync(0xffffffffu, lt);
+    if (lane == 0) warp_cnt[wid] = (__popc(blt) << 16) | __popc(beq);
+    __syncthreads();
+    uint32_t pre_lt = 0, pre_eq = 0, tot_lt = 0, tot_eq = 0;
+    for (int w = 0; w < kSelThreads / 32; ++w) {
+      const uint32_t c = warp_cnt[w];
+      if (w < wid) {
+        pre_lt += c >> 16;
+        pre_eq += c & 0xffffu;
+      }
+      tot_lt += c >> 16;
+      tot_eq += c & 0xffffu;
+    }
+    const uint32_t my_lt = s_base_lt + pre_lt + __popc(blt & ((1u << lane) - 1u));
+    const uint32_t my_eq = s_base_eq + pre_eq + __popc(beq & ((1u << lane) - 1u));
+    // output position = number of selected entries with smaller index
+    // selected = lt, or eq with rank < take_eq
+    if (lt || (eq && my_eq < take_eq)) {
+      const uint32_t eq_before = min(my_eq, take_eq);
+      out[my_lt + eq_before] = i;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      s_base_lt += tot_lt;
+      s_base_eq += tot_eq;
+    }
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// row gather: 16-byte vectors, one (b, h, row) per warp-stride
+// ---------------------------------------------------------------------------
+__global__ void gather_rows_kernel(const char* __restrict__ src, int64_t s_sb, int64_t s_sh, int64_t s_sn,
+                                   const int64_t* __restrict__ idx, int n, int B, int H, int64_t row_bytes,
+                                   char* __restrict__ dst, int64_t d_sb, int64_t d_sh, int64_t d_sn) {
+  const int64_t vpr = row_bytes / 16;
+  const int64_t total = static_cast<int64_t>(B) * H * n * vpr;
+  for (int64_t w = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; w < total;
+       w += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t v = w % vpr;
+    int64_t r = w / vpr;
+    const int i = static_cast<int>(r % n);
+    r /= n;
+    const int h = static_cast<int>(r % H);
+    const int b = static_cast<int>(r / H);
+    const uint4 x = ldg_nc_v4(src + b * s_sb + h * s_sh + idx[i] * s_sn + v * 16);
+    *reinterpret_cast<uint4*>(dst + b * d_sb + h * d_sh + i * d_sn + v * 16) = x;
+  }
+}
+
+}  // namespace akv
+
+using namespace akv;
+
+extern "C" const char* akv_strerror(int status) {
+  switch (status) {
+    case AKV_OK: return "ok";
+    case AKV_ERR_SHAPE: return "bad or unsupported shape";
+    case AKV_ERR_BITS: return "bit width must be 2, 3 or 4";
+    case AKV_ERR_ALIGN: return "pointer or stride misaligned";
+    case AKV_ERR_UNSUPPORTED: return "request not supported by this build";
+    case AKV_ERR_LAUNCH: return "CUDA launch or runtime error";
+    case AKV_ERR_TIMEOUT: return "device-side wait timed out";
+    case AKV_ERR_NULL: return "required pointer is NULL";
+    case AKV_ERR_WORKSPACE: return "workspace too small";
+    default: return "unknown status";
+  }
+}
+
+extern "C" int akv_abi_version(void) { return AKV_ABI_VERSION; }
+
+extern "C" int akv_warm_layout_init(int D, int kb, int vb, int n, akv_warm_layout* L) {
+  if (!L) return AKV_ERR_NULL;
+  if (kb < 2 || kb > 4 || vb < 2 || vb > 4) return AKV_ERR_BITS;
+  if (D <= 0 || D % 32 || D > 256 || n < 0 || n > D) return AKV_ERR_SHAPE;
+  auto up16 = [](int x) { return (x + 15) & ~15; };
+  L->head_dim = D;
+  L->key_bits = kb;
+  L->value_bits = vb;
+  L->n_outlier = n;
+  int off = 0;
+  L->kc = off;
+  off = up16(off + kBlockTokens * D * kb / 8);
+  L->vc = off;
+  off = up16(off + kBlockTokens * D * vb / 8);
+  L->ks = off;
+  off = up16(off + 2 * D);
+  L->kz = off;
+  off = up16(off + 2 * D);
+  L->vs = off;
+  off = up16(off + 2 * kBlockTokens);
+  L->vz = off;
+  off = up16(off + 2 * kBlockTokens);
+  L->ko = off;
+  off = up16(off + 2 * kBlockTokens * n);
+  L->vo = off;
+  off = up16(off + 2 * kBlockTokens * n);
+  L->ki = off;                          // n int16 K outlier ids
+  L->vi = off + 2 * n;                  // n int16 V outlier ids
+  L->mask = off + ((4 * n + 3) & ~3);   // u32 valid-slot mask
+  off = up16(L->mask + 4);
+  L->bytes = off;
+  return AKV_OK;
+}
+
+extern "C" int akv_importance_update(const float* attn, int B, int H, int M, int Na, float* scores, int N,
+                                     float decay, void* stream) {
+  if (!scores || (!attn && Na > 0)) return AKV_ERR_NULL;
+  if (B <= 0 || H <= 0 || M <= 0 || Na < 0 || N < 0) return AKV_ERR_SHAPE;
+  if (N == 0) return AKV_OK;
+  importance_update_kernel<<<(N + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(attn, B, H, M, Na,
+                                                                                          scores, N, decay);
+  return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_LAUNCH;
+}
+
+extern "C" size_t akv_select_workspace_bytes(int n) { return n >= 0 ? 16 : 0; }
+
+extern "C" int akv_select_bottomk(const float* scores, int n, int k, int protect_first, int protect_last,
+                                  int64_t* idx_out, void* workspace, size_t workspace_bytes, void* stream) {
+  (void)workspace;
+  (void)workspace_bytes;
+  if (!scores || !idx_out) return AKV_ERR_NULL;
+  if (n < 0 || k < 0 || k > n || protect_first < 0 || protect_last < 0) return AKV_ERR_SHAPE;
+  if (k == 0) return AKV_OK;
+  if (protect_first > n) protect_first = n;
+  if (protect_last > n) protect_last = n;
+  select_bottomk_kernel<<<1, kSelThreads, 0, static_cast<cudaStream_t>(stream)>>>(scores, n, k, protect_first,
+                                                                                 protect_last, idx_out);
+  return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_LAUNCH;
+}
+
+extern "C" int akv_gather_rows(const void* src, int64_t s_sb, int64_t s_sh, int64_t s_sn, const int64_t* idx, int n,
+                               int B, int H, int64_t row_bytes, void* dst, int64_t d_sb, int64_t d_sh, int64_t d_sn,
+                               void* stream) {
+  if (!src || !dst || (!idx && n > 0)) return AKV_ERR_NULL;
+  if (n < 0 || B <= 0 || H <= 0 || row_bytes <= 0) return AKV_ERR_SHAPE;
+  if (n == 0) return AKV_OK;
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) % 16) == 0; };
+  if (row_bytes % 16 || !al(src) || !al(dst) || s_sb % 16 || s_sh % 16 || s_sn % 16 || d_sb % 16 || d_sh % 16 ||
+      d_sn % 16)
+    return AKV_ERR_ALIGN;
+  const int64_t total = static_cast<int64_t>(B) * H * n * (row_bytes / 16);
+  const int64_t blocks = std::min<int64_t>((total + 255) / 256, 148 * 16);
+  gather_rows_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const char*>(src), s_sb, s_sh, s_sn, idx, n, B, H, row_bytes, static_cast<char*>(dst), d_sb,
+      d_sh, d_sn);
+  return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_LAUNCH;
+}
+
+extern "C" int akv_cold_copy(void* dst, int64_t dst_stride, const void* src, int64_t src_stride, int64_t chunk_bytes,
+                             int64_t count, int dir, void* stream, void* event) {
+  if (!dst || !src) return AKV_ERR_NULL;
+  if (chunk_bytes <= 0 || count < 0 || dst_stride < chunk_bytes || src_stride < chunk_bytes) return AKV_ERR_SHAPE;
+  if (dir != 0 && dir != 1) return AKV_ERR_SHAPE;
+  if (count == 0) return AKV_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const cudaMemcpyKind kind = dir == 0 ? cudaMemcpyDeviceToHost : cudaMemcpyHostToDevice;
+  if (cudaMemcpy2DAsync(dst, static_cast<size_t>(dst_stride), src, static_cast<size_t>(src_stride),
+                        static_cast<size_t>(chunk_bytes), static_cast<size_t>(count), kind, st) != cudaSuccess)
+    return AKV_ERR_LAUNCH;
+  if (event && cudaEventRecord(static_cast<cudaEvent_t>(event), st) != cudaSuccess) return AKV_ERR_LAUNCH;
+  return AKV_OK;
+}

@@ -1,0 +1,222 @@
+/*
+ * akv_b200.h — C ABI of the B200 (sm_100a) warm-tier library libakv_sm100.so.
+ *
+ * The reference package (akv 1.4.0) is pure Python/PyTorch; these entry
+ * points are what its Python API for the warm tier binds to in this build
+ * (through ctypes, see adaptive-kv-memory_b200/akv/_C.py).  Each function
+ * names the reference interface it replaces as path:line in the reference
+ * project.
+ *
+ * Conventions
+ *   - Plain pointers and sizes only.  Device pointers unless stated.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *   - Every call validates its arguments on the host and returns AKV_OK (0) or
+ *     a negative AKV_ERR_* code without launching anything on error.
+ *   - Work is enqueued asynchronously on `stream`; no call synchronises.
+ *   - `status` (nullable) is a device int that kernels set to a negative
+ *     AKV_ERR_* code when a bounded device-side wait runs out; callers read it
+ *     after synchronising.  It is never cleared by the library.
+ *   - The library never allocates device memory: scratch comes from the
+ *     caller as `workspace`.
+ *   - fp16 = IEEE binary16 stored as uint16_t.
+ */
+#ifndef AKV_B200_H_
+#define AKV_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define AKV_ABI_VERSION 1
+#define AKV_BLOCK_TOKENS 32 /* tokens per warm block record */
+
+enum {
+  AKV_OK = 0,
+  AKV_ERR_SHAPE = -1,       /* bad or unsupported shape / length */
+  AKV_ERR_BITS = -2,        /* bit width not in {2,3,4} */
+  AKV_ERR_ALIGN = -3,       /* pointer or stride alignment */
+  AKV_ERR_UNSUPPORTED = -4, /* valid request this build does not handle */
+  AKV_ERR_LAUNCH = -5,      /* kernel launch / CUDA runtime error */
+  AKV_ERR_TIMEOUT = -6,     /* a bounded device-side wait ran out */
+  AKV_ERR_NULL = -7,        /* required pointer is NULL */
+  AKV_ERR_WORKSPACE = -8    /* workspace too small */
+};
+
+const char* akv_strerror(int status);
+int akv_abi_version(void);
+
+/* ------------------------------------------------------------------------
+ * Warm block record layout.
+ *
+ * The warm tier is stored as fixed 32-token block records, one per
+ * (batch row, KV head, block).  A record holds exactly the fields of one
+ * reference quantiser call (akv/affine_quantizer.py:97-110) restricted to
+ * those 32 tokens:
+ *   kc  K codes   [32][D*kbits/8]  u8  (akv/bitpack.py layout along D)
+ *   vc  V codes   [32][D*vbits/8]  u8
+ *   ks  K scale   [D]  fp16   kz  K zero [D]  fp16  (per channel, per group)
+ *   vs  V scale   [32] fp16   vz  V zero [32] fp16  (per token)
+ *   ko  K outlier data [32][n] fp16     vo  V outlier data [32][n] fp16
+ *   ki  K outlier channel ids [n] int16 vi  V outlier channel ids [n] int16
+ *   mask  u32 bitmask of valid token slots
+ * All offsets are multiples of 16 bytes and `bytes` (the record stride) is a
+ * multiple of 16 so records can be moved with 1-D bulk TMA copies.
+ * ---------------------------------------------------------------------- */
+typedef struct {
+  int32_t head_dim, key_bits, value_bits, n_outlier;
+  int32_t kc, vc, ks, kz, vs, vz, ko, vo, ki, vi, mask, bytes;
+} akv_warm_layout;
+
+/* Fill `out` for the given shape.  Returns AKV_ERR_SHAPE / AKV_ERR_BITS on bad input. */
+int akv_warm_layout_init(int head_dim, int key_bits, int value_bits, int n_outlier, akv_warm_layout* out);
+
+/* Strided byte view used to address quantiser outputs:
+ *   addr(b, h, blk, slot) = ptr + b*sb + h*sh + blk*sblk + slot*sslot
+ * where blk = token / 32 and slot = token % 32 of the call. */
+typedef struct {
+  void* ptr;
+  int64_t sb, sh, sblk, sslot;
+} akv_view;
+
+/* Destination of one quantiser call (keys or values).  NULL ptr = not written.
+ *   codes        packed codes, D*bits/8 bytes per token
+ *   scale/zero   keys: D fp16 per (b, h, blk) (sslot unused; the group's value
+ *                is written to every block the group covers);
+ *                values: one fp16 per token
+ *   out_data     n fp16 per token
+ *   out_idx      n int16 per (b, h, blk) (sslot unused)
+ *   mask         u32 per (b, h, blk): bit s set for each slot this call wrote */
+typedef struct {
+  akv_view codes, scale, zero, out_data, out_idx, mask;
+} akv_qdest;
+
+/* ------------------------------------------------------------------------
+ * A3: bit packing.  Replaces akv/bitpack.py:95-114 (pack / unpack) and the
+ * per-width helpers :13-90.  `rows` rows of `dim` uint8 codes each; packed
+ * rows are dim*bits/8 bytes (right-padded like the reference).
+ * ---------------------------------------------------------------------- */
+int akv_pack_codes(const uint8_t* codes, int64_t rows, int dim, int bits, uint8_t* packed, void* stream);
+int akv_unpack_codes(const uint8_t* packed, int64_t rows, int dim, int bits, uint8_t* codes, void* stream);
+
+/* ------------------------------------------------------------------------
+ * A1/A2: block-affine quantise + bit-pack.
+ * Replaces AffineQuantizer.quantize_keys (akv/affine_quantizer.py:63-110)
+ * and quantize_values (:131-176), including the fp16 op-by-op rounding
+ * (scale = fp16(fp16(max-min)/maxval), codes = clamp(rint(fp16(fp16(x-zero)/scale)))),
+ * the NaN->0 code for zero-range groups and the outlier-channel side store.
+ *
+ *   src          fp16, element (b, h, n, d) at src + b*src_sb + h*src_sh + n*src_sn + d
+ *                (d contiguous, rows 16-byte aligned)
+ *   tok_idx      optional int64 row indices: token t of the call reads row
+ *                tok_idx[b*tok_sb + t] (fused gather for demotion); NULL = rows 0..N-1
+ *   B, H, N, D   batch rows, heads, tokens in the call, head dim (D % 32 == 0, D <= 256)
+ *   group        tokens per scale group (K min/max and outlier selection run
+ *                per group of `group` consecutive tokens; N = one reference call)
+ *   n_outlier    channels kept in fp16 (0 = off); the reference's
+ *                max(1, int(D*outlier_fraction))
+ * ---------------------------------------------------------------------- */
+int akv_quantize(const uint16_t* src, int64_t src_sb, int64_t src_sh, int64_t src_sn,
+                 const int64_t* tok_idx, int64_t tok_sb,
+                 int B, int H, int N, int D, int bits, int is_key, int group, int n_outlier,
+                 const akv_qdest* dst, int* status, void* stream);
+
+/* ------------------------------------------------------------------------
+ * A4: unpack + dequantise to fp16.
+ * Replaces AffineQuantizer.dequantize_keys/values (akv/affine_quantizer.py:112-124,
+ * :178-189): out = fp16(fp16(code*scale) + zero), outlier channels overwritten.
+ *   src          the same view struct the quantiser wrote (mask ignored)
+ *   tok_idx      optional int64 token indices into the source token space
+ *                (token p lives in blk p/32, slot p%32); NULL = tokens 0..N-1
+ *   out          fp16 (b, h, n, d) at out + b*out_sb + h*out_sh + n*out_sn + d
+ * ---------------------------------------------------------------------- */
+int akv_dequantize(const akv_qdest* src, const int64_t* tok_idx, int64_t tok_sb,
+                   int B, int H, int N, int D, int bits, int is_key, int n_outlier,
+                   uint16_t* out, int64_t out_sb, int64_t out_sh, int64_t out_sn, void* stream);
+
+/* ------------------------------------------------------------------------
+ * A5: mixed-tier decode attention (one query token per sequence).
+ * Replaces the reference's decode paths that attend over [warm; hot]:
+ * fused_attention.mixed_precision_decode_attention (akv/fused_attention.py:324-366),
+ * triton_ops.fused_mixed_precision_attention (akv/triton_ops.py:466-515) and the
+ * SDPA over AKVLayer's dequantised view (akv/drop_in.py:753-787).
+ * softmax(q.[K_warm;K_hot]^T * sm_scale) . [V_warm;V_hot], fp32 accumulation,
+ * warm tier read straight from packed block records (never materialised).
+ *
+ *   q            fp16 (b, hq, d) at q + b*q_sb + hq*q_sh + d
+ *   hot_k/hot_v  fp16 (b, hkv, t, d) at p + b*sb + h*sh + t*sn + d (NULL if n_hot == 0)
+ *   hot_len      optional int32[B] hot tokens per row (NULL = n_hot for all)
+ *   warm         block records: record j of (b, hkv) at warm + b*w_sb + h*w_sh + j*layout.bytes
+ *   warm_len     optional int32[B] warm blocks per row (NULL = n_warm_blocks for all);
+ *                token validity inside a block comes from the record mask
+ *   Hq % Hkv == 0 (GQA: q head h reads KV head h / (Hq/Hkv))
+ *   out          fp16 (b, hq, d) at out + b*o_sb + hq*o_sh + d
+ *   lse          optional fp32 [B*Hq] natural-log LSE of the scaled logits
+ *   workspace    device scratch of at least akv_decode_workspace_bytes(...) bytes
+ * ---------------------------------------------------------------------- */
+size_t akv_decode_workspace_bytes(int B, int Hq, int Hkv, int D, int n_hot, int n_warm_blocks);
+
+int akv_mixed_decode(const uint16_t* q, int64_t q_sb, int64_t q_sh,
+                     const uint16_t* hot_k, const uint16_t* hot_v, int64_t h_sb, int64_t h_sh, int64_t h_sn,
+                     int n_hot, const int32_t* hot_len,
+                     const uint8_t* warm, int64_t w_sb, int64_t w_sh, const akv_warm_layout* layout,
+                     int n_warm_blocks, const int32_t* warm_len,
+                     int B, int Hq, int Hkv, int D, float sm_scale,
+                     uint16_t* out, int64_t o_sb, int64_t o_sh, float* lse,
+                     void* workspace, size_t workspace_bytes, int* status, void* stream);
+
+/* Log-sum-exp combine of split partials (also used across GPUs for a
+ * sequence split).  acc fp32 [rows][splits][D] (unnormalised, relative to m),
+ * ml fp32 [rows][splits][2] = (m in log2 units, l).  Writes fp16 out[rows][D]
+ * (row r at out + r*o_sr) and optional lse[rows] (natural log). */
+int akv_lse_combine(const float* acc, const float* ml, int rows, int splits, int D,
+                    uint16_t* out, int64_t o_sr, float* lse, void* stream);
+
+/* ------------------------------------------------------------------------
+ * A6: importance update.  Replaces triton_ops.fused_importance_update
+ * (akv/triton_ops.py:604-650): scores = scores*decay + sum_M mean_{B,H} attn,
+ * as two roundings (mul then add, no FMA).  attn fp32 (B, H, M, Na) contiguous;
+ * scores fp32 [N] updated in place; attention columns beyond N are ignored and
+ * missing ones count as 0 (:627-633).
+ * ---------------------------------------------------------------------- */
+int akv_importance_update(const float* attn, int B, int H, int M, int Na, float* scores, int N, float decay,
+                          void* stream);
+
+/* ------------------------------------------------------------------------
+ * A7: demote selection.  Replaces AKVLayer._select_demote_indices
+ * (akv/drop_in.py:392-413) and ImportanceBasedMigrator.get_eviction_candidates
+ * (akv/vmm.py:221-242): the k lowest scores with the first `protect_first`
+ * and last `protect_last` positions excluded (treated as +inf), returned as
+ * ascending int64 indices.  Equal scores are taken lowest index first.
+ * workspace >= akv_select_workspace_bytes(n).
+ * ---------------------------------------------------------------------- */
+size_t akv_select_workspace_bytes(int n);
+int akv_select_bottomk(const float* scores, int n, int k, int protect_first, int protect_last,
+                       int64_t* idx_out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Row gather/compaction for tier moves (drop_in.py:684-685 gather,
+ * :739-751 keep-mask compaction, :474-475 promote-prepend).
+ * Copies `n` rows of `row_bytes` (multiple of 16) for every (b, h):
+ *   dst + b*d_sb + h*d_sh + i*d_sn  <-  src + b*s_sb + h*s_sh + idx[i]*s_sn   */
+int akv_gather_rows(const void* src, int64_t s_sb, int64_t s_sh, int64_t s_sn,
+                    const int64_t* idx, int n, int B, int H, int64_t row_bytes,
+                    void* dst, int64_t d_sb, int64_t d_sh, int64_t d_sn, void* stream);
+
+/* ------------------------------------------------------------------------
+ * A8: cold tier copies.  Replaces AsyncMigrator._do_warm_to_cold /
+ * _do_cold_to_warm (akv/async_migration.py:303-349): warm block records move
+ * byte-for-byte between HBM and a pinned host arena with cudaMemcpy2DAsync
+ * on `stream` (a side stream), followed by an event record when `event` is
+ * non-NULL.  dir = 0: device -> host (demote), 1: host -> device (promote).
+ * `count` strided chunks of `chunk_bytes`, strides in bytes.
+ * ---------------------------------------------------------------------- */
+int akv_cold_copy(void* dst, int64_t dst_stride, const void* src, int64_t src_stride,
+                  int64_t chunk_bytes, int64_t count, int dir, void* stream, void* event);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AKV_B200_H_ */

@@ -1,0 +1,180 @@
+"""GPU parity: mixed-tier decode attention vs the oracle.
+
+The oracle dequantises the warm tier exactly like the reference (one
+AffineQuantizer call per 32-token group and batch row), concatenates the FP16
+hot window and runs fp32 softmax attention (akv/fused_attention.py:362-366).
+Bar (north star): max-abs error <= 2e-3 on the fp16 output.
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import akv_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda:0"
+ATOL = 2e-3
+
+
+def _np(t):
+    return t.detach().cpu().numpy()
+
+
+def _rope(x, start=0, base=10000.0):
+    """Half-split rotary embedding on (..., N, D) fp16 (reference _diag_quant_rope.py recipe)."""
+    D = x.shape[-1]
+    half = D // 2
+    inv = 1.0 / (base ** (np.arange(half, dtype=np.float32) / half))
+    ang = (np.arange(start, start + x.shape[-2], dtype=np.float32)[:, None] * inv[None, :])
+    cos, sin = np.cos(ang), np.sin(ang)
+    xf = x.astype(np.float32)
+    x1, x2 = xf[..., :half], xf[..., half:]
+    return np.concatenate([x1 * cos - x2 * sin, x1 * sin + x2 * cos], -1).astype(np.float16)
+
+
+def make_case(seed, B, Hq, Hkv, D, n_warm, n_hot, outlier_ch=(), rope=True):
+    rng = np.random.default_rng(seed)
+    N = n_warm + n_hot
+    k = rng.standard_normal((B, Hkv, N, D)).astype(np.float32)
+    for c in outlier_ch:
+        k[..., c] *= 12.0
+    k = k.astype(np.float16)
+    if rope:
+        k = _rope(k)
+    v = rng.standard_normal((B, Hkv, N, D)).astype(np.float16)
+    q = rng.standard_normal((B, Hq, D)).astype(np.float16)
+    return q, k[:, :, :n_warm], v[:, :, :n_warm], k[:, :, n_warm:], v[:, :, n_warm:]
+
+
+def run_case(q, wk, wv, hk, hv, kb, vb, frac, hot_len=None, warm_blocks=None):
+    import akv
+    B, Hkv, n_warm, D = wk.shape
+    n_hot = hk.shape[2]
+    arena = None
+    if n_warm:
+        arena = akv.WarmArena(B, Hkv, D, kb, vb, outlier_fraction=frac,
+                              max_blocks=(n_warm + 31) // 32 + 1, device=DEV)
+        arena.append(torch.from_numpy(wk).to(DEV), torch.from_numpy(wv).to(DEV), group=32)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    hkt = torch.from_numpy(hk).to(DEV) if n_hot else None
+    hvt = torch.from_numpy(hv).to(DEV) if n_hot else None
+    hl = torch.tensor(hot_len, dtype=torch.int32, device=DEV) if hot_len is not None else None
+    wl = torch.tensor(warm_blocks, dtype=torch.int32, device=DEV) if warm_blocks is not None else None
+    out, lse = akv.mixed_tier_decode_attention(torch.from_numpy(q).to(DEV), hkt, hvt, arena,
+                                               hot_len=hl, warm_len=wl, return_lse=True, status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    return _np(out).astype(np.float32), _np(lse)
+
+
+def oracle_case(q, wk, wv, hk, hv, kb, vb, frac, hot_len=None, warm_blocks=None):
+    B, Hkv, n_warm, D = wk.shape
+    outs, lses = [], []
+    for b in range(B):
+        nw = n_warm if warm_blocks is None else min(n_warm, 32 * warm_blocks[b])
+        nh = hk.shape[2] if hot_len is None else hot_len[b]
+        parts_k, parts_v = [], []
+        if nw:
+            parts_k.append(O.dequantize_groups(O.quantize_groups(wk[b:b + 1, :, :nw], kb, 32, True, frac)))
+            parts_v.append(O.dequantize_groups(O.quantize_groups(wv[b:b + 1, :, :nw], vb, 32, False, frac)))
+        parts_k.append(hk[b:b + 1, :, :nh])
+        parts_v.append(hv[b:b + 1, :, :nh])
+        o, l = O.decode_attention(q[b:b + 1], np.concatenate(parts_k, 2), np.concatenate(parts_v, 2),
+                                  return_lse=True)
+        outs.append(o)
+        lses.append(l)
+    return np.concatenate(outs), np.concatenate(lses)
+
+
+def check(seed, B, Hq, Hkv, n_warm, n_hot, kb, vb, frac, D=128, outlier_ch=(7,), **kw):
+    q, wk, wv, hk, hv = make_case(seed, B, Hq, Hkv, D, n_warm, n_hot, outlier_ch)
+    out, lse = run_case(q, wk, wv, hk, hv, kb, vb, frac, **kw)
+    ref, rlse = oracle_case(q, wk, wv, hk, hv, kb, vb, frac, **kw)
+    err = np.abs(out - ref).max()
+    assert err <= ATOL, f"max abs err {err}"
+    np.testing.assert_allclose(lse, rlse, atol=2e-3, rtol=0)
+    return err
+
+
+def test_config1_full():
+    """B1, 12 Q / 2 KV heads, D128, 512 hot + 3584 warm at 3 bits, 32-token groups,
+    1% of K channels x12 outliers, RoPE on K."""
+    check(0, 1, 12, 2, 3584, 512, 3, 3, 0.0, outlier_ch=(100,))
+
+
+def test_config3_shape_small():
+    """Config-3 shape family (32 Q / 8 KV heads, k4v2, outlier_fraction 0.01) at a short context."""
+    check(1, 2, 32, 8, 32 * 20 + 5, 70, 4, 2, 0.01, outlier_ch=(3, 77))
+
+
+@pytest.mark.parametrize("kb", [2, 3, 4])
+@pytest.mark.parametrize("vb", [2, 3, 4])
+def test_bit_combinations(kb, vb):
+    check(10 + kb * 5 + vb, 2, 8, 2, 32 * 6, 40, kb, vb, 0.0)
+
+
+@pytest.mark.parametrize("frac", [0.01, 0.05])
+def test_outlier_channels(frac):
+    check(20, 1, 16, 4, 32 * 9 + 17, 33, 3, 3, frac, outlier_ch=(1, 64, 127))
+
+
+def test_warm_only_mha():
+    check(30, 2, 4, 4, 96, 0, 2, 2, 0.0)
+
+
+def test_hot_only_gqa():
+    check(31, 3, 8, 2, 0, 300, 4, 4, 0.0)
+
+
+def test_group16_heads():
+    """g = Hq/Hkv = 16 > 8: two head groups per KV head."""
+    check(32, 1, 32, 2, 32 * 4, 64, 4, 4, 0.0)
+
+
+def test_ragged_batch():
+    check(33, 3, 8, 2, 32 * 5, 50, 3, 3, 0.0, hot_len=[50, 7, 0], warm_blocks=[5, 2, 3])
+
+
+def test_single_token():
+    check(34, 1, 8, 1, 0, 1, 4, 4, 0.0)
+    check(35, 1, 8, 1, 1, 0, 4, 4, 0.0)
+
+
+def test_large_logits_stable():
+    """Scaled-up queries: softmax must stay finite and match (online max subtraction)."""
+    q, wk, wv, hk, hv = make_case(40, 1, 8, 2, 128, 32 * 8, 64)
+    q = (q.astype(np.float32) * 8).astype(np.float16)
+    out, _ = run_case(q, wk, wv, hk, hv, 4, 4, 0.0)
+    ref, _ = oracle_case(q, wk, wv, hk, hv, 4, 4, 0.0)
+    assert np.isfinite(out).all()
+    assert np.abs(out - ref).max() <= ATOL
+
+
+def test_reference_signature_hot_only(golden_dir):
+    import os
+    import akv
+    z = np.load(os.path.join(golden_dir, "attention.npz"))
+    t = "hot_B2_H2_N100_D128"
+    out = akv.mixed_precision_decode_attention(torch.from_numpy(z[f"{t}/q"]).to(DEV),
+                                               torch.from_numpy(z[f"{t}/k"]).to(DEV),
+                                               torch.from_numpy(z[f"{t}/v"]).to(DEV))
+    assert out.shape == (2, 2, 1, 128)
+    np.testing.assert_allclose(_np(out).astype(np.float32), z[f"{t}/out"].astype(np.float32), atol=ATOL, rtol=0)
+
+
+def test_affine_gqa_golden(golden_dir):
+    """Golden from the reference: dequantised affine warm + hot, GQA, fp32 attention."""
+    import os
+    import akv
+    z = np.load(os.path.join(golden_dir, "attention.npz"))
+    t = "affine_gqa"
+    wk, wv = z[f"{t}/wk"], z[f"{t}/wv"]
+    arena = akv.WarmArena(1, 2, 128, 3, 3, max_blocks=4, device=DEV)
+    arena.append(torch.from_numpy(wk).to(DEV), torch.from_numpy(wv).to(DEV), group=32)
+    out = akv.mixed_tier_decode_attention(torch.from_numpy(z[f"{t}/q"]).to(DEV),
+                                          torch.from_numpy(z[f"{t}/hk"]).to(DEV),
+                                          torch.from_numpy(z[f"{t}/hv"]).to(DEV), arena)
+    np.testing.assert_allclose(_np(out).astype(np.float32), z[f"{t}/out"].astype(np.float32), atol=ATOL, rtol=0)

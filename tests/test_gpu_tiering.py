@@ -1,0 +1,90 @@
+"""GPU parity: importance update, demote selection, row gather, cold-tier copies."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import akv_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda:0"
+
+
+def _np(t):
+    return t.detach().cpu().numpy()
+
+
+def test_importance_update_golden(golden_dir):
+    from akv import tiering
+    z = np.load(os.path.join(golden_dir, "importance.npz"))
+    for (B, H, M, N) in ((1, 4, 1, 64), (2, 8, 3, 257), (8, 8, 1, 512)):
+        t = f"imp_B{B}_H{H}_M{M}_N{N}"
+        attn = torch.from_numpy(z[f"{t}/attn"]).to(DEV)
+        scores = torch.from_numpy(z[f"{t}/scores_in"]).to(DEV)
+        out = tiering.fused_importance_update(attn, scores, decay=float(z[f"{t}/decay"]))
+        assert out.data_ptr() == scores.data_ptr()  # in place, like the reference
+        np.testing.assert_allclose(_np(out), z[f"{t}/scores_out"], rtol=2e-6, atol=1e-7)
+    s = torch.ones(32, device=DEV)
+    out = tiering.fused_importance_update(torch.zeros(1, 1, 1, 32, device=DEV), s, decay=0.5)
+    np.testing.assert_array_equal(_np(out), z["imp_zero/scores_out"])
+
+
+def test_importance_update_pad_and_truncate():
+    from akv import tiering
+    rng = np.random.default_rng(0)
+    for na, n in ((40, 64), (100, 64)):
+        attn = rng.random((2, 3, 2, na)).astype(np.float32)
+        scores = rng.random(n).astype(np.float32)
+        ref = O.importance_update(attn, scores, 0.9)
+        out = tiering.fused_importance_update(torch.from_numpy(attn).to(DEV), torch.from_numpy(scores).to(DEV), 0.9)
+        np.testing.assert_allclose(_np(out), ref, rtol=2e-6, atol=1e-7)
+
+
+def test_select_golden(golden_dir):
+    from akv import tiering
+    z = np.load(os.path.join(golden_dir, "importance.npz"))
+    for key in [k for k in z.files if k.startswith("sel_") and k.endswith("/meta")]:
+        t = key[:-5]
+        hot_len, budget, n_dem = (int(x) for x in z[key])
+        idx = tiering.select_demote_indices(torch.from_numpy(z[f"{t}/scores"]).to(DEV), n_dem, budget)
+        np.testing.assert_array_equal(_np(idx), z[f"{t}/idx"], err_msg=t)
+
+
+@pytest.mark.parametrize("n,k", [(1, 1), (10, 3), (1000, 999), (4096, 3584), (131072, 8192), (131072, 1)])
+def test_select_vs_oracle_ties(n, k):
+    """Ties (quantised scores) resolve lowest index first, like the oracle."""
+    from akv import tiering
+    rng = np.random.default_rng(n + k)
+    scores = (rng.integers(0, 50, n) / 7.0).astype(np.float32)
+    budget = 64
+    pf, pl = min(4, n), min(16, budget // 4)
+    k = max(0, min(k, n - pf - pl)) if n > pf + pl else 0
+    if k == 0:
+        return
+    idx = tiering.select_bottomk(torch.from_numpy(scores).to(DEV), k, pf, pl)
+    ref = O.select_demote(scores, k, budget)
+    np.testing.assert_array_equal(_np(idx), ref)
+
+
+def test_gather_rows():
+    from akv import tiering
+    x = torch.randn(2, 3, 50, 128, device=DEV).half()
+    idx = torch.tensor([0, 7, 7, 49, 3], device=DEV)
+    y = tiering.gather_rows(x, idx)
+    torch.testing.assert_close(y, x[:, :, idx], rtol=0, atol=0)
+
+
+def test_cold_copy_roundtrip():
+    from akv import tiering
+    src = torch.randint(0, 255, (2, 4, 10, 3856), dtype=torch.uint8, device=DEV)
+    host = torch.empty(2, 4, 3, 3856, dtype=torch.uint8).pin_memory()
+    side = torch.cuda.Stream()
+    ev = tiering.cold_copy_blocks(src, 5, 3, host, stream=side)
+    ev.synchronize()
+    np.testing.assert_array_equal(host.numpy(), _np(src[:, :, 5:8]))
+    dst = torch.zeros_like(src)
+    ev = tiering.cold_restore_blocks(host, dst, 2, stream=side)
+    ev.synchronize()
+    np.testing.assert_array_equal(_np(dst[:, :, 2:5]), _np(src[:, :, 5:8]))
