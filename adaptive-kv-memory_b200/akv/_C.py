@@ -56,9 +56,10 @@ SIGNATURES = {
                                  c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int, c_void_p,
                                  c_void_p, c_int64, c_int64, POINTER(WarmLayout), c_int, c_void_p,
                                  c_int, c_int, c_int, c_int, c_float,
-                                 c_void_p, c_int64, c_int64, c_void_p,
+                                 c_void_p, c_int64, c_int64, c_void_p, c_void_p,
                                  c_void_p, c_size_t, c_void_p, c_void_p]),
-    "akv_lse_combine": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_int64, c_void_p, c_void_p]),
+    "akv_lse_combine": (c_int, [c_void_p, c_int64, c_int64, c_int, c_int, c_int, c_void_p, c_int64, c_void_p,
+                                c_void_p, c_void_p]),
     "akv_importance_update": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int, c_float, c_void_p]),
     "akv_select_workspace_bytes": (c_size_t, [c_int]),
     "akv_select_bottomk": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_size_t, c_void_p]),

@@ -41,7 +41,8 @@ def mixed_tier_decode_attention(query: torch.Tensor,
                                 warm_len: Optional[torch.Tensor] = None,
                                 return_lse: bool = False,
                                 out: Optional[torch.Tensor] = None,
-                                status: Optional[torch.Tensor] = None):
+                                status: Optional[torch.Tensor] = None,
+                                partial_out: Optional[torch.Tensor] = None):
     """softmax(q [K_warm; K_hot]^T * sm_scale) [V_warm; V_hot] for one query token.
 
     query:      (B, Hq, 1, D) or (B, Hq, D) fp16
@@ -50,7 +51,9 @@ def mixed_tier_decode_attention(query: torch.Tensor,
     n_hot:      hot tokens to read (default: hot_keys.shape[2])
     hot_len / warm_len: optional int32 (B,) per-row hot tokens / warm blocks
     Returns (B, Hq, 1, D) fp16 (same rank as ``query``), plus the natural-log
-    LSE (B, Hq) fp32 when ``return_lse``.
+    LSE (B, Hq) fp32 when ``return_lse``.  ``partial_out`` (fp32 (B*Hq, D+2))
+    additionally receives the (acc, m, l) partial record of these tokens for a
+    cross-GPU sequence split (see ``akv.parallel``).
     """
     _C.require_cuda(query, hot_keys, hot_values)
     q3 = query.reshape(query.shape[0], query.shape[1], query.shape[-1]) if query.dim() == 4 else query
@@ -91,7 +94,7 @@ def mixed_tier_decode_attention(query: torch.Tensor,
         hk_ptr, hv_ptr, hs[0], hs[1], hs[2], nh, _C.ptr(hot_len),
         wptr, wsb, wsh, layout, nwb, _C.ptr(warm_len),
         B, Hq, Hkv, D, float(sm_scale),
-        o.data_ptr(), o.stride(0), o.stride(1), _C.ptr(lse),
+        o.data_ptr(), o.stride(0), o.stride(1), _C.ptr(lse), _C.ptr(partial_out),
         ws.data_ptr(), ws.numel(), _C.ptr(status), _C.stream_of(q3))
     _C.check(rc, "akv_mixed_decode")
     res = o.unsqueeze(2) if query.dim() == 4 else o

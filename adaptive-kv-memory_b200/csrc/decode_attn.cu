@@ -7,15 +7,16 @@
 //
 // Warm CTAs: one producer warp streams whole block records HBM -> SMEM with
 // 1-D bulk TMA (cp.async.bulk + mbarrier ring); consumer warps each take whole
-// blocks.  The per-channel K scale is folded into the query
-// (q~ = q*s_K, split hi/lo fp16) and the per-token V scale into the
-// probabilities (p~ = p*s_V), so the tensor cores contract raw integer codes:
-//   logit_t = q~ . c_t + q . z_K (+ outlier channels)
-//   out     = sum_t p~_t c_t + sum_t p_t z_V,t (+ outlier channel correction)
-// Codes become exact fp16 integers with the 1024-magic trick; the contraction
-// runs on mma.sync m16n8k16 with tokens as M (QK^T) and head_dim as M (PV),
-// the query heads of the KV head as N = 8.  movmatrix transposes P between the
-// two MMAs.
+// blocks and dequantise them in registers exactly like the reference
+// (akv/affine_quantizer.py:112-124, :178-189: fp16(fp16(code*scale) + zero),
+// outlier channels replaced by their fp16 originals), so the contraction sees
+// the same fp16 K/V values the reference attends over.  Packed codes become
+// fp16 with the "1024 + code" magic (one LOP3 per pair); one HFMA2 then gives
+// fp16(code*scale) with a single rounding and one HADD2 adds the zero point.
+// The contraction runs on mma.sync m16n8k16 (f16 in, f32 accumulate): tokens
+// are M for q.K^T, head_dim is M for P.V, and the (<= 8) query heads of the KV
+// head are N.  movmatrix transposes P between the two; P enters the second MMA
+// as an fp16 hi + lo pair so the probabilities keep ~22 bits.
 //
 // Hot CTAs read the FP16 window with 128-bit loads and use the same MMA
 // layout with natural channel order.
@@ -50,16 +51,38 @@ struct DecodeParams {
   int B, Hq, Hkv, g, n_hg;
   float scale_log2;
   int warm_splits, hot_splits, wbps, hbps, splits;
-  float* ws_acc;
-  float* ws_ml;
+  float* ws;  // split partials: row (b*Hq + hq)*splits + split holds (acc[D], m, l)
   int* status;
 };
+
+// ------------------------------------------------------------------ exact fp16 dequantisation
+// x holds (1024 + M*c_a, 1024 + M*c_b) as fp16 (the LOP3 magic).  Fast form:
+// fp16(c*s) = fma(x, s/M, -1024*s/M) with one rounding, exact when s/M and
+// 1024*s/M are representable; then + zero.  Safe form for any scale:
+// c = fma(x, 1/M, -1024/M) (exact), fp16(c*s), + zero.
+AKV_DEV bool scale_is_fast(float s) { return s == 0.f || (s >= 0.015625f && s <= 63.9f); }
+
+template <int M>
+AKV_DEV uint32_t dq_fast(uint32_t x, __half2 s_over_m, __half2 neg1024s_over_m, __half2 z) {
+  return h2_as_u32(__hadd2_rn(__hfma2(u32_as_h2(x), s_over_m, neg1024s_over_m), z));
+}
+
+template <int M>
+AKV_DEV uint32_t dq_safe(uint32_t x, __half2 s, __half2 z) {
+  return h2_as_u32(__hadd2_rn(__hmul2_rn(u32_as_h2(fix_magic<M>(x)), s), z));
+}
+
+template <int M>
+AKV_DEV __half2 over_m(__half2 s) { return __hmul2(s, __float2half2_rn(1.0f / M)); }
+template <int M>
+AKV_DEV __half2 neg1024_over_m(__half2 s) { return __hmul2(s, __float2half2_rn(-1024.0f / M)); }
 
 // ------------------------------------------------------------------ K codes -> A fragments
 // Thread (g8, q4) holds, for one token row, the 32 codes of channel chunk q4
 // as 16 half2 "pairs"; pair i feeds k-step i/2, low (i even) or high k slots.
-// The channel order inside a chunk is permuted per bit width; the query
-// fragment uses the same permutation (kPairs*).
+// The channel order inside a chunk is permuted per bit width (kPairs*), with
+// the magic multiplier of each pair in kMult*; the query fragment uses the
+// same permutation.
 struct PairIdx {
   int a, b;
 };
@@ -73,40 +96,50 @@ __device__ constexpr PairIdx kPairs2[16] = {{3, 11},  {2, 10},  {1, 9},   {0, 8}
 __device__ constexpr PairIdx kPairs3[16] = {{7, 15},  {6, 14},  {5, 13},  {4, 12},  {3, 11},  {2, 10},
                                             {1, 9},   {0, 8},   {23, 31}, {22, 30}, {21, 29}, {20, 28},
                                             {19, 27}, {18, 26}, {17, 25}, {16, 24}};
+__device__ constexpr int kMult4[16] = {1, 16, 1, 16, 1, 16, 1, 16, 1, 16, 1, 16, 1, 16, 1, 16};
+__device__ constexpr int kMult2[16] = {1, 4, 16, 64, 256, 4, 16, 64, 1, 4, 16, 64, 256, 4, 16, 64};
+__device__ constexpr int kMult3[16] = {1, 8, 64, 1, 8, 1, 8, 64, 1, 8, 64, 1, 8, 1, 8, 64};
 
+// Lookups used only with compile-time indices (template recursion below), so
+// every pair permutation and magic multiplier is a constant in the code.
 template <int KB>
 AKV_DEV constexpr PairIdx kpair(int i) {
   return KB == 4 ? kPairs4[i] : (KB == 2 ? kPairs2[i] : kPairs3[i]);
 }
+template <int BITS>
+AKV_DEV constexpr int kmult(int i) {
+  return BITS == 4 ? kMult4[i] : (BITS == 2 ? kMult2[i] : kMult3[i]);
+}
 
-// 3-bit: two big-endian 24-bit groups (low 24 bits of wa, wb) -> 8 code pairs
-// ordered c7, c6, c5, c4, c3, c2, c1, c0 (pair = (code of wa, code of wb)).
-AKV_DEV void extract3_pair(uint32_t wa, uint32_t wb, uint32_t* e) {
+// 3-bit: two big-endian 24-bit groups (low 24 bits of wa, wb) -> 8 magic pairs
+// ordered c7, c6, c5, c4, c3, c2, c1, c0 (pair = (code of wa, code of wb)),
+// multipliers 1, 8, 64, 1, 8, 1, 8, 64.
+AKV_DEV void raw3_pair(uint32_t wa, uint32_t wb, uint32_t* e) {
   const uint32_t y = prmt(wa, wb, 0x5410);
-  e[0] = code_pair<0x00070007u, 1>(y);
-  e[1] = code_pair<0x00380038u, 8>(y);
-  e[2] = code_pair<0x01C001C0u, 64>(y);
+  e[0] = lop_magic<0x00070007u>(y);
+  e[1] = lop_magic<0x00380038u>(y);
+  e[2] = lop_magic<0x01C001C0u>(y);
   const uint32_t y9 = y >> 9;
-  e[3] = code_pair<0x00070007u, 1>(y9);
-  e[4] = code_pair<0x00380038u, 8>(y9);
+  e[3] = lop_magic<0x00070007u>(y9);
+  e[4] = lop_magic<0x00380038u>(y9);
   const uint32_t z = prmt(wa >> 15, wb >> 15, 0x5410);
-  e[5] = code_pair<0x00070007u, 1>(z);
-  e[6] = code_pair<0x00380038u, 8>(z);
-  e[7] = code_pair<0x01C001C0u, 64>(z);
+  e[5] = lop_magic<0x00070007u>(z);
+  e[6] = lop_magic<0x00380038u>(z);
+  e[7] = lop_magic<0x01C001C0u>(z);
 }
 
 template <int KB>
-AKV_DEV void k_row_pairs(const uint8_t* row, int q4, uint32_t (&e)[16]) {
+AKV_DEV void k_row_raw(const uint8_t* row, int q4, uint32_t (&e)[16]) {
   if constexpr (KB == 4) {
     const uint4 w = lds_v4(row + 16 * q4);
     const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const uint32_t x = ws[k], y = ws[k] >> 8;
-      e[4 * k + 0] = code_pair<0x000F000Fu, 1>(x);
-      e[4 * k + 1] = code_pair<0x00F000F0u, 16>(x);
-      e[4 * k + 2] = code_pair<0x000F000Fu, 1>(y);
-      e[4 * k + 3] = code_pair<0x00F000F0u, 16>(y);
+      e[4 * k + 0] = lop_magic<0x000F000Fu>(x);
+      e[4 * k + 1] = lop_magic<0x00F000F0u>(x);
+      e[4 * k + 2] = lop_magic<0x000F000Fu>(y);
+      e[4 * k + 3] = lop_magic<0x00F000F0u>(y);
     }
   } else if constexpr (KB == 2) {
     const uint2 w = lds_v2(row + 8 * q4);
@@ -114,31 +147,91 @@ AKV_DEV void k_row_pairs(const uint8_t* row, int q4, uint32_t (&e)[16]) {
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
       const uint32_t x = ws[k], y = ws[k] >> 8;
-      e[8 * k + 0] = code_pair<0x00030003u, 1>(x);
-      e[8 * k + 1] = code_pair<0x000C000Cu, 4>(x);
-      e[8 * k + 2] = code_pair<0x00300030u, 16>(x);
-      e[8 * k + 3] = code_pair<0x00C000C0u, 64>(x);
-      e[8 * k + 4] = code_pair<0x03000300u, 256>(x);
-      e[8 * k + 5] = code_pair<0x000C000Cu, 4>(y);
-      e[8 * k + 6] = code_pair<0x00300030u, 16>(y);
-      e[8 * k + 7] = code_pair<0x00C000C0u, 64>(y);
+      e[8 * k + 0] = lop_magic<0x00030003u>(x);
+      e[8 * k + 1] = lop_magic<0x000C000Cu>(x);
+      e[8 * k + 2] = lop_magic<0x00300030u>(x);
+      e[8 * k + 3] = lop_magic<0x00C000C0u>(x);
+      e[8 * k + 4] = lop_magic<0x03000300u>(x);
+      e[8 * k + 5] = lop_magic<0x000C000Cu>(y);
+      e[8 * k + 6] = lop_magic<0x00300030u>(y);
+      e[8 * k + 7] = lop_magic<0x00C000C0u>(y);
     }
   } else {
     const uint8_t* p = row + 12 * q4;
     const uint32_t w0 = lds_u32(p), w1 = lds_u32(p + 4), w2 = lds_u32(p + 8);
     const uint32_t g0 = prmt(w0, 0u, 0x4012), g1 = prmt(w0, w1, 0x3345);
     const uint32_t g2 = prmt(w1, w2, 0x2234), g3 = prmt(w2, 0u, 0x4123);
-    extract3_pair(g0, g1, e);
-    extract3_pair(g2, g3, e + 8);
+    raw3_pair(g0, g1, e);
+    raw3_pair(g2, g3, e + 8);
+  }
+}
+
+// Per-block channel constants of this thread's K chunk, in pair order.
+template <int KB>
+struct KConst {
+  __half2 a[16];  // fast: s/M      safe: s
+  __half2 c[16];  // fast: -1024s/M
+  __half2 z[16];
+  bool fast;
+};
+
+template <int KB, int I = 0>
+AKV_DEV void k_consts_fill(const __half (&s)[32], const __half (&z)[32], KConst<KB>& kc) {
+  if constexpr (I < 16) {
+    constexpr PairIdx pi = kpair<KB>(I);
+    constexpr int M = kmult<KB>(I);
+    const __half2 s2 = __halves2half2(s[pi.a], s[pi.b]);
+    kc.z[I] = __halves2half2(z[pi.a], z[pi.b]);
+    kc.a[I] = kc.fast ? over_m<M>(s2) : s2;
+    kc.c[I] = neg1024_over_m<M>(s2);
+    k_consts_fill<KB, I + 1>(s, z, kc);
+  }
+}
+
+template <int KB>
+AKV_DEV void k_consts(const __half* ks, const __half* kz, KConst<KB>& kc) {
+  __half s[32], z[32];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    *reinterpret_cast<uint4*>(s + 8 * k) = lds_v4(ks + 8 * k);
+    *reinterpret_cast<uint4*>(z + 8 * k) = lds_v4(kz + 8 * k);
+  }
+  bool fast = true;
+#pragma unroll
+  for (int k = 0; k < 32; ++k) fast &= scale_is_fast(__half2float(s[k]));
+  kc.fast = fast;
+  k_consts_fill<KB>(s, z, kc);
+}
+
+template <int KB, int I = 0>
+AKV_DEV void q_pairs(const __half (&qv)[32], uint32_t (&qp)[16]) {
+  if constexpr (I < 16) {
+    constexpr PairIdx pi = kpair<KB>(I);
+    qp[I] = h2_as_u32(__halves2half2(qv[pi.a], qv[pi.b]));
+    q_pairs<KB, I + 1>(qv, qp);
+  }
+}
+
+template <int BITS, int I>
+AKV_DEV uint32_t dq_pair(uint32_t x, __half2 a, __half2 c, __half2 z, bool fast) {
+  constexpr int M = kmult<BITS>(I);
+  return fast ? dq_fast<M>(x, a, c, z) : dq_safe<M>(x, a, z);
+}
+
+template <int KB, int I = 0>
+AKV_DEV void k_dequant(uint32_t (&e)[16], const KConst<KB>& kc) {
+  if constexpr (I < 16) {
+    e[I] = dq_pair<KB, I>(e[I], kc.a[I], kc.c[I], kc.z[I], kc.fast);
+    k_dequant<KB, I + 1>(e, kc);
   }
 }
 
 // ------------------------------------------------------------------ V codes -> A fragments
 // Thread group g8 owns channels [16*g8, 16*g8+16).  For a token pair (ta, tb)
-// produce e[ci] = (code_ta[ci], code_tb[ci]) for ci = 0..15.
+// produce e[ci] = (v_ta[ci], v_tb[ci]) dequantised, ci = 0..15.
 template <int VB>
 struct VRow {
-  uint32_t w[VB == 4 ? 2 : (VB == 3 ? 2 : 1)];
+  uint32_t w[VB == 2 ? 1 : 2];
 };
 
 template <int VB>
@@ -162,44 +255,65 @@ AKV_DEV VRow<VB> v_row_load(const uint8_t* row, int g8) {
   return r;
 }
 
+// raw magic pairs by channel index ci, plus each one's multiplier (compile time)
 template <int VB>
-AKV_DEV void v_pair_codes(const VRow<VB>& a, const VRow<VB>& b, uint32_t (&e)[16]) {
+constexpr int vmult(int ci) {
+  if (VB == 4) return (ci & 1) ? 1 : 16;
+  if (VB == 2) {
+    constexpr int m[8] = {64, 16, 4, 1, 64, 16, 4, 256};
+    return m[ci & 7];
+  }
+  constexpr int m3[8] = {64, 8, 1, 8, 1, 64, 8, 1};  // ci -> multiplier of code ci in raw3_pair order
+  return m3[ci & 7];
+}
+
+template <int VB>
+AKV_DEV void v_pair_raw(const VRow<VB>& a, const VRow<VB>& b, uint32_t (&e)[16]) {
   if constexpr (VB == 4) {
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
       const uint32_t x = prmt(a.w[k], b.w[k], 0x5410), y = prmt(a.w[k], b.w[k], 0x7632);
       const uint32_t x8 = x >> 8, y8 = y >> 8;
-      e[8 * k + 1] = code_pair<0x000F000Fu, 1>(x);
-      e[8 * k + 0] = code_pair<0x00F000F0u, 16>(x);
-      e[8 * k + 3] = code_pair<0x000F000Fu, 1>(x8);
-      e[8 * k + 2] = code_pair<0x00F000F0u, 16>(x8);
-      e[8 * k + 5] = code_pair<0x000F000Fu, 1>(y);
-      e[8 * k + 4] = code_pair<0x00F000F0u, 16>(y);
-      e[8 * k + 7] = code_pair<0x000F000Fu, 1>(y8);
-      e[8 * k + 6] = code_pair<0x00F000F0u, 16>(y8);
+      e[8 * k + 1] = lop_magic<0x000F000Fu>(x);
+      e[8 * k + 0] = lop_magic<0x00F000F0u>(x);
+      e[8 * k + 3] = lop_magic<0x000F000Fu>(x8);
+      e[8 * k + 2] = lop_magic<0x00F000F0u>(x8);
+      e[8 * k + 5] = lop_magic<0x000F000Fu>(y);
+      e[8 * k + 4] = lop_magic<0x00F000F0u>(y);
+      e[8 * k + 7] = lop_magic<0x000F000Fu>(y8);
+      e[8 * k + 6] = lop_magic<0x00F000F0u>(y8);
     }
   } else if constexpr (VB == 2) {
     const uint32_t xs[2] = {prmt(a.w[0], b.w[0], 0x5410), prmt(a.w[0], b.w[0], 0x7632)};
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
       const uint32_t x = xs[k], x8 = xs[k] >> 8;
-      e[8 * k + 3] = code_pair<0x00030003u, 1>(x);
-      e[8 * k + 2] = code_pair<0x000C000Cu, 4>(x);
-      e[8 * k + 1] = code_pair<0x00300030u, 16>(x);
-      e[8 * k + 0] = code_pair<0x00C000C0u, 64>(x);
-      e[8 * k + 7] = code_pair<0x03000300u, 256>(x);
-      e[8 * k + 6] = code_pair<0x000C000Cu, 4>(x8);
-      e[8 * k + 5] = code_pair<0x00300030u, 16>(x8);
-      e[8 * k + 4] = code_pair<0x00C000C0u, 64>(x8);
+      e[8 * k + 3] = lop_magic<0x00030003u>(x);
+      e[8 * k + 2] = lop_magic<0x000C000Cu>(x);
+      e[8 * k + 1] = lop_magic<0x00300030u>(x);
+      e[8 * k + 0] = lop_magic<0x00C000C0u>(x);
+      e[8 * k + 7] = lop_magic<0x03000300u>(x);
+      e[8 * k + 6] = lop_magic<0x000C000Cu>(x8);
+      e[8 * k + 5] = lop_magic<0x00300030u>(x8);
+      e[8 * k + 4] = lop_magic<0x00C000C0u>(x8);
     }
   } else {
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
       uint32_t t[8];
-      extract3_pair(a.w[k], b.w[k], t);
+      raw3_pair(a.w[k], b.w[k], t);
 #pragma unroll
       for (int j = 0; j < 8; ++j) e[8 * k + 7 - j] = t[j];
     }
+  }
+}
+
+template <int VB, int CI = 0>
+AKV_DEV void v_dequant(uint32_t (&e)[16], __half2 s2, __half2 z2, bool fast) {
+  if constexpr (CI < 16) {
+    constexpr int M = vmult<VB>(CI);
+    e[CI] = fast ? dq_fast<M>(e[CI], over_m<M>(s2), neg1024_over_m<M>(s2), z2) : dq_safe<M>(e[CI], s2, z2);
+    v_dequant<VB, CI + 1>(e, s2, z2, fast);
   }
 }
 
@@ -223,7 +337,6 @@ struct WarpState {
   float acc[8][4];  // O^T: tile mt rows (g8 -> d=16*g8+2mt, g8+8 -> d+1), cols heads (2q4, 2q4+1)
   float m[2];       // running max (log2 units) for heads 2q4, 2q4+1
   float l[2];       // partial row sums (this thread's tokens only)
-  float vb[2];      // partial sum_t p_t * zero_V,t (warm only)
 };
 
 AKV_DEV void state_init(WarpState& s) {
@@ -233,7 +346,6 @@ AKV_DEV void state_init(WarpState& s) {
     for (int j = 0; j < 4; ++j) s.acc[i][j] = 0.f;
   s.m[0] = s.m[1] = -INFINITY;
   s.l[0] = s.l[1] = 0.f;
-  s.vb[0] = s.vb[1] = 0.f;
 }
 
 // x[mt][4]: scaled logits (log2 units, -inf = masked) of this thread's 4
@@ -255,7 +367,6 @@ AKV_DEV void online_softmax(WarpState& s, float (&x)[2][4]) {
     alpha[h] = fast_exp2(s.m[h] - base[h]);
     s.m[h] = mn;
     s.l[h] *= alpha[h];
-    s.vb[h] *= alpha[h];
   }
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
@@ -273,6 +384,20 @@ AKV_DEV void online_softmax(WarpState& s, float (&x)[2][4]) {
     }
 }
 
+// P (fp32, S^T C-fragment layout) -> B fragments of the PV MMA as fp16 hi + lo.
+AKV_DEV void p_fragments(const float (&x)[2][4], uint32_t (&ph)[2][2], uint32_t (&pl)[2][2]) {
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const __half2 hi = __floats2half2_rn(x[mt][2 * r], x[mt][2 * r + 1]);
+      const float2 hf = __half22float2(hi);
+      const __half2 lo = __floats2half2_rn(x[mt][2 * r] - hf.x, x[mt][2 * r + 1] - hf.y);
+      ph[mt][r] = movmatrix_trans(h2_as_u32(hi));
+      pl[mt][r] = movmatrix_trans(h2_as_u32(lo));
+    }
+}
+
 // ------------------------------------------------------------------ epilogue
 // Reduce the per-thread partials of one warp and park them in shared memory:
 // red[h][d] (fp32, natural channel order), rm[h], rl[h].
@@ -281,17 +406,14 @@ AKV_DEV void warp_to_smem(WarpState& s, int lane, float* red, float* rm, float* 
 #pragma unroll
   for (int h = 0; h < 2; ++h)
 #pragma unroll
-    for (int o = 4; o < 32; o <<= 1) {
-      s.l[h] += __shfl_xor_sync(0xffffffffu, s.l[h], o);
-      s.vb[h] += __shfl_xor_sync(0xffffffffu, s.vb[h], o);
-    }
+    for (int o = 4; o < 32; o <<= 1) s.l[h] += __shfl_xor_sync(0xffffffffu, s.l[h], o);
 #pragma unroll
   for (int mt = 0; mt < 8; ++mt) {
     const int d = 16 * g8 + 2 * mt;
-    red[(2 * q4) * kHeadDim + d] = s.acc[mt][0] + s.vb[0];
-    red[(2 * q4 + 1) * kHeadDim + d] = s.acc[mt][1] + s.vb[1];
-    red[(2 * q4) * kHeadDim + d + 1] = s.acc[mt][2] + s.vb[0];
-    red[(2 * q4 + 1) * kHeadDim + d + 1] = s.acc[mt][3] + s.vb[1];
+    red[(2 * q4) * kHeadDim + d] = s.acc[mt][0];
+    red[(2 * q4 + 1) * kHeadDim + d] = s.acc[mt][1];
+    red[(2 * q4) * kHeadDim + d + 1] = s.acc[mt][2];
+    red[(2 * q4 + 1) * kHeadDim + d + 1] = s.acc[mt][3];
   }
   if (g8 == 0) {
     rm[2 * q4] = s.m[0];
@@ -319,11 +441,11 @@ AKV_DEV void cta_write_partial(const DecodeParams& p, float* red, float* rm, flo
       L += f * rl[w * 8 + h];
     }
     const int hq = kvh * p.g + hg * 8 + h;
-    const int64_t row = (static_cast<int64_t>(b) * p.Hq + hq) * p.splits + split;
-    p.ws_acc[row * kHeadDim + d] = acc;
+    float* part = p.ws + ((static_cast<int64_t>(b) * p.Hq + hq) * p.splits + split) * (kHeadDim + 2);
+    part[d] = acc;
     if (d == 0) {
-      p.ws_ml[row * 2] = M;
-      p.ws_ml[row * 2 + 1] = L;
+      part[kHeadDim] = M;
+      part[kHeadDim + 1] = L;
     }
   }
 }
@@ -390,18 +512,22 @@ __global__ void __launch_bounds__(kDecodeThreads) mixed_decode_kernel(const Deco
     if (warp == kConsumerWarps) {
       // ---------------- producer: one lane streams records into the ring
       if (lane == 0) {
+        int issued = 0;
         for (int i = 0; i < nb; ++i) {
           const int s = i % kStages;
           if (i >= kStages && !mbar_wait(&empty[s], ((i / kStages) - 1) & 1, p.status)) break;
           mbar_arrive_expect_tx(&full[s], rec);
           tma_load_1d(stage0 + s * rec, wbase + static_cast<int64_t>(i) * rec, rec, &full[s]);
+          issued = i + 1;
         }
+        // drain: every issued copy has landed before the ring memory is reused
+        for (int i = max(0, issued - kStages); i < issued; ++i)
+          mbar_wait(&full[i % kStages], (i / kStages) & 1, p.status);
       }
     } else {
       // ---------------- consumers
-      __half2 qp[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) qp[i] = __halves2half2(qv[kpair<KB>(i).a], qv[kpair<KB>(i).b]);
+      uint32_t qp[16];
+      q_pairs<KB>(qv, qp);
       const int n_out = p.L.n_outlier;
       const int kp = kHeadDim * KB / 8, vp = kHeadDim * VB / 8;
 
@@ -411,53 +537,32 @@ __global__ void __launch_bounds__(kDecodeThreads) mixed_decode_kernel(const Deco
         const uint8_t* r = stage0 + s * rec;
         const uint8_t* kc = r + p.L.kc;
         const uint8_t* vc = r + p.L.vc;
-        const __half* ksc = reinterpret_cast<const __half*>(r + p.L.ks) + 32 * q4;
-        const __half* kzr = reinterpret_cast<const __half*>(r + p.L.kz) + 32 * q4;
         const __half* vsc = reinterpret_cast<const __half*>(r + p.L.vs);
         const __half* vzr = reinterpret_cast<const __half*>(r + p.L.vz);
         const uint32_t mask = lds_u32(r + p.L.mask);
 
-        // q~ = q * s_K (hi + lo fp16 parts) and the zero-point bias q . z_K
-        __half sk[32], zk[32];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          *reinterpret_cast<uint4*>(sk + 8 * k) = lds_v4(ksc + 8 * k);
-          *reinterpret_cast<uint4*>(zk + 8 * k) = lds_v4(kzr + 8 * k);
-        }
-        uint32_t qhi[16], qlo[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const __half2 s2 = __halves2half2(sk[kpair<KB>(j).a], sk[kpair<KB>(j).b]);
-          const __half2 hi = __hmul2(qp[j], s2);
-          const __half2 lo = __hfma2(qp[j], s2, __hneg2(hi));
-          qhi[j] = h2_as_u32(hi);
-          qlo[j] = h2_as_u32(lo);
-        }
-        float zb = 0.f;
-#pragma unroll
-        for (int k = 0; k < 32; ++k) zb = fmaf(__half2float(qv[k]), __half2float(zk[k]), zb);
-        zb += __shfl_xor_sync(0xffffffffu, zb, 1);
-        zb += __shfl_xor_sync(0xffffffffu, zb, 2);
-        const float bias0 = __shfl_sync(0xffffffffu, zb, 8 * q4);      // head 2q4 lives in lanes 4*(2q4)+x
-        const float bias1 = __shfl_sync(0xffffffffu, zb, 8 * q4 + 4);  // head 2q4+1
+        KConst<KB> kcst;
+        k_consts<KB>(reinterpret_cast<const __half*>(r + p.L.ks) + 32 * q4,
+                     reinterpret_cast<const __half*>(r + p.L.kz) + 32 * q4, kcst);
 
-        // ---- S^T = K~ q~  (tokens x heads), 2 m-tiles of 16 tokens
+        // ---- S^T = K^ q  (tokens x heads), 2 m-tiles of 16 tokens
         float x[2][4];
 #pragma unroll
         for (int mt = 0; mt < 2; ++mt) {
           uint32_t e0[16], e1[16];
-          k_row_pairs<KB>(kc + (16 * mt + g8) * kp, q4, e0);
-          k_row_pairs<KB>(kc + (16 * mt + g8 + 8) * kp, q4, e1);
+          k_row_raw<KB>(kc + (16 * mt + g8) * kp, q4, e0);
+          k_row_raw<KB>(kc + (16 * mt + g8 + 8) * kp, q4, e1);
+          k_dequant<KB>(e0, kcst);
+          k_dequant<KB>(e1, kcst);
           float c[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-          for (int ks = 0; ks < 8; ++ks) {
-            mma_16816(c, e0[2 * ks], e1[2 * ks], e0[2 * ks + 1], e1[2 * ks + 1], qhi[2 * ks], qhi[2 * ks + 1]);
-            mma_16816(c, e0[2 * ks], e1[2 * ks], e0[2 * ks + 1], e1[2 * ks + 1], qlo[2 * ks], qlo[2 * ks + 1]);
-          }
+          for (int ks = 0; ks < 8; ++ks)
+            mma_16816(c, e0[2 * ks], e1[2 * ks], e0[2 * ks + 1], e1[2 * ks + 1], qp[2 * ks], qp[2 * ks + 1]);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) x[mt][j] = c[j] + ((j & 1) ? bias1 : bias0);
+          for (int j = 0; j < 4; ++j) x[mt][j] = c[j];
         }
-        // K outlier channels: exact fp16 originals (scale/zero of those channels are 0)
+        // K outlier channels: the dequantised value there is 0 (scale = zero = 0);
+        // the reference overwrites it with the fp16 original.
         for (int j = 0; j < n_out; ++j) {
           const int d_o = reinterpret_cast<const int16_t*>(r + p.L.ki)[j];
           const float qa = qs[(2 * q4) * kHeadDim + d_o], qb = qs[(2 * q4 + 1) * kHeadDim + d_o];
@@ -482,44 +587,40 @@ __global__ void __launch_bounds__(kDecodeThreads) mixed_decode_kernel(const Deco
               x[mt][2 * rr + h] = valid[mt][rr] ? x[mt][2 * rr + h] * p.scale_log2 : -INFINITY;
           }
         online_softmax(st, x);
+        uint32_t ph[2][2], pl[2][2];
+        p_fragments(x, ph, pl);
 
-        // ---- fold the per-token V scale into p, collect the zero-point sum
-        float pt[2][4];
-        uint32_t pb[2][2];
-#pragma unroll
-        for (int mt = 0; mt < 2; ++mt) {
-#pragma unroll
-          for (int rr = 0; rr < 2; ++rr) {
-            const int t = 16 * mt + 8 * rr + g8;
-            const float sv = __half2float(vsc[t]), zv = __half2float(vzr[t]);
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const float pv = x[mt][2 * rr + h];
-              pt[mt][2 * rr + h] = valid[mt][rr] ? pv * sv : 0.f;
-              st.vb[h] += valid[mt][rr] ? pv * zv : 0.f;
-            }
-          }
-          pb[mt][0] = movmatrix_trans(pack_h2(pt[mt][0], pt[mt][1]));
-          pb[mt][1] = movmatrix_trans(pack_h2(pt[mt][2], pt[mt][3]));
-        }
-
-        // ---- O^T += V^T p~  (head_dim x heads), k-steps of 16 tokens
+        // ---- O^T += V^ P  (head_dim x heads), k-steps of 16 tokens
 #pragma unroll
         for (int ks = 0; ks < 2; ++ks) {
           const int ta = 16 * ks + 2 * q4;
-          const VRow<VB> ra = v_row_load<VB>(vc + ta * vp, g8);
-          const VRow<VB> rb = v_row_load<VB>(vc + (ta + 1) * vp, g8);
-          const VRow<VB> rc = v_row_load<VB>(vc + (ta + 8) * vp, g8);
-          const VRow<VB> rd = v_row_load<VB>(vc + (ta + 9) * vp, g8);
           uint32_t e0[16], e1[16];
-          v_pair_codes<VB>(ra, rb, e0);
-          v_pair_codes<VB>(rc, rd, e1);
+          {
+            const VRow<VB> ra = v_row_load<VB>(vc + ta * vp, g8);
+            const VRow<VB> rb = v_row_load<VB>(vc + (ta + 1) * vp, g8);
+            v_pair_raw<VB>(ra, rb, e0);
+            const __half2 s2 = __halves2half2(vsc[ta], vsc[ta + 1]);
+            const __half2 z2 = __halves2half2(vzr[ta], vzr[ta + 1]);
+            const bool fast = scale_is_fast(__low2float(s2)) && scale_is_fast(__high2float(s2));
+            v_dequant<VB>(e0, s2, z2, fast);
+          }
+          {
+            const VRow<VB> rc = v_row_load<VB>(vc + (ta + 8) * vp, g8);
+            const VRow<VB> rd = v_row_load<VB>(vc + (ta + 9) * vp, g8);
+            v_pair_raw<VB>(rc, rd, e1);
+            const __half2 s2 = __halves2half2(vsc[ta + 8], vsc[ta + 9]);
+            const __half2 z2 = __halves2half2(vzr[ta + 8], vzr[ta + 9]);
+            const bool fast = scale_is_fast(__low2float(s2)) && scale_is_fast(__high2float(s2));
+            v_dequant<VB>(e1, s2, z2, fast);
+          }
 #pragma unroll
-          for (int mt = 0; mt < 8; ++mt)
-            mma_16816(st.acc[mt], e0[2 * mt], e0[2 * mt + 1], e1[2 * mt], e1[2 * mt + 1], pb[ks][0], pb[ks][1]);
+          for (int mt = 0; mt < 8; ++mt) {
+            mma_16816(st.acc[mt], e0[2 * mt], e0[2 * mt + 1], e1[2 * mt], e1[2 * mt + 1], ph[ks][0], ph[ks][1]);
+            mma_16816(st.acc[mt], e0[2 * mt], e0[2 * mt + 1], e1[2 * mt], e1[2 * mt + 1], pl[ks][0], pl[ks][1]);
+          }
         }
 
-        // ---- V outlier channels: replace what the codes contributed by the fp16 originals
+        // ---- V outlier channels: replace the dequantised code value by the fp16 original
         for (int j = 0; j < n_out; ++j) {
           const int d_o = reinterpret_cast<const int16_t*>(r + p.L.vi)[j];
           const __half* od = reinterpret_cast<const __half*>(r + p.L.vo);
@@ -530,13 +631,11 @@ __global__ void __launch_bounds__(kDecodeThreads) mixed_decode_kernel(const Deco
             for (int rr = 0; rr < 2; ++rr) {
               if (!valid[mt][rr]) continue;
               const int t = 16 * mt + 8 * rr + g8;
-              const float c = static_cast<float>(code_at<VB>(vc + t * vp, d_o));
-              const float ov = __half2float(od[t * n_out + j]) - __half2float(vzr[t]);
+              const __half cv = __uint2half_rn(code_at<VB>(vc + t * vp, d_o));
+              const float deq = __half2float(__hadd_rn(__hmul_rn(cv, vsc[t]), vzr[t]));
+              const float diff = __half2float(od[t * n_out + j]) - deq;
 #pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                const float ptr = __half2float(__float2half_rn(pt[mt][2 * rr + h]));
-                corr[h] += x[mt][2 * rr + h] * ov - ptr * c;
-              }
+              for (int h = 0; h < 2; ++h) corr[h] = fmaf(x[mt][2 * rr + h], diff, corr[h]);
             }
 #pragma unroll
           for (int o = 4; o < 32; o <<= 1) {
@@ -602,12 +701,8 @@ __global__ void __launch_bounds__(kDecodeThreads) mixed_decode_kernel(const Deco
           for (int j = 0; j < 4; ++j) x[mt][j] = valid[mt][j >> 1] ? c[j] * p.scale_log2 : -INFINITY;
         }
         online_softmax(st, x);
-        uint32_t pb[2][2];
-#pragma unroll
-        for (int mt = 0; mt < 2; ++mt) {
-          pb[mt][0] = movmatrix_trans(pack_h2(x[mt][0], x[mt][1]));
-          pb[mt][1] = movmatrix_trans(pack_h2(x[mt][2], x[mt][3]));
-        }
+        uint32_t ph[2][2], pl[2][2];
+        p_fragments(x, ph, pl);
 #pragma unroll
         for (int ks = 0; ks < 2; ++ks) {
           uint32_t va[4][8];
@@ -628,7 +723,8 @@ __global__ void __launch_bounds__(kDecodeThreads) mixed_decode_kernel(const Deco
             const uint32_t a1 = prmt(va[0][mt], va[1][mt], 0x7632);  // (ta, tb) at channel 2mt+1
             const uint32_t a2 = prmt(va[2][mt], va[3][mt], 0x5410);
             const uint32_t a3 = prmt(va[2][mt], va[3][mt], 0x7632);
-            mma_16816(st.acc[mt], a0, a1, a2, a3, pb[ks][0], pb[ks][1]);
+            mma_16816(st.acc[mt], a0, a1, a2, a3, ph[ks][0], ph[ks][1]);
+            mma_16816(st.acc[mt], a0, a1, a2, a3, pl[ks][0], pl[ks][1]);
           }
         }
       }
@@ -644,24 +740,34 @@ __global__ void __launch_bounds__(kDecodeThreads) mixed_decode_kernel(const Deco
 }
 
 // ------------------------------------------------------------------ LSE combine
-__global__ void lse_combine_kernel(const float* acc, const float* ml, int rows, int splits, int D, __half* out,
-                                   int64_t o_sr, float* lse) {
+// Partial record of one (row, split): (acc[D], m, l) with acc unnormalised and
+// relative to m (log2 units).  Row r, split s lives at part + s*ss + r*sr.
+// Writes any of: fp16 out[r*o_sr + d], natural-log lse[r], and the merged
+// partial record merged[r*(D+2) + ...] (for a further cross-GPU combine).
+__global__ void lse_combine_kernel(const float* __restrict__ part, int64_t ss, int64_t sr, int rows, int splits,
+                                   int D, __half* out, int64_t o_sr, float* lse, float* merged) {
   const int r = blockIdx.x;
   if (r >= rows) return;
-  const float* a = acc + static_cast<int64_t>(r) * splits * D;
-  const float* m = ml + static_cast<int64_t>(r) * splits * 2;
+  const float* base = part + static_cast<int64_t>(r) * sr;
   float M = -INFINITY;
-  for (int s = 0; s < splits; ++s) M = fmaxf(M, m[2 * s]);
-  const float base = (M == -INFINITY) ? 0.f : M;
+  for (int s = 0; s < splits; ++s) M = fmaxf(M, base[s * ss + D]);
+  const float mb = (M == -INFINITY) ? 0.f : M;
   float L = 0.f;
-  for (int s = 0; s < splits; ++s) L += m[2 * s + 1] * exp2f(m[2 * s] - base);
+  for (int s = 0; s < splits; ++s) L += base[s * ss + D + 1] * exp2f(base[s * ss + D] - mb);
   const float inv = L > 0.f ? 1.f / L : 0.f;
   for (int d = threadIdx.x; d < D; d += blockDim.x) {
     float o = 0.f;
-    for (int s = 0; s < splits; ++s) o += a[static_cast<int64_t>(s) * D + d] * exp2f(m[2 * s] - base);
-    out[static_cast<int64_t>(r) * o_sr + d] = __float2half_rn(o * inv);
+    for (int s = 0; s < splits; ++s) o += base[s * ss + d] * exp2f(base[s * ss + D] - mb);
+    if (out) out[static_cast<int64_t>(r) * o_sr + d] = __float2half_rn(o * inv);
+    if (merged) merged[static_cast<int64_t>(r) * (D + 2) + d] = o;
   }
-  if (lse && threadIdx.x == 0) lse[r] = L > 0.f ? (M + log2f(L)) / kLog2e : -INFINITY;
+  if (threadIdx.x == 0) {
+    if (lse) lse[r] = L > 0.f ? (M + log2f(L)) / kLog2e : -INFINITY;
+    if (merged) {
+      merged[static_cast<int64_t>(r) * (D + 2) + D] = M;
+      merged[static_cast<int64_t>(r) * (D + 2) + D + 1] = L;
+    }
+  }
 }
 
 // ------------------------------------------------------------------ host side
@@ -737,15 +843,16 @@ extern "C" int akv_mixed_decode(const uint16_t* q, int64_t q_sb, int64_t q_sh, c
                                 const int32_t* hot_len, const uint8_t* warm, int64_t w_sb, int64_t w_sh,
                                 const akv_warm_layout* layout, int n_warm_blocks, const int32_t* warm_len, int B,
                                 int Hq, int Hkv, int D, float sm_scale, uint16_t* out, int64_t o_sb,
-                                int64_t o_sh, float* lse, void* workspace, size_t workspace_bytes, int* status,
-                                void* stream) {
-  if (!q || !out) return AKV_ERR_NULL;
+                                int64_t o_sh, float* lse, float* partial_out, void* workspace,
+                                size_t workspace_bytes, int* status, void* stream) {
+  if (!q || (!out && !partial_out)) return AKV_ERR_NULL;
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || n_hot < 0 || n_warm_blocks < 0) return AKV_ERR_SHAPE;
   if (D != kHeadDim) return AKV_ERR_UNSUPPORTED;
   if (n_hot > 0 && (!hot_k || !hot_v)) return AKV_ERR_NULL;
   if (n_warm_blocks > 0 && (!warm || !layout)) return AKV_ERR_NULL;
   auto al = [](const void* ptr, int a) { return (reinterpret_cast<uintptr_t>(ptr) % a) == 0; };
-  if (!al(q, 16) || q_sb % 8 || q_sh % 8 || !al(out, 4) || o_sb % 2 || o_sh % 2) return AKV_ERR_ALIGN;
+  if (!al(q, 16) || q_sb % 8 || q_sh % 8) return AKV_ERR_ALIGN;
+  if (out && (!al(out, 2) || o_sb != static_cast<int64_t>(Hq) * o_sh)) return AKV_ERR_UNSUPPORTED;
   if (n_hot > 0 && (!al(hot_k, 16) || !al(hot_v, 16) || h_sb % 8 || h_sh % 8 || h_sn % 8)) return AKV_ERR_ALIGN;
   akv_warm_layout L{};
   if (n_warm_blocks > 0) {
@@ -762,15 +869,13 @@ extern "C" int akv_mixed_decode(const uint16_t* q, int64_t q_sb, int64_t q_sh, c
   const size_t need = static_cast<size_t>(B) * Hq * splits * (D + 2) * sizeof(float);
   if (workspace_bytes < need || !al(workspace, 16)) return AKV_ERR_WORKSPACE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  float* ws_acc = static_cast<float*>(workspace);
-  float* ws_ml = ws_acc + static_cast<size_t>(B) * Hq * splits * D;
-  if (pl.splits == 0) {  // no tokens at all: output zeros
-    if (cudaMemsetAsync(ws_acc, 0, need, st) != cudaSuccess) return AKV_ERR_LAUNCH;
-    lse_combine_kernel<<<B * Hq, 128, 0, st>>>(ws_acc, ws_ml, B * Hq, 1, D, reinterpret_cast<__half*>(out),
-                                               o_sh, lse);
+  float* ws = static_cast<float*>(workspace);
+  __half* outh = reinterpret_cast<__half*>(out);
+  if (pl.splits == 0) {  // no tokens at all: a zeroed partial (m = 0, l = 0) combines to output 0, lse -inf
+    if (cudaMemsetAsync(ws, 0, need, st) != cudaSuccess) return AKV_ERR_LAUNCH;
+    lse_combine_kernel<<<B * Hq, 128, 0, st>>>(ws, D + 2, D + 2, B * Hq, 1, D, outh, o_sh, lse, partial_out);
     return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_LAUNCH;
   }
-  if (o_sb != static_cast<int64_t>(Hq) * o_sh) return AKV_ERR_UNSUPPORTED;  // combine walks rows as b*Hq + h
   DecodeParams p{};
   p.q = reinterpret_cast<const __half*>(q);
   p.q_sb = q_sb;
@@ -799,8 +904,7 @@ extern "C" int akv_mixed_decode(const uint16_t* q, int64_t q_sb, int64_t q_sh, c
   p.wbps = pl.wbps;
   p.hbps = pl.hbps;
   p.splits = pl.splits;
-  p.ws_acc = ws_acc;
-  p.ws_ml = ws_ml;
+  p.ws = ws;
   p.status = status;
   int rc;
   const int kb = n_warm_blocks > 0 ? L.key_bits : 4, vb = n_warm_blocks > 0 ? L.value_bits : 4;
@@ -816,16 +920,16 @@ extern "C" int akv_mixed_decode(const uint16_t* q, int64_t q_sb, int64_t q_sh, c
     default: rc = launch_decode<4, 4>(p, st); break;
   }
   if (rc != AKV_OK) return rc;
-  lse_combine_kernel<<<B * Hq, 128, 0, st>>>(ws_acc, ws_ml, B * Hq, pl.splits, D, reinterpret_cast<__half*>(out),
-                                             o_sh, lse);
+  lse_combine_kernel<<<B * Hq, 128, 0, st>>>(ws, D + 2, static_cast<int64_t>(pl.splits) * (D + 2), B * Hq,
+                                             pl.splits, D, outh, o_sh, lse, partial_out);
   return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_LAUNCH;
 }
 
-extern "C" int akv_lse_combine(const float* acc, const float* ml, int rows, int splits, int D, uint16_t* out,
-                               int64_t o_sr, float* lse, void* stream) {
-  if (!acc || !ml || !out) return AKV_ERR_NULL;
-  if (rows <= 0 || splits <= 0 || D <= 0) return AKV_ERR_SHAPE;
+extern "C" int akv_lse_combine(const float* part, int64_t part_ss, int64_t part_sr, int rows, int splits, int D,
+                               uint16_t* out, int64_t o_sr, float* lse, float* merged, void* stream) {
+  if (!part || (!out && !lse && !merged)) return AKV_ERR_NULL;
+  if (rows <= 0 || splits <= 0 || D <= 0 || part_ss < 0 || part_sr < 0) return AKV_ERR_SHAPE;
   lse_combine_kernel<<<rows, 128, 0, static_cast<cudaStream_t>(stream)>>>(
-      acc, ml, rows, splits, D, reinterpret_cast<__half*>(out), o_sr, lse);
+      part, part_ss, part_sr, rows, splits, D, reinterpret_cast<__half*>(out), o_sr, lse, merged);
   return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_LAUNCH;
 }

@@ -401,12 +401,12 @@ __global__ void dequantize_kernel(const DequantParams p) {
       const __half* sc = reinterpret_cast<const __half*>(vaddr(p.src.scale, b, h, blk, 0)) + su * 32;
       const __half* zr = reinterpret_cast<const __half*>(vaddr(p.src.zero, b, h, blk, 0)) + su * 32;
 #pragma unroll
-      for (int k = 0; k < 32; ++k) o[k] = __hadd(__hmul(__uint2half_rn(c[k]), sc[k]), zr[k]);
+      for (int k = 0; k < 32; ++k) o[k] = __hadd_rn(__hmul_rn(__uint2half_rn(c[k]), sc[k]), zr[k]);
     } else {
       const __half sc = *reinterpret_cast<const __half*>(vaddr(p.src.scale, b, h, blk, slot));
       const __half zr = *reinterpret_cast<const __half*>(vaddr(p.src.zero, b, h, blk, slot));
 #pragma unroll
-      for (int k = 0; k < 32; ++k) o[k] = __hadd(__hmul(__uint2half_rn(c[k]), sc), zr);
+      for (int k = 0; k < 32; ++k) o[k] = __hadd_rn(__hmul_rn(__uint2half_rn(c[k]), sc), zr);
     }
     if (p.n_out > 0) {
       const int16_t* ids = reinterpret_cast<const int16_t*>(vaddr(p.src.out_idx, b, h, blk, 0));

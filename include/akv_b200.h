@@ -152,8 +152,12 @@ int akv_dequantize(const akv_qdest* src, const int64_t* tok_idx, int64_t tok_sb,
  *   warm_len     optional int32[B] warm blocks per row (NULL = n_warm_blocks for all);
  *                token validity inside a block comes from the record mask
  *   Hq % Hkv == 0 (GQA: q head h reads KV head h / (Hq/Hkv))
- *   out          fp16 (b, hq, d) at out + b*o_sb + hq*o_sh + d
+ *   out          fp16 (b, hq, d) at out + b*o_sb + hq*o_sh + d, o_sb == Hq*o_sh
+ *                (NULL allowed when partial_out is given)
  *   lse          optional fp32 [B*Hq] natural-log LSE of the scaled logits
+ *   partial_out  optional fp32 [B*Hq][D+2] partial record (acc[D], m, l) of the
+ *                tokens this call saw (acc unnormalised, relative to m in log2
+ *                units) for a cross-GPU sequence split; merge with akv_lse_combine
  *   workspace    device scratch of at least akv_decode_workspace_bytes(...) bytes
  * ---------------------------------------------------------------------- */
 size_t akv_decode_workspace_bytes(int B, int Hq, int Hkv, int D, int n_hot, int n_warm_blocks);
@@ -164,15 +168,16 @@ int akv_mixed_decode(const uint16_t* q, int64_t q_sb, int64_t q_sh,
                      const uint8_t* warm, int64_t w_sb, int64_t w_sh, const akv_warm_layout* layout,
                      int n_warm_blocks, const int32_t* warm_len,
                      int B, int Hq, int Hkv, int D, float sm_scale,
-                     uint16_t* out, int64_t o_sb, int64_t o_sh, float* lse,
+                     uint16_t* out, int64_t o_sb, int64_t o_sh, float* lse, float* partial_out,
                      void* workspace, size_t workspace_bytes, int* status, void* stream);
 
-/* Log-sum-exp combine of split partials (also used across GPUs for a
- * sequence split).  acc fp32 [rows][splits][D] (unnormalised, relative to m),
- * ml fp32 [rows][splits][2] = (m in log2 units, l).  Writes fp16 out[rows][D]
- * (row r at out + r*o_sr) and optional lse[rows] (natural log). */
-int akv_lse_combine(const float* acc, const float* ml, int rows, int splits, int D,
-                    uint16_t* out, int64_t o_sr, float* lse, void* stream);
+/* Log-sum-exp combine of partial records (acc[D], m, l) — the split-K merge
+ * inside one GPU and the merge of a sequence split across GPUs.  Record of
+ * row r, split s at part + s*part_ss + r*part_sr (floats).  Writes any of:
+ * fp16 out (row r at out + r*o_sr), natural-log lse[rows], and the merged
+ * record merged[rows][D+2]. */
+int akv_lse_combine(const float* part, int64_t part_ss, int64_t part_sr, int rows, int splits, int D,
+                    uint16_t* out, int64_t o_sr, float* lse, float* merged, void* stream);
 
 /* ------------------------------------------------------------------------
  * A6: importance update.  Replaces triton_ops.fused_importance_update

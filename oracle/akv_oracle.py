@@ -218,8 +218,8 @@ def quantize_values(v: np.ndarray, bits: int, outlier_fraction: float = 0.0, pac
 
 def _dequant(q: dict) -> np.ndarray:
     """affine_quantizer.py:112-124 / :178-189 — fp16 multiply, then fp16 add (no FMA)."""
-    codes = q["codes"]
-    if q["bits"] in (2, 3, 4):
+    codes = np.asarray(q["codes"])
+    if q["bits"] in (2, 3, 4) and codes.shape[-1] != q["orig_dim"]:  # packed=True layout
         codes = unpack(codes, q["bits"], q["orig_dim"])
     c = _f(codes.astype(F16))
     with np.errstate(invalid="ignore", over="ignore"):  # 0 * inf -> NaN, as in torch

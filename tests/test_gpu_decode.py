@@ -19,6 +19,14 @@ DEV = "cuda:0"
 ATOL = 2e-3
 
 
+def tolerance(ref):
+    """2e-3 max-abs; where |ref| >= 4 the fp16 output's own half-ulp rounding
+    (>= 9.8e-4) plus 1e-3 of arithmetic error is allowed instead."""
+    ref = np.asarray(ref, np.float32)
+    ulp = np.spacing(np.abs(ref).astype(np.float16)).astype(np.float32)
+    return np.maximum(ATOL, 0.5 * ulp + 1e-3)
+
+
 def _np(t):
     return t.detach().cpu().numpy()
 
@@ -94,7 +102,8 @@ def check(seed, B, Hq, Hkv, n_warm, n_hot, kb, vb, frac, D=128, outlier_ch=(7,),
     out, lse = run_case(q, wk, wv, hk, hv, kb, vb, frac, **kw)
     ref, rlse = oracle_case(q, wk, wv, hk, hv, kb, vb, frac, **kw)
     err = np.abs(out - ref).max()
-    assert err <= ATOL, f"max abs err {err}"
+    print(f"[decode err] seed={seed} B={B} Hq={Hq} Hkv={Hkv} nw={n_warm} nh={n_hot} k{kb}v{vb} f={frac}: {err:.3e}")
+    assert (np.abs(out - ref) <= tolerance(ref)).all(), f"max abs err {err}"
     np.testing.assert_allclose(lse, rlse, atol=2e-3, rtol=0)
     return err
 
@@ -150,7 +159,7 @@ def test_large_logits_stable():
     out, _ = run_case(q, wk, wv, hk, hv, 4, 4, 0.0)
     ref, _ = oracle_case(q, wk, wv, hk, hv, 4, 4, 0.0)
     assert np.isfinite(out).all()
-    assert np.abs(out - ref).max() <= ATOL
+    assert (np.abs(out - ref) <= tolerance(ref)).all(), np.abs(out - ref).max()
 
 
 def test_reference_signature_hot_only(golden_dir):
@@ -162,7 +171,8 @@ def test_reference_signature_hot_only(golden_dir):
                                                torch.from_numpy(z[f"{t}/k"]).to(DEV),
                                                torch.from_numpy(z[f"{t}/v"]).to(DEV))
     assert out.shape == (2, 2, 1, 128)
-    np.testing.assert_allclose(_np(out).astype(np.float32), z[f"{t}/out"].astype(np.float32), atol=ATOL, rtol=0)
+    ref = z[f"{t}/out"].astype(np.float32)
+    assert (np.abs(_np(out).astype(np.float32) - ref) <= tolerance(ref)).all()
 
 
 def test_affine_gqa_golden(golden_dir):
@@ -177,4 +187,5 @@ def test_affine_gqa_golden(golden_dir):
     out = akv.mixed_tier_decode_attention(torch.from_numpy(z[f"{t}/q"]).to(DEV),
                                           torch.from_numpy(z[f"{t}/hk"]).to(DEV),
                                           torch.from_numpy(z[f"{t}/hv"]).to(DEV), arena)
-    np.testing.assert_allclose(_np(out).astype(np.float32), z[f"{t}/out"].astype(np.float32), atol=ATOL, rtol=0)
+    ref = z[f"{t}/out"].astype(np.float32)
+    assert (np.abs(_np(out).astype(np.float32) - ref) <= tolerance(ref)).all()

@@ -25,7 +25,12 @@ def _np(t):
 
 
 def _bits16(a):
-    return np.ascontiguousarray(np.asarray(a, dtype=np.float16)).view(np.uint16)
+    """fp16 bit patterns, with every NaN mapped to one canonical pattern (NaN payloads
+    differ between torch's CPU kernels and the GPU; NaN arises only from inf scales)."""
+    h = np.ascontiguousarray(np.asarray(a, dtype=np.float16))
+    bits = h.view(np.uint16).copy()
+    bits[np.isnan(h)] = 0x7E00
+    return bits
 
 
 @pytest.mark.parametrize("bits", [2, 3, 4])
@@ -83,7 +88,7 @@ def test_affine_golden(golden_dir):
                 ref["outlier_idx"] = z[f"{name}/{tag}_outlier_idx"]
                 ref["outlier_data"] = z[f"{name}/{tag}_outlier_data"]
             _compare_q(q, ref, f"{name}/{tag}")
-            np.testing.assert_array_equal(_bits16(_np(dfn(q))), z[f"{name}/{tag}_deq"].view(np.uint16),
+            np.testing.assert_array_equal(_bits16(_np(dfn(q))), _bits16(z[f"{name}/{tag}_deq"]),
                                           err_msg=f"{name}/{tag} dequant")
             assert akv.measure_packed_bytes(q, int(kb if tag == "qk" else vb)) == int(z[f"{name}/{tag}_bytes"])
         ran += 1
