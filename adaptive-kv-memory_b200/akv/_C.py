@@ -58,6 +58,12 @@ SIGNATURES = {
                                  c_int, c_int, c_int, c_int, c_float,
                                  c_void_p, c_int64, c_int64, c_void_p, c_void_p,
                                  c_void_p, c_size_t, c_void_p, c_void_p]),
+    "akv_mixed_decode_noalloc": (c_int, [c_void_p, c_int64, c_int64,
+                                         c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int, c_void_p,
+                                         c_void_p, c_int64, c_int64, POINTER(WarmLayout), c_int, c_void_p,
+                                         c_int, c_int, c_int, c_int, c_float,
+                                         c_void_p, c_int64, c_int64, c_void_p, c_void_p,
+                                         c_void_p, c_void_p]),
     "akv_lse_combine": (c_int, [c_void_p, c_int64, c_int64, c_int, c_int, c_int, c_void_p, c_int64, c_void_p,
                                 c_void_p, c_void_p]),
     "akv_importance_update": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int, c_float, c_void_p]),

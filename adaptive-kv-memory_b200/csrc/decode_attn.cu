@@ -933,3 +933,44 @@ extern "C" int akv_lse_combine(const float* part, int64_t part_ss, int64_t part_
       part, part_ss, part_sr, rows, splits, D, reinterpret_cast<__half*>(out), o_sr, lse, merged);
   return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_LAUNCH;
 }
+
+// ---------------------------------------------------------------------------
+// Zero-allocation variant of akv_mixed_decode.
+//
+// Some callers cannot allocate device memory on the decode path: an attention
+// backend hook inside another framework's serving loop is handed only the
+// q / KV / output pointers and a stream, has no handle on that framework's
+// memory pool, and must not call cudaMalloc there (it synchronises the device
+// and is not allowed inside the engine's step).  For them the split-K partials
+// live in this fixed device array instead of a caller workspace.  Every GPU
+// that loads the library holds the array until the process exits.
+// ---------------------------------------------------------------------------
+namespace akv {
+constexpr size_t kNoAllocScratchBytes = static_cast<size_t>(8) << 20;  // AKV_NOALLOC_SCRATCH_BYTES
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+constexpr int kMaxDevices = 64;
+static void* g_noalloc_ptr[kMaxDevices];  // device address of g_noalloc_scratch, per device
+}  // namespace akv
+
+extern "C" int akv_mixed_decode_noalloc(const uint16_t* q, int64_t q_sb, int64_t q_sh, const uint16_t* hot_k,
+                                        const uint16_t* hot_v, int64_t h_sb, int64_t h_sh, int64_t h_sn, int n_hot,
+                                        const int32_t* hot_len, const uint8_t* warm, int64_t w_sb, int64_t w_sh,
+                                        const akv_warm_layout* layout, int n_warm_blocks, const int32_t* warm_len,
+                                        int B, int Hq, int Hkv, int D, float sm_scale, uint16_t* out, int64_t o_sb,
+                                        int64_t o_sh, float* lse, float* partial_out, int* status, void* stream) {
+  const size_t need = akv_decode_workspace_bytes(B, Hq, Hkv, D, n_hot, n_warm_blocks);
+  if (need == 0) return D != kHeadDim ? AKV_ERR_UNSUPPORTED : AKV_ERR_SHAPE;
+  if (need > kNoAllocScratchBytes) return AKV_ERR_WORKSPACE;  // beyond the fixed scratch array
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return AKV_ERR_LAUNCH;
+  if (!g_noalloc_ptr[dev]) {
+    // one-time set-up per device, with that device current: the host-side name
+    // g_noalloc_scratch is not a device address, so ask the runtime for it
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return AKV_ERR_LAUNCH;
+    g_noalloc_ptr[dev] = p;
+  }
+  return akv_mixed_decode(q, q_sb, q_sh, hot_k, hot_v, h_sb, h_sh, h_sn, n_hot, hot_len, warm, w_sb, w_sh, layout,
+                          n_warm_blocks, warm_len, B, Hq, Hkv, D, sm_scale, out, o_sb, o_sh, lse, partial_out,
+                          g_noalloc_ptr[dev], kNoAllocScratchBytes, status, stream);
+}

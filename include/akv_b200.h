@@ -171,6 +171,28 @@ int akv_mixed_decode(const uint16_t* q, int64_t q_sb, int64_t q_sh,
                      uint16_t* out, int64_t o_sb, int64_t o_sh, float* lse, float* partial_out,
                      void* workspace, size_t workspace_bytes, int* status, void* stream);
 
+/* Zero-allocation form of akv_mixed_decode (no counterpart in the reference,
+ * which has no native interface).  For callers that cannot allocate device
+ * memory on their decode path (e.g. an attention hook inside another serving
+ * engine, given only tensors and a stream): the split partials live in a fixed
+ * device array of AKV_NOALLOC_SCRATCH_BYTES inside the library instead of a
+ * caller workspace; every GPU that loads the library keeps that array until
+ * the process exits.  Shapes whose akv_decode_workspace_bytes exceeds it are
+ * rejected with AKV_ERR_WORKSPACE before anything is launched.  The first call
+ * on a device looks up the array's device address (cudaGetSymbolAddress) with
+ * that device current; make that first call before any stream capture.  All
+ * calls on a device share the one array, so calls that overlap on the GPU
+ * (different streams, no ordering between them) race and must not be issued. */
+#define AKV_NOALLOC_SCRATCH_BYTES (8u << 20)
+int akv_mixed_decode_noalloc(const uint16_t* q, int64_t q_sb, int64_t q_sh,
+                             const uint16_t* hot_k, const uint16_t* hot_v, int64_t h_sb, int64_t h_sh,
+                             int64_t h_sn, int n_hot, const int32_t* hot_len,
+                             const uint8_t* warm, int64_t w_sb, int64_t w_sh, const akv_warm_layout* layout,
+                             int n_warm_blocks, const int32_t* warm_len,
+                             int B, int Hq, int Hkv, int D, float sm_scale,
+                             uint16_t* out, int64_t o_sb, int64_t o_sh, float* lse, float* partial_out,
+                             int* status, void* stream);
+
 /* Log-sum-exp combine of partial records (acc[D], m, l) — the split-K merge
  * inside one GPU and the merge of a sequence split across GPUs.  Record of
  * row r, split s at part + s*part_ss + r*part_sr (floats).  Writes any of:
