@@ -11,8 +11,8 @@
 // (akv/affine_quantizer.py:112-124, :178-189: fp16(fp16(code*scale) + zero),
 // outlier channels replaced by their fp16 originals), so the contraction sees
 // the same fp16 K/V values the reference attends over.  Packed codes become
-// fp16 with the "1024 + code" magic (one LOP3 per pair); one HFMA2 then gives
-// fp16(code*scale) with a single rounding and one HADD2 adds the zero point.
+// fp16 with the "1024 + code" magic (one LOP3 per pair), then three packed
+// fp16 ops per pair: exact code, fp16(code*scale), + zero (no contraction).
 // The contraction runs on mma.sync m16n8k16 (f16 in, f32 accumulate): tokens
 // are M for q.K^T, head_dim is M for P.V, and the (<= 8) query heads of the KV
 // head are N.  movmatrix transposes P between the two; P enters the second MMA
@@ -56,26 +56,13 @@ struct DecodeParams {
 };
 
 // ------------------------------------------------------------------ exact fp16 dequantisation
-// x holds (1024 + M*c_a, 1024 + M*c_b) as fp16 (the LOP3 magic).  Fast form:
-// fp16(c*s) = fma(x, s/M, -1024*s/M) with one rounding, exact when s/M and
-// 1024*s/M are representable; then + zero.  Safe form for any scale:
-// c = fma(x, 1/M, -1024/M) (exact), fp16(c*s), + zero.
-AKV_DEV bool scale_is_fast(float s) { return s == 0.f || (s >= 0.015625f && s <= 63.9f); }
-
+// x holds (1024 + M*c_a, 1024 + M*c_b) as fp16 (the LOP3 magic).
+// c = fma(x, 1/M, -1024/M) is exact; fp16(c*s) and + zero round like the
+// reference's `codes.half() * scale + zero` (two roundings, never fused).
 template <int M>
-AKV_DEV uint32_t dq_fast(uint32_t x, __half2 s_over_m, __half2 neg1024s_over_m, __half2 z) {
-  return h2_as_u32(__hadd2_rn(__hfma2(u32_as_h2(x), s_over_m, neg1024s_over_m), z));
-}
-
-template <int M>
-AKV_DEV uint32_t dq_safe(uint32_t x, __half2 s, __half2 z) {
+AKV_DEV uint32_t dq(uint32_t x, __half2 s, __half2 z) {
   return h2_as_u32(__hadd2_rn(__hmul2_rn(u32_as_h2(fix_magic<M>(x)), s), z));
 }
-
-template <int M>
-AKV_DEV __half2 over_m(__half2 s) { return __hmul2(s, __float2half2_rn(1.0f / M)); }
-template <int M>
-AKV_DEV __half2 neg1024_over_m(__half2 s) { return __hmul2(s, __float2half2_rn(-1024.0f / M)); }
 
 // ------------------------------------------------------------------ K codes -> A fragments
 // Thread (g8, q4) holds, for one token row, the 32 codes of channel chunk q4
@@ -111,96 +98,83 @@ AKV_DEV constexpr int kmult(int i) {
   return BITS == 4 ? kMult4[i] : (BITS == 2 ? kMult2[i] : kMult3[i]);
 }
 
-// 3-bit: two big-endian 24-bit groups (low 24 bits of wa, wb) -> 8 magic pairs
-// ordered c7, c6, c5, c4, c3, c2, c1, c0 (pair = (code of wa, code of wb)),
-// multipliers 1, 8, 64, 1, 8, 1, 8, 64.
-AKV_DEV void raw3_pair(uint32_t wa, uint32_t wb, uint32_t* e) {
-  const uint32_t y = prmt(wa, wb, 0x5410);
-  e[0] = lop_magic<0x00070007u>(y);
-  e[1] = lop_magic<0x00380038u>(y);
-  e[2] = lop_magic<0x01C001C0u>(y);
-  const uint32_t y9 = y >> 9;
-  e[3] = lop_magic<0x00070007u>(y9);
-  e[4] = lop_magic<0x00380038u>(y9);
-  const uint32_t z = prmt(wa >> 15, wb >> 15, 0x5410);
-  e[5] = lop_magic<0x00070007u>(z);
-  e[6] = lop_magic<0x00380038u>(z);
-  e[7] = lop_magic<0x01C001C0u>(z);
-}
+// ---- K row chunk: the code words of thread q4's 32 channels of one token
+// (3 bits: the four 24-bit groups, each turned big-endian into the low bits)
+template <int KB>
+struct KWords {
+  uint32_t w[KB == 2 ? 2 : 4];
+};
 
 template <int KB>
-AKV_DEV void k_row_raw(const uint8_t* row, int q4, uint32_t (&e)[16]) {
+AKV_DEV KWords<KB> k_words(const uint8_t* row, int q4) {
+  KWords<KB> r;
   if constexpr (KB == 4) {
-    const uint4 w = lds_v4(row + 16 * q4);
-    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const uint32_t x = ws[k], y = ws[k] >> 8;
-      e[4 * k + 0] = lop_magic<0x000F000Fu>(x);
-      e[4 * k + 1] = lop_magic<0x00F000F0u>(x);
-      e[4 * k + 2] = lop_magic<0x000F000Fu>(y);
-      e[4 * k + 3] = lop_magic<0x00F000F0u>(y);
-    }
+    const uint4 v = lds_v4(row + 16 * q4);
+    r.w[0] = v.x;
+    r.w[1] = v.y;
+    r.w[2] = v.z;
+    r.w[3] = v.w;
   } else if constexpr (KB == 2) {
-    const uint2 w = lds_v2(row + 8 * q4);
-    const uint32_t ws[2] = {w.x, w.y};
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      const uint32_t x = ws[k], y = ws[k] >> 8;
-      e[8 * k + 0] = lop_magic<0x00030003u>(x);
-      e[8 * k + 1] = lop_magic<0x000C000Cu>(x);
-      e[8 * k + 2] = lop_magic<0x00300030u>(x);
-      e[8 * k + 3] = lop_magic<0x00C000C0u>(x);
-      e[8 * k + 4] = lop_magic<0x03000300u>(x);
-      e[8 * k + 5] = lop_magic<0x000C000Cu>(y);
-      e[8 * k + 6] = lop_magic<0x00300030u>(y);
-      e[8 * k + 7] = lop_magic<0x00C000C0u>(y);
-    }
+    const uint2 v = lds_v2(row + 8 * q4);
+    r.w[0] = v.x;
+    r.w[1] = v.y;
   } else {
     const uint8_t* p = row + 12 * q4;
     const uint32_t w0 = lds_u32(p), w1 = lds_u32(p + 4), w2 = lds_u32(p + 8);
-    const uint32_t g0 = prmt(w0, 0u, 0x4012), g1 = prmt(w0, w1, 0x3345);
-    const uint32_t g2 = prmt(w1, w2, 0x2234), g3 = prmt(w2, 0u, 0x4123);
-    raw3_pair(g0, g1, e);
-    raw3_pair(g2, g3, e + 8);
+    r.w[0] = prmt(w0, 0u, 0x4012);
+    r.w[1] = prmt(w0, w1, 0x3345);
+    r.w[2] = prmt(w1, w2, 0x2234);
+    r.w[3] = prmt(w2, 0u, 0x4123);
+  }
+  return r;
+}
+
+// Magic pair I (codes kPairs*[I], multiplier kMult*[I]) of a K row chunk.
+template <int KB, int I>
+AKV_DEV uint32_t k_raw(const KWords<KB>& kw) {
+  if constexpr (KB == 4) {
+    constexpr int k = I / 4, sub = I % 4;
+    const uint32_t x = sub < 2 ? kw.w[k] : (kw.w[k] >> 8);
+    if constexpr (sub & 1) return lop_magic<0x00F000F0u>(x);
+    else return lop_magic<0x000F000Fu>(x);
+  } else if constexpr (KB == 2) {
+    constexpr int k = I / 8, sub = I % 8;
+    const uint32_t x = kw.w[k];
+    if constexpr (sub == 0) return lop_magic<0x00030003u>(x);
+    else if constexpr (sub == 1) return lop_magic<0x000C000Cu>(x);
+    else if constexpr (sub == 2) return lop_magic<0x00300030u>(x);
+    else if constexpr (sub == 3) return lop_magic<0x00C000C0u>(x);
+    else if constexpr (sub == 4) return lop_magic<0x03000300u>(x);
+    else if constexpr (sub == 5) return lop_magic<0x000C000Cu>(x >> 8);
+    else if constexpr (sub == 6) return lop_magic<0x00300030u>(x >> 8);
+    else return lop_magic<0x00C000C0u>(x >> 8);
+  } else {
+    constexpr int k = I / 8, sub = I % 8;  // group pair (2k, 2k+1): codes c7..c0 of each group
+    const uint32_t wa = kw.w[2 * k], wb = kw.w[2 * k + 1];
+    if constexpr (sub < 3) {
+      const uint32_t y = prmt(wa, wb, 0x5410);
+      if constexpr (sub == 0) return lop_magic<0x00070007u>(y);
+      else if constexpr (sub == 1) return lop_magic<0x00380038u>(y);
+      else return lop_magic<0x01C001C0u>(y);
+    } else if constexpr (sub < 5) {
+      const uint32_t y9 = prmt(wa, wb, 0x5410) >> 9;
+      if constexpr (sub == 3) return lop_magic<0x00070007u>(y9);
+      else return lop_magic<0x00380038u>(y9);
+    } else {
+      const uint32_t z = prmt(wa >> 15, wb >> 15, 0x5410);
+      if constexpr (sub == 5) return lop_magic<0x00070007u>(z);
+      else if constexpr (sub == 6) return lop_magic<0x00380038u>(z);
+      else return lop_magic<0x01C001C0u>(z);
+    }
   }
 }
 
-// Per-block channel constants of this thread's K chunk, in pair order.
-template <int KB>
-struct KConst {
-  __half2 a[16];  // fast: s/M      safe: s
-  __half2 c[16];  // fast: -1024s/M
-  __half2 z[16];
-  bool fast;
-};
-
-template <int KB, int I = 0>
-AKV_DEV void k_consts_fill(const __half (&s)[32], const __half (&z)[32], KConst<KB>& kc) {
-  if constexpr (I < 16) {
-    constexpr PairIdx pi = kpair<KB>(I);
-    constexpr int M = kmult<KB>(I);
-    const __half2 s2 = __halves2half2(s[pi.a], s[pi.b]);
-    kc.z[I] = __halves2half2(z[pi.a], z[pi.b]);
-    kc.a[I] = kc.fast ? over_m<M>(s2) : s2;
-    kc.c[I] = neg1024_over_m<M>(s2);
-    k_consts_fill<KB, I + 1>(s, z, kc);
-  }
-}
-
-template <int KB>
-AKV_DEV void k_consts(const __half* ks, const __half* kz, KConst<KB>& kc) {
-  __half s[32], z[32];
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    *reinterpret_cast<uint4*>(s + 8 * k) = lds_v4(ks + 8 * k);
-    *reinterpret_cast<uint4*>(z + 8 * k) = lds_v4(kz + 8 * k);
-  }
-  bool fast = true;
-#pragma unroll
-  for (int k = 0; k < 32; ++k) fast &= scale_is_fast(__half2float(s[k]));
-  kc.fast = fast;
-  k_consts_fill<KB>(s, z, kc);
+// (scale or zero of channel A, of channel B) from the 8 natural-order words
+// (16 channels) of the chunk half that holds both channels.
+template <int A, int B>
+AKV_DEV __half2 pick2(const uint32_t (&S8)[8]) {
+  constexpr uint32_t sel = ((A & 1) ? 0x32u : 0x10u) | (((B & 1) ? 0x76u : 0x54u) << 8);
+  return u32_as_h2(prmt(S8[(A % 16) / 2], S8[(B % 16) / 2], sel));
 }
 
 template <int KB, int I = 0>
@@ -212,23 +186,30 @@ AKV_DEV void q_pairs(const __half (&qv)[32], uint32_t (&qp)[16]) {
   }
 }
 
-template <int BITS, int I>
-AKV_DEV uint32_t dq_pair(uint32_t x, __half2 a, __half2 c, __half2 z, bool fast) {
-  constexpr int M = kmult<BITS>(I);
-  return fast ? dq_fast<M>(x, a, c, z) : dq_safe<M>(x, a, z);
-}
-
-template <int KB, int I = 0>
-AKV_DEV void k_dequant(uint32_t (&e)[16], const KConst<KB>& kc) {
-  if constexpr (I < 16) {
-    e[I] = dq_pair<KB, I>(e[I], kc.a[I], kc.c[I], kc.z[I], kc.fast);
-    k_dequant<KB, I + 1>(e, kc);
+// q.K^T k-steps KS..KEND-1: per step, two channel pairs of the 4 token rows,
+// dequantised exactly, into the two m-tile accumulators.
+template <int KB, int KS, int KEND>
+AKV_DEV void qk_steps(const KWords<KB> (&W)[2][2], const uint32_t (&S8)[8], const uint32_t (&Z8)[8],
+                      const uint32_t (&qp)[16], float (&c)[2][4]) {
+  if constexpr (KS < KEND) {
+    constexpr int I0 = 2 * KS, I1 = 2 * KS + 1;
+    constexpr PairIdx p0 = kpair<KB>(I0), p1 = kpair<KB>(I1);
+    constexpr int M0 = kmult<KB>(I0), M1 = kmult<KB>(I1);
+    const __half2 s0 = pick2<p0.a, p0.b>(S8), z0 = pick2<p0.a, p0.b>(Z8);
+    const __half2 s1 = pick2<p1.a, p1.b>(S8), z1 = pick2<p1.a, p1.b>(Z8);
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt) {
+      const uint32_t a0 = dq<M0>(k_raw<KB, I0>(W[mt][0]), s0, z0);
+      const uint32_t a1 = dq<M0>(k_raw<KB, I0>(W[mt][1]), s0, z0);
+      const uint32_t a2 = dq<M1>(k_raw<KB, I1>(W[mt][0]), s1, z1);
+      const uint32_t a3 = dq<M1>(k_raw<KB, I1>(W[mt][1]), s1, z1);
+      mma_16816(c[mt], a0, a1, a2, a3, qp[I0], qp[I1]);
+    }
+    qk_steps<KB, KS + 1, KEND>(W, S8, Z8, qp, c);
   }
 }
 
-// ------------------------------------------------------------------ V codes -> A fragments
-// Thread group g8 owns channels [16*g8, 16*g8+16).  For a token pair (ta, tb)
-// produce e[ci] = (v_ta[ci], v_tb[ci]) dequantised, ci = 0..15.
+// ---- V token pair (ta, tb) of thread group g8 (channels 16*g8 .. +15)
 template <int VB>
 struct VRow {
   uint32_t w[VB == 2 ? 1 : 2];
@@ -255,88 +236,91 @@ AKV_DEV VRow<VB> v_row_load(const uint8_t* row, int g8) {
   return r;
 }
 
-// raw magic pairs by channel index ci, plus each one's multiplier (compile time)
+// interleaved token pair: both tokens' codes side by side in each 16-bit half
 template <int VB>
-constexpr int vmult(int ci) {
+struct VPair {
+  uint32_t x[VB == 2 ? 4 : (VB == 4 ? 8 : 6)];
+};
+
+template <int VB>
+AKV_DEV VPair<VB> v_pair(const VRow<VB>& a, const VRow<VB>& b) {
+  VPair<VB> v;
+  if constexpr (VB == 2) {
+    v.x[0] = prmt(a.w[0], b.w[0], 0x5410);  // codes 0..7
+    v.x[1] = v.x[0] >> 8;
+    v.x[2] = prmt(a.w[0], b.w[0], 0x7632);  // codes 8..15
+    v.x[3] = v.x[2] >> 8;
+  } else if constexpr (VB == 4) {
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      v.x[4 * k + 0] = prmt(a.w[k], b.w[k], 0x5410);
+      v.x[4 * k + 1] = v.x[4 * k + 0] >> 8;
+      v.x[4 * k + 2] = prmt(a.w[k], b.w[k], 0x7632);
+      v.x[4 * k + 3] = v.x[4 * k + 2] >> 8;
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      v.x[3 * k + 0] = prmt(a.w[k], b.w[k], 0x5410);
+      v.x[3 * k + 1] = v.x[3 * k + 0] >> 9;
+      v.x[3 * k + 2] = prmt(a.w[k] >> 15, b.w[k] >> 15, 0x5410);
+    }
+  }
+  return v;
+}
+
+// magic pair of channel CI (multiplier vmult<VB>(CI))
+template <int VB, int CI>
+AKV_DEV uint32_t v_raw(const VPair<VB>& v) {
+  constexpr int k = CI / 8, sub = CI % 8;
+  if constexpr (VB == 2) {
+    const uint32_t x = v.x[2 * k], x8 = v.x[2 * k + 1];
+    if constexpr (sub == 0) return lop_magic<0x00C000C0u>(x);
+    else if constexpr (sub == 1) return lop_magic<0x00300030u>(x);
+    else if constexpr (sub == 2) return lop_magic<0x000C000Cu>(x);
+    else if constexpr (sub == 3) return lop_magic<0x00030003u>(x);
+    else if constexpr (sub == 4) return lop_magic<0x00C000C0u>(x8);
+    else if constexpr (sub == 5) return lop_magic<0x00300030u>(x8);
+    else if constexpr (sub == 6) return lop_magic<0x000C000Cu>(x8);
+    else return lop_magic<0x03000300u>(x);
+  } else if constexpr (VB == 4) {
+    const uint32_t* x = v.x + 4 * k;
+    constexpr int src = sub / 2;  // 0: X, 1: X>>8, 2: Y, 3: Y>>8
+    if constexpr (sub & 1) return lop_magic<0x000F000Fu>(x[src]);
+    else return lop_magic<0x00F000F0u>(x[src]);
+  } else {
+    const uint32_t y = v.x[3 * k], y9 = v.x[3 * k + 1], z = v.x[3 * k + 2];
+    if constexpr (sub == 0) return lop_magic<0x01C001C0u>(z);
+    else if constexpr (sub == 1) return lop_magic<0x00380038u>(z);
+    else if constexpr (sub == 2) return lop_magic<0x00070007u>(z);
+    else if constexpr (sub == 3) return lop_magic<0x00380038u>(y9);
+    else if constexpr (sub == 4) return lop_magic<0x00070007u>(y9);
+    else if constexpr (sub == 5) return lop_magic<0x01C001C0u>(y);
+    else if constexpr (sub == 6) return lop_magic<0x00380038u>(y);
+    else return lop_magic<0x00070007u>(y);
+  }
+}
+
+template <int VB>
+__host__ __device__ constexpr int vmult(int ci) {
   if (VB == 4) return (ci & 1) ? 1 : 16;
   if (VB == 2) {
     constexpr int m[8] = {64, 16, 4, 1, 64, 16, 4, 256};
     return m[ci & 7];
   }
-  constexpr int m3[8] = {64, 8, 1, 8, 1, 64, 8, 1};  // ci -> multiplier of code ci in raw3_pair order
+  constexpr int m3[8] = {64, 8, 1, 8, 1, 64, 8, 1};
   return m3[ci & 7];
 }
 
-template <int VB>
-AKV_DEV void v_pair_raw(const VRow<VB>& a, const VRow<VB>& b, uint32_t (&e)[16]) {
-  if constexpr (VB == 4) {
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      const uint32_t x = prmt(a.w[k], b.w[k], 0x5410), y = prmt(a.w[k], b.w[k], 0x7632);
-      const uint32_t x8 = x >> 8, y8 = y >> 8;
-      e[8 * k + 1] = lop_magic<0x000F000Fu>(x);
-      e[8 * k + 0] = lop_magic<0x00F000F0u>(x);
-      e[8 * k + 3] = lop_magic<0x000F000Fu>(x8);
-      e[8 * k + 2] = lop_magic<0x00F000F0u>(x8);
-      e[8 * k + 5] = lop_magic<0x000F000Fu>(y);
-      e[8 * k + 4] = lop_magic<0x00F000F0u>(y);
-      e[8 * k + 7] = lop_magic<0x000F000Fu>(y8);
-      e[8 * k + 6] = lop_magic<0x00F000F0u>(y8);
-    }
-  } else if constexpr (VB == 2) {
-    const uint32_t xs[2] = {prmt(a.w[0], b.w[0], 0x5410), prmt(a.w[0], b.w[0], 0x7632)};
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      const uint32_t x = xs[k], x8 = xs[k] >> 8;
-      e[8 * k + 3] = lop_magic<0x00030003u>(x);
-      e[8 * k + 2] = lop_magic<0x000C000Cu>(x);
-      e[8 * k + 1] = lop_magic<0x00300030u>(x);
-      e[8 * k + 0] = lop_magic<0x00C000C0u>(x);
-      e[8 * k + 7] = lop_magic<0x03000300u>(x);
-      e[8 * k + 6] = lop_magic<0x000C000Cu>(x8);
-      e[8 * k + 5] = lop_magic<0x00300030u>(x8);
-      e[8 * k + 4] = lop_magic<0x00C000C0u>(x8);
-    }
-  } else {
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      uint32_t t[8];
-      raw3_pair(a.w[k], b.w[k], t);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) e[8 * k + 7 - j] = t[j];
-    }
-  }
-}
-
-template <int VB, int CI = 0>
-AKV_DEV void v_dequant(uint32_t (&e)[16], __half2 s2, __half2 z2, bool fast) {
-  if constexpr (CI < 16) {
-    constexpr int M = vmult<VB>(CI);
-    e[CI] = fast ? dq_fast<M>(e[CI], over_m<M>(s2), neg1024_over_m<M>(s2), z2) : dq_safe<M>(e[CI], s2, z2);
-    v_dequant<VB, CI + 1>(e, s2, z2, fast);
-  }
-}
-
-// code of channel d in a packed row (akv/bitpack.py layout)
-template <int BITS>
-AKV_DEV uint32_t code_at(const uint8_t* row, int d) {
-  if constexpr (BITS == 4) {
-    const uint32_t byte = row[d >> 1];
-    return (d & 1) ? (byte & 15u) : (byte >> 4);
-  } else if constexpr (BITS == 2) {
-    return (row[d >> 2] >> (6 - 2 * (d & 3))) & 3u;
-  } else {
-    const uint8_t* p = row + 3 * (d >> 3);
-    const uint32_t word = (static_cast<uint32_t>(p[0]) << 16) | (p[1] << 8) | p[2];
-    return (word >> (21 - 3 * (d & 7))) & 7u;
-  }
-}
-
 // ------------------------------------------------------------------ shared softmax/PV state
+constexpr int kRegOutliers = 2;  // V outlier channels whose residual sum stays in registers
+
 struct WarpState {
   float acc[8][4];  // O^T: tile mt rows (g8 -> d=16*g8+2mt, g8+8 -> d+1), cols heads (2q4, 2q4+1)
   float m[2];       // running max (log2 units) for heads 2q4, 2q4+1
   float l[2];       // partial row sums (this thread's tokens only)
+  float vcorr[kRegOutliers][2];  // V outlier residual sums (warp-reduced), pending for channel vch[j]
+  int vch[kRegOutliers];
 };
 
 AKV_DEV void state_init(WarpState& s) {
@@ -346,6 +330,25 @@ AKV_DEV void state_init(WarpState& s) {
     for (int j = 0; j < 4; ++j) s.acc[i][j] = 0.f;
   s.m[0] = s.m[1] = -INFINITY;
   s.l[0] = s.l[1] = 0.f;
+#pragma unroll
+  for (int j = 0; j < kRegOutliers; ++j) {
+    s.vcorr[j][0] = s.vcorr[j][1] = 0.f;
+    s.vch[j] = -1;
+  }
+}
+
+// add (c0, c1) to output row `ch` (heads 2q4, 2q4+1) in the owning thread group
+AKV_DEV void acc_add_row(WarpState& s, int g8, int ch, float c0, float c1) {
+  if (ch < 0 || (ch >> 4) != g8) return;
+  const int ci = ch & 15;
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt)
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf)
+      if (ci == 2 * mt + hf) {
+        s.acc[mt][2 * hf] += c0;
+        s.acc[mt][2 * hf + 1] += c1;
+      }
 }
 
 // x[mt][4]: scaled logits (log2 units, -inf = masked) of this thread's 4
@@ -368,12 +371,20 @@ AKV_DEV void online_softmax(WarpState& s, float (&x)[2][4]) {
     s.m[h] = mn;
     s.l[h] *= alpha[h];
   }
+  // the running max rarely moves once a few blocks are in: skip the rescale then
+  if (__any_sync(0xffffffffu, alpha[0] != 1.f || alpha[1] != 1.f)) {
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    s.acc[i][0] *= alpha[0];
-    s.acc[i][1] *= alpha[1];
-    s.acc[i][2] *= alpha[0];
-    s.acc[i][3] *= alpha[1];
+    for (int i = 0; i < 8; ++i) {
+      s.acc[i][0] *= alpha[0];
+      s.acc[i][1] *= alpha[1];
+      s.acc[i][2] *= alpha[0];
+      s.acc[i][3] *= alpha[1];
+    }
+#pragma unroll
+    for (int j = 0; j < kRegOutliers; ++j) {
+      s.vcorr[j][0] *= alpha[0];
+      s.vcorr[j][1] *= alpha[1];
+    }
   }
 #pragma unroll
   for (int mt = 0; mt < 2; ++mt)
@@ -396,6 +407,23 @@ AKV_DEV void p_fragments(const float (&x)[2][4], uint32_t (&ph)[2][2], uint32_t 
       ph[mt][r] = movmatrix_trans(h2_as_u32(hi));
       pl[mt][r] = movmatrix_trans(h2_as_u32(lo));
     }
+}
+
+// P.V k-step over 16 tokens: for each of the 8 m-tiles (channel pairs 2mt,
+// 2mt+1 of this thread group), the two token pairs, dequantised exactly.
+template <int VB, int MT>
+AKV_DEV void pv_tiles(WarpState& st, const VPair<VB>& v0, const VPair<VB>& v1, __half2 s0, __half2 z0, __half2 s1,
+                      __half2 z1, const uint32_t (&ph)[2], const uint32_t (&pl)[2]) {
+  if constexpr (MT < 8) {
+    constexpr int C0 = 2 * MT, C1 = 2 * MT + 1;
+    const uint32_t a0 = dq<vmult<VB>(C0)>(v_raw<VB, C0>(v0), s0, z0);
+    const uint32_t a1 = dq<vmult<VB>(C1)>(v_raw<VB, C1>(v0), s0, z0);
+    const uint32_t a2 = dq<vmult<VB>(C0)>(v_raw<VB, C0>(v1), s1, z1);
+    const uint32_t a3 = dq<vmult<VB>(C1)>(v_raw<VB, C1>(v1), s1, z1);
+    mma_16816(st.acc[MT], a0, a1, a2, a3, ph[0], ph[1]);
+    mma_16816(st.acc[MT], a0, a1, a2, a3, pl[0], pl[1]);
+    pv_tiles<VB, MT + 1>(st, v0, v1, s0, z0, s1, z1, ph, pl);
+  }
 }
 
 // ------------------------------------------------------------------ epilogue
@@ -452,7 +480,7 @@ AKV_DEV void cta_write_partial(const DecodeParams& p, float* red, float* rm, flo
 
 // ------------------------------------------------------------------ the kernel
 template <int KB, int VB>
-__global__ void __launch_bounds__(kDecodeThreads) mixed_decode_kernel(const DecodeParams p) {
+__global__ void __launch_bounds__(kDecodeThreads, 3) mixed_decode_kernel(const DecodeParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g8 = lane >> 2, q4 = lane & 3;
@@ -541,41 +569,53 @@ __global__ void __launch_bounds__(kDecodeThreads) mixed_decode_kernel(const Deco
         const __half* vzr = reinterpret_cast<const __half*>(r + p.L.vz);
         const uint32_t mask = lds_u32(r + p.L.mask);
 
-        KConst<KB> kcst;
-        k_consts<KB>(reinterpret_cast<const __half*>(r + p.L.ks) + 32 * q4,
-                     reinterpret_cast<const __half*>(r + p.L.kz) + 32 * q4, kcst);
-
-        // ---- S^T = K^ q  (tokens x heads), 2 m-tiles of 16 tokens
-        float x[2][4];
+        // ---- S^T = K^ q  (tokens x heads): rows 16mt + 8rr + g8, k-steps over channel pairs
+        KWords<KB> W[2][2];
 #pragma unroll
-        for (int mt = 0; mt < 2; ++mt) {
-          uint32_t e0[16], e1[16];
-          k_row_raw<KB>(kc + (16 * mt + g8) * kp, q4, e0);
-          k_row_raw<KB>(kc + (16 * mt + g8 + 8) * kp, q4, e1);
-          k_dequant<KB>(e0, kcst);
-          k_dequant<KB>(e1, kcst);
-          float c[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-          for (int ks = 0; ks < 8; ++ks)
-            mma_16816(c, e0[2 * ks], e1[2 * ks], e0[2 * ks + 1], e1[2 * ks + 1], qp[2 * ks], qp[2 * ks + 1]);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) x[mt][j] = c[j];
+          for (int rr = 0; rr < 2; ++rr) W[mt][rr] = k_words<KB>(kc + (16 * mt + 8 * rr + g8) * kp, q4);
+        float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        {
+          const uint32_t* ks32 = reinterpret_cast<const uint32_t*>(r + p.L.ks) + 16 * q4;
+          const uint32_t* kz32 = reinterpret_cast<const uint32_t*>(r + p.L.kz) + 16 * q4;
+          uint32_t S8[8], Z8[8];
+          *reinterpret_cast<uint4*>(S8) = lds_v4(ks32);
+          *reinterpret_cast<uint4*>(S8 + 4) = lds_v4(ks32 + 4);
+          *reinterpret_cast<uint4*>(Z8) = lds_v4(kz32);
+          *reinterpret_cast<uint4*>(Z8 + 4) = lds_v4(kz32 + 4);
+          qk_steps<KB, 0, 4>(W, S8, Z8, qp, c);
+          *reinterpret_cast<uint4*>(S8) = lds_v4(ks32 + 8);
+          *reinterpret_cast<uint4*>(S8 + 4) = lds_v4(ks32 + 12);
+          *reinterpret_cast<uint4*>(Z8) = lds_v4(kz32 + 8);
+          *reinterpret_cast<uint4*>(Z8 + 4) = lds_v4(kz32 + 12);
+          qk_steps<KB, 4, 8>(W, S8, Z8, qp, c);
         }
-        // K outlier channels: the dequantised value there is 0 (scale = zero = 0);
-        // the reference overwrites it with the fp16 original.
-        for (int j = 0; j < n_out; ++j) {
-          const int d_o = reinterpret_cast<const int16_t*>(r + p.L.ki)[j];
-          const float qa = qs[(2 * q4) * kHeadDim + d_o], qb = qs[(2 * q4 + 1) * kHeadDim + d_o];
-          const __half* od = reinterpret_cast<const __half*>(r + p.L.ko);
+        // K outlier channels: their dequantised value is 0 (scale = zero = 0) and the
+        // reference puts the fp16 original there; add q . original with one more MMA
+        // whose k slots 2q4, 2q4+1 are outliers j = 2q4, 2q4+1 (n_outlier <= 8).
+        if (n_out > 0) {
+          const __half* ko = reinterpret_cast<const __half*>(r + p.L.ko);
+          const int16_t* kid = reinterpret_cast<const int16_t*>(r + p.L.ki);
+          const int j0 = 2 * q4, j1 = 2 * q4 + 1;
+          const __half hz = __float2half_rn(0.f);
+          const __half qa = j0 < n_out ? __float2half_rn(qs[g8 * kHeadDim + kid[j0]]) : hz;
+          const __half qb = j1 < n_out ? __float2half_rn(qs[g8 * kHeadDim + kid[j1]]) : hz;
+          const uint32_t bq = h2_as_u32(__halves2half2(qa, qb));
 #pragma unroll
-          for (int mt = 0; mt < 2; ++mt)
+          for (int mt = 0; mt < 2; ++mt) {
+            uint32_t a[2];
 #pragma unroll
             for (int rr = 0; rr < 2; ++rr) {
-              const float o = __half2float(od[(16 * mt + 8 * rr + g8) * n_out + j]);
-              x[mt][2 * rr] = fmaf(qa, o, x[mt][2 * rr]);
-              x[mt][2 * rr + 1] = fmaf(qb, o, x[mt][2 * rr + 1]);
+              const int t = 16 * mt + 8 * rr + g8;
+              const __half oa = j0 < n_out ? ko[t * n_out + j0] : hz;
+              const __half ob = j1 < n_out ? ko[t * n_out + j1] : hz;
+              a[rr] = h2_as_u32(__halves2half2(oa, ob));
             }
+            mma_16816(c[mt], a[0], a[1], 0u, 0u, bq, 0u);
+          }
         }
+        float x[2][4];
         bool valid[2][2];
 #pragma unroll
         for (int mt = 0; mt < 2; ++mt)
@@ -584,7 +624,7 @@ __global__ void __launch_bounds__(kDecodeThreads) mixed_decode_kernel(const Deco
             valid[mt][rr] = (mask >> (16 * mt + 8 * rr + g8)) & 1u;
 #pragma unroll
             for (int h = 0; h < 2; ++h)
-              x[mt][2 * rr + h] = valid[mt][rr] ? x[mt][2 * rr + h] * p.scale_log2 : -INFINITY;
+              x[mt][2 * rr + h] = valid[mt][rr] ? c[mt][2 * rr + h] * p.scale_log2 : -INFINITY;
           }
         online_softmax(st, x);
         uint32_t ph[2][2], pl[2][2];
@@ -594,69 +634,58 @@ __global__ void __launch_bounds__(kDecodeThreads) mixed_decode_kernel(const Deco
 #pragma unroll
         for (int ks = 0; ks < 2; ++ks) {
           const int ta = 16 * ks + 2 * q4;
-          uint32_t e0[16], e1[16];
-          {
-            const VRow<VB> ra = v_row_load<VB>(vc + ta * vp, g8);
-            const VRow<VB> rb = v_row_load<VB>(vc + (ta + 1) * vp, g8);
-            v_pair_raw<VB>(ra, rb, e0);
-            const __half2 s2 = __halves2half2(vsc[ta], vsc[ta + 1]);
-            const __half2 z2 = __halves2half2(vzr[ta], vzr[ta + 1]);
-            const bool fast = scale_is_fast(__low2float(s2)) && scale_is_fast(__high2float(s2));
-            v_dequant<VB>(e0, s2, z2, fast);
-          }
-          {
-            const VRow<VB> rc = v_row_load<VB>(vc + (ta + 8) * vp, g8);
-            const VRow<VB> rd = v_row_load<VB>(vc + (ta + 9) * vp, g8);
-            v_pair_raw<VB>(rc, rd, e1);
-            const __half2 s2 = __halves2half2(vsc[ta + 8], vsc[ta + 9]);
-            const __half2 z2 = __halves2half2(vzr[ta + 8], vzr[ta + 9]);
-            const bool fast = scale_is_fast(__low2float(s2)) && scale_is_fast(__high2float(s2));
-            v_dequant<VB>(e1, s2, z2, fast);
-          }
-#pragma unroll
-          for (int mt = 0; mt < 8; ++mt) {
-            mma_16816(st.acc[mt], e0[2 * mt], e0[2 * mt + 1], e1[2 * mt], e1[2 * mt + 1], ph[ks][0], ph[ks][1]);
-            mma_16816(st.acc[mt], e0[2 * mt], e0[2 * mt + 1], e1[2 * mt], e1[2 * mt + 1], pl[ks][0], pl[ks][1]);
-          }
+          const VPair<VB> v0 = v_pair<VB>(v_row_load<VB>(vc + ta * vp, g8), v_row_load<VB>(vc + (ta + 1) * vp, g8));
+          const VPair<VB> v1 =
+              v_pair<VB>(v_row_load<VB>(vc + (ta + 8) * vp, g8), v_row_load<VB>(vc + (ta + 9) * vp, g8));
+          const __half2 s0 = *reinterpret_cast<const __half2*>(vsc + ta);
+          const __half2 z0 = *reinterpret_cast<const __half2*>(vzr + ta);
+          const __half2 s1 = *reinterpret_cast<const __half2*>(vsc + ta + 8);
+          const __half2 z1 = *reinterpret_cast<const __half2*>(vzr + ta + 8);
+          pv_tiles<VB, 0>(st, v0, v1, s0, z0, s1, z1, ph[ks], pl[ks]);
         }
 
-        // ---- V outlier channels: replace the dequantised code value by the fp16 original
-        for (int j = 0; j < n_out; ++j) {
-          const int d_o = reinterpret_cast<const int16_t*>(r + p.L.vi)[j];
-          const __half* od = reinterpret_cast<const __half*>(r + p.L.vo);
-          float corr[2] = {0.f, 0.f};
+        // ---- V outlier channels: add sum_t p_t * (original - dequantised) to their rows
+        if (n_out > 0) {
+          const float* vr = reinterpret_cast<const float*>(r + p.L.vr);
+          const int16_t* vid = reinterpret_cast<const int16_t*>(r + p.L.vi);
+          for (int j = 0; j < n_out; ++j) {
+            float cr[2] = {0.f, 0.f};
 #pragma unroll
-          for (int mt = 0; mt < 2; ++mt)
+            for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-            for (int rr = 0; rr < 2; ++rr) {
-              if (!valid[mt][rr]) continue;
-              const int t = 16 * mt + 8 * rr + g8;
-              const __half cv = __uint2half_rn(code_at<VB>(vc + t * vp, d_o));
-              const float deq = __half2float(__hadd_rn(__hmul_rn(cv, vsc[t]), vzr[t]));
-              const float diff = __half2float(od[t * n_out + j]) - deq;
+              for (int rr = 0; rr < 2; ++rr) {
+                const float rv = vr[(16 * mt + 8 * rr + g8) * n_out + j];
+                cr[0] = fmaf(x[mt][2 * rr], rv, cr[0]);
+                cr[1] = fmaf(x[mt][2 * rr + 1], rv, cr[1]);
+              }
 #pragma unroll
-              for (int h = 0; h < 2; ++h) corr[h] = fmaf(x[mt][2 * rr + h], diff, corr[h]);
+            for (int o = 4; o < 32; o <<= 1) {
+              cr[0] += __shfl_xor_sync(0xffffffffu, cr[0], o);
+              cr[1] += __shfl_xor_sync(0xffffffffu, cr[1], o);
             }
+            const int ch = vid[j];
+            if (j < kRegOutliers) {
 #pragma unroll
-          for (int o = 4; o < 32; o <<= 1) {
-            corr[0] += __shfl_xor_sync(0xffffffffu, corr[0], o);
-            corr[1] += __shfl_xor_sync(0xffffffffu, corr[1], o);
-          }
-          if ((d_o >> 4) == g8) {
-            const int ci = d_o & 15;
-#pragma unroll
-            for (int mt = 0; mt < 8; ++mt)
-#pragma unroll
-              for (int hf = 0; hf < 2; ++hf)
-                if (ci == 2 * mt + hf) {
-                  st.acc[mt][2 * hf] += corr[0];
-                  st.acc[mt][2 * hf + 1] += corr[1];
+              for (int jj = 0; jj < kRegOutliers; ++jj) {
+                if (jj != j) continue;
+                if (ch != st.vch[jj]) {  // channel changed: settle the pending sum into its row
+                  acc_add_row(st, g8, st.vch[jj], st.vcorr[jj][0], st.vcorr[jj][1]);
+                  st.vcorr[jj][0] = st.vcorr[jj][1] = 0.f;
+                  st.vch[jj] = ch;
                 }
+                st.vcorr[jj][0] += cr[0];
+                st.vcorr[jj][1] += cr[1];
+              }
+            } else {
+              acc_add_row(st, g8, ch, cr[0], cr[1]);
+            }
           }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
       }
+#pragma unroll
+      for (int jj = 0; jj < kRegOutliers; ++jj) acc_add_row(st, g8, st.vch[jj], st.vcorr[jj][0], st.vcorr[jj][1]);
     }
   } else {
     // ---------------- hot CTA: FP16 window, 128-bit loads, all warps consume (producer warp too)

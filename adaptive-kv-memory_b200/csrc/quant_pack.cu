@@ -166,6 +166,7 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_group_kernel(const Qua
   float* norms = reinterpret_cast<float*>(kmax + H * D);                 // [H][D]
   float* score = norms + H * D;                                          // [D]
   int* oidx = reinterpret_cast<int*>(score + D);                         // [kMaxOutliers]
+  __half* od_s = reinterpret_cast<__half*>(oidx + kMaxOutliers);         // [H][nt][n_out] originals
 
   // ---- stage the group's rows (128-bit loads, 16 B per thread-iteration)
   const int vpr = D / 8;
@@ -227,15 +228,14 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_group_kernel(const Qua
     __syncthreads();
     // side store: fp16 originals of the outlier channels, then their ids
     const akv_view& od = p.dst.out_data;
-    if (od.ptr) {
-      for (int w = tid; w < H * nt * p.n_out; w += kQuantThreads) {
-        const int j = w % p.n_out;
-        const int t = (w / p.n_out) % nt;
-        const int h = w / (p.n_out * nt);
-        const int tt = t0 + t;
-        reinterpret_cast<__half*>(vaddr(od, b, h, tt / kBlockTokens, tt % kBlockTokens))[j] =
-            xs[(static_cast<size_t>(h) * nt + t) * pitch + oidx[j]];
-      }
+    for (int w = tid; w < H * nt * p.n_out; w += kQuantThreads) {
+      const int j = w % p.n_out;
+      const int t = (w / p.n_out) % nt;
+      const int h = w / (p.n_out * nt);
+      const int tt = t0 + t;
+      const __half o = xs[(static_cast<size_t>(h) * nt + t) * pitch + oidx[j]];
+      od_s[w] = o;  // w == (h*nt + t)*n_out + j
+      if (od.ptr) reinterpret_cast<__half*>(vaddr(od, b, h, tt / kBlockTokens, tt % kBlockTokens))[j] = o;
     }
     const akv_view& oi = p.dst.out_idx;
     if (oi.ptr) {
@@ -345,6 +345,23 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_group_kernel(const Qua
     uint32_t c[32];
 #pragma unroll
     for (int k = 0; k < 32; ++k) c[k] = quant_code(__half2float(x[k]), zf[k], sf[k], maxval);
+    if constexpr (!IS_KEY) {
+      // outlier residual: fp16 original minus what the zeroed channel dequantises to
+      if (p.n_out > 0 && p.dst.out_resid.ptr) {
+        const int tt = t0 + t;
+        float* rp = reinterpret_cast<float*>(vaddr(p.dst.out_resid, b, h, tt / kBlockTokens, tt % kBlockTokens));
+        for (int j = 0; j < p.n_out; ++j) {
+          const int d = oidx[j] - su * 32;
+          if (d < 0 || d >= 32) continue;
+          uint32_t cv = 0;
+#pragma unroll
+          for (int k = 0; k < 32; ++k)
+            if (k == d) cv = c[k];
+          const __half deq = __hadd_rn(__hmul_rn(__uint2half_rn(cv), __float2half_rn(sf[0])), __float2half_rn(zf[0]));
+          rp[j] = __half2float(od_s[(h * nt + t) * p.n_out + j]) - __half2float(deq);
+        }
+      }
+    }
     uint32_t wds[BITS];
     pack32<BITS>(c, wds);
     const int tt = t0 + t;
@@ -490,16 +507,16 @@ __global__ void unpack_codes_kernel(const uint8_t* packed, int64_t rows, int dim
 // ---------------------------------------------------------------------------
 static inline bool aligned(const void* p, int a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
-size_t quant_smem_bytes(int H, int nt, int D) {
+size_t quant_smem_bytes(int H, int nt, int D, int n_out) {
   return static_cast<size_t>(H) * nt * pad_pitch(D) * 2 + static_cast<size_t>(H) * D * 4 +
-         static_cast<size_t>(H) * D * 4 + D * 4 + kMaxOutliers * 4;
+         static_cast<size_t>(H) * D * 4 + D * 4 + kMaxOutliers * 4 + static_cast<size_t>(H) * nt * n_out * 2;
 }
 
 template <int BITS, bool IS_KEY>
 static int launch_quant(const QuantParams& p, cudaStream_t st) {
   const int ngroups = (p.N + p.group - 1) / p.group;
   const int nt = min(p.group, p.N);
-  const size_t smem = quant_smem_bytes(p.H, nt, p.D);
+  const size_t smem = quant_smem_bytes(p.H, nt, p.D, p.n_out);
   auto kern = quantize_group_kernel<BITS, IS_KEY>;
   if (smem > 48 * 1024) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
@@ -545,7 +562,8 @@ extern "C" int akv_quantize(const uint16_t* src, int64_t src_sb, int64_t src_sh,
                                   dst->zero.sblk % 4))
     return AKV_ERR_ALIGN;
   if (dst->mask.ptr && !aligned(dst->mask.ptr, 4)) return AKV_ERR_ALIGN;
-  if (quant_smem_bytes(H, group, D) > 220 * 1024) return AKV_ERR_UNSUPPORTED;
+  if (dst->out_resid.ptr && (!aligned(dst->out_resid.ptr, 4) || dst->out_resid.sslot % 4)) return AKV_ERR_ALIGN;
+  if (quant_smem_bytes(H, group, D, n_outlier) > 220 * 1024) return AKV_ERR_UNSUPPORTED;
   QuantParams p{reinterpret_cast<const __half*>(src), src_sb, src_sh, src_sn, tok_idx, tok_sb, B, H, N, D,
                 bits, is_key, group, n_outlier, *dst, status};
   cudaStream_t st = static_cast<cudaStream_t>(stream);
