@@ -76,6 +76,10 @@ AKV_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int* status) {
   return false;
 }
 
+// Order this thread's earlier generic-proxy shared-memory accesses before
+// later async-proxy (TMA) writes to the same buffer.
+AKV_DEV void fence_proxy_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 // 1-D bulk TMA copy global -> shared, completion counted on an mbarrier.
 // dst/src 16-byte aligned, bytes a multiple of 16.  No multicast.
 AKV_DEV void tma_load_1d(void* dst_smem, const void* src_gmem, uint32_t bytes, uint64_t* bar) {
@@ -135,8 +139,7 @@ AKV_DEV uint32_t pack_h2(float lo, float hi) { return h2_as_u32(__floats2half2_r
 // D = A(16x16, row) * B(16x8, col) + D, f16 inputs, f32 accumulate.
 AKV_DEV void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                        uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
@@ -145,7 +148,7 @@ AKV_DEV void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uin
 // Transpose an 8x8 b16 matrix held in the m8n8 fragment layout.
 AKV_DEV uint32_t movmatrix_trans(uint32_t a) {
   uint32_t d;
-  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
+  asm("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
   return d;
 }
 

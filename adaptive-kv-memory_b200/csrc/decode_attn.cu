@@ -15,8 +15,7 @@
 // fp16 ops per pair: exact code, fp16(code*scale), + zero (no contraction).
 // The contraction runs on mma.sync m16n8k16 (f16 in, f32 accumulate): tokens
 // are M for q.K^T, head_dim is M for P.V, and the (<= 8) query heads of the KV
-// head are N.  movmatrix transposes P between the two; P enters the second MMA
-// as an fp16 hi + lo pair so the probabilities keep ~22 bits.
+// head are N.  movmatrix transposes P (fp16) between the two.
 //
 // Hot CTAs read the FP16 window with 128-bit loads and use the same MMA
 // layout with natural channel order.
@@ -395,34 +394,27 @@ AKV_DEV void online_softmax(WarpState& s, float (&x)[2][4]) {
     }
 }
 
-// P (fp32, S^T C-fragment layout) -> B fragments of the PV MMA as fp16 hi + lo.
-AKV_DEV void p_fragments(const float (&x)[2][4], uint32_t (&ph)[2][2], uint32_t (&pl)[2][2]) {
+// P (fp32, S^T C-fragment layout) -> B fragments of the PV MMA (fp16).
+AKV_DEV void p_fragments(const float (&x)[2][4], uint32_t (&pb)[2][2]) {
 #pragma unroll
   for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      const __half2 hi = __floats2half2_rn(x[mt][2 * r], x[mt][2 * r + 1]);
-      const float2 hf = __half22float2(hi);
-      const __half2 lo = __floats2half2_rn(x[mt][2 * r] - hf.x, x[mt][2 * r + 1] - hf.y);
-      ph[mt][r] = movmatrix_trans(h2_as_u32(hi));
-      pl[mt][r] = movmatrix_trans(h2_as_u32(lo));
-    }
+    for (int r = 0; r < 2; ++r) pb[mt][r] = movmatrix_trans(pack_h2(x[mt][2 * r], x[mt][2 * r + 1]));
 }
 
 // P.V k-step over 16 tokens: for each of the 8 m-tiles (channel pairs 2mt,
 // 2mt+1 of this thread group), the two token pairs, dequantised exactly.
 template <int VB, int MT>
 AKV_DEV void pv_tiles(WarpState& st, const VPair<VB>& v0, const VPair<VB>& v1, __half2 s0, __half2 z0, __half2 s1,
-                      __half2 z1, const uint32_t (&ph)[2], const uint32_t (&pl)[2]) {
+                      __half2 z1, const uint32_t (&pb)[2]) {
   if constexpr (MT < 8) {
     constexpr int C0 = 2 * MT, C1 = 2 * MT + 1;
     const uint32_t a0 = dq<vmult<VB>(C0)>(v_raw<VB, C0>(v0), s0, z0);
     const uint32_t a1 = dq<vmult<VB>(C1)>(v_raw<VB, C1>(v0), s0, z0);
     const uint32_t a2 = dq<vmult<VB>(C0)>(v_raw<VB, C0>(v1), s1, z1);
     const uint32_t a3 = dq<vmult<VB>(C1)>(v_raw<VB, C1>(v1), s1, z1);
-    mma_16816(st.acc[MT], a0, a1, a2, a3, ph[0], ph[1]);
-    mma_16816(st.acc[MT], a0, a1, a2, a3, pl[0], pl[1]);
-    pv_tiles<VB, MT + 1>(st, v0, v1, s0, z0, s1, z1, ph, pl);
+    mma_16816(st.acc[MT], a0, a1, a2, a3, pb[0], pb[1]);
+    pv_tiles<VB, MT + 1>(st, v0, v1, s0, z0, s1, z1, pb);
   }
 }
 
@@ -627,8 +619,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 3) mixed_decode_kernel(const D
               x[mt][2 * rr + h] = valid[mt][rr] ? c[mt][2 * rr + h] * p.scale_log2 : -INFINITY;
           }
         online_softmax(st, x);
-        uint32_t ph[2][2], pl[2][2];
-        p_fragments(x, ph, pl);
+        uint32_t pb[2][2];
+        p_fragments(x, pb);
 
         // ---- O^T += V^ P  (head_dim x heads), k-steps of 16 tokens
 #pragma unroll
@@ -641,7 +633,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 3) mixed_decode_kernel(const D
           const __half2 z0 = *reinterpret_cast<const __half2*>(vzr + ta);
           const __half2 s1 = *reinterpret_cast<const __half2*>(vsc + ta + 8);
           const __half2 z1 = *reinterpret_cast<const __half2*>(vzr + ta + 8);
-          pv_tiles<VB, 0>(st, v0, v1, s0, z0, s1, z1, ph[ks], pl[ks]);
+          pv_tiles<VB, 0>(st, v0, v1, s0, z0, s1, z1, pb[ks]);
         }
 
         // ---- V outlier channels: add sum_t p_t * (original - dequantised) to their rows
@@ -730,8 +722,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 3) mixed_decode_kernel(const D
           for (int j = 0; j < 4; ++j) x[mt][j] = valid[mt][j >> 1] ? c[j] * p.scale_log2 : -INFINITY;
         }
         online_softmax(st, x);
-        uint32_t ph[2][2], pl[2][2];
-        p_fragments(x, ph, pl);
+        uint32_t pb[2][2];
+        p_fragments(x, pb);
 #pragma unroll
         for (int ks = 0; ks < 2; ++ks) {
           uint32_t va[4][8];
@@ -752,8 +744,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 3) mixed_decode_kernel(const D
             const uint32_t a1 = prmt(va[0][mt], va[1][mt], 0x7632);  // (ta, tb) at channel 2mt+1
             const uint32_t a2 = prmt(va[2][mt], va[3][mt], 0x5410);
             const uint32_t a3 = prmt(va[2][mt], va[3][mt], 0x7632);
-            mma_16816(st.acc[mt], a0, a1, a2, a3, ph[ks][0], ph[ks][1]);
-            mma_16816(st.acc[mt], a0, a1, a2, a3, pl[ks][0], pl[ks][1]);
+            mma_16816(st.acc[mt], a0, a1, a2, a3, pb[ks][0], pb[ks][1]);
           }
         }
       }
@@ -809,7 +800,7 @@ static DecodePlan plan_decode(int B, int Hq, int Hkv, int n_hot, int n_warm_bloc
   const int g = Hq / Hkv;
   pl.n_hg = (g + 7) / 8;
   const int units = B * Hkv * pl.n_hg;
-  const int target = 148 * 6;  // ~2 waves of 3 resident CTAs per SM
+  const int target = 148 * 6;  // ~1.5 waves of 4 resident CTAs per SM
   const int per_unit = max(1, (target + units - 1) / units);
   const int nhb = (n_hot + 31) / 32;
   const double wbytes = static_cast<double>(n_warm_blocks) * rec_bytes;
