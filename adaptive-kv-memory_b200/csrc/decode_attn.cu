@@ -5,9 +5,10 @@
 // (batch row, KV head, <= 8 query heads) and a contiguous range of 32-token
 // blocks (split-K over the sequence); an LSE combine merges the splits.
 //
-// Warm CTAs: one producer warp streams whole block records HBM -> SMEM with
-// 1-D bulk TMA (cp.async.bulk + mbarrier ring); consumer warps each take whole
-// blocks and dequantise them in registers exactly like the reference
+// Warm CTAs: every warp streams its own whole block records HBM -> SMEM with
+// 1-D bulk TMA (cp.async.bulk + one mbarrier per stage) into three private
+// stages, refilling a stage right after consuming it, and dequantises the
+// blocks in registers exactly like the reference
 // (akv/affine_quantizer.py:112-124, :178-189: fp16(fp16(code*scale) + zero),
 // outlier channels replaced by their fp16 originals), so the contraction sees
 // the same fp16 K/V values the reference attends over.  Packed codes become
@@ -29,8 +30,9 @@ namespace akv {
 
 constexpr int kHeadDim = 128;
 constexpr int kConsumerWarps = 4;
-constexpr int kDecodeThreads = (kConsumerWarps + 1) * 32;
-constexpr int kStages = 8;
+constexpr int kDecodeThreads = kConsumerWarps * 32;
+constexpr int kStagesPerWarp = 3;                          // blocks each warp keeps in flight
+constexpr int kStages = kConsumerWarps * kStagesPerWarp;
 constexpr int kMaxDecodeOutliers = 8;
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -472,7 +474,7 @@ AKV_DEV void cta_write_partial(const DecodeParams& p, float* red, float* rm, flo
 
 // ------------------------------------------------------------------ the kernel
 template <int KB, int VB>
-__global__ void __launch_bounds__(kDecodeThreads, 3) mixed_decode_kernel(const DecodeParams p) {
+__global__ void __launch_bounds__(kDecodeThreads, 4) mixed_decode_kernel(const DecodeParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g8 = lane >> 2, q4 = lane & 3;
@@ -483,8 +485,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 3) mixed_decode_kernel(const D
 
   // shared memory map
   const int rec = p.L.bytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-  uint64_t* empty = full + kStages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);        // [kStages], 96 bytes
   float* qs = reinterpret_cast<float*>(smem + 256);               // [8][128] query (fp32) for outliers
   unsigned char* stage0 = smem + 256 + 8 * kHeadDim * 4;          // [kStages][rec]
   // epilogue buffers alias the stages once the main loop is over
@@ -511,10 +512,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 3) mixed_decode_kernel(const D
     qs[i] = h < nh ? __half2float(p.q[b * p.q_sb + (qh_base + h) * p.q_sh + d]) : 0.f;
   }
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
-    }
+    for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
     fence_mbar_init();
   }
   __syncthreads();
@@ -529,32 +527,31 @@ __global__ void __launch_bounds__(kDecodeThreads, 3) mixed_decode_kernel(const D
     const int nb = max(0, bhi - blo);
     const uint8_t* wbase = p.warm + b * p.w_sb + kvh * p.w_sh + static_cast<int64_t>(blo) * rec;
 
-    if (warp == kConsumerWarps) {
-      // ---------------- producer: one lane streams records into the ring
+    {
+      // warp `warp` owns blocks i = warp + 4*li (li = 0, 1, ...) and stages
+      // warp*3 + li%3; lane 0 keeps up to three of its blocks in flight
+      uint64_t* wbar = full + warp * kStagesPerWarp;
+      unsigned char* wstage = stage0 + warp * kStagesPerWarp * rec;
+      const int nmine = nb > warp ? (nb - warp + kConsumerWarps - 1) / kConsumerWarps : 0;
       if (lane == 0) {
-        int issued = 0;
-        for (int i = 0; i < nb; ++i) {
-          const int s = i % kStages;
-          if (i >= kStages && !mbar_wait(&empty[s], ((i / kStages) - 1) & 1, p.status)) break;
-          mbar_arrive_expect_tx(&full[s], rec);
-          tma_load_1d(stage0 + s * rec, wbase + static_cast<int64_t>(i) * rec, rec, &full[s]);
-          issued = i + 1;
+        for (int li = 0; li < min(nmine, kStagesPerWarp); ++li) {
+          mbar_arrive_expect_tx(&wbar[li], rec);
+          tma_load_1d(wstage + li * rec, wbase + static_cast<int64_t>(warp + kConsumerWarps * li) * rec, rec,
+                      &wbar[li]);
         }
-        // drain: every issued copy has landed before the ring memory is reused
-        for (int i = max(0, issued - kStages); i < issued; ++i)
-          mbar_wait(&full[i % kStages], (i / kStages) & 1, p.status);
       }
-    } else {
       // ---------------- consumers
       uint32_t qp[16];
       q_pairs<KB>(qv, qp);
       const int n_out = p.L.n_outlier;
       const int kp = kHeadDim * KB / 8, vp = kHeadDim * VB / 8;
 
-      for (int i = warp; i < nb; i += kConsumerWarps) {
-        const int s = i % kStages;
-        if (!mbar_wait(&full[s], (i / kStages) & 1, p.status)) break;
-        const uint8_t* r = stage0 + s * rec;
+      int waited = 0;  // blocks whose copy this warp has seen land
+      for (int li = 0; li < nmine; ++li) {
+        const int s = li % kStagesPerWarp;
+        if (!mbar_wait(&wbar[s], (li / kStagesPerWarp) & 1, p.status)) break;
+        waited = li + 1;
+        const uint8_t* r = wstage + s * rec;
         const uint8_t* kc = r + p.L.kc;
         const uint8_t* vc = r + p.L.vc;
         const __half* vsc = reinterpret_cast<const __half*>(r + p.L.vs);
@@ -673,14 +670,26 @@ __global__ void __launch_bounds__(kDecodeThreads, 3) mixed_decode_kernel(const D
             }
           }
         }
+        // refill this stage with the warp's block li+3 once every lane is done reading it
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
+        if (lane == 0 && li + kStagesPerWarp < nmine) {
+          fence_proxy_async_shared();
+          mbar_arrive_expect_tx(&wbar[s], rec);
+          tma_load_1d(wstage + s * rec,
+                      wbase + static_cast<int64_t>(warp + kConsumerWarps * (li + kStagesPerWarp)) * rec, rec,
+                      &wbar[s]);
+        }
       }
+      // after a timed-out wait, let the copies still in flight land before the
+      // stages are reused as epilogue scratch (bounded waits)
+      if (lane == 0)
+        for (int li = waited; li < min(nmine, waited + kStagesPerWarp); ++li)
+          mbar_wait(&wbar[li % kStagesPerWarp], (li / kStagesPerWarp) & 1, p.status);
 #pragma unroll
       for (int jj = 0; jj < kRegOutliers; ++jj) acc_add_row(st, g8, st.vch[jj], st.vcorr[jj][0], st.vcorr[jj][1]);
     }
   } else {
-    // ---------------- hot CTA: FP16 window, 128-bit loads, all warps consume (producer warp too)
+    // ---------------- hot CTA: FP16 window, 128-bit loads
     const int hs = split - p.warm_splits;
     const int nhot_b = p.hot_len ? min(p.hot_len[b], p.n_hot) : p.n_hot;
     const int nhb = (nhot_b + 31) / 32;
@@ -753,8 +762,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 3) mixed_decode_kernel(const D
 
   // ---------------- epilogue: merge consumer warps, write the split partial
   __syncthreads();
-  if (warp < kConsumerWarps)
-    warp_to_smem(st, lane, red + warp * 8 * kHeadDim, rm + warp * 8, rl + warp * 8);
+  warp_to_smem(st, lane, red + warp * 8 * kHeadDim, rm + warp * 8, rl + warp * 8);
   __syncthreads();
   cta_write_partial(p, red, rm, rl, b, kvh, hg, split);
 }
