@@ -91,6 +91,17 @@ AKV_DEV void tma_load_1d(void* dst_smem, const void* src_gmem, uint32_t bytes, u
 }
 
 // ---------------------------------------------------------------- loads
+// 16-byte global -> shared copy that bypasses registers and L1 (cp.async.cg);
+// both addresses 16-byte aligned.
+AKV_DEV void cp_async16(void* dst_smem, const void* src_gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst_smem)), "l"(src_gmem) : "memory");
+}
+
+// Wait until every cp.async this thread issued has landed in shared memory.
+AKV_DEV void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
 AKV_DEV uint4 ldg_nc_v4(const void* p) {
   uint4 r;
   asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"

@@ -9,10 +9,17 @@
 // The clamp(min=1e-8) of the reference is a no-op in fp16 (1e-8 underflows
 // to 0), so a zero-range group keeps scale 0 and its 0/0 codes become 0.
 //
-// One CTA quantises one scale group (all heads of one batch row): it stages
-// the group's fp16 rows in shared memory with 128-bit loads, runs the
-// outlier-channel selection and the min/max reductions there, then encodes
-// and packs 32 codes per thread.
+// One CTA quantises one scale group (all heads of one batch row, up to three
+// CTAs per SM): cp.async stages the group's fp16 rows in shared memory, one
+// pass over the columns yields the outlier norms and the key min/max, a pass
+// over the rows yields the value min/max, and the encode pass turns 8
+// channels of one token into BITS packed bytes per work item.  The division
+// is exact without a divide: with r = RN(1/s) precomputed per scale,
+//   q0 = x*r,  e = fma(-s, q0, x),  q = fma(e, r, q0)
+// equals RN(x/s) for every pair of non-negative finite fp16 x and s (checked
+// exhaustively against double division, all 2^30 pairs).  fp16(q) + 1024 in
+// fp16 is 1024 + rint(fp16(q)) with ties to even, so one packed fp16 add
+// rounds, and a max/min pair clamps (max(NaN, 1024) = 1024: NaN -> code 0).
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -32,59 +39,90 @@ struct QuantParams {
 };
 
 constexpr int kQuantThreads = 256;
+constexpr int kQuantCtasPerSm = 3;
 constexpr int kMaxOutliers = 32;
-
-__host__ __device__ inline int pad_pitch(int D) { return D + 8; }  // halves; +16 B per row
+constexpr int kEncChunk = 8;               // channels per encode work item (one 16-byte shared load)
+constexpr float kZeroScale = 0x1p-100f;    // stands in for scale 0: x > 0 -> beyond fp16 -> maxval; 0 -> 0
+constexpr uint32_t kMagic2 = 0x64006400u;  // (1024, 1024) as fp16x2
 
 AKV_DEV char* vaddr(const akv_view& v, int b, int h, int blk, int slot) {
   return static_cast<char*>(v.ptr) + b * v.sb + h * v.sh + blk * v.sblk + slot * v.sslot;
 }
 
-AKV_DEV uint32_t quant_code(float x, float zero, float scale, float maxval) {
-  const float diff = __half2float(__float2half_rn(__fsub_rn(x, zero)));
-  float r = __half2float(__float2half_rn(__fdiv_rn(diff, scale)));
-  r = rintf(r);
-  r = fminf(fmaxf(r, 0.0f), maxval);  // fmaxf(NaN, 0) == 0: the reference's NaN -> 0 cast
-  return static_cast<uint32_t>(r);
+// fp16 scale -> (s_eff, RN(1/s_eff)) for the exact division below.
+AKV_DEV float scale_eff(__half s) {
+  const float f = __half2float(s);
+  return f == 0.f ? kZeroScale : f;
 }
 
-// Pack 32 codes (c[0..31]) into 4*BITS bytes following akv/bitpack.py, as
-// little-endian u32 words w[0..BITS-1].
+// RN(x / s) for x = fp16 value >= 0, s = scale_eff(), r = RN(1/s).
+AKV_DEV float div_exact(float x, float s, float r) {
+  const float q0 = __fmul_rn(x, r);
+  const float e = __fmaf_rn(-s, q0, x);
+  return __fmaf_rn(e, r, q0);
+}
+
+// scale = fp16(fp16(hi - lo) / maxval) from fp16 min/max.
+AKV_DEV __half affine_scale(__half lo, __half hi, float maxval) {
+  const float range = __half2float(__float2half_rn(__fsub_rn(__half2float(hi), __half2float(lo))));
+  return __float2half_rn(__fdiv_rn(range, maxval));
+}
+
+// Two codes as (1024 + c0, 1024 + c1) fp16x2 ("magic" form: the low byte of
+// each half is the code).
 template <int BITS>
-AKV_DEV void pack32(const uint32_t (&c)[32], uint32_t (&w)[BITS]) {
+AKV_DEV uint32_t encode_pair(uint32_t x2, uint32_t z2, float s0, float s1, float r0, float r1) {
+  constexpr uint32_t top = kMagic2 + ((1u << BITS) - 1) * 0x00010001u;
+  const float2 d = __half22float2(__hsub2_rn(u32_as_h2(x2), u32_as_h2(z2)));
+  __half2 h = __floats2half2_rn(div_exact(d.x, s0, r0), div_exact(d.y, s1, r1));
+  h = __hadd2_rn(h, u32_as_h2(kMagic2));
+  h = __hmin2(__hmax2(h, u32_as_h2(kMagic2)), u32_as_h2(top));
+  return h2_as_u32(h);
+}
+
+template <int BITS>
+AKV_DEV uint32_t encode_one(__half x, __half z, float s, float r) {
+  const float d = __half2float(__hsub_rn(x, z));
+  __half h = __hadd_rn(__float2half_rn(div_exact(d, s, r)), __ushort_as_half(0x6400));
+  h = __hmin(__hmax(h, __ushort_as_half(0x6400)), __ushort_as_half(0x6400 + (1 << BITS) - 1));
+  return __half_as_ushort(h) & 0xFFu;
+}
+
+// 8 codes in magic form (m[i] = channels 2i, 2i+1) -> packed bytes (akv/bitpack.py):
+//   4 bits: 4 bytes, even channel in the high nibble;
+//   2 bits: 2 bytes (low half), first channel in the two high bits;
+//   3 bits: one 24-bit big-endian group in bytes 0..2.
+template <int BITS>
+AKV_DEV uint32_t pack8(const uint32_t (&m)[4]) {
   if constexpr (BITS == 4) {
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      uint32_t x = 0;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) x |= ((c[8 * k + 2 * i] << 4) | c[8 * k + 2 * i + 1]) << (8 * i);
-      w[k] = x;
-    }
+    const uint32_t va = prmt(m[0], m[1], 0x6420), vb = prmt(m[2], m[3], 0x6420);  // bytes = codes
+    const uint32_t ta = ((va << 4) & 0x00F000F0u) | ((va >> 8) & 0x000F000Fu);
+    const uint32_t tb = ((vb << 4) & 0x00F000F0u) | ((vb >> 8) & 0x000F000Fu);
+    return prmt(ta, tb, 0x6420);
   } else if constexpr (BITS == 2) {
+    // bytes (c0, c1, c2, c3) * (2^30 + 2^20 + 2^10 + 1): the top byte collects
+    // c0<<6 | c1<<4 | c2<<2 | c3 and the cross terms stay below bit 24
+    const uint32_t pa = prmt(m[0], m[1], 0x6420) * 0x40100401u;
+    const uint32_t pb = prmt(m[2], m[3], 0x6420) * 0x40100401u;
+    return prmt(pa, pb, 0x4473);
+  } else {
+    uint32_t w = 0;
 #pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      uint32_t x = 0;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int j = 16 * k + 4 * i;
-        x |= ((c[j] << 6) | (c[j + 1] << 4) | (c[j + 2] << 2) | c[j + 3]) << (8 * i);
-      }
-      w[k] = x;
-    }
-  } else {  // 3 bits: 8 codes -> 24-bit big-endian group -> 3 bytes
-    uint32_t bytes[12];
-#pragma unroll
-    for (int gq = 0; gq < 4; ++gq) {
-      uint32_t word = 0;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) word |= c[8 * gq + j] << (21 - 3 * j);
-      bytes[3 * gq + 0] = (word >> 16) & 0xFF;
-      bytes[3 * gq + 1] = (word >> 8) & 0xFF;
-      bytes[3 * gq + 2] = word & 0xFF;
-    }
-#pragma unroll
-    for (int k = 0; k < 3; ++k)
-      w[k] = bytes[4 * k] | (bytes[4 * k + 1] << 8) | (bytes[4 * k + 2] << 16) | (bytes[4 * k + 3] << 24);
+    for (int i = 0; i < 4; ++i) w |= ((m[i] & 7u) << (21 - 6 * i)) | (((m[i] >> 16) & 7u) << (18 - 6 * i));
+    return prmt(w, 0u, 0x4012);
+  }
+}
+
+template <int BITS>
+AKV_DEV void store_packed8(char* p, uint32_t w) {
+  if constexpr (BITS == 4) {
+    *reinterpret_cast<uint32_t*>(p) = w;
+  } else if constexpr (BITS == 2) {
+    *reinterpret_cast<uint16_t*>(p) = static_cast<uint16_t>(w);
+  } else {
+    p[0] = static_cast<char>(w);
+    p[1] = static_cast<char>(w >> 8);
+    p[2] = static_cast<char>(w >> 16);
   }
 }
 
@@ -124,80 +162,114 @@ AKV_DEV void unpack32(const uint32_t (&w)[BITS], uint32_t (&c)[32]) {
 }
 
 template <int BITS>
-AKV_DEV void store_words(char* p, const uint32_t (&w)[BITS]) {
-  if constexpr (BITS == 4) {
-    if ((reinterpret_cast<uintptr_t>(p) & 15) == 0) {
-      *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
-      return;
-    }
-  } else if constexpr (BITS == 2) {
-    if ((reinterpret_cast<uintptr_t>(p) & 7) == 0) {
-      *reinterpret_cast<uint2*>(p) = make_uint2(w[0], w[1]);
-      return;
-    }
-  }
-#pragma unroll
-  for (int k = 0; k < BITS; ++k) reinterpret_cast<uint32_t*>(p)[k] = w[k];
-}
-
-template <int BITS>
 AKV_DEV void load_words(const char* p, uint32_t (&w)[BITS]) {
 #pragma unroll
   for (int k = 0; k < BITS; ++k) w[k] = reinterpret_cast<const uint32_t*>(p)[k];
+}
+
+// Shared memory of one quantiser CTA (byte offsets; rows = H * nt):
+//   xs    [rows][D]    fp16   the group's tokens (outlier channels zeroed later)
+//   cz    [ncoef]      fp16   zero = min      (keys: per (head, channel); values: per row)
+//   cs    [ncoef]      fp16   max, then scale
+//   cr    [ncoef]      fp32   RN(1 / scale_eff)       -- shares its space with
+//   norms [H][D]       fp32   per-(head, channel) L2 norms (dead before cr is written)
+//   score [D] fp32, oidx [kMaxOutliers] int, od_s [rows][n_out] fp16 originals
+struct QuantSmem {
+  size_t cz, cs, cr, score, oidx, od, total;
+};
+
+__host__ __device__ inline QuantSmem quant_smem_layout(int H, int nt, int D, int n_out, bool is_key) {
+  QuantSmem m{};
+  const size_t rows = static_cast<size_t>(H) * nt, hd = static_cast<size_t>(H) * D;
+  const size_t ncoef = is_key ? hd : rows;
+  m.cz = rows * D * 2;
+  m.cs = m.cz + ncoef * 2;
+  m.cr = m.cs + ncoef * 2;  // 4-byte aligned: cz is, and 4*ncoef bytes lie between
+  m.score = m.cr + (ncoef > hd ? ncoef : hd) * 4;
+  m.oidx = m.score + static_cast<size_t>(D) * 4;
+  m.od = m.oidx + kMaxOutliers * 4;
+  m.total = m.od + rows * n_out * 2;
+  return m;
 }
 
 // ---------------------------------------------------------------------------
 // quantise: grid (n_groups, B), block kQuantThreads
 // ---------------------------------------------------------------------------
 template <int BITS, bool IS_KEY>
-__global__ void __launch_bounds__(kQuantThreads) quantize_group_kernel(const QuantParams p) {
+__global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group_kernel(const QuantParams p) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int tid = threadIdx.x;
   const int b = blockIdx.y;
   const int t0 = blockIdx.x * p.group;
   const int nt = min(p.group, p.N - t0);
-  const int H = p.H, D = p.D;
-  const int pitch = pad_pitch(D);
+  const int H = p.H, D = p.D, D2 = D / 2;
+  const int rows = H * nt;
   const float maxval = static_cast<float>((1 << BITS) - 1);
+  const QuantSmem lay = quant_smem_layout(H, nt, D, p.n_out, IS_KEY);
 
-  __half* xs = reinterpret_cast<__half*>(smem_raw);                      // [H][nt][pitch]
-  __half* kmin = xs + static_cast<size_t>(H) * nt * pitch;               // [H][D] (keys)
-  __half* kmax = kmin + H * D;                                           // [H][D] -> scale
-  float* norms = reinterpret_cast<float*>(kmax + H * D);                 // [H][D]
-  float* score = norms + H * D;                                          // [D]
-  int* oidx = reinterpret_cast<int*>(score + D);                         // [kMaxOutliers]
-  __half* od_s = reinterpret_cast<__half*>(oidx + kMaxOutliers);         // [H][nt][n_out] originals
-
-  // ---- stage the group's rows (128-bit loads, 16 B per thread-iteration)
-  const int vpr = D / 8;
-  for (int v = tid; v < H * nt * vpr; v += kQuantThreads) {
-    const int c = v % vpr;
-    const int r = v / vpr;
-    const int t = r % nt;
-    const int h = r / nt;
-    const int64_t row = p.tok_idx ? p.tok_idx[b * p.tok_sb + t0 + t] : static_cast<int64_t>(t0 + t);
-    const __half* g = p.src + b * p.sb + h * p.sh + row * p.sn + c * 8;
-    *reinterpret_cast<uint4*>(xs + (static_cast<size_t>(h) * nt + t) * pitch + c * 8) = ldg_nc_v4(g);
-  }
-  __syncthreads();
-
+  __half* xs = reinterpret_cast<__half*>(smem_raw);
+  __half* cz = reinterpret_cast<__half*>(smem_raw + lay.cz);
+  __half* cs = reinterpret_cast<__half*>(smem_raw + lay.cs);
+  float* cr = reinterpret_cast<float*>(smem_raw + lay.cr);
+  float* norms = cr;
+  float* score = reinterpret_cast<float*>(smem_raw + lay.score);
+  int* oidx = reinterpret_cast<int*>(smem_raw + lay.oidx);
+  __half* od_s = reinterpret_cast<__half*>(smem_raw + lay.od);
   const __half2* xs2 = reinterpret_cast<const __half2*>(xs);
-  const int p2 = pitch / 2;
 
-  // ---- outlier channels (affine_quantizer.py:75-85 / :143-151)
-  if (p.n_out > 0) {
-    for (int w = tid; w < H * (D / 2); w += kQuantThreads) {
-      const int h = w / (D / 2), dp = w % (D / 2);
-      float s0 = 0.f, s1 = 0.f;
-      for (int t = 0; t < nt; ++t) {
-        const float2 x = __half22float2(xs2[(h * nt + t) * p2 + dp]);
-        s0 = fmaf(x.x, x.x, s0);
-        s1 = fmaf(x.y, x.y, s1);
+  // ---- stage the group's rows: 16-byte cp.async, all in flight at once
+  {
+    const int vpr = D / 8;
+    for (int v = tid; v < rows * vpr; v += kQuantThreads) {
+      const int c = v % vpr;
+      const int r = v / vpr;
+      const int t = r % nt;
+      const int h = r / nt;
+      const int64_t row = p.tok_idx ? p.tok_idx[b * p.tok_sb + t0 + t] : static_cast<int64_t>(t0 + t);
+      cp_async16(xs + r * D + c * 8, p.src + b * p.sb + h * p.sh + row * p.sn + c * 8);
+    }
+    cp_async_wait_all();
+    __syncthreads();
+  }
+
+  // ---- one pass over the columns: outlier norms (affine_quantizer.py:75-85 /
+  //      :143-151) and, for keys, the per-(head, channel) min/max
+  if (p.n_out > 0 || IS_KEY) {
+    for (int w = tid; w < H * D2; w += kQuantThreads) {
+      const int h = w / D2, dp = w % D2;
+      const __half2* col = xs2 + h * nt * D2 + dp;
+      __half2 mn = __float2half2_rn(INFINITY), mx = __float2half2_rn(-INFINITY);
+      if (p.n_out > 0) {
+        float s0 = 0.f, s1 = 0.f;
+        for (int t = 0; t < nt; ++t) {
+          const __half2 x = col[t * D2];
+          const float2 f = __half22float2(x);
+          s0 = fmaf(f.x, f.x, s0);
+          s1 = fmaf(f.y, f.y, s1);
+          if constexpr (IS_KEY) {
+            mn = __hmin2(mn, x);
+            mx = __hmax2(mx, x);
+          }
+        }
+        norms[h * D + 2 * dp] = sqrtf(s0);
+        norms[h * D + 2 * dp + 1] = sqrtf(s1);
+      } else {
+        for (int t = 0; t < nt; ++t) {
+          const __half2 x = col[t * D2];
+          mn = __hmin2(mn, x);
+          mx = __hmax2(mx, x);
+        }
       }
-      norms[h * D + 2 * dp] = sqrtf(s0);
-      norms[h * D + 2 * dp + 1] = sqrtf(s1);
+      if constexpr (IS_KEY) {
+        reinterpret_cast<__half2*>(cz)[w] = mn;
+        reinterpret_cast<__half2*>(cs)[w] = mx;
+      }
     }
     __syncthreads();
+  }
+
+  // ---- outlier channels: score = mean over heads of the norms, top-n
+  if (p.n_out > 0) {
     for (int d = tid; d < D; d += kQuantThreads) {
       float s = 0.f;
       for (int h = 0; h < H; ++h) s += norms[h * D + d];
@@ -228,14 +300,13 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_group_kernel(const Qua
     __syncthreads();
     // side store: fp16 originals of the outlier channels, then their ids
     const akv_view& od = p.dst.out_data;
-    for (int w = tid; w < H * nt * p.n_out; w += kQuantThreads) {
+    for (int w = tid; w < rows * p.n_out; w += kQuantThreads) {
       const int j = w % p.n_out;
-      const int t = (w / p.n_out) % nt;
-      const int h = w / (p.n_out * nt);
-      const int tt = t0 + t;
-      const __half o = xs[(static_cast<size_t>(h) * nt + t) * pitch + oidx[j]];
-      od_s[w] = o;  // w == (h*nt + t)*n_out + j
-      if (od.ptr) reinterpret_cast<__half*>(vaddr(od, b, h, tt / kBlockTokens, tt % kBlockTokens))[j] = o;
+      const int r = w / p.n_out;
+      const int tt = t0 + r % nt;
+      const __half o = xs[r * D + oidx[j]];
+      od_s[w] = o;  // w == r*n_out + j
+      if (od.ptr) reinterpret_cast<__half*>(vaddr(od, b, r / nt, tt / kBlockTokens, tt % kBlockTokens))[j] = o;
     }
     const akv_view& oi = p.dst.out_idx;
     if (oi.ptr) {
@@ -248,125 +319,130 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_group_kernel(const Qua
       }
     }
     __syncthreads();
-    // zero the outlier channels before min/max (affine_quantizer.py:84-85)
-    for (int w = tid; w < H * nt * p.n_out; w += kQuantThreads) {
-      const int j = w % p.n_out;
-      const int r = w / p.n_out;
-      xs[static_cast<size_t>(r) * pitch + oidx[j]] = __float2half_rn(0.0f);
+    // zero the outlier channels before min/max (affine_quantizer.py:84-85); a
+    // zeroed key column has min = max = 0
+    for (int w = tid; w < rows * p.n_out; w += kQuantThreads)
+      xs[(w / p.n_out) * D + oidx[w % p.n_out]] = __float2half_rn(0.0f);
+    if constexpr (IS_KEY) {
+      for (int w = tid; w < H * p.n_out; w += kQuantThreads) {
+        const int c = (w / p.n_out) * D + oidx[w % p.n_out];
+        cz[c] = cs[c] = __float2half_rn(0.0f);
+      }
     }
     __syncthreads();
   }
 
-  // ---- keys: per-(head, channel) min/max over the group's tokens -> scale/zero
   if constexpr (IS_KEY) {
-    for (int w = tid; w < H * (D / 2); w += kQuantThreads) {
-      const int h = w / (D / 2), dp = w % (D / 2);
-      __half2 mn = __float2half2_rn(INFINITY), mx = __float2half2_rn(-INFINITY);
-      for (int t = 0; t < nt; ++t) {
-        const __half2 x = xs2[(h * nt + t) * p2 + dp];
-        mn = __hmin2(mn, x);
-        mx = __hmax2(mx, x);
-      }
-      const float2 lo = __half22float2(mn), hi = __half22float2(mx);
-      const float sc0 = __half2float(__float2half_rn(__fsub_rn(hi.x, lo.x)));
-      const float sc1 = __half2float(__float2half_rn(__fsub_rn(hi.y, lo.y)));
-      reinterpret_cast<__half2*>(kmin)[w] = mn;
-      reinterpret_cast<__half2*>(kmax)[w] =
-          __halves2half2(__float2half_rn(__fdiv_rn(sc0, maxval)), __float2half_rn(__fdiv_rn(sc1, maxval)));
+    // ---- keys: scale per (head, channel), written once per block record
+    for (int w = tid; w < H * D; w += kQuantThreads) {
+      const __half sc = affine_scale(cz[w], cs[w], maxval);
+      cs[w] = sc;
+      cr[w] = __frcp_rn(scale_eff(sc));
     }
     __syncthreads();
     const int blk0 = t0 / kBlockTokens, nblk = (t0 + nt - 1) / kBlockTokens - blk0 + 1;
-    for (int w = tid; w < H * nblk * (D / 2); w += kQuantThreads) {
-      const int dp = w % (D / 2);
-      const int bl = (w / (D / 2)) % nblk;
-      const int h = w / ((D / 2) * nblk);
+    for (int w = tid; w < H * nblk * D2; w += kQuantThreads) {
+      const int dp = w % D2;
+      const int bl = (w / D2) % nblk;
+      const int h = w / (D2 * nblk);
       if (p.dst.scale.ptr)
         reinterpret_cast<__half2*>(vaddr(p.dst.scale, b, h, blk0 + bl, 0))[dp] =
-            reinterpret_cast<const __half2*>(kmax)[h * (D / 2) + dp];
+            reinterpret_cast<const __half2*>(cs)[h * D2 + dp];
       if (p.dst.zero.ptr)
         reinterpret_cast<__half2*>(vaddr(p.dst.zero, b, h, blk0 + bl, 0))[dp] =
-            reinterpret_cast<const __half2*>(kmin)[h * (D / 2) + dp];
+            reinterpret_cast<const __half2*>(cz)[h * D2 + dp];
     }
-  }
-
-  // ---- encode + pack: one thread per (head, token, 32-code chunk)
-  const int nsu = D / 32;  // 1..8, divides 32
-  const int total = H * nt * nsu;
-  const int rounds = (total + kQuantThreads - 1) / kQuantThreads;
-  for (int rd = 0; rd < rounds; ++rd) {
-    const int w = rd * kQuantThreads + tid;
-    const bool valid = w < total;
-    const int su = w % nsu;
-    const int r = valid ? w / nsu : 0;
-    const int t = r % nt;
-    const int h = r / nt;
-    const __half* row = xs + static_cast<size_t>(r) * pitch + su * 32;
-    __half x[32];
+  } else {
+    // ---- values: per-token min/max over D, one thread per row; the 16-byte
+    //      chunks are visited from a row-dependent start so that neighbouring
+    //      rows hit different banks
+    const int nc = D / 8;
+    for (int r = tid; r < rows; r += kQuantThreads) {
+      const __half* xr = xs + r * D;
+      __half2 mn = __float2half2_rn(INFINITY), mx = __float2half2_rn(-INFINITY);
+      int c = r % nc;
+      for (int j = 0; j < nc; ++j) {
+        const uint4 v = lds_v4(xr + 8 * c);
+        const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-    for (int k = 0; k < 4; ++k) *reinterpret_cast<uint4*>(x + 8 * k) = lds_v4(row + 8 * k);
-    float zf[32], sf[32];
-    if constexpr (IS_KEY) {
-#pragma unroll
-      for (int k = 0; k < 32; ++k) {
-        zf[k] = __half2float(kmin[h * D + su * 32 + k]);
-        sf[k] = __half2float(kmax[h * D + su * 32 + k]);
+        for (int i = 0; i < 4; ++i) {
+          mn = __hmin2(mn, u32_as_h2(w4[i]));
+          mx = __hmax2(mx, u32_as_h2(w4[i]));
+        }
+        c = (c + 1 == nc) ? 0 : c + 1;
       }
-    } else {
-      // per-token min/max over D: reduce this chunk, then across the nsu lanes of the row
-      __half mn = x[0], mx = x[0];
-#pragma unroll
-      for (int k = 1; k < 32; ++k) {
-        mn = __hmin(mn, x[k]);
-        mx = __hmax(mx, x[k]);
-      }
-      for (int o = 1; o < nsu; o <<= 1) {
-        const __half omn = __shfl_xor_sync(0xffffffffu, mn, o);
-        const __half omx = __shfl_xor_sync(0xffffffffu, mx, o);
-        mn = __hmin(mn, omn);
-        mx = __hmax(mx, omx);
-      }
-      const float lo = __half2float(mn), hi = __half2float(mx);
-      const float range = __half2float(__float2half_rn(__fsub_rn(hi, lo)));
-      const __half sc = __float2half_rn(__fdiv_rn(range, maxval));
-      if (valid && su == 0) {
-        const int tt = t0 + t;
-        if (p.dst.scale.ptr)
-          *reinterpret_cast<__half*>(vaddr(p.dst.scale, b, h, tt / kBlockTokens, tt % kBlockTokens)) = sc;
-        if (p.dst.zero.ptr)
-          *reinterpret_cast<__half*>(vaddr(p.dst.zero, b, h, tt / kBlockTokens, tt % kBlockTokens)) = mn;
-      }
-#pragma unroll
-      for (int k = 0; k < 32; ++k) {
-        zf[k] = lo;
-        sf[k] = __half2float(sc);
-      }
-    }
-    if (!valid) continue;
-    uint32_t c[32];
-#pragma unroll
-    for (int k = 0; k < 32; ++k) c[k] = quant_code(__half2float(x[k]), zf[k], sf[k], maxval);
-    if constexpr (!IS_KEY) {
+      const __half lo = __hmin(__low2half(mn), __high2half(mn));
+      const __half hi = __hmax(__low2half(mx), __high2half(mx));
+      const __half sc = affine_scale(lo, hi, maxval);
+      const float se = scale_eff(sc), rc = __frcp_rn(se);
+      cz[r] = lo;
+      cs[r] = sc;
+      cr[r] = rc;
+      const int h = r / nt, tt = t0 + r % nt;
+      const int blk = tt / kBlockTokens, slot = tt % kBlockTokens;
+      if (p.dst.scale.ptr) *reinterpret_cast<__half*>(vaddr(p.dst.scale, b, h, blk, slot)) = sc;
+      if (p.dst.zero.ptr) *reinterpret_cast<__half*>(vaddr(p.dst.zero, b, h, blk, slot)) = lo;
       // outlier residual: fp16 original minus what the zeroed channel dequantises to
       if (p.n_out > 0 && p.dst.out_resid.ptr) {
-        const int tt = t0 + t;
-        float* rp = reinterpret_cast<float*>(vaddr(p.dst.out_resid, b, h, tt / kBlockTokens, tt % kBlockTokens));
-        for (int j = 0; j < p.n_out; ++j) {
-          const int d = oidx[j] - su * 32;
-          if (d < 0 || d >= 32) continue;
-          uint32_t cv = 0;
-#pragma unroll
-          for (int k = 0; k < 32; ++k)
-            if (k == d) cv = c[k];
-          const __half deq = __hadd_rn(__hmul_rn(__uint2half_rn(cv), __float2half_rn(sf[0])), __float2half_rn(zf[0]));
-          rp[j] = __half2float(od_s[(h * nt + t) * p.n_out + j]) - __half2float(deq);
-        }
+        float* rp = reinterpret_cast<float*>(vaddr(p.dst.out_resid, b, h, blk, slot));
+        const uint32_t c0 = encode_one<BITS>(__float2half_rn(0.0f), lo, se, rc);
+        const __half deq = __hadd_rn(__hmul_rn(__uint2half_rn(c0), sc), lo);
+        for (int j = 0; j < p.n_out; ++j) rp[j] = __half2float(od_s[r * p.n_out + j]) - __half2float(deq);
       }
     }
-    uint32_t wds[BITS];
-    pack32<BITS>(c, wds);
-    const int tt = t0 + t;
-    if (p.dst.codes.ptr)
-      store_words<BITS>(vaddr(p.dst.codes, b, h, tt / kBlockTokens, tt % kBlockTokens) + su * 4 * BITS, wds);
+  }
+  __syncthreads();
+
+  // ---- encode + pack: a work item is 8 channels of one head; its threads walk
+  //      the tokens (keys keep the 8 channels' zero / scale / 1/scale in registers)
+  {
+    const int ncs = D / kEncChunk;
+    const int cols = H * ncs;
+    const int tpc = max(1, kQuantThreads / cols);
+    for (int w = tid; w < cols * tpc; w += kQuantThreads) {
+      const int col = w % cols, sub = w / cols;
+      const int h = col / ncs, c8 = col % ncs;
+      uint32_t z2[4];
+      float sf[8], rf[8];
+      if constexpr (IS_KEY) {
+        const int c0 = h * D + c8 * kEncChunk;
+        const uint4 zz = lds_v4(cz + c0);
+        const uint4 ss = lds_v4(cs + c0);
+        z2[0] = zz.x; z2[1] = zz.y; z2[2] = zz.z; z2[3] = zz.w;
+        const uint32_t s2[4] = {ss.x, ss.y, ss.z, ss.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          sf[2 * i] = scale_eff(__low2half(u32_as_h2(s2[i])));
+          sf[2 * i + 1] = scale_eff(__high2half(u32_as_h2(s2[i])));
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) rf[i] = cr[c0 + i];
+      }
+      for (int t = sub; t < nt; t += tpc) {
+        const int r = h * nt + t;
+        if constexpr (!IS_KEY) {
+          const __half zh = cz[r];
+          const float se = scale_eff(cs[r]), rc = cr[r];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) z2[i] = h2_as_u32(__half2half2(zh));
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            sf[i] = se;
+            rf[i] = rc;
+          }
+        }
+        const uint4 xv = lds_v4(xs + r * D + c8 * kEncChunk);
+        const uint32_t x2[4] = {xv.x, xv.y, xv.z, xv.w};
+        uint32_t m[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          m[i] = encode_pair<BITS>(x2[i], z2[i], sf[2 * i], sf[2 * i + 1], rf[2 * i], rf[2 * i + 1]);
+        const int tt = t0 + t;
+        if (p.dst.codes.ptr)
+          store_packed8<BITS>(vaddr(p.dst.codes, b, h, tt / kBlockTokens, tt % kBlockTokens) + c8 * BITS,
+                              pack8<BITS>(m));
+      }
+    }
   }
 
   // ---- valid-slot masks for the blocks this group wrote
@@ -507,16 +583,15 @@ __global__ void unpack_codes_kernel(const uint8_t* packed, int64_t rows, int dim
 // ---------------------------------------------------------------------------
 static inline bool aligned(const void* p, int a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
-size_t quant_smem_bytes(int H, int nt, int D, int n_out) {
-  return static_cast<size_t>(H) * nt * pad_pitch(D) * 2 + static_cast<size_t>(H) * D * 4 +
-         static_cast<size_t>(H) * D * 4 + D * 4 + kMaxOutliers * 4 + static_cast<size_t>(H) * nt * n_out * 2;
+size_t quant_smem_bytes(int H, int nt, int D, int n_out, bool is_key) {
+  return quant_smem_layout(H, nt, D, n_out, is_key).total;
 }
 
 template <int BITS, bool IS_KEY>
 static int launch_quant(const QuantParams& p, cudaStream_t st) {
   const int ngroups = (p.N + p.group - 1) / p.group;
   const int nt = min(p.group, p.N);
-  const size_t smem = quant_smem_bytes(p.H, nt, p.D, p.n_out);
+  const size_t smem = quant_smem_bytes(p.H, nt, p.D, p.n_out, IS_KEY);
   auto kern = quantize_group_kernel<BITS, IS_KEY>;
   if (smem > 48 * 1024) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
@@ -563,7 +638,7 @@ extern "C" int akv_quantize(const uint16_t* src, int64_t src_sb, int64_t src_sh,
     return AKV_ERR_ALIGN;
   if (dst->mask.ptr && !aligned(dst->mask.ptr, 4)) return AKV_ERR_ALIGN;
   if (dst->out_resid.ptr && (!aligned(dst->out_resid.ptr, 4) || dst->out_resid.sslot % 4)) return AKV_ERR_ALIGN;
-  if (quant_smem_bytes(H, group, D, n_outlier) > 220 * 1024) return AKV_ERR_UNSUPPORTED;
+  if (quant_smem_bytes(H, group, D, n_outlier, is_key != 0) > 220 * 1024) return AKV_ERR_UNSUPPORTED;
   QuantParams p{reinterpret_cast<const __half*>(src), src_sb, src_sh, src_sn, tok_idx, tok_sb, B, H, N, D,
                 bits, is_key, group, n_outlier, *dst, status};
   cudaStream_t st = static_cast<cudaStream_t>(stream);
