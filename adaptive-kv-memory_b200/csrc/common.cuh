@@ -163,6 +163,40 @@ AKV_DEV uint32_t movmatrix_trans(uint32_t a) {
   return d;
 }
 
+// ---------------------------------------------------------------- packed fp32 (sm_100)
+// Two IEEE fp32 lanes per 64-bit register; each lane rounds like the scalar op.
+AKV_DEV uint64_t f2_make(float lo, float hi) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
+  return d;
+}
+
+AKV_DEV float2 f2_split(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+
+AKV_DEV uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+AKV_DEV uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+// c + a*b for fp16 a, b and fp32 c with one rounding; the fp16 product is
+// exact in fp32, so this equals fmaf(float(a), float(b), c).
+AKV_DEV float fma_f16_f32(__half a, __half b, float c) {
+  float d;
+  asm("fma.rn.f32.f16 %0, %1, %2, %3;" : "=f"(d) : "h"(__half_as_ushort(a)), "h"(__half_as_ushort(b)), "f"(c));
+  return d;
+}
+
 AKV_DEV float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

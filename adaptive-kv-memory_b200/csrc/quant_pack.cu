@@ -10,12 +10,13 @@
 // to 0), so a zero-range group keeps scale 0 and its 0/0 codes become 0.
 //
 // One CTA quantises one scale group (all heads of one batch row, up to three
-// CTAs per SM): cp.async stages the group's fp16 rows in shared memory, one
-// pass over the columns yields the outlier norms and the key min/max, a pass
-// over the rows yields the value min/max, and the encode pass turns 8
+// CTAs per SM): 1-D bulk TMA stages the group's fp16 rows in shared memory
+// (one copy per head when the rows are contiguous, one per row for a gather),
+// one pass over the columns yields the outlier norms and the key min/max, a
+// pass over the rows yields the value min/max, and the encode pass turns 8
 // channels of one token into BITS packed bytes per work item.  The division
 // is exact without a divide: with r = RN(1/s) precomputed per scale,
-//   q0 = x*r,  e = fma(-s, q0, x),  q = fma(e, r, q0)
+//   q0 = x*r,  e = fma(-s, q0, x),  q = fma(e, r, q0)   (packed fp32x2 ops)
 // equals RN(x/s) for every pair of non-negative finite fp16 x and s (checked
 // exhaustively against double division, all 2^30 pairs).  fp16(q) + 1024 in
 // fp16 is 1024 + rint(fp16(q)) with ties to even, so one packed fp16 add
@@ -62,19 +63,44 @@ AKV_DEV float div_exact(float x, float s, float r) {
   return __fmaf_rn(e, r, q0);
 }
 
-// scale = fp16(fp16(hi - lo) / maxval) from fp16 min/max.
-AKV_DEV __half affine_scale(__half lo, __half hi, float maxval) {
-  const float range = __half2float(__float2half_rn(__fsub_rn(__half2float(hi), __half2float(lo))));
-  return __float2half_rn(__fdiv_rn(range, maxval));
+// Two lanes of div_exact: x2, r2 = (r0, r1), ns2 = (-s0, -s1).
+AKV_DEV uint64_t div_exact2(uint64_t x2, uint64_t ns2, uint64_t r2) {
+  const uint64_t q0 = f2_mul(x2, r2);
+  return f2_fma(f2_fma(ns2, q0, x2), r2, q0);
+}
+
+// RN(1/s) for s an fp16 value or kZeroScale: one Newton step from the
+// hardware approximation (within 1 ulp) lands on the correctly rounded
+// reciprocal for every such s (checked exhaustively from starts up to 3 ulp off).
+AKV_DEV float rcp_exact(float s) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(s));
+  return __fmaf_rn(__fmaf_rn(-s, y, 1.0f), y, y);
+}
+
+// scale = fp16(fp16(hi - lo) / maxval) for two (lo, hi) pairs; the division
+// by the constant maxval is div_exact with r = RN(1/maxval).  A range that
+// overflowed fp16 stays inf (div_exact would turn inf into NaN).  With scale
+// inf the encoder's quotients are NaN, which its clamp maps to code 0, the
+// reference's code for x/inf = 0.
+template <int BITS>
+AKV_DEV __half2 affine_scale2(__half2 lo, __half2 hi) {
+  constexpr float kMax = static_cast<float>((1 << BITS) - 1);
+  constexpr float kInv = 1.0f / kMax;
+  const float2 range = __half22float2(__hsub2_rn(hi, lo));
+  const float q0 = range.x == INFINITY ? INFINITY : div_exact(range.x, kMax, kInv);
+  const float q1 = range.y == INFINITY ? INFINITY : div_exact(range.y, kMax, kInv);
+  return __floats2half2_rn(q0, q1);
 }
 
 // Two codes as (1024 + c0, 1024 + c1) fp16x2 ("magic" form: the low byte of
 // each half is the code).
 template <int BITS>
-AKV_DEV uint32_t encode_pair(uint32_t x2, uint32_t z2, float s0, float s1, float r0, float r1) {
+AKV_DEV uint32_t encode_pair(uint32_t x2, uint32_t z2, uint64_t ns2, uint64_t r2) {
   constexpr uint32_t top = kMagic2 + ((1u << BITS) - 1) * 0x00010001u;
   const float2 d = __half22float2(__hsub2_rn(u32_as_h2(x2), u32_as_h2(z2)));
-  __half2 h = __floats2half2_rn(div_exact(d.x, s0, r0), div_exact(d.y, s1, r1));
+  const float2 q = f2_split(div_exact2(f2_make(d.x, d.y), ns2, r2));
+  __half2 h = __floats2half2_rn(q.x, q.y);
   h = __hadd2_rn(h, u32_as_h2(kMagic2));
   h = __hmin2(__hmax2(h, u32_as_h2(kMagic2)), u32_as_h2(top));
   return h2_as_u32(h);
@@ -171,7 +197,8 @@ AKV_DEV void load_words(const char* p, uint32_t (&w)[BITS]) {
 //   xs    [rows][D]    fp16   the group's tokens (outlier channels zeroed later)
 //   cz    [ncoef]      fp16   zero = min      (keys: per (head, channel); values: per row)
 //   cs    [ncoef]      fp16   max, then scale
-//   cr    [ncoef]      fp32   RN(1 / scale_eff)       -- shares its space with
+//   cr    keys: [H][D] fp32 RN(1 / scale_eff); values: [rows] float2 (-scale_eff, RN(1 / scale_eff))
+//                             -- shares its space with
 //   norms [H][D]       fp32   per-(head, channel) L2 norms (dead before cr is written)
 //   score [D] fp32, oidx [kMaxOutliers] int, od_s [rows][n_out] fp16 originals
 struct QuantSmem {
@@ -184,8 +211,9 @@ __host__ __device__ inline QuantSmem quant_smem_layout(int H, int nt, int D, int
   const size_t ncoef = is_key ? hd : rows;
   m.cz = rows * D * 2;
   m.cs = m.cz + ncoef * 2;
-  m.cr = m.cs + ncoef * 2;  // 4-byte aligned: cz is, and 4*ncoef bytes lie between
-  m.score = m.cr + (ncoef > hd ? ncoef : hd) * 4;
+  m.cr = (m.cs + ncoef * 2 + 7) & ~static_cast<size_t>(7);
+  const size_t crb = ncoef * (is_key ? 4 : 8);
+  m.score = m.cr + (crb > hd * 4 ? crb : hd * 4);
   m.oidx = m.score + static_cast<size_t>(D) * 4;
   m.od = m.oidx + kMaxOutliers * 4;
   m.total = m.od + rows * n_out * 2;
@@ -200,11 +228,12 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int tid = threadIdx.x;
   const int b = blockIdx.y;
-  const int t0 = blockIdx.x * p.group;
+  const int t0 = blockIdx.x * p.group;  // a multiple of 32, or 0
+  const int blk0 = t0 / kBlockTokens;
   const int nt = min(p.group, p.N - t0);
+  const int nblk = (nt + kBlockTokens - 1) / kBlockTokens;
   const int H = p.H, D = p.D, D2 = D / 2;
   const int rows = H * nt;
-  const float maxval = static_cast<float>((1 << BITS) - 1);
   const QuantSmem lay = quant_smem_layout(H, nt, D, p.n_out, IS_KEY);
 
   __half* xs = reinterpret_cast<__half*>(smem_raw);
@@ -215,54 +244,97 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
   float* score = reinterpret_cast<float*>(smem_raw + lay.score);
   int* oidx = reinterpret_cast<int*>(smem_raw + lay.oidx);
   __half* od_s = reinterpret_cast<__half*>(smem_raw + lay.od);
-  const __half2* xs2 = reinterpret_cast<const __half2*>(xs);
 
-  // ---- stage the group's rows: 16-byte cp.async, all in flight at once
-  {
-    const int vpr = D / 8;
-    for (int v = tid; v < rows * vpr; v += kQuantThreads) {
-      const int c = v % vpr;
-      const int r = v / vpr;
-      const int t = r % nt;
-      const int h = r / nt;
-      const int64_t row = p.tok_idx ? p.tok_idx[b * p.tok_sb + t0 + t] : static_cast<int64_t>(t0 + t);
-      cp_async16(xs + r * D + c * 8, p.src + b * p.sb + h * p.sh + row * p.sn + c * 8);
+  // ---- stage the group's rows with 1-D bulk TMA (warp 0 issues, all wait)
+  __shared__ __align__(8) uint64_t stage_bar;
+  if (tid == 0) {
+    mbar_init(&stage_bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (tid < 32) {
+    if (tid == 0) mbar_arrive_expect_tx(&stage_bar, static_cast<uint32_t>(rows) * D * 2);
+    __syncwarp();
+    if (!p.tok_idx && p.sn == D) {  // each head's nt rows are one contiguous run
+      for (int h = tid; h < H; h += 32)
+        tma_load_1d(xs + h * nt * D, p.src + b * p.sb + h * p.sh + static_cast<int64_t>(t0) * D,
+                    static_cast<uint32_t>(nt) * D * 2, &stage_bar);
+    } else {
+      for (int r = tid; r < rows; r += 32) {
+        const int t = r % nt, h = r / nt;
+        const int64_t row = p.tok_idx ? p.tok_idx[b * p.tok_sb + t0 + t] : static_cast<int64_t>(t0 + t);
+        tma_load_1d(xs + r * D, p.src + b * p.sb + h * p.sh + row * p.sn, D * 2, &stage_bar);
+      }
     }
-    cp_async_wait_all();
-    __syncthreads();
+  }
+  {
+    const bool ok = mbar_wait(&stage_bar, 0, p.status);
+    if (__syncthreads_or(!ok)) {  // timed out: let the copies land (bounded), then give up
+      if (!ok) mbar_wait(&stage_bar, 0, p.status);
+      return;
+    }
   }
 
-  // ---- one pass over the columns: outlier norms (affine_quantizer.py:75-85 /
-  //      :143-151) and, for keys, the per-(head, channel) min/max
+  // ---- column statistics: outlier norms (affine_quantizer.py:75-85 / :143-151)
+  //      and, for keys, the per-(head, channel) min/max.  A work item is 8
+  //      channels of one head; two neighbouring lanes split its tokens.
+  const int ncs = D / kEncChunk;
   if (p.n_out > 0 || IS_KEY) {
-    for (int w = tid; w < H * D2; w += kQuantThreads) {
-      const int h = w / D2, dp = w % D2;
-      const __half2* col = xs2 + h * nt * D2 + dp;
-      __half2 mn = __float2half2_rn(INFINITY), mx = __float2half2_rn(-INFINITY);
-      if (p.n_out > 0) {
-        float s0 = 0.f, s1 = 0.f;
-        for (int t = 0; t < nt; ++t) {
-          const __half2 x = col[t * D2];
-          const float2 f = __half22float2(x);
-          s0 = fmaf(f.x, f.x, s0);
-          s1 = fmaf(f.y, f.y, s1);
+    const int items = H * ncs * 2;
+    for (int w0 = 0; w0 < items; w0 += kQuantThreads) {
+      const int w = w0 + tid;
+      const bool act = w < items;
+      const unsigned mask = __ballot_sync(0xffffffffu, act);
+      if (!act) continue;
+      const int half = w & 1, col = w >> 1;
+      const int h = col / ncs, c8 = col % ncs;
+      const __half* base = xs + h * nt * D + c8 * kEncChunk;
+      float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      __half2 mn[4], mx[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        mn[i] = __float2half2_rn(INFINITY);
+        mx[i] = __float2half2_rn(-INFINITY);
+      }
+      for (int t = half; t < nt; t += 2) {
+        const uint4 v = lds_v4(base + t * D);
+        const uint32_t x4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const __half2 x = u32_as_h2(x4[i]);
+          if (p.n_out > 0) {
+            s[2 * i] = fma_f16_f32(__low2half(x), __low2half(x), s[2 * i]);
+            s[2 * i + 1] = fma_f16_f32(__high2half(x), __high2half(x), s[2 * i + 1]);
+          }
           if constexpr (IS_KEY) {
-            mn = __hmin2(mn, x);
-            mx = __hmax2(mx, x);
+            mn[i] = __hmin2(mn[i], x);
+            mx[i] = __hmax2(mx[i], x);
           }
         }
-        norms[h * D + 2 * dp] = sqrtf(s0);
-        norms[h * D + 2 * dp + 1] = sqrtf(s1);
-      } else {
-        for (int t = 0; t < nt; ++t) {
-          const __half2 x = col[t * D2];
-          mn = __hmin2(mn, x);
-          mx = __hmax2(mx, x);
-        }
+      }
+      if (p.n_out > 0) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) s[i] += __shfl_xor_sync(mask, s[i], 1);
       }
       if constexpr (IS_KEY) {
-        reinterpret_cast<__half2*>(cz)[w] = mn;
-        reinterpret_cast<__half2*>(cs)[w] = mx;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          mn[i] = __hmin2(mn[i], u32_as_h2(__shfl_xor_sync(mask, h2_as_u32(mn[i]), 1)));
+          mx[i] = __hmax2(mx[i], u32_as_h2(__shfl_xor_sync(mask, h2_as_u32(mx[i]), 1)));
+        }
+      }
+      if (half == 0) {
+        const int c0 = h * D + c8 * kEncChunk;
+        if (p.n_out > 0) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) norms[c0 + i] = sqrtf(s[i]);
+        }
+        if constexpr (IS_KEY) {
+          *reinterpret_cast<uint4*>(cz + c0) =
+              make_uint4(h2_as_u32(mn[0]), h2_as_u32(mn[1]), h2_as_u32(mn[2]), h2_as_u32(mn[3]));
+          *reinterpret_cast<uint4*>(cs + c0) =
+              make_uint4(h2_as_u32(mx[0]), h2_as_u32(mx[1]), h2_as_u32(mx[2]), h2_as_u32(mx[3]));
+        }
       }
     }
     __syncthreads();
@@ -298,88 +370,77 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
       }
     }
     __syncthreads();
-    // side store: fp16 originals of the outlier channels, then their ids
+    // side store: fp16 originals of the outlier channels (then zeroed in the
+    // staged rows, affine_quantizer.py:84-85) and their ids
     const akv_view& od = p.dst.out_data;
-    for (int w = tid; w < rows * p.n_out; w += kQuantThreads) {
-      const int j = w % p.n_out;
-      const int r = w / p.n_out;
-      const int tt = t0 + r % nt;
-      const __half o = xs[r * D + oidx[j]];
-      od_s[w] = o;  // w == r*n_out + j
-      if (od.ptr) reinterpret_cast<__half*>(vaddr(od, b, r / nt, tt / kBlockTokens, tt % kBlockTokens))[j] = o;
+    for (int r = tid; r < rows; r += kQuantThreads) {
+      const int h = r / nt, t = r - (r / nt) * nt;
+      __half* orow = od.ptr ? reinterpret_cast<__half*>(vaddr(od, b, h, blk0 + (t >> 5), t & 31)) : nullptr;
+      for (int j = 0; j < p.n_out; ++j) {
+        __half* x = xs + r * D + oidx[j];
+        od_s[r * p.n_out + j] = *x;
+        if (orow) orow[j] = *x;
+        *x = __float2half_rn(0.0f);
+      }
     }
     const akv_view& oi = p.dst.out_idx;
     if (oi.ptr) {
-      const int blk0 = t0 / kBlockTokens, nblk = (t0 + nt - 1) / kBlockTokens - blk0 + 1;
-      for (int w = tid; w < H * nblk * p.n_out; w += kQuantThreads) {
-        const int j = w % p.n_out;
-        const int bl = (w / p.n_out) % nblk;
-        const int h = w / (p.n_out * nblk);
-        reinterpret_cast<int16_t*>(vaddr(oi, b, h, blk0 + bl, 0))[j] = static_cast<int16_t>(oidx[j]);
+      for (int w = tid; w < H * nblk; w += kQuantThreads) {
+        int16_t* ids = reinterpret_cast<int16_t*>(vaddr(oi, b, w / nblk, blk0 + w % nblk, 0));
+        for (int j = 0; j < p.n_out; ++j) ids[j] = static_cast<int16_t>(oidx[j]);
       }
     }
-    __syncthreads();
-    // zero the outlier channels before min/max (affine_quantizer.py:84-85); a
-    // zeroed key column has min = max = 0
-    for (int w = tid; w < rows * p.n_out; w += kQuantThreads)
-      xs[(w / p.n_out) * D + oidx[w % p.n_out]] = __float2half_rn(0.0f);
-    if constexpr (IS_KEY) {
-      for (int w = tid; w < H * p.n_out; w += kQuantThreads) {
-        const int c = (w / p.n_out) * D + oidx[w % p.n_out];
-        cz[c] = cs[c] = __float2half_rn(0.0f);
-      }
+    if constexpr (IS_KEY) {  // a zeroed key column has min = max = 0
+      for (int h = tid; h < H; h += kQuantThreads)
+        for (int j = 0; j < p.n_out; ++j) cz[h * D + oidx[j]] = cs[h * D + oidx[j]] = __float2half_rn(0.0f);
     }
     __syncthreads();
   }
 
   if constexpr (IS_KEY) {
-    // ---- keys: scale per (head, channel), written once per block record
-    for (int w = tid; w < H * D; w += kQuantThreads) {
-      const __half sc = affine_scale(cz[w], cs[w], maxval);
-      cs[w] = sc;
-      cr[w] = __frcp_rn(scale_eff(sc));
-    }
-    __syncthreads();
-    const int blk0 = t0 / kBlockTokens, nblk = (t0 + nt - 1) / kBlockTokens - blk0 + 1;
-    for (int w = tid; w < H * nblk * D2; w += kQuantThreads) {
-      const int dp = w % D2;
-      const int bl = (w / D2) % nblk;
-      const int h = w / (D2 * nblk);
-      if (p.dst.scale.ptr)
-        reinterpret_cast<__half2*>(vaddr(p.dst.scale, b, h, blk0 + bl, 0))[dp] =
-            reinterpret_cast<const __half2*>(cs)[h * D2 + dp];
-      if (p.dst.zero.ptr)
-        reinterpret_cast<__half2*>(vaddr(p.dst.zero, b, h, blk0 + bl, 0))[dp] =
-            reinterpret_cast<const __half2*>(cz)[h * D2 + dp];
+    // ---- keys: scale per (head, channel pair); 1/scale for the encoder; the
+    //      scale / zero rows of every block record the group covers
+    const akv_view& sv = p.dst.scale;
+    const akv_view& zv = p.dst.zero;
+    for (int w = tid; w < H * D2; w += kQuantThreads) {
+      const int h = w / D2, dp = w - h * D2;
+      const __half2 lo = reinterpret_cast<const __half2*>(cz)[w];
+      const __half2 hi = reinterpret_cast<const __half2*>(cs)[w];
+      const __half2 sc = affine_scale2<BITS>(lo, hi);
+      reinterpret_cast<__half2*>(cs)[w] = sc;
+      reinterpret_cast<float2*>(cr)[w] =
+          make_float2(rcp_exact(scale_eff(__low2half(sc))), rcp_exact(scale_eff(__high2half(sc))));
+      for (int bl = 0; bl < nblk; ++bl) {
+        if (sv.ptr) reinterpret_cast<__half2*>(vaddr(sv, b, h, blk0 + bl, 0))[dp] = sc;
+        if (zv.ptr) reinterpret_cast<__half2*>(vaddr(zv, b, h, blk0 + bl, 0))[dp] = lo;
+      }
     }
   } else {
     // ---- values: per-token min/max over D, one thread per row; the 16-byte
     //      chunks are visited from a row-dependent start so that neighbouring
     //      rows hit different banks
-    const int nc = D / 8;
     for (int r = tid; r < rows; r += kQuantThreads) {
       const __half* xr = xs + r * D;
       __half2 mn = __float2half2_rn(INFINITY), mx = __float2half2_rn(-INFINITY);
-      int c = r % nc;
-      for (int j = 0; j < nc; ++j) {
-        const uint4 v = lds_v4(xr + 8 * c);
+      int c = r % ncs;
+      for (int j = 0; j < ncs; ++j) {
+        const uint4 v = lds_v4(xr + kEncChunk * c);
         const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           mn = __hmin2(mn, u32_as_h2(w4[i]));
           mx = __hmax2(mx, u32_as_h2(w4[i]));
         }
-        c = (c + 1 == nc) ? 0 : c + 1;
+        c = (c + 1 == ncs) ? 0 : c + 1;
       }
       const __half lo = __hmin(__low2half(mn), __high2half(mn));
       const __half hi = __hmax(__low2half(mx), __high2half(mx));
-      const __half sc = affine_scale(lo, hi, maxval);
-      const float se = scale_eff(sc), rc = __frcp_rn(se);
+      const __half sc = __low2half(affine_scale2<BITS>(__half2half2(lo), __half2half2(hi)));
+      const float se = scale_eff(sc), rc = rcp_exact(se);
       cz[r] = lo;
-      cs[r] = sc;
-      cr[r] = rc;
-      const int h = r / nt, tt = t0 + r % nt;
-      const int blk = tt / kBlockTokens, slot = tt % kBlockTokens;
+      reinterpret_cast<float2*>(cr)[r] = make_float2(-se, rc);
+      const int h = r / nt, t = r - h * nt;
+      const int blk = blk0 + (t >> 5), slot = t & 31;
       if (p.dst.scale.ptr) *reinterpret_cast<__half*>(vaddr(p.dst.scale, b, h, blk, slot)) = sc;
       if (p.dst.zero.ptr) *reinterpret_cast<__half*>(vaddr(p.dst.zero, b, h, blk, slot)) = lo;
       // outlier residual: fp16 original minus what the zeroed channel dequantises to
@@ -394,16 +455,15 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
   __syncthreads();
 
   // ---- encode + pack: a work item is 8 channels of one head; its threads walk
-  //      the tokens (keys keep the 8 channels' zero / scale / 1/scale in registers)
+  //      the tokens (keys keep the 8 channels' zero, -scale and 1/scale in registers)
   {
-    const int ncs = D / kEncChunk;
     const int cols = H * ncs;
     const int tpc = max(1, kQuantThreads / cols);
     for (int w = tid; w < cols * tpc; w += kQuantThreads) {
       const int col = w % cols, sub = w / cols;
-      const int h = col / ncs, c8 = col % ncs;
+      const int h = col / ncs, c8 = col - h * ncs;
       uint32_t z2[4];
-      float sf[8], rf[8];
+      uint64_t ns2[4], r2[4];
       if constexpr (IS_KEY) {
         const int c0 = h * D + c8 * kEncChunk;
         const uint4 zz = lds_v4(cz + c0);
@@ -412,45 +472,39 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
         const uint32_t s2[4] = {ss.x, ss.y, ss.z, ss.w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          sf[2 * i] = scale_eff(__low2half(u32_as_h2(s2[i])));
-          sf[2 * i + 1] = scale_eff(__high2half(u32_as_h2(s2[i])));
+          ns2[i] = f2_make(-scale_eff(__low2half(u32_as_h2(s2[i]))), -scale_eff(__high2half(u32_as_h2(s2[i]))));
+          const float2 rr = reinterpret_cast<const float2*>(cr)[c0 / 2 + i];
+          r2[i] = f2_make(rr.x, rr.y);
         }
-#pragma unroll
-        for (int i = 0; i < 8; ++i) rf[i] = cr[c0 + i];
       }
+      char* cbase = p.dst.codes.ptr ? vaddr(p.dst.codes, b, h, blk0, 0) + c8 * BITS : nullptr;
       for (int t = sub; t < nt; t += tpc) {
         const int r = h * nt + t;
         if constexpr (!IS_KEY) {
-          const __half zh = cz[r];
-          const float se = scale_eff(cs[r]), rc = cr[r];
+          const uint32_t zz = h2_as_u32(__half2half2(cz[r]));
+          const float2 c = reinterpret_cast<const float2*>(cr)[r];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) z2[i] = h2_as_u32(__half2half2(zh));
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            sf[i] = se;
-            rf[i] = rc;
+          for (int i = 0; i < 4; ++i) {
+            z2[i] = zz;
+            ns2[i] = f2_make(c.x, c.x);
+            r2[i] = f2_make(c.y, c.y);
           }
         }
         const uint4 xv = lds_v4(xs + r * D + c8 * kEncChunk);
         const uint32_t x2[4] = {xv.x, xv.y, xv.z, xv.w};
         uint32_t m[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-          m[i] = encode_pair<BITS>(x2[i], z2[i], sf[2 * i], sf[2 * i + 1], rf[2 * i], rf[2 * i + 1]);
-        const int tt = t0 + t;
-        if (p.dst.codes.ptr)
-          store_packed8<BITS>(vaddr(p.dst.codes, b, h, tt / kBlockTokens, tt % kBlockTokens) + c8 * BITS,
-                              pack8<BITS>(m));
+        for (int i = 0; i < 4; ++i) m[i] = encode_pair<BITS>(x2[i], z2[i], ns2[i], r2[i]);
+        if (cbase)
+          store_packed8<BITS>(cbase + (t >> 5) * p.dst.codes.sblk + (t & 31) * p.dst.codes.sslot, pack8<BITS>(m));
       }
     }
   }
 
   // ---- valid-slot masks for the blocks this group wrote
   if (p.dst.mask.ptr) {
-    const int blk0 = t0 / kBlockTokens, blk1 = (t0 + nt - 1) / kBlockTokens;
-    for (int w = tid; w < H * (blk1 - blk0 + 1); w += kQuantThreads) {
-      const int bl = blk0 + w % (blk1 - blk0 + 1);
-      const int h = w / (blk1 - blk0 + 1);
+    for (int w = tid; w < H * nblk; w += kQuantThreads) {
+      const int h = w / nblk, bl = blk0 + w % nblk;
       const int lo = max(t0, bl * kBlockTokens) - bl * kBlockTokens;
       const int hi = min(t0 + nt, (bl + 1) * kBlockTokens) - bl * kBlockTokens;  // exclusive
       const uint32_t m = (hi - lo == 32) ? 0xffffffffu : (((1u << (hi - lo)) - 1u) << lo);
