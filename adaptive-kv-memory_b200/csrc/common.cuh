@@ -111,6 +111,13 @@ AKV_DEV uint4 ldg_nc_v4(const void* p) {
 }
 
 AKV_DEV uint4 lds_v4(const void* p) { return *reinterpret_cast<const uint4*>(p); }
+AKV_DEV void lds_u32x4(const void* p, uint32_t (&w)[4]) {
+  const uint4 v = *reinterpret_cast<const uint4*>(p);
+  w[0] = v.x;
+  w[1] = v.y;
+  w[2] = v.z;
+  w[3] = v.w;
+}
 AKV_DEV uint2 lds_v2(const void* p) { return *reinterpret_cast<const uint2*>(p); }
 AKV_DEV uint32_t lds_u32(const void* p) { return *reinterpret_cast<const uint32_t*>(p); }
 

@@ -114,6 +114,45 @@ AKV_DEV uint32_t encode_one(__half x, __half z, float s, float r) {
   return __half_as_ushort(h) & 0xFFu;
 }
 
+// fp16 path.  For a scale s with 0 < s < 16384 and s * 2^15 >= 1/8, let
+// m = 2^k scale s into s' = s*m in [1/8, 16384), ns = -s', r = RN16(1/s').
+// Then  d = fp16(x - z) * m (exact),  q0 = fp16(d*r),  e = fma16(ns, q0, d),
+// q = fma16(e, r, q0)  rounds (via + 1024) to the reference code for every fp16
+// d and maxval 3, 7, 15 (checked exhaustively over all such s; the quotient q
+// itself can be 1 ulp off, never across a rounding boundary of the code).  q
+// is never negative or NaN there, so one min clamps.  Scale 0 also takes the
+// fp16 path: it means max - min <= 7 * 2^-24, so every d is 0 or a few
+// subnormal steps, and m = 2^15, ns = 0, r = 65504 send d > 0 past maxval and
+// d = 0 to 0 (the reference's x/0 = inf and 0/0 = NaN -> 0).  Other scales
+// (inf, >= 16384, < 2^-18) take the fp32 path.
+AKV_DEV bool fast_coef(__half s, __half& m, __half& ns, __half& r) {
+  const float f = __half2float(s);
+  if (f == 0.f) {
+    m = __ushort_as_half(0x7800);   // 2^15
+    ns = __ushort_as_half(0);
+    r = __ushort_as_half(0x7BFF);   // 65504
+    return true;
+  }
+  if (!(f > 0.f && f < 16384.f)) return false;
+  const int e = static_cast<int>((__float_as_uint(f) >> 23) & 0xFF) - 127;  // floor(log2 s)
+  const int k = max(0, -3 - e);
+  if (k > 15) return false;
+  const float sp = f * __uint_as_float(static_cast<uint32_t>(k + 127) << 23);  // exact
+  m = __ushort_as_half(static_cast<unsigned short>((k + 15) << 10));
+  ns = __float2half_rn(-sp);
+  r = __float2half_rn(rcp_exact(sp));  // RN16(RN32(1/s')) == RN16(1/s')
+  return true;
+}
+
+template <int BITS>
+AKV_DEV uint32_t encode_pair16(uint32_t x2, uint32_t z2, uint32_t m2, uint32_t ns2, uint32_t r2) {
+  constexpr uint32_t top = kMagic2 + ((1u << BITS) - 1) * 0x00010001u;
+  const __half2 d = __hmul2_rn(__hsub2_rn(u32_as_h2(x2), u32_as_h2(z2)), u32_as_h2(m2));
+  const __half2 q0 = __hmul2_rn(d, u32_as_h2(r2));
+  const __half2 q = __hfma2(__hfma2(u32_as_h2(ns2), q0, d), u32_as_h2(r2), q0);
+  return h2_as_u32(__hmin2(__hadd2_rn(q, u32_as_h2(kMagic2)), u32_as_h2(top)));
+}
+
 // 8 codes in magic form (m[i] = channels 2i, 2i+1) -> packed bytes (akv/bitpack.py):
 //   4 bits: 4 bytes, even channel in the high nibble;
 //   2 bits: 2 bytes (low half), first channel in the two high bits;
@@ -194,27 +233,28 @@ AKV_DEV void load_words(const char* p, uint32_t (&w)[BITS]) {
 }
 
 // Shared memory of one quantiser CTA (byte offsets; rows = H * nt):
-//   xs    [rows][D]    fp16   the group's tokens (outlier channels zeroed later)
-//   cz    [ncoef]      fp16   zero = min      (keys: per (head, channel); values: per row)
-//   cs    [ncoef]      fp16   max, then scale
-//   cr    keys: [H][D] fp32 RN(1 / scale_eff); values: [rows] float2 (-scale_eff, RN(1 / scale_eff))
-//                             -- shares its space with
-//   norms [H][D]       fp32   per-(head, channel) L2 norms (dead before cr is written)
-//   score [D] fp32, oidx [kMaxOutliers] int, od_s [rows][n_out] fp16 originals
+//   xs    [rows][D]   fp16  the group's tokens (outlier channels zeroed later)
+//   cz    [H][D]      fp16  keys: column min (= zero)
+//   cs    [H][D]      fp16  keys: column max, then scale
+//   co    keys:   km, kns, kr [H][D/2] fp16x2: fp16-path m, -s', 1/s' per channel pair
+//         values: [rows] 16-byte records {z | m, -s' | 1/s' (fp16), -s_eff, 1/s_eff (fp32)}
+//         -- shares its space with norms [H][D] fp32 and score [D] fp32, dead by then
+//   oidx  [kMaxOutliers] int,  od_s [rows][n_out] fp16 outlier originals
 struct QuantSmem {
-  size_t cz, cs, cr, score, oidx, od, total;
+  size_t cz, cs, co, score, oidx, od, total;
 };
 
 __host__ __device__ inline QuantSmem quant_smem_layout(int H, int nt, int D, int n_out, bool is_key) {
   QuantSmem m{};
   const size_t rows = static_cast<size_t>(H) * nt, hd = static_cast<size_t>(H) * D;
-  const size_t ncoef = is_key ? hd : rows;
+  const size_t kz = is_key ? hd : 0;
   m.cz = rows * D * 2;
-  m.cs = m.cz + ncoef * 2;
-  m.cr = (m.cs + ncoef * 2 + 7) & ~static_cast<size_t>(7);
-  const size_t crb = ncoef * (is_key ? 4 : 8);
-  m.score = m.cr + (crb > hd * 4 ? crb : hd * 4);
-  m.oidx = m.score + static_cast<size_t>(D) * 4;
+  m.cs = m.cz + kz * 2;
+  m.co = (m.cs + kz * 2 + 15) & ~static_cast<size_t>(15);
+  const size_t cob = is_key ? hd * 6 : rows * 16;
+  const size_t nsb = hd * 4 + static_cast<size_t>(D) * 4;
+  m.score = m.co + hd * 4;
+  m.oidx = m.co + (cob > nsb ? cob : nsb);
   m.od = m.oidx + kMaxOutliers * 4;
   m.total = m.od + rows * n_out * 2;
   return m;
@@ -239,9 +279,12 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
   __half* xs = reinterpret_cast<__half*>(smem_raw);
   __half* cz = reinterpret_cast<__half*>(smem_raw + lay.cz);
   __half* cs = reinterpret_cast<__half*>(smem_raw + lay.cs);
-  float* cr = reinterpret_cast<float*>(smem_raw + lay.cr);
-  float* norms = cr;
+  float* norms = reinterpret_cast<float*>(smem_raw + lay.co);
   float* score = reinterpret_cast<float*>(smem_raw + lay.score);
+  uint32_t* km = reinterpret_cast<uint32_t*>(smem_raw + lay.co);  // keys
+  uint32_t* kns = km + H * D2;
+  uint32_t* kr = kns + H * D2;
+  uint4* vco = reinterpret_cast<uint4*>(smem_raw + lay.co);       // values
   int* oidx = reinterpret_cast<int*>(smem_raw + lay.oidx);
   __half* od_s = reinterpret_cast<__half*>(smem_raw + lay.od);
 
@@ -289,10 +332,11 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
       const int half = w & 1, col = w >> 1;
       const int h = col / ncs, c8 = col % ncs;
       const __half* base = xs + h * nt * D + c8 * kEncChunk;
-      float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      uint64_t s2[4];
       __half2 mn[4], mx[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
+        s2[i] = f2_make(0.f, 0.f);
         mn[i] = __float2half2_rn(INFINITY);
         mx[i] = __float2half2_rn(-INFINITY);
       }
@@ -303,8 +347,9 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
         for (int i = 0; i < 4; ++i) {
           const __half2 x = u32_as_h2(x4[i]);
           if (p.n_out > 0) {
-            s[2 * i] = fma_f16_f32(__low2half(x), __low2half(x), s[2 * i]);
-            s[2 * i + 1] = fma_f16_f32(__high2half(x), __high2half(x), s[2 * i + 1]);
+            const float2 f = __half22float2(x);
+            const uint64_t f2 = f2_make(f.x, f.y);
+            s2[i] = f2_fma(f2, f2, s2[i]);
           }
           if constexpr (IS_KEY) {
             mn[i] = __hmin2(mn[i], x);
@@ -312,9 +357,14 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
           }
         }
       }
+      float s[8];
       if (p.n_out > 0) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) s[i] += __shfl_xor_sync(mask, s[i], 1);
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = f2_split(s2[i]);
+          s[2 * i] = f.x + __shfl_xor_sync(mask, f.x, 1);
+          s[2 * i + 1] = f.y + __shfl_xor_sync(mask, f.y, 1);
+        }
       }
       if constexpr (IS_KEY) {
 #pragma unroll
@@ -397,6 +447,7 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
     __syncthreads();
   }
 
+  bool all_fast = true;  // every scale of the group takes the fp16 path
   if constexpr (IS_KEY) {
     // ---- keys: scale per (head, channel pair); 1/scale for the encoder; the
     //      scale / zero rows of every block record the group covers
@@ -408,8 +459,18 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
       const __half2 hi = reinterpret_cast<const __half2*>(cs)[w];
       const __half2 sc = affine_scale2<BITS>(lo, hi);
       reinterpret_cast<__half2*>(cs)[w] = sc;
-      reinterpret_cast<float2*>(cr)[w] =
-          make_float2(rcp_exact(scale_eff(__low2half(sc))), rcp_exact(scale_eff(__high2half(sc))));
+      __half m0, n0, r0, m1, n1, r1;
+      if (!fast_coef(__low2half(sc), m0, n0, r0)) {
+        m0 = n0 = r0 = __ushort_as_half(0);
+        all_fast = false;
+      }
+      if (!fast_coef(__high2half(sc), m1, n1, r1)) {
+        m1 = n1 = r1 = __ushort_as_half(0);
+        all_fast = false;
+      }
+      km[w] = h2_as_u32(__halves2half2(m0, m1));
+      kns[w] = h2_as_u32(__halves2half2(n0, n1));
+      kr[w] = h2_as_u32(__halves2half2(r0, r1));
       for (int bl = 0; bl < nblk; ++bl) {
         if (sv.ptr) reinterpret_cast<__half2*>(vaddr(sv, b, h, blk0 + bl, 0))[dp] = sc;
         if (zv.ptr) reinterpret_cast<__half2*>(vaddr(zv, b, h, blk0 + bl, 0))[dp] = lo;
@@ -437,8 +498,14 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
       const __half hi = __hmax(__low2half(mx), __high2half(mx));
       const __half sc = __low2half(affine_scale2<BITS>(__half2half2(lo), __half2half2(hi)));
       const float se = scale_eff(sc), rc = rcp_exact(se);
-      cz[r] = lo;
-      reinterpret_cast<float2*>(cr)[r] = make_float2(-se, rc);
+      __half fm, fns, fr;
+      if (!fast_coef(sc, fm, fns, fr)) {
+        fm = fns = fr = __ushort_as_half(0);
+        all_fast = false;
+      }
+      vco[r] = make_uint4(__half_as_ushort(lo) | (static_cast<uint32_t>(__half_as_ushort(fm)) << 16),
+                          __half_as_ushort(fns) | (static_cast<uint32_t>(__half_as_ushort(fr)) << 16),
+                          __float_as_uint(-se), __float_as_uint(rc));
       const int h = r / nt, t = r - h * nt;
       const int blk = blk0 + (t >> 5), slot = t & 31;
       if (p.dst.scale.ptr) *reinterpret_cast<__half*>(vaddr(p.dst.scale, b, h, blk, slot)) = sc;
@@ -452,51 +519,91 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
       }
     }
   }
-  __syncthreads();
+  all_fast = __syncthreads_and(all_fast);
 
   // ---- encode + pack: a work item is 8 channels of one head; its threads walk
-  //      the tokens (keys keep the 8 channels' zero, -scale and 1/scale in registers)
+  //      the tokens.  Keys keep the 8 channels' coefficients in registers and
+  //      take the fp16 path unless one of the 8 scales needs the fp32 path;
+  //      values read one 16-byte coefficient record per token.
   {
     const int cols = H * ncs;
     const int tpc = max(1, kQuantThreads / cols);
+    const akv_view& cv = p.dst.codes;
     for (int w = tid; w < cols * tpc; w += kQuantThreads) {
       const int col = w % cols, sub = w / cols;
       const int h = col / ncs, c8 = col - h * ncs;
-      uint32_t z2[4];
-      uint64_t ns2[4], r2[4];
+      char* cbase = cv.ptr ? vaddr(cv, b, h, blk0, 0) + c8 * BITS : nullptr;
+      const __half* xcol = xs + h * nt * D + c8 * kEncChunk;
+      uint32_t m[4];
       if constexpr (IS_KEY) {
-        const int c0 = h * D + c8 * kEncChunk;
-        const uint4 zz = lds_v4(cz + c0);
-        const uint4 ss = lds_v4(cs + c0);
-        z2[0] = zz.x; z2[1] = zz.y; z2[2] = zz.z; z2[3] = zz.w;
-        const uint32_t s2[4] = {ss.x, ss.y, ss.z, ss.w};
+        const int c0 = h * D + c8 * kEncChunk, p0 = c0 / 2;
+        uint32_t z2[4], m2[4], ns2[4], r2[4];
+        lds_u32x4(cz + c0, z2);
+        lds_u32x4(km + p0, m2);
+        lds_u32x4(kns + p0, ns2);
+        lds_u32x4(kr + p0, r2);
+        bool fast = all_fast;
+        if (!fast) {
+          fast = true;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          ns2[i] = f2_make(-scale_eff(__low2half(u32_as_h2(s2[i]))), -scale_eff(__high2half(u32_as_h2(s2[i]))));
-          const float2 rr = reinterpret_cast<const float2*>(cr)[c0 / 2 + i];
-          r2[i] = f2_make(rr.x, rr.y);
+          for (int i = 0; i < 4; ++i) fast = fast && (m2[i] & 0x7FFFu) && (m2[i] & 0x7FFF0000u);
         }
-      }
-      char* cbase = p.dst.codes.ptr ? vaddr(p.dst.codes, b, h, blk0, 0) + c8 * BITS : nullptr;
-      for (int t = sub; t < nt; t += tpc) {
-        const int r = h * nt + t;
-        if constexpr (!IS_KEY) {
-          const uint32_t zz = h2_as_u32(__half2half2(cz[r]));
-          const float2 c = reinterpret_cast<const float2*>(cr)[r];
+        if (fast) {
+          for (int t = sub; t < nt; t += tpc) {
+            uint32_t x2[4];
+            lds_u32x4(xcol + t * D, x2);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) m[i] = encode_pair16<BITS>(x2[i], z2[i], m2[i], ns2[i], r2[i]);
+            if (cbase) store_packed8<BITS>(cbase + (t >> 5) * cv.sblk + (t & 31) * cv.sslot, pack8<BITS>(m));
+          }
+        } else {
+          uint32_t s2[4];
+          uint64_t nsf[4], rf[4];
+          lds_u32x4(cs + c0, s2);
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            z2[i] = zz;
-            ns2[i] = f2_make(c.x, c.x);
-            r2[i] = f2_make(c.y, c.y);
+            const float s0 = scale_eff(__low2half(u32_as_h2(s2[i]))), s1 = scale_eff(__high2half(u32_as_h2(s2[i])));
+            nsf[i] = f2_make(-s0, -s1);
+            rf[i] = f2_make(rcp_exact(s0), rcp_exact(s1));
+          }
+          for (int t = sub; t < nt; t += tpc) {
+            uint32_t x2[4];
+            lds_u32x4(xcol + t * D, x2);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) m[i] = encode_pair<BITS>(x2[i], z2[i], nsf[i], rf[i]);
+            if (cbase) store_packed8<BITS>(cbase + (t >> 5) * cv.sblk + (t & 31) * cv.sslot, pack8<BITS>(m));
           }
         }
-        const uint4 xv = lds_v4(xs + r * D + c8 * kEncChunk);
-        const uint32_t x2[4] = {xv.x, xv.y, xv.z, xv.w};
-        uint32_t m[4];
+      } else if (all_fast) {
+        for (int t = sub; t < nt; t += tpc) {
+          const uint2 rec = *reinterpret_cast<const uint2*>(vco + h * nt + t);
+          uint32_t x2[4];
+          lds_u32x4(xcol + t * D, x2);
+          const uint32_t z2 = prmt(rec.x, rec.x, 0x1010), m2 = prmt(rec.x, rec.x, 0x3232);
+          const uint32_t ns2 = prmt(rec.y, rec.y, 0x1010), r2 = prmt(rec.y, rec.y, 0x3232);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) m[i] = encode_pair<BITS>(x2[i], z2[i], ns2[i], r2[i]);
-        if (cbase)
-          store_packed8<BITS>(cbase + (t >> 5) * p.dst.codes.sblk + (t & 31) * p.dst.codes.sslot, pack8<BITS>(m));
+          for (int i = 0; i < 4; ++i) m[i] = encode_pair16<BITS>(x2[i], z2, m2, ns2, r2);
+          if (cbase) store_packed8<BITS>(cbase + (t >> 5) * cv.sblk + (t & 31) * cv.sslot, pack8<BITS>(m));
+        }
+      } else {
+        for (int t = sub; t < nt; t += tpc) {
+          const uint4 rec = vco[h * nt + t];
+          uint32_t x2[4];
+          lds_u32x4(xcol + t * D, x2);
+          const uint32_t z2 = prmt(rec.x, rec.x, 0x1010);
+          if (rec.x >> 16) {  // fp16 path
+            const uint32_t m2 = prmt(rec.x, rec.x, 0x3232);
+            const uint32_t ns2 = prmt(rec.y, rec.y, 0x1010), r2 = prmt(rec.y, rec.y, 0x3232);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) m[i] = encode_pair16<BITS>(x2[i], z2, m2, ns2, r2);
+          } else {
+            const uint64_t nsf = f2_make(__uint_as_float(rec.z), __uint_as_float(rec.z));
+            const uint64_t rf = f2_make(__uint_as_float(rec.w), __uint_as_float(rec.w));
+#pragma unroll
+            for (int i = 0; i < 4; ++i) m[i] = encode_pair<BITS>(x2[i], z2, nsf, rf);
+          }
+          if (cbase) store_packed8<BITS>(cbase + (t >> 5) * cv.sblk + (t & 31) * cv.sslot, pack8<BITS>(m));
+        }
       }
     }
   }
