@@ -49,6 +49,10 @@ SIGNATURES = {
     "akv_quantize": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64,
                              c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                              POINTER(QDest), c_void_p, c_void_p]),
+    "akv_quantize_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int, c_int, c_int]),
+    "akv_quantize_ws": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64,
+                                c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
+                                POINTER(QDest), c_void_p, c_size_t, c_void_p, c_void_p]),
     "akv_dequantize": (c_int, [POINTER(QDest), c_void_p, c_int64, c_int, c_int, c_int, c_int, c_int, c_int,
                                c_int, c_void_p, c_int64, c_int64, c_int64, c_void_p]),
     "akv_decode_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int, c_int]),
@@ -131,3 +135,16 @@ def warm_layout(head_dim: int, key_bits: int, value_bits: int, n_outlier: int) -
     check(load().akv_warm_layout_init(head_dim, key_bits, value_bits, n_outlier, ctypes.byref(L)),
           "akv_warm_layout_init")
     return L
+
+
+def quantize(x_ptr: int, sb: int, sh: int, sn: int, tok_ptr, tok_sb: int, B: int, H: int, N: int, D: int,
+             bits: int, is_key: bool, group: int, n_out: int, dest: QDest, status_ptr, device) -> None:
+    """akv_quantize_ws with a workspace from torch's allocator when the shape needs one."""
+    import torch
+    lib = load()
+    need = lib.akv_quantize_workspace_bytes(B, H, N, D, group, n_out, int(is_key))
+    ws = torch.empty(need + 256, dtype=torch.uint8, device=device) if need else None
+    wp = None if ws is None else (ws.data_ptr() + 255) // 256 * 256
+    rc = lib.akv_quantize_ws(x_ptr, sb, sh, sn, tok_ptr, tok_sb, B, H, N, D, bits, int(is_key), group, n_out,
+                             ctypes.byref(dest), wp, need, status_ptr, torch.cuda.current_stream(device).cuda_stream)
+    check(rc, "akv_quantize")

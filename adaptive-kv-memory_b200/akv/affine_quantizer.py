@@ -89,9 +89,7 @@ class AffineQuantizer:
         out_data = torch.empty(H, N, n, dtype=torch.float16, device=dev) if n else None
         out_idx = torch.empty(n, dtype=torch.int16, device=dev) if n else None
         dest = dict_dest(codes, scale, zero, out_data, out_idx, N, D, bits, n, is_key)
-        rc = _C.load().akv_quantize(x.data_ptr(), 0, N * D, D, None, 0, 1, H, N, D, bits, int(is_key), N, n,
-                                    ctypes.byref(dest), None, _C.stream_of(x))
-        _C.check(rc, "akv_quantize")
+        _C.quantize(x.data_ptr(), 0, N * D, D, None, 0, 1, H, N, D, bits, is_key, N, n, dest, None, dev)
         res = {"scale": scale, "zero": zero, "orig_dim": D, "bits": bits}
         if n:
             res["outlier_idx"] = out_idx.to(torch.int64)

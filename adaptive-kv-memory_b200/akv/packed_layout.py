@@ -106,8 +106,6 @@ class WarmArena:
         if self.n_blocks + nblk > self.max_blocks:
             raise RuntimeError(f"warm arena full ({self.n_blocks}+{nblk} > {self.max_blocks} blocks)")
         blk0 = self.n_blocks
-        lib = _C.load()
-        st = _C.stream_of(k)
         ti = None if tok_idx is None else tok_idx.contiguous()
         tsb = 0 if ti is None or ti.dim() == 1 else ti.stride(0)
         sp = None if status is None else status.data_ptr()
@@ -115,11 +113,9 @@ class WarmArena:
             if x.stride(-1) != 1:
                 x = x.contiguous()
             dest = self.dest(is_key, blk0)
-            rc = lib.akv_quantize(x.data_ptr(), x.stride(0), x.stride(1), x.stride(2),
-                                  None if ti is None else ti.data_ptr(), tsb,
-                                  B, H, N, D, bits, int(is_key), min(group, N), self.n_out,
-                                  ctypes.byref(dest), sp, st)
-            _C.check(rc, "akv_quantize")
+            _C.quantize(x.data_ptr(), x.stride(0), x.stride(1), x.stride(2),
+                        None if ti is None else ti.data_ptr(), tsb,
+                        B, H, N, D, bits, is_key, min(group, N), self.n_out, dest, sp, x.device)
         self.n_blocks += nblk
         return blk0
 

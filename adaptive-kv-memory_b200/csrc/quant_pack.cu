@@ -37,7 +37,19 @@ struct QuantParams {
   int B, H, N, D, bits, is_key, group, n_out;
   akv_qdest dst;
   int* status;
+  // chunked path (groups too large for one CTA): per-chunk partials and the
+  // per-group results of the reduction, see QuantWs
+  int n_chunks, n_groups, heads_per_cta;
+  __half* ws_min;    // [B][n_chunks][H][D]
+  __half* ws_max;    // [B][n_chunks][H][D]
+  float* ws_sq;      // [B][n_chunks][H][D]   sum of squares
+  __half* ws_zero;   // [B][n_groups][H][D]   keys: zero (min), outlier channels 0
+  __half* ws_scale;  // [B][n_groups][H][D]   keys: scale
+  int* ws_oidx;      // [B][n_groups][kMaxOutliersWs]
 };
+
+constexpr int kMaxOutliersWs = 32;
+enum QuantMode { kQuantFull = 0, kQuantStats = 1, kQuantEncode = 2 };
 
 constexpr int kQuantThreads = 256;
 constexpr int kQuantCtasPerSm = 3;
@@ -261,18 +273,27 @@ __host__ __device__ inline QuantSmem quant_smem_layout(int H, int nt, int D, int
 }
 
 // ---------------------------------------------------------------------------
-// quantise: grid (n_groups, B), block kQuantThreads
+// quantise.  MODE kQuantFull: grid (n_groups, B), one CTA per scale group
+// (all heads).  Groups too large for one CTA take the chunked path: MODE
+// kQuantStats (grid (n_chunks, B, head groups)) writes per-32-token-chunk
+// column partials, quant_reduce_kernel turns them into the group's outlier
+// channels and key scales, and MODE kQuantEncode (same grid) encodes each
+// chunk with them.
 // ---------------------------------------------------------------------------
-template <int BITS, bool IS_KEY>
+template <int BITS, bool IS_KEY, int MODE>
 __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group_kernel(const QuantParams p) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int tid = threadIdx.x;
   const int b = blockIdx.y;
-  const int t0 = blockIdx.x * p.group;  // a multiple of 32, or 0
+  const int t0 = MODE == kQuantFull ? blockIdx.x * p.group : blockIdx.x * kBlockTokens;  // multiple of 32, or 0
+  const int chunk = blockIdx.x;
+  const int grp = t0 / p.group;
+  const int h0 = MODE == kQuantFull ? 0 : blockIdx.z * p.heads_per_cta;  // first head of this CTA
   const int blk0 = t0 / kBlockTokens;
-  const int nt = min(p.group, p.N - t0);
+  const int nt = MODE == kQuantFull ? min(p.group, p.N - t0) : min(kBlockTokens, p.N - t0);
   const int nblk = (nt + kBlockTokens - 1) / kBlockTokens;
-  const int H = p.H, D = p.D, D2 = D / 2;
+  const int H = MODE == kQuantFull ? p.H : min(p.heads_per_cta, p.H - h0);  // heads in this CTA
+  const int D = p.D, D2 = D / 2;
   const int rows = H * nt;
   const QuantSmem lay = quant_smem_layout(H, nt, D, p.n_out, IS_KEY);
 
@@ -300,13 +321,13 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
     __syncwarp();
     if (!p.tok_idx && p.sn == D) {  // each head's nt rows are one contiguous run
       for (int h = tid; h < H; h += 32)
-        tma_load_1d(xs + h * nt * D, p.src + b * p.sb + h * p.sh + static_cast<int64_t>(t0) * D,
+        tma_load_1d(xs + h * nt * D, p.src + b * p.sb + (h0 + h) * p.sh + static_cast<int64_t>(t0) * D,
                     static_cast<uint32_t>(nt) * D * 2, &stage_bar);
     } else {
       for (int r = tid; r < rows; r += 32) {
         const int t = r % nt, h = r / nt;
         const int64_t row = p.tok_idx ? p.tok_idx[b * p.tok_sb + t0 + t] : static_cast<int64_t>(t0 + t);
-        tma_load_1d(xs + r * D, p.src + b * p.sb + h * p.sh + row * p.sn, D * 2, &stage_bar);
+        tma_load_1d(xs + r * D, p.src + b * p.sb + (h0 + h) * p.sh + row * p.sn, D * 2, &stage_bar);
       }
     }
   }
@@ -322,7 +343,7 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
   //      and, for keys, the per-(head, channel) min/max.  A work item is 8
   //      channels of one head; two neighbouring lanes split its tokens.
   const int ncs = D / kEncChunk;
-  if (p.n_out > 0 || IS_KEY) {
+  if (MODE == kQuantStats || (MODE == kQuantFull && (p.n_out > 0 || IS_KEY))) {
     const int items = H * ncs * 2;
     for (int w0 = 0; w0 < items; w0 += kQuantThreads) {
       const int w = w0 + tid;
@@ -373,7 +394,20 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
           mx[i] = __hmax2(mx[i], u32_as_h2(__shfl_xor_sync(mask, h2_as_u32(mx[i]), 1)));
         }
       }
-      if (half == 0) {
+      if (MODE == kQuantStats && half == 0) {  // this chunk's partials
+        const size_t o = ((static_cast<size_t>(b) * p.n_chunks + chunk) * p.H + h0 + h) * D + c8 * kEncChunk;
+        if (p.n_out > 0) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) p.ws_sq[o + i] = s[i];
+        }
+        if constexpr (IS_KEY) {
+          *reinterpret_cast<uint4*>(p.ws_min + o) =
+              make_uint4(h2_as_u32(mn[0]), h2_as_u32(mn[1]), h2_as_u32(mn[2]), h2_as_u32(mn[3]));
+          *reinterpret_cast<uint4*>(p.ws_max + o) =
+              make_uint4(h2_as_u32(mx[0]), h2_as_u32(mx[1]), h2_as_u32(mx[2]), h2_as_u32(mx[3]));
+        }
+      }
+      if (MODE == kQuantFull && half == 0) {
         const int c0 = h * D + c8 * kEncChunk;
         if (p.n_out > 0) {
 #pragma unroll
@@ -389,9 +423,15 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
     }
     __syncthreads();
   }
+  if constexpr (MODE == kQuantStats) return;
 
   // ---- outlier channels: score = mean over heads of the norms, top-n
-  if (p.n_out > 0) {
+  //      (chunked path: the reduction kernel chose them for the whole group)
+  if (MODE == kQuantEncode && p.n_out > 0) {
+    for (int j = tid; j < p.n_out; j += kQuantThreads)
+      oidx[j] = p.ws_oidx[(static_cast<size_t>(b) * p.n_groups + grp) * kMaxOutliersWs + j];
+  }
+  if (MODE == kQuantFull && p.n_out > 0) {
     for (int d = tid; d < D; d += kQuantThreads) {
       float s = 0.f;
       for (int h = 0; h < H; ++h) s += norms[h * D + d];
@@ -419,13 +459,15 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
         __syncwarp();
       }
     }
+  }
+  if (p.n_out > 0) {
     __syncthreads();
     // side store: fp16 originals of the outlier channels (then zeroed in the
     // staged rows, affine_quantizer.py:84-85) and their ids
     const akv_view& od = p.dst.out_data;
     for (int r = tid; r < rows; r += kQuantThreads) {
       const int h = r / nt, t = r - (r / nt) * nt;
-      __half* orow = od.ptr ? reinterpret_cast<__half*>(vaddr(od, b, h, blk0 + (t >> 5), t & 31)) : nullptr;
+      __half* orow = od.ptr ? reinterpret_cast<__half*>(vaddr(od, b, h0 + h, blk0 + (t >> 5), t & 31)) : nullptr;
       for (int j = 0; j < p.n_out; ++j) {
         __half* x = xs + r * D + oidx[j];
         od_s[r * p.n_out + j] = *x;
@@ -436,11 +478,11 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
     const akv_view& oi = p.dst.out_idx;
     if (oi.ptr) {
       for (int w = tid; w < H * nblk; w += kQuantThreads) {
-        int16_t* ids = reinterpret_cast<int16_t*>(vaddr(oi, b, w / nblk, blk0 + w % nblk, 0));
+        int16_t* ids = reinterpret_cast<int16_t*>(vaddr(oi, b, h0 + w / nblk, blk0 + w % nblk, 0));
         for (int j = 0; j < p.n_out; ++j) ids[j] = static_cast<int16_t>(oidx[j]);
       }
     }
-    if constexpr (IS_KEY) {  // a zeroed key column has min = max = 0
+    if (IS_KEY && MODE == kQuantFull) {  // a zeroed key column has min = max = 0
       for (int h = tid; h < H; h += kQuantThreads)
         for (int j = 0; j < p.n_out; ++j) cz[h * D + oidx[j]] = cs[h * D + oidx[j]] = __float2half_rn(0.0f);
     }
@@ -455,9 +497,16 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
     const akv_view& zv = p.dst.zero;
     for (int w = tid; w < H * D2; w += kQuantThreads) {
       const int h = w / D2, dp = w - h * D2;
-      const __half2 lo = reinterpret_cast<const __half2*>(cz)[w];
-      const __half2 hi = reinterpret_cast<const __half2*>(cs)[w];
-      const __half2 sc = affine_scale2<BITS>(lo, hi);
+      __half2 lo, sc;
+      if constexpr (MODE == kQuantEncode) {
+        const size_t o = ((static_cast<size_t>(b) * p.n_groups + grp) * p.H + h0 + h) * D2 + dp;
+        lo = reinterpret_cast<const __half2*>(p.ws_zero)[o];
+        sc = reinterpret_cast<const __half2*>(p.ws_scale)[o];
+        reinterpret_cast<__half2*>(cz)[w] = lo;
+      } else {
+        lo = reinterpret_cast<const __half2*>(cz)[w];
+        sc = affine_scale2<BITS>(lo, reinterpret_cast<const __half2*>(cs)[w]);
+      }
       reinterpret_cast<__half2*>(cs)[w] = sc;
       __half m0, n0, r0, m1, n1, r1;
       if (!fast_coef(__low2half(sc), m0, n0, r0)) {
@@ -472,8 +521,8 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
       kns[w] = h2_as_u32(__halves2half2(n0, n1));
       kr[w] = h2_as_u32(__halves2half2(r0, r1));
       for (int bl = 0; bl < nblk; ++bl) {
-        if (sv.ptr) reinterpret_cast<__half2*>(vaddr(sv, b, h, blk0 + bl, 0))[dp] = sc;
-        if (zv.ptr) reinterpret_cast<__half2*>(vaddr(zv, b, h, blk0 + bl, 0))[dp] = lo;
+        if (sv.ptr) reinterpret_cast<__half2*>(vaddr(sv, b, h0 + h, blk0 + bl, 0))[dp] = sc;
+        if (zv.ptr) reinterpret_cast<__half2*>(vaddr(zv, b, h0 + h, blk0 + bl, 0))[dp] = lo;
       }
     }
   } else {
@@ -508,11 +557,11 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
                           __float_as_uint(-se), __float_as_uint(rc));
       const int h = r / nt, t = r - h * nt;
       const int blk = blk0 + (t >> 5), slot = t & 31;
-      if (p.dst.scale.ptr) *reinterpret_cast<__half*>(vaddr(p.dst.scale, b, h, blk, slot)) = sc;
-      if (p.dst.zero.ptr) *reinterpret_cast<__half*>(vaddr(p.dst.zero, b, h, blk, slot)) = lo;
+      if (p.dst.scale.ptr) *reinterpret_cast<__half*>(vaddr(p.dst.scale, b, h0 + h, blk, slot)) = sc;
+      if (p.dst.zero.ptr) *reinterpret_cast<__half*>(vaddr(p.dst.zero, b, h0 + h, blk, slot)) = lo;
       // outlier residual: fp16 original minus what the zeroed channel dequantises to
       if (p.n_out > 0 && p.dst.out_resid.ptr) {
-        float* rp = reinterpret_cast<float*>(vaddr(p.dst.out_resid, b, h, blk, slot));
+        float* rp = reinterpret_cast<float*>(vaddr(p.dst.out_resid, b, h0 + h, blk, slot));
         const uint32_t c0 = encode_one<BITS>(__float2half_rn(0.0f), lo, se, rc);
         const __half deq = __hadd_rn(__hmul_rn(__uint2half_rn(c0), sc), lo);
         for (int j = 0; j < p.n_out; ++j) rp[j] = __half2float(od_s[r * p.n_out + j]) - __half2float(deq);
@@ -532,7 +581,7 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
     for (int w = tid; w < cols * tpc; w += kQuantThreads) {
       const int col = w % cols, sub = w / cols;
       const int h = col / ncs, c8 = col - h * ncs;
-      char* cbase = cv.ptr ? vaddr(cv, b, h, blk0, 0) + c8 * BITS : nullptr;
+      char* cbase = cv.ptr ? vaddr(cv, b, h0 + h, blk0, 0) + c8 * BITS : nullptr;
       const __half* xcol = xs + h * nt * D + c8 * kEncChunk;
       uint32_t m[4];
       if constexpr (IS_KEY) {
@@ -615,7 +664,91 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
       const int lo = max(t0, bl * kBlockTokens) - bl * kBlockTokens;
       const int hi = min(t0 + nt, (bl + 1) * kBlockTokens) - bl * kBlockTokens;  // exclusive
       const uint32_t m = (hi - lo == 32) ? 0xffffffffu : (((1u << (hi - lo)) - 1u) << lo);
-      *reinterpret_cast<uint32_t*>(vaddr(p.dst.mask, b, h, bl, 0)) = m;
+      *reinterpret_cast<uint32_t*>(vaddr(p.dst.mask, b, h0 + h, bl, 0)) = m;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// chunked path, step 2: one CTA per (group, b) folds the chunk partials in
+// chunk order (a fixed summation order), picks the group's outlier channels
+// (mean over all heads of the per-(head, channel) L2 norms, top-n, lower
+// index on ties) and, for keys, computes zero / scale per (head, channel)
+// with the outlier columns at 0 / 0.  Shared memory: [H][D] fp32 norms, or
+// [H][D] fp16 min and max for keys without outliers, plus [D] fp32 scores.
+// ---------------------------------------------------------------------------
+template <int BITS, bool IS_KEY>
+__global__ void __launch_bounds__(kQuantThreads) quant_reduce_kernel(const QuantParams p) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int tid = threadIdx.x;
+  const int g = blockIdx.x, b = blockIdx.y;
+  const int H = p.H, D = p.D, D2 = D / 2;
+  const int c0 = g * p.group / kBlockTokens;
+  const int c1 = min(p.n_chunks, ((g + 1) * p.group + kBlockTokens - 1) / kBlockTokens);
+  float* norms = reinterpret_cast<float*>(smem_raw);              // [H][D]
+  float* score = norms + static_cast<size_t>(H) * D;               // [D]
+  __shared__ int oidx[kMaxOutliersWs];
+  const size_t rowb = static_cast<size_t>(b) * p.n_chunks;
+
+  if (p.n_out > 0) {
+    for (int w = tid; w < H * D; w += kQuantThreads) {
+      float sq = 0.f;
+      for (int c = c0; c < c1; ++c) sq += p.ws_sq[((rowb + c) * H) * D + w];
+      norms[w] = sqrtf(sq);
+    }
+    __syncthreads();
+    for (int d = tid; d < D; d += kQuantThreads) {
+      float s = 0.f;
+      for (int h = 0; h < H; ++h) s += norms[h * D + d];
+      score[d] = s / static_cast<float>(H);
+    }
+    __syncthreads();
+    if (tid < 32) {
+      for (int j = 0; j < p.n_out; ++j) {
+        float best = -INFINITY;
+        int bi = D;
+        for (int d = tid; d < D; d += 32) {
+          const float s = score[d];
+          if (s > best || (s == best && d < bi)) { best = s; bi = d; }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+          const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+          if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
+        }
+        if (tid == 0) {
+          oidx[j] = bi;
+          score[bi] = -INFINITY;
+          p.ws_oidx[(static_cast<size_t>(b) * p.n_groups + g) * kMaxOutliersWs + j] = bi;
+        }
+        __syncwarp();
+      }
+    }
+    __syncthreads();
+  }
+  if constexpr (IS_KEY) {
+    for (int w = tid; w < H * D2; w += kQuantThreads) {
+      __half2 mn = __float2half2_rn(INFINITY), mx = __float2half2_rn(-INFINITY);
+      for (int c = c0; c < c1; ++c) {
+        const size_t o = (rowb + c) * H * D2 + w;
+        mn = __hmin2(mn, reinterpret_cast<const __half2*>(p.ws_min)[o]);
+        mx = __hmax2(mx, reinterpret_cast<const __half2*>(p.ws_max)[o]);
+      }
+      const int d0 = 2 * (w % D2);
+      for (int j = 0; j < p.n_out; ++j) {  // zeroed outlier column: min = max = 0
+        if (oidx[j] == d0) {
+          mn = __halves2half2(__float2half_rn(0.f), __high2half(mn));
+          mx = __halves2half2(__float2half_rn(0.f), __high2half(mx));
+        }
+        if (oidx[j] == d0 + 1) {
+          mn = __halves2half2(__low2half(mn), __float2half_rn(0.f));
+          mx = __halves2half2(__low2half(mx), __float2half_rn(0.f));
+        }
+      }
+      const size_t o = (static_cast<size_t>(b) * p.n_groups + g) * H * D2 + w;
+      reinterpret_cast<__half2*>(p.ws_zero)[o] = mn;
+      reinterpret_cast<__half2*>(p.ws_scale)[o] = affine_scale2<BITS>(mn, mx);
     }
   }
 }
@@ -748,18 +881,80 @@ size_t quant_smem_bytes(int H, int nt, int D, int n_out, bool is_key) {
   return quant_smem_layout(H, nt, D, n_out, is_key).total;
 }
 
+constexpr size_t kQuantSmemLimit = 220 * 1024;
+
+// How one akv_quantize call runs: one CTA per scale group when the group's
+// rows fit in shared memory, else the chunked path (32-token chunks, heads
+// split into groups of heads_per_cta) with a caller workspace.
+struct QuantPlan {
+  bool chunked;
+  int n_groups, n_chunks, heads_per_cta;
+  size_t smem, reduce_smem;
+  size_t off_min, off_max, off_sq, off_zero, off_scale, off_oidx, ws_bytes;
+};
+
+static size_t up256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+static QuantPlan plan_quant(int B, int H, int N, int D, int group, int n_out, bool is_key) {
+  QuantPlan pl{};
+  pl.n_groups = (N + group - 1) / group;
+  pl.smem = quant_smem_bytes(H, std::min(group, N), D, n_out, is_key);
+  if (pl.smem <= kQuantSmemLimit) return pl;
+  pl.chunked = true;
+  pl.n_chunks = (N + kBlockTokens - 1) / kBlockTokens;
+  int hs = H;
+  while (hs > 1 && quant_smem_bytes(hs, kBlockTokens, D, n_out, is_key) > kQuantSmemLimit) --hs;
+  pl.heads_per_cta = hs;
+  pl.smem = quant_smem_bytes(hs, kBlockTokens, D, n_out, is_key);
+  pl.reduce_smem = (static_cast<size_t>(H) * D + D) * sizeof(float);
+  const size_t part = static_cast<size_t>(B) * pl.n_chunks * H * D;
+  const size_t grp = static_cast<size_t>(B) * pl.n_groups * H * D;
+  pl.off_min = 0;
+  pl.off_max = pl.off_min + up256(part * 2);
+  pl.off_sq = pl.off_max + up256(part * 2);
+  pl.off_zero = pl.off_sq + up256(part * 4);
+  pl.off_scale = pl.off_zero + up256(grp * 2);
+  pl.off_oidx = pl.off_scale + up256(grp * 2);
+  pl.ws_bytes = pl.off_oidx + up256(static_cast<size_t>(B) * pl.n_groups * kMaxOutliersWs * 4);
+  return pl;
+}
+
+template <typename K>
+static bool set_smem(K kern, size_t smem) {
+  return smem <= 48 * 1024 ||
+         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) ==
+             cudaSuccess;
+}
+
 template <int BITS, bool IS_KEY>
-static int launch_quant(const QuantParams& p, cudaStream_t st) {
-  const int ngroups = (p.N + p.group - 1) / p.group;
-  const int nt = min(p.group, p.N);
-  const size_t smem = quant_smem_bytes(p.H, nt, p.D, p.n_out, IS_KEY);
-  auto kern = quantize_group_kernel<BITS, IS_KEY>;
-  if (smem > 48 * 1024) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
-        cudaSuccess)
-      return AKV_ERR_LAUNCH;
+static int launch_quant(QuantParams p, const QuantPlan& pl, void* ws, cudaStream_t st) {
+  if (!pl.chunked) {
+    auto kern = quantize_group_kernel<BITS, IS_KEY, kQuantFull>;
+    if (!set_smem(kern, pl.smem)) return AKV_ERR_LAUNCH;
+    kern<<<dim3(pl.n_groups, p.B), kQuantThreads, pl.smem, st>>>(p);
+    return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_LAUNCH;
   }
-  kern<<<dim3(ngroups, p.B), kQuantThreads, smem, st>>>(p);
+  char* w = static_cast<char*>(ws);
+  p.n_chunks = pl.n_chunks;
+  p.n_groups = pl.n_groups;
+  p.heads_per_cta = pl.heads_per_cta;
+  p.ws_min = reinterpret_cast<__half*>(w + pl.off_min);
+  p.ws_max = reinterpret_cast<__half*>(w + pl.off_max);
+  p.ws_sq = reinterpret_cast<float*>(w + pl.off_sq);
+  p.ws_zero = reinterpret_cast<__half*>(w + pl.off_zero);
+  p.ws_scale = reinterpret_cast<__half*>(w + pl.off_scale);
+  p.ws_oidx = reinterpret_cast<int*>(w + pl.off_oidx);
+  const dim3 grid(pl.n_chunks, p.B, (p.H + pl.heads_per_cta - 1) / pl.heads_per_cta);
+  if (IS_KEY || p.n_out > 0) {
+    auto stats = quantize_group_kernel<BITS, IS_KEY, kQuantStats>;
+    auto reduce = quant_reduce_kernel<BITS, IS_KEY>;
+    if (!set_smem(stats, pl.smem) || !set_smem(reduce, pl.reduce_smem)) return AKV_ERR_LAUNCH;
+    stats<<<grid, kQuantThreads, pl.smem, st>>>(p);
+    reduce<<<dim3(pl.n_groups, p.B), kQuantThreads, pl.reduce_smem, st>>>(p);
+  }
+  auto enc = quantize_group_kernel<BITS, IS_KEY, kQuantEncode>;
+  if (!set_smem(enc, pl.smem)) return AKV_ERR_LAUNCH;
+  enc<<<grid, kQuantThreads, pl.smem, st>>>(p);
   return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_LAUNCH;
 }
 
@@ -776,10 +971,26 @@ static int launch_dequant(const DequantParams& p, cudaStream_t st) {
 
 using namespace akv;
 
+extern "C" size_t akv_quantize_workspace_bytes(int B, int H, int N, int D, int group, int n_outlier, int is_key) {
+  if (B <= 0 || H <= 0 || N <= 0 || D <= 0 || D % 32 != 0 || D > 256) return 0;
+  if (n_outlier < 0 || n_outlier > kMaxOutliers || n_outlier > D) return 0;
+  if (group <= 0 || group > N) group = N;
+  const QuantPlan pl = plan_quant(B, H, N, D, group, n_outlier, is_key != 0);
+  return pl.chunked ? pl.ws_bytes : 0;
+}
+
 extern "C" int akv_quantize(const uint16_t* src, int64_t src_sb, int64_t src_sh, int64_t src_sn,
                             const int64_t* tok_idx, int64_t tok_sb, int B, int H, int N, int D, int bits,
                             int is_key, int group, int n_outlier, const akv_qdest* dst, int* status,
                             void* stream) {
+  return akv_quantize_ws(src, src_sb, src_sh, src_sn, tok_idx, tok_sb, B, H, N, D, bits, is_key, group, n_outlier,
+                         dst, nullptr, 0, status, stream);
+}
+
+extern "C" int akv_quantize_ws(const uint16_t* src, int64_t src_sb, int64_t src_sh, int64_t src_sn,
+                               const int64_t* tok_idx, int64_t tok_sb, int B, int H, int N, int D, int bits,
+                               int is_key, int group, int n_outlier, const akv_qdest* dst, void* workspace,
+                               size_t workspace_bytes, int* status, void* stream) {
   if (!src || !dst) return AKV_ERR_NULL;
   if (bits < 2 || bits > 4) return AKV_ERR_BITS;
   if (B <= 0 || H <= 0 || N <= 0 || D <= 0 || D % 32 != 0 || D > 256) return AKV_ERR_SHAPE;
@@ -799,17 +1010,34 @@ extern "C" int akv_quantize(const uint16_t* src, int64_t src_sb, int64_t src_sh,
     return AKV_ERR_ALIGN;
   if (dst->mask.ptr && !aligned(dst->mask.ptr, 4)) return AKV_ERR_ALIGN;
   if (dst->out_resid.ptr && (!aligned(dst->out_resid.ptr, 4) || dst->out_resid.sslot % 4)) return AKV_ERR_ALIGN;
-  if (quant_smem_bytes(H, group, D, n_outlier, is_key != 0) > 220 * 1024) return AKV_ERR_UNSUPPORTED;
-  QuantParams p{reinterpret_cast<const __half*>(src), src_sb, src_sh, src_sn, tok_idx, tok_sb, B, H, N, D,
-                bits, is_key, group, n_outlier, *dst, status};
+  const QuantPlan pl = plan_quant(B, H, N, D, group, n_outlier, is_key != 0);
+  if (pl.smem > kQuantSmemLimit) return AKV_ERR_UNSUPPORTED;
+  if (pl.chunked && (!workspace || workspace_bytes < pl.ws_bytes || !aligned(workspace, 256))) return AKV_ERR_WORKSPACE;
+  QuantParams p{};
+  p.src = reinterpret_cast<const __half*>(src);
+  p.sb = src_sb;
+  p.sh = src_sh;
+  p.sn = src_sn;
+  p.tok_idx = tok_idx;
+  p.tok_sb = tok_sb;
+  p.B = B;
+  p.H = H;
+  p.N = N;
+  p.D = D;
+  p.bits = bits;
+  p.is_key = is_key;
+  p.group = group;
+  p.n_out = n_outlier;
+  p.dst = *dst;
+  p.status = status;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   switch (bits * 2 + (is_key ? 1 : 0)) {
-    case 5: return launch_quant<2, true>(p, st);
-    case 4: return launch_quant<2, false>(p, st);
-    case 7: return launch_quant<3, true>(p, st);
-    case 6: return launch_quant<3, false>(p, st);
-    case 9: return launch_quant<4, true>(p, st);
-    default: return launch_quant<4, false>(p, st);
+    case 5: return launch_quant<2, true>(p, pl, workspace, st);
+    case 4: return launch_quant<2, false>(p, pl, workspace, st);
+    case 7: return launch_quant<3, true>(p, pl, workspace, st);
+    case 6: return launch_quant<3, false>(p, pl, workspace, st);
+    case 9: return launch_quant<4, true>(p, pl, workspace, st);
+    default: return launch_quant<4, false>(p, pl, workspace, st);
   }
 }
 

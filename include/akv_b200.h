@@ -127,6 +127,21 @@ int akv_quantize(const uint16_t* src, int64_t src_sb, int64_t src_sh, int64_t sr
                  int B, int H, int N, int D, int bits, int is_key, int group, int n_outlier,
                  const akv_qdest* dst, int* status, void* stream);
 
+/* Bytes of caller workspace akv_quantize_ws needs for this shape: 0 when one
+ * CTA holds a whole scale group (akv_quantize then suffices), else the
+ * chunked path's per-chunk column partials and per-group results (a demotion
+ * event quantised as one group, e.g. AKVLayer's drop_in.py:699-701, or any
+ * AffineQuantizer call over more tokens than fit in shared memory). */
+size_t akv_quantize_workspace_bytes(int B, int H, int N, int D, int group, int n_outlier, int is_key);
+
+/* akv_quantize with a workspace (256-byte aligned, at least
+ * akv_quantize_workspace_bytes); identical results.  Without enough
+ * workspace a shape that needs the chunked path returns AKV_ERR_WORKSPACE. */
+int akv_quantize_ws(const uint16_t* src, int64_t src_sb, int64_t src_sh, int64_t src_sn,
+                    const int64_t* tok_idx, int64_t tok_sb,
+                    int B, int H, int N, int D, int bits, int is_key, int group, int n_outlier,
+                    const akv_qdest* dst, void* workspace, size_t workspace_bytes, int* status, void* stream);
+
 /* ------------------------------------------------------------------------
  * A4: unpack + dequantise to fp16.
  * Replaces AffineQuantizer.dequantize_keys/values (akv/affine_quantizer.py:112-124,
