@@ -10,10 +10,12 @@ from .affine_quantizer import AffineQuantConfig, AffineQuantizer
 from .bitpack import pack, unpack, packed_bytes
 from .fused_attention import mixed_precision_decode_attention, mixed_tier_decode_attention
 from .packed_layout import WarmArena, measure_packed_bytes
+from .drop_in import AKVCache, AKVLayer, recommend_preset
 
 __version__ = "0.1.0"
 
 __all__ = [
+    "AKVCache", "AKVLayer", "recommend_preset",
     "AffineQuantConfig", "AffineQuantizer", "WarmArena", "measure_packed_bytes",
     "mixed_tier_decode_attention", "mixed_precision_decode_attention",
     "pack", "unpack", "packed_bytes",

@@ -1,0 +1,590 @@
+"""HuggingFace drop-in: ``AKVCache`` / ``AKVLayer`` (reference akv/drop_in.py).
+
+``AKVCache`` subclasses ``transformers.DynamicCache`` and ``AKVLayer``
+subclasses ``DynamicLayer``, with the reference's constructor arguments,
+presets, tier policy and bookkeeping (drop_in.py:131-878, :885-1318):
+
+* every ``update()`` appends the new tokens to the FP16 hot tier, decays
+  the recency importance (x0.3, new tokens 1.0, :376-390), optionally
+  promotes warm tokens (attention weights, :415-484, or the key-similarity
+  proxy, :486-589), and demotes the lowest-importance hot tokens beyond the
+  budget (:676-751);
+* a demote event is quantised as ONE scale group per batch row, exactly the
+  reference's single ``AffineQuantizer`` call per event (:699-701), by the
+  sm_100a quantiser reading the hot rows in place through the demote indices
+  (fused gather) and writing packed warm block records (``WarmArena``, the
+  source of truth for the warm tier);
+* the returned K/V is the chronologically sorted [warm; hot] FP16 view
+  (:753-787); the warm part is the exact dequantisation of the packed
+  records, produced by the dequantise kernel once per demoted token and kept
+  as the working copy, as the reference does.
+
+Demote selection uses ``torch.topk`` on the CPU importance vector like the
+reference (:392-413): the recency scores are full of ties and the reference's
+tier indices are defined by that call's tie order.  ``akv.tiering`` offers
+the GPU bottom-k kernel for callers whose scores need no such tie parity.
+
+Everything that touches K/V runs on CUDA; a demotion on CPU tensors raises
+(no CPU fallback).  Layers that never demote (large budget, protected
+layers) only concatenate tensors and work on any device, like the
+reference.
+"""
+from __future__ import annotations
+
+import logging
+from typing import Any, Optional, Tuple
+
+import torch
+
+from . import _C
+from .bitpack import packed_width
+from .packed_layout import BLOCK, WarmArena
+
+logger = logging.getLogger(__name__)
+
+try:
+    from transformers.cache_utils import DynamicCache as _CacheBase
+    from transformers.cache_utils import DynamicLayer as _LayerBase
+except ImportError:  # transformers absent: plain containers with the same surface
+    class _CacheBase:  # type: ignore[no-redef]
+        def __init__(self, *args, **kwargs):
+            self.layers = []
+
+    class _LayerBase:  # type: ignore[no-redef]
+        def __init__(self):
+            self.keys = None
+            self.values = None
+            self.is_initialized = False
+
+        def get_seq_length(self) -> int:
+            return 0 if self.keys is None else self.keys.shape[-2]
+
+
+# presets of the reference (drop_in.py:89-126)
+_PRESETS = {
+    "quality": {"warm_bits": 4, "hot_budget": 256, "description": "Near-lossless 4-bit. +1-2% PPL."},
+    "balanced": {"warm_bits": 3, "hot_budget": 128, "description": "Block-affine 3-bit. +3.3% PPL, 5x compression."},
+    "compact": {"warm_bits": 2, "hot_budget": 64, "description": "Block-affine 2-bit. +11% PPL, 8x compression."},
+    "k4v2": {"warm_bits": 4, "warm_key_bits": 4, "warm_value_bits": 2, "hot_budget": 128,
+             "description": "Asymmetric K4/V2. Keys preserved, values aggressively compressed."},
+    "k4v3": {"warm_bits": 4, "warm_key_bits": 4, "warm_value_bits": 3, "hot_budget": 128,
+             "description": "Asymmetric K4/V3. Near-quality keys with balanced value compression."},
+}
+
+
+class AKVLayer(_LayerBase):
+    """Per-layer tiered KV state (reference drop_in.py:131-878)."""
+
+    is_compileable: bool = False
+    is_sliding: bool = False
+
+    def __init__(self, warm_bits: int = 3, hot_budget: int = 128, group_size: int = 64, protect: bool = False,
+                 enable_promotion: bool = True, promotion_threshold: float = 0.05,
+                 per_head_bits: Optional[list] = None, enable_promotion_proxy: bool = True,
+                 proxy_decay: float = 0.7, adaptive_hot_frac: float = 0.0,
+                 warm_key_bits: Optional[int] = None, warm_value_bits: Optional[int] = None,
+                 outlier_fraction: float = 0.0):
+        try:
+            super().__init__()
+        except TypeError:
+            self.keys = None
+            self.values = None
+            self.is_initialized = False
+        if per_head_bits is not None:
+            raise NotImplementedError("per-head warm bit widths are not supported by the packed warm tier")
+        self.warm_bits = warm_bits
+        self.hot_budget = hot_budget
+        self.group_size = group_size
+        self.protect = protect
+        self.enable_promotion = enable_promotion
+        self.promotion_threshold = promotion_threshold
+        self.enable_promotion_proxy = enable_promotion_proxy
+        self.proxy_decay = proxy_decay
+        self.adaptive_hot_frac = adaptive_hot_frac
+        self.warm_key_bits = warm_key_bits or warm_bits
+        self.warm_value_bits = warm_value_bits or warm_bits
+        self.outlier_fraction = outlier_fraction
+        self.per_head_bits = None
+
+        self._hot_keys: Optional[torch.Tensor] = None
+        self._hot_values: Optional[torch.Tensor] = None
+        self._warm_keys_fp16: Optional[torch.Tensor] = None  # exact dequantisation of the warm records
+        self._warm_values_fp16: Optional[torch.Tensor] = None
+        self._warm: Optional[WarmArena] = None  # packed warm block records (source of truth)
+        self._warm_slots: Optional[torch.Tensor] = None  # arena slot (blk*32 + s) of each warm token
+        self._warm_len = 0
+        self._total_len = 0
+        self._warm_bytes_packed = 0
+        self._proxy_score: Optional[torch.Tensor] = None
+        self._hot_positions: Optional[torch.Tensor] = None
+        self._warm_positions: Optional[torch.Tensor] = None
+        self._importance: Optional[torch.Tensor] = None
+        self._decay = 0.3
+        self._n_anchors = 16
+        self._step = 0
+
+    # ------------------------------------------------------------------ importance / selection
+    def _update_importance(self, n_new: int, hot_len: int) -> None:
+        """Recency importance on the CPU (drop_in.py:376-390)."""
+        if self._importance is None or self._importance.shape[0] != hot_len - n_new:
+            self._importance = torch.ones(hot_len, dtype=torch.float32)
+        else:
+            self._importance = torch.cat([self._importance * self._decay, torch.ones(n_new, dtype=torch.float32)])
+
+    def _select_demote_indices(self, n_demote: int, hot_len: int) -> torch.Tensor:
+        """Lowest importance, first 4 / last min(16, budget//4) protected, ascending (drop_in.py:392-413)."""
+        protect_initial = 4
+        protect_recent = min(16, self.hot_budget // 4)
+        if self._importance is None or self._importance.shape[0] != hot_len:
+            return torch.arange(n_demote)
+        scores = self._importance.clone()
+        scores[:protect_initial] = float("inf")
+        scores[max(0, hot_len - protect_recent):] = float("inf")
+        _, idx = scores.topk(n_demote, largest=False)
+        idx, _ = idx.sort()
+        return idx
+
+    # ------------------------------------------------------------------ warm tier
+    def _demote(self, demote_idx: torch.Tensor) -> None:
+        """Quantise the selected hot rows into new warm records (one scale group per batch row)."""
+        hk, hv = self._hot_keys, self._hot_values
+        _C.require_cuda(hk, hv)
+        B, H, _, D = hk.shape
+        n = int(demote_idx.numel())
+        if self._warm is None:
+            self._warm = WarmArena(B, H, D, self.warm_key_bits, self.warm_value_bits, self.outlier_fraction,
+                                   max_blocks=max(4, (n + BLOCK - 1) // BLOCK), device=hk.device)
+        arena = self._warm
+        nblk = (n + BLOCK - 1) // BLOCK
+        arena.grow(arena.n_blocks + nblk)
+        idx_dev = demote_idx.to(hk.device)
+        blk0 = arena.append(hk, hv, group=n, tok_idx=idx_dev)
+        slots = torch.arange(blk0 * BLOCK, blk0 * BLOCK + n, dtype=torch.int64, device=hk.device)
+        dk, dv = arena.dequantize(tok_idx=slots)
+        # the reference's measure_packed_bytes of this event's K and V dicts (drop_in.py:331-336)
+        kb, vb = self.warm_key_bits, self.warm_value_bits
+        self._warm_bytes_packed += B * (H * n * packed_width(D, kb) + 4 * H * D + H * n * packed_width(D, vb) + 4 * H * n)
+        if self._warm_keys_fp16 is None:
+            self._warm_keys_fp16, self._warm_values_fp16, self._warm_slots = dk, dv, slots
+        else:
+            self._warm_keys_fp16 = torch.cat([self._warm_keys_fp16, dk], dim=2)
+            self._warm_values_fp16 = torch.cat([self._warm_values_fp16, dv], dim=2)
+            self._warm_slots = torch.cat([self._warm_slots, slots])
+
+    def _remove_warm(self, promote_mask: torch.Tensor, n_promote: int, warm_len: int) -> None:
+        """Drop promoted tokens from the warm tier (records keep the bytes, mask bits cleared)."""
+        keep = ~promote_mask
+        gone = self._warm_slots[promote_mask.to(self._warm_slots.device)]
+        if self._warm is not None and gone.numel():
+            words = self._warm.buf[:, :, :, self._warm.layout.mask:self._warm.layout.mask + 4]
+            m = words.contiguous().view(torch.int32)[..., 0]
+            blk = gone // BLOCK
+            bit = torch.ones_like(gone, dtype=torch.int64) << (gone % BLOCK)
+            clear = torch.zeros(m.shape[-1], dtype=torch.int64, device=m.device).index_add_(0, blk, bit)
+            m &= (~clear).to(torch.int32)
+            words.copy_(m.unsqueeze(-1).view(torch.uint8).view(words.shape))
+        self._warm_keys_fp16 = self._warm_keys_fp16[:, :, keep, :]
+        self._warm_values_fp16 = self._warm_values_fp16[:, :, keep, :]
+        self._warm_slots = self._warm_slots[keep.to(self._warm_slots.device)]
+        if self._warm_positions is not None:
+            self._warm_positions = self._warm_positions[keep.detach().to("cpu")]
+        if warm_len > 0:
+            keep_frac = max(0, warm_len - n_promote) / warm_len
+            self._warm_bytes_packed = int(self._warm_bytes_packed * keep_frac)
+        self._warm_len -= n_promote
+
+    def _promote(self, promote_mask: torch.Tensor, n_promote: int, filter_proxy: bool) -> None:
+        """Move warm tokens to the front of the hot tier with importance 2.0.
+
+        The proxy path keeps its scores aligned with the warm tier; the
+        attention path leaves them as they are, like the reference (the next
+        proxy update then restarts the EMA on the length mismatch)."""
+        warm_len = self._warm_keys_fp16.shape[2]
+        promote_idx = promote_mask.nonzero(as_tuple=True)[0]
+        promoted_k = self._warm_keys_fp16[:, :, promote_idx, :]
+        promoted_v = self._warm_values_fp16[:, :, promote_idx, :]
+        promoted_pos = self._warm_positions[promote_idx.detach().to("cpu")] if self._warm_positions is not None else None
+        if filter_proxy:
+            self._proxy_score = self._proxy_score[~promote_mask]
+        self._remove_warm(promote_mask, n_promote, warm_len)
+        self._hot_keys = torch.cat([promoted_k, self._hot_keys], dim=2)
+        self._hot_values = torch.cat([promoted_v, self._hot_values], dim=2)
+        if promoted_pos is not None and self._hot_positions is not None:
+            self._hot_positions = torch.cat([promoted_pos, self._hot_positions])
+        if self._importance is not None:
+            self._importance = torch.cat([torch.ones(n_promote) * 2.0, self._importance])
+
+    def _cap_promotion(self, score: torch.Tensor, promote_mask: torch.Tensor) -> Tuple[torch.Tensor, int]:
+        n_promote = int(promote_mask.sum().item())
+        max_promote = max(1, self.hot_budget // 8)
+        if n_promote > max_promote:
+            _, top_idx = score.topk(max_promote)
+            promote_mask = torch.zeros_like(promote_mask)
+            promote_mask[top_idx] = True
+            n_promote = max_promote
+        return promote_mask, n_promote
+
+    def _promote_from_warm(self, attention_weights: torch.Tensor) -> None:
+        """Promotion by mean attention to warm tokens (drop_in.py:415-484)."""
+        if self._warm_keys_fp16 is None or self._warm_keys_fp16.shape[2] == 0 or self._hot_keys is None:
+            return
+        warm_len = self._warm_keys_fp16.shape[2]
+        hot_len = self._hot_keys.shape[2]
+        if attention_weights.dim() == 4 and attention_weights.shape[-1] >= warm_len + hot_len:
+            warm_attn = attention_weights[:, :, :, :warm_len].mean(dim=(0, 1, 2))
+            promote_mask = warm_attn > self.promotion_threshold
+            if int(promote_mask.sum().item()) > 0:
+                promote_mask, n_promote = self._cap_promotion(warm_attn, promote_mask)
+                self._promote(promote_mask, n_promote, filter_proxy=False)
+
+    def _update_proxy_score(self, key_states: torch.Tensor) -> None:
+        """EMA of |cos(mean new key, warm key)| per warm token (drop_in.py:486-525)."""
+        if self._warm_keys_fp16 is None or self._warm_keys_fp16.shape[2] == 0:
+            self._proxy_score = None
+            return
+        probe = key_states.detach().float().mean(dim=(0, 1, 2))
+        probe = probe / (probe.norm() + 1e-6)
+        wk = self._warm_keys_fp16.detach().float().mean(dim=(0, 1))
+        wk = wk / (wk.norm(dim=-1, keepdim=True) + 1e-6)
+        sim = wk @ probe
+        if self._proxy_score is None or self._proxy_score.shape[0] != sim.shape[0]:
+            self._proxy_score = sim.abs()
+        else:
+            d = self.proxy_decay
+            self._proxy_score = d * self._proxy_score + (1 - d) * sim.abs()
+
+    def _promote_from_proxy(self) -> None:
+        """Attention-free promotion (drop_in.py:527-589)."""
+        if (self._proxy_score is None or self._warm_keys_fp16 is None or self._warm_keys_fp16.shape[2] == 0
+                or self._hot_keys is None):
+            return
+        if self._proxy_score.shape[0] != self._warm_keys_fp16.shape[2]:
+            return
+        promote_mask = self._proxy_score > self.promotion_threshold
+        if int(promote_mask.sum().item()) == 0:
+            return
+        promote_mask, n_promote = self._cap_promotion(self._proxy_score, promote_mask)
+        self._promote(promote_mask, n_promote, filter_proxy=True)
+
+    # ------------------------------------------------------------------ update
+    def _publish(self, k: torch.Tensor, v: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+        self.keys, self.values = k, v
+        self.dtype, self.device = k.dtype, k.device
+        self.is_initialized = True
+        return k, v
+
+    def update(self, key_states: torch.Tensor, value_states: torch.Tensor,
+               cache_kwargs: Optional[dict] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Append, migrate, return the chronological full view (drop_in.py:591-787)."""
+        N = key_states.shape[2]
+        new_positions = torch.arange(self._total_len, self._total_len + N, dtype=torch.long)
+        if self._hot_keys is None:
+            self._hot_keys, self._hot_values, self._hot_positions = key_states, value_states, new_positions
+        else:
+            self._hot_keys = torch.cat([self._hot_keys, key_states], dim=2)
+            self._hot_values = torch.cat([self._hot_values, value_states], dim=2)
+            self._hot_positions = torch.cat([self._hot_positions, new_positions])
+        self._total_len += N
+        if self.protect:
+            return self._publish(self._hot_keys, self._hot_values)
+        self._step += 1
+
+        hot_len = self._hot_keys.shape[2]
+        self._update_importance(N, hot_len)
+        if self.enable_promotion_proxy:
+            self._update_proxy_score(key_states)
+        if self.enable_promotion and cache_kwargs and "attention_weights" in cache_kwargs:
+            self._promote_from_warm(cache_kwargs["attention_weights"])
+            hot_len = self._hot_keys.shape[2]
+        elif self.enable_promotion and self.enable_promotion_proxy:
+            self._promote_from_proxy()
+            hot_len = self._hot_keys.shape[2]
+
+        budget = self.hot_budget
+        if self.adaptive_hot_frac > 0.0:
+            budget = max(self.hot_budget, int(self.adaptive_hot_frac * self._total_len))
+
+        if hot_len > budget:
+            n_demote = hot_len - budget
+            demote_idx = self._select_demote_indices(n_demote, hot_len)
+            demote_positions = self._hot_positions[demote_idx]
+            self._demote(demote_idx)
+            self._warm_positions = (demote_positions if self._warm_positions is None
+                                    else torch.cat([self._warm_positions, demote_positions]))
+            self._warm_len += n_demote
+            if self._proxy_score is not None:
+                pad = torch.zeros(n_demote, dtype=self._proxy_score.dtype, device=self._warm_keys_fp16.device)
+                self._proxy_score = torch.cat([self._proxy_score.to(pad.device), pad])
+            keep = torch.ones(hot_len, dtype=torch.bool)
+            keep[demote_idx] = False
+            keep_dev = keep.to(self._hot_keys.device)
+            self._hot_keys = self._hot_keys[:, :, keep_dev, :]
+            self._hot_values = self._hot_values[:, :, keep_dev, :]
+            self._hot_positions = self._hot_positions[keep]
+            if self._importance is not None:
+                self._importance = self._importance[keep]
+
+        if self._warm_keys_fp16 is not None:
+            full_k = torch.cat([self._warm_keys_fp16, self._hot_keys], dim=2)
+            full_v = torch.cat([self._warm_values_fp16, self._hot_values], dim=2)
+            order = torch.cat([self._warm_positions, self._hot_positions]).argsort().to(full_k.device)
+            full_k = full_k.index_select(2, order)
+            full_v = full_v.index_select(2, order)
+        else:
+            full_k, full_v = self._hot_keys, self._hot_values
+        return self._publish(full_k, full_v)
+
+    # ------------------------------------------------------------------ accounting
+    def memory_usage_bytes(self) -> dict:
+        """Per-layer byte accounting with the reference's keys (drop_in.py:794-878)."""
+        H, D = 1, 128
+        hot = 0
+        if self._hot_keys is not None:
+            hot = (self._hot_keys.element_size() * self._hot_keys.numel()
+                   + self._hot_values.element_size() * self._hot_values.numel())
+            H, D = self._hot_keys.shape[1], self._hot_keys.shape[3]
+        live = 0
+        if self._warm_keys_fp16 is not None:
+            live = (self._warm_keys_fp16.element_size() * self._warm_keys_fp16.numel()
+                    + self._warm_values_fp16.element_size() * self._warm_values_fp16.numel())
+        packed = int(self._warm_bytes_packed)
+        formula = 0
+        if self._warm_len > 0:
+            groups = (D + self.group_size - 1) // self.group_size
+            formula = self._warm_len * (((H * D * self.warm_bits + 7) // 8) + groups * H * 4) * 2
+        total = hot + packed
+        fp16_equiv = self._total_len * H * D * 2 * 2
+        return {"hot_bytes": hot, "warm_bytes": packed, "warm_bytes_live": live, "warm_bytes_packed": packed,
+                "warm_bytes_formula": formula, "total_bytes": total, "fp16_equivalent_bytes": fp16_equiv,
+                "savings_ratio": fp16_equiv / max(total, 1),
+                "warm_bytes_resident": 0 if self._warm is None else self._warm.resident_bytes()}
+
+    # ------------------------------------------------------------------ batch ops
+    def _select_batch(self, fn) -> None:
+        if self._hot_keys is not None:
+            self._hot_keys, self._hot_values = fn(self._hot_keys), fn(self._hot_values)
+        if self._warm_keys_fp16 is not None:
+            self._warm_keys_fp16, self._warm_values_fp16 = fn(self._warm_keys_fp16), fn(self._warm_values_fp16)
+
+
+class AKVCache(_CacheBase):
+    """Drop-in ``DynamicCache`` with a packed warm tier (reference drop_in.py:885-1318)."""
+
+    def __init__(self, preset: Optional[str] = None, warm_bits: Optional[int] = None,
+                 warm_key_bits: Optional[int] = None, warm_value_bits: Optional[int] = None,
+                 hot_budget: Optional[int] = None, group_size: int = 64, outlier_fraction: float = 0.0,
+                 protect_first: int = 0, protect_last: int = 0, protect_layers: Optional[list] = None,
+                 num_hidden_layers: Optional[int] = None, enable_promotion: bool = True,
+                 promotion_threshold: float = 0.05, enable_promotion_proxy: bool = True,
+                 proxy_decay: float = 0.7, adaptive_hot_frac: float = 0.0):
+        if preset is not None:
+            if preset not in _PRESETS:
+                raise ValueError(f"Unknown preset {preset!r}. Choose from: {sorted(_PRESETS.keys())}")
+            if warm_bits is not None or hot_budget is not None:
+                raise ValueError("preset= is mutually exclusive with warm_bits/hot_budget. "
+                                 "Pick a preset OR pass explicit params.")
+            p = _PRESETS[preset]
+            self.warm_bits, self.hot_budget = p["warm_bits"], p["hot_budget"]
+        else:
+            self.warm_bits = warm_bits or 3
+            self.hot_budget = hot_budget or 128
+        if preset and "warm_key_bits" in _PRESETS[preset]:
+            self.warm_key_bits = _PRESETS[preset]["warm_key_bits"]
+            self.warm_value_bits = _PRESETS[preset]["warm_value_bits"]
+        else:
+            self.warm_key_bits = warm_key_bits or self.warm_bits
+            self.warm_value_bits = warm_value_bits or self.warm_bits
+        self.group_size = group_size
+        self.outlier_fraction = outlier_fraction
+        self.num_hidden_layers = num_hidden_layers
+        self.enable_promotion = enable_promotion
+        self.promotion_threshold = promotion_threshold
+        self.enable_promotion_proxy = enable_promotion_proxy
+        self.proxy_decay = proxy_decay
+        self.adaptive_hot_frac = adaptive_hot_frac
+        self._protect_first = protect_first
+        self._protect_last = protect_last
+        self._protect_explicit = list(protect_layers) if protect_layers else []
+        if protect_last > 0 and num_hidden_layers is None:
+            raise ValueError("protect_last requires num_hidden_layers. "
+                             "Use AKVCache.for_model(model, ...) or pass num_hidden_layers=.")
+        self._protected_set: set = set(range(protect_first))
+        if num_hidden_layers is not None:
+            for i in range(protect_last):
+                self._protected_set.add(num_hidden_layers - 1 - i)
+            for p in self._protect_explicit:
+                self._protected_set.add(p if p >= 0 else num_hidden_layers + p)
+        else:
+            for p in self._protect_explicit:
+                if p < 0:
+                    raise ValueError("Negative protect_layers indices require num_hidden_layers. "
+                                     "Use AKVCache.for_model(model, ...).")
+                self._protected_set.add(p)
+        super().__init__()
+        self._seen_tokens = 0
+
+    @classmethod
+    def for_model(cls, model, **kwargs) -> "AKVCache":
+        """Cache sized from ``model.config.num_hidden_layers`` (drop_in.py:1011-1054, no adapter registry)."""
+        config = getattr(model, "config", None)
+        if config is None:
+            raise ValueError("model has no .config attribute")
+        n_layers = getattr(config, "num_hidden_layers", None) or getattr(config, "n_layer", None)
+        if n_layers is None:
+            raise ValueError("Could not find num_hidden_layers in model.config. Pass num_hidden_layers= explicitly.")
+        return cls(num_hidden_layers=n_layers, **kwargs)
+
+    def _is_protected(self, layer_idx: int) -> bool:
+        return layer_idx in self._protected_set
+
+    def _new_layer(self, idx: int) -> AKVLayer:
+        return AKVLayer(warm_bits=self.warm_bits, hot_budget=self.hot_budget, group_size=self.group_size,
+                        protect=self._is_protected(idx), enable_promotion=self.enable_promotion,
+                        promotion_threshold=self.promotion_threshold,
+                        enable_promotion_proxy=self.enable_promotion_proxy, proxy_decay=self.proxy_decay,
+                        adaptive_hot_frac=self.adaptive_hot_frac, warm_key_bits=self.warm_key_bits,
+                        warm_value_bits=self.warm_value_bits, outlier_fraction=self.outlier_fraction)
+
+    def update(self, key_states: torch.Tensor, value_states: torch.Tensor, layer_idx: int,
+               cache_kwargs: Optional[dict[str, Any]] = None, *args, **kwargs) -> Tuple[torch.Tensor, torch.Tensor]:
+        """``DynamicCache.update`` contract (drop_in.py:1059-1096)."""
+        while len(self.layers) <= layer_idx:
+            self.layers.append(self._new_layer(len(self.layers)))
+        if layer_idx == 0:
+            self._seen_tokens += key_states.shape[2]
+        return self.layers[layer_idx].update(key_states, value_states, cache_kwargs)
+
+    def get_seq_length(self, layer_idx: int = 0, *args, **kwargs) -> int:
+        if layer_idx < len(self.layers):
+            return self.layers[layer_idx].get_seq_length()
+        return 0
+
+    def get_usable_length(self, max_length: int, layer_idx: int = 0) -> int:
+        return self.get_seq_length(layer_idx)
+
+    def get_max_length(self) -> Optional[int]:
+        return None
+
+    @property
+    def seen_tokens(self) -> int:
+        return self._seen_tokens
+
+    @seen_tokens.setter
+    def seen_tokens(self, value: int):
+        self._seen_tokens = value
+
+    # ------------------------------------------------------------------ batch / beam ops
+    def _each_batch(self, fn, arena_index=None) -> None:
+        for layer in self.layers:
+            layer._select_batch(fn)
+            if layer._warm is not None and arena_index is not None:
+                layer._warm.select_batch(arena_index)
+            if layer.keys is not None and layer._hot_keys is not None:
+                layer.keys, layer.values = fn(layer.keys), fn(layer.values)
+
+    def reorder_cache(self, beam_idx: torch.LongTensor):
+        self._each_batch(lambda t: t.index_select(0, beam_idx.to(t.device)), beam_idx)
+
+    def batch_repeat_interleave(self, repeats: int):
+        idx = None
+        if self.layers and self.layers[0]._hot_keys is not None:
+            B = self.layers[0]._hot_keys.shape[0]
+            idx = torch.arange(B).repeat_interleave(repeats)
+        self._each_batch(lambda t: t.repeat_interleave(repeats, dim=0), idx)
+        return self
+
+    def batch_select_indices(self, indices: torch.LongTensor):
+        self._each_batch(lambda t: t.index_select(0, indices.to(t.device)), indices)
+        return self
+
+    def crop(self, max_length: int):
+        """Trim the hot tier from the end (drop_in.py:1231-1243)."""
+        for layer in self.layers:
+            if layer._hot_keys is not None:
+                cur = layer._hot_keys.shape[2] + (0 if layer._warm_keys_fp16 is None else layer._warm_keys_fp16.shape[2])
+                if cur > max_length:
+                    keep = max(0, layer._hot_keys.shape[2] - (cur - max_length))
+                    layer._hot_keys = layer._hot_keys[:, :, :keep, :]
+                    layer._hot_values = layer._hot_values[:, :, :keep, :]
+                    layer._total_len = max_length
+
+    def reset(self):
+        self.layers.clear()
+        self._seen_tokens = 0
+
+    # ------------------------------------------------------------------ accounting
+    def memory_usage(self) -> dict:
+        keys = ("hot_bytes", "warm_bytes", "warm_bytes_live", "warm_bytes_packed", "warm_bytes_formula",
+                "total_bytes", "fp16_equivalent_bytes", "warm_bytes_resident")
+        totals = {k: 0 for k in keys}
+        for layer in self.layers:
+            stats = layer.memory_usage_bytes()
+            for k in keys:
+                totals[k] += stats.get(k, 0)
+        totals["savings_ratio"] = totals["fp16_equivalent_bytes"] / max(totals["total_bytes"], 1)
+        totals["num_layers"] = len(self.layers)
+        return totals
+
+    def memory_report(self) -> dict:
+        stats = self.memory_usage()
+        return {"compressed_bytes": stats["total_bytes"], "fp16_equiv_bytes": stats["fp16_equivalent_bytes"],
+                "savings_ratio": round(stats["savings_ratio"], 2), "key_bits": self.warm_key_bits,
+                "value_bits": self.warm_value_bits, "num_layers": stats["num_layers"],
+                "seq_length": self.get_seq_length(0)}
+
+    # ------------------------------------------------------------------ legacy accessors
+    def __len__(self) -> int:
+        return len(self.layers)
+
+    def __getitem__(self, layer_idx: int):
+        if layer_idx < len(self.layers):
+            layer = self.layers[layer_idx]
+            if layer._hot_keys is not None:
+                if layer._warm_keys_fp16 is not None:
+                    return (torch.cat([layer._warm_keys_fp16, layer._hot_keys], dim=2),
+                            torch.cat([layer._warm_values_fp16, layer._hot_values], dim=2))
+                return (layer._hot_keys, layer._hot_values)
+        return (torch.tensor([]), torch.tensor([]))
+
+    def __iter__(self):
+        for i in range(len(self.layers)):
+            yield self[i]
+
+    def to_legacy_cache(self):
+        return tuple(self[i] for i in range(len(self.layers)))
+
+    @property
+    def key_cache(self):
+        return [self[i][0] for i in range(len(self.layers))]
+
+    @property
+    def value_cache(self):
+        return [self[i][1] for i in range(len(self.layers))]
+
+    @classmethod
+    def from_legacy_cache(cls, past_key_values=None):
+        cache = cls()
+        if past_key_values is not None:
+            for layer_idx, (k, v) in enumerate(past_key_values):
+                cache.update(k, v, layer_idx)
+        return cache
+
+
+def recommend_preset(model, tokenizer=None, sample_text: str = None) -> dict:
+    """Preset heuristic from the model config (reference drop_in.py:1321-1366)."""
+    config = getattr(model, "config", None)
+    if config is None:
+        return {"preset": "balanced", "reason": "No config found, using default"}
+    n_layers = getattr(config, "num_hidden_layers", 32)
+    n_heads = getattr(config, "num_key_value_heads", getattr(config, "num_attention_heads", 32))
+    head_dim = getattr(config, "head_dim",
+                       getattr(config, "hidden_size", 4096) // getattr(config, "num_attention_heads", 32))
+    est = n_layers * n_heads * head_dim * head_dim * 4
+    if est > 5e9:
+        return {"preset": "balanced", "warm_bits": 3, "hot_budget": 128, "protect_first": 2, "protect_last": 2,
+                "reason": f"Large model ({est/1e9:.0f}B est.) — robust to 3-bit"}
+    if est > 1e9:
+        return {"preset": "quality", "warm_bits": 4, "hot_budget": 256, "protect_first": 1, "protect_last": 1,
+                "reason": f"Medium model ({est/1e9:.1f}B est.) — use 4-bit for safety"}
+    return {"preset": "quality", "warm_bits": 4, "hot_budget": 512, "protect_first": 2, "protect_last": 2,
+            "reason": f"Small model ({est/1e9:.1f}B est.) — protect more layers"}

@@ -90,6 +90,20 @@ class WarmArena:
         d.mask = _C.View(base + L.mask, sb, sh, rec, 0)
         return d
 
+    def grow(self, min_blocks: int) -> None:
+        """Make room for at least ``min_blocks`` blocks (capacity doubles; records are copied)."""
+        if min_blocks <= self.max_blocks:
+            return
+        new_max = max(min_blocks, 2 * self.max_blocks)
+        buf = torch.zeros(self.B, self.H, new_max, self.rec, dtype=torch.uint8, device=self.buf.device)
+        buf[:, :, : self.n_blocks] = self.buf[:, :, : self.n_blocks]
+        self.buf, self.max_blocks = buf, new_max
+
+    def select_batch(self, index: torch.Tensor) -> None:
+        """Keep / repeat batch rows (beam search reorder, batch_select_indices)."""
+        self.buf = self.buf.index_select(0, index.to(self.buf.device))
+        self.B = self.buf.shape[0]
+
     # -------------------------------------------------------------- writes
     def append(self, k: torch.Tensor, v: torch.Tensor, group: int = BLOCK, tok_idx: torch.Tensor | None = None,
                status: torch.Tensor | None = None) -> int:

@@ -255,5 +255,80 @@ def main(ref_path: str):
     print("golden fixtures written to", HERE)
 
 
+def make_drop_in_traces(ref_path: str):
+    """AKVCache update traces of the reference (tier positions after every
+    update, final chronological K/V view, byte accounting) for seeded inputs.
+
+    Promotion, where enabled, is driven by attention weights on a grid of
+    powers of two, so the promotion threshold test is exact on any device."""
+    import torch
+    torch.set_num_threads(1)
+    sys.path.insert(0, ref_path)
+    from akv.drop_in import AKVCache
+    cases = {
+        "a": dict(kw=dict(warm_bits=3, hot_budget=64, enable_promotion=False, enable_promotion_proxy=False),
+                  steps=[200] + [1] * 20 + [40] + [1] * 10, attn=False, outlier=()),
+        "b": dict(kw=dict(preset="k4v2", outlier_fraction=0.01, enable_promotion=True, enable_promotion_proxy=False,
+                          promotion_threshold=0.3),
+                  steps=[160] + [1] * 30, attn=True, outlier=(5,), budget=48),
+        "c": dict(kw=dict(warm_bits=2, hot_budget=32, adaptive_hot_frac=0.25, enable_promotion=False,
+                          enable_promotion_proxy=False),
+                  steps=[300] + [1] * 20, attn=False, outlier=()),
+    }
+    out = {}
+    H, D = 2, 64
+    for name, c in cases.items():
+        g = torch.Generator().manual_seed(ord(name))
+        kw = dict(c["kw"])
+        cache = AKVCache(num_hidden_layers=1, **kw)
+        if "budget" in c:  # presets fix the budget; the trace uses a smaller one
+            cache.hot_budget = c["budget"]
+        warm_pos, hot_pos, ks, vs, attns = [], [], [], [], []
+        total = 0
+        for si, n in enumerate(c["steps"]):
+            k = make_kv(g, H, n, D, outlier_ch=c["outlier"]).unsqueeze(0)
+            v = make_kv(g, H, n, D).unsqueeze(0)
+            ck = None
+            if c["attn"] and si > 0:
+                layer = cache.layers[0]
+                warm_len = 0 if layer._warm_keys_fp16 is None else layer._warm_keys_fp16.shape[2]
+                a = torch.zeros(1, H, 1, total + n)
+                if warm_len:
+                    pick = torch.randperm(warm_len, generator=g)[:3]
+                    a[0, 0, 0, pick] = 0.5
+                    a[0, 1, 0, pick[:2]] = 0.25
+                ck = {"attention_weights": a}
+                attns.append(a.reshape(-1).numpy())
+            full_k, full_v = cache.update(k, v, 0, ck)
+            total += n
+            layer = cache.layers[0]
+            warm_pos.append(np.array([] if layer._warm_positions is None else layer._warm_positions.tolist(),
+                                     dtype=np.int64))
+            hot_pos.append(layer._hot_positions.numpy().astype(np.int64))
+            ks.append(k.numpy())
+            vs.append(v.numpy())
+        out[f"{name}/steps"] = np.array(c["steps"], dtype=np.int64)
+        out[f"{name}/k_in"] = np.concatenate(ks, axis=2)
+        out[f"{name}/v_in"] = np.concatenate(vs, axis=2)
+        out[f"{name}/warm_pos"] = np.concatenate(warm_pos)
+        out[f"{name}/warm_len"] = np.array([len(w) for w in warm_pos], dtype=np.int64)
+        out[f"{name}/hot_pos"] = np.concatenate(hot_pos)
+        out[f"{name}/hot_len"] = np.array([len(h) for h in hot_pos], dtype=np.int64)
+        if attns:
+            out[f"{name}/attn"] = np.concatenate(attns)
+            out[f"{name}/attn_len"] = np.array([len(a) for a in attns], dtype=np.int64)
+        out[f"{name}/full_k"] = full_k.numpy()
+        out[f"{name}/full_v"] = full_v.numpy()
+        mu = cache.memory_usage()
+        for key in ("hot_bytes", "warm_bytes_packed", "warm_bytes_live", "fp16_equivalent_bytes", "total_bytes"):
+            out[f"{name}/mem/{key}"] = np.array(mu[key], dtype=np.int64)
+    np.savez_compressed(os.path.join(HERE, "drop_in.npz"), **out)
+    print("drop-in traces written to", HERE)
+
+
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) > 2 and sys.argv[2] == "drop_in":
+        make_drop_in_traces(sys.argv[1])
+    else:
+        main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+        make_drop_in_traces(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")

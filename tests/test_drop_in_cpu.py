@@ -1,0 +1,121 @@
+"""AKVCache host logic that runs without a GPU.
+
+Ported from the reference's tests/test_bit_exact.py (HF contract when no
+token is demoted) and tests/test_cache_ordering.py (position bookkeeping
+without demotion), plus the constructor contract of drop_in.py:910-1010.
+Anything that demotes needs the CUDA kernels and lives in
+tests/test_gpu_drop_in.py.
+"""
+import pytest
+import torch
+
+transformers = pytest.importorskip("transformers")
+from transformers import DynamicCache, LlamaConfig, LlamaForCausalLM  # noqa: E402
+
+from akv import AKVCache, recommend_preset  # noqa: E402
+
+
+@pytest.fixture(scope="module")
+def tiny_llama():
+    torch.manual_seed(0)
+    cfg = LlamaConfig(vocab_size=128, hidden_size=64, intermediate_size=128, num_hidden_layers=2,
+                      num_attention_heads=4, num_key_value_heads=2, max_position_embeddings=128, rms_norm_eps=1e-5)
+    return cfg, LlamaForCausalLM(cfg).eval()
+
+
+def _generate(model, cache, ids, n=8):
+    return model.generate(ids, max_new_tokens=n, do_sample=False, past_key_values=cache, pad_token_id=0)
+
+
+def test_bit_exact_with_dynamic_cache_when_no_demotion(tiny_llama):
+    cfg, model = tiny_llama
+    ids = torch.tensor([[1, 2, 3, 4, 5, 6, 7, 8, 9, 10]])
+    with torch.no_grad():
+        ref = _generate(model, DynamicCache(), ids)
+        cache = AKVCache(warm_bits=4, hot_budget=4096, num_hidden_layers=cfg.num_hidden_layers,
+                         enable_promotion=False)
+        got = _generate(model, cache, ids)
+    assert torch.equal(ref, got), (ref.tolist(), got.tolist())
+    assert cache.get_seq_length() == ids.shape[1] + 8 - 1
+    assert len(cache) == cfg.num_hidden_layers
+
+
+def test_protected_layers_never_demote_on_cpu(tiny_llama):
+    cfg, model = tiny_llama
+    ids = torch.tensor([[1, 2, 3, 4, 5, 6, 7, 8, 9, 10]])
+    with torch.no_grad():
+        ref = _generate(model, DynamicCache(), ids)
+        cache = AKVCache(warm_bits=4, hot_budget=4, num_hidden_layers=2, protect_first=1, protect_last=1)
+        got = _generate(model, cache, ids)
+    assert torch.equal(ref, got)
+    assert all(layer._warm_keys_fp16 is None for layer in cache.layers)
+
+
+def _prefill(N, hot_budget, num_layers=1, heads=2, head_dim=8):
+    cache = AKVCache(warm_bits=3, hot_budget=hot_budget, enable_promotion=False, enable_promotion_proxy=False,
+                     num_hidden_layers=num_layers)
+    K = torch.arange(N, dtype=torch.float32).view(1, 1, N, 1).expand(1, heads, N, head_dim).contiguous().half()
+    for layer_idx in range(num_layers):
+        cache.update(K, K.clone(), layer_idx=layer_idx)
+    return cache
+
+
+def test_prefill_no_demote_keeps_positions_in_order():
+    layer = _prefill(64, 256).layers[0]
+    assert layer._warm_positions is None
+    assert layer._hot_positions.tolist() == list(range(64))
+
+
+def test_decode_step_appends_at_correct_position():
+    cache = _prefill(64, 256)
+    layer = cache.layers[0]
+    cache.update(torch.zeros(1, 2, 1, 8, dtype=torch.float16), torch.zeros(1, 2, 1, 8, dtype=torch.float16), 0)
+    assert layer._hot_positions.tolist() == list(range(65))
+    cache.update(torch.zeros(1, 2, 16, 8, dtype=torch.float16), torch.zeros(1, 2, 16, 8, dtype=torch.float16), 0)
+    assert layer._hot_positions.tolist() == list(range(81))
+
+
+def test_demotion_needs_cuda():
+    with pytest.raises(RuntimeError, match="CUDA"):
+        _prefill(64, 16, head_dim=32)
+
+
+def test_presets_and_argument_contract():
+    c = AKVCache(preset="k4v2")
+    assert (c.warm_key_bits, c.warm_value_bits, c.hot_budget) == (4, 2, 128)
+    c = AKVCache(preset="compact")
+    assert (c.warm_bits, c.warm_key_bits, c.warm_value_bits, c.hot_budget) == (2, 2, 2, 64)
+    with pytest.raises(ValueError):
+        AKVCache(preset="nope")
+    with pytest.raises(ValueError):
+        AKVCache(preset="quality", warm_bits=3)
+    with pytest.raises(ValueError):
+        AKVCache(protect_last=2)
+    with pytest.raises(ValueError):
+        AKVCache(protect_layers=[-1])
+    c = AKVCache(num_hidden_layers=10, protect_first=2, protect_last=1, protect_layers=[5, -3])
+    assert c._protected_set == {0, 1, 9, 5, 7}
+    c = AKVCache(warm_bits=2, warm_value_bits=4)
+    assert (c.warm_key_bits, c.warm_value_bits) == (2, 4)
+
+
+def test_memory_report_and_reset():
+    cache = _prefill(40, 256)
+    rep = cache.memory_report()
+    assert rep["seq_length"] == 40 and rep["num_layers"] == 1
+    mu = cache.memory_usage()
+    assert mu["hot_bytes"] == 2 * 2 * 40 * 8 * 2
+    assert mu["warm_bytes_packed"] == 0 and mu["total_bytes"] == mu["hot_bytes"]
+    k, v = cache[0]
+    assert k.shape == (1, 2, 40, 8)
+    assert len(cache.to_legacy_cache()) == 1
+    cache.reset()
+    assert len(cache) == 0 and cache.get_seq_length() == 0
+
+
+def test_for_model_and_recommend_preset(tiny_llama):
+    cfg, model = tiny_llama
+    c = AKVCache.for_model(model, preset="balanced", protect_last=1)
+    assert c.num_hidden_layers == 2 and c._protected_set == {1}
+    rec = recommend_preset(model)
+    assert rec["preset"] in ("quality", "balanced")

@@ -1,0 +1,149 @@
+"""AKVCache on CUDA against update traces recorded from the reference
+AKVCache (tests/golden/make_golden.py: make_drop_in_traces).
+
+After every update the warm and hot position sets must equal the
+reference's (tier indices bit-exact: the same CPU topk on the same recency
+scores, the same promotion by attention weights), and the final
+chronological K/V view must be bit-identical (the warm part is the exact
+dequantisation of packed records written by the sm_100a quantiser).  Also
+ports the reference's ordering tests (tests/test_cache_ordering.py) to a
+head_dim the kernels take, and runs HF generate under demotion.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda:0"
+
+
+def _traces(golden_dir):
+    return np.load(os.path.join(golden_dir, "drop_in.npz"))
+
+
+CASES = {
+    "a": dict(warm_bits=3, hot_budget=64, enable_promotion=False, enable_promotion_proxy=False),
+    "b": dict(preset="k4v2", outlier_fraction=0.01, enable_promotion=True, enable_promotion_proxy=False,
+              promotion_threshold=0.3),
+    "c": dict(warm_bits=2, hot_budget=32, adaptive_hot_frac=0.25, enable_promotion=False,
+              enable_promotion_proxy=False),
+}
+
+
+@pytest.mark.parametrize("name", ["a", "b", "c"])
+def test_update_trace_matches_reference(name, golden_dir):
+    from akv import AKVCache
+    z = _traces(golden_dir)
+    cache = AKVCache(num_hidden_layers=1, **CASES[name])
+    if name == "b":
+        cache.hot_budget = 48
+    steps = z[f"{name}/steps"]
+    k_in = torch.from_numpy(z[f"{name}/k_in"]).to(DEV)
+    v_in = torch.from_numpy(z[f"{name}/v_in"]).to(DEV)
+    wl, hl = z[f"{name}/warm_len"], z[f"{name}/hot_len"]
+    wo = np.concatenate([[0], np.cumsum(wl)])
+    ho = np.concatenate([[0], np.cumsum(hl)])
+    if f"{name}/attn" in z:
+        al = z[f"{name}/attn_len"]
+        ao = np.concatenate([[0], np.cumsum(al)])
+    t = 0
+    for i, n in enumerate(steps):
+        ck = None
+        if f"{name}/attn" in z and i > 0:
+            a = z[f"{name}/attn"][ao[i - 1]:ao[i]]
+            ck = {"attention_weights": torch.from_numpy(a).view(1, 2, 1, -1).to(DEV)}
+        full_k, full_v = cache.update(k_in[:, :, t:t + n], v_in[:, :, t:t + n], 0, ck)
+        t += n
+        layer = cache.layers[0]
+        warm = [] if layer._warm_positions is None else layer._warm_positions.tolist()
+        assert warm == z[f"{name}/warm_pos"][wo[i]:wo[i + 1]].tolist(), f"step {i}: warm positions"
+        assert layer._hot_positions.tolist() == z[f"{name}/hot_pos"][ho[i]:ho[i + 1]].tolist(), f"step {i}: hot"
+    np.testing.assert_array_equal(full_k.cpu().numpy().view(np.uint16), z[f"{name}/full_k"].view(np.uint16))
+    np.testing.assert_array_equal(full_v.cpu().numpy().view(np.uint16), z[f"{name}/full_v"].view(np.uint16))
+    mu = cache.memory_usage()
+    for key in ("hot_bytes", "warm_bytes_packed", "warm_bytes_live", "fp16_equivalent_bytes", "total_bytes"):
+        assert mu[key] == int(z[f"{name}/mem/{key}"]), key
+    # the packed records hold exactly the warm tokens (valid-slot masks)
+    masks = cache.layers[0]._warm.masks()[0, 0].tolist()
+    assert sum(bin(int(m)).count("1") for m in masks) == int(wl[-1])
+
+
+def _prefill(N, hot_budget, num_layers=1, heads=2, head_dim=32):
+    from akv import AKVCache
+    cache = AKVCache(warm_bits=3, hot_budget=hot_budget, enable_promotion=False, enable_promotion_proxy=False,
+                     num_hidden_layers=num_layers)
+    K = torch.arange(N, dtype=torch.float32).view(1, 1, N, 1).expand(1, heads, N, head_dim).contiguous().half()
+    K = K.to(DEV)
+    for layer_idx in range(num_layers):
+        cache.update(K, K.clone(), layer_idx=layer_idx)
+    return cache
+
+
+def test_prefill_with_demote_position_coverage_is_complete():
+    layer = _prefill(256, 32).layers[0]
+    warm, hot = layer._warm_positions.tolist(), layer._hot_positions.tolist()
+    assert len(warm) + len(hot) == 256 and sorted(warm + hot) == list(range(256))
+
+
+def test_full_view_is_chronologically_sorted():
+    layer = _prefill(256, 32).layers[0]
+    assert layer.keys.shape[2] == 256
+    pos = torch.cat([layer._warm_positions, layer._hot_positions])
+    assert pos[pos.argsort()].tolist() == list(range(256))
+    # warm rows are quantised, hot rows exact: each slot's value stays near its position
+    approx = layer.keys[0, 0, :, 0].float().cpu()
+    assert torch.all((approx - torch.arange(256).float()).abs() <= 256 / 7 / 2 + 1)
+
+
+def test_promote_preserves_position_coverage():
+    from akv import AKVCache
+    N = 128
+    cache = AKVCache(warm_bits=3, hot_budget=16, enable_promotion=True, enable_promotion_proxy=True,
+                     promotion_threshold=0.0, num_hidden_layers=1)
+    K = torch.arange(N, dtype=torch.float32).view(1, 1, N, 1).expand(1, 2, N, 32).contiguous().half().to(DEV)
+    cache.update(K, K.clone(), layer_idx=0)
+    g = torch.Generator(device=DEV).manual_seed(0)
+    for _ in range(8):
+        k1 = torch.randn(1, 2, 1, 32, generator=g, device=DEV).half()
+        cache.update(k1, k1.clone(), layer_idx=0)
+    layer = cache.layers[0]
+    warm = layer._warm_positions.tolist() if layer._warm_positions is not None else []
+    hot = layer._hot_positions.tolist()
+    assert sorted(warm + hot) == list(range(N + 8))
+    # promoted tokens are gone from the packed records too
+    live = sum(bin(int(m)).count("1") for m in layer._warm.masks()[0, 0].tolist())
+    assert live == len(warm)
+
+
+def test_multilayer_independence():
+    cache = _prefill(128, 32, num_layers=3)
+    for layer in cache.layers:
+        assert sorted(layer._warm_positions.tolist() + layer._hot_positions.tolist()) == list(range(128))
+
+
+def test_generate_under_demotion_and_beam_ops():
+    pytest.importorskip("transformers")
+    from transformers import LlamaConfig, LlamaForCausalLM
+    from akv import AKVCache
+    torch.manual_seed(0)
+    cfg = LlamaConfig(vocab_size=128, hidden_size=128, intermediate_size=256, num_hidden_layers=2,
+                      num_attention_heads=4, num_key_value_heads=2, max_position_embeddings=256, rms_norm_eps=1e-5)
+    model = LlamaForCausalLM(cfg).eval().half().to(DEV)
+    ids = torch.arange(1, 81, device=DEV).view(1, -1) % 127 + 1
+    with torch.no_grad():
+        cache = AKVCache(preset="k4v2", num_hidden_layers=2, outlier_fraction=0.05)
+        cache.hot_budget = 24
+        out = model.generate(ids, max_new_tokens=12, do_sample=False, past_key_values=cache, pad_token_id=0)
+    assert out.shape[1] == ids.shape[1] + 12
+    layer = cache.layers[0]
+    assert layer._warm_keys_fp16 is not None and layer._hot_keys.shape[2] == 24
+    mu = cache.memory_usage()
+    assert mu["warm_bytes_packed"] > 0 and mu["savings_ratio"] > 1.0
+    # beam-style batch ops keep every tier consistent
+    cache.batch_repeat_interleave(2)
+    assert layer._hot_keys.shape[0] == 2 and layer._warm.B == 2 and layer._warm_keys_fp16.shape[0] == 2
+    cache.batch_select_indices(torch.tensor([1], device=DEV))
+    assert layer._hot_keys.shape[0] == 1 and layer._warm.buf.shape[0] == 1
