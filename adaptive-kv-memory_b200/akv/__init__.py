@@ -8,7 +8,8 @@ the sm_100a library ``akv/_lib/libakv_sm100.so``; there is no CPU fallback.
 from . import _C
 from .affine_quantizer import AffineQuantConfig, AffineQuantizer
 from .bitpack import pack, unpack, packed_bytes
-from .fused_attention import mixed_precision_decode_attention, mixed_tier_decode_attention
+from .fused_attention import (fused_int4_decode_attention, int4_group_dequant, mixed_precision_decode_attention,
+                              mixed_tier_decode_attention)
 from .packed_layout import WarmArena, measure_packed_bytes
 from .drop_in import AKVCache, AKVLayer, recommend_preset
 
@@ -17,6 +18,7 @@ __version__ = "0.1.0"
 __all__ = [
     "AKVCache", "AKVLayer", "recommend_preset",
     "AffineQuantConfig", "AffineQuantizer", "WarmArena", "measure_packed_bytes",
-    "mixed_tier_decode_attention", "mixed_precision_decode_attention",
+    "mixed_tier_decode_attention", "mixed_precision_decode_attention", "fused_int4_decode_attention",
+    "int4_group_dequant",
     "pack", "unpack", "packed_bytes",
 ]

@@ -6,8 +6,11 @@ per sequence attends over the FP16 hot window and the packed warm tier
 (``akv_mixed_decode`` in ``libakv_sm100.so``).  The warm tier is never
 dequantised into memory.
 
-``mixed_precision_decode_attention`` keeps the reference signature
-(akv/fused_attention.py:324-366) for callers of the reference API.
+``mixed_precision_decode_attention`` and ``fused_int4_decode_attention``
+keep the reference signatures (akv/fused_attention.py:213-366) on the
+reference's INT4 per-token-group warm layout: the layout is dequantised by a
+CUDA kernel and attended by the same decode kernel, hot and warm partials
+merged by the LSE combine.
 """
 from __future__ import annotations
 
@@ -20,6 +23,16 @@ import torch
 from . import _C
 
 _workspaces: dict = {}
+KERNEL_HEAD_DIM = 128  # head dim of the decode kernel; smaller hot-only inputs are zero-padded to it
+
+
+def _pad_dim(x: torch.Tensor, d: int = KERNEL_HEAD_DIM) -> torch.Tensor:
+    """Zero-pad the last dim to d: padded channels add 0 to every q.k and give all-zero output columns."""
+    if x.shape[-1] == d:
+        return x
+    out = torch.zeros(*x.shape[:-1], d, dtype=x.dtype, device=x.device)
+    out[..., : x.shape[-1]] = x
+    return out
 
 
 def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
@@ -62,6 +75,14 @@ def mixed_tier_decode_attention(query: torch.Tensor,
     B, Hq, D = q3.shape
     if sm_scale is None:
         sm_scale = 1.0 / math.sqrt(D)
+    if D < KERNEL_HEAD_DIM and D % 8 == 0 and warm is None and partial_out is None and out is None:
+        nh = hot_keys.shape[2] if n_hot is None else int(n_hot)
+        res = mixed_tier_decode_attention(_pad_dim(q3), _pad_dim(hot_keys[:, :, :nh]), _pad_dim(hot_values[:, :, :nh]),
+                                          None, nh, sm_scale, hot_len, None, return_lse, None, status, None)
+        o, lse = res if return_lse else (res, None)
+        o = o[..., :D]
+        o = o.unsqueeze(2) if query.dim() == 4 else o
+        return (o, lse) if return_lse else o
     if hot_keys is not None:
         Hkv = hot_keys.shape[1]
         nh = hot_keys.shape[2] if n_hot is None else int(n_hot)
@@ -101,16 +122,94 @@ def mixed_tier_decode_attention(query: torch.Tensor,
     return (res, lse) if return_lse else res
 
 
+def int4_group_dequant(packed: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor, head_dim: int,
+                       group_size: int, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """The reference's ``_dequant_int4_tile`` (akv/fused_attention.py:293-317) on CUDA: (H, N, D) fp16."""
+    _C.require_cuda(packed, scales, zeros)
+    H, N, _ = packed.shape
+    if scales.dtype != torch.float16 or zeros.dtype != torch.float16:
+        raise TypeError("INT4 scales / zeros are fp16")
+    if scales.stride() != zeros.stride() or scales.stride(-1) != 1 or packed.stride(-1) != 1:
+        raise ValueError("scales and zeros need equal strides and a contiguous last dim; packed rows contiguous")
+    if out is None:
+        out = torch.empty(H, N, head_dim, dtype=torch.float16, device=packed.device)
+    rc = _C.load().akv_int4_group_dequant(packed.data_ptr(), packed.stride(0), packed.stride(1),
+                                          scales.data_ptr(), zeros.data_ptr(), scales.stride(0), scales.stride(1),
+                                          H, N, head_dim, group_size, out.data_ptr(), out.stride(0), out.stride(1),
+                                          _C.stream_of(packed))
+    _C.check(rc, "akv_int4_group_dequant")
+    return out
+
+
+def _int4_partials(query, packed_k, ks, kz, packed_v, vs, vz, group_size, sm_scale, tile_tokens, parts):
+    """Partial records of the shared INT4 warm tier, dequantised one bounded tile at a time."""
+    B, H, Dp = query.shape  # query already padded to the kernel head dim
+    D = 2 * packed_k.shape[2]
+    N = packed_k.shape[1]
+    tile = max(32, min(N, tile_tokens))
+    kbuf = torch.zeros(H, tile, Dp, dtype=torch.float16, device=query.device)
+    vbuf = torch.zeros_like(kbuf)
+    for t0 in range(0, N, tile):
+        n = min(tile, N - t0)
+        int4_group_dequant(packed_k[:, t0:t0 + n], ks[:, t0:t0 + n], kz[:, t0:t0 + n], D, group_size,
+                           out=kbuf[:, :n, :D])
+        int4_group_dequant(packed_v[:, t0:t0 + n], vs[:, t0:t0 + n], vz[:, t0:t0 + n], D, group_size,
+                           out=vbuf[:, :n, :D])
+        k, v = kbuf[:, :n], vbuf[:, :n]
+        p = torch.empty(B * H, Dp + 2, dtype=torch.float32, device=query.device)
+        # the tier is shared by every batch row: batch stride 0
+        mixed_tier_decode_attention(query, k.unsqueeze(0).expand(B, -1, -1, -1),
+                                    v.unsqueeze(0).expand(B, -1, -1, -1), n_hot=n, sm_scale=sm_scale,
+                                    partial_out=p)
+        parts.append(p)
+
+
+def _combine(parts, B, H, D, device) -> torch.Tensor:
+    part = torch.stack(parts, 1).contiguous()  # (B*H, splits, D+2)
+    out = torch.empty(B, H, D, dtype=torch.float16, device=device)
+    rc = _C.load().akv_lse_combine(part.data_ptr(), D + 2, part.stride(0), B * H, part.shape[1], D,
+                                   out.data_ptr(), D, None, None, _C.stream_of(part))
+    _C.check(rc, "akv_lse_combine")
+    return out
+
+
+def fused_int4_decode_attention(query: torch.Tensor, k_packed: torch.Tensor, k_scales: torch.Tensor,
+                                k_zeros: torch.Tensor, v_packed: torch.Tensor, v_scales: torch.Tensor,
+                                v_zeros: torch.Tensor, group_size: int = 128,
+                                memory_limit_mb: float = 512.0) -> torch.Tensor:
+    """Reference signature (akv/fused_attention.py:213-290): attention of (B, H, 1, D) queries over one
+    INT4 tier (H, N, D/2) shared by the batch.  The tier is dequantised by the CUDA kernel in tiles of at
+    most ``memory_limit_mb`` (K + V fp16), each tile runs through the split-K decode kernel, and the
+    tiles' partials are merged by the LSE combine.  Returns (B, H, 1, D) fp16."""
+    _C.require_cuda(query, k_packed, v_packed)
+    B, H, _, D = query.shape
+    q = _pad_dim(query.reshape(B, H, D))
+    tile = int(memory_limit_mb * 1e6 // (2 * H * D * 2))
+    parts: list = []
+    _int4_partials(q, k_packed, k_scales, k_zeros, v_packed, v_scales, v_zeros, group_size,
+                   1.0 / math.sqrt(D), tile, parts)
+    return _combine(parts, B, H, q.shape[-1], q.device)[..., :D].unsqueeze(2)
+
+
 def mixed_precision_decode_attention(query, hot_keys, hot_values,
                                      warm_k_packed=None, warm_k_scales=None, warm_k_zeros=None,
                                      warm_v_packed=None, warm_v_scales=None, warm_v_zeros=None,
                                      group_size: int = 128):
-    """Reference-signature entry (akv/fused_attention.py:324-366).
-
-    The hot-only form (no warm tier) runs through ``akv_mixed_decode``.  The
-    reference's INT4 per-token-group warm layout is a different quantiser
-    from the affine warm tier and is not supported by this build.
-    """
-    if warm_k_packed is not None and warm_k_packed.shape[1] > 0:
-        raise NotImplementedError("INT4 per-token-group warm layout: use WarmArena + mixed_tier_decode_attention")
-    return mixed_tier_decode_attention(query, hot_keys, hot_values)
+    """Reference signature (akv/fused_attention.py:324-366): (B, H, 1, D) queries over the per-row FP16
+    hot tier (B, H, N_hot, D) plus an optional INT4 warm tier (H, N_warm, D/2) shared by the batch.
+    Hot and warm each give a split-K partial record; the LSE combine merges them.  Returns (B, H, 1, D)."""
+    if warm_k_packed is None or warm_k_packed.shape[1] == 0:
+        return mixed_tier_decode_attention(query, hot_keys, hot_values)
+    _C.require_cuda(query, hot_keys, hot_values, warm_k_packed)
+    B, H, _, D = query.shape
+    q = _pad_dim(query.reshape(B, H, D))
+    Dp = q.shape[-1]
+    sm_scale = 1.0 / math.sqrt(D)
+    parts: list = []
+    if hot_keys is not None and hot_keys.shape[2] > 0:
+        p = torch.empty(B * H, Dp + 2, dtype=torch.float32, device=q.device)
+        mixed_tier_decode_attention(q, _pad_dim(hot_keys), _pad_dim(hot_values), sm_scale=sm_scale, partial_out=p)
+        parts.append(p)
+    _int4_partials(q, warm_k_packed, warm_k_scales, warm_k_zeros, warm_v_packed, warm_v_scales, warm_v_zeros,
+                   group_size, sm_scale, warm_k_packed.shape[1], parts)
+    return _combine(parts, B, H, Dp, q.device)[..., :D].unsqueeze(2)

@@ -156,6 +156,21 @@ int akv_dequantize(const akv_qdest* src, const int64_t* tok_idx, int64_t tok_sb,
                    uint16_t* out, int64_t out_sb, int64_t out_sh, int64_t out_sn, void* stream);
 
 /* ------------------------------------------------------------------------
+ * Dequantise the reference's INT4 per-token, per-D-group layout
+ * (akv/fused_attention.py:293-317, the warm operands of
+ * fused_int4_decode_attention :213-290 and mixed_precision_decode_attention
+ * :324-366): packed (h, n) row of D/2 bytes at packed + h*p_sh + n*p_sn,
+ * even channel in the high nibble; fp16 scale / zero of group g at
+ * scales + h*s_sh + n*s_sn + g (element strides; zeros alike);
+ * out = fp16(fp32(fp32(code*scale) + zero)) at out + h*o_sh + n*o_sn + d.
+ * D % 8 == 0; group g = d / group_size.
+ * ---------------------------------------------------------------------- */
+int akv_int4_group_dequant(const uint8_t* packed, int64_t p_sh, int64_t p_sn,
+                           const uint16_t* scales, const uint16_t* zeros, int64_t s_sh, int64_t s_sn,
+                           int H, int N, int D, int group_size,
+                           uint16_t* out, int64_t o_sh, int64_t o_sn, void* stream);
+
+/* ------------------------------------------------------------------------
  * A5: mixed-tier decode attention (one query token per sequence).
  * Replaces the reference's decode paths that attend over [warm; hot]:
  * fused_attention.mixed_precision_decode_attention (akv/fused_attention.py:324-366),

@@ -189,3 +189,28 @@ def test_affine_gqa_golden(golden_dir):
                                           torch.from_numpy(z[f"{t}/hv"]).to(DEV), arena)
     ref = z[f"{t}/out"].astype(np.float32)
     assert (np.abs(_np(out).astype(np.float32) - ref) <= tolerance(ref)).all()
+
+
+@pytest.mark.parametrize("gs", [32, 128])
+def test_reference_int4_layout_golden(golden_dir, gs):
+    """The reference's INT4 per-token-group warm layout: dequant bit-exact, the
+    fused / mixed entry points within tolerance of the reference outputs."""
+    import os
+    import akv
+    z = np.load(os.path.join(golden_dir, "attention.npz"))
+    t = f"int4_gs{gs}"
+    T = {k: torch.from_numpy(z[f"{t}/{k}"]).to(DEV) for k in ("q", "hk", "hv", "wkp", "wks", "wkz",
+                                                               "wvp", "wvs", "wvz")}
+    D = T["q"].shape[-1]
+    dk = akv.int4_group_dequant(T["wkp"], T["wks"], T["wkz"], D, gs)
+    np.testing.assert_array_equal(_np(dk).view(np.uint16), z[f"{t}/deq_k"].view(np.uint16))
+    warm = (T["wkp"], T["wks"], T["wkz"], T["wvp"], T["wvs"], T["wvz"])
+    mixed = akv.mixed_precision_decode_attention(T["q"], T["hk"], T["hv"], *warm, group_size=gs)
+    ref = z[f"{t}/mixed"].astype(np.float32)
+    assert mixed.shape == T["q"].shape
+    assert (np.abs(_np(mixed).astype(np.float32) - ref) <= tolerance(ref)).all()
+    for tag, limit in (("int4", 512.0), ("int4_tiled", 1e-3)):  # one tile / many tiles
+        out = akv.fused_int4_decode_attention(T["q"], *warm, group_size=gs, memory_limit_mb=limit)
+        ref = z[f"{t}/{tag}"].astype(np.float32)
+        err = np.abs(_np(out).astype(np.float32) - ref)
+        assert (err <= tolerance(ref)).all(), (tag, err.max())
