@@ -53,6 +53,12 @@ SIGNATURES = {
     "akv_quantize_ws": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64,
                                 c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                                 POINTER(QDest), c_void_p, c_size_t, c_void_p, c_void_p]),
+    "akv_outlier_norm_sums_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
+    "akv_outlier_norm_sums": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64,
+                                      c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "akv_quantize_ext": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64,
+                                 c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
+                                 POINTER(QDest), c_void_p, c_int, c_void_p, c_size_t, c_void_p, c_void_p]),
     "akv_dequantize": (c_int, [POINTER(QDest), c_void_p, c_int64, c_int, c_int, c_int, c_int, c_int, c_int,
                                c_int, c_void_p, c_int64, c_int64, c_int64, c_void_p]),
     "akv_int4_group_dequant": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int64,
@@ -140,13 +146,35 @@ def warm_layout(head_dim: int, key_bits: int, value_bits: int, n_outlier: int) -
 
 
 def quantize(x_ptr: int, sb: int, sh: int, sn: int, tok_ptr, tok_sb: int, B: int, H: int, N: int, D: int,
-             bits: int, is_key: bool, group: int, n_out: int, dest: QDest, status_ptr, device) -> None:
-    """akv_quantize_ws with a workspace from torch's allocator when the shape needs one."""
+             bits: int, is_key: bool, group: int, n_out: int, dest: QDest, status_ptr, device,
+             score_sum=None, score_heads: int = 0) -> None:
+    """akv_quantize_ext with a workspace from torch's allocator when the shape needs one
+    (``score_sum``: all-reduced outlier norm sums when heads are sharded over GPUs)."""
     import torch
     lib = load()
     need = lib.akv_quantize_workspace_bytes(B, H, N, D, group, n_out, int(is_key))
     ws = torch.empty(need + 256, dtype=torch.uint8, device=device) if need else None
     wp = None if ws is None else (ws.data_ptr() + 255) // 256 * 256
-    rc = lib.akv_quantize_ws(x_ptr, sb, sh, sn, tok_ptr, tok_sb, B, H, N, D, bits, int(is_key), group, n_out,
-                             ctypes.byref(dest), wp, need, status_ptr, torch.cuda.current_stream(device).cuda_stream)
+    rc = lib.akv_quantize_ext(x_ptr, sb, sh, sn, tok_ptr, tok_sb, B, H, N, D, bits, int(is_key), group, n_out,
+                              ctypes.byref(dest), None if score_sum is None else score_sum.data_ptr(), score_heads,
+                              wp, need, status_ptr, torch.cuda.current_stream(device).cuda_stream)
     check(rc, "akv_quantize")
+
+
+def outlier_norm_sums(x, tok_idx, N: int, group: int):
+    """(B, n_groups, D) fp32: per scale group, the sum over x's heads of the per-(head, channel) L2 norms."""
+    import torch
+    lib = load()
+    B, H, _, D = x.shape
+    n_groups = (N + group - 1) // group
+    out = torch.empty(B, n_groups, D, dtype=torch.float32, device=x.device)
+    need = lib.akv_outlier_norm_sums_workspace_bytes(B, H, N, D, group)
+    ws = torch.empty(need + 256, dtype=torch.uint8, device=x.device)
+    wp = (ws.data_ptr() + 255) // 256 * 256
+    ti = None if tok_idx is None else tok_idx.contiguous()
+    rc = lib.akv_outlier_norm_sums(x.data_ptr(), x.stride(0), x.stride(1), x.stride(2),
+                                   None if ti is None else ti.data_ptr(), 0 if ti is None or ti.dim() == 1 else ti.stride(0),
+                                   B, H, N, D, group, out.data_ptr(), wp, need,
+                                   torch.cuda.current_stream(x.device).cuda_stream)
+    check(rc, "akv_outlier_norm_sums")
+    return out

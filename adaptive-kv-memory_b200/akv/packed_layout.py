@@ -106,11 +106,14 @@ class WarmArena:
 
     # -------------------------------------------------------------- writes
     def append(self, k: torch.Tensor, v: torch.Tensor, group: int = BLOCK, tok_idx: torch.Tensor | None = None,
-               status: torch.Tensor | None = None) -> int:
+               status: torch.Tensor | None = None, score_sums: tuple | None = None, score_heads: int = 0) -> int:
         """Quantise (B, H, N, D) fp16 K/V (optionally gathered by ``tok_idx``) into new blocks.
 
         ``group`` tokens share one K scale (32 = one block; N = one reference
-        call over the whole event).  Returns the first block index written.
+        call over the whole event).  ``score_sums`` = (K, V) all-reduced
+        outlier norm sums (B, n_groups, D) when the heads are sharded over
+        GPUs (``akv.parallel``), over ``score_heads`` heads in total.
+        Returns the first block index written.
         """
         _C.require_cuda(k, v)
         B, H, N, D = (k.shape if tok_idx is None else (k.shape[0], k.shape[1], tok_idx.shape[-1], k.shape[3]))
@@ -123,13 +126,15 @@ class WarmArena:
         ti = None if tok_idx is None else tok_idx.contiguous()
         tsb = 0 if ti is None or ti.dim() == 1 else ti.stride(0)
         sp = None if status is None else status.data_ptr()
-        for x, is_key, bits in ((k, True, self.key_bits), (v, False, self.value_bits)):
+        for i, (x, is_key, bits) in enumerate(((k, True, self.key_bits), (v, False, self.value_bits))):
             if x.stride(-1) != 1:
                 x = x.contiguous()
             dest = self.dest(is_key, blk0)
+            ss = None if score_sums is None else score_sums[i].contiguous()
             _C.quantize(x.data_ptr(), x.stride(0), x.stride(1), x.stride(2),
                         None if ti is None else ti.data_ptr(), tsb,
-                        B, H, N, D, bits, is_key, min(group, N), self.n_out, dest, sp, x.device)
+                        B, H, N, D, bits, is_key, min(group, N), self.n_out, dest, sp, x.device,
+                        score_sum=ss, score_heads=score_heads)
         self.n_blocks += nblk
         return blk0
 

@@ -1,0 +1,150 @@
+"""Multi-GPU partitioning of the warm-tier hot path.
+
+One process per GPU with ``torch.distributed`` (NCCL); three partitions:
+
+* ``batch``    batch rows split over the GPUs.  Every GPU holds all KV heads
+               of its rows, so quantisation (outlier selection averages over
+               all heads) and attention are local: no collective at all.
+* ``head``     KV heads (and their query heads) split over the GPUs.
+               Attention is local.  The one exchange step is the outlier
+               score of quantisation: the reference picks outlier channels by
+               the mean over ALL heads of the per-(head, channel) L2 norms
+               (affine_quantizer.py:79 / :146), so each GPU computes its
+               heads' norm sums per (batch row, scale group) with the CUDA
+               kernel and an all-reduce (SUM) of those D floats per group
+               precedes the quantiser (``quantize_head_sharded``).
+* ``sequence`` the warm blocks of one sequence split contiguously over the
+               GPUs (batch 1 at very long context).  Each GPU's decode writes
+               the split-K partial record (acc, m, l) of its tokens; an
+               all-gather over NVLink and the same LSE combine kernel that
+               merges intra-GPU splits give the output on every GPU
+               (``sequence_split_decode``).
+
+The compute steps are CUDA kernels; the orchestration functions take them as
+arguments (defaulting to the kernels) so the collective pattern can also be
+driven by CPU ``gloo`` ranks in tests.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable, Optional
+
+import torch
+
+from . import _C
+
+
+@dataclass(frozen=True)
+class ShardPlan:
+    mode: str   # "single" | "batch" | "head" | "sequence"
+    world: int
+    rank: int
+
+    def span(self, n: int) -> tuple:
+        """This rank's contiguous [lo, hi) share of n items (the first n % world ranks get one more)."""
+        base, extra = divmod(n, self.world)
+        lo = self.rank * base + min(self.rank, extra)
+        return lo, lo + base + (1 if self.rank < extra else 0)
+
+
+def plan(batch: int, kv_heads: int, world: int, rank: int, prefer: str = "batch") -> ShardPlan:
+    """Batch rows when they divide evenly (no collective), else KV heads, else the sequence."""
+    if world == 1:
+        return ShardPlan("single", 1, 0)
+    order = ("batch", "head") if prefer == "batch" else ("head", "batch")
+    for mode in order:
+        if mode == "batch" and batch % world == 0:
+            return ShardPlan("batch", world, rank)
+        if mode == "head" and kv_heads % world == 0:
+            return ShardPlan("head", world, rank)
+    return ShardPlan("sequence", world, rank)
+
+
+def _all_reduce_sum(t: torch.Tensor, group=None) -> torch.Tensor:
+    import torch.distributed as dist
+    dist.all_reduce(t, op=dist.ReduceOp.SUM, group=group)
+    return t
+
+
+def quantize_head_sharded(arena, k: torch.Tensor, v: torch.Tensor, total_heads: int, group: int = 32,
+                          tok_idx: Optional[torch.Tensor] = None, status: Optional[torch.Tensor] = None,
+                          process_group=None, norm_sums: Optional[Callable] = None,
+                          all_reduce: Optional[Callable] = None) -> int:
+    """Append this GPU's heads of (B, H_local, N, D) K/V to its arena with outlier
+    channels chosen over all ``total_heads`` heads (reference semantics).
+
+    Without outlier channels nothing crosses GPUs.  Returns the first block written."""
+    if arena.n_out == 0:
+        return arena.append(k, v, group=group, tok_idx=tok_idx, status=status)
+    N = k.shape[2] if tok_idx is None else tok_idx.shape[-1]
+    g = min(group, N)
+    norm_sums = norm_sums or (lambda x: _C.outlier_norm_sums(x, tok_idx, N, g))
+    all_reduce = all_reduce or (lambda t: _all_reduce_sum(t, process_group))
+    sums = []
+    for x in (k, v):  # same order on every rank
+        s = norm_sums(x)
+        all_reduce(s)
+        sums.append(s)
+    return arena.append(k, v, group=group, tok_idx=tok_idx, status=status, score_sums=tuple(sums),
+                        score_heads=total_heads)
+
+
+def _empty_partial(rows: int, D: int, device) -> torch.Tensor:
+    p = torch.zeros(rows, D + 2, dtype=torch.float32, device=device)
+    p[:, D] = float("-inf")
+    return p
+
+
+def local_partial(query: torch.Tensor, hot_keys: Optional[torch.Tensor], hot_values: Optional[torch.Tensor],
+                  warm, sm_scale: Optional[float] = None) -> torch.Tensor:
+    """(B*Hq, D+2) partial record of this GPU's tokens (the decode kernel's ``partial_out``)."""
+    from .fused_attention import mixed_tier_decode_attention
+    q3 = query.reshape(query.shape[0], query.shape[1], query.shape[-1])
+    B, Hq, D = q3.shape
+    has_hot = hot_keys is not None and hot_keys.shape[2] > 0
+    has_warm = warm is not None and warm.n_blocks > 0
+    if not has_hot and not has_warm:
+        return _empty_partial(B * Hq, D, q3.device)
+    p = torch.empty(B * Hq, D + 2, dtype=torch.float32, device=q3.device)
+    mixed_tier_decode_attention(q3, hot_keys if has_hot else None, hot_values if has_hot else None,
+                                warm if has_warm else None, sm_scale=sm_scale, partial_out=p)
+    return p
+
+
+def combine_partials(part: torch.Tensor) -> torch.Tensor:
+    """(rows, splits, D+2) partial records -> (rows, D) fp16 via the LSE combine kernel."""
+    _C.require_cuda(part)
+    part = part.contiguous()
+    rows, splits, D2 = part.shape
+    D = D2 - 2
+    out = torch.empty(rows, D, dtype=torch.float16, device=part.device)
+    _C.check(_C.load().akv_lse_combine(part.data_ptr(), D2, part.stride(0), rows, splits, D, out.data_ptr(), D,
+                                       None, None, _C.stream_of(part)), "akv_lse_combine")
+    return out
+
+
+def _all_gather(t: torch.Tensor, world: int, group=None) -> torch.Tensor:
+    import torch.distributed as dist
+    outs = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(outs, t.contiguous(), group=group)
+    return torch.stack(outs)
+
+
+def sequence_split_decode(query: torch.Tensor, hot_keys: Optional[torch.Tensor],
+                          hot_values: Optional[torch.Tensor], warm, world: int,
+                          sm_scale: Optional[float] = None, process_group=None,
+                          partial: Optional[Callable] = None, all_gather: Optional[Callable] = None,
+                          combine: Optional[Callable] = None) -> torch.Tensor:
+    """Decode attention of one sequence whose tokens are spread over ``world`` GPUs.
+
+    Each GPU passes the tokens it holds (its contiguous share of warm blocks,
+    and the hot window on whichever GPU keeps it; others pass None).  Returns
+    (B, Hq, D) fp16 on every GPU."""
+    partial = partial or local_partial
+    all_gather = all_gather or (lambda t: _all_gather(t, world, process_group))
+    combine = combine or combine_partials
+    p = partial(query, hot_keys, hot_values, warm, sm_scale)
+    gathered = all_gather(p)                       # (world, rows, D+2)
+    part = gathered.permute(1, 0, 2).contiguous()  # (rows, world, D+2)
+    q3 = query.reshape(query.shape[0], query.shape[1], query.shape[-1])
+    return combine(part).reshape(q3.shape)

@@ -46,6 +46,12 @@ struct QuantParams {
   __half* ws_zero;   // [B][n_groups][H][D]   keys: zero (min), outlier channels 0
   __half* ws_scale;  // [B][n_groups][H][D]   keys: scale
   int* ws_oidx;      // [B][n_groups][kMaxOutliersWs]
+  // outlier scores from outside (heads sharded over GPUs): per (b, group) the
+  // sum over ALL heads of the per-(head, channel) L2 norms, [B][n_groups][D];
+  // score = score_sum / score_heads.  NULL: computed from this call's heads.
+  const float* score_sum;
+  int score_heads;
+  float* norm_sums_out;  // akv_outlier_norm_sums: write [B][n_groups][D] sums over this call's heads
 };
 
 constexpr int kMaxOutliersWs = 32;
@@ -343,7 +349,8 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
   //      and, for keys, the per-(head, channel) min/max.  A work item is 8
   //      channels of one head; two neighbouring lanes split its tokens.
   const int ncs = D / kEncChunk;
-  if (MODE == kQuantStats || (MODE == kQuantFull && (p.n_out > 0 || IS_KEY))) {
+  const bool want_norms = p.n_out > 0 && !p.score_sum;  // this CTA computes outlier norms
+  if (MODE == kQuantStats || (MODE == kQuantFull && (want_norms || IS_KEY))) {
     const int items = H * ncs * 2;
     for (int w0 = 0; w0 < items; w0 += kQuantThreads) {
       const int w = w0 + tid;
@@ -367,7 +374,7 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const __half2 x = u32_as_h2(x4[i]);
-          if (p.n_out > 0) {
+          if (want_norms) {
             const float2 f = __half22float2(x);
             const uint64_t f2 = f2_make(f.x, f.y);
             s2[i] = f2_fma(f2, f2, s2[i]);
@@ -379,7 +386,7 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
         }
       }
       float s[8];
-      if (p.n_out > 0) {
+      if (want_norms) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const float2 f = f2_split(s2[i]);
@@ -396,7 +403,7 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
       }
       if (MODE == kQuantStats && half == 0) {  // this chunk's partials
         const size_t o = ((static_cast<size_t>(b) * p.n_chunks + chunk) * p.H + h0 + h) * D + c8 * kEncChunk;
-        if (p.n_out > 0) {
+        if (want_norms) {
 #pragma unroll
           for (int i = 0; i < 8; ++i) p.ws_sq[o + i] = s[i];
         }
@@ -409,7 +416,7 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
       }
       if (MODE == kQuantFull && half == 0) {
         const int c0 = h * D + c8 * kEncChunk;
-        if (p.n_out > 0) {
+        if (want_norms) {
 #pragma unroll
           for (int i = 0; i < 8; ++i) norms[c0 + i] = sqrtf(s[i]);
         }
@@ -433,9 +440,13 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
   }
   if (MODE == kQuantFull && p.n_out > 0) {
     for (int d = tid; d < D; d += kQuantThreads) {
-      float s = 0.f;
-      for (int h = 0; h < H; ++h) s += norms[h * D + d];
-      score[d] = s / static_cast<float>(H);
+      if (p.score_sum) {
+        score[d] = p.score_sum[(static_cast<size_t>(b) * p.n_groups + grp) * D + d] / static_cast<float>(p.score_heads);
+      } else {
+        float s = 0.f;
+        for (int h = 0; h < H; ++h) s += norms[h * D + d];
+        score[d] = s / static_cast<float>(H);
+      }
     }
     __syncthreads();
     if (tid < 32) {  // warp 0: top-n, largest first, lower index on ties
@@ -690,18 +701,27 @@ __global__ void __launch_bounds__(kQuantThreads) quant_reduce_kernel(const Quant
   __shared__ int oidx[kMaxOutliersWs];
   const size_t rowb = static_cast<size_t>(b) * p.n_chunks;
 
-  if (p.n_out > 0) {
-    for (int w = tid; w < H * D; w += kQuantThreads) {
-      float sq = 0.f;
-      for (int c = c0; c < c1; ++c) sq += p.ws_sq[((rowb + c) * H) * D + w];
-      norms[w] = sqrtf(sq);
+  if (p.n_out > 0 || p.norm_sums_out) {
+    if (!p.score_sum) {
+      for (int w = tid; w < H * D; w += kQuantThreads) {
+        float sq = 0.f;
+        for (int c = c0; c < c1; ++c) sq += p.ws_sq[((rowb + c) * H) * D + w];
+        norms[w] = sqrtf(sq);
+      }
+      __syncthreads();
     }
-    __syncthreads();
     for (int d = tid; d < D; d += kQuantThreads) {
-      float s = 0.f;
-      for (int h = 0; h < H; ++h) s += norms[h * D + d];
-      score[d] = s / static_cast<float>(H);
+      const size_t o = (static_cast<size_t>(b) * p.n_groups + g) * D + d;
+      if (p.score_sum) {
+        score[d] = p.score_sum[o] / static_cast<float>(p.score_heads);
+      } else {
+        float s = 0.f;
+        for (int h = 0; h < H; ++h) s += norms[h * D + d];
+        if (p.norm_sums_out) p.norm_sums_out[o] = s;
+        score[d] = s / static_cast<float>(H);
+      }
     }
+    if (p.norm_sums_out) return;
     __syncthreads();
     if (tid < 32) {
       for (int j = 0; j < p.n_out; ++j) {
@@ -928,11 +948,12 @@ struct QuantPlan {
 
 static size_t up256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
-static QuantPlan plan_quant(int B, int H, int N, int D, int group, int n_out, bool is_key) {
+static QuantPlan plan_quant(int B, int H, int N, int D, int group, int n_out, bool is_key,
+                            bool force_chunked = false) {
   QuantPlan pl{};
   pl.n_groups = (N + group - 1) / group;
   pl.smem = quant_smem_bytes(H, std::min(group, N), D, n_out, is_key);
-  if (pl.smem <= kQuantSmemLimit) return pl;
+  if (pl.smem <= kQuantSmemLimit && !force_chunked) return pl;
   pl.chunked = true;
   pl.n_chunks = (N + kBlockTokens - 1) / kBlockTokens;
   int hs = H;
@@ -961,6 +982,7 @@ static bool set_smem(K kern, size_t smem) {
 
 template <int BITS, bool IS_KEY>
 static int launch_quant(QuantParams p, const QuantPlan& pl, void* ws, cudaStream_t st) {
+  p.n_groups = pl.n_groups;
   if (!pl.chunked) {
     auto kern = quantize_group_kernel<BITS, IS_KEY, kQuantFull>;
     if (!set_smem(kern, pl.smem)) return AKV_ERR_LAUNCH;
@@ -978,11 +1000,15 @@ static int launch_quant(QuantParams p, const QuantPlan& pl, void* ws, cudaStream
   p.ws_scale = reinterpret_cast<__half*>(w + pl.off_scale);
   p.ws_oidx = reinterpret_cast<int*>(w + pl.off_oidx);
   const dim3 grid(pl.n_chunks, p.B, (p.H + pl.heads_per_cta - 1) / pl.heads_per_cta);
-  if (IS_KEY || p.n_out > 0) {
+  if (IS_KEY || (p.n_out > 0 && !p.score_sum)) {
     auto stats = quantize_group_kernel<BITS, IS_KEY, kQuantStats>;
     auto reduce = quant_reduce_kernel<BITS, IS_KEY>;
     if (!set_smem(stats, pl.smem) || !set_smem(reduce, pl.reduce_smem)) return AKV_ERR_LAUNCH;
     stats<<<grid, kQuantThreads, pl.smem, st>>>(p);
+    reduce<<<dim3(pl.n_groups, p.B), kQuantThreads, pl.reduce_smem, st>>>(p);
+  } else if (p.n_out > 0) {  // external scores: the reduction only picks the outlier channels
+    auto reduce = quant_reduce_kernel<BITS, IS_KEY>;
+    if (!set_smem(reduce, pl.reduce_smem)) return AKV_ERR_LAUNCH;
     reduce<<<dim3(pl.n_groups, p.B), kQuantThreads, pl.reduce_smem, st>>>(p);
   }
   auto enc = quantize_group_kernel<BITS, IS_KEY, kQuantEncode>;
@@ -1024,7 +1050,17 @@ extern "C" int akv_quantize_ws(const uint16_t* src, int64_t src_sb, int64_t src_
                                const int64_t* tok_idx, int64_t tok_sb, int B, int H, int N, int D, int bits,
                                int is_key, int group, int n_outlier, const akv_qdest* dst, void* workspace,
                                size_t workspace_bytes, int* status, void* stream) {
+  return akv_quantize_ext(src, src_sb, src_sh, src_sn, tok_idx, tok_sb, B, H, N, D, bits, is_key, group,
+                          n_outlier, dst, nullptr, 0, workspace, workspace_bytes, status, stream);
+}
+
+extern "C" int akv_quantize_ext(const uint16_t* src, int64_t src_sb, int64_t src_sh, int64_t src_sn,
+                                const int64_t* tok_idx, int64_t tok_sb, int B, int H, int N, int D, int bits,
+                                int is_key, int group, int n_outlier, const akv_qdest* dst,
+                                const float* score_sum, int score_heads, void* workspace, size_t workspace_bytes,
+                                int* status, void* stream) {
   if (!src || !dst) return AKV_ERR_NULL;
+  if (score_sum && score_heads <= 0) return AKV_ERR_SHAPE;
   if (bits < 2 || bits > 4) return AKV_ERR_BITS;
   if (B <= 0 || H <= 0 || N <= 0 || D <= 0 || D % 32 != 0 || D > 256) return AKV_ERR_SHAPE;
   if (group <= 0) group = N;
@@ -1063,6 +1099,8 @@ extern "C" int akv_quantize_ws(const uint16_t* src, int64_t src_sb, int64_t src_
   p.n_out = n_outlier;
   p.dst = *dst;
   p.status = status;
+  p.score_sum = score_sum;
+  p.score_heads = score_heads;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   switch (bits * 2 + (is_key ? 1 : 0)) {
     case 5: return launch_quant<2, true>(p, pl, workspace, st);
@@ -1139,5 +1177,61 @@ extern "C" int akv_int4_group_dequant(const uint8_t* packed, int64_t p_sh, int64
   int4_group_dequant_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       packed, p_sh, p_sn, reinterpret_cast<const __half*>(scales), reinterpret_cast<const __half*>(zeros), s_sh,
       s_sn, H, N, D, group_size, reinterpret_cast<__half*>(out), o_sh, o_sn);
+  return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_LAUNCH;
+}
+
+// Sum over this call's heads of the per-(head, channel) L2 norms over each
+// scale group's tokens: the partial outlier score of heads held by one GPU,
+// all-reduced over the GPUs before akv_quantize_ext (the reference scores
+// channels by the mean over all heads, affine_quantizer.py:79 / :146).
+// Always the chunked statistics path; workspace from
+// akv_outlier_norm_sums_workspace_bytes.
+static QuantPlan plan_norms(int B, int H, int N, int D, int group) {
+  return plan_quant(B, H, N, D, group, 1, false, true);
+}
+
+extern "C" size_t akv_outlier_norm_sums_workspace_bytes(int B, int H, int N, int D, int group) {
+  if (B <= 0 || H <= 0 || N <= 0 || D <= 0 || D % 32 != 0 || D > 256) return 0;
+  if (group <= 0 || group > N) group = N;
+  return plan_norms(B, H, N, D, group).ws_bytes;
+}
+
+extern "C" int akv_outlier_norm_sums(const uint16_t* src, int64_t src_sb, int64_t src_sh, int64_t src_sn,
+                                     const int64_t* tok_idx, int64_t tok_sb, int B, int H, int N, int D, int group,
+                                     float* out, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!src || !out) return AKV_ERR_NULL;
+  if (B <= 0 || H <= 0 || N <= 0 || D <= 0 || D % 32 != 0 || D > 256) return AKV_ERR_SHAPE;
+  if (group <= 0 || group > N) group = N;
+  if (N > group && group % kBlockTokens != 0) return AKV_ERR_SHAPE;
+  if (!aligned(src, 16) || src_sb % 8 || src_sh % 8 || src_sn % 8) return AKV_ERR_ALIGN;
+  const QuantPlan pl = plan_norms(B, H, N, D, group);
+  if (pl.smem > kQuantSmemLimit) return AKV_ERR_UNSUPPORTED;
+  if (!workspace || workspace_bytes < pl.ws_bytes || !aligned(workspace, 256)) return AKV_ERR_WORKSPACE;
+  QuantParams p{};
+  p.src = reinterpret_cast<const __half*>(src);
+  p.sb = src_sb;
+  p.sh = src_sh;
+  p.sn = src_sn;
+  p.tok_idx = tok_idx;
+  p.tok_sb = tok_sb;
+  p.B = B;
+  p.H = H;
+  p.N = N;
+  p.D = D;
+  p.bits = 4;
+  p.group = group;
+  p.n_out = 1;
+  p.n_chunks = pl.n_chunks;
+  p.n_groups = pl.n_groups;
+  p.heads_per_cta = pl.heads_per_cta;
+  char* w = static_cast<char*>(workspace);
+  p.ws_sq = reinterpret_cast<float*>(w + pl.off_sq);
+  p.norm_sums_out = out;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto stats = quantize_group_kernel<4, false, kQuantStats>;
+  auto reduce = quant_reduce_kernel<4, false>;
+  if (!set_smem(stats, pl.smem) || !set_smem(reduce, pl.reduce_smem)) return AKV_ERR_LAUNCH;
+  stats<<<dim3(pl.n_chunks, B, (H + pl.heads_per_cta - 1) / pl.heads_per_cta), kQuantThreads, pl.smem, st>>>(p);
+  reduce<<<dim3(pl.n_groups, B), kQuantThreads, pl.reduce_smem, st>>>(p);
   return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_LAUNCH;
 }

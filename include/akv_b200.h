@@ -142,6 +142,26 @@ int akv_quantize_ws(const uint16_t* src, int64_t src_sb, int64_t src_sh, int64_t
                     int B, int H, int N, int D, int bits, int is_key, int group, int n_outlier,
                     const akv_qdest* dst, void* workspace, size_t workspace_bytes, int* status, void* stream);
 
+/* Heads sharded over GPUs: the reference picks outlier channels by the mean
+ * over ALL heads of the per-(head, channel) L2 norms (affine_quantizer.py:79,
+ * :146).  akv_outlier_norm_sums writes, per (b, group), this call's heads'
+ * sum of those norms ([B][n_groups][D] fp32, n_groups = ceil(N/group)); the
+ * caller all-reduces it over the GPUs and passes it to akv_quantize_ext with
+ * score_heads = total heads.  Workspace from
+ * akv_outlier_norm_sums_workspace_bytes (256-byte aligned). */
+size_t akv_outlier_norm_sums_workspace_bytes(int B, int H, int N, int D, int group);
+int akv_outlier_norm_sums(const uint16_t* src, int64_t src_sb, int64_t src_sh, int64_t src_sn,
+                          const int64_t* tok_idx, int64_t tok_sb, int B, int H, int N, int D, int group,
+                          float* out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* akv_quantize_ws with outlier scores from outside: score_sum [B][n_groups][D]
+ * (NULL = from this call's heads), score = score_sum / score_heads. */
+int akv_quantize_ext(const uint16_t* src, int64_t src_sb, int64_t src_sh, int64_t src_sn,
+                     const int64_t* tok_idx, int64_t tok_sb,
+                     int B, int H, int N, int D, int bits, int is_key, int group, int n_outlier,
+                     const akv_qdest* dst, const float* score_sum, int score_heads,
+                     void* workspace, size_t workspace_bytes, int* status, void* stream);
+
 /* ------------------------------------------------------------------------
  * A4: unpack + dequantise to fp16.
  * Replaces AffineQuantizer.dequantize_keys/values (akv/affine_quantizer.py:112-124,

@@ -141,7 +141,18 @@ def packed_width(dim: int, bits: int) -> int:
 # Block-affine quantiser — reference akv/affine_quantizer.py
 # ---------------------------------------------------------------------------
 
-def _outlier_select(x16: np.ndarray, fraction: float):
+def outlier_norm_sum(x16: np.ndarray) -> np.ndarray:
+    """Sum over heads of the per-(head, channel) fp32 L2 norms over tokens: (D,).
+
+    The reference's channel score is this sum divided by the head count
+    (affine_quantizer.py:79 / :146); with heads sharded over GPUs each GPU
+    contributes its heads' sum and the sums are all-reduced."""
+    xf = _f(x16)
+    norms = np.sqrt(np.sum(xf * xf, axis=1, dtype=F32)).astype(F32)  # (H, D)
+    return np.sum(norms, axis=0, dtype=F32).astype(F32)
+
+
+def _outlier_select(x16: np.ndarray, fraction: float, score_sum=None, score_heads: int = 0):
     """affine_quantizer.py:75-85 (keys) / :143-151 (values).
 
     Channel score = L2 norm over tokens (fp32) per (head, channel), then the
@@ -151,9 +162,10 @@ def _outlier_select(x16: np.ndarray, fraction: float):
     """
     D = x16.shape[-1]
     n = max(1, int(D * fraction))
-    xf = _f(x16)
-    norms = np.sqrt(np.sum(xf * xf, axis=1, dtype=F32)).astype(F32)  # (H, D)
-    score = (np.sum(norms, axis=0, dtype=F32) / F32(norms.shape[0])).astype(F32)
+    if score_sum is None:
+        score = (outlier_norm_sum(x16) / F32(x16.shape[0])).astype(F32)
+    else:  # scores over heads held elsewhere too (sharded heads)
+        score = (np.asarray(score_sum, F32) / F32(score_heads)).astype(F32)
     idx = np.argsort(-score, kind="stable")[:n]
     data = x16[..., idx].astype(F16)
     x16 = x16.copy()
@@ -181,7 +193,8 @@ def _affine_codes(x16: np.ndarray, lo: np.ndarray, hi: np.ndarray, bits: int):
     return r.astype(np.uint8), scale, zero
 
 
-def quantize_keys(k: np.ndarray, bits: int, outlier_fraction: float = 0.0, packed: bool = True) -> dict:
+def quantize_keys(k: np.ndarray, bits: int, outlier_fraction: float = 0.0, packed: bool = True,
+                  score_sum=None, score_heads: int = 0) -> dict:
     """affine_quantizer.py:63-110 — per-(head, channel) min/max over the tokens of the call.
 
     k: (H, N, D) fp16.  Returns the reference's dict layout.
@@ -189,7 +202,7 @@ def quantize_keys(k: np.ndarray, bits: int, outlier_fraction: float = 0.0, packe
     k16 = np.asarray(k).astype(F16)
     out = {}
     if outlier_fraction > 0:
-        k16, idx, data = _outlier_select(k16, outlier_fraction)
+        k16, idx, data = _outlier_select(k16, outlier_fraction, score_sum, score_heads)
         out["outlier_idx"] = idx
         out["outlier_data"] = data
     lo = k16.min(axis=1, keepdims=True)
@@ -200,12 +213,13 @@ def quantize_keys(k: np.ndarray, bits: int, outlier_fraction: float = 0.0, packe
     return out
 
 
-def quantize_values(v: np.ndarray, bits: int, outlier_fraction: float = 0.0, packed: bool = True) -> dict:
+def quantize_values(v: np.ndarray, bits: int, outlier_fraction: float = 0.0, packed: bool = True,
+                    score_sum=None, score_heads: int = 0) -> dict:
     """affine_quantizer.py:131-176 — per-(head, token) min/max over channels."""
     v16 = np.asarray(v).astype(F16)
     out = {}
     if outlier_fraction > 0:
-        v16, idx, data = _outlier_select(v16, outlier_fraction)
+        v16, idx, data = _outlier_select(v16, outlier_fraction, score_sum, score_heads)
         out["outlier_idx"] = idx
         out["outlier_data"] = data
     lo = v16.min(axis=2, keepdims=True)
@@ -311,6 +325,49 @@ def decode_attention(q: np.ndarray, keys: np.ndarray, values: np.ndarray,
             lse[b, h] = m + np.log(l)
     return (out, lse) if return_lse else out
 
+
+
+LOG2E = 1.4426950408889634
+
+
+def decode_partial(q: np.ndarray, keys: np.ndarray, values: np.ndarray, sm_scale: float | None = None) -> np.ndarray:
+    """Split-K partial record of one token range: (B*Hq, D+2) fp32 rows
+    (acc[D] = sum_t 2^(x_t - m) v_t, m = max_t x_t, l = sum_t 2^(x_t - m)),
+    x = q.k * sm_scale * log2(e); an empty range gives (0, -inf, 0).  This is
+    the record ``akv_mixed_decode`` writes to ``partial_out``."""
+    q = _f(q)
+    B, Hq, D = q.shape
+    Hkv = keys.shape[1]
+    g = Hq // Hkv
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    kf, vf = _f(keys), _f(values)
+    out = np.zeros((B * Hq, D + 2), F32)
+    for b in range(B):
+        for h in range(Hq):
+            r = b * Hq + h
+            if kf.shape[2] == 0:
+                out[r, D] = -np.inf
+                continue
+            x = (kf[b, h // g] @ q[b, h]).astype(F32) * F32(sm_scale * LOG2E)
+            m = x.max()
+            p = np.exp2(x - m).astype(F32)
+            out[r, :D] = p @ vf[b, h // g]
+            out[r, D], out[r, D + 1] = m, p.sum(dtype=F32)
+    return out
+
+
+def lse_combine(part: np.ndarray) -> np.ndarray:
+    """Merge split partial records (rows, splits, D+2) -> (rows, D) fp32 outputs."""
+    part = np.asarray(part, F32)
+    D = part.shape[-1] - 2
+    m = part[..., D]
+    M = m.max(axis=1, keepdims=True)
+    Mb = np.where(np.isneginf(M), 0.0, M)
+    w = np.exp2(m - Mb)  # (rows, splits)
+    L = (part[..., D + 1] * w).sum(axis=1)
+    acc = (part[..., :D] * w[..., None]).sum(axis=1)
+    return np.where(L[:, None] > 0, acc / np.where(L[:, None] > 0, L[:, None], 1.0), 0.0).astype(F32)
 
 def int4_group_dequant(packed: np.ndarray, scales: np.ndarray, zeros: np.ndarray,
                        head_dim: int, group_size: int) -> np.ndarray:
