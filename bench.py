@@ -152,7 +152,17 @@ def run_ours(args):
     hk0 = make_kv(torch, gen, (B, hkv, n_hot, D), dev)
     hv0 = make_kv(torch, gen, (B, hkv, n_hot, D), dev)
 
-    # ---- quantise + pack: prefill demotion of the warm tokens (one layer)
+    # ---- quantise + pack: prefill demotion of the warm tokens (one layer).
+    #      With KV heads sharded, outlier channels are still chosen over all
+    #      heads: the per-group norm sums are all-reduced before quantising.
+    from akv import parallel as P
+
+    def demote(arena):
+        if world > 1:
+            P.quantize_head_sharded(arena, wk, wv, total_heads=c["Hkv"], group=32)
+        else:
+            arena.append(wk, wv, group=32)
+
     arenas = [akv.WarmArena(B, hkv, D, c["key_bits"], c["value_bits"], c["outlier_fraction"],
                             max_blocks=nblk, device=dev) for _ in range(L)]
     st = torch.cuda.current_stream(dev)
@@ -163,14 +173,14 @@ def run_ours(args):
         scratch.n_blocks = 0
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(st)
-        scratch.append(wk, wv, group=32)
+        demote(scratch)
         e1.record(st)
         e1.synchronize()
         if i >= args.warmup:
             qp_times.append(e0.elapsed_time(e1))
     del scratch
     for a in arenas:
-        a.append(wk, wv, group=32)
+        demote(a)
     qp_ms = statistics.median(qp_times)
     qp_bytes = 2 * B * hkv * n_warm * D * 2 + B * hkv * nblk * arenas[0].rec
     hot_k = [hk0.clone() for _ in range(L)]
