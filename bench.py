@@ -258,8 +258,15 @@ def run_ours(args):
     e2e_ms = max_over_ranks(t0.elapsed_time(t1) / args.steps)
 
     # ---- roofline of the dominant kernel (per layer launch)
-    rec = arenas[0].rec
-    alg_bytes_layer = B * hkv * (nblk * rec + n_hot * D * 2 * 2) + 2 * B * hq * D * 2
+    # algorithmic bytes per layer launch, per (batch row, KV head): warm codes
+    # N_w*D*(bk+bv)/8 + K scale/zero per 32-token group D*4 + V scale/zero
+    # N_w*4 + fp16 outlier originals (K and V) N_w*n*4 + hot K/V N_h*D*4, plus
+    # q and out.  The record's extra bytes (fp32 V outlier residuals, masks,
+    # ids, padding) are format overhead and show up in `traffic`, not here.
+    n_out = arenas[0].n_out
+    per_kvh = (n_warm * D * (c["key_bits"] + c["value_bits"]) // 8 + nblk * D * 4 + n_warm * 4
+               + n_warm * n_out * 4 + n_hot * D * 4)
+    alg_bytes_layer = B * hkv * per_kvh + 2 * B * hq * D * 2
     per_launch_ms = ms_step / L  # decode kernel + its tiny LSE-combine kernel
     achieved = alg_bytes_layer / (per_launch_ms * 1e-3) / 1e9
     pk = peaks()
