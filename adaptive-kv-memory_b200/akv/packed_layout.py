@@ -86,7 +86,7 @@ class WarmArena:
             if n:
                 d.out_data = _C.View(base + L.vo, sb, sh, rec, 2 * n)
                 d.out_idx = _C.View(base + L.vi, sb, sh, rec, 0)
-                d.out_resid = _C.View(base + L.vr, sb, sh, rec, 4 * n)
+                d.out_vdq = _C.View(base + L.vd, sb, sh, rec, 2 * n)
         d.mask = _C.View(base + L.mask, sb, sh, rec, 0)
         return d
 

@@ -314,14 +314,10 @@ __host__ __device__ constexpr int vmult(int ci) {
 }
 
 // ------------------------------------------------------------------ shared softmax/PV state
-constexpr int kRegOutliers = 2;  // V outlier channels whose residual sum stays in registers
-
 struct WarpState {
   float acc[8][4];  // O^T: tile mt rows (g8 -> d=16*g8+2mt, g8+8 -> d+1), cols heads (2q4, 2q4+1)
   float m[2];       // running max (log2 units) for heads 2q4, 2q4+1
   float l[2];       // partial row sums (this thread's tokens only)
-  float vcorr[kRegOutliers][2];  // V outlier residual sums (warp-reduced), pending for channel vch[j]
-  int vch[kRegOutliers];
 };
 
 AKV_DEV void state_init(WarpState& s) {
@@ -331,25 +327,6 @@ AKV_DEV void state_init(WarpState& s) {
     for (int j = 0; j < 4; ++j) s.acc[i][j] = 0.f;
   s.m[0] = s.m[1] = -INFINITY;
   s.l[0] = s.l[1] = 0.f;
-#pragma unroll
-  for (int j = 0; j < kRegOutliers; ++j) {
-    s.vcorr[j][0] = s.vcorr[j][1] = 0.f;
-    s.vch[j] = -1;
-  }
-}
-
-// add (c0, c1) to output row `ch` (heads 2q4, 2q4+1) in the owning thread group
-AKV_DEV void acc_add_row(WarpState& s, int g8, int ch, float c0, float c1) {
-  if (ch < 0 || (ch >> 4) != g8) return;
-  const int ci = ch & 15;
-#pragma unroll
-  for (int mt = 0; mt < 8; ++mt)
-#pragma unroll
-    for (int hf = 0; hf < 2; ++hf)
-      if (ci == 2 * mt + hf) {
-        s.acc[mt][2 * hf] += c0;
-        s.acc[mt][2 * hf + 1] += c1;
-      }
 }
 
 // x[mt][4]: scaled logits (log2 units, -inf = masked) of this thread's 4
@@ -380,11 +357,6 @@ AKV_DEV void online_softmax(WarpState& s, float (&x)[2][4]) {
       s.acc[i][1] *= alpha[1];
       s.acc[i][2] *= alpha[0];
       s.acc[i][3] *= alpha[1];
-    }
-#pragma unroll
-    for (int j = 0; j < kRegOutliers; ++j) {
-      s.vcorr[j][0] *= alpha[0];
-      s.vcorr[j][1] *= alpha[1];
     }
   }
 #pragma unroll
@@ -417,6 +389,32 @@ AKV_DEV void pv_tiles(WarpState& st, const VPair<VB>& v0, const VPair<VB>& v1, _
     const uint32_t a3 = dq<vmult<VB>(C1)>(v_raw<VB, C1>(v1), s1, z1);
     mma_16816(st.acc[MT], a0, a1, a2, a3, pb[0], pb[1]);
     pv_tiles<VB, MT + 1>(st, v0, v1, s0, z0, s1, z1, pb);
+  }
+}
+
+// V outlier channel ch of a block: the reference attends over the fp16
+// original there, the codes dequantise to vd.  O^T row ch gets
+// sum_t (original_t - vd_t) p_t, as two MMAs (originals, then -vd, both exact
+// fp16) whose A operand is zero except row ch.  ch is the same for the whole
+// warp, so the target tile MT = (ch & 15) / 2 is a warp-uniform switch and
+// every accumulator index stays a compile-time constant.
+template <int MT>
+AKV_DEV void outlier_tile(WarpState& st, const uint32_t (&ao)[4], const uint32_t (&an)[4], const uint32_t (&pb)[2]) {
+  mma_16816(st.acc[MT], ao[0], ao[1], ao[2], ao[3], pb[0], pb[1]);
+  mma_16816(st.acc[MT], an[0], an[1], an[2], an[3], pb[0], pb[1]);
+}
+
+AKV_DEV void outlier_mma(WarpState& st, int mt, const uint32_t (&ao)[4], const uint32_t (&an)[4],
+                         const uint32_t (&pb)[2]) {
+  switch (mt) {
+    case 0: outlier_tile<0>(st, ao, an, pb); break;
+    case 1: outlier_tile<1>(st, ao, an, pb); break;
+    case 2: outlier_tile<2>(st, ao, an, pb); break;
+    case 3: outlier_tile<3>(st, ao, an, pb); break;
+    case 4: outlier_tile<4>(st, ao, an, pb); break;
+    case 5: outlier_tile<5>(st, ao, an, pb); break;
+    case 6: outlier_tile<6>(st, ao, an, pb); break;
+    default: outlier_tile<7>(st, ao, an, pb); break;
   }
 }
 
@@ -633,40 +631,28 @@ __global__ void __launch_bounds__(kDecodeThreads, 4) mixed_decode_kernel(const D
           pv_tiles<VB, 0>(st, v0, v1, s0, z0, s1, z1, pb[ks]);
         }
 
-        // ---- V outlier channels: add sum_t p_t * (original - dequantised) to their rows
+        // ---- V outlier channels: O^T row ch += sum_t p_t (original_t - vd_t)
         if (n_out > 0) {
-          const float* vr = reinterpret_cast<const float*>(r + p.L.vr);
+          const __half* vo = reinterpret_cast<const __half*>(r + p.L.vo);
+          const __half* vdq = reinterpret_cast<const __half*>(r + p.L.vd);
           const int16_t* vid = reinterpret_cast<const int16_t*>(r + p.L.vi);
           for (int j = 0; j < n_out; ++j) {
-            float cr[2] = {0.f, 0.f};
-#pragma unroll
-            for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-              for (int rr = 0; rr < 2; ++rr) {
-                const float rv = vr[(16 * mt + 8 * rr + g8) * n_out + j];
-                cr[0] = fmaf(x[mt][2 * rr], rv, cr[0]);
-                cr[1] = fmaf(x[mt][2 * rr + 1], rv, cr[1]);
-              }
-#pragma unroll
-            for (int o = 4; o < 32; o <<= 1) {
-              cr[0] += __shfl_xor_sync(0xffffffffu, cr[0], o);
-              cr[1] += __shfl_xor_sync(0xffffffffu, cr[1], o);
-            }
             const int ch = vid[j];
-            if (j < kRegOutliers) {
+            const bool own = (ch >> 4) == g8;
+            const int hf = ch & 1;
 #pragma unroll
-              for (int jj = 0; jj < kRegOutliers; ++jj) {
-                if (jj != j) continue;
-                if (ch != st.vch[jj]) {  // channel changed: settle the pending sum into its row
-                  acc_add_row(st, g8, st.vch[jj], st.vcorr[jj][0], st.vcorr[jj][1]);
-                  st.vcorr[jj][0] = st.vcorr[jj][1] = 0.f;
-                  st.vch[jj] = ch;
-                }
-                st.vcorr[jj][0] += cr[0];
-                st.vcorr[jj][1] += cr[1];
-              }
-            } else {
-              acc_add_row(st, g8, ch, cr[0], cr[1]);
+            for (int ks = 0; ks < 2; ++ks) {
+              const int ta = 16 * ks + 2 * q4;
+              const uint32_t o0 = h2_as_u32(__halves2half2(vo[ta * n_out + j], vo[(ta + 1) * n_out + j]));
+              const uint32_t o1 = h2_as_u32(__halves2half2(vo[(ta + 8) * n_out + j], vo[(ta + 9) * n_out + j]));
+              const uint32_t d0 = h2_as_u32(__halves2half2(vdq[ta * n_out + j], vdq[(ta + 1) * n_out + j]));
+              const uint32_t d1 = h2_as_u32(__halves2half2(vdq[(ta + 8) * n_out + j], vdq[(ta + 9) * n_out + j]));
+              const uint32_t on = own ? 0xFFFFFFFFu : 0u;  // A is zero outside row ch
+              const uint32_t m0 = hf ? 0u : on, m1 = hf ? on : 0u;
+              const uint32_t ao[4] = {o0 & m0, o0 & m1, o1 & m0, o1 & m1};
+              const uint32_t an[4] = {(d0 ^ 0x80008000u) & m0, (d0 ^ 0x80008000u) & m1, (d1 ^ 0x80008000u) & m0,
+                                      (d1 ^ 0x80008000u) & m1};
+              outlier_mma(st, (ch & 15) >> 1, ao, an, pb[ks]);
             }
           }
         }
@@ -685,8 +671,6 @@ __global__ void __launch_bounds__(kDecodeThreads, 4) mixed_decode_kernel(const D
       if (lane == 0)
         for (int li = waited; li < min(nmine, waited + kStagesPerWarp); ++li)
           mbar_wait(&wbar[li % kStagesPerWarp], (li / kStagesPerWarp) & 1, p.status);
-#pragma unroll
-      for (int jj = 0; jj < kRegOutliers; ++jj) acc_add_row(st, g8, st.vch[jj], st.vcorr[jj][0], st.vcorr[jj][1]);
     }
   } else {
     // ---------------- hot CTA: FP16 window, 128-bit loads

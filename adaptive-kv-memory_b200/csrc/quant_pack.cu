@@ -257,9 +257,9 @@ AKV_DEV void load_words(const char* p, uint32_t (&w)[BITS]) {
 //   co    keys:   km, kns, kr [H][D/2] fp16x2: fp16-path m, -s', 1/s' per channel pair
 //         values: [rows] 16-byte records {z | m, -s' | 1/s' (fp16), -s_eff, 1/s_eff (fp32)}
 //         -- shares its space with norms [H][D] fp32 and score [D] fp32, dead by then
-//   oidx  [kMaxOutliers] int,  od_s [rows][n_out] fp16 outlier originals
+//   oidx  [kMaxOutliers] int
 struct QuantSmem {
-  size_t cz, cs, co, score, oidx, od, total;
+  size_t cz, cs, co, score, oidx, total;
 };
 
 __host__ __device__ inline QuantSmem quant_smem_layout(int H, int nt, int D, int n_out, bool is_key) {
@@ -273,8 +273,7 @@ __host__ __device__ inline QuantSmem quant_smem_layout(int H, int nt, int D, int
   const size_t nsb = hd * 4 + static_cast<size_t>(D) * 4;
   m.score = m.co + hd * 4;
   m.oidx = m.co + (cob > nsb ? cob : nsb);
-  m.od = m.oidx + kMaxOutliers * 4;
-  m.total = m.od + rows * n_out * 2;
+  m.total = m.oidx + kMaxOutliers * 4;
   return m;
 }
 
@@ -313,7 +312,6 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
   uint32_t* kr = kns + H * D2;
   uint4* vco = reinterpret_cast<uint4*>(smem_raw + lay.co);       // values
   int* oidx = reinterpret_cast<int*>(smem_raw + lay.oidx);
-  __half* od_s = reinterpret_cast<__half*>(smem_raw + lay.od);
 
   // ---- stage the group's rows with 1-D bulk TMA (warp 0 issues, all wait)
   __shared__ __align__(8) uint64_t stage_bar;
@@ -481,7 +479,6 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
       __half* orow = od.ptr ? reinterpret_cast<__half*>(vaddr(od, b, h0 + h, blk0 + (t >> 5), t & 31)) : nullptr;
       for (int j = 0; j < p.n_out; ++j) {
         __half* x = xs + r * D + oidx[j];
-        od_s[r * p.n_out + j] = *x;
         if (orow) orow[j] = *x;
         *x = __float2half_rn(0.0f);
       }
@@ -570,12 +567,12 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
       const int blk = blk0 + (t >> 5), slot = t & 31;
       if (p.dst.scale.ptr) *reinterpret_cast<__half*>(vaddr(p.dst.scale, b, h0 + h, blk, slot)) = sc;
       if (p.dst.zero.ptr) *reinterpret_cast<__half*>(vaddr(p.dst.zero, b, h0 + h, blk, slot)) = lo;
-      // outlier residual: fp16 original minus what the zeroed channel dequantises to
-      if (p.n_out > 0 && p.dst.out_resid.ptr) {
-        float* rp = reinterpret_cast<float*>(vaddr(p.dst.out_resid, b, h0 + h, blk, slot));
+      // what the zeroed outlier channel dequantises to (attention adds p . (original - this))
+      if (p.n_out > 0 && p.dst.out_vdq.ptr) {
+        __half* rp = reinterpret_cast<__half*>(vaddr(p.dst.out_vdq, b, h0 + h, blk, slot));
         const uint32_t c0 = encode_one<BITS>(__float2half_rn(0.0f), lo, se, rc);
         const __half deq = __hadd_rn(__hmul_rn(__uint2half_rn(c0), sc), lo);
-        for (int j = 0; j < p.n_out; ++j) rp[j] = __half2float(od_s[r * p.n_out + j]) - __half2float(deq);
+        for (int j = 0; j < p.n_out; ++j) rp[j] = deq;
       }
     }
   }
@@ -1078,7 +1075,7 @@ extern "C" int akv_quantize_ext(const uint16_t* src, int64_t src_sb, int64_t src
                                   dst->zero.sblk % 4))
     return AKV_ERR_ALIGN;
   if (dst->mask.ptr && !aligned(dst->mask.ptr, 4)) return AKV_ERR_ALIGN;
-  if (dst->out_resid.ptr && (!aligned(dst->out_resid.ptr, 4) || dst->out_resid.sslot % 4)) return AKV_ERR_ALIGN;
+  if (dst->out_vdq.ptr && (!aligned(dst->out_vdq.ptr, 2) || dst->out_vdq.sslot % 2)) return AKV_ERR_ALIGN;
   const QuantPlan pl = plan_quant(B, H, N, D, group, n_outlier, is_key != 0);
   if (pl.smem > kQuantSmemLimit) return AKV_ERR_UNSUPPORTED;
   if (pl.chunked && (!workspace || workspace_bytes < pl.ws_bytes || !aligned(workspace, 256))) return AKV_ERR_WORKSPACE;

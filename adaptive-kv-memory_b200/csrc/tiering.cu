@@ -202,8 +202,8 @@ extern "C" int akv_warm_layout_init(int D, int kb, int vb, int n, akv_warm_layou
   off = up16(off + 2 * kBlockTokens * n);
   L->vo = off;
   off = up16(off + 2 * kBlockTokens * n);
-  L->vr = off;
-  off = up16(off + 4 * kBlockTokens * n);
+  L->vd = off;
+  off = up16(off + 2 * kBlockTokens * n);
   L->ki = off;                          // n int16 K outlier ids
   L->vi = off + 2 * n;                  // n int16 V outlier ids
   L->mask = off + ((4 * n + 3) & ~3);   // u32 valid-slot mask

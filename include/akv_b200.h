@@ -61,15 +61,16 @@ int akv_abi_version(void);
  *   vs  V scale   [32] fp16   vz  V zero [32] fp16  (per token)
  *   ko  K outlier data [32][n] fp16     vo  V outlier data [32][n] fp16
  *   ki  K outlier channel ids [n] int16 vi  V outlier channel ids [n] int16
- *   vr  V outlier residuals [32][n] fp32: original - dequantised code value of
- *       each V outlier channel (what attention adds so it sees the original)
+ *   vd  V outlier dequantised values [32][n] fp16: what the codes of each
+ *       zeroed V outlier channel dequantise to; attention adds
+ *       p . (original - vd) so it sees the original
  *   mask  u32 bitmask of valid token slots
  * All offsets are multiples of 16 bytes and `bytes` (the record stride) is a
  * multiple of 16 so records can be moved with 1-D bulk TMA copies.
  * ---------------------------------------------------------------------- */
 typedef struct {
   int32_t head_dim, key_bits, value_bits, n_outlier;
-  int32_t kc, vc, ks, kz, vs, vz, ko, vo, vr, ki, vi, mask, bytes;
+  int32_t kc, vc, ks, kz, vs, vz, ko, vo, vd, ki, vi, mask, bytes;
 } akv_warm_layout;
 
 /* Fill `out` for the given shape.  Returns AKV_ERR_SHAPE / AKV_ERR_BITS on bad input. */
@@ -90,11 +91,11 @@ typedef struct {
  *                values: one fp16 per token
  *   out_data     n fp16 per token
  *   out_idx      n int16 per (b, h, blk) (sslot unused)
- *   out_resid    values only: n fp32 per token, original minus the dequantised
- *                code value of each outlier channel (the warm record's vr field)
+ *   out_vdq      values only: n fp16 per token, the dequantised code value of
+ *                each (zeroed) outlier channel (the warm record's vd field)
  *   mask         u32 per (b, h, blk): bit s set for each slot this call wrote */
 typedef struct {
-  akv_view codes, scale, zero, out_data, out_idx, out_resid, mask;
+  akv_view codes, scale, zero, out_data, out_idx, out_vdq, mask;
 } akv_qdest;
 
 /* ------------------------------------------------------------------------
