@@ -79,6 +79,10 @@ SIGNATURES = {
     "akv_lse_combine": (c_int, [c_void_p, c_int64, c_int64, c_int, c_int, c_int, c_void_p, c_int64, c_void_p,
                                 c_void_p, c_void_p]),
     "akv_importance_update": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int, c_float, c_void_p]),
+    "akv_migrator_update": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int,
+                                    c_int64, c_float, c_void_p]),
+    "akv_migrator_importance": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int64, c_float, c_float, c_float,
+                                        c_int, c_int, c_void_p, c_void_p, c_size_t, c_void_p]),
     "akv_select_workspace_bytes": (c_size_t, [c_int]),
     "akv_select_bottomk": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_size_t, c_void_p]),
     "akv_gather_rows": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int, c_int, c_int, c_int64,

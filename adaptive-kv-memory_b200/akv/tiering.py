@@ -11,6 +11,8 @@ gather/compaction and cold-tier (pinned host) copies.
 """
 from __future__ import annotations
 
+from typing import Optional
+
 import torch
 
 from . import _C
@@ -98,3 +100,91 @@ def cold_restore_blocks(host: torch.Tensor, arena_buf: torch.Tensor, blk0: int,
     ev = torch.cuda.Event()
     ev.record(st)
     return ev
+
+
+class ImportanceMigrator:
+    """GPU state and scoring of the reference's ``ImportanceBasedMigrator``
+    (akv/vmm.py:113-245): per layer, fp32 attention scores, int64 last-access
+    steps and fp32 retrieval flags, grown as the sequence grows.
+
+    ``update`` and ``compute_importance`` run in the CUDA library
+    (``akv_migrator_update``, ``akv_migrator_importance``), eviction candidates
+    come from the bottom-k kernel.  Defaults follow the reference's VMMConfig.
+    """
+
+    def __init__(self, importance_decay: float = 0.95, attention_weight: float = 0.6,
+                 recency_weight: float = 0.2, retrieval_weight: float = 0.2, protect_initial: int = 4,
+                 protect_recent: int = 32, device="cuda"):
+        self.decay = importance_decay
+        self.w = (attention_weight, recency_weight, retrieval_weight)
+        self.protect_initial, self.protect_recent = protect_initial, protect_recent
+        self.device = torch.device(device)
+        self._state: dict = {}  # layer -> [scores, access, retrieval, length]
+        self._step = 0
+        self._ws = torch.empty(64, dtype=torch.uint8, device=self.device)
+
+    def _grow(self, layer: int, n: int):
+        st = self._state.get(layer)
+        if st is None:
+            cap = max(n, 64)
+            st = [torch.zeros(cap, device=self.device), torch.zeros(cap, dtype=torch.int64, device=self.device),
+                  torch.zeros(cap, device=self.device), 0]
+            self._state[layer] = st
+        elif st[0].shape[0] < n:
+            cap = max(n, 2 * st[0].shape[0])
+            for i in range(3):
+                t = torch.zeros(cap, dtype=st[i].dtype, device=self.device)
+                t[: st[i].shape[0]] = st[i]
+                st[i] = t
+        return st
+
+    def update(self, layer_idx: int, attention_weights: torch.Tensor, seq_len: Optional[int] = None) -> None:
+        """Fold one step's (B, H, Q, KV) attention into the layer's scores (vmm.py:121-164)."""
+        _C.require_cuda(attention_weights)
+        a = attention_weights.float().contiguous()
+        B, H, M, Na = a.shape
+        st = self._grow(layer_idx, Na)
+        n_prev = min(st[3], Na)
+        _C.check(_C.load().akv_migrator_update(a.data_ptr(), B, H, M, Na, st[0].data_ptr(), st[1].data_ptr(),
+                                               st[2].data_ptr(), n_prev, self._step, float(self.decay),
+                                               _C.stream_of(a)), "akv_migrator_update")
+        st[3] = max(st[3], Na)
+
+    def mark_promoted(self, layer_idx: int, indices: torch.Tensor) -> None:
+        st = self._state.get(layer_idx)
+        if st is not None and indices.numel() > 0:
+            st[2][indices.to(self.device)] = 1.0
+
+    def advance_step(self) -> None:
+        self._step += 1
+        for st in self._state.values():
+            st[2].mul_(0.9)
+
+    def compute_importance(self, layer_idx: int, seq_len: int) -> torch.Tensor:
+        """(seq_len,) composite importance, protected ends +inf (vmm.py:175-219)."""
+        st = self._state.get(layer_idx)
+        if st is None:
+            return torch.arange(seq_len, dtype=torch.float32, device=self.device)
+        out = torch.empty(seq_len, dtype=torch.float32, device=self.device)
+        wa, wr, wt = self.w
+        _C.check(_C.load().akv_migrator_importance(st[0].data_ptr(), st[1].data_ptr(), st[2].data_ptr(), seq_len,
+                                                   self._step, float(wa), float(wr), float(wt),
+                                                   self.protect_initial, self.protect_recent, out.data_ptr(),
+                                                   self._ws.data_ptr(), self._ws.numel(), _C.stream_of(out)),
+                 "akv_migrator_importance")
+        return out
+
+    def get_eviction_candidates(self, layer_idx: int, seq_len: int, num_to_evict: int) -> torch.Tensor:
+        """Ascending indices of the least important positions (vmm.py:221-242)."""
+        if num_to_evict <= 0:
+            return torch.empty(0, dtype=torch.int64, device=self.device)
+        imp = self.compute_importance(layer_idx, seq_len)
+        protected = min(seq_len, min(self.protect_initial, seq_len) + min(self.protect_recent, seq_len))
+        k = min(num_to_evict, seq_len - protected)
+        if k <= 0:
+            return torch.empty(0, dtype=torch.int64, device=self.device)
+        return select_bottomk(imp, k, 0, 0)
+
+    def reset(self) -> None:
+        self._state.clear()
+        self._step = 0

@@ -133,14 +133,24 @@ AKV_DEV uint32_t lop_magic(uint32_t x) {
   return r;
 }
 
+// fp16 bits of +-2^e (|e| <= 14), as a compile-time constant
+constexpr uint32_t fp16_pow2_bits(int e, bool negative) {
+  return (negative ? 0x8000u : 0u) | (static_cast<uint32_t>(15 + e) << 10);
+}
+
+constexpr int log2_pow2(int m) { return m <= 1 ? 0 : 1 + log2_pow2(m / 2); }
+
 // Undo the magic offset exactly: (1024 + m*c)/m - 1024/m == c for power-of-two m.
+// Both constants are exact fp16 powers of two, written as compile-time bit
+// patterns (no runtime conversion).
 template <int MULT>
 AKV_DEV uint32_t fix_magic(uint32_t x) {
-  const __half2 inv = __float2half2_rn(1.0f / MULT);
-  const __half2 off = __float2half2_rn(-1024.0f / MULT);
-  __half2 h = *reinterpret_cast<__half2*>(&x);
-  h = __hfma2(h, inv, off);
-  return *reinterpret_cast<uint32_t*>(&h);
+  constexpr int k = log2_pow2(MULT);
+  constexpr uint32_t inv = fp16_pow2_bits(-k, false) * 0x10001u;     // (1/m, 1/m)
+  constexpr uint32_t off = fp16_pow2_bits(10 - k, true) * 0x10001u;  // (-1024/m, -1024/m)
+  uint32_t r;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(x), "r"(inv), "r"(off));
+  return r;
 }
 
 template <uint32_t MASK, int MULT>

@@ -32,6 +32,98 @@ __global__ void importance_update_kernel(const float* __restrict__ attn, int B, 
 }
 
 // ---------------------------------------------------------------------------
+// ImportanceBasedMigrator (akv/vmm.py:113-245) on the GPU.
+//
+// update (:121-164): attention received per position = sum over queries of the
+// mean over batch and heads (the same reduction order as above); positions in
+// [n_prev, Na) are new and start at score 0, last access = step, retrieval 0;
+// scores = fl(fl(scores*decay) + received); last access = step where
+// received > 0.01.
+// ---------------------------------------------------------------------------
+__global__ void migrator_update_kernel(const float* __restrict__ attn, int B, int H, int M, int Na,
+                                       float* __restrict__ scores, int64_t* __restrict__ access,
+                                       float* __restrict__ retrieval, int n_prev, int64_t step, float decay) {
+  const int n = blockIdx.x * blockDim.x + threadIdx.x;
+  if (n >= Na) return;
+  const float cnt = static_cast<float>(B * H);
+  float imp = 0.f;
+  for (int m = 0; m < M; ++m) {
+    float s = 0.f;
+    for (int bh = 0; bh < B * H; ++bh) s = __fadd_rn(s, attn[(static_cast<int64_t>(bh) * M + m) * Na + n]);
+    imp = __fadd_rn(imp, __fdiv_rn(s, cnt));
+  }
+  float sc = scores[n];
+  if (n >= n_prev) {
+    sc = 0.f;
+    access[n] = step;
+    retrieval[n] = 0.f;
+  }
+  scores[n] = __fadd_rn(__fmul_rn(sc, decay), imp);
+  if (imp > 0.01f) access[n] = step;
+}
+
+// compute_importance (:175-219), step 1: max of scores, min of last access,
+// max of retrieval over [0, N) -> red[0..2] (one CTA)
+__global__ void migrator_reduce_kernel(const float* __restrict__ scores, const int64_t* __restrict__ access,
+                                       const float* __restrict__ retrieval, int N, float* red) {
+  __shared__ float smax[32], rmax[32];
+  __shared__ float amin[32];
+  float a = -INFINITY, r = -INFINITY, t = INFINITY;
+  for (int i = threadIdx.x; i < N; i += blockDim.x) {
+    a = fmaxf(a, scores[i]);
+    r = fmaxf(r, retrieval[i]);
+    t = fminf(t, static_cast<float>(access[i]));  // access.float().min()
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+    r = fmaxf(r, __shfl_xor_sync(0xffffffffu, r, o));
+    t = fminf(t, __shfl_xor_sync(0xffffffffu, t, o));
+  }
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    smax[w] = a;
+    rmax[w] = r;
+    amin[w] = t;
+  }
+  __syncthreads();
+  if (w == 0) {
+    const int nw = blockDim.x >> 5;
+    a = lane < nw ? smax[lane] : -INFINITY;
+    r = lane < nw ? rmax[lane] : -INFINITY;
+    t = lane < nw ? amin[lane] : INFINITY;
+    for (int o = 16; o > 0; o >>= 1) {
+      a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+      r = fmaxf(r, __shfl_xor_sync(0xffffffffu, r, o));
+      t = fminf(t, __shfl_xor_sync(0xffffffffu, t, o));
+    }
+    if (lane == 0) {
+      red[0] = a;
+      red[1] = t;
+      red[2] = r;
+    }
+  }
+}
+
+// step 2: importance = w_a*attn_norm + w_r*recency + w_t*retr_norm, each op
+// rounded like torch's, protected ends at +inf
+__global__ void migrator_importance_kernel(const float* __restrict__ scores, const int64_t* __restrict__ access,
+                                           const float* __restrict__ retrieval, int N, int64_t step,
+                                           const float* __restrict__ red, float w_a, float w_r, float w_t,
+                                           int n_first, int n_last, float* __restrict__ out) {
+  const int n = blockIdx.x * blockDim.x + threadIdx.x;
+  if (n >= N) return;
+  const float smax = red[0], amin = red[1], rmax = red[2];
+  const float attn_norm = __fdiv_rn(scores[n], fmaxf(smax, 1e-10f));
+  // max(1.0, step - access.min()) is Python double arithmetic, then a float32 divisor
+  const double den = fmax(1.0, static_cast<double>(step) - static_cast<double>(amin));
+  const float recency = __fdiv_rn(__fsub_rn(static_cast<float>(access[n]), amin), static_cast<float>(den));
+  const float retr = __fdiv_rn(retrieval[n], __fadd_rn(fmaxf(rmax, 1e-10f), 1e-10f));
+  float imp = __fadd_rn(__fadd_rn(__fmul_rn(w_a, attn_norm), __fmul_rn(w_r, recency)), __fmul_rn(w_t, retr));
+  if (n < n_first || n >= N - n_last) imp = INFINITY;
+  out[n] = imp;
+}
+
+// ---------------------------------------------------------------------------
 // bottom-k selection with protected ends (akv/drop_in.py:392-413)
 //
 // Scores map to order-preserving u32 keys; protected positions get the key
@@ -269,4 +361,31 @@ extern "C" int akv_cold_copy(void* dst, int64_t dst_stride, const void* src, int
     return AKV_ERR_LAUNCH;
   if (event && cudaEventRecord(static_cast<cudaEvent_t>(event), st) != cudaSuccess) return AKV_ERR_LAUNCH;
   return AKV_OK;
+}
+
+extern "C" int akv_migrator_update(const float* attn, int B, int H, int M, int Na, float* scores, int64_t* last_access,
+                                   float* retrieval, int n_prev, int64_t step, float decay, void* stream) {
+  if (!attn || !scores || !last_access || !retrieval) return AKV_ERR_NULL;
+  if (B <= 0 || H <= 0 || M <= 0 || Na < 0 || n_prev < 0) return AKV_ERR_SHAPE;
+  if (Na == 0) return AKV_OK;
+  migrator_update_kernel<<<(Na + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      attn, B, H, M, Na, scores, last_access, retrieval, n_prev, step, decay);
+  return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_LAUNCH;
+}
+
+extern "C" int akv_migrator_importance(const float* scores, const int64_t* last_access, const float* retrieval, int N,
+                                       int64_t step, float w_attn, float w_recency, float w_retrieval,
+                                       int protect_first, int protect_last, float* out, void* workspace,
+                                       size_t workspace_bytes, void* stream) {
+  if (!scores || !last_access || !retrieval || !out) return AKV_ERR_NULL;
+  if (N < 0 || protect_first < 0 || protect_last < 0) return AKV_ERR_SHAPE;
+  if (N == 0) return AKV_OK;
+  if (!workspace || workspace_bytes < 16) return AKV_ERR_WORKSPACE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  float* red = static_cast<float*>(workspace);
+  migrator_reduce_kernel<<<1, 1024, 0, st>>>(scores, last_access, retrieval, N, red);
+  migrator_importance_kernel<<<(N + 255) / 256, 256, 0, st>>>(scores, last_access, retrieval, N, step, red, w_attn,
+                                                               w_recency, w_retrieval, std::min(protect_first, N),
+                                                               std::min(protect_last, N), out);
+  return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_LAUNCH;
 }

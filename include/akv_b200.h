@@ -267,6 +267,25 @@ int akv_importance_update(const float* attn, int B, int H, int M, int Na, float*
                           void* stream);
 
 /* ------------------------------------------------------------------------
+ * A6: ImportanceBasedMigrator (akv/vmm.py:113-245) state on the GPU: fp32
+ * scores, int64 last-access steps and fp32 retrieval flags per position.
+ * akv_migrator_update replaces update() (:121-164): positions [n_prev, Na)
+ * are new (score 0, last access = step, retrieval 0); scores = scores*decay
+ * + (sum over queries of the mean over batch and heads of attn (B,H,M,Na));
+ * last access = step where that sum exceeds 0.01.
+ * akv_migrator_importance replaces compute_importance() (:175-219): the
+ * weighted sum of max-normalised scores, min-shifted recency and normalised
+ * retrieval, first protect_first / last protect_last positions +inf.
+ * Workspace: 16 bytes.
+ * ---------------------------------------------------------------------- */
+int akv_migrator_update(const float* attn, int B, int H, int M, int Na, float* scores, int64_t* last_access,
+                        float* retrieval, int n_prev, int64_t step, float decay, void* stream);
+int akv_migrator_importance(const float* scores, const int64_t* last_access, const float* retrieval, int N,
+                            int64_t step, float w_attn, float w_recency, float w_retrieval,
+                            int protect_first, int protect_last, float* out, void* workspace,
+                            size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
  * A7: demote selection.  Replaces AKVLayer._select_demote_indices
  * (akv/drop_in.py:392-413) and ImportanceBasedMigrator.get_eviction_candidates
  * (akv/vmm.py:221-242): the k lowest scores with the first `protect_first`

@@ -326,9 +326,47 @@ def make_drop_in_traces(ref_path: str):
     print("drop-in traces written to", HERE)
 
 
+def make_migrator_trace(ref_path: str):
+    """ImportanceBasedMigrator (akv/vmm.py:113-245) of the reference driven by
+    seeded attention: importance and eviction candidates after some steps.
+    Attention is continuous (no ties among candidates); positions grow."""
+    import torch
+    torch.set_num_threads(1)
+    sys.path.insert(0, ref_path)
+    from akv.vmm import ImportanceBasedMigrator, VMMConfig
+    cfg = VMMConfig(importance_decay=0.9, protect_initial=4, protect_recent=32)
+    mig = ImportanceBasedMigrator(cfg)
+    g = torch.Generator().manual_seed(9)
+    out = {}
+    B, H = 1, 2
+    N = 700
+    snaps = 0
+    for step in range(40):
+        N += 3
+        logits = torch.randn(B, H, 1, N, generator=g) * 3
+        attn = torch.softmax(logits, dim=-1)
+        out[f"attn{step}"] = attn.numpy()
+        mig.update(0, attn, N)
+        if step % 7 == 3:
+            idx = torch.randperm(N, generator=g)[:5]
+            out[f"promote{step}"] = idx.numpy()
+            mig.mark_promoted(0, idx)
+        if step % 5 == 4:
+            out[f"imp{step}"] = mig.compute_importance(0, N).numpy()
+            out[f"evict{step}"] = mig.get_eviction_candidates(0, N, 50).numpy()
+            snaps += 1
+        mig.advance_step()
+    np.savez_compressed(os.path.join(HERE, "migrator.npz"), **out)
+    print("migrator trace written to", HERE, snaps, "snapshots")
+
+
 if __name__ == "__main__":
+    if len(sys.argv) > 2 and sys.argv[2] == "migrator":
+        make_migrator_trace(sys.argv[1])
+        sys.exit(0)
     if len(sys.argv) > 2 and sys.argv[2] == "drop_in":
         make_drop_in_traces(sys.argv[1])
     else:
         main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
         make_drop_in_traces(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+        make_migrator_trace(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
