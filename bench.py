@@ -123,6 +123,72 @@ def make_kv(torch, gen, shape, device, outlier_ch=(3, 77)):
     return x.half()
 
 
+# ---------------------------------------------------------------------------- migration (config 4)
+def migration_bench(torch, akv, dev) -> dict:
+    """Secondary numbers for the tier-management rows at config 4's shape
+    (batch 8, 8 KV heads, 128K context, 2-bit warm tier, pinned cold tier):
+    the per-step importance update, the demote selection, one demote pass
+    (fused gather + quantise of 64 tokens per row and head, hot compaction)
+    and cold-tier copies over PCIe.  Device times from CUDA events (median)."""
+    import statistics
+    from akv import tiering
+    B, H, N, D = 8, 8, 128 * 1024, 128
+    g = torch.Generator(device=dev).manual_seed(7)
+    attn = torch.rand(B, H, 1, N, generator=g, device=dev)
+    attn /= attn.sum(-1, keepdim=True)
+    mig = tiering.ImportanceMigrator(importance_decay=0.9, device=dev)
+
+    def timed(fn, reps=20):
+        for _ in range(3):
+            fn()
+        ts = []
+        for _ in range(reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1) * 1e3)
+        return statistics.median(ts)
+
+    t_upd = timed(lambda: mig.update(0, attn, N))
+    upd_bytes = attn.numel() * 4 + N * (4 + 4 + 8 + 8)  # attention read, scores r/w, last access r/w
+    t_sel = timed(lambda: mig.get_eviction_candidates(0, N, 64))
+    hot = 4096
+    hk = torch.randn(B, H, hot, D, generator=g, device=dev).half()
+    hv = torch.randn(B, H, hot, D, generator=g, device=dev).half()
+    idx = torch.randperm(hot, generator=g, device=dev)[:64].sort().values
+    keep = torch.ones(hot, dtype=torch.bool, device=dev)
+    keep[idx] = False
+    kidx = keep.nonzero().squeeze(1)
+    arena = akv.WarmArena(B, H, D, 2, 2, 0.0, max_blocks=4, device=dev)
+
+    def demote():
+        arena.n_blocks = 0
+        arena.append(hk, hv, group=32, tok_idx=idx)
+        tiering.gather_rows(hk, kidx)
+        tiering.gather_rows(hv, kidx)
+    t_dem = timed(demote)
+    nblk = 256
+    cold_src = torch.randint(0, 255, (B, H, nblk, arena.rec), dtype=torch.uint8, device=dev, generator=g)
+    host = torch.empty(B, H, nblk, arena.rec, dtype=torch.uint8).pin_memory()
+    side = torch.cuda.Stream(device=dev)
+    cb = cold_src.numel()
+
+    def d2h():
+        tiering.cold_copy_blocks(cold_src, 0, nblk, host, stream=side).synchronize()
+
+    def h2d():
+        tiering.cold_restore_blocks(host, cold_src, 0, stream=side).synchronize()
+    t_d2h, t_h2d = timed(d2h, 10), timed(h2d, 10)
+    return {"workload": "config 4 shape: batch 8, 8 KV heads, 128K tokens, 2-bit warm, pinned cold tier",
+            "importance_update_us": round(t_upd, 2), "importance_update_gbs": round(upd_bytes / (t_upd * 1e3), 1),
+            "evict_select_us": round(t_sel, 2),
+            "demote_pass_us": round(t_dem, 2), "demote_tokens": 64,
+            "cold_d2h_gbs": round(cb / (t_d2h * 1e3), 1), "cold_h2d_gbs": round(cb / (t_h2d * 1e3), 1),
+            "cold_bytes": cb}
+
+
 # ---------------------------------------------------------------------------- our arm
 def run_ours(args):
     import torch
@@ -295,6 +361,8 @@ def run_ours(args):
             "gpu_launches": 2 * L * args.steps,
             "clocks": clocks,
         }
+        if world == 1 and not args.no_migration:
+            res["migration"] = migration_bench(torch, akv, dev)
         if world == 1 and not args.no_cpu_baseline:
             res["cpu_baseline"] = cpu_baseline(units=args.cpu_units, world=1)
         print(json.dumps(res), flush=True)
@@ -379,6 +447,7 @@ def main():
     ap.add_argument("--layers", type=int, default=CFG["layers"])
     ap.add_argument("--cpu-units", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-migration", action="store_true")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
