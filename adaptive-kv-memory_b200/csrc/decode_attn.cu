@@ -787,17 +787,17 @@ struct DecodePlan {
   int n_hg, warm_splits, hot_splits, wbps, hbps, splits;
 };
 
-static DecodePlan plan_decode(int B, int Hq, int Hkv, int n_hot, int n_warm_blocks, int rec_bytes) {
-  DecodePlan pl{};
-  const int g = Hq / Hkv;
-  pl.n_hg = (g + 7) / 8;
-  const int units = B * Hkv * pl.n_hg;
-  const int target = 148 * 6;  // ~1.5 waves of 4 resident CTAs per SM
-  const int per_unit = max(1, (target + units - 1) / units);
-  const int nhb = (n_hot + 31) / 32;
-  const double wbytes = static_cast<double>(n_warm_blocks) * rec_bytes;
-  const double hbytes = static_cast<double>(nhb) * 32 * kHeadDim * 4;
+// Split-K plan.  A unit is one (batch row, KV head, <= 8 query heads); its
+// tokens are split into warm and hot splits in proportion to their bytes.
+// The split count per unit is chosen so that the grid fills its last wave of
+// kDecodeSlots resident CTAs well, from at least ~3 waves (a half-empty last
+// wave leaves SMs idle at the end of the launch); config 3 (128 units) gets
+// 18 splits: 2,304 CTAs, 3.9 waves.
+constexpr int kDecodeSlots = 148 * 4;  // 148 SMs x 4 resident decode CTAs
+
+static void split_shares(int per_unit, int n_warm_blocks, int nhb, double wbytes, double hbytes, DecodePlan& pl) {
   const double tot = wbytes + hbytes;
+  pl.warm_splits = pl.hot_splits = pl.wbps = pl.hbps = 0;
   if (n_warm_blocks > 0) {
     int want = tot > 0 ? static_cast<int>(per_unit * wbytes / tot + 0.5) : 1;
     want = max(1, min(want, (n_warm_blocks + 3) / 4));
@@ -811,6 +811,40 @@ static DecodePlan plan_decode(int B, int Hq, int Hkv, int n_hot, int n_warm_bloc
     pl.hot_splits = (nhb + pl.hbps - 1) / pl.hbps;
   }
   pl.splits = pl.warm_splits + pl.hot_splits;
+}
+
+// candidate split counts per unit: [lo, hi]
+static void per_unit_range(int units, int& lo, int& hi) {
+  lo = max(1, (3 * kDecodeSlots + units - 1) / units);
+  hi = lo + max(8, lo);
+}
+
+static DecodePlan plan_decode(int B, int Hq, int Hkv, int n_hot, int n_warm_blocks, int rec_bytes) {
+  DecodePlan pl{};
+  const int g = Hq / Hkv;
+  pl.n_hg = (g + 7) / 8;
+  const int units = B * Hkv * pl.n_hg;
+  const int nhb = (n_hot + 31) / 32;
+  const double wbytes = static_cast<double>(n_warm_blocks) * rec_bytes;
+  const double hbytes = static_cast<double>(nhb) * 32 * kHeadDim * 4;
+  int lo, hi;
+  per_unit_range(units, lo, hi);
+  double best = -1.0;
+  DecodePlan cand = pl;
+  for (int pu = lo; pu <= hi; ++pu) {
+    split_shares(pu, n_warm_blocks, nhb, wbytes, hbytes, cand);
+    const int64_t ctas = static_cast<int64_t>(units) * cand.splits;
+    const int64_t waves = (ctas + kDecodeSlots - 1) / kDecodeSlots;
+    const double fill = static_cast<double>(ctas) / static_cast<double>(waves * kDecodeSlots);
+    if (fill > best + 0.03) {  // more splits only for a clearly fuller last wave
+      best = fill;
+      pl.warm_splits = cand.warm_splits;
+      pl.hot_splits = cand.hot_splits;
+      pl.wbps = cand.wbps;
+      pl.hbps = cand.hbps;
+      pl.splits = cand.splits;
+    }
+  }
   return pl;
 }
 
@@ -836,13 +870,14 @@ static int launch_decode(const DecodeParams& p, cudaStream_t st) {
 using namespace akv;
 
 // Upper bound on the split count of plan_decode for any record size: the warm
-// and hot shares round to at most per_unit + 1 splits together.
+// and hot shares of the largest candidate round to at most hi + 1 splits.
 static int max_splits(int B, int Hq, int Hkv, int n_hot, int n_warm_blocks) {
   const int g = Hq / Hkv;
   const int units = B * Hkv * ((g + 7) / 8);
-  const int per_unit = max(1, (148 * 6 + units - 1) / units);
+  int lo, hi;
+  per_unit_range(units, lo, hi);
   const int cap = n_warm_blocks + (n_hot + 31) / 32;
-  return max(1, min(per_unit + 2, cap));
+  return max(1, min(hi + 2, cap));
 }
 
 extern "C" size_t akv_decode_workspace_bytes(int B, int Hq, int Hkv, int D, int n_hot, int n_warm_blocks) {
