@@ -331,26 +331,31 @@ AKV_DEV void state_init(WarpState& s) {
 
 // x[mt][4]: scaled logits (log2 units, -inf = masked) of this thread's 4
 // tokens x 2 heads.  Rescales the state and turns x into probabilities.
+// Lazy rescaling: the running max m only moves (warp-wide max, rescale of
+// acc and l) when some logit of the block exceeds it by more than kLazyMax;
+// otherwise p = 2^(x - m) <= 2^kLazyMax, far inside fp16 and fp32 range, and
+// the block costs no shuffles.  acc / l and m + log2(l) do not depend on
+// which m was used.
+constexpr float kLazyMax = 8.f;
+
 AKV_DEV void online_softmax(WarpState& s, float (&x)[2][4]) {
   float mx[2];
   mx[0] = fmaxf(fmaxf(x[0][0], x[0][2]), fmaxf(x[1][0], x[1][2]));
   mx[1] = fmaxf(fmaxf(x[0][1], x[0][3]), fmaxf(x[1][1], x[1][3]));
+  if (__any_sync(0xffffffffu, mx[0] > s.m[0] + kLazyMax || mx[1] > s.m[1] + kLazyMax)) {
 #pragma unroll
-  for (int o = 4; o < 32; o <<= 1) {
-    mx[0] = fmaxf(mx[0], __shfl_xor_sync(0xffffffffu, mx[0], o));
-    mx[1] = fmaxf(mx[1], __shfl_xor_sync(0xffffffffu, mx[1], o));
-  }
-  float alpha[2], base[2];
+    for (int o = 4; o < 32; o <<= 1) {
+      mx[0] = fmaxf(mx[0], __shfl_xor_sync(0xffffffffu, mx[0], o));
+      mx[1] = fmaxf(mx[1], __shfl_xor_sync(0xffffffffu, mx[1], o));
+    }
+    float alpha[2];
 #pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const float mn = fmaxf(s.m[h], mx[h]);
-    base[h] = (mn == -INFINITY) ? 0.f : mn;
-    alpha[h] = fast_exp2(s.m[h] - base[h]);
-    s.m[h] = mn;
-    s.l[h] *= alpha[h];
-  }
-  // the running max rarely moves once a few blocks are in: skip the rescale then
-  if (__any_sync(0xffffffffu, alpha[0] != 1.f || alpha[1] != 1.f)) {
+    for (int h = 0; h < 2; ++h) {
+      const float mn = fmaxf(s.m[h], mx[h]);
+      alpha[h] = (mn == -INFINITY) ? 1.f : fast_exp2(s.m[h] - mn);
+      s.m[h] = mn;
+      s.l[h] *= alpha[h];
+    }
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       s.acc[i][0] *= alpha[0];
@@ -359,6 +364,7 @@ AKV_DEV void online_softmax(WarpState& s, float (&x)[2][4]) {
       s.acc[i][3] *= alpha[1];
     }
   }
+  const float base[2] = {s.m[0] == -INFINITY ? 0.f : s.m[0], s.m[1] == -INFINITY ? 0.f : s.m[1]};
 #pragma unroll
   for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
