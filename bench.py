@@ -44,9 +44,9 @@ CFG = dict(layers=32, B=16, Hq=32, Hkv=8, D=128, ctx=32768, hot=2048, key_bits=4
            outlier_fraction=0.01)
 
 
-def workload_config(world: int) -> dict:
-    c = dict(CFG)
-    return {"workload": "llama3-8b-shaped KV, ctx 32K, batch 16, k4v2 warm + 2048 fp16 hot, 32 layers",
+def workload_config(world: int, B: int = CFG["B"]) -> dict:
+    c = dict(CFG, B=B)
+    return {"workload": f"llama3-8b-shaped KV, ctx 32K, batch {B}, k4v2 warm + 2048 fp16 hot, 32 layers",
             "global_batch": c["B"], "seq_len": c["ctx"], "layers": c["layers"], "q_heads": c["Hq"],
             "kv_heads": c["Hkv"], "head_dim": c["D"], "hot_tokens": c["hot"], "warm_tokens": c["ctx"] - c["hot"],
             "key_bits": c["key_bits"], "value_bits": c["value_bits"], "outlier_fraction": c["outlier_fraction"],
@@ -201,7 +201,7 @@ def run_ours(args):
         import datetime
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    c = CFG
+    c = dict(CFG, B=args.batch)
     L = args.layers
     B, D = c["B"], c["D"]
     if c["Hkv"] % world:
@@ -327,8 +327,9 @@ def run_ours(args):
     # algorithmic bytes per layer launch, per (batch row, KV head): warm codes
     # N_w*D*(bk+bv)/8 + K scale/zero per 32-token group D*4 + V scale/zero
     # N_w*4 + fp16 outlier originals (K and V) N_w*n*4 + hot K/V N_h*D*4, plus
-    # q and out.  The record's extra bytes (fp32 V outlier residuals, masks,
-    # ids, padding) are format overhead and show up in `traffic`, not here.
+    # q and out.  The record's extra bytes (the dequantised values of the
+    # zeroed V outlier channels, masks, ids, padding) are format overhead and
+    # show up in `traffic`, not here.
     n_out = arenas[0].n_out
     per_kvh = (n_warm * D * (c["key_bits"] + c["value_bits"]) // 8 + nblk * D * 4 + n_warm * 4
                + n_warm * n_out * 4 + n_hot * D * 4)
@@ -340,7 +341,10 @@ def run_ours(args):
     tr_path = os.path.join(ROOT, "profiles", "decode_traffic.json")
     if os.path.exists(tr_path):
         with open(tr_path) as f:
-            traffic = json.load(f).get("bytes_per_launch")
+            tr = json.load(f)
+        # the capture is one config-3 layer launch (B16 x 8 KV heads); other
+        # shapes scale it by the (row, KV head) units they process
+        traffic = int(tr["bytes_per_launch"] * (B * hkv) / (CFG["B"] * CFG["Hkv"]))
 
     if rank == 0:
         res = {
@@ -348,7 +352,7 @@ def run_ours(args):
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
             "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "f16 in, f32 acc",
             "data": "synthetic (seeded N(0,1) K/V, x12 outlier channels)",
-            "config": workload_config(world),
+            "config": workload_config(world, B),
             "hbm_gbs": round(alg_bytes_layer * L * world / (ms_step * 1e-3) / 1e9, 1),
             "quant_pack_gbs": round(qp_bytes * world / (qp_ms * 1e-3) / 1e9, 1),
             "quant_pack_ms": round(qp_ms, 4),
@@ -448,6 +452,8 @@ def main():
     ap.add_argument("--cpu-units", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-migration", action="store_true")
+    ap.add_argument("--batch", type=int, default=CFG["B"],
+                    help="batch rows (default: config 3's 16; smaller only for profiler captures)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
