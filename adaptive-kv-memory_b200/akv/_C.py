@@ -27,13 +27,14 @@ class View(ctypes.Structure):
 
 class QDest(ctypes.Structure):
     """akv_qdest: where one quantiser call writes (or one dequantiser call reads)."""
-    _fields_ = [(n, View) for n in ("codes", "scale", "zero", "out_data", "out_idx", "out_vdq", "mask")]
+    _fields_ = [(n, View) for n in ("codes", "scale", "zero", "out_data", "out_idx", "out_vdq", "mask", "flags")]
 
 
 class WarmLayout(ctypes.Structure):
     """akv_warm_layout: byte offsets inside one 32-token warm block record."""
     _fields_ = [(n, c_int32) for n in ("head_dim", "key_bits", "value_bits", "n_outlier", "kc", "vc", "ks",
-                                        "kz", "vs", "vz", "ko", "vo", "vd", "ki", "vi", "mask", "bytes")]
+                                        "kz", "vs", "vz", "ko", "vo", "vd", "ki", "vi", "mask", "flags",
+                                        "bytes")]
 
     def as_dict(self) -> dict:
         return {n: getattr(self, n) for n, _ in self._fields_}

@@ -88,6 +88,7 @@ class WarmArena:
                 d.out_idx = _C.View(base + L.vi, sb, sh, rec, 0)
                 d.out_vdq = _C.View(base + L.vd, sb, sh, rec, 2 * n)
         d.mask = _C.View(base + L.mask, sb, sh, rec, 0)
+        d.flags = _C.View(base + L.flags + (0 if is_key else 1), sb, sh, rec, 0)
         return d
 
     def grow(self, min_blocks: int) -> None:

@@ -19,6 +19,34 @@ namespace akv {
 
 constexpr int kBlockTokens = 32;   // tokens per warm block record
 
+// Byte offsets inside one warm block record (the akv_warm_layout fields);
+// akv_warm_layout_init and the decode kernel's compile-time offsets both
+// come from here.  Everything up to ki depends only on (D, kb, vb).
+struct RecLayout {
+  int kc, vc, ks, kz, vs, vz, mask, flags, ki, vi, ko, vo, vd, bytes;
+};
+
+__host__ __device__ constexpr int up16c(int x) { return (x + 15) & ~15; }
+
+__host__ __device__ constexpr RecLayout rec_layout(int D, int kb, int vb, int n) {
+  RecLayout r{};
+  r.kc = 0;
+  r.vc = up16c(kBlockTokens * D * kb / 8);
+  r.ks = r.vc + up16c(kBlockTokens * D * vb / 8);
+  r.kz = r.ks + up16c(2 * D);
+  r.vs = r.kz + up16c(2 * D);
+  r.vz = r.vs + up16c(2 * kBlockTokens);
+  r.mask = r.vz + up16c(2 * kBlockTokens);  // u32 valid-slot mask
+  r.flags = r.mask + 4;                      // u8[4]: K / V decode flags
+  r.ki = r.mask + 8;                         // n int16 K outlier ids
+  r.vi = r.ki + 2 * n;                       // n int16 V outlier ids
+  r.ko = up16c(r.ki + 4 * n);
+  r.vo = r.ko + up16c(2 * kBlockTokens * n);
+  r.vd = r.vo + up16c(2 * kBlockTokens * n);
+  r.bytes = r.vd + up16c(2 * kBlockTokens * n);
+  return r;
+}
+
 // Bounded spin limit for every mbarrier wait (each try_wait may itself
 // suspend the thread for a while).  A wait that runs out records
 // AKV_ERR_TIMEOUT in the status word and the kernel stops issuing work.
@@ -151,6 +179,20 @@ AKV_DEV uint32_t fix_magic(uint32_t x) {
   uint32_t r;
   asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(x), "r"(inv), "r"(off));
   return r;
+}
+
+// Scales for which the decode's two-op dequantisation is exact: +0 or
+// [2^-14, 65504/1024].  With x = 1024 + M*c (the magic form, M = 2^k),
+//   y = fma(x, s, -1024*s) = fp16(M*c*s) = M*fp16(c*s)   (-1024*s exact, no overflow,
+//                                                          c*s normal or 0)
+//   fma(y, 1/M, z) = fp16(fp16(c*s) + z)                  (y/M exact)
+// which is the reference's codes.half() * scale + zero with both roundings
+// (checked exhaustively over every such scale, code, multiplier and a
+// stride-7 sample of all fp16 zeros).  The quantiser flags each warm record
+// whose scales all qualify.
+AKV_DEV bool dq2_scale_ok(__half s) {
+  const unsigned short u = __half_as_ushort(s);
+  return u == 0 || (u >= 0x0400 && u <= 0x53FF);
 }
 
 template <uint32_t MASK, int MULT>

@@ -23,6 +23,8 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cfloat>
+#include <cmath>
 
 #include "common.cuh"
 
@@ -31,7 +33,7 @@ namespace akv {
 constexpr int kHeadDim = 128;
 constexpr int kConsumerWarps = 4;
 constexpr int kDecodeThreads = kConsumerWarps * 32;
-constexpr int kStagesPerWarp = 3;                          // blocks each warp keeps in flight
+constexpr int kStagesPerWarp = 2;                          // blocks each warp keeps in flight
 constexpr int kStages = kConsumerWarps * kStagesPerWarp;
 constexpr int kMaxDecodeOutliers = 8;
 constexpr float kLog2e = 1.4426950408889634f;
@@ -50,7 +52,9 @@ struct DecodeParams {
   int n_warm_blocks;
   const int32_t* warm_len;
   int B, Hq, Hkv, g, n_hg;
-  float scale_log2;
+  float scale_log2;  // |sm_scale| * log2(e), at least FLT_MIN (scale 0: every logit weighs 2^0)
+  float lazy_raw;    // kLazyMax / scale_log2: raw-logit headroom before the running max moves
+  int q_neg;         // sm_scale < 0: the kernel negates q (exact) and uses |sm_scale|
   int warm_splits, hot_splits, wbps, hbps, splits;
   float* ws;  // split partials: row (b*Hq + hq)*splits + split holds (acc[D], m, l)
   int* status;
@@ -63,6 +67,33 @@ struct DecodeParams {
 template <int M>
 AKV_DEV uint32_t dq(uint32_t x, __half2 s, __half2 z) {
   return h2_as_u32(__hadd2_rn(__hmul2_rn(u32_as_h2(fix_magic<M>(x)), s), z));
+}
+
+// The same value in two fused ops for records whose scales pass
+// dq2_scale_ok: y = fma(x, s, b) = M*fp16(c*s) with b = -1024*s, then
+// fma(y, 1/M, z) = fp16(fp16(c*s) + z).
+template <int M>
+AKV_DEV uint32_t dq2(uint32_t x, uint32_t s, uint32_t b, uint32_t z) {
+  constexpr uint32_t inv = fp16_pow2_bits(-log2_pow2(M), false) * 0x10001u;  // (1/M, 1/M)
+  uint32_t y, r;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(y) : "r"(x), "r"(s), "r"(b));
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(y), "r"(inv), "r"(z));
+  return r;
+}
+
+// b = -1024 * s for a scale pair (exact for dq2_scale_ok scales)
+AKV_DEV uint32_t neg1024(uint32_t s) {
+  constexpr uint32_t k = fp16_pow2_bits(10, true) * 0x10001u;  // (-1024, -1024)
+  uint32_t b;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(b) : "r"(s), "r"(k));
+  return b;
+}
+
+// exact dequantisation of a magic pair: two-op form on flagged records
+template <int M, bool FAST>
+AKV_DEV uint32_t dqx(uint32_t x, uint32_t s, uint32_t b, uint32_t z) {
+  if constexpr (FAST) return dq2<M>(x, s, b, z);
+  else return dq<M>(x, u32_as_h2(s), u32_as_h2(z));
 }
 
 // ------------------------------------------------------------------ K codes -> A fragments
@@ -189,24 +220,25 @@ AKV_DEV void q_pairs(const __half (&qv)[32], uint32_t (&qp)[16]) {
 
 // q.K^T k-steps KS..KEND-1: per step, two channel pairs of the 4 token rows,
 // dequantised exactly, into the two m-tile accumulators.
-template <int KB, int KS, int KEND>
+template <int KB, bool FAST, int KS, int KEND>
 AKV_DEV void qk_steps(const KWords<KB> (&W)[2][2], const uint32_t (&S8)[8], const uint32_t (&Z8)[8],
                       const uint32_t (&qp)[16], float (&c)[2][4]) {
   if constexpr (KS < KEND) {
     constexpr int I0 = 2 * KS, I1 = 2 * KS + 1;
     constexpr PairIdx p0 = kpair<KB>(I0), p1 = kpair<KB>(I1);
     constexpr int M0 = kmult<KB>(I0), M1 = kmult<KB>(I1);
-    const __half2 s0 = pick2<p0.a, p0.b>(S8), z0 = pick2<p0.a, p0.b>(Z8);
-    const __half2 s1 = pick2<p1.a, p1.b>(S8), z1 = pick2<p1.a, p1.b>(Z8);
+    const uint32_t s0 = h2_as_u32(pick2<p0.a, p0.b>(S8)), z0 = h2_as_u32(pick2<p0.a, p0.b>(Z8));
+    const uint32_t s1 = h2_as_u32(pick2<p1.a, p1.b>(S8)), z1 = h2_as_u32(pick2<p1.a, p1.b>(Z8));
+    const uint32_t b0 = FAST ? neg1024(s0) : 0u, b1 = FAST ? neg1024(s1) : 0u;
 #pragma unroll
     for (int mt = 0; mt < 2; ++mt) {
-      const uint32_t a0 = dq<M0>(k_raw<KB, I0>(W[mt][0]), s0, z0);
-      const uint32_t a1 = dq<M0>(k_raw<KB, I0>(W[mt][1]), s0, z0);
-      const uint32_t a2 = dq<M1>(k_raw<KB, I1>(W[mt][0]), s1, z1);
-      const uint32_t a3 = dq<M1>(k_raw<KB, I1>(W[mt][1]), s1, z1);
+      const uint32_t a0 = dqx<M0, FAST>(k_raw<KB, I0>(W[mt][0]), s0, b0, z0);
+      const uint32_t a1 = dqx<M0, FAST>(k_raw<KB, I0>(W[mt][1]), s0, b0, z0);
+      const uint32_t a2 = dqx<M1, FAST>(k_raw<KB, I1>(W[mt][0]), s1, b1, z1);
+      const uint32_t a3 = dqx<M1, FAST>(k_raw<KB, I1>(W[mt][1]), s1, b1, z1);
       mma_16816(c[mt], a0, a1, a2, a3, qp[I0], qp[I1]);
     }
-    qk_steps<KB, KS + 1, KEND>(W, S8, Z8, qp, c);
+    qk_steps<KB, FAST, KS + 1, KEND>(W, S8, Z8, qp, c);
   }
 }
 
@@ -316,8 +348,14 @@ __host__ __device__ constexpr int vmult(int ci) {
 // ------------------------------------------------------------------ shared softmax/PV state
 struct WarpState {
   float acc[8][4];  // O^T: tile mt rows (g8 -> d=16*g8+2mt, g8+8 -> d+1), cols heads (2q4, 2q4+1)
-  float m[2];       // running max (log2 units) for heads 2q4, 2q4+1
+  float mr[2];      // running max of the raw logits q.k for heads 2q4, 2q4+1 (-inf: none yet)
+  float nb[2];      // -mr * scale_log2: the exponent offset in use (0 while mr = -inf)
   float l[2];       // partial row sums (this thread's tokens only)
+  // one-outlier records: sum_t p_t * original_t (side-tile row 0) and
+  // sum_t p_t * -vd_t (row 8) for V outlier channel vch, held by lanes g8 = 0
+  // until vch changes, then added to O^T row vch (flush_vout)
+  float vo_acc[4];
+  int vch;
 };
 
 AKV_DEV void state_init(WarpState& s) {
@@ -325,24 +363,53 @@ AKV_DEV void state_init(WarpState& s) {
   for (int i = 0; i < 8; ++i)
 #pragma unroll
     for (int j = 0; j < 4; ++j) s.acc[i][j] = 0.f;
-  s.m[0] = s.m[1] = -INFINITY;
+  s.mr[0] = s.mr[1] = -INFINITY;
+  s.nb[0] = s.nb[1] = 0.f;
   s.l[0] = s.l[1] = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) s.vo_acc[j] = 0.f;
+  s.vch = -1;
 }
 
-// x[mt][4]: scaled logits (log2 units, -inf = masked) of this thread's 4
-// tokens x 2 heads.  Rescales the state and turns x into probabilities.
-// Lazy rescaling: the running max m only moves (warp-wide max, rescale of
-// acc and l) when some logit of the block exceeds it by more than kLazyMax;
-// otherwise p = 2^(x - m) <= 2^kLazyMax, far inside fp16 and fp32 range, and
-// the block costs no shuffles.  acc / l and m + log2(l) do not depend on
-// which m was used.
+// Add the side tile's correction sum_t p_t (original_t - vd_t) into O^T row
+// vch and clear it.  Every lane takes part (shuffles); vch is warp-uniform.
+AKV_DEV void flush_vout(WarpState& s, int g8, int q4) {
+  const float v0 = __shfl_sync(0xffffffffu, s.vo_acc[0] + s.vo_acc[2], q4);
+  const float v1 = __shfl_sync(0xffffffffu, s.vo_acc[1] + s.vo_acc[3], q4);
+  const int ch = s.vch;
+  if (ch >= 0 && (ch >> 4) == g8) {
+    const int mt = (ch & 15) >> 1;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (i == mt) {
+        if (ch & 1) {
+          s.acc[i][2] += v0;
+          s.acc[i][3] += v1;
+        } else {
+          s.acc[i][0] += v0;
+          s.acc[i][1] += v1;
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) s.vo_acc[j] = 0.f;
+}
+
+// x[mt][4]: raw logits q.k of this thread's 4 tokens x 2 heads (-inf =
+// masked); p = 2^(x * scale_log2 + nb) overwrites x.  Lazy rescaling: the
+// running max moves (warp-wide max, rescale of acc and l) only when some logit
+// of the block exceeds it by more than lazy_raw = kLazyMax / scale_log2;
+// otherwise p <= 2^kLazyMax, far inside fp16 and fp32 range, and the block
+// costs no shuffles.  acc / l and -nb + log2(l) do not depend on which
+// offset was used.  scale_log2 > 0, so a masked -inf logit gives p = 0.
 constexpr float kLazyMax = 8.f;
 
-AKV_DEV void online_softmax(WarpState& s, float (&x)[2][4]) {
+AKV_DEV void online_softmax(WarpState& s, float (&x)[2][4], float sl2, float lazy_raw) {
   float mx[2];
   mx[0] = fmaxf(fmaxf(x[0][0], x[0][2]), fmaxf(x[1][0], x[1][2]));
   mx[1] = fmaxf(fmaxf(x[0][1], x[0][3]), fmaxf(x[1][1], x[1][3]));
-  if (__any_sync(0xffffffffu, mx[0] > s.m[0] + kLazyMax || mx[1] > s.m[1] + kLazyMax)) {
+  if (__any_sync(0xffffffffu, mx[0] > s.mr[0] + lazy_raw || mx[1] > s.mr[1] + lazy_raw)) {
 #pragma unroll
     for (int o = 4; o < 32; o <<= 1) {
       mx[0] = fmaxf(mx[0], __shfl_xor_sync(0xffffffffu, mx[0], o));
@@ -351,11 +418,17 @@ AKV_DEV void online_softmax(WarpState& s, float (&x)[2][4]) {
     float alpha[2];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      const float mn = fmaxf(s.m[h], mx[h]);
-      alpha[h] = (mn == -INFINITY) ? 1.f : fast_exp2(s.m[h] - mn);
-      s.m[h] = mn;
+      const float mn = fmaxf(s.mr[h], mx[h]);
+      const float nbn = (mn == -INFINITY) ? 0.f : -mn * sl2;
+      alpha[h] = (s.mr[h] == -INFINITY) ? 1.f : fast_exp2(fmaf(s.mr[h], sl2, nbn));
+      s.mr[h] = mn;
+      s.nb[h] = nbn;
       s.l[h] *= alpha[h];
     }
+    s.vo_acc[0] *= alpha[0];
+    s.vo_acc[1] *= alpha[1];
+    s.vo_acc[2] *= alpha[0];
+    s.vo_acc[3] *= alpha[1];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       s.acc[i][0] *= alpha[0];
@@ -364,12 +437,11 @@ AKV_DEV void online_softmax(WarpState& s, float (&x)[2][4]) {
       s.acc[i][3] *= alpha[1];
     }
   }
-  const float base[2] = {s.m[0] == -INFINITY ? 0.f : s.m[0], s.m[1] == -INFINITY ? 0.f : s.m[1]};
 #pragma unroll
   for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      x[mt][j] = fast_exp2(x[mt][j] - base[j & 1]);
+      x[mt][j] = fast_exp2(fmaf(x[mt][j], sl2, s.nb[j & 1]));
       s.l[j & 1] += x[mt][j];
     }
 }
@@ -384,17 +456,17 @@ AKV_DEV void p_fragments(const float (&x)[2][4], uint32_t (&pb)[2][2]) {
 
 // P.V k-step over 16 tokens: for each of the 8 m-tiles (channel pairs 2mt,
 // 2mt+1 of this thread group), the two token pairs, dequantised exactly.
-template <int VB, int MT>
-AKV_DEV void pv_tiles(WarpState& st, const VPair<VB>& v0, const VPair<VB>& v1, __half2 s0, __half2 z0, __half2 s1,
-                      __half2 z1, const uint32_t (&pb)[2]) {
+template <int VB, bool FAST, int MT>
+AKV_DEV void pv_tiles(WarpState& st, const VPair<VB>& v0, const VPair<VB>& v1, uint32_t s0, uint32_t b0,
+                      uint32_t z0, uint32_t s1, uint32_t b1, uint32_t z1, const uint32_t (&pb)[2]) {
   if constexpr (MT < 8) {
     constexpr int C0 = 2 * MT, C1 = 2 * MT + 1;
-    const uint32_t a0 = dq<vmult<VB>(C0)>(v_raw<VB, C0>(v0), s0, z0);
-    const uint32_t a1 = dq<vmult<VB>(C1)>(v_raw<VB, C1>(v0), s0, z0);
-    const uint32_t a2 = dq<vmult<VB>(C0)>(v_raw<VB, C0>(v1), s1, z1);
-    const uint32_t a3 = dq<vmult<VB>(C1)>(v_raw<VB, C1>(v1), s1, z1);
+    const uint32_t a0 = dqx<vmult<VB>(C0), FAST>(v_raw<VB, C0>(v0), s0, b0, z0);
+    const uint32_t a1 = dqx<vmult<VB>(C1), FAST>(v_raw<VB, C1>(v0), s0, b0, z0);
+    const uint32_t a2 = dqx<vmult<VB>(C0), FAST>(v_raw<VB, C0>(v1), s1, b1, z1);
+    const uint32_t a3 = dqx<vmult<VB>(C1), FAST>(v_raw<VB, C1>(v1), s1, b1, z1);
     mma_16816(st.acc[MT], a0, a1, a2, a3, pb[0], pb[1]);
-    pv_tiles<VB, MT + 1>(st, v0, v1, s0, z0, s1, z1, pb);
+    pv_tiles<VB, FAST, MT + 1>(st, v0, v1, s0, b0, z0, s1, b1, z1, pb);
   }
 }
 
@@ -441,9 +513,9 @@ AKV_DEV void warp_to_smem(WarpState& s, int lane, float* red, float* rm, float* 
     red[(2 * q4) * kHeadDim + d + 1] = s.acc[mt][2];
     red[(2 * q4 + 1) * kHeadDim + d + 1] = s.acc[mt][3];
   }
-  if (g8 == 0) {
-    rm[2 * q4] = s.m[0];
-    rm[2 * q4 + 1] = s.m[1];
+  if (g8 == 0) {  // partial (acc, m, l) with acc and l relative to 2^m, m = -nb (log2 units)
+    rm[2 * q4] = s.l[0] == 0.f ? -INFINITY : -s.nb[0];
+    rm[2 * q4 + 1] = s.l[1] == 0.f ? -INFINITY : -s.nb[1];
     rl[2 * q4] = s.l[0];
     rl[2 * q4 + 1] = s.l[1];
   }
@@ -477,8 +549,171 @@ AKV_DEV void cta_write_partial(const DecodeParams& p, float* red, float* rm, flo
 }
 
 // ------------------------------------------------------------------ the kernel
-template <int KB, int VB>
+// One warm block record (32 tokens of one (row, KV head)) staged at r:
+// S^T = K^ q on the tensor cores, online softmax, O^T += V^ P.  FAST: every
+// scale of the record passes dq2_scale_ok (record flags), so dequantisation
+// takes two fused fp16 ops per code pair instead of four; the values are the
+// same.  Offsets of the fixed fields are compile-time constants.
+// NOUT: 0 = no outlier channels; 1 = one (K: q[ch] * original added to the
+// logits with FFMAs, V: the side tile of WarpState); 2 = any n_out <= 8
+// (extra MMAs per channel).
+template <int KB, int VB, int NOUT, bool FAST>
+AKV_DEV void warm_block(WarpState& st, const uint8_t* r, uint32_t mask, const uint32_t (&qp)[16], const float* qs,
+                        int n_out, float sl2, float lazy_raw, int g8, int q4) {
+  constexpr RecLayout R = rec_layout(kHeadDim, KB, VB, 0);
+  constexpr RecLayout R1 = rec_layout(kHeadDim, KB, VB, 1);
+  constexpr int kp = kHeadDim * KB / 8, vp = kHeadDim * VB / 8;
+
+  // one outlier channel: fetch its ids, the query at the K channel and the K
+  // originals of this thread's tokens before the main work
+  float qk1[2] = {0.f, 0.f}, ko1[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+  if constexpr (NOUT == 1) {
+    const int kch = *reinterpret_cast<const int16_t*>(r + R1.ki);
+    const int vch = *reinterpret_cast<const int16_t*>(r + R1.vi);
+    qk1[0] = qs[(2 * q4) * kHeadDim + kch];
+    qk1[1] = qs[(2 * q4 + 1) * kHeadDim + kch];
+    const __half* ko = reinterpret_cast<const __half*>(r + R1.ko);
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) ko1[mt][rr] = __half2float(ko[16 * mt + 8 * rr + g8]);
+    if (vch != st.vch) {  // the V outlier channel moved: settle the side tile
+      flush_vout(st, g8, q4);
+      st.vch = vch;
+    }
+  }
+
+  // ---- S^T = K^ q  (tokens x heads): rows 16mt + 8rr + g8, k-steps over channel pairs
+  KWords<KB> W[2][2];
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) W[mt][rr] = k_words<KB>(r + R.kc + (16 * mt + 8 * rr + g8) * kp, q4);
+  float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+  {
+    const uint32_t* ks32 = reinterpret_cast<const uint32_t*>(r + R.ks) + 16 * q4;
+    const uint32_t* kz32 = reinterpret_cast<const uint32_t*>(r + R.kz) + 16 * q4;
+    uint32_t S8[8], Z8[8];
+    *reinterpret_cast<uint4*>(S8) = lds_v4(ks32);
+    *reinterpret_cast<uint4*>(S8 + 4) = lds_v4(ks32 + 4);
+    *reinterpret_cast<uint4*>(Z8) = lds_v4(kz32);
+    *reinterpret_cast<uint4*>(Z8 + 4) = lds_v4(kz32 + 4);
+    qk_steps<KB, FAST, 0, 4>(W, S8, Z8, qp, c);
+    *reinterpret_cast<uint4*>(S8) = lds_v4(ks32 + 8);
+    *reinterpret_cast<uint4*>(S8 + 4) = lds_v4(ks32 + 12);
+    *reinterpret_cast<uint4*>(Z8) = lds_v4(kz32 + 8);
+    *reinterpret_cast<uint4*>(Z8 + 4) = lds_v4(kz32 + 12);
+    qk_steps<KB, FAST, 4, 8>(W, S8, Z8, qp, c);
+  }
+  // K outlier channels: their dequantised value is 0 (scale = zero = 0) and the
+  // reference puts the fp16 original there.  One channel: + q[ch] * original
+  // per logit.  General: one more MMA whose k slots 2q4, 2q4+1 are outliers
+  // j = 2q4, 2q4+1 (n_outlier <= 8).
+  if constexpr (NOUT == 1) {
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) c[mt][2 * rr + h] = fmaf(qk1[h], ko1[mt][rr], c[mt][2 * rr + h]);
+  }
+  if (NOUT == 2 && n_out > 0) {
+    const __half* ko = reinterpret_cast<const __half*>(r + up16c(R.ki + 4 * n_out));
+    const int16_t* kid = reinterpret_cast<const int16_t*>(r + R.ki);
+    const int j0 = 2 * q4, j1 = 2 * q4 + 1;
+    const __half hz = __float2half_rn(0.f);
+    const __half qa = j0 < n_out ? __float2half_rn(qs[g8 * kHeadDim + kid[j0]]) : hz;
+    const __half qb = j1 < n_out ? __float2half_rn(qs[g8 * kHeadDim + kid[j1]]) : hz;
+    const uint32_t bq = h2_as_u32(__halves2half2(qa, qb));
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt) {
+      uint32_t a[2];
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) {
+        const int t = 16 * mt + 8 * rr + g8;
+        const __half oa = j0 < n_out ? ko[t * n_out + j0] : hz;
+        const __half ob = j1 < n_out ? ko[t * n_out + j1] : hz;
+        a[rr] = h2_as_u32(__halves2half2(oa, ob));
+      }
+      mma_16816(c[mt], a[0], a[1], 0u, 0u, bq, 0u);
+    }
+  }
+  // raw logits; masked slots -inf (only partial blocks pay for the selects)
+  if (mask != 0xffffffffu) {
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) {
+        const bool valid = (mask >> (16 * mt + 8 * rr + g8)) & 1u;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) c[mt][2 * rr + h] = valid ? c[mt][2 * rr + h] : -INFINITY;
+      }
+  }
+  online_softmax(st, c, sl2, lazy_raw);
+  uint32_t pb[2][2];
+  p_fragments(c, pb);
+
+  // ---- O^T += V^ P  (head_dim x heads), k-steps of 16 tokens
+  const __half* vsc = reinterpret_cast<const __half*>(r + R.vs);
+  const __half* vzr = reinterpret_cast<const __half*>(r + R.vz);
+#pragma unroll
+  for (int ks = 0; ks < 2; ++ks) {
+    const int ta = 16 * ks + 2 * q4;
+    const uint8_t* vc = r + R.vc;
+    const VPair<VB> v0 = v_pair<VB>(v_row_load<VB>(vc + ta * vp, g8), v_row_load<VB>(vc + (ta + 1) * vp, g8));
+    const VPair<VB> v1 = v_pair<VB>(v_row_load<VB>(vc + (ta + 8) * vp, g8), v_row_load<VB>(vc + (ta + 9) * vp, g8));
+    const uint32_t s0 = lds_u32(vsc + ta), z0 = lds_u32(vzr + ta);
+    const uint32_t s1 = lds_u32(vsc + ta + 8), z1 = lds_u32(vzr + ta + 8);
+    const uint32_t b0 = FAST ? neg1024(s0) : 0u, b1 = FAST ? neg1024(s1) : 0u;
+    pv_tiles<VB, FAST, 0>(st, v0, v1, s0, b0, z0, s1, b1, z1, pb[ks]);
+  }
+
+  // ---- V outlier channels: O^T row ch += sum_t p_t (original_t - vd_t).
+  // One channel: rows 0 / 8 of the side tile take originals / -vd from lanes
+  // g8 = 0 (one MMA per k-step, flushed when the channel moves).
+  if constexpr (NOUT == 1) {
+    const __half* vo = reinterpret_cast<const __half*>(r + R1.vo);
+    const __half* vdq = reinterpret_cast<const __half*>(r + R1.vd);
+    const bool lead = g8 == 0;
+#pragma unroll
+    for (int ks = 0; ks < 2; ++ks) {
+      const int ta = 16 * ks + 2 * q4;
+      const uint32_t o0 = lead ? lds_u32(vo + ta) : 0u, o1 = lead ? lds_u32(vo + ta + 8) : 0u;
+      const uint32_t n0 = lead ? (lds_u32(vdq + ta) ^ 0x80008000u) : 0u;
+      const uint32_t n1 = lead ? (lds_u32(vdq + ta + 8) ^ 0x80008000u) : 0u;
+      mma_16816(st.vo_acc, o0, n0, o1, n1, pb[ks][0], pb[ks][1]);
+    }
+  }
+  if (NOUT == 2 && n_out > 0) {
+    const int o_vo = up16c(R.ki + 4 * n_out) + up16c(2 * kBlockTokens * n_out);
+    const __half* vo = reinterpret_cast<const __half*>(r + o_vo);
+    const __half* vdq = reinterpret_cast<const __half*>(r + o_vo + up16c(2 * kBlockTokens * n_out));
+    const int16_t* vid = reinterpret_cast<const int16_t*>(r + R.ki + 2 * n_out);
+    for (int j = 0; j < n_out; ++j) {
+      const int ch = vid[j];
+      const bool own = (ch >> 4) == g8;
+      const int hf = ch & 1;
+#pragma unroll
+      for (int ks = 0; ks < 2; ++ks) {
+        const int ta = 16 * ks + 2 * q4;
+        const uint32_t o0 = h2_as_u32(__halves2half2(vo[ta * n_out + j], vo[(ta + 1) * n_out + j]));
+        const uint32_t o1 = h2_as_u32(__halves2half2(vo[(ta + 8) * n_out + j], vo[(ta + 9) * n_out + j]));
+        const uint32_t d0 = h2_as_u32(__halves2half2(vdq[ta * n_out + j], vdq[(ta + 1) * n_out + j]));
+        const uint32_t d1 = h2_as_u32(__halves2half2(vdq[(ta + 8) * n_out + j], vdq[(ta + 9) * n_out + j]));
+        const uint32_t on = own ? 0xFFFFFFFFu : 0u;  // A is zero outside row ch
+        const uint32_t m0 = hf ? 0u : on, m1 = hf ? on : 0u;
+        const uint32_t ao[4] = {o0 & m0, o0 & m1, o1 & m0, o1 & m1};
+        const uint32_t an[4] = {(d0 ^ 0x80008000u) & m0, (d0 ^ 0x80008000u) & m1, (d1 ^ 0x80008000u) & m0,
+                                (d1 ^ 0x80008000u) & m1};
+        outlier_mma(st, (ch & 15) >> 1, ao, an, pb[ks]);
+      }
+    }
+  }
+}
+
+template <int KB, int VB, int NOUT>
 __global__ void __launch_bounds__(kDecodeThreads, 4) mixed_decode_kernel(const DecodeParams p) {
+  constexpr RecLayout R = rec_layout(kHeadDim, KB, VB, 0);
   extern __shared__ __align__(128) unsigned char smem[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g8 = lane >> 2, q4 = lane & 3;
@@ -499,8 +734,11 @@ __global__ void __launch_bounds__(kDecodeThreads, 4) mixed_decode_kernel(const D
 
   const int nh = min(8, p.g - hg * 8);
   const int qh_base = kvh * p.g + hg * 8;
+  const float sl2 = p.scale_log2, lazy_raw = p.lazy_raw;
 
-  // this thread's query column (head g8 of the head group; zero padding beyond nh)
+  // this thread's query column (head g8 of the head group; zero padding beyond nh);
+  // a negative softmax scale is applied as -q (exact) with scale |sm_scale|
+  const uint32_t qflip = p.q_neg ? 0x80008000u : 0u;
   __half qv[32];
   {
     const bool have = g8 < nh;
@@ -508,12 +746,17 @@ __global__ void __launch_bounds__(kDecodeThreads, 4) mixed_decode_kernel(const D
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       uint4 v = have ? ldg_nc_v4(qrow + 8 * k) : make_uint4(0, 0, 0, 0);
+      v.x ^= qflip;
+      v.y ^= qflip;
+      v.z ^= qflip;
+      v.w ^= qflip;
       *reinterpret_cast<uint4*>(qv + 8 * k) = v;
     }
   }
   for (int i = threadIdx.x; i < 8 * kHeadDim; i += blockDim.x) {
     const int h = i / kHeadDim, d = i % kHeadDim;
-    qs[i] = h < nh ? __half2float(p.q[b * p.q_sb + (qh_base + h) * p.q_sh + d]) : 0.f;
+    const float qf = h < nh ? __half2float(p.q[b * p.q_sb + (qh_base + h) * p.q_sh + d]) : 0.f;
+    qs[i] = p.q_neg ? -qf : qf;
   }
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
@@ -531,153 +774,47 @@ __global__ void __launch_bounds__(kDecodeThreads, 4) mixed_decode_kernel(const D
     const int nb = max(0, bhi - blo);
     const uint8_t* wbase = p.warm + b * p.w_sb + kvh * p.w_sh + static_cast<int64_t>(blo) * rec;
 
-    {
-      // warp `warp` owns blocks i = warp + 4*li (li = 0, 1, ...) and stages
-      // warp*3 + li%3; lane 0 keeps up to three of its blocks in flight
-      uint64_t* wbar = full + warp * kStagesPerWarp;
-      unsigned char* wstage = stage0 + warp * kStagesPerWarp * rec;
-      const int nmine = nb > warp ? (nb - warp + kConsumerWarps - 1) / kConsumerWarps : 0;
-      if (lane == 0) {
-        for (int li = 0; li < min(nmine, kStagesPerWarp); ++li) {
-          mbar_arrive_expect_tx(&wbar[li], rec);
-          tma_load_1d(wstage + li * rec, wbase + static_cast<int64_t>(warp + kConsumerWarps * li) * rec, rec,
-                      &wbar[li]);
-        }
+    // warp `warp` owns blocks i = warp + 4*li (li = 0, 1, ...) and stages
+    // warp*3 + li%3; lane 0 keeps up to three of its blocks in flight
+    uint64_t* wbar = full + warp * kStagesPerWarp;
+    unsigned char* wstage = stage0 + warp * kStagesPerWarp * rec;
+    const int nmine = nb > warp ? (nb - warp + kConsumerWarps - 1) / kConsumerWarps : 0;
+    if (lane == 0) {
+      for (int li = 0; li < min(nmine, kStagesPerWarp); ++li) {
+        mbar_arrive_expect_tx(&wbar[li], rec);
+        tma_load_1d(wstage + li * rec, wbase + static_cast<int64_t>(warp + kConsumerWarps * li) * rec, rec,
+                    &wbar[li]);
       }
-      // ---------------- consumers
-      uint32_t qp[16];
-      q_pairs<KB>(qv, qp);
-      const int n_out = p.L.n_outlier;
-      const int kp = kHeadDim * KB / 8, vp = kHeadDim * VB / 8;
-
-      int waited = 0;  // blocks whose copy this warp has seen land
-      for (int li = 0; li < nmine; ++li) {
-        const int s = li % kStagesPerWarp;
-        if (!mbar_wait(&wbar[s], (li / kStagesPerWarp) & 1, p.status)) break;
-        waited = li + 1;
-        const uint8_t* r = wstage + s * rec;
-        const uint8_t* kc = r + p.L.kc;
-        const uint8_t* vc = r + p.L.vc;
-        const __half* vsc = reinterpret_cast<const __half*>(r + p.L.vs);
-        const __half* vzr = reinterpret_cast<const __half*>(r + p.L.vz);
-        const uint32_t mask = lds_u32(r + p.L.mask);
-
-        // ---- S^T = K^ q  (tokens x heads): rows 16mt + 8rr + g8, k-steps over channel pairs
-        KWords<KB> W[2][2];
-#pragma unroll
-        for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-          for (int rr = 0; rr < 2; ++rr) W[mt][rr] = k_words<KB>(kc + (16 * mt + 8 * rr + g8) * kp, q4);
-        float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-        {
-          const uint32_t* ks32 = reinterpret_cast<const uint32_t*>(r + p.L.ks) + 16 * q4;
-          const uint32_t* kz32 = reinterpret_cast<const uint32_t*>(r + p.L.kz) + 16 * q4;
-          uint32_t S8[8], Z8[8];
-          *reinterpret_cast<uint4*>(S8) = lds_v4(ks32);
-          *reinterpret_cast<uint4*>(S8 + 4) = lds_v4(ks32 + 4);
-          *reinterpret_cast<uint4*>(Z8) = lds_v4(kz32);
-          *reinterpret_cast<uint4*>(Z8 + 4) = lds_v4(kz32 + 4);
-          qk_steps<KB, 0, 4>(W, S8, Z8, qp, c);
-          *reinterpret_cast<uint4*>(S8) = lds_v4(ks32 + 8);
-          *reinterpret_cast<uint4*>(S8 + 4) = lds_v4(ks32 + 12);
-          *reinterpret_cast<uint4*>(Z8) = lds_v4(kz32 + 8);
-          *reinterpret_cast<uint4*>(Z8 + 4) = lds_v4(kz32 + 12);
-          qk_steps<KB, 4, 8>(W, S8, Z8, qp, c);
-        }
-        // K outlier channels: their dequantised value is 0 (scale = zero = 0) and the
-        // reference puts the fp16 original there; add q . original with one more MMA
-        // whose k slots 2q4, 2q4+1 are outliers j = 2q4, 2q4+1 (n_outlier <= 8).
-        if (n_out > 0) {
-          const __half* ko = reinterpret_cast<const __half*>(r + p.L.ko);
-          const int16_t* kid = reinterpret_cast<const int16_t*>(r + p.L.ki);
-          const int j0 = 2 * q4, j1 = 2 * q4 + 1;
-          const __half hz = __float2half_rn(0.f);
-          const __half qa = j0 < n_out ? __float2half_rn(qs[g8 * kHeadDim + kid[j0]]) : hz;
-          const __half qb = j1 < n_out ? __float2half_rn(qs[g8 * kHeadDim + kid[j1]]) : hz;
-          const uint32_t bq = h2_as_u32(__halves2half2(qa, qb));
-#pragma unroll
-          for (int mt = 0; mt < 2; ++mt) {
-            uint32_t a[2];
-#pragma unroll
-            for (int rr = 0; rr < 2; ++rr) {
-              const int t = 16 * mt + 8 * rr + g8;
-              const __half oa = j0 < n_out ? ko[t * n_out + j0] : hz;
-              const __half ob = j1 < n_out ? ko[t * n_out + j1] : hz;
-              a[rr] = h2_as_u32(__halves2half2(oa, ob));
-            }
-            mma_16816(c[mt], a[0], a[1], 0u, 0u, bq, 0u);
-          }
-        }
-        float x[2][4];
-        bool valid[2][2];
-#pragma unroll
-        for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-          for (int rr = 0; rr < 2; ++rr) {
-            valid[mt][rr] = (mask >> (16 * mt + 8 * rr + g8)) & 1u;
-#pragma unroll
-            for (int h = 0; h < 2; ++h)
-              x[mt][2 * rr + h] = valid[mt][rr] ? c[mt][2 * rr + h] * p.scale_log2 : -INFINITY;
-          }
-        online_softmax(st, x);
-        uint32_t pb[2][2];
-        p_fragments(x, pb);
-
-        // ---- O^T += V^ P  (head_dim x heads), k-steps of 16 tokens
-#pragma unroll
-        for (int ks = 0; ks < 2; ++ks) {
-          const int ta = 16 * ks + 2 * q4;
-          const VPair<VB> v0 = v_pair<VB>(v_row_load<VB>(vc + ta * vp, g8), v_row_load<VB>(vc + (ta + 1) * vp, g8));
-          const VPair<VB> v1 =
-              v_pair<VB>(v_row_load<VB>(vc + (ta + 8) * vp, g8), v_row_load<VB>(vc + (ta + 9) * vp, g8));
-          const __half2 s0 = *reinterpret_cast<const __half2*>(vsc + ta);
-          const __half2 z0 = *reinterpret_cast<const __half2*>(vzr + ta);
-          const __half2 s1 = *reinterpret_cast<const __half2*>(vsc + ta + 8);
-          const __half2 z1 = *reinterpret_cast<const __half2*>(vzr + ta + 8);
-          pv_tiles<VB, 0>(st, v0, v1, s0, z0, s1, z1, pb[ks]);
-        }
-
-        // ---- V outlier channels: O^T row ch += sum_t p_t (original_t - vd_t)
-        if (n_out > 0) {
-          const __half* vo = reinterpret_cast<const __half*>(r + p.L.vo);
-          const __half* vdq = reinterpret_cast<const __half*>(r + p.L.vd);
-          const int16_t* vid = reinterpret_cast<const int16_t*>(r + p.L.vi);
-          for (int j = 0; j < n_out; ++j) {
-            const int ch = vid[j];
-            const bool own = (ch >> 4) == g8;
-            const int hf = ch & 1;
-#pragma unroll
-            for (int ks = 0; ks < 2; ++ks) {
-              const int ta = 16 * ks + 2 * q4;
-              const uint32_t o0 = h2_as_u32(__halves2half2(vo[ta * n_out + j], vo[(ta + 1) * n_out + j]));
-              const uint32_t o1 = h2_as_u32(__halves2half2(vo[(ta + 8) * n_out + j], vo[(ta + 9) * n_out + j]));
-              const uint32_t d0 = h2_as_u32(__halves2half2(vdq[ta * n_out + j], vdq[(ta + 1) * n_out + j]));
-              const uint32_t d1 = h2_as_u32(__halves2half2(vdq[(ta + 8) * n_out + j], vdq[(ta + 9) * n_out + j]));
-              const uint32_t on = own ? 0xFFFFFFFFu : 0u;  // A is zero outside row ch
-              const uint32_t m0 = hf ? 0u : on, m1 = hf ? on : 0u;
-              const uint32_t ao[4] = {o0 & m0, o0 & m1, o1 & m0, o1 & m1};
-              const uint32_t an[4] = {(d0 ^ 0x80008000u) & m0, (d0 ^ 0x80008000u) & m1, (d1 ^ 0x80008000u) & m0,
-                                      (d1 ^ 0x80008000u) & m1};
-              outlier_mma(st, (ch & 15) >> 1, ao, an, pb[ks]);
-            }
-          }
-        }
-        // refill this stage with the warp's block li+3 once every lane is done reading it
-        __syncwarp();
-        if (lane == 0 && li + kStagesPerWarp < nmine) {
-          fence_proxy_async_shared();
-          mbar_arrive_expect_tx(&wbar[s], rec);
-          tma_load_1d(wstage + s * rec,
-                      wbase + static_cast<int64_t>(warp + kConsumerWarps * (li + kStagesPerWarp)) * rec, rec,
-                      &wbar[s]);
-        }
-      }
-      // after a timed-out wait, let the copies still in flight land before the
-      // stages are reused as epilogue scratch (bounded waits)
-      if (lane == 0)
-        for (int li = waited; li < min(nmine, waited + kStagesPerWarp); ++li)
-          mbar_wait(&wbar[li % kStagesPerWarp], (li / kStagesPerWarp) & 1, p.status);
     }
+    uint32_t qp[16];
+    q_pairs<KB>(qv, qp);
+    const int n_out = p.L.n_outlier;
+
+    int waited = 0;  // blocks whose copy this warp has seen land
+    for (int li = 0; li < nmine; ++li) {
+      const int s = li % kStagesPerWarp;
+      if (!mbar_wait(&wbar[s], (li / kStagesPerWarp) & 1, p.status)) break;
+      waited = li + 1;
+      const uint8_t* r = wstage + s * rec;
+      const uint2 mf = lds_v2(r + R.mask);  // valid-slot mask, decode flags
+      if ((mf.y & 0xFFFFu) == 0x0101u)
+        warm_block<KB, VB, NOUT, true>(st, r, mf.x, qp, qs, n_out, sl2, lazy_raw, g8, q4);
+      else
+        warm_block<KB, VB, NOUT, false>(st, r, mf.x, qp, qs, n_out, sl2, lazy_raw, g8, q4);
+      // refill this stage with the warp's block li+3 once every lane is done reading it
+      __syncwarp();
+      if (lane == 0 && li + kStagesPerWarp < nmine) {
+        fence_proxy_async_shared();
+        mbar_arrive_expect_tx(&wbar[s], rec);
+        tma_load_1d(wstage + s * rec, wbase + static_cast<int64_t>(warp + kConsumerWarps * (li + kStagesPerWarp)) * rec,
+                    rec, &wbar[s]);
+      }
+    }
+    // after a timed-out wait, let the copies still in flight land before the
+    // stages are reused as epilogue scratch (bounded waits)
+    if (lane == 0)
+      for (int li = waited; li < min(nmine, waited + kStagesPerWarp); ++li)
+        mbar_wait(&wbar[li % kStagesPerWarp], (li / kStagesPerWarp) & 1, p.status);
   } else {
     // ---------------- hot CTA: FP16 window, 128-bit loads
     const int hs = split - p.warm_splits;
@@ -685,72 +822,71 @@ __global__ void __launch_bounds__(kDecodeThreads, 4) mixed_decode_kernel(const D
     const int nhb = (nhot_b + 31) / 32;
     const int blo = hs * p.hbps;
     const int bhi = min(nhb, blo + p.hbps);
-    if (warp < kConsumerWarps) {
-      uint32_t qn[16];
+    uint32_t qn[16];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) qn[i] = h2_as_u32(__halves2half2(qv[2 * i], qv[2 * i + 1]));
-      const __half* kb = p.hk + b * p.h_sb + kvh * p.h_sh;
-      const __half* vb = p.hv + b * p.h_sb + kvh * p.h_sh;
-      for (int blk = blo + warp; blk < bhi; blk += kConsumerWarps) {
-        const int t0 = blk * 32;
-        float x[2][4];
-        bool valid[2][2];
+    for (int i = 0; i < 16; ++i) qn[i] = h2_as_u32(__halves2half2(qv[2 * i], qv[2 * i + 1]));
+    const __half* kb = p.hk + b * p.h_sb + kvh * p.h_sh;
+    const __half* vb = p.hv + b * p.h_sb + kvh * p.h_sh;
+    for (int blk = blo + warp; blk < bhi; blk += kConsumerWarps) {
+      const int t0 = blk * 32;
+      float x[2][4];
+      bool valid[2][2];
 #pragma unroll
-        for (int mt = 0; mt < 2; ++mt) {
-          uint32_t e0[16], e1[16];
+      for (int mt = 0; mt < 2; ++mt) {
+        uint32_t e0[16], e1[16];
 #pragma unroll
-          for (int rr = 0; rr < 2; ++rr) {
-            const int t = t0 + 16 * mt + 8 * rr + g8;
-            valid[mt][rr] = t < nhot_b;
-            uint32_t* e = rr ? e1 : e0;
-            const __half* row = kb + static_cast<int64_t>(valid[mt][rr] ? t : 0) * p.h_sn + 32 * q4;
+        for (int rr = 0; rr < 2; ++rr) {
+          const int t = t0 + 16 * mt + 8 * rr + g8;
+          valid[mt][rr] = t < nhot_b;
+          uint32_t* e = rr ? e1 : e0;
+          const __half* row = kb + static_cast<int64_t>(valid[mt][rr] ? t : 0) * p.h_sn + 32 * q4;
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const uint4 v = valid[mt][rr] ? ldg_nc_v4(row + 8 * k) : make_uint4(0, 0, 0, 0);
-              e[4 * k + 0] = v.x;
-              e[4 * k + 1] = v.y;
-              e[4 * k + 2] = v.z;
-              e[4 * k + 3] = v.w;
-            }
+          for (int k = 0; k < 4; ++k) {
+            const uint4 v = valid[mt][rr] ? ldg_nc_v4(row + 8 * k) : make_uint4(0, 0, 0, 0);
+            e[4 * k + 0] = v.x;
+            e[4 * k + 1] = v.y;
+            e[4 * k + 2] = v.z;
+            e[4 * k + 3] = v.w;
           }
-          float c[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-          for (int ks = 0; ks < 8; ++ks)
-            mma_16816(c, e0[2 * ks], e1[2 * ks], e0[2 * ks + 1], e1[2 * ks + 1], qn[2 * ks], qn[2 * ks + 1]);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) x[mt][j] = valid[mt][j >> 1] ? c[j] * p.scale_log2 : -INFINITY;
         }
-        online_softmax(st, x);
-        uint32_t pb[2][2];
-        p_fragments(x, pb);
+        float c[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int ks = 0; ks < 2; ++ks) {
-          uint32_t va[4][8];
+        for (int ks = 0; ks < 8; ++ks)
+          mma_16816(c, e0[2 * ks], e1[2 * ks], e0[2 * ks + 1], e1[2 * ks + 1], qn[2 * ks], qn[2 * ks + 1]);
 #pragma unroll
-          for (int tt = 0; tt < 4; ++tt) {
-            const int t = t0 + 16 * ks + 2 * q4 + (tt & 1) + 8 * (tt >> 1);
-            const bool ok = t < nhot_b;
-            const __half* row = vb + static_cast<int64_t>(ok ? t : 0) * p.h_sn + 16 * g8;
-            const uint4 v0 = ok ? ldg_nc_v4(row) : make_uint4(0, 0, 0, 0);
-            const uint4 v1 = ok ? ldg_nc_v4(row + 8) : make_uint4(0, 0, 0, 0);
-            va[tt][0] = v0.x; va[tt][1] = v0.y; va[tt][2] = v0.z; va[tt][3] = v0.w;
-            va[tt][4] = v1.x; va[tt][5] = v1.y; va[tt][6] = v1.z; va[tt][7] = v1.w;
-          }
+        for (int j = 0; j < 4; ++j) x[mt][j] = valid[mt][j >> 1] ? c[j] : -INFINITY;
+      }
+      online_softmax(st, x, sl2, lazy_raw);
+      uint32_t pb[2][2];
+      p_fragments(x, pb);
 #pragma unroll
-          for (int mt = 0; mt < 8; ++mt) {
-            // channel pair (2mt, 2mt+1) of this thread group's chunk lives in word mt
-            const uint32_t a0 = prmt(va[0][mt], va[1][mt], 0x5410);  // (ta, tb) at channel 2mt
-            const uint32_t a1 = prmt(va[0][mt], va[1][mt], 0x7632);  // (ta, tb) at channel 2mt+1
-            const uint32_t a2 = prmt(va[2][mt], va[3][mt], 0x5410);
-            const uint32_t a3 = prmt(va[2][mt], va[3][mt], 0x7632);
-            mma_16816(st.acc[mt], a0, a1, a2, a3, pb[ks][0], pb[ks][1]);
-          }
+      for (int ks = 0; ks < 2; ++ks) {
+        uint32_t va[4][8];
+#pragma unroll
+        for (int tt = 0; tt < 4; ++tt) {
+          const int t = t0 + 16 * ks + 2 * q4 + (tt & 1) + 8 * (tt >> 1);
+          const bool ok = t < nhot_b;
+          const __half* row = vb + static_cast<int64_t>(ok ? t : 0) * p.h_sn + 16 * g8;
+          const uint4 v0 = ok ? ldg_nc_v4(row) : make_uint4(0, 0, 0, 0);
+          const uint4 v1 = ok ? ldg_nc_v4(row + 8) : make_uint4(0, 0, 0, 0);
+          va[tt][0] = v0.x; va[tt][1] = v0.y; va[tt][2] = v0.z; va[tt][3] = v0.w;
+          va[tt][4] = v1.x; va[tt][5] = v1.y; va[tt][6] = v1.z; va[tt][7] = v1.w;
+        }
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+          // channel pair (2mt, 2mt+1) of this thread group's chunk lives in word mt
+          const uint32_t a0 = prmt(va[0][mt], va[1][mt], 0x5410);  // (ta, tb) at channel 2mt
+          const uint32_t a1 = prmt(va[0][mt], va[1][mt], 0x7632);  // (ta, tb) at channel 2mt+1
+          const uint32_t a2 = prmt(va[2][mt], va[3][mt], 0x5410);
+          const uint32_t a3 = prmt(va[2][mt], va[3][mt], 0x7632);
+          mma_16816(st.acc[mt], a0, a1, a2, a3, pb[ks][0], pb[ks][1]);
         }
       }
     }
   }
 
   // ---------------- epilogue: merge consumer warps, write the split partial
+  if constexpr (NOUT == 1) flush_vout(st, g8, q4);
   __syncthreads();
   warp_to_smem(st, lane, red + warp * 8 * kHeadDim, rm + warp * 8, rl + warp * 8);
   __syncthreads();
@@ -860,15 +996,23 @@ static size_t decode_smem_bytes(int rec_bytes) {
   return 256 + 8 * kHeadDim * 4 + (ring > epi ? ring : epi);
 }
 
-template <int KB, int VB>
-static int launch_decode(const DecodeParams& p, cudaStream_t st) {
+template <int KB, int VB, int NOUT>
+static int launch_decode3(const DecodeParams& p, cudaStream_t st) {
   const size_t smem = decode_smem_bytes(p.L.bytes);
-  auto kern = mixed_decode_kernel<KB, VB>;
+  auto kern = mixed_decode_kernel<KB, VB, NOUT>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
       cudaSuccess)
     return AKV_ERR_LAUNCH;
   kern<<<dim3(p.splits, p.Hkv * p.n_hg, p.B), kDecodeThreads, smem, st>>>(p);
   return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_LAUNCH;
+}
+
+template <int KB, int VB>
+static int launch_decode(const DecodeParams& p, cudaStream_t st) {
+  const int n = p.n_warm_blocks > 0 ? p.L.n_outlier : 0;
+  if (n == 0) return launch_decode3<KB, VB, 0>(p, st);
+  if (n == 1) return launch_decode3<KB, VB, 1>(p, st);
+  return launch_decode3<KB, VB, 2>(p, st);
 }
 
 }  // namespace akv
@@ -914,6 +1058,12 @@ extern "C" int akv_mixed_decode(const uint16_t* q, int64_t q_sb, int64_t q_sh, c
     if (L.key_bits < 2 || L.key_bits > 4 || L.value_bits < 2 || L.value_bits > 4) return AKV_ERR_BITS;
     if (L.n_outlier < 0 || L.n_outlier > kMaxDecodeOutliers) return AKV_ERR_UNSUPPORTED;
     if (L.bytes % 16 || !al(warm, 16) || w_sb % 16 || w_sh % 16) return AKV_ERR_ALIGN;
+    // the kernel addresses record fields at the offsets akv_warm_layout_init gives
+    const RecLayout R = rec_layout(D, L.key_bits, L.value_bits, L.n_outlier);
+    if (L.kc != R.kc || L.vc != R.vc || L.ks != R.ks || L.kz != R.kz || L.vs != R.vs || L.vz != R.vz ||
+        L.mask != R.mask || L.flags != R.flags || L.ki != R.ki || L.vi != R.vi || L.ko != R.ko || L.vo != R.vo ||
+        L.vd != R.vd || L.bytes != R.bytes)
+      return AKV_ERR_UNSUPPORTED;
   }
   if (!workspace) return AKV_ERR_NULL;
   const DecodePlan pl = plan_decode(B, Hq, Hkv, n_hot, n_warm_blocks, n_warm_blocks > 0 ? L.bytes : 1);
@@ -951,7 +1101,9 @@ extern "C" int akv_mixed_decode(const uint16_t* q, int64_t q_sb, int64_t q_sh, c
   p.Hkv = Hkv;
   p.g = Hq / Hkv;
   p.n_hg = pl.n_hg;
-  p.scale_log2 = sm_scale * kLog2e;
+  p.q_neg = sm_scale < 0.f ? 1 : 0;
+  p.scale_log2 = fmaxf(fabsf(sm_scale) * kLog2e, FLT_MIN);
+  p.lazy_raw = kLazyMax / p.scale_log2;
   p.warm_splits = pl.warm_splits;
   p.hot_splits = pl.hot_splits;
   p.wbps = pl.wbps;

@@ -258,8 +258,10 @@ AKV_DEV void load_words(const char* p, uint32_t (&w)[BITS]) {
 //         values: [rows] 16-byte records {z | m, -s' | 1/s' (fp16), -s_eff, 1/s_eff (fp32)}
 //         -- shares its space with norms [H][D] fp32 and score [D] fp32, dead by then
 //   oidx  [kMaxOutliers] int
+//   flg   [H][nblk] u32  nonzero once a scale of that (head, block) is outside
+//                        the decode's two-op dequantisation range
 struct QuantSmem {
-  size_t cz, cs, co, score, oidx, total;
+  size_t cz, cs, co, score, oidx, flg, total;
 };
 
 __host__ __device__ inline QuantSmem quant_smem_layout(int H, int nt, int D, int n_out, bool is_key) {
@@ -273,7 +275,8 @@ __host__ __device__ inline QuantSmem quant_smem_layout(int H, int nt, int D, int
   const size_t nsb = hd * 4 + static_cast<size_t>(D) * 4;
   m.score = m.co + hd * 4;
   m.oidx = m.co + (cob > nsb ? cob : nsb);
-  m.total = m.oidx + kMaxOutliers * 4;
+  m.flg = m.oidx + kMaxOutliers * 4;
+  m.total = m.flg + static_cast<size_t>(H) * ((nt + kBlockTokens - 1) / kBlockTokens) * 4;
   return m;
 }
 
@@ -312,6 +315,9 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
   uint32_t* kr = kns + H * D2;
   uint4* vco = reinterpret_cast<uint4*>(smem_raw + lay.co);       // values
   int* oidx = reinterpret_cast<int*>(smem_raw + lay.oidx);
+  uint32_t* flg = reinterpret_cast<uint32_t*>(smem_raw + lay.flg);
+  if (MODE != kQuantStats)
+    for (int i = tid; i < H * nblk; i += kQuantThreads) flg[i] = 0;  // ordered by the staging barrier below
 
   // ---- stage the group's rows with 1-D bulk TMA (warp 0 issues, all wait)
   __shared__ __align__(8) uint64_t stage_bar;
@@ -516,6 +522,7 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
         sc = affine_scale2<BITS>(lo, reinterpret_cast<const __half2*>(cs)[w]);
       }
       reinterpret_cast<__half2*>(cs)[w] = sc;
+      if (!dq2_scale_ok(__low2half(sc)) || !dq2_scale_ok(__high2half(sc))) flg[h * nblk] = 1u;
       __half m0, n0, r0, m1, n1, r1;
       if (!fast_coef(__low2half(sc), m0, n0, r0)) {
         m0 = n0 = r0 = __ushort_as_half(0);
@@ -554,6 +561,7 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
       const __half lo = __hmin(__low2half(mn), __high2half(mn));
       const __half hi = __hmax(__low2half(mx), __high2half(mx));
       const __half sc = __low2half(affine_scale2<BITS>(__half2half2(lo), __half2half2(hi)));
+      if (!dq2_scale_ok(sc)) flg[(r / nt) * nblk + ((r % nt) >> 5)] = 1u;
       const float se = scale_eff(sc), rc = rcp_exact(se);
       __half fm, fns, fr;
       if (!fast_coef(sc, fm, fns, fr)) {
@@ -665,14 +673,20 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
     }
   }
 
-  // ---- valid-slot masks for the blocks this group wrote
-  if (p.dst.mask.ptr) {
+  // ---- valid-slot masks and decode flags for the blocks this group wrote
+  if (p.dst.mask.ptr || p.dst.flags.ptr) {
     for (int w = tid; w < H * nblk; w += kQuantThreads) {
       const int h = w / nblk, bl = blk0 + w % nblk;
-      const int lo = max(t0, bl * kBlockTokens) - bl * kBlockTokens;
-      const int hi = min(t0 + nt, (bl + 1) * kBlockTokens) - bl * kBlockTokens;  // exclusive
-      const uint32_t m = (hi - lo == 32) ? 0xffffffffu : (((1u << (hi - lo)) - 1u) << lo);
-      *reinterpret_cast<uint32_t*>(vaddr(p.dst.mask, b, h0 + h, bl, 0)) = m;
+      if (p.dst.mask.ptr) {
+        const int lo = max(t0, bl * kBlockTokens) - bl * kBlockTokens;
+        const int hi = min(t0 + nt, (bl + 1) * kBlockTokens) - bl * kBlockTokens;  // exclusive
+        const uint32_t m = (hi - lo == 32) ? 0xffffffffu : (((1u << (hi - lo)) - 1u) << lo);
+        *reinterpret_cast<uint32_t*>(vaddr(p.dst.mask, b, h0 + h, bl, 0)) = m;
+      }
+      if (p.dst.flags.ptr) {  // keys: one scale row per head for all its blocks
+        const uint32_t bad = IS_KEY ? flg[h * nblk] : flg[w];
+        *reinterpret_cast<uint8_t*>(vaddr(p.dst.flags, b, h0 + h, bl, 0)) = bad ? 0 : 1;
+      }
     }
   }
 }

@@ -272,35 +272,25 @@ extern "C" int akv_warm_layout_init(int D, int kb, int vb, int n, akv_warm_layou
   if (!L) return AKV_ERR_NULL;
   if (kb < 2 || kb > 4 || vb < 2 || vb > 4) return AKV_ERR_BITS;
   if (D <= 0 || D % 32 || D > 256 || n < 0 || n > D) return AKV_ERR_SHAPE;
-  auto up16 = [](int x) { return (x + 15) & ~15; };
+  const RecLayout r = rec_layout(D, kb, vb, n);
   L->head_dim = D;
   L->key_bits = kb;
   L->value_bits = vb;
   L->n_outlier = n;
-  int off = 0;
-  L->kc = off;
-  off = up16(off + kBlockTokens * D * kb / 8);
-  L->vc = off;
-  off = up16(off + kBlockTokens * D * vb / 8);
-  L->ks = off;
-  off = up16(off + 2 * D);
-  L->kz = off;
-  off = up16(off + 2 * D);
-  L->vs = off;
-  off = up16(off + 2 * kBlockTokens);
-  L->vz = off;
-  off = up16(off + 2 * kBlockTokens);
-  L->ko = off;
-  off = up16(off + 2 * kBlockTokens * n);
-  L->vo = off;
-  off = up16(off + 2 * kBlockTokens * n);
-  L->vd = off;
-  off = up16(off + 2 * kBlockTokens * n);
-  L->ki = off;                          // n int16 K outlier ids
-  L->vi = off + 2 * n;                  // n int16 V outlier ids
-  L->mask = off + ((4 * n + 3) & ~3);   // u32 valid-slot mask
-  off = up16(L->mask + 4);
-  L->bytes = off;
+  L->kc = r.kc;
+  L->vc = r.vc;
+  L->ks = r.ks;
+  L->kz = r.kz;
+  L->vs = r.vs;
+  L->vz = r.vz;
+  L->mask = r.mask;
+  L->flags = r.flags;
+  L->ki = r.ki;
+  L->vi = r.vi;
+  L->ko = r.ko;
+  L->vo = r.vo;
+  L->vd = r.vd;
+  L->bytes = r.bytes;
   return AKV_OK;
 }
 

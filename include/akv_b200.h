@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define AKV_ABI_VERSION 1
+#define AKV_ABI_VERSION 2
 #define AKV_BLOCK_TOKENS 32 /* tokens per warm block record */
 
 enum {
@@ -65,12 +65,19 @@ int akv_abi_version(void);
  *       zeroed V outlier channel dequantise to; attention adds
  *       p . (original - vd) so it sees the original
  *   mask  u32 bitmask of valid token slots
- * All offsets are multiples of 16 bytes and `bytes` (the record stride) is a
- * multiple of 16 so records can be moved with 1-D bulk TMA copies.
+ *   flags u8[4]: byte 0 = 1 when every K scale of the record, byte 1 = 1
+ *       when every V scale, is +0 or lies in [2^-14, 65504/1024]; for such
+ *       scales the decode dequantises exactly with two fused fp16 ops per
+ *       code pair (other records take a four-op path with the same result)
+ * Field order: kc, vc, ks, kz, vs, vz, mask, flags, ki, vi, ko, vo, vd, so
+ * for a given (head_dim, key_bits, value_bits) every field up to ki sits at
+ * a fixed offset.  kc..vz, ko, vo, vd start on 16-byte boundaries and
+ * `bytes` (the record stride) is a multiple of 16 so records can be moved
+ * with 1-D bulk TMA copies.
  * ---------------------------------------------------------------------- */
 typedef struct {
   int32_t head_dim, key_bits, value_bits, n_outlier;
-  int32_t kc, vc, ks, kz, vs, vz, ko, vo, vd, ki, vi, mask, bytes;
+  int32_t kc, vc, ks, kz, vs, vz, ko, vo, vd, ki, vi, mask, flags, bytes;
 } akv_warm_layout;
 
 /* Fill `out` for the given shape.  Returns AKV_ERR_SHAPE / AKV_ERR_BITS on bad input. */
@@ -93,9 +100,12 @@ typedef struct {
  *   out_idx      n int16 per (b, h, blk) (sslot unused)
  *   out_vdq      values only: n fp16 per token, the dequantised code value of
  *                each (zeroed) outlier channel (the warm record's vd field)
- *   mask         u32 per (b, h, blk): bit s set for each slot this call wrote */
+ *   mask         u32 per (b, h, blk): bit s set for each slot this call wrote
+ *   flags        u8 per (b, h, blk) (sslot unused): 1 when every scale this
+ *                call wrote into that block is +0 or in [2^-14, 65504/1024],
+ *                else 0 (the warm record's flags byte 0 for keys, 1 for values) */
 typedef struct {
-  akv_view codes, scale, zero, out_data, out_idx, out_vdq, mask;
+  akv_view codes, scale, zero, out_data, out_idx, out_vdq, mask, flags;
 } akv_qdest;
 
 /* ------------------------------------------------------------------------

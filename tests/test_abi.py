@@ -40,7 +40,7 @@ def test_ctypes_table_matches_header():
 def test_version_and_strerror():
     from akv import _C
     lib = _C.load()
-    assert lib.akv_abi_version() == 1
+    assert lib.akv_abi_version() == 2
     assert _C.strerror(0) == "ok"
     for code in range(-1, -9, -1):
         assert _C.strerror(code) != "unknown status"
@@ -53,9 +53,10 @@ def test_layout_offsets_aligned():
             for n in (0, 1, 3, 8):
                 L = _C.warm_layout(128, kb, vb, n)
                 assert L.bytes % 16 == 0
-                for f in ("kc", "vc", "ks", "kz", "vs", "vz", "ko", "vo", "ki"):
+                for f in ("kc", "vc", "ks", "kz", "vs", "vz", "mask", "ko", "vo", "vd"):
                     assert getattr(L, f) % 16 == 0, f
-                assert L.mask % 4 == 0 and L.mask + 4 <= L.bytes
+                assert L.mask % 16 == 0 and L.flags == L.mask + 4 and L.ki == L.mask + 8
+                assert L.vi == L.ki + 2 * n and L.vi + 2 * n <= L.ko
                 assert L.vc == 32 * 128 * kb // 8
 
 
