@@ -27,7 +27,8 @@ class View(ctypes.Structure):
 
 class QDest(ctypes.Structure):
     """akv_qdest: where one quantiser call writes (or one dequantiser call reads)."""
-    _fields_ = [(n, View) for n in ("codes", "scale", "zero", "out_data", "out_idx", "out_vdq", "mask", "flags")]
+    _fields_ = [(n, View) for n in ("codes", "scale", "zero", "out_data", "out_idx", "out_vdq", "mask", "flags")] + \
+        [("pair_order", c_int32)]
 
 
 class WarmLayout(ctypes.Structure):

@@ -25,6 +25,27 @@ from .bitpack import packed_width
 BLOCK = _C.BLOCK_TOKENS
 
 
+def key_scale_channels(bits: int, head_dim: int) -> list:
+    """Channel stored in each slot of a warm record's K scale / zero field.
+
+    Records keep the per-channel K scale and zero of every 32-channel chunk in
+    the decode kernel's pair order (include/akv_b200.h, ``akv_warm_layout``):
+    slot 2i / 2i+1 of a chunk hold channels a / b of pair i.
+    """
+    out = []
+    for base in range(0, head_dim, 32):
+        for i in range(16):
+            j = i % 8
+            if bits == 4:
+                a = 8 * (i // 4) + ((i % 4) ^ 1)
+                b = a + 4
+            else:
+                a = 16 * (i // 8) + ((3 - j if j < 4 else 11 - j) if bits == 2 else 7 - j)
+                b = a + 8
+            out += [base + a, base + b]
+    return out
+
+
 def measure_packed_bytes(qdata: dict, bits: int) -> int:
     """Bytes a quantiser call's output occupies (reference packed_layout.py:501-543)."""
     if "codes" not in qdata:
@@ -73,6 +94,7 @@ class WarmArena:
         d = _C.QDest()
         n = self.n_out
         if is_key:
+            d.pair_order = 1  # records keep K scale / zero in the decode pair order
             d.codes = _C.View(base + L.kc, sb, sh, rec, packed_width(self.D, self.key_bits))
             d.scale = _C.View(base + L.ks, sb, sh, rec, 0)
             d.zero = _C.View(base + L.kz, sb, sh, rec, 0)

@@ -28,6 +28,38 @@ struct RecLayout {
 
 __host__ __device__ constexpr int up16c(int x) { return (x + 15) & ~15; }
 
+// Decode pair order of a key chunk.  The decode kernel turns the packed K
+// codes of 32 channels (one 16/12/8-byte chunk of a token row) into 16 fp16
+// pairs with one LOP3 "magic" each; pair i holds channels (a, b) =
+// key_pair(bits, i) of the chunk, chosen so that both codes sit in the low 10
+// bits of their 16-bit half (4 bits: nibbles n and n+4 of a byte pair; 2/3
+// bits: codes 8 apart).  Warm records store the K scale and zero of each
+// chunk in this order (word i = (channel a, channel b)), so the decoder reads
+// each pair's scale and zero with one load.
+struct PairIdx {
+  int a, b;
+};
+
+__host__ __device__ constexpr PairIdx key_pair(int bits, int i) {
+  const int j = i % 8;
+  if (bits == 4) {
+    const int a = 8 * (i / 4) + ((i % 4) ^ 1);
+    return PairIdx{a, a + 4};
+  }
+  const int a = 16 * (i / 8) + (bits == 2 ? (j < 4 ? 3 - j : 11 - j) : 7 - j);
+  return PairIdx{a, a + 8};
+}
+
+// slot (0..31) of channel c (0..31) of a chunk in the decode pair order
+__host__ __device__ constexpr int key_pair_slot(int bits, int c) {
+  for (int i = 0; i < 16; ++i) {
+    const PairIdx p = key_pair(bits, i);
+    if (p.a == c) return 2 * i;
+    if (p.b == c) return 2 * i + 1;
+  }
+  return -1;
+}
+
 __host__ __device__ constexpr RecLayout rec_layout(int D, int kb, int vb, int n) {
   RecLayout r{};
   r.kc = 0;

@@ -102,19 +102,6 @@ AKV_DEV uint32_t dqx(uint32_t x, uint32_t s, uint32_t b, uint32_t z) {
 // The channel order inside a chunk is permuted per bit width (kPairs*), with
 // the magic multiplier of each pair in kMult*; the query fragment uses the
 // same permutation.
-struct PairIdx {
-  int a, b;
-};
-
-__device__ constexpr PairIdx kPairs4[16] = {{1, 5},   {0, 4},   {3, 7},   {2, 6},   {9, 13},  {8, 12},
-                                            {11, 15}, {10, 14}, {17, 21}, {16, 20}, {19, 23}, {18, 22},
-                                            {25, 29}, {24, 28}, {27, 31}, {26, 30}};
-__device__ constexpr PairIdx kPairs2[16] = {{3, 11},  {2, 10},  {1, 9},   {0, 8},   {7, 15},  {6, 14},
-                                            {5, 13},  {4, 12},  {19, 27}, {18, 26}, {17, 25}, {16, 24},
-                                            {23, 31}, {22, 30}, {21, 29}, {20, 28}};
-__device__ constexpr PairIdx kPairs3[16] = {{7, 15},  {6, 14},  {5, 13},  {4, 12},  {3, 11},  {2, 10},
-                                            {1, 9},   {0, 8},   {23, 31}, {22, 30}, {21, 29}, {20, 28},
-                                            {19, 27}, {18, 26}, {17, 25}, {16, 24}};
 __device__ constexpr int kMult4[16] = {1, 16, 1, 16, 1, 16, 1, 16, 1, 16, 1, 16, 1, 16, 1, 16};
 __device__ constexpr int kMult2[16] = {1, 4, 16, 64, 256, 4, 16, 64, 1, 4, 16, 64, 256, 4, 16, 64};
 __device__ constexpr int kMult3[16] = {1, 8, 64, 1, 8, 1, 8, 64, 1, 8, 64, 1, 8, 1, 8, 64};
@@ -123,7 +110,7 @@ __device__ constexpr int kMult3[16] = {1, 8, 64, 1, 8, 1, 8, 64, 1, 8, 64, 1, 8,
 // every pair permutation and magic multiplier is a constant in the code.
 template <int KB>
 AKV_DEV constexpr PairIdx kpair(int i) {
-  return KB == 4 ? kPairs4[i] : (KB == 2 ? kPairs2[i] : kPairs3[i]);
+  return key_pair(KB, i);
 }
 template <int BITS>
 AKV_DEV constexpr int kmult(int i) {
@@ -201,14 +188,6 @@ AKV_DEV uint32_t k_raw(const KWords<KB>& kw) {
   }
 }
 
-// (scale or zero of channel A, of channel B) from the 8 natural-order words
-// (16 channels) of the chunk half that holds both channels.
-template <int A, int B>
-AKV_DEV __half2 pick2(const uint32_t (&S8)[8]) {
-  constexpr uint32_t sel = ((A & 1) ? 0x32u : 0x10u) | (((B & 1) ? 0x76u : 0x54u) << 8);
-  return u32_as_h2(prmt(S8[(A % 16) / 2], S8[(B % 16) / 2], sel));
-}
-
 template <int KB, int I = 0>
 AKV_DEV void q_pairs(const __half (&qv)[32], uint32_t (&qp)[16]) {
   if constexpr (I < 16) {
@@ -219,16 +198,17 @@ AKV_DEV void q_pairs(const __half (&qv)[32], uint32_t (&qp)[16]) {
 }
 
 // q.K^T k-steps KS..KEND-1: per step, two channel pairs of the 4 token rows,
-// dequantised exactly, into the two m-tile accumulators.
+// dequantised exactly, into the two m-tile accumulators.  ks2 / kz2 point at
+// this thread's chunk of the record's K scale / zero (decode pair order), so
+// each step reads its two (scale, zero) pairs with two 8-byte loads.
 template <int KB, bool FAST, int KS, int KEND>
-AKV_DEV void qk_steps(const KWords<KB> (&W)[2][2], const uint32_t (&S8)[8], const uint32_t (&Z8)[8],
-                      const uint32_t (&qp)[16], float (&c)[2][4]) {
+AKV_DEV void qk_steps(const KWords<KB> (&W)[2][2], const uint2* ks2, const uint2* kz2, const uint32_t (&qp)[16],
+                      float (&c)[2][4]) {
   if constexpr (KS < KEND) {
     constexpr int I0 = 2 * KS, I1 = 2 * KS + 1;
-    constexpr PairIdx p0 = kpair<KB>(I0), p1 = kpair<KB>(I1);
     constexpr int M0 = kmult<KB>(I0), M1 = kmult<KB>(I1);
-    const uint32_t s0 = h2_as_u32(pick2<p0.a, p0.b>(S8)), z0 = h2_as_u32(pick2<p0.a, p0.b>(Z8));
-    const uint32_t s1 = h2_as_u32(pick2<p1.a, p1.b>(S8)), z1 = h2_as_u32(pick2<p1.a, p1.b>(Z8));
+    const uint2 sp = ks2[KS], zp = kz2[KS];
+    const uint32_t s0 = sp.x, s1 = sp.y, z0 = zp.x, z1 = zp.y;
     const uint32_t b0 = FAST ? neg1024(s0) : 0u, b1 = FAST ? neg1024(s1) : 0u;
 #pragma unroll
     for (int mt = 0; mt < 2; ++mt) {
@@ -238,7 +218,7 @@ AKV_DEV void qk_steps(const KWords<KB> (&W)[2][2], const uint32_t (&S8)[8], cons
       const uint32_t a3 = dqx<M1, FAST>(k_raw<KB, I1>(W[mt][1]), s1, b1, z1);
       mma_16816(c[mt], a0, a1, a2, a3, qp[I0], qp[I1]);
     }
-    qk_steps<KB, FAST, KS + 1, KEND>(W, S8, Z8, qp, c);
+    qk_steps<KB, FAST, KS + 1, KEND>(W, ks2, kz2, qp, c);
   }
 }
 
@@ -590,21 +570,8 @@ AKV_DEV void warm_block(WarpState& st, const uint8_t* r, uint32_t mask, const ui
 #pragma unroll
     for (int rr = 0; rr < 2; ++rr) W[mt][rr] = k_words<KB>(r + R.kc + (16 * mt + 8 * rr + g8) * kp, q4);
   float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-  {
-    const uint32_t* ks32 = reinterpret_cast<const uint32_t*>(r + R.ks) + 16 * q4;
-    const uint32_t* kz32 = reinterpret_cast<const uint32_t*>(r + R.kz) + 16 * q4;
-    uint32_t S8[8], Z8[8];
-    *reinterpret_cast<uint4*>(S8) = lds_v4(ks32);
-    *reinterpret_cast<uint4*>(S8 + 4) = lds_v4(ks32 + 4);
-    *reinterpret_cast<uint4*>(Z8) = lds_v4(kz32);
-    *reinterpret_cast<uint4*>(Z8 + 4) = lds_v4(kz32 + 4);
-    qk_steps<KB, FAST, 0, 4>(W, S8, Z8, qp, c);
-    *reinterpret_cast<uint4*>(S8) = lds_v4(ks32 + 8);
-    *reinterpret_cast<uint4*>(S8 + 4) = lds_v4(ks32 + 12);
-    *reinterpret_cast<uint4*>(Z8) = lds_v4(kz32 + 8);
-    *reinterpret_cast<uint4*>(Z8 + 4) = lds_v4(kz32 + 12);
-    qk_steps<KB, FAST, 4, 8>(W, S8, Z8, qp, c);
-  }
+  qk_steps<KB, FAST, 0, 8>(W, reinterpret_cast<const uint2*>(r + R.ks) + 8 * q4,
+                           reinterpret_cast<const uint2*>(r + R.kz) + 8 * q4, qp, c);
   // K outlier channels: their dequantised value is 0 (scale = zero = 0) and the
   // reference puts the fp16 original there.  One channel: + q[ch] * original
   // per logit.  General: one more MMA whose k slots 2q4, 2q4+1 are outliers

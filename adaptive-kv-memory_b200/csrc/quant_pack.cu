@@ -535,9 +535,26 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
       km[w] = h2_as_u32(__halves2half2(m0, m1));
       kns[w] = h2_as_u32(__halves2half2(n0, n1));
       kr[w] = h2_as_u32(__halves2half2(r0, r1));
-      for (int bl = 0; bl < nblk; ++bl) {
-        if (sv.ptr) reinterpret_cast<__half2*>(vaddr(sv, b, h0 + h, blk0 + bl, 0))[dp] = sc;
-        if (zv.ptr) reinterpret_cast<__half2*>(vaddr(zv, b, h0 + h, blk0 + bl, 0))[dp] = lo;
+      if (p.dst.pair_order) {  // warm records: each 32-channel chunk in the decode pair order
+        const int c0 = 2 * dp, base = c0 & ~31;
+        const int s0 = base + key_pair_slot(BITS, c0 & 31), s1 = base + key_pair_slot(BITS, (c0 + 1) & 31);
+        for (int bl = 0; bl < nblk; ++bl) {
+          if (sv.ptr) {
+            __half* o = reinterpret_cast<__half*>(vaddr(sv, b, h0 + h, blk0 + bl, 0));
+            o[s0] = __low2half(sc);
+            o[s1] = __high2half(sc);
+          }
+          if (zv.ptr) {
+            __half* o = reinterpret_cast<__half*>(vaddr(zv, b, h0 + h, blk0 + bl, 0));
+            o[s0] = __low2half(lo);
+            o[s1] = __high2half(lo);
+          }
+        }
+      } else {
+        for (int bl = 0; bl < nblk; ++bl) {
+          if (sv.ptr) reinterpret_cast<__half2*>(vaddr(sv, b, h0 + h, blk0 + bl, 0))[dp] = sc;
+          if (zv.ptr) reinterpret_cast<__half2*>(vaddr(zv, b, h0 + h, blk0 + bl, 0))[dp] = lo;
+        }
       }
     }
   } else {
@@ -818,8 +835,16 @@ __global__ void dequantize_kernel(const DequantParams p) {
     if constexpr (IS_KEY) {
       const __half* sc = reinterpret_cast<const __half*>(vaddr(p.src.scale, b, h, blk, 0)) + su * 32;
       const __half* zr = reinterpret_cast<const __half*>(vaddr(p.src.zero, b, h, blk, 0)) + su * 32;
+      if (p.src.pair_order) {  // warm records: decode pair order within the chunk
 #pragma unroll
-      for (int k = 0; k < 32; ++k) o[k] = __hadd_rn(__hmul_rn(__uint2half_rn(c[k]), sc[k]), zr[k]);
+        for (int k = 0; k < 32; ++k) {
+          const int sl = key_pair_slot(BITS, k);
+          o[k] = __hadd_rn(__hmul_rn(__uint2half_rn(c[k]), sc[sl]), zr[sl]);
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < 32; ++k) o[k] = __hadd_rn(__hmul_rn(__uint2half_rn(c[k]), sc[k]), zr[k]);
+      }
     } else {
       const __half sc = *reinterpret_cast<const __half*>(vaddr(p.src.scale, b, h, blk, slot));
       const __half zr = *reinterpret_cast<const __half*>(vaddr(p.src.zero, b, h, blk, slot));

@@ -57,7 +57,12 @@ int akv_abi_version(void);
  * those 32 tokens:
  *   kc  K codes   [32][D*kbits/8]  u8  (akv/bitpack.py layout along D)
  *   vc  V codes   [32][D*vbits/8]  u8
- *   ks  K scale   [D]  fp16   kz  K zero [D]  fp16  (per channel, per group)
+ *   ks  K scale   [D]  fp16   kz  K zero [D]  fp16  (per channel, per group;
+ *       within each 32-channel chunk in the decode pair order: word i holds
+ *       channels (a, b) with, for chunk-local i = 0..15,
+ *         4 bits: a = 8*(i/4) + ((i%4)^1),             b = a + 4
+ *         2 bits: a = 16*(i/8) + (i%8 < 4 ? 3 : 11) - i%8, b = a + 8
+ *         3 bits: a = 16*(i/8) + 7 - i%8,               b = a + 8)
  *   vs  V scale   [32] fp16   vz  V zero [32] fp16  (per token)
  *   ko  K outlier data [32][n] fp16     vo  V outlier data [32][n] fp16
  *   ki  K outlier channel ids [n] int16 vi  V outlier channel ids [n] int16
@@ -103,9 +108,12 @@ typedef struct {
  *   mask         u32 per (b, h, blk): bit s set for each slot this call wrote
  *   flags        u8 per (b, h, blk) (sslot unused): 1 when every scale this
  *                call wrote into that block is +0 or in [2^-14, 65504/1024],
- *                else 0 (the warm record's flags byte 0 for keys, 1 for values) */
+ *                else 0 (the warm record's flags byte 0 for keys, 1 for values)
+ *   pair_order   keys: 0 = scale / zero in channel order; 1 = in the warm
+ *                record's decode pair order (see akv_warm_layout) */
 typedef struct {
   akv_view codes, scale, zero, out_data, out_idx, out_vdq, mask, flags;
+  int32_t pair_order;
 } akv_qdest;
 
 /* ------------------------------------------------------------------------

@@ -158,6 +158,7 @@ def test_warm_arena_groups_vs_oracle(kb, vb, frac):
     np.testing.assert_array_equal(_bits16(_np(dk)), _bits16(O.dequantize_groups(gk)))
     np.testing.assert_array_equal(_bits16(_np(dv)), _bits16(O.dequantize_groups(gv)))
     # raw record fields == oracle dict fields
+    from akv.packed_layout import key_scale_channels
     L = arena.layout
     buf = _np(arena.buf)
     dpk, dpv = O.packed_width(D, kb), O.packed_width(D, vb)
@@ -168,8 +169,16 @@ def test_warm_arena_groups_vs_oracle(kb, vb, frac):
                 rec = buf[b, h, j]
                 np.testing.assert_array_equal(rec[L.kc:L.kc + nt * dpk].reshape(nt, dpk), qk["codes"][h])
                 np.testing.assert_array_equal(rec[L.vc:L.vc + nt * dpv].reshape(nt, dpv), qv["codes"][h])
-                np.testing.assert_array_equal(rec[L.ks:L.ks + 2 * D].view(np.uint16), _bits16(qk["scale"][h, 0]))
+                # K scale / zero in the decode pair order
+                perm = key_scale_channels(kb, D)
+                np.testing.assert_array_equal(rec[L.ks:L.ks + 2 * D].view(np.uint16), _bits16(qk["scale"][h, 0])[perm])
+                np.testing.assert_array_equal(rec[L.kz:L.kz + 2 * D].view(np.uint16), _bits16(qk["zero"][h, 0])[perm])
                 np.testing.assert_array_equal(rec[L.vs:L.vs + 2 * nt].view(np.uint16), _bits16(qv["scale"][h, :, 0]))
+                # decode flags: 1 where every scale is +0 or in [2^-14, 65504/1024]
+                def dq2_ok(bits16):
+                    return bool(np.all((bits16 == 0) | ((bits16 >= 0x0400) & (bits16 <= 0x53FF))))
+                assert rec[L.flags] == dq2_ok(_bits16(qk["scale"][h, 0]))
+                assert rec[L.flags + 1] == dq2_ok(_bits16(qv["scale"][h, :, 0]))
                 mask = int(rec[L.mask:L.mask + 4].view(np.uint32)[0])
                 assert mask == (0xFFFFFFFF if nt == 32 else (1 << nt) - 1)
                 if frac > 0:

@@ -90,6 +90,7 @@ def test_large_demotion_event_into_arena_vs_oracle():
     arena.append(torch.from_numpy(hot_k).to(DEV), torch.from_numpy(hot_v).to(DEV), group=10 ** 9,
                  tok_idx=torch.from_numpy(idx).to(DEV))
     dk, dv = arena.dequantize(n_tokens=n_ev)
+    from akv.packed_layout import key_scale_channels
     L = arena.layout
     buf = _np(arena.buf)
     for b in range(B):
@@ -100,7 +101,8 @@ def test_large_demotion_event_into_arena_vs_oracle():
         for h in range(H):  # the group's key scale sits in every block record it covers
             for blk in range(arena.n_blocks):
                 rec = buf[b, h, blk]
-                np.testing.assert_array_equal(rec[L.ks:L.ks + 2 * D].view(np.uint16), _bits16(rk["scale"][h, 0]))
+                np.testing.assert_array_equal(rec[L.ks:L.ks + 2 * D].view(np.uint16),
+                                              _bits16(rk["scale"][h, 0])[key_scale_channels(4, D)])
                 np.testing.assert_array_equal(rec[L.ki:L.ki + 2].view(np.int16), rk["outlier_idx"])
 
 
