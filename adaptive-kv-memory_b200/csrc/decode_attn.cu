@@ -703,6 +703,37 @@ __global__ void __launch_bounds__(kDecodeThreads, 4) mixed_decode_kernel(const D
   const int qh_base = kvh * p.g + hg * 8;
   const float sl2 = p.scale_log2, lazy_raw = p.lazy_raw;
 
+  WarpState st;
+  state_init(st);
+
+  // warm CTAs: every warp initialises its own stage barriers and puts its
+  // first blocks in flight before anything else, so the query loads below
+  // overlap the first copies instead of preceding them
+  int nmine = 0;
+  const uint8_t* wbase = nullptr;
+  uint64_t* wbar = full + warp * kStagesPerWarp;
+  unsigned char* wstage = stage0 + warp * kStagesPerWarp * rec;
+  if (warm_cta) {
+    const int nblk_b = p.warm_len ? min(p.warm_len[b], p.n_warm_blocks) : p.n_warm_blocks;
+    const int blo = split * p.wbps;
+    const int bhi = min(nblk_b, blo + p.wbps);
+    const int nb = max(0, bhi - blo);
+    wbase = p.warm + b * p.w_sb + kvh * p.w_sh + static_cast<int64_t>(blo) * rec;
+    // warp `warp` owns blocks i = warp + 4*li (li = 0, 1, ...) and stages
+    // warp*kStagesPerWarp + li%kStagesPerWarp; lane 0 keeps them in flight
+    nmine = nb > warp ? (nb - warp + kConsumerWarps - 1) / kConsumerWarps : 0;
+    if (lane == 0) {
+      for (int s = 0; s < kStagesPerWarp; ++s) mbar_init(&wbar[s], 1);
+      fence_mbar_init();
+      for (int li = 0; li < min(nmine, kStagesPerWarp); ++li) {
+        mbar_arrive_expect_tx(&wbar[li], rec);
+        tma_load_1d(wstage + li * rec, wbase + static_cast<int64_t>(warp + kConsumerWarps * li) * rec, rec,
+                    &wbar[li]);
+      }
+    }
+    __syncwarp();
+  }
+
   // this thread's query column (head g8 of the head group; zero padding beyond nh);
   // a negative softmax scale is applied as -q (exact) with scale |sm_scale|
   const uint32_t qflip = p.q_neg ? 0x80008000u : 0u;
@@ -720,39 +751,17 @@ __global__ void __launch_bounds__(kDecodeThreads, 4) mixed_decode_kernel(const D
       *reinterpret_cast<uint4*>(qv + 8 * k) = v;
     }
   }
-  for (int i = threadIdx.x; i < 8 * kHeadDim; i += blockDim.x) {
-    const int h = i / kHeadDim, d = i % kHeadDim;
-    const float qf = h < nh ? __half2float(p.q[b * p.q_sb + (qh_base + h) * p.q_sh + d]) : 0.f;
-    qs[i] = p.q_neg ? -qf : qf;
-  }
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
-    fence_mbar_init();
+  if (warp == 0) {  // fp32 copy of the head group's queries for the outlier terms
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float4 f = make_float4(__half2float(qv[4 * k]), __half2float(qv[4 * k + 1]), __half2float(qv[4 * k + 2]),
+                                   __half2float(qv[4 * k + 3]));
+      *reinterpret_cast<float4*>(qs + g8 * kHeadDim + 32 * q4 + 4 * k) = f;
+    }
   }
   __syncthreads();
 
-  WarpState st;
-  state_init(st);
-
   if (warm_cta) {
-    const int nblk_b = p.warm_len ? min(p.warm_len[b], p.n_warm_blocks) : p.n_warm_blocks;
-    const int blo = split * p.wbps;
-    const int bhi = min(nblk_b, blo + p.wbps);
-    const int nb = max(0, bhi - blo);
-    const uint8_t* wbase = p.warm + b * p.w_sb + kvh * p.w_sh + static_cast<int64_t>(blo) * rec;
-
-    // warp `warp` owns blocks i = warp + 4*li (li = 0, 1, ...) and stages
-    // warp*3 + li%3; lane 0 keeps up to three of its blocks in flight
-    uint64_t* wbar = full + warp * kStagesPerWarp;
-    unsigned char* wstage = stage0 + warp * kStagesPerWarp * rec;
-    const int nmine = nb > warp ? (nb - warp + kConsumerWarps - 1) / kConsumerWarps : 0;
-    if (lane == 0) {
-      for (int li = 0; li < min(nmine, kStagesPerWarp); ++li) {
-        mbar_arrive_expect_tx(&wbar[li], rec);
-        tma_load_1d(wstage + li * rec, wbase + static_cast<int64_t>(warp + kConsumerWarps * li) * rec, rec,
-                    &wbar[li]);
-      }
-    }
     uint32_t qp[16];
     q_pairs<KB>(qv, qp);
     const int n_out = p.L.n_outlier;
