@@ -50,14 +50,12 @@ __host__ __device__ constexpr PairIdx key_pair(int bits, int i) {
   return PairIdx{a, a + 8};
 }
 
-// slot (0..31) of channel c (0..31) of a chunk in the decode pair order
+// slot (0..31) of channel c (0..31) of a chunk in the decode pair order (the
+// inverse of key_pair in closed form: channel c is the a (b) member of pair i
+// and sits in slot 2i (2i + 1))
 __host__ __device__ constexpr int key_pair_slot(int bits, int c) {
-  for (int i = 0; i < 16; ++i) {
-    const PairIdx p = key_pair(bits, i);
-    if (p.a == c) return 2 * i;
-    if (p.b == c) return 2 * i + 1;
-  }
-  return -1;
+  if (bits == 4) return 2 * (4 * (c >> 3) + ((c & 3) ^ 1)) + ((c & 7) >> 2);
+  return 2 * (8 * (c >> 4) + ((c & 7) ^ (bits == 2 ? 3 : 7))) + ((c & 15) >> 3);
 }
 
 __host__ __device__ constexpr RecLayout rec_layout(int D, int kb, int vb, int n) {

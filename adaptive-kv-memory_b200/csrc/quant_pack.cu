@@ -209,6 +209,36 @@ AKV_DEV void store_packed8(char* p, uint32_t w) {
   }
 }
 
+// Runs body(x, c, t) for the tokens t = sub, sub + step, ... < nt of one
+// encode work item: x = the item's 8 staged channels of token t, c = where its
+// packed codes go (nullptr: codes not written).  Both pointers advance by
+// increments; a group longer than one block moves c to the next block record
+// each time the slot passes 31.
+template <typename Body>
+AKV_DEV void walk_tokens(int sub, int nt, int step, const __half* xcol, int D, char* cbase, const akv_view& cv,
+                         Body&& body) {
+  const __half* x = xcol + sub * D;
+  const int xstep = step * D;
+  if (!cbase) {
+#pragma unroll 4
+    for (int t = sub; t < nt; t += step, x += xstep) body(x, static_cast<char*>(nullptr), t);
+    return;
+  }
+  char* c = cbase + (sub >> 5) * cv.sblk + (sub & 31) * cv.sslot;
+  const int64_t cstep = static_cast<int64_t>(step) * cv.sslot;
+  if (nt <= kBlockTokens) {  // one block record
+#pragma unroll 4
+    for (int t = sub; t < nt; t += step, x += xstep, c += cstep) body(x, c, t);
+    return;
+  }
+  const int64_t cwrap = cv.sblk - kBlockTokens * cv.sslot;
+  int slot = sub & 31;
+  for (int t = sub; t < nt; t += step, x += xstep, c += cstep) {
+    body(x, c, t);
+    for (slot += step; slot >= kBlockTokens; slot -= kBlockTokens) c += cwrap;
+  }
+}
+
 template <int BITS>
 AKV_DEV void unpack32(const uint32_t (&w)[BITS], uint32_t (&c)[32]) {
   if constexpr (BITS == 4) {
@@ -248,6 +278,31 @@ template <int BITS>
 AKV_DEV void load_words(const char* p, uint32_t (&w)[BITS]) {
 #pragma unroll
   for (int k = 0; k < BITS; ++k) w[k] = reinterpret_cast<const uint32_t*>(p)[k];
+}
+
+// Column statistics of one stats work item: 8 channels over n staged tokens
+// `stride` halves apart: sums of squares (fp32, for the outlier norms) and,
+// for keys, min / max.
+template <bool IS_KEY, bool NORMS>
+AKV_DEV void column_stats(const __half* x, int n, int stride, uint64_t (&s2)[4], __half2 (&mn)[4], __half2 (&mx)[4]) {
+#pragma unroll 4
+  for (int t = 0; t < n; ++t, x += stride) {
+    const uint4 v = lds_v4(x);
+    const uint32_t x4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const __half2 xh = u32_as_h2(x4[i]);
+      if constexpr (NORMS) {
+        const float2 f = __half22float2(xh);
+        const uint64_t f2 = f2_make(f.x, f.y);
+        s2[i] = f2_fma(f2, f2, s2[i]);
+      }
+      if constexpr (IS_KEY) {
+        mn[i] = __hmin2(mn[i], xh);
+        mx[i] = __hmax2(mx[i], xh);
+      }
+    }
+  }
 }
 
 // Shared memory of one quantiser CTA (byte offsets; rows = H * nt):
@@ -372,23 +427,10 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
         mn[i] = __float2half2_rn(INFINITY);
         mx[i] = __float2half2_rn(-INFINITY);
       }
-      for (int t = half; t < nt; t += 2) {
-        const uint4 v = lds_v4(base + t * D);
-        const uint32_t x4[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const __half2 x = u32_as_h2(x4[i]);
-          if (want_norms) {
-            const float2 f = __half22float2(x);
-            const uint64_t f2 = f2_make(f.x, f.y);
-            s2[i] = f2_fma(f2, f2, s2[i]);
-          }
-          if constexpr (IS_KEY) {
-            mn[i] = __hmin2(mn[i], x);
-            mx[i] = __hmax2(mx[i], x);
-          }
-        }
-      }
+      if (want_norms)
+        column_stats<IS_KEY, true>(base + half * D, (nt - half + 1) >> 1, 2 * D, s2, mn, mx);
+      else
+        column_stats<IS_KEY, false>(base + half * D, (nt - half + 1) >> 1, 2 * D, s2, mn, mx);
       float s[8];
       if (want_norms) {
 #pragma unroll
@@ -631,13 +673,13 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
           for (int i = 0; i < 4; ++i) fast = fast && (m2[i] & 0x7FFFu) && (m2[i] & 0x7FFF0000u);
         }
         if (fast) {
-          for (int t = sub; t < nt; t += tpc) {
-            uint32_t x2[4];
-            lds_u32x4(xcol + t * D, x2);
+          walk_tokens(sub, nt, tpc, xcol, D, cbase, cv, [&](const __half* x, char* c, int) {
+            uint32_t x2[4], mm[4];
+            lds_u32x4(x, x2);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) m[i] = encode_pair16<BITS>(x2[i], z2[i], m2[i], ns2[i], r2[i]);
-            if (cbase) store_packed8<BITS>(cbase + (t >> 5) * cv.sblk + (t & 31) * cv.sslot, pack8<BITS>(m));
-          }
+            for (int i = 0; i < 4; ++i) mm[i] = encode_pair16<BITS>(x2[i], z2[i], m2[i], ns2[i], r2[i]);
+            if (c) store_packed8<BITS>(c, pack8<BITS>(mm));
+          });
         } else {
           uint32_t s2[4];
           uint64_t nsf[4], rf[4];
@@ -648,25 +690,26 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
             nsf[i] = f2_make(-s0, -s1);
             rf[i] = f2_make(rcp_exact(s0), rcp_exact(s1));
           }
-          for (int t = sub; t < nt; t += tpc) {
-            uint32_t x2[4];
-            lds_u32x4(xcol + t * D, x2);
+          walk_tokens(sub, nt, tpc, xcol, D, cbase, cv, [&](const __half* x, char* c, int) {
+            uint32_t x2[4], mm[4];
+            lds_u32x4(x, x2);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) m[i] = encode_pair<BITS>(x2[i], z2[i], nsf[i], rf[i]);
-            if (cbase) store_packed8<BITS>(cbase + (t >> 5) * cv.sblk + (t & 31) * cv.sslot, pack8<BITS>(m));
-          }
+            for (int i = 0; i < 4; ++i) mm[i] = encode_pair<BITS>(x2[i], z2[i], nsf[i], rf[i]);
+            if (c) store_packed8<BITS>(c, pack8<BITS>(mm));
+          });
         }
       } else if (all_fast) {
-        for (int t = sub; t < nt; t += tpc) {
-          const uint2 rec = *reinterpret_cast<const uint2*>(vco + h * nt + t);
-          uint32_t x2[4];
-          lds_u32x4(xcol + t * D, x2);
+        const uint4* vrow = vco + h * nt;
+        walk_tokens(sub, nt, tpc, xcol, D, cbase, cv, [&](const __half* x, char* c, int t) {
+          const uint2 rec = *reinterpret_cast<const uint2*>(vrow + t);
+          uint32_t x2[4], mm[4];
+          lds_u32x4(x, x2);
           const uint32_t z2 = prmt(rec.x, rec.x, 0x1010), m2 = prmt(rec.x, rec.x, 0x3232);
           const uint32_t ns2 = prmt(rec.y, rec.y, 0x1010), r2 = prmt(rec.y, rec.y, 0x3232);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) m[i] = encode_pair16<BITS>(x2[i], z2, m2, ns2, r2);
-          if (cbase) store_packed8<BITS>(cbase + (t >> 5) * cv.sblk + (t & 31) * cv.sslot, pack8<BITS>(m));
-        }
+          for (int i = 0; i < 4; ++i) mm[i] = encode_pair16<BITS>(x2[i], z2, m2, ns2, r2);
+          if (c) store_packed8<BITS>(c, pack8<BITS>(mm));
+        });
       } else {
         for (int t = sub; t < nt; t += tpc) {
           const uint4 rec = vco[h * nt + t];
