@@ -874,20 +874,53 @@ __global__ void __launch_bounds__(kDecodeThreads, 4) mixed_decode_kernel(const D
 // relative to m (log2 units).  Row r, split s lives at part + s*ss + r*sr.
 // Writes any of: fp16 out[r*o_sr + d], natural-log lse[r], and the merged
 // partial record merged[r*(D+2) + ...] (for a further cross-GPU combine).
+constexpr int kCombineMaxSplits = 256;  // splits merged per pass (larger counts loop)
+
 __global__ void lse_combine_kernel(const float* __restrict__ part, int64_t ss, int64_t sr, int rows, int splits,
                                    int D, __half* out, int64_t o_sr, float* lse, float* merged) {
+  // one CTA per row: warp 0 turns the splits' (m, l) into weights
+  // w_s = 2^(m_s - M) in shared memory once; every thread then sums one
+  // channel over the splits with independent loads in flight
+  __shared__ float w[kCombineMaxSplits];
+  __shared__ float sM, sL;
   const int r = blockIdx.x;
   if (r >= rows) return;
   const float* base = part + static_cast<int64_t>(r) * sr;
-  float M = -INFINITY;
-  for (int s = 0; s < splits; ++s) M = fmaxf(M, base[s * ss + D]);
-  const float mb = (M == -INFINITY) ? 0.f : M;
-  float L = 0.f;
-  for (int s = 0; s < splits; ++s) L += base[s * ss + D + 1] * exp2f(base[s * ss + D] - mb);
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x < 32) {
+    float M = -INFINITY;
+    for (int s = lane; s < splits; s += 32) M = fmaxf(M, base[s * ss + D]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    const float mb = (M == -INFINITY) ? 0.f : M;
+    float L = 0.f;
+    for (int s = lane; s < splits; s += 32) {
+      const float ws = exp2f(base[s * ss + D] - mb);
+      if (s < kCombineMaxSplits) w[s] = ws;
+      L += base[s * ss + D + 1] * ws;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+    if (lane == 0) {
+      sM = M;
+      sL = L;
+    }
+  }
+  __syncthreads();
+  const float M = sM, L = sL, mb = (M == -INFINITY) ? 0.f : M;
   const float inv = L > 0.f ? 1.f / L : 0.f;
   for (int d = threadIdx.x; d < D; d += blockDim.x) {
     float o = 0.f;
-    for (int s = 0; s < splits; ++s) o += base[s * ss + d] * exp2f(base[s * ss + D] - mb);
+    const float* col = base + d;
+    int s = 0;
+    for (; s + 8 <= splits && s + 8 <= kCombineMaxSplits; s += 8) {
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = col[(s + j) * ss];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o = fmaf(v[j], w[s + j], o);
+    }
+    for (; s < splits; ++s) o = fmaf(col[s * ss], s < kCombineMaxSplits ? w[s] : exp2f(base[s * ss + D] - mb), o);
     if (out) out[static_cast<int64_t>(r) * o_sr + d] = __float2half_rn(o * inv);
     if (merged) merged[static_cast<int64_t>(r) * (D + 2) + d] = o;
   }
