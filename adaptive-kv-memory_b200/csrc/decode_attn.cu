@@ -945,6 +945,11 @@ struct DecodePlan {
 // wave leaves SMs idle at the end of the launch); config 3 (128 units) gets
 // 18 splits: 2,304 CTAs, 3.9 waves.
 constexpr int kDecodeSlots = 148 * 4;  // 148 SMs x 4 resident decode CTAs
+// Device time per byte of a hot CTA relative to a warm one: a hot warp streams
+// plain fp16 rows (16 KB per 32-token block, two DRAM round trips, little
+// arithmetic) while a warm warp dequantises ~3.9 KB records, so hot splits
+// take proportionally more bytes.
+constexpr double kHotCost = 0.75;
 
 static void split_shares(int per_unit, int n_warm_blocks, int nhb, double wbytes, double hbytes, DecodePlan& pl) {
   const double tot = wbytes + hbytes;
@@ -977,7 +982,7 @@ static DecodePlan plan_decode(int B, int Hq, int Hkv, int n_hot, int n_warm_bloc
   const int units = B * Hkv * pl.n_hg;
   const int nhb = (n_hot + 31) / 32;
   const double wbytes = static_cast<double>(n_warm_blocks) * rec_bytes;
-  const double hbytes = static_cast<double>(nhb) * 32 * kHeadDim * 4;
+  const double hbytes = static_cast<double>(nhb) * 32 * kHeadDim * 4 * kHotCost;
   int lo, hi;
   per_unit_range(units, lo, hi);
   double best = -1.0;
