@@ -60,6 +60,17 @@ except ImportError:  # transformers absent: plain containers with the same surfa
             return 0 if self.keys is None else self.keys.shape[-2]
 
 
+def _to_device(t: torch.Tensor, device: torch.device) -> torch.Tensor:
+    """A small CPU index tensor on ``device`` without a stream sync: staged in
+    pinned memory and copied asynchronously (a copy from pageable memory
+    waits for the stream first)."""
+    if t.device == device:
+        return t
+    if device.type == "cuda":
+        return t.pin_memory().to(device, non_blocking=True)
+    return t.to(device)
+
+
 # presets of the reference (drop_in.py:89-126)
 _PRESETS = {
     "quality": {"warm_bits": 4, "hot_budget": 256, "description": "Near-lossless 4-bit. +1-2% PPL."},
@@ -83,7 +94,7 @@ class AKVLayer(_LayerBase):
                  per_head_bits: Optional[list] = None, enable_promotion_proxy: bool = True,
                  proxy_decay: float = 0.7, adaptive_hot_frac: float = 0.0,
                  warm_key_bits: Optional[int] = None, warm_value_bits: Optional[int] = None,
-                 outlier_fraction: float = 0.0):
+                 outlier_fraction: float = 0.0, fused_decode: bool = False):
         try:
             super().__init__()
         except TypeError:
@@ -105,11 +116,21 @@ class AKVLayer(_LayerBase):
         self.warm_value_bits = warm_value_bits or warm_bits
         self.outlier_fraction = outlier_fraction
         self.per_head_bits = None
+        # decode steps (one new token) return a placeholder instead of the
+        # chronological FP16 view; the "akv" attention function
+        # (akv.hf_attention) attends over the packed warm records and the hot
+        # tier in place
+        self.fused_decode = fused_decode
 
         self._hot_keys: Optional[torch.Tensor] = None
         self._hot_values: Optional[torch.Tensor] = None
         self._warm_keys_fp16: Optional[torch.Tensor] = None  # exact dequantisation of the warm records
         self._warm_values_fp16: Optional[torch.Tensor] = None
+        # capacity buffers behind the two tensors above: appends write in place
+        # (doubling on overflow) instead of re-concatenating the whole warm copy
+        self._warm_kbuf: Optional[torch.Tensor] = None
+        self._warm_vbuf: Optional[torch.Tensor] = None
+        self._nan: Optional[torch.Tensor] = None  # one-element source of the fused-decode placeholder
         self._warm: Optional[WarmArena] = None  # packed warm block records (source of truth)
         self._warm_slots: Optional[torch.Tensor] = None  # arena slot (blk*32 + s) of each warm token
         self._warm_len = 0
@@ -157,19 +178,42 @@ class AKVLayer(_LayerBase):
         arena = self._warm
         nblk = (n + BLOCK - 1) // BLOCK
         arena.grow(arena.n_blocks + nblk)
-        idx_dev = demote_idx.to(hk.device)
+        idx_dev = _to_device(demote_idx, hk.device)
         blk0 = arena.append(hk, hv, group=n, tok_idx=idx_dev)
         slots = torch.arange(blk0 * BLOCK, blk0 * BLOCK + n, dtype=torch.int64, device=hk.device)
         dk, dv = arena.dequantize(tok_idx=slots)
         # the reference's measure_packed_bytes of this event's K and V dicts (drop_in.py:331-336)
         kb, vb = self.warm_key_bits, self.warm_value_bits
         self._warm_bytes_packed += B * (H * n * packed_width(D, kb) + 4 * H * D + H * n * packed_width(D, vb) + 4 * H * n)
-        if self._warm_keys_fp16 is None:
-            self._warm_keys_fp16, self._warm_values_fp16, self._warm_slots = dk, dv, slots
-        else:
-            self._warm_keys_fp16 = torch.cat([self._warm_keys_fp16, dk], dim=2)
-            self._warm_values_fp16 = torch.cat([self._warm_values_fp16, dv], dim=2)
-            self._warm_slots = torch.cat([self._warm_slots, slots])
+        self._append_warm_fp16(dk, dv)
+        self._warm_slots = slots if self._warm_slots is None else torch.cat([self._warm_slots, slots])
+
+    def _append_warm_fp16(self, dk: torch.Tensor, dv: torch.Tensor) -> None:
+        """Append dequantised warm rows to the FP16 working copy.
+
+        The copy lives at the front of capacity buffers; an append that fits
+        writes only the new rows.  A copy that is no longer a view of the
+        buffers (after promotion or a batch op rebuilt it) is moved into new
+        buffers of twice the needed capacity first."""
+        old_k, old_v = self._warm_keys_fp16, self._warm_values_fp16
+        n_old = 0 if old_k is None else old_k.shape[2]
+        n = n_old + dk.shape[2]
+        kb = self._warm_kbuf
+        in_buf = (old_k is None or (kb is not None and old_k.data_ptr() == kb.data_ptr()
+                                    and old_k.shape[:2] == kb.shape[:2]))
+        if kb is None or not in_buf or n > kb.shape[2] or kb.shape[:2] != dk.shape[:2]:
+            cap = max(2 * n, 64)
+            B, H, _, D = dk.shape
+            kb = torch.empty(B, H, cap, D, dtype=dk.dtype, device=dk.device)
+            vb = torch.empty(B, H, cap, D, dtype=dv.dtype, device=dv.device)
+            if n_old:
+                kb[:, :, :n_old].copy_(old_k)
+                vb[:, :, :n_old].copy_(old_v)
+            self._warm_kbuf, self._warm_vbuf = kb, vb
+        self._warm_kbuf[:, :, n_old:n].copy_(dk)
+        self._warm_vbuf[:, :, n_old:n].copy_(dv)
+        self._warm_keys_fp16 = self._warm_kbuf[:, :, :n]
+        self._warm_values_fp16 = self._warm_vbuf[:, :, :n]
 
     def _remove_warm(self, promote_mask: torch.Tensor, n_promote: int, warm_len: int) -> None:
         """Drop promoted tokens from the warm tier (records keep the bytes, mask bits cleared)."""
@@ -317,22 +361,46 @@ class AKVLayer(_LayerBase):
                 self._proxy_score = torch.cat([self._proxy_score.to(pad.device), pad])
             keep = torch.ones(hot_len, dtype=torch.bool)
             keep[demote_idx] = False
-            keep_dev = keep.to(self._hot_keys.device)
-            self._hot_keys = self._hot_keys[:, :, keep_dev, :]
-            self._hot_values = self._hot_values[:, :, keep_dev, :]
+            kept_dev = _to_device(keep.nonzero().squeeze(1), self._hot_keys.device)
+            self._hot_keys = self._hot_keys.index_select(2, kept_dev)
+            self._hot_values = self._hot_values.index_select(2, kept_dev)
             self._hot_positions = self._hot_positions[keep]
             if self._importance is not None:
                 self._importance = self._importance[keep]
 
-        if self._warm_keys_fp16 is not None:
-            full_k = torch.cat([self._warm_keys_fp16, self._hot_keys], dim=2)
-            full_v = torch.cat([self._warm_values_fp16, self._hot_values], dim=2)
-            order = torch.cat([self._warm_positions, self._hot_positions]).argsort().to(full_k.device)
-            full_k = full_k.index_select(2, order)
-            full_v = full_v.index_select(2, order)
-        else:
-            full_k, full_v = self._hot_keys, self._hot_values
-        return self._publish(full_k, full_v)
+        if self.fused_decode and N == 1 and self._warm_keys_fp16 is not None:
+            return self._publish(*self._placeholder())
+        return self._publish(*self.full_view())
+
+    def full_view(self) -> Tuple[torch.Tensor, torch.Tensor]:
+        """The chronologically sorted [warm; hot] FP16 K/V (drop_in.py:753-787)."""
+        if self._warm_keys_fp16 is None:
+            return self._hot_keys, self._hot_values
+        full_k = torch.cat([self._warm_keys_fp16, self._hot_keys], dim=2)
+        full_v = torch.cat([self._warm_values_fp16, self._hot_values], dim=2)
+        order = torch.cat([self._warm_positions, self._hot_positions]).argsort().to(full_k.device)
+        return full_k.index_select(2, order), full_v.index_select(2, order)
+
+    def _placeholder(self) -> Tuple[torch.Tensor, torch.Tensor]:
+        """What a fused decode step returns instead of the view: NaN-filled
+        zero-stride tensors of the view's shape, the key tagged with this
+        layer.  Only the "akv" attention function reads the tag; any other
+        attention over them produces NaN, never a silently wrong result."""
+        hk = self._hot_keys
+        if self._nan is None or self._nan.dtype != hk.dtype or self._nan.device != hk.device:
+            self._nan = torch.full((1, 1, 1, 1), float("nan"), dtype=hk.dtype, device=hk.device)
+        B, H, _, D = hk.shape
+        n = hk.shape[2] + self._warm_keys_fp16.shape[2]
+        k = self._nan.expand(B, H, n, D)
+        v = self._nan.expand(B, H, n, D)
+        k._akv_layer = self
+        return k, v
+
+    def decode_attention(self, query: torch.Tensor, sm_scale: Optional[float] = None) -> torch.Tensor:
+        """One decode query (B, Hq, 1, D) over the packed warm records and the
+        FP16 hot tier, in place (akv_mixed_decode).  Returns (B, Hq, 1, D)."""
+        from .fused_attention import mixed_tier_decode_attention
+        return mixed_tier_decode_attention(query, self._hot_keys, self._hot_values, self._warm, sm_scale=sm_scale)
 
     # ------------------------------------------------------------------ accounting
     def memory_usage_bytes(self) -> dict:
@@ -376,7 +444,7 @@ class AKVCache(_CacheBase):
                  protect_first: int = 0, protect_last: int = 0, protect_layers: Optional[list] = None,
                  num_hidden_layers: Optional[int] = None, enable_promotion: bool = True,
                  promotion_threshold: float = 0.05, enable_promotion_proxy: bool = True,
-                 proxy_decay: float = 0.7, adaptive_hot_frac: float = 0.0):
+                 proxy_decay: float = 0.7, adaptive_hot_frac: float = 0.0, fused_decode: bool = False):
         if preset is not None:
             if preset not in _PRESETS:
                 raise ValueError(f"Unknown preset {preset!r}. Choose from: {sorted(_PRESETS.keys())}")
@@ -402,6 +470,7 @@ class AKVCache(_CacheBase):
         self.enable_promotion_proxy = enable_promotion_proxy
         self.proxy_decay = proxy_decay
         self.adaptive_hot_frac = adaptive_hot_frac
+        self.fused_decode = fused_decode
         self._protect_first = protect_first
         self._protect_last = protect_last
         self._protect_explicit = list(protect_layers) if protect_layers else []
@@ -443,7 +512,8 @@ class AKVCache(_CacheBase):
                         promotion_threshold=self.promotion_threshold,
                         enable_promotion_proxy=self.enable_promotion_proxy, proxy_decay=self.proxy_decay,
                         adaptive_hot_frac=self.adaptive_hot_frac, warm_key_bits=self.warm_key_bits,
-                        warm_value_bits=self.warm_value_bits, outlier_fraction=self.outlier_fraction)
+                        warm_value_bits=self.warm_value_bits, outlier_fraction=self.outlier_fraction,
+                        fused_decode=self.fused_decode)
 
     def update(self, key_states: torch.Tensor, value_states: torch.Tensor, layer_idx: int,
                cache_kwargs: Optional[dict[str, Any]] = None, *args, **kwargs) -> Tuple[torch.Tensor, torch.Tensor]:
@@ -480,7 +550,10 @@ class AKVCache(_CacheBase):
             if layer._warm is not None and arena_index is not None:
                 layer._warm.select_batch(arena_index)
             if layer.keys is not None and layer._hot_keys is not None:
-                layer.keys, layer.values = fn(layer.keys), fn(layer.values)
+                if getattr(layer.keys, "_akv_layer", None) is not None:
+                    layer.keys, layer.values = layer._placeholder()
+                else:
+                    layer.keys, layer.values = fn(layer.keys), fn(layer.values)
 
     def reorder_cache(self, beam_idx: torch.LongTensor):
         self._each_batch(lambda t: t.index_select(0, beam_idx.to(t.device)), beam_idx)

@@ -77,10 +77,14 @@ __host__ __device__ constexpr RecLayout rec_layout(int D, int kb, int vb, int n)
   return r;
 }
 
-// Bounded spin limit for every mbarrier wait (each try_wait may itself
-// suspend the thread for a while).  A wait that runs out records
-// AKV_ERR_TIMEOUT in the status word and the kernel stops issuing work.
-constexpr uint32_t kSpinLimit = 1u << 22;
+// Every mbarrier wait is bounded in time: after kWaitLimitNs of global-timer
+// time without the phase completing it records AKV_ERR_TIMEOUT in the status
+// word and the kernel stops issuing work.  Each try_wait asks the hardware to
+// suspend the waiting thread for up to kSuspendHintNs (it resumes as soon as
+// the phase completes), so waiting warps leave the issue slots to the warps
+// that have work instead of spinning.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+constexpr uint32_t kSuspendHintNs = 1000000u;     // 1 ms
 
 // ---------------------------------------------------------------- status
 AKV_DEV void set_status(int* status, int code) {
@@ -117,21 +121,32 @@ AKV_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
       : "memory");
   return ok != 0;
 }
 
-// Bounded wait: returns false (and records a timeout) if the phase never completes.
+AKV_DEV uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait: returns false (and records a timeout) if the phase does not
+// complete within kWaitLimitNs.
 AKV_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int* status) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      set_status(status, AKV_ERR_TIMEOUT);
+      return false;
+    }
   }
-  set_status(status, AKV_ERR_TIMEOUT);
-  return false;
+  return true;
 }
 
 // Order this thread's earlier generic-proxy shared-memory accesses before

@@ -189,6 +189,90 @@ def migration_bench(torch, akv, dev) -> dict:
             "cold_bytes": cb}
 
 
+# ---------------------------------------------------------------------------- HF decoding (config 2)
+def hf_decode_bench(torch, akv, dev, new_tokens: int = 256, prompt: int = 32768) -> dict:
+    """Config 2 end to end: a Qwen2.5-1.5B-shaped random-init decoder (28
+    layers, hidden 1536, 12 Q / 2 KV heads, vocab 151936, fp16), greedy
+    decoding of `new_tokens` after a `prompt`-token prompt of seeded random
+    ids, batch 1.  Arms on the same model and prompt:
+      view:    AKVCache (3-bit warm tier, 1024-token hot window) returning the
+               chronological FP16 view, SDPA over it (the reference data flow);
+      fused:   AKVCache(fused_decode=True) + the "akv" attention hook (decode
+               reads the packed warm records and the hot tier in place);
+      dynamic: transformers' DynamicCache, uncompressed FP16, SDPA (context).
+    Each arm's decode loop is timed with CUDA events after a synchronize, so
+    host work (HF's Python, the cache's tier bookkeeping) is included.  SDPA
+    runs on its flash / memory-efficient backends in every arm."""
+    from transformers import DynamicCache, Qwen2Config, Qwen2ForCausalLM
+    import akv.hf_attention as hook
+    hook.register()
+    torch.manual_seed(0)
+    cfg = Qwen2Config(vocab_size=151936, hidden_size=1536, intermediate_size=8960, num_hidden_layers=28,
+                      num_attention_heads=12, num_key_value_heads=2, max_position_embeddings=131072,
+                      rope_theta=1e6, rms_norm_eps=1e-6, tie_word_embeddings=True)
+    with torch.device(dev):
+        model = Qwen2ForCausalLM(cfg).half().eval()
+    g = torch.Generator(device=dev).manual_seed(2)
+    ids = torch.randint(0, cfg.vocab_size, (1, prompt), generator=g, device=dev)
+
+    def make_cache(mode):
+        model.config._attn_implementation = "akv" if mode == "fused" else "sdpa"
+        if mode == "dynamic":
+            return DynamicCache()
+        return akv.AKVCache(warm_bits=3, hot_budget=1024, num_hidden_layers=cfg.num_hidden_layers,
+                            enable_promotion=False, enable_promotion_proxy=False, fused_decode=(mode == "fused"))
+
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+    # torch's cuDNN SDPA backend re-plans on every new KV length (~1 ms of host
+    # time per call at decode); the SDPA arms use flash / memory-efficient
+    sdpa_backends = [SDPBackend.FLASH_ATTENTION, SDPBackend.EFFICIENT_ATTENTION, SDPBackend.MATH]
+
+    def decode(mode, prompt_ids, n):
+        with sdpa_kernel(sdpa_backends):
+            return _decode(mode, prompt_ids, n)
+
+    def _decode(mode, prompt_ids, n):
+        cache = make_cache(mode)
+        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        seq = []
+        with torch.no_grad():
+            torch.cuda.synchronize()
+            p0.record()
+            out = model(input_ids=prompt_ids, past_key_values=cache, use_cache=True, logits_to_keep=1)
+            p1.record()
+            tok = out.logits[:, -1].argmax(-1, keepdim=True)
+            torch.cuda.synchronize()
+            e0.record()
+            for _ in range(n):
+                out = model(input_ids=tok, past_key_values=cache, use_cache=True, logits_to_keep=1)
+                tok = out.logits[:, -1].argmax(-1, keepdim=True)
+                seq.append(tok)
+            e1.record()
+            torch.cuda.synchronize()
+        del cache, out
+        torch.cuda.empty_cache()
+        return p0.elapsed_time(p1), e0.elapsed_time(e1), torch.cat(seq, 1)
+
+    modes = ("dynamic", "view", "fused")
+    for mode in modes:  # warm-up: kernels, allocator pools, HF's first-call paths
+        decode(mode, ids[:, :4096], 4)
+    res, toks = {}, {}
+    for mode in modes:
+        pre_ms, ms, toks[mode] = decode(mode, ids, new_tokens)
+        res[f"{mode}_tok_s"] = round(new_tokens / (ms * 1e-3), 1)
+        res[f"{mode}_ms_per_token"] = round(ms / new_tokens, 3)
+        res[f"{mode}_prefill_ms"] = round(pre_ms, 1)
+    model.config._attn_implementation = "sdpa"
+    res["greedy_match_fused_vs_view"] = round((toks["view"] == toks["fused"]).float().mean().item(), 4)
+    res["speedup_fused_vs_view"] = round(res["fused_tok_s"] / res["view_tok_s"], 3)
+    res = {"workload": f"qwen2.5-1.5b-shaped random-init decoder, prompt {prompt}, greedy {new_tokens} tokens, "
+                       "batch 1, AKVCache 3-bit warm + 1024 hot (promotion off)", **res}
+    del model
+    torch.cuda.empty_cache()
+    return res
+
+
 # ---------------------------------------------------------------------------- our arm
 def run_ours(args):
     import torch
@@ -367,6 +451,10 @@ def run_ours(args):
         }
         if world == 1 and not args.no_migration:
             res["migration"] = migration_bench(torch, akv, dev)
+        if world == 1 and args.hf_tokens > 0:
+            del arenas, hot_k, hot_v, graph
+            torch.cuda.empty_cache()
+            res["hf_decode"] = hf_decode_bench(torch, akv, dev, new_tokens=args.hf_tokens)
         if world == 1 and not args.no_cpu_baseline:
             res["cpu_baseline"] = cpu_baseline(units=args.cpu_units, world=1)
         print(json.dumps(res), flush=True)
@@ -452,6 +540,8 @@ def main():
     ap.add_argument("--cpu-units", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-migration", action="store_true")
+    ap.add_argument("--hf-tokens", type=int, default=256,
+                    help="config-2 HF greedy decoding length (0: skip the end-to-end model run)")
     ap.add_argument("--batch", type=int, default=CFG["B"],
                     help="batch rows (default: config 3's 16; smaller only for profiler captures)")
     args = ap.parse_args()

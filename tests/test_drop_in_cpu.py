@@ -119,3 +119,56 @@ def test_for_model_and_recommend_preset(tiny_llama):
     assert c.num_hidden_layers == 2 and c._protected_set == {1}
     rec = recommend_preset(model)
     assert rec["preset"] in ("quality", "balanced")
+
+
+def test_akv_attention_registered_and_sdpa_equivalent_without_warm(tiny_llama):
+    """The "akv" attention implementation: without a warm tier (nothing
+    demoted) every call is SDPA over the returned K/V, so generation is
+    bit-identical to attn_implementation="sdpa"."""
+    import akv.hf_attention as hook
+    from transformers import AttentionInterface
+    assert hook.register() == "akv"
+    assert AttentionInterface._global_mapping["akv"] is hook.akv_attention_forward
+    cfg, model = tiny_llama
+    ids = torch.tensor([[3, 1, 4, 1, 5, 9, 2, 6]])
+    impl = model.config._attn_implementation
+    try:
+        with torch.no_grad():
+            model.config._attn_implementation = "sdpa"
+            ref = _generate(model, AKVCache(warm_bits=4, hot_budget=4096, enable_promotion=False), ids)
+            model.config._attn_implementation = "akv"
+            cache = AKVCache(warm_bits=4, hot_budget=4096, enable_promotion=False, fused_decode=True)
+            got = _generate(model, cache, ids)
+    finally:
+        model.config._attn_implementation = impl
+    assert torch.equal(ref, got)
+    assert getattr(cache.layers[0].keys, "_akv_layer", None) is None  # no warm tier: the view is returned
+
+
+def test_fused_placeholder_and_warm_append_on_cpu():
+    """Fused-decode placeholder (NaN, zero-stride, tagged) and the in-place
+    warm-copy append, with the warm tier filled by hand (demotion itself
+    needs CUDA).  The tagged decode call raises on CPU: no CPU fallback."""
+    import akv.hf_attention as hook
+    from akv import AKVLayer
+    layer = AKVLayer(warm_bits=3, hot_budget=8, enable_promotion=False, enable_promotion_proxy=False,
+                     fused_decode=True)
+    g = torch.Generator().manual_seed(0)
+    chunks = [torch.randn(1, 2, n, 128, generator=g).half() for n in (5, 40, 3)]
+    for c in chunks:
+        layer._append_warm_fp16(c, -c)
+    want = torch.cat(chunks, 2)
+    assert torch.equal(layer._warm_keys_fp16, want) and torch.equal(layer._warm_values_fp16, -want)
+    assert layer._warm_keys_fp16.data_ptr() == layer._warm_kbuf.data_ptr()
+    layer._warm_keys_fp16 = layer._warm_keys_fp16[:, :, 1:].clone()  # rebuilt elsewhere (promotion)
+    layer._warm_values_fp16 = layer._warm_values_fp16[:, :, 1:].clone()
+    layer._append_warm_fp16(chunks[0], -chunks[0])
+    assert torch.equal(layer._warm_keys_fp16, torch.cat([want[:, :, 1:], chunks[0]], 2))
+    layer._hot_keys = torch.randn(1, 2, 8, 128, generator=g).half()
+    layer._hot_values = layer._hot_keys.clone()
+    k, v = layer._placeholder()
+    assert k.shape == (1, 2, 8 + 52, 128) and k.untyped_storage().nbytes() == 2  # one fp16 element
+    assert torch.isnan(k).all() and k._akv_layer is layer
+    q = torch.randn(1, 4, 1, 128).half()
+    with pytest.raises(RuntimeError):
+        hook.akv_attention_forward(None, q, k, v, None, scaling=128 ** -0.5)

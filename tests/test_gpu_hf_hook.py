@@ -1,0 +1,153 @@
+"""GPU: the "akv" HuggingFace attention hook over AKVCache(fused_decode=True).
+
+A decode step of a fused cache attends over the packed warm records and the
+hot tier in place (akv.hf_attention).  Checked against the reference data
+flow (drop_in.py:753-787): SDPA over the chronological [dequantised warm;
+hot] FP16 view that a non-fused AKVCache returns.
+
+* per call: on every decode step of a Qwen2-shaped model, the hook's output
+  equals SDPA over the same layer's full view within the attention bar;
+* end to end: teacher-forced decoding through the fused cache gives the same
+  logits as the view cache, within a tolerance that allows each layer's
+  attention to differ by the attention bar.
+"""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda:0"
+ATOL = 2e-3
+
+
+def _excess(out, ref):
+    """max over elements of |out - ref| - tol(ref), the attention bar of the
+    decode tests: 2e-3, or the fp16 output's half-ulp + 1e-3 where |ref| >= 4."""
+    ulp = torch.abs(ref).half().float()
+    ulp = torch.nextafter(ulp.half(), torch.tensor(float("inf"), dtype=torch.float16, device=ref.device)).float() - ulp
+    tol = torch.clamp(0.5 * ulp + 1e-3, min=ATOL)
+    return ((out - ref).abs() - tol).max().item()
+
+
+def _model(layers=2, vocab=1000):
+    from transformers import Qwen2Config, Qwen2ForCausalLM
+    import akv.hf_attention as hook
+    hook.register()
+    torch.manual_seed(0)
+    cfg = Qwen2Config(vocab_size=vocab, hidden_size=512, intermediate_size=1024, num_hidden_layers=layers,
+                      num_attention_heads=4, num_key_value_heads=2, max_position_embeddings=4096,
+                      rms_norm_eps=1e-6, initializer_range=0.08)
+    return Qwen2ForCausalLM(cfg).eval().half().to(DEV)
+
+
+def _step(model, cache, ids):
+    out = model(input_ids=ids, past_key_values=cache, use_cache=True, logits_to_keep=1)
+    return out.logits[:, -1].float()
+
+
+@pytest.mark.parametrize("policy", ["recency", "proxy_promotion", "k4v2_outliers"])
+def test_hook_matches_sdpa_over_view_each_step(policy, monkeypatch):
+    """Every fused decode call against SDPA over that layer's full view."""
+    import akv
+    import akv.hf_attention as hook
+    from transformers.integrations.sdpa_attention import sdpa_attention_forward
+    kw = {
+        "recency": dict(warm_bits=3, hot_budget=48, enable_promotion=False, enable_promotion_proxy=False),
+        "proxy_promotion": dict(warm_bits=3, hot_budget=48, enable_promotion=True, enable_promotion_proxy=True,
+                                promotion_threshold=0.05),
+        "k4v2_outliers": dict(warm_key_bits=4, warm_value_bits=2, warm_bits=4, hot_budget=40,
+                              outlier_fraction=0.02, enable_promotion=False, enable_promotion_proxy=False),
+    }[policy]
+    model = _model()
+    model.config._attn_implementation = "akv"
+    errs, calls = [], [0]
+    real = hook.akv_attention_forward
+
+    def checked(module, query, key, value, attention_mask, **k2):
+        out, w = real(module, query, key, value, attention_mask, **k2)
+        layer = getattr(key, "_akv_layer", None)
+        if layer is not None and query.shape[2] == 1 and attention_mask is None:
+            calls[0] += 1
+            fk, fv = layer.full_view()
+            ref, _ = sdpa_attention_forward(module, query.float(), fk.float(), fv.float(), None,
+                                            scaling=k2.get("scaling"))
+            errs.append(((out.float() - ref).abs().max().item(), _excess(out.float(), ref)))
+        return out, w
+
+    from transformers import AttentionInterface
+    AttentionInterface.register("akv", checked)
+    try:
+        cache = akv.AKVCache(num_hidden_layers=2, fused_decode=True, **kw)
+        g = torch.Generator(device=DEV).manual_seed(1)
+        ids = torch.randint(1, 1000, (1, 200), generator=g, device=DEV)
+        with torch.no_grad():
+            _step(model, cache, ids)
+            for _ in range(24):
+                ids = torch.randint(1, 1000, (1, 1), generator=g, device=DEV)
+                _step(model, cache, ids)
+    finally:
+        AttentionInterface.register("akv", real)
+    assert calls[0] == 2 * 24, calls
+    print(f"[hf hook {policy}] max |fused - sdpa(view)| = {max(e[0] for e in errs):.2e}")
+    assert max(e[1] for e in errs) <= 0.0
+    layer = cache.layers[0]
+    assert layer._warm is not None and layer._hot_keys.shape[2] == cache.hot_budget
+    if policy == "proxy_promotion":
+        live = sum(bin(int(m) & 0xFFFFFFFF).count("1") for m in layer._warm.masks()[0, 0].tolist())
+        assert live == layer._warm_keys_fp16.shape[2]
+
+
+def test_fused_decoding_logits_match_view_cache():
+    """Teacher-forced decoding: fused cache + "akv" hook against a view cache + SDPA."""
+    import akv
+    model = _model()
+    g = torch.Generator(device=DEV).manual_seed(2)
+    prompt = torch.randint(1, 1000, (1, 300), generator=g, device=DEV)
+    toks = torch.randint(1, 1000, (1, 32), generator=g, device=DEV)
+    kw = dict(warm_bits=3, hot_budget=64, enable_promotion=False, enable_promotion_proxy=False, num_hidden_layers=2)
+    logits = {}
+    for mode in ("view", "fused"):
+        model.config._attn_implementation = "sdpa" if mode == "view" else "akv"
+        cache = akv.AKVCache(fused_decode=(mode == "fused"), **kw)
+        rows = []
+        with torch.no_grad():
+            rows.append(_step(model, cache, prompt))
+            for i in range(toks.shape[1]):
+                rows.append(_step(model, cache, toks[:, i:i + 1]))
+        logits[mode] = torch.cat(rows)
+        assert cache.layers[1]._warm is not None
+    model.config._attn_implementation = "sdpa"
+    a, b = logits["view"], logits["fused"]
+    err = (a - b).abs().max().item()
+    scale = a.abs().max().item()
+    print(f"[hf hook e2e] max |logits fused - view| = {err:.3e} (max |logit| {scale:.2f})")
+    assert torch.isfinite(b).all()
+    assert err <= 2e-2 * max(scale, 1.0)
+    assert (a.argmax(-1) == b.argmax(-1)).float().mean().item() >= 0.9
+
+
+def test_generate_with_hook_and_beam_ops():
+    """HF generate through the hook; padded batches fall back to SDPA over the view."""
+    import akv
+    model = _model()
+    model.config._attn_implementation = "akv"
+    g = torch.Generator(device=DEV).manual_seed(3)
+    ids = torch.randint(1, 1000, (2, 120), generator=g, device=DEV)
+    mask = torch.ones_like(ids)
+    mask[1, :7] = 0  # left padding on row 1: the mask path, not the fused one
+    with torch.no_grad():
+        cache = akv.AKVCache(warm_bits=3, hot_budget=32, enable_promotion=False, enable_promotion_proxy=False,
+                             num_hidden_layers=2, fused_decode=True)
+        out = model.generate(ids, attention_mask=mask, max_new_tokens=8, do_sample=False, past_key_values=cache,
+                             pad_token_id=0)
+        assert out.shape == (2, 128)
+        cache2 = akv.AKVCache(warm_bits=3, hot_budget=32, enable_promotion=False, enable_promotion_proxy=False,
+                              num_hidden_layers=2, fused_decode=True)
+        out2 = model.generate(ids[:1], max_new_tokens=8, do_sample=False, past_key_values=cache2, pad_token_id=0)
+        assert out2.shape == (1, 128)
+    layer = cache2.layers[0]
+    assert getattr(layer.keys, "_akv_layer", None) is layer
+    assert layer.get_seq_length() == 127
+    cache2.batch_repeat_interleave(2)
+    assert layer._hot_keys.shape[0] == 2 and layer.keys.shape[0] == 2
+    model.config._attn_implementation = "sdpa"
