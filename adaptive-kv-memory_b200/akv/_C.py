@@ -151,6 +151,19 @@ def warm_layout(head_dim: int, key_bits: int, value_bits: int, n_outlier: int) -
     return L
 
 
+_ws_sizes: dict = {}
+
+
+def workspace_bytes(name: str, *args) -> int:
+    """Memoised workspace-size query (``akv_*_workspace_bytes``): pure
+    functions of their shape arguments, asked on every call of the hot path."""
+    key = (name,) + args
+    n = _ws_sizes.get(key)
+    if n is None:
+        n = _ws_sizes[key] = int(getattr(load(), name)(*args))
+    return n
+
+
 def quantize(x_ptr: int, sb: int, sh: int, sn: int, tok_ptr, tok_sb: int, B: int, H: int, N: int, D: int,
              bits: int, is_key: bool, group: int, n_out: int, dest: QDest, status_ptr, device,
              score_sum=None, score_heads: int = 0) -> None:
@@ -158,7 +171,7 @@ def quantize(x_ptr: int, sb: int, sh: int, sn: int, tok_ptr, tok_sb: int, B: int
     (``score_sum``: all-reduced outlier norm sums when heads are sharded over GPUs)."""
     import torch
     lib = load()
-    need = lib.akv_quantize_workspace_bytes(B, H, N, D, group, n_out, int(is_key))
+    need = workspace_bytes("akv_quantize_workspace_bytes", B, H, N, D, group, n_out, int(is_key))
     ws = torch.empty(need + 256, dtype=torch.uint8, device=device) if need else None
     wp = None if ws is None else (ws.data_ptr() + 255) // 256 * 256
     rc = lib.akv_quantize_ext(x_ptr, sb, sh, sn, tok_ptr, tok_sb, B, H, N, D, bits, int(is_key), group, n_out,

@@ -181,12 +181,26 @@ class AKVLayer(_LayerBase):
         idx_dev = _to_device(demote_idx, hk.device)
         blk0 = arena.append(hk, hv, group=n, tok_idx=idx_dev)
         slots = torch.arange(blk0 * BLOCK, blk0 * BLOCK + n, dtype=torch.int64, device=hk.device)
-        dk, dv = arena.dequantize(tok_idx=slots)
+        self._warm_slots = slots if self._warm_slots is None else torch.cat([self._warm_slots, slots])
         # the reference's measure_packed_bytes of this event's K and V dicts (drop_in.py:331-336)
         kb, vb = self.warm_key_bits, self.warm_value_bits
         self._warm_bytes_packed += B * (H * n * packed_width(D, kb) + 4 * H * D + H * n * packed_width(D, vb) + 4 * H * n)
-        self._append_warm_fp16(dk, dv)
-        self._warm_slots = slots if self._warm_slots is None else torch.cat([self._warm_slots, slots])
+        if not self._no_fp16_copy:
+            self._append_warm_fp16(*arena.dequantize(tok_idx=slots))
+
+    @property
+    def _no_fp16_copy(self) -> bool:
+        """A fused cache that never promotes keeps no FP16 working copy of the
+        warm tier: nothing reads it at decode, and the view for a prefill or a
+        masked step is dequantised from the records when asked for."""
+        return self.fused_decode and not self.enable_promotion and not self.enable_promotion_proxy
+
+    def warm_fp16(self) -> Tuple[Optional[torch.Tensor], Optional[torch.Tensor]]:
+        """FP16 K/V of the warm tokens in warm order (the working copy, or the
+        records dequantised on demand when no copy is kept)."""
+        if self._warm_keys_fp16 is not None or self._warm is None or self._warm_slots is None:
+            return self._warm_keys_fp16, self._warm_values_fp16
+        return self._warm.dequantize(tok_idx=self._warm_slots)
 
     def _append_warm_fp16(self, dk: torch.Tensor, dv: torch.Tensor) -> None:
         """Append dequantised warm rows to the FP16 working copy.
@@ -368,16 +382,17 @@ class AKVLayer(_LayerBase):
             if self._importance is not None:
                 self._importance = self._importance[keep]
 
-        if self.fused_decode and N == 1 and self._warm_keys_fp16 is not None:
+        if self.fused_decode and N == 1 and self._warm is not None:
             return self._publish(*self._placeholder())
         return self._publish(*self.full_view())
 
     def full_view(self) -> Tuple[torch.Tensor, torch.Tensor]:
         """The chronologically sorted [warm; hot] FP16 K/V (drop_in.py:753-787)."""
-        if self._warm_keys_fp16 is None:
+        wk, wv = self.warm_fp16()
+        if wk is None:
             return self._hot_keys, self._hot_values
-        full_k = torch.cat([self._warm_keys_fp16, self._hot_keys], dim=2)
-        full_v = torch.cat([self._warm_values_fp16, self._hot_values], dim=2)
+        full_k = torch.cat([wk, self._hot_keys], dim=2)
+        full_v = torch.cat([wv, self._hot_values], dim=2)
         order = torch.cat([self._warm_positions, self._hot_positions]).argsort().to(full_k.device)
         return full_k.index_select(2, order), full_v.index_select(2, order)
 
@@ -390,7 +405,7 @@ class AKVLayer(_LayerBase):
         if self._nan is None or self._nan.dtype != hk.dtype or self._nan.device != hk.device:
             self._nan = torch.full((1, 1, 1, 1), float("nan"), dtype=hk.dtype, device=hk.device)
         B, H, _, D = hk.shape
-        n = hk.shape[2] + self._warm_keys_fp16.shape[2]
+        n = hk.shape[2] + self._warm_len
         k = self._nan.expand(B, H, n, D)
         v = self._nan.expand(B, H, n, D)
         k._akv_layer = self
@@ -574,7 +589,7 @@ class AKVCache(_CacheBase):
         """Trim the hot tier from the end (drop_in.py:1231-1243)."""
         for layer in self.layers:
             if layer._hot_keys is not None:
-                cur = layer._hot_keys.shape[2] + (0 if layer._warm_keys_fp16 is None else layer._warm_keys_fp16.shape[2])
+                cur = layer._hot_keys.shape[2] + layer._warm_len
                 if cur > max_length:
                     keep = max(0, layer._hot_keys.shape[2] - (cur - max_length))
                     layer._hot_keys = layer._hot_keys[:, :, :keep, :]
@@ -613,9 +628,9 @@ class AKVCache(_CacheBase):
         if layer_idx < len(self.layers):
             layer = self.layers[layer_idx]
             if layer._hot_keys is not None:
-                if layer._warm_keys_fp16 is not None:
-                    return (torch.cat([layer._warm_keys_fp16, layer._hot_keys], dim=2),
-                            torch.cat([layer._warm_values_fp16, layer._hot_values], dim=2))
+                wk, wv = layer.warm_fp16()
+                if wk is not None:
+                    return (torch.cat([wk, layer._hot_keys], dim=2), torch.cat([wv, layer._hot_values], dim=2))
                 return (layer._hot_keys, layer._hot_values)
         return (torch.tensor([]), torch.tensor([]))
 

@@ -97,7 +97,7 @@ def mixed_tier_decode_attention(query: torch.Tensor,
     if warm is not None and (warm.B != B or warm.H != Hkv or warm.D != D):
         raise ValueError("warm arena shape does not match the query / hot tier")
     lib = _C.load()
-    need = lib.akv_decode_workspace_bytes(B, Hq, Hkv, D, nh, nwb)
+    need = _C.workspace_bytes("akv_decode_workspace_bytes", B, Hq, Hkv, D, nh, nwb)
     if need == 0:
         raise ValueError(f"unsupported decode shape B={B} Hq={Hq} Hkv={Hkv} D={D}")
     ws = _workspace(q3.device, need)

@@ -969,10 +969,20 @@ static void split_shares(int per_unit, int n_warm_blocks, int nhb, double wbytes
   pl.splits = pl.warm_splits + pl.hot_splits;
 }
 
-// candidate split counts per unit: [lo, hi]
-static void per_unit_range(int units, int& lo, int& hi) {
+// Fewest 32-token blocks a split gets when the wave target would cut a unit
+// finer (few units: batch 1, few KV heads): every warp then has several blocks
+// to stream, and the split partials the combine reads stay few.
+constexpr int kMinBlocksPerSplit = 16;
+
+// candidate split counts per unit: [lo, hi]; unit_blocks = warm + hot blocks of one unit
+static void per_unit_range(int units, int unit_blocks, int& lo, int& hi) {
   lo = max(1, (3 * kDecodeSlots + units - 1) / units);
   hi = lo + max(8, lo);
+  const int cap = max(1, unit_blocks / kMinBlocksPerSplit);
+  if (hi > cap) {
+    hi = cap;
+    lo = min(lo, cap);
+  }
 }
 
 static DecodePlan plan_decode(int B, int Hq, int Hkv, int n_hot, int n_warm_blocks, int rec_bytes) {
@@ -984,7 +994,7 @@ static DecodePlan plan_decode(int B, int Hq, int Hkv, int n_hot, int n_warm_bloc
   const double wbytes = static_cast<double>(n_warm_blocks) * rec_bytes;
   const double hbytes = static_cast<double>(nhb) * 32 * kHeadDim * 4 * kHotCost;
   int lo, hi;
-  per_unit_range(units, lo, hi);
+  per_unit_range(units, n_warm_blocks + nhb, lo, hi);
   double best = -1.0;
   DecodePlan cand = pl;
   for (int pu = lo; pu <= hi; ++pu) {
@@ -1039,7 +1049,7 @@ static int max_splits(int B, int Hq, int Hkv, int n_hot, int n_warm_blocks) {
   const int g = Hq / Hkv;
   const int units = B * Hkv * ((g + 7) / 8);
   int lo, hi;
-  per_unit_range(units, lo, hi);
+  per_unit_range(units, n_warm_blocks + (n_hot + 31) / 32, lo, hi);
   const int cap = n_warm_blocks + (n_hot + 31) / 32;
   return max(1, min(hi + 2, cap));
 }

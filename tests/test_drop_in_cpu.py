@@ -166,6 +166,7 @@ def test_fused_placeholder_and_warm_append_on_cpu():
     assert torch.equal(layer._warm_keys_fp16, torch.cat([want[:, :, 1:], chunks[0]], 2))
     layer._hot_keys = torch.randn(1, 2, 8, 128, generator=g).half()
     layer._hot_values = layer._hot_keys.clone()
+    layer._warm_len = layer._warm_keys_fp16.shape[2]
     k, v = layer._placeholder()
     assert k.shape == (1, 2, 8 + 52, 128) and k.untyped_storage().nbytes() == 2  # one fp16 element
     assert torch.isnan(k).all() and k._akv_layer is layer

@@ -92,6 +92,8 @@ def test_hook_matches_sdpa_over_view_each_step(policy, monkeypatch):
     assert max(e[1] for e in errs) <= 0.0
     layer = cache.layers[0]
     assert layer._warm is not None and layer._hot_keys.shape[2] == cache.hot_budget
+    if policy != "proxy_promotion":  # fused and never promoting: no FP16 warm copy is kept
+        assert layer._warm_keys_fp16 is None and cache.memory_usage()["warm_bytes_live"] == 0
     if policy == "proxy_promotion":
         live = sum(bin(int(m) & 0xFFFFFFFF).count("1") for m in layer._warm.masks()[0, 0].tolist())
         assert live == layer._warm_keys_fp16.shape[2]
