@@ -874,19 +874,27 @@ __global__ void __launch_bounds__(kDecodeThreads, 4) mixed_decode_kernel(const D
 // relative to m (log2 units).  Row r, split s lives at part + s*ss + r*sr.
 // Writes any of: fp16 out[r*o_sr + d], natural-log lse[r], and the merged
 // partial record merged[r*(D+2) + ...] (for a further cross-GPU combine).
-constexpr int kCombineMaxSplits = 256;  // splits merged per pass (larger counts loop)
+constexpr int kCombineMaxSplits = 256;  // splits whose weights are kept in shared memory
+constexpr int kCombineThreads = 128;
+constexpr int kCombineChunk = 32;                                 // channels per CTA
+constexpr int kCombineGroups = kCombineThreads / kCombineChunk;  // split groups per CTA
 
-__global__ void lse_combine_kernel(const float* __restrict__ part, int64_t ss, int64_t sr, int rows, int splits,
-                                   int D, __half* out, int64_t o_sr, float* lse, float* merged) {
-  // one CTA per row: warp 0 turns the splits' (m, l) into weights
-  // w_s = 2^(m_s - M) in shared memory once; every thread then sums one
-  // channel over the splits with independent loads in flight
+// grid (rows, ceil(D / 32)): a CTA merges 32 channels of one row.  Warp 0
+// turns the splits' (m, l) into weights w_s = 2^(m_s - M) in shared memory;
+// thread (group, c) then sums channel c over the splits s = group (mod 4),
+// eight loads in flight, and the four group sums meet in shared memory.
+// Every warp's loads of one split are 128 contiguous bytes.
+__global__ void __launch_bounds__(kCombineThreads) lse_combine_kernel(const float* __restrict__ part, int64_t ss,
+                                                                      int64_t sr, int rows, int splits, int D,
+                                                                      __half* out, int64_t o_sr, float* lse,
+                                                                      float* merged) {
   __shared__ float w[kCombineMaxSplits];
+  __shared__ float acc[kCombineGroups][kCombineChunk];
   __shared__ float sM, sL;
   const int r = blockIdx.x;
   if (r >= rows) return;
   const float* base = part + static_cast<int64_t>(r) * sr;
-  const int lane = threadIdx.x & 31;
+  const int lane = threadIdx.x & 31, grp = threadIdx.x >> 5;
   if (threadIdx.x < 32) {
     float M = -INFINITY;
     for (int s = lane; s < splits; s += 32) M = fmaxf(M, base[s * ss + D]);
@@ -908,23 +916,32 @@ __global__ void lse_combine_kernel(const float* __restrict__ part, int64_t ss, i
   }
   __syncthreads();
   const float M = sM, L = sL, mb = (M == -INFINITY) ? 0.f : M;
-  const float inv = L > 0.f ? 1.f / L : 0.f;
-  for (int d = threadIdx.x; d < D; d += blockDim.x) {
-    float o = 0.f;
+  const int d = blockIdx.y * kCombineChunk + lane;
+  float o = 0.f;
+  if (d < D) {
     const float* col = base + d;
-    int s = 0;
-    for (; s + 8 <= splits && s + 8 <= kCombineMaxSplits; s += 8) {
+    const int lim = min(splits, kCombineMaxSplits);
+    int s = grp;
+    for (; s + 7 * kCombineGroups < lim; s += 8 * kCombineGroups) {
       float v[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = col[(s + j) * ss];
+      for (int j = 0; j < 8; ++j) v[j] = col[(s + j * kCombineGroups) * ss];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) o = fmaf(v[j], w[s + j], o);
+      for (int j = 0; j < 8; ++j) o = fmaf(v[j], w[s + j * kCombineGroups], o);
     }
-    for (; s < splits; ++s) o = fmaf(col[s * ss], s < kCombineMaxSplits ? w[s] : exp2f(base[s * ss + D] - mb), o);
+    for (; s < splits; s += kCombineGroups)
+      o = fmaf(col[s * ss], s < kCombineMaxSplits ? w[s] : exp2f(base[s * ss + D] - mb), o);
+  }
+  acc[grp][lane] = o;
+  __syncthreads();
+  if (grp == 0 && d < D) {
+#pragma unroll
+    for (int g = 1; g < kCombineGroups; ++g) o += acc[g][lane];
+    const float inv = L > 0.f ? 1.f / L : 0.f;
     if (out) out[static_cast<int64_t>(r) * o_sr + d] = __float2half_rn(o * inv);
     if (merged) merged[static_cast<int64_t>(r) * (D + 2) + d] = o;
   }
-  if (threadIdx.x == 0) {
+  if (blockIdx.y == 0 && threadIdx.x == 0) {
     if (lse) lse[r] = L > 0.f ? (M + log2f(L)) / kLog2e : -INFINITY;
     if (merged) {
       merged[static_cast<int64_t>(r) * (D + 2) + D] = M;
@@ -932,6 +949,8 @@ __global__ void lse_combine_kernel(const float* __restrict__ part, int64_t ss, i
     }
   }
 }
+
+static dim3 combine_grid(int rows, int D) { return dim3(rows, (D + kCombineChunk - 1) / kCombineChunk); }
 
 // ------------------------------------------------------------------ host side
 struct DecodePlan {
@@ -1100,7 +1119,7 @@ extern "C" int akv_mixed_decode(const uint16_t* q, int64_t q_sb, int64_t q_sh, c
   __half* outh = reinterpret_cast<__half*>(out);
   if (pl.splits == 0) {  // no tokens at all: a zeroed partial (m = 0, l = 0) combines to output 0, lse -inf
     if (cudaMemsetAsync(ws, 0, need, st) != cudaSuccess) return AKV_ERR_LAUNCH;
-    lse_combine_kernel<<<B * Hq, 128, 0, st>>>(ws, D + 2, D + 2, B * Hq, 1, D, outh, o_sh, lse, partial_out);
+    lse_combine_kernel<<<combine_grid(B * Hq, D), kCombineThreads, 0, st>>>(ws, D + 2, D + 2, B * Hq, 1, D, outh, o_sh, lse, partial_out);
     return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_LAUNCH;
   }
   DecodeParams p{};
@@ -1149,7 +1168,7 @@ extern "C" int akv_mixed_decode(const uint16_t* q, int64_t q_sb, int64_t q_sh, c
     default: rc = launch_decode<4, 4>(p, st); break;
   }
   if (rc != AKV_OK) return rc;
-  lse_combine_kernel<<<B * Hq, 128, 0, st>>>(ws, D + 2, static_cast<int64_t>(pl.splits) * (D + 2), B * Hq,
+  lse_combine_kernel<<<combine_grid(B * Hq, D), kCombineThreads, 0, st>>>(ws, D + 2, static_cast<int64_t>(pl.splits) * (D + 2), B * Hq,
                                              pl.splits, D, outh, o_sh, lse, partial_out);
   return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_LAUNCH;
 }
@@ -1158,7 +1177,7 @@ extern "C" int akv_lse_combine(const float* part, int64_t part_ss, int64_t part_
                                uint16_t* out, int64_t o_sr, float* lse, float* merged, void* stream) {
   if (!part || (!out && !lse && !merged)) return AKV_ERR_NULL;
   if (rows <= 0 || splits <= 0 || D <= 0 || part_ss < 0 || part_sr < 0) return AKV_ERR_SHAPE;
-  lse_combine_kernel<<<rows, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+  lse_combine_kernel<<<combine_grid(rows, D), kCombineThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       part, part_ss, part_sr, rows, splits, D, reinterpret_cast<__half*>(out), o_sr, lse, merged);
   return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_LAUNCH;
 }

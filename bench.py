@@ -189,6 +189,74 @@ def migration_bench(torch, akv, dev) -> dict:
             "cold_bytes": cb}
 
 
+# ---------------------------------------------------------------------------- other decode shapes
+DECODE_SHAPES = {
+    # name: (B, Hq, Hkv, hot, warm, key_bits, value_bits, outlier_fraction)
+    "config1": (1, 12, 2, 512, 3584, 3, 3, 0.0),
+    "config2": (1, 12, 2, 1024, 31744, 3, 3, 0.0),
+    "config5a": (32, 64, 8, 4096, 61440, 4, 4, 0.0),
+    "config5b_shard": (1, 64, 8, 4096, 65536 - 4096, 4, 4, 0.0),  # one of 8 sequence shards of 512K
+}
+
+
+def decode_shapes_bench(torch, akv, dev, reps: int = 20) -> dict:
+    """Per-layer device time of one decode launch (decode + combine) at the
+    other BASELINE shapes.  Each shape cycles through enough layer copies
+    that the working set is >= 256 MB (twice the L2), inside one CUDA graph
+    replayed `reps` times; algorithmic bytes as for the headline metric."""
+    out = {}
+    D = 128
+    for name, (B, Hq, Hkv, n_hot, n_warm, kb, vb, frac) in DECODE_SHAPES.items():
+        gen = torch.Generator(device=dev).manual_seed(11)
+        nblk = n_warm // 32
+        arena = akv.WarmArena(B, Hkv, D, kb, vb, frac, max_blocks=nblk, device=dev)
+        step = 8192
+        for t0 in range(0, n_warm, step):  # quantise in slices to bound the fp32 temporaries
+            n = min(step, n_warm - t0)
+            arena.append(make_kv(torch, gen, (B, Hkv, n, D), dev), make_kv(torch, gen, (B, Hkv, n, D), dev), group=32)
+        hk = make_kv(torch, gen, (B, Hkv, n_hot, D), dev)
+        hv = make_kv(torch, gen, (B, Hkv, n_hot, D), dev)
+        per_kvh = n_warm * D * (kb + vb) // 8 + nblk * D * 4 + n_warm * 4 + n_warm * arena.n_out * 4 + n_hot * D * 4
+        layer_bytes = B * Hkv * per_kvh + 2 * B * Hq * D * 2
+        copies = max(1, -(-(256 << 20) // layer_bytes))
+        arenas, hks, hvs = [arena], [hk], [hv]
+        for _ in range(copies - 1):
+            a = akv.WarmArena(B, Hkv, D, kb, vb, frac, max_blocks=nblk, device=dev)
+            a.buf.copy_(arena.buf)
+            a.n_blocks = arena.n_blocks
+            arenas.append(a)
+            hks.append(hk.clone())
+            hvs.append(hv.clone())
+        q = torch.randn(B, Hq, D, generator=gen, device=dev).half()
+        o = torch.empty(B, Hq, D, dtype=torch.float16, device=dev)
+
+        def run():
+            for i in range(copies):
+                akv.mixed_tier_decode_attention(q, hks[i], hvs[i], arenas[i], out=o)
+
+        for _ in range(3):
+            run()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            run()
+        graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (reps * copies)
+        out[name] = {"B": B, "q_heads": Hq, "kv_heads": Hkv, "hot": n_hot, "warm": n_warm, "bits": f"k{kb}v{vb}",
+                     "layer_us": round(us, 2), "algorithmic_bytes": layer_bytes,
+                     "gbs": round(layer_bytes / (us * 1e-6) / 1e9, 1), "layer_copies": copies}
+        del graph, arenas, hks, hvs, arena, hk, hv
+        torch.cuda.empty_cache()
+    return out
+
+
 # ---------------------------------------------------------------------------- HF decoding (config 2)
 def hf_decode_bench(torch, akv, dev, new_tokens: int = 256, prompt: int = 32768) -> dict:
     """Config 2 end to end: a Qwen2.5-1.5B-shaped random-init decoder (28
@@ -451,9 +519,12 @@ def run_ours(args):
         }
         if world == 1 and not args.no_migration:
             res["migration"] = migration_bench(torch, akv, dev)
-        if world == 1 and args.hf_tokens > 0:
+        if world == 1 and (not args.no_shapes or args.hf_tokens > 0):
             del arenas, hot_k, hot_v, graph
             torch.cuda.empty_cache()
+        if world == 1 and not args.no_shapes:
+            res["decode_shapes"] = decode_shapes_bench(torch, akv, dev)
+        if world == 1 and args.hf_tokens > 0:
             res["hf_decode"] = hf_decode_bench(torch, akv, dev, new_tokens=args.hf_tokens)
         if world == 1 and not args.no_cpu_baseline:
             res["cpu_baseline"] = cpu_baseline(units=args.cpu_units, world=1)
@@ -540,6 +611,7 @@ def main():
     ap.add_argument("--cpu-units", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-migration", action="store_true")
+    ap.add_argument("--no-shapes", action="store_true", help="skip the per-layer decode timings of configs 1, 2, 5")
     ap.add_argument("--hf-tokens", type=int, default=256,
                     help="config-2 HF greedy decoding length (0: skip the end-to-end model run)")
     ap.add_argument("--batch", type=int, default=CFG["B"],
