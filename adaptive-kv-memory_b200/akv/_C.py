@@ -72,6 +72,13 @@ SIGNATURES = {
                                  c_int, c_int, c_int, c_int, c_float,
                                  c_void_p, c_int64, c_int64, c_void_p, c_void_p,
                                  c_void_p, c_size_t, c_void_p, c_void_p]),
+    "akv_mixed_decode_paged": (c_int, [c_void_p, c_int64, c_int64,
+                                       c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int, c_void_p,
+                                       c_void_p, c_int, c_int64, c_int64, c_void_p, c_int64, POINTER(WarmLayout),
+                                       c_int, c_void_p,
+                                       c_int, c_int, c_int, c_int, c_float,
+                                       c_void_p, c_int64, c_int64, c_void_p, c_void_p,
+                                       c_void_p, c_size_t, c_void_p, c_void_p]),
     "akv_mixed_decode_noalloc": (c_int, [c_void_p, c_int64, c_int64,
                                          c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int, c_void_p,
                                          c_void_p, c_int64, c_int64, POINTER(WarmLayout), c_int, c_void_p,

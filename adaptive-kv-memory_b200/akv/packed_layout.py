@@ -64,6 +64,32 @@ def measure_packed_bytes(qdata: dict, bits: int) -> int:
     return int(total)
 
 
+def record_dest(L: _C.WarmLayout, base: int, sb: int, sh: int, sblk: int, is_key: bool) -> _C.QDest:
+    """QDest addressing the K (or V) fields of block records: the record of
+    (b, h, blk) starts at base + b*sb + h*sh + blk*sblk (bytes)."""
+    n = L.n_outlier
+    d = _C.QDest()
+    if is_key:
+        d.pair_order = 1  # records keep K scale / zero in the decode pair order
+        d.codes = _C.View(base + L.kc, sb, sh, sblk, packed_width(L.head_dim, L.key_bits))
+        d.scale = _C.View(base + L.ks, sb, sh, sblk, 0)
+        d.zero = _C.View(base + L.kz, sb, sh, sblk, 0)
+        if n:
+            d.out_data = _C.View(base + L.ko, sb, sh, sblk, 2 * n)
+            d.out_idx = _C.View(base + L.ki, sb, sh, sblk, 0)
+    else:
+        d.codes = _C.View(base + L.vc, sb, sh, sblk, packed_width(L.head_dim, L.value_bits))
+        d.scale = _C.View(base + L.vs, sb, sh, sblk, 2)
+        d.zero = _C.View(base + L.vz, sb, sh, sblk, 2)
+        if n:
+            d.out_data = _C.View(base + L.vo, sb, sh, sblk, 2 * n)
+            d.out_idx = _C.View(base + L.vi, sb, sh, sblk, 0)
+            d.out_vdq = _C.View(base + L.vd, sb, sh, sblk, 2 * n)
+    d.mask = _C.View(base + L.mask, sb, sh, sblk, 0)
+    d.flags = _C.View(base + L.flags + (0 if is_key else 1), sb, sh, sblk, 0)
+    return d
+
+
 class WarmArena:
     """Packed warm tier: (B, H, max_blocks) block records in one uint8 buffer."""
 
@@ -88,30 +114,9 @@ class WarmArena:
 
     def dest(self, is_key: bool, blk0: int = 0) -> _C.QDest:
         """QDest addressing K (or V) fields of the records starting at block blk0."""
-        L, rec = self.layout, self.rec
-        sb, sh = self.H * self.max_blocks * rec, self.max_blocks * rec
-        base = self._base(blk0)
-        d = _C.QDest()
-        n = self.n_out
-        if is_key:
-            d.pair_order = 1  # records keep K scale / zero in the decode pair order
-            d.codes = _C.View(base + L.kc, sb, sh, rec, packed_width(self.D, self.key_bits))
-            d.scale = _C.View(base + L.ks, sb, sh, rec, 0)
-            d.zero = _C.View(base + L.kz, sb, sh, rec, 0)
-            if n:
-                d.out_data = _C.View(base + L.ko, sb, sh, rec, 2 * n)
-                d.out_idx = _C.View(base + L.ki, sb, sh, rec, 0)
-        else:
-            d.codes = _C.View(base + L.vc, sb, sh, rec, packed_width(self.D, self.value_bits))
-            d.scale = _C.View(base + L.vs, sb, sh, rec, 2)
-            d.zero = _C.View(base + L.vz, sb, sh, rec, 2)
-            if n:
-                d.out_data = _C.View(base + L.vo, sb, sh, rec, 2 * n)
-                d.out_idx = _C.View(base + L.vi, sb, sh, rec, 0)
-                d.out_vdq = _C.View(base + L.vd, sb, sh, rec, 2 * n)
-        d.mask = _C.View(base + L.mask, sb, sh, rec, 0)
-        d.flags = _C.View(base + L.flags + (0 if is_key else 1), sb, sh, rec, 0)
-        return d
+        rec = self.rec
+        return record_dest(self.layout, self._base(blk0), self.H * self.max_blocks * rec, self.max_blocks * rec, rec,
+                           is_key)
 
     def grow(self, min_blocks: int) -> None:
         """Make room for at least ``min_blocks`` blocks (capacity doubles; records are copied)."""

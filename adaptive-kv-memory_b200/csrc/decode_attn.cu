@@ -48,6 +48,11 @@ struct DecodeParams {
   const int32_t* hot_len;
   const uint8_t* warm;
   int64_t w_sb, w_sh;
+  // paged warm pool (nullptr: contiguous rows): record (b, kvh, blk) lives at
+  // warm + btab[b * bt_sb + blk] * w_page + kvh * w_sh
+  const int32_t* btab;
+  int64_t bt_sb, w_page;
+  int n_pages;  // pages in the pool: an entry outside [0, n_pages) records AKV_ERR_SHAPE and reads page 0
   akv_warm_layout L;
   int n_warm_blocks;
   const int32_t* warm_len;
@@ -711,6 +716,16 @@ __global__ void __launch_bounds__(kDecodeThreads, 4) mixed_decode_kernel(const D
   // overlap the first copies instead of preceding them
   int nmine = 0;
   const uint8_t* wbase = nullptr;
+  const int32_t* wtab = nullptr;  // paged pool: this row's block table, from this split's first block
+  int32_t next_page = 0;          // lane 0: page of the warp's next refill, fetched one block ahead
+  auto page_at = [&](int i) {
+    int32_t pg = __ldg(wtab + i);
+    if (static_cast<uint32_t>(pg) >= static_cast<uint32_t>(p.n_pages)) {
+      set_status(p.status, AKV_ERR_SHAPE);
+      pg = 0;
+    }
+    return pg;
+  };
   uint64_t* wbar = full + warp * kStagesPerWarp;
   unsigned char* wstage = stage0 + warp * kStagesPerWarp * rec;
   if (warm_cta) {
@@ -718,7 +733,12 @@ __global__ void __launch_bounds__(kDecodeThreads, 4) mixed_decode_kernel(const D
     const int blo = split * p.wbps;
     const int bhi = min(nblk_b, blo + p.wbps);
     const int nb = max(0, bhi - blo);
-    wbase = p.warm + b * p.w_sb + kvh * p.w_sh + static_cast<int64_t>(blo) * rec;
+    if (p.btab) {
+      wtab = p.btab + b * p.bt_sb + blo;
+      wbase = p.warm + kvh * p.w_sh;
+    } else {
+      wbase = p.warm + b * p.w_sb + kvh * p.w_sh + static_cast<int64_t>(blo) * rec;
+    }
     // warp `warp` owns blocks i = warp + 4*li (li = 0, 1, ...) and stages
     // warp*kStagesPerWarp + li%kStagesPerWarp; lane 0 keeps them in flight
     nmine = nb > warp ? (nb - warp + kConsumerWarps - 1) / kConsumerWarps : 0;
@@ -726,10 +746,13 @@ __global__ void __launch_bounds__(kDecodeThreads, 4) mixed_decode_kernel(const D
       for (int s = 0; s < kStagesPerWarp; ++s) mbar_init(&wbar[s], 1);
       fence_mbar_init();
       for (int li = 0; li < min(nmine, kStagesPerWarp); ++li) {
+        const int i = warp + kConsumerWarps * li;
+        const uint8_t* src = wtab ? wbase + static_cast<int64_t>(page_at(i)) * p.w_page
+                                  : wbase + static_cast<int64_t>(i) * rec;
         mbar_arrive_expect_tx(&wbar[li], rec);
-        tma_load_1d(wstage + li * rec, wbase + static_cast<int64_t>(warp + kConsumerWarps * li) * rec, rec,
-                    &wbar[li]);
+        tma_load_1d(wstage + li * rec, src, rec, &wbar[li]);
       }
+      if (wtab && kStagesPerWarp < nmine) next_page = page_at(warp + kConsumerWarps * kStagesPerWarp);
     }
     __syncwarp();
   }
@@ -780,10 +803,13 @@ __global__ void __launch_bounds__(kDecodeThreads, 4) mixed_decode_kernel(const D
       // refill this stage with the warp's block li+3 once every lane is done reading it
       __syncwarp();
       if (lane == 0 && li + kStagesPerWarp < nmine) {
+        const int i = warp + kConsumerWarps * (li + kStagesPerWarp);
+        const uint8_t* src = wtab ? wbase + static_cast<int64_t>(next_page) * p.w_page
+                                  : wbase + static_cast<int64_t>(i) * rec;
+        if (wtab && li + kStagesPerWarp + 1 < nmine) next_page = page_at(i + kConsumerWarps);
         fence_proxy_async_shared();
         mbar_arrive_expect_tx(&wbar[s], rec);
-        tma_load_1d(wstage + s * rec, wbase + static_cast<int64_t>(warp + kConsumerWarps * (li + kStagesPerWarp)) * rec,
-                    rec, &wbar[s]);
+        tma_load_1d(wstage + s * rec, src, rec, &wbar[s]);
       }
     }
     // after a timed-out wait, let the copies still in flight land before the
@@ -1078,13 +1104,16 @@ extern "C" size_t akv_decode_workspace_bytes(int B, int Hq, int Hkv, int D, int 
   return static_cast<size_t>(B) * Hq * max_splits(B, Hq, Hkv, n_hot, n_warm_blocks) * (D + 2) * sizeof(float);
 }
 
-extern "C" int akv_mixed_decode(const uint16_t* q, int64_t q_sb, int64_t q_sh, const uint16_t* hot_k,
-                                const uint16_t* hot_v, int64_t h_sb, int64_t h_sh, int64_t h_sn, int n_hot,
-                                const int32_t* hot_len, const uint8_t* warm, int64_t w_sb, int64_t w_sh,
-                                const akv_warm_layout* layout, int n_warm_blocks, const int32_t* warm_len, int B,
-                                int Hq, int Hkv, int D, float sm_scale, uint16_t* out, int64_t o_sb,
-                                int64_t o_sh, float* lse, float* partial_out, void* workspace,
-                                size_t workspace_bytes, int* status, void* stream) {
+// Shared body of akv_mixed_decode (btab == nullptr: row b's records are
+// contiguous at warm + b*w_sb + kvh*w_sh) and akv_mixed_decode_paged (row b's
+// block blk is the record at warm + btab[b*bt_sb + blk]*w_page + kvh*w_sh).
+static int decode_impl(const uint16_t* q, int64_t q_sb, int64_t q_sh, const uint16_t* hot_k, const uint16_t* hot_v,
+                       int64_t h_sb, int64_t h_sh, int64_t h_sn, int n_hot, const int32_t* hot_len,
+                       const uint8_t* warm, int64_t w_sb, int64_t w_sh, const int32_t* btab, int64_t bt_sb,
+                       int64_t w_page, int n_pages, const akv_warm_layout* layout, int n_warm_blocks, const int32_t* warm_len,
+                       int B, int Hq, int Hkv, int D, float sm_scale, uint16_t* out, int64_t o_sb, int64_t o_sh,
+                       float* lse, float* partial_out, void* workspace, size_t workspace_bytes, int* status,
+                       void* stream) {
   if (!q || (!out && !partial_out)) return AKV_ERR_NULL;
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || n_hot < 0 || n_warm_blocks < 0) return AKV_ERR_SHAPE;
   if (D != kHeadDim) return AKV_ERR_UNSUPPORTED;
@@ -1100,7 +1129,8 @@ extern "C" int akv_mixed_decode(const uint16_t* q, int64_t q_sb, int64_t q_sh, c
     if (L.head_dim != D) return AKV_ERR_SHAPE;
     if (L.key_bits < 2 || L.key_bits > 4 || L.value_bits < 2 || L.value_bits > 4) return AKV_ERR_BITS;
     if (L.n_outlier < 0 || L.n_outlier > kMaxDecodeOutliers) return AKV_ERR_UNSUPPORTED;
-    if (L.bytes % 16 || !al(warm, 16) || w_sb % 16 || w_sh % 16) return AKV_ERR_ALIGN;
+    if (L.bytes % 16 || !al(warm, 16) || w_sb % 16 || w_sh % 16 || w_page % 16) return AKV_ERR_ALIGN;
+    if (btab && (bt_sb < n_warm_blocks || w_page <= 0 || n_pages <= 0)) return AKV_ERR_SHAPE;
     // the kernel addresses record fields at the offsets akv_warm_layout_init gives
     const RecLayout R = rec_layout(D, L.key_bits, L.value_bits, L.n_outlier);
     if (L.kc != R.kc || L.vc != R.vc || L.ks != R.ks || L.kz != R.kz || L.vs != R.vs || L.vz != R.vz ||
@@ -1136,6 +1166,10 @@ extern "C" int akv_mixed_decode(const uint16_t* q, int64_t q_sb, int64_t q_sh, c
   p.warm = warm;
   p.w_sb = w_sb;
   p.w_sh = w_sh;
+  p.btab = btab;
+  p.bt_sb = bt_sb;
+  p.w_page = w_page;
+  p.n_pages = n_pages;
   p.L = L;
   p.n_warm_blocks = n_warm_blocks;
   p.warm_len = warm_len;
@@ -1171,6 +1205,33 @@ extern "C" int akv_mixed_decode(const uint16_t* q, int64_t q_sb, int64_t q_sh, c
   lse_combine_kernel<<<combine_grid(B * Hq, D), kCombineThreads, 0, st>>>(ws, D + 2, static_cast<int64_t>(pl.splits) * (D + 2), B * Hq,
                                              pl.splits, D, outh, o_sh, lse, partial_out);
   return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_LAUNCH;
+}
+
+extern "C" int akv_mixed_decode(const uint16_t* q, int64_t q_sb, int64_t q_sh, const uint16_t* hot_k,
+                                const uint16_t* hot_v, int64_t h_sb, int64_t h_sh, int64_t h_sn, int n_hot,
+                                const int32_t* hot_len, const uint8_t* warm, int64_t w_sb, int64_t w_sh,
+                                const akv_warm_layout* layout, int n_warm_blocks, const int32_t* warm_len, int B,
+                                int Hq, int Hkv, int D, float sm_scale, uint16_t* out, int64_t o_sb,
+                                int64_t o_sh, float* lse, float* partial_out, void* workspace,
+                                size_t workspace_bytes, int* status, void* stream) {
+  return decode_impl(q, q_sb, q_sh, hot_k, hot_v, h_sb, h_sh, h_sn, n_hot, hot_len, warm, w_sb, w_sh, nullptr, 0, 0, 0,
+                     layout, n_warm_blocks, warm_len, B, Hq, Hkv, D, sm_scale, out, o_sb, o_sh, lse, partial_out,
+                     workspace, workspace_bytes, status, stream);
+}
+
+extern "C" int akv_mixed_decode_paged(const uint16_t* q, int64_t q_sb, int64_t q_sh, const uint16_t* hot_k,
+                                      const uint16_t* hot_v, int64_t h_sb, int64_t h_sh, int64_t h_sn, int n_hot,
+                                      const int32_t* hot_len, const uint8_t* pool, int n_pages,
+                                      int64_t page_stride, int64_t head_stride, const int32_t* block_table,
+                                      int64_t bt_stride,
+                                      const akv_warm_layout* layout, int max_blocks, const int32_t* warm_len, int B,
+                                      int Hq, int Hkv, int D, float sm_scale, uint16_t* out, int64_t o_sb,
+                                      int64_t o_sh, float* lse, float* partial_out, void* workspace,
+                                      size_t workspace_bytes, int* status, void* stream) {
+  if (max_blocks > 0 && !block_table) return AKV_ERR_NULL;
+  return decode_impl(q, q_sb, q_sh, hot_k, hot_v, h_sb, h_sh, h_sn, n_hot, hot_len, pool, 0, head_stride,
+                     block_table, bt_stride, page_stride, n_pages, layout, max_blocks, warm_len, B, Hq, Hkv, D, sm_scale, out,
+                     o_sb, o_sh, lse, partial_out, workspace, workspace_bytes, status, stream);
 }
 
 extern "C" int akv_lse_combine(const float* part, int64_t part_ss, int64_t part_sr, int rows, int splits, int D,

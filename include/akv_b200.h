@@ -244,6 +244,29 @@ int akv_mixed_decode(const uint16_t* q, int64_t q_sb, int64_t q_sh,
                      uint16_t* out, int64_t o_sb, int64_t o_sh, float* lse, float* partial_out,
                      void* workspace, size_t workspace_bytes, int* status, void* stream);
 
+/* Paged form of akv_mixed_decode for a pool of block records shared by many
+ * sequences (continuous batching).  Replaces the attention call of the
+ * reference's vLLM backend, AdaptiveAttentionBackend.forward
+ * (akv/vllm_integration.py:304-343), which attends per sequence over a
+ * per-sequence cache.  Row b's warm block j (j < warm_len[b] <= max_blocks) is
+ * the record of KV head h at
+ *     pool + block_table[b*bt_stride + j]*page_stride + h*head_stride
+ * (one page = the records of one 32-token block for every KV head, e.g.
+ * page_stride = Hkv*layout.bytes, head_stride = layout.bytes).  bt_stride >=
+ * max_blocks.  A table entry outside [0, n_pages) records AKV_ERR_SHAPE in
+ * *status and reads page 0 instead.  Everything else, the workspace
+ * (akv_decode_workspace_bytes with n_warm_blocks = max_blocks) included, is as
+ * for akv_mixed_decode. */
+int akv_mixed_decode_paged(const uint16_t* q, int64_t q_sb, int64_t q_sh,
+                           const uint16_t* hot_k, const uint16_t* hot_v, int64_t h_sb, int64_t h_sh, int64_t h_sn,
+                           int n_hot, const int32_t* hot_len,
+                           const uint8_t* pool, int n_pages, int64_t page_stride, int64_t head_stride,
+                           const int32_t* block_table, int64_t bt_stride, const akv_warm_layout* layout,
+                           int max_blocks, const int32_t* warm_len,
+                           int B, int Hq, int Hkv, int D, float sm_scale,
+                           uint16_t* out, int64_t o_sb, int64_t o_sh, float* lse, float* partial_out,
+                           void* workspace, size_t workspace_bytes, int* status, void* stream);
+
 /* Zero-allocation form of akv_mixed_decode (no counterpart in the reference,
  * which has no native interface).  For callers that cannot allocate device
  * memory on their decode path (e.g. an attention hook inside another serving

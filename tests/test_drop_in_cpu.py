@@ -173,3 +173,15 @@ def test_fused_placeholder_and_warm_append_on_cpu():
     q = torch.randn(1, 4, 1, 128).half()
     with pytest.raises(RuntimeError):
         hook.akv_attention_forward(None, q, k, v, None, scaling=128 ** -0.5)
+
+
+def test_vllm_engine_config_and_no_cpu_fallback():
+    """AdaptiveVLLMConfig keeps the reference's fields and defaults
+    (akv/vllm_integration.py:48-75); the engine refuses a CPU device."""
+    from akv.vllm_integration import AdaptiveCacheEngine, AdaptiveVLLMConfig
+    c = AdaptiveVLLMConfig()
+    assert (c.hot_budget_per_seq, c.warm_budget_per_seq, c.cold_budget_per_seq, c.warm_bits, c.cold_bits,
+            c.group_size, c.eviction_trigger_ratio, c.eviction_batch_size, c.initial_tokens_protected,
+            c.recent_tokens_protected, c.importance_decay) == (1024, 4096, 8192, 4, 2, 128, 0.9, 64, 4, 32, 0.95)
+    with pytest.raises(RuntimeError):
+        AdaptiveCacheEngine(c, num_layers=1, num_heads=2, head_dim=128, device="cpu")
