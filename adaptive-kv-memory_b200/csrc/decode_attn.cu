@@ -683,7 +683,10 @@ AKV_DEV void warm_block(WarpState& st, const uint8_t* r, uint32_t mask, const ui
   }
 }
 
-template <int KB, int VB, int NOUT>
+// PAGED: warm records are found through the block table (p.btab), else row
+// b's records are contiguous; a compile-time choice, so the contiguous kernel
+// carries no table logic.
+template <int KB, int VB, int NOUT, bool PAGED>
 __global__ void __launch_bounds__(kDecodeThreads, 4) mixed_decode_kernel(const DecodeParams p) {
   constexpr RecLayout R = rec_layout(kHeadDim, KB, VB, 0);
   extern __shared__ __align__(128) unsigned char smem[];
@@ -733,7 +736,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 4) mixed_decode_kernel(const D
     const int blo = split * p.wbps;
     const int bhi = min(nblk_b, blo + p.wbps);
     const int nb = max(0, bhi - blo);
-    if (p.btab) {
+    if constexpr (PAGED) {
       wtab = p.btab + b * p.bt_sb + blo;
       wbase = p.warm + kvh * p.w_sh;
     } else {
@@ -747,12 +750,12 @@ __global__ void __launch_bounds__(kDecodeThreads, 4) mixed_decode_kernel(const D
       fence_mbar_init();
       for (int li = 0; li < min(nmine, kStagesPerWarp); ++li) {
         const int i = warp + kConsumerWarps * li;
-        const uint8_t* src = wtab ? wbase + static_cast<int64_t>(page_at(i)) * p.w_page
-                                  : wbase + static_cast<int64_t>(i) * rec;
+        const uint8_t* src = PAGED ? wbase + static_cast<int64_t>(page_at(i)) * p.w_page
+                                   : wbase + static_cast<int64_t>(i) * rec;
         mbar_arrive_expect_tx(&wbar[li], rec);
         tma_load_1d(wstage + li * rec, src, rec, &wbar[li]);
       }
-      if (wtab && kStagesPerWarp < nmine) next_page = page_at(warp + kConsumerWarps * kStagesPerWarp);
+      if (PAGED && kStagesPerWarp < nmine) next_page = page_at(warp + kConsumerWarps * kStagesPerWarp);
     }
     __syncwarp();
   }
@@ -804,9 +807,9 @@ __global__ void __launch_bounds__(kDecodeThreads, 4) mixed_decode_kernel(const D
       __syncwarp();
       if (lane == 0 && li + kStagesPerWarp < nmine) {
         const int i = warp + kConsumerWarps * (li + kStagesPerWarp);
-        const uint8_t* src = wtab ? wbase + static_cast<int64_t>(next_page) * p.w_page
-                                  : wbase + static_cast<int64_t>(i) * rec;
-        if (wtab && li + kStagesPerWarp + 1 < nmine) next_page = page_at(i + kConsumerWarps);
+        const uint8_t* src = PAGED ? wbase + static_cast<int64_t>(next_page) * p.w_page
+                                   : wbase + static_cast<int64_t>(i) * rec;
+        if (PAGED && li + kStagesPerWarp + 1 < nmine) next_page = page_at(i + kConsumerWarps);
         fence_proxy_async_shared();
         mbar_arrive_expect_tx(&wbar[s], rec);
         tma_load_1d(wstage + s * rec, src, rec, &wbar[s]);
@@ -1068,7 +1071,7 @@ static size_t decode_smem_bytes(int rec_bytes) {
 template <int KB, int VB, int NOUT>
 static int launch_decode3(const DecodeParams& p, cudaStream_t st) {
   const size_t smem = decode_smem_bytes(p.L.bytes);
-  auto kern = mixed_decode_kernel<KB, VB, NOUT>;
+  auto kern = p.btab ? mixed_decode_kernel<KB, VB, NOUT, true> : mixed_decode_kernel<KB, VB, NOUT, false>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
       cudaSuccess)
     return AKV_ERR_LAUNCH;

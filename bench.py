@@ -257,6 +257,75 @@ def decode_shapes_bench(torch, akv, dev, reps: int = 20) -> dict:
     return out
 
 
+# ---------------------------------------------------------------------------- paged pool (vLLM-style batch)
+def paged_bench(torch, akv, dev, n_seqs: int = 64, reps: int = 20) -> dict:
+    """Continuous-batching shape: `n_seqs` sequences with seeded ragged warm
+    lengths (1,024 to 30,720 tokens, multiples of 32) and a full 512-token
+    hot window each, Llama-3-8B heads (32 Q / 8 KV, D 128), k4v2 + 1 %
+    outliers, pages handed out in a shuffled order.  Device time of one
+    layer's decode as one akv_mixed_decode_paged launch over the batch,
+    against one launch per sequence (the reference backend's per-sequence
+    forward).  Both as CUDA graphs replayed `reps` times."""
+    from akv.paged import PagedWarmPool, paged_decode_attention
+    Hq, Hkv, D, hot = 32, 8, 128, 512
+    g = torch.Generator().manual_seed(21)
+    lens = [32 * int(x) for x in torch.randint(32, 961, (n_seqs,), generator=g)]
+    nblk = [n // 32 for n in lens]
+    pool = PagedWarmPool(sum(nblk), Hkv, D, 4, 2, 0.01, device=dev)
+    order = torch.randperm(sum(nblk), generator=g).tolist()
+    pool._free = list(reversed(order))
+    gd = torch.Generator(device=dev).manual_seed(22)
+    table = torch.zeros(n_seqs, max(nblk), dtype=torch.int32)
+    for b, n in enumerate(lens):
+        pg = pool.alloc(nblk[b])
+        pool.write(make_kv(torch, gd, (1, Hkv, n, D), dev), make_kv(torch, gd, (1, Hkv, n, D), dev, (5,)), pg)
+        table[b, :len(pg)] = torch.tensor(pg, dtype=torch.int32)
+    table = table.to(dev)
+    wl = torch.tensor(nblk, dtype=torch.int32, device=dev)
+    hk = make_kv(torch, gd, (n_seqs, Hkv, hot, D), dev)
+    hv = make_kv(torch, gd, (n_seqs, Hkv, hot, D), dev)
+    hl = torch.full((n_seqs,), hot, dtype=torch.int32, device=dev)
+    q = torch.randn(n_seqs, Hq, D, generator=gd, device=dev).half()
+    o = torch.empty_like(q)
+
+    def batched():
+        paged_decode_attention(q, hk, hv, hl, pool, table, wl, out=o)
+
+    def per_seq():
+        for b in range(n_seqs):
+            paged_decode_attention(q[b:b + 1], hk[b:b + 1], hv[b:b + 1], hl[b:b + 1], pool, table[b:b + 1],
+                                   wl[b:b + 1], out=o[b:b + 1])
+
+    res = {}
+    for name, fn in (("batched", batched), ("per_sequence", per_seq)):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fn()
+        graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        res[f"{name}_layer_us"] = round(e0.elapsed_time(e1) * 1e3 / reps, 2)
+        del graph
+    per_tok = D * 6 // 8 + 4 + 4 + 4  # k4v2 codes, V scale/zero, K+V outlier originals (1 channel)
+    alg = sum(n * per_tok + (n // 32) * D * 4 + hot * D * 4 for n in lens) * Hkv + 2 * n_seqs * Hq * D * 2
+    res["algorithmic_bytes"] = alg
+    res["batched_gbs"] = round(alg / (res["batched_layer_us"] * 1e-6) / 1e9, 1)
+    res["per_sequence_gbs"] = round(alg / (res["per_sequence_layer_us"] * 1e-6) / 1e9, 1)
+    res = {"workload": f"{n_seqs} sequences, warm 1,024-30,720 tokens (seeded), 512 hot each, 32/8 heads, "
+                       "k4v2 + 1% outliers, shuffled pages", "total_warm_tokens": sum(lens), **res}
+    del pool, hk, hv
+    torch.cuda.empty_cache()
+    return res
+
+
 # ---------------------------------------------------------------------------- HF decoding (config 2)
 def hf_decode_bench(torch, akv, dev, new_tokens: int = 256, prompt: int = 32768) -> dict:
     """Config 2 end to end: a Qwen2.5-1.5B-shaped random-init decoder (28
@@ -524,6 +593,7 @@ def run_ours(args):
             torch.cuda.empty_cache()
         if world == 1 and not args.no_shapes:
             res["decode_shapes"] = decode_shapes_bench(torch, akv, dev)
+            res["paged_decode"] = paged_bench(torch, akv, dev)
         if world == 1 and args.hf_tokens > 0:
             res["hf_decode"] = hf_decode_bench(torch, akv, dev, new_tokens=args.hf_tokens)
         if world == 1 and not args.no_cpu_baseline:
