@@ -38,7 +38,7 @@ import torch
 
 from . import _C
 from .bitpack import packed_width
-from .packed_layout import BLOCK, WarmArena
+from .packed_layout import BLOCK, HeadGroupArena, WarmArena
 
 logger = logging.getLogger(__name__)
 
@@ -101,8 +101,6 @@ class AKVLayer(_LayerBase):
             self.keys = None
             self.values = None
             self.is_initialized = False
-        if per_head_bits is not None:
-            raise NotImplementedError("per-head warm bit widths are not supported by the packed warm tier")
         self.warm_bits = warm_bits
         self.hot_budget = hot_budget
         self.group_size = group_size
@@ -115,7 +113,10 @@ class AKVLayer(_LayerBase):
         self.warm_key_bits = warm_key_bits or warm_bits
         self.warm_value_bits = warm_value_bits or warm_bits
         self.outlier_fraction = outlier_fraction
-        self.per_head_bits = None
+        # bit width per KV head (calibrated caches, drop_in.py:315-374): K and V
+        # of head h at per_head_bits[h], each head quantised on its own; used
+        # when the list matches the head count, else the layer's widths apply
+        self.per_head_bits = list(per_head_bits) if per_head_bits is not None else None
         # decode steps (one new token) return a placeholder instead of the
         # chronological FP16 view; the "akv" attention function
         # (akv.hf_attention) attends over the packed warm records and the hot
@@ -173,8 +174,13 @@ class AKVLayer(_LayerBase):
         B, H, _, D = hk.shape
         n = int(demote_idx.numel())
         if self._warm is None:
-            self._warm = WarmArena(B, H, D, self.warm_key_bits, self.warm_value_bits, self.outlier_fraction,
-                                   max_blocks=max(4, (n + BLOCK - 1) // BLOCK), device=hk.device)
+            cap = max(4, (n + BLOCK - 1) // BLOCK)
+            if self.per_head_bits is not None and len(self.per_head_bits) == H:
+                self._warm = HeadGroupArena(B, self.per_head_bits, D, self.outlier_fraction, max_blocks=cap,
+                                            device=hk.device)
+            else:
+                self._warm = WarmArena(B, H, D, self.warm_key_bits, self.warm_value_bits, self.outlier_fraction,
+                                       max_blocks=cap, device=hk.device)
         arena = self._warm
         nblk = (n + BLOCK - 1) // BLOCK
         arena.grow(arena.n_blocks + nblk)
@@ -183,8 +189,12 @@ class AKVLayer(_LayerBase):
         slots = torch.arange(blk0 * BLOCK, blk0 * BLOCK + n, dtype=torch.int64, device=hk.device)
         self._warm_slots = slots if self._warm_slots is None else torch.cat([self._warm_slots, slots])
         # the reference's measure_packed_bytes of this event's K and V dicts (drop_in.py:331-336)
-        kb, vb = self.warm_key_bits, self.warm_value_bits
-        self._warm_bytes_packed += B * (H * n * packed_width(D, kb) + 4 * H * D + H * n * packed_width(D, vb) + 4 * H * n)
+        if isinstance(arena, HeadGroupArena):  # one K and one V dict per head, at that head's width
+            self._warm_bytes_packed += B * sum(2 * n * packed_width(D, b) + 4 * D + 4 * n for b in self.per_head_bits)
+        else:
+            kb, vb = self.warm_key_bits, self.warm_value_bits
+            self._warm_bytes_packed += B * (H * n * packed_width(D, kb) + 4 * H * D + H * n * packed_width(D, vb)
+                                            + 4 * H * n)
         if not self._no_fp16_copy:
             self._append_warm_fp16(*arena.dequantize(tok_idx=slots))
 
@@ -234,13 +244,7 @@ class AKVLayer(_LayerBase):
         keep = ~promote_mask
         gone = self._warm_slots[promote_mask.to(self._warm_slots.device)]
         if self._warm is not None and gone.numel():
-            words = self._warm.buf[:, :, :, self._warm.layout.mask:self._warm.layout.mask + 4]
-            m = words.contiguous().view(torch.int32)[..., 0]
-            blk = gone // BLOCK
-            bit = torch.ones_like(gone, dtype=torch.int64) << (gone % BLOCK)
-            clear = torch.zeros(m.shape[-1], dtype=torch.int64, device=m.device).index_add_(0, blk, bit)
-            m &= (~clear).to(torch.int32)
-            words.copy_(m.unsqueeze(-1).view(torch.uint8).view(words.shape))
+            self._warm.drop_slots(gone)
         self._warm_keys_fp16 = self._warm_keys_fp16[:, :, keep, :]
         self._warm_values_fp16 = self._warm_values_fp16[:, :, keep, :]
         self._warm_slots = self._warm_slots[keep.to(self._warm_slots.device)]
@@ -415,6 +419,8 @@ class AKVLayer(_LayerBase):
         """One decode query (B, Hq, 1, D) over the packed warm records and the
         FP16 hot tier, in place (akv_mixed_decode).  Returns (B, Hq, 1, D)."""
         from .fused_attention import mixed_tier_decode_attention
+        if isinstance(self._warm, HeadGroupArena):
+            return self._warm.decode(query, self._hot_keys, self._hot_values, sm_scale=sm_scale)
         return mixed_tier_decode_attention(query, self._hot_keys, self._hot_values, self._warm, sm_scale=sm_scale)
 
     # ------------------------------------------------------------------ accounting
@@ -506,6 +512,28 @@ class AKVCache(_CacheBase):
                 self._protected_set.add(p)
         super().__init__()
         self._seen_tokens = 0
+        self._calibration_per_head_bits: dict = {}
+
+    @classmethod
+    def from_calibration(cls, calibration_path, **overrides) -> "AKVCache":
+        """Cache from a calibration report JSON (reference drop_in.py:1281-1313):
+        protect window and layer count from the report, ``warm_bits`` from its
+        average bits when in [2, 4] (else its preset), the per-(layer, head)
+        bit widths applied to each layer; ``overrides`` win."""
+        import json
+        with open(calibration_path) as f:
+            rep = json.load(f)
+        kwargs = dict(protect_first=rep["recommended_protect_first"], protect_last=rep["recommended_protect_last"],
+                      num_hidden_layers=rep["num_layers"])
+        avg = float(rep["recommended_average_bits"])
+        if 2.0 <= avg <= 4.0:
+            kwargs["warm_bits"] = int(round(avg))
+        else:
+            kwargs["preset"] = rep["recommended_preset"]
+        kwargs.update(overrides)
+        cache = cls(**kwargs)
+        cache._calibration_per_head_bits = {int(k): list(v) for k, v in rep.get("per_head_bits", {}).items()}
+        return cache
 
     @classmethod
     def for_model(cls, model, **kwargs) -> "AKVCache":
@@ -528,7 +556,8 @@ class AKVCache(_CacheBase):
                         enable_promotion_proxy=self.enable_promotion_proxy, proxy_decay=self.proxy_decay,
                         adaptive_hot_frac=self.adaptive_hot_frac, warm_key_bits=self.warm_key_bits,
                         warm_value_bits=self.warm_value_bits, outlier_fraction=self.outlier_fraction,
-                        fused_decode=self.fused_decode)
+                        fused_decode=self.fused_decode,
+                        per_head_bits=self._calibration_per_head_bits.get(idx))
 
     def update(self, key_states: torch.Tensor, value_states: torch.Tensor, layer_idx: int,
                cache_kwargs: Optional[dict[str, Any]] = None, *args, **kwargs) -> Tuple[torch.Tensor, torch.Tensor]:

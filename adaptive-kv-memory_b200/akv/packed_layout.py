@@ -190,6 +190,38 @@ class WarmArena:
         m = self.buf[:, :, : self.n_blocks, L.mask:L.mask + 4].contiguous().view(torch.int32)
         return m[..., 0].to(torch.int64) & 0xFFFFFFFF
 
+    def write_head(self, k: torch.Tensor, v: torch.Tensor, src_head: int, dst_head: int, blk0: int, group: int,
+                   tok_idx: torch.Tensor | None = None) -> None:
+        """Quantise model head ``src_head`` of (B, H, N, D) K/V (gathered by
+        ``tok_idx``) on its own (outlier channels from that head alone) into
+        arena head ``dst_head``, blocks from ``blk0``.  Does not move
+        ``n_blocks``."""
+        _C.require_cuda(k, v)
+        B, N, D = k.shape[0], (k.shape[2] if tok_idx is None else tok_idx.shape[-1]), k.shape[3]
+        ti = None if tok_idx is None else tok_idx.contiguous()
+        tsb = 0 if ti is None or ti.dim() == 1 else ti.stride(0)
+        rec = self.rec
+        sb, sh = self.H * self.max_blocks * rec, self.max_blocks * rec
+        for x, is_key, bits in ((k, True, self.key_bits), (v, False, self.value_bits)):
+            xh = x[:, src_head:src_head + 1]
+            if xh.stride(-1) != 1:
+                xh = xh.contiguous()
+            dest = record_dest(self.layout, self._base(blk0) + dst_head * sh, sb, sh, rec, is_key)
+            _C.quantize(xh.data_ptr(), xh.stride(0), xh.stride(1), xh.stride(2),
+                        None if ti is None else ti.data_ptr(), tsb,
+                        B, 1, N, D, bits, is_key, min(group, N), self.n_out, dest, None, x.device)
+
+    def drop_slots(self, slots: torch.Tensor) -> None:
+        """Drop warm tokens (slot = blk*32 + s, int64 on the device) from every
+        row and head by clearing their mask bits (promotion)."""
+        words = self.buf[:, :, :, self.layout.mask:self.layout.mask + 4]
+        m = words.contiguous().view(torch.int32)[..., 0]
+        blk = slots // BLOCK
+        bit = torch.ones_like(slots, dtype=torch.int64) << (slots % BLOCK)
+        clear = torch.zeros(m.shape[-1], dtype=torch.int64, device=m.device).index_add_(0, blk, bit)
+        m &= (~clear).to(torch.int32)
+        words.copy_(m.unsqueeze(-1).view(torch.uint8).view(words.shape))
+
     def clear_slots(self, blk: torch.Tensor, slot_mask: torch.Tensor) -> None:
         """Drop tokens from the warm tier by clearing their mask bits (promotion)."""
         L = self.layout
@@ -204,3 +236,106 @@ class WarmArena:
 
     def resident_bytes(self) -> int:
         return self.buf.numel()
+
+
+class HeadGroupArena:
+    """Warm tier of a layer whose KV heads have their own bit widths
+    (reference drop_in.py:315-374, ``per_head_bits``): one ``WarmArena`` per
+    distinct width over that width's heads (K and V at the head's width, as
+    the reference's per-width quantiser pool), every head quantised on its
+    own like the reference's per-head quantiser calls.  Block j of every
+    group's arena holds the same tokens, so slots and masks agree across
+    groups.  Offers the ``WarmArena`` surface the cache uses, and ``decode``:
+    one mixed-tier decode launch per width group over that group's query
+    heads."""
+
+    def __init__(self, batch: int, per_head_bits: list, head_dim: int, outlier_fraction: float = 0.0,
+                 max_blocks: int = 64, device="cuda"):
+        self.B, self.H, self.D = batch, len(per_head_bits), head_dim
+        self.per_head_bits = list(per_head_bits)
+        self.groups = []  # (bits, model heads, arena)
+        for bits in sorted(set(per_head_bits)):
+            heads = [h for h, b in enumerate(per_head_bits) if b == bits]
+            self.groups.append((bits, heads, WarmArena(batch, len(heads), head_dim, bits, bits, outlier_fraction,
+                                                       max_blocks=max_blocks, device=device)))
+        self.max_blocks = max_blocks
+        self.n_blocks = 0
+        self._idx: dict = {}
+
+    @property
+    def device(self):
+        return self.groups[0][2].device
+
+    def _index(self, key, values) -> torch.Tensor:
+        t = self._idx.get(key)
+        if t is None:
+            t = self._idx[key] = torch.tensor(values, dtype=torch.int64, device=self.device)
+        return t
+
+    def grow(self, min_blocks: int) -> None:
+        for _, _, a in self.groups:
+            a.grow(min_blocks)
+        self.max_blocks = self.groups[0][2].max_blocks
+
+    def append(self, k: torch.Tensor, v: torch.Tensor, group: int = BLOCK, tok_idx: torch.Tensor | None = None) -> int:
+        N = k.shape[2] if tok_idx is None else tok_idx.shape[-1]
+        nblk = (N + BLOCK - 1) // BLOCK
+        if self.n_blocks + nblk > self.max_blocks:
+            raise RuntimeError(f"warm arena full ({self.n_blocks}+{nblk} > {self.max_blocks} blocks)")
+        blk0 = self.n_blocks
+        for _, heads, a in self.groups:
+            for j, h in enumerate(heads):
+                a.write_head(k, v, h, j, blk0, group, tok_idx)
+            a.n_blocks = blk0 + nblk
+        self.n_blocks = blk0 + nblk
+        return blk0
+
+    def dequantize(self, tok_idx: torch.Tensor | None = None, n_tokens: int | None = None) -> tuple:
+        N = tok_idx.shape[-1] if tok_idx is not None else (n_tokens if n_tokens is not None
+                                                            else self.n_blocks * BLOCK)
+        out_k = torch.empty(self.B, self.H, N, self.D, dtype=torch.float16, device=self.device)
+        out_v = torch.empty_like(out_k)
+        for bits, heads, a in self.groups:
+            dk, dv = a.dequantize(tok_idx=tok_idx, n_tokens=n_tokens)
+            idx = self._index(("kv", bits), heads)
+            out_k.index_copy_(1, idx, dk)
+            out_v.index_copy_(1, idx, dv)
+        return out_k, out_v
+
+    def masks(self) -> torch.Tensor:
+        out = torch.empty(self.B, self.H, self.n_blocks, dtype=torch.int64, device=self.device)
+        for bits, heads, a in self.groups:
+            out.index_copy_(1, self._index(("kv", bits), heads), a.masks())
+        return out
+
+    def drop_slots(self, slots: torch.Tensor) -> None:
+        for _, _, a in self.groups:
+            a.drop_slots(slots)
+
+    def select_batch(self, index: torch.Tensor) -> None:
+        for _, _, a in self.groups:
+            a.select_batch(index)
+        self.B = self.groups[0][2].B
+
+    def packed_bytes(self) -> int:
+        return sum(a.packed_bytes() for _, _, a in self.groups)
+
+    def resident_bytes(self) -> int:
+        return sum(a.resident_bytes() for _, _, a in self.groups)
+
+    def decode(self, query: torch.Tensor, hot_keys: torch.Tensor, hot_values: torch.Tensor,
+               sm_scale: float | None = None) -> torch.Tensor:
+        """query (B, Hq, 1, D) over the hot tier and every group's records ->
+        (B, Hq, 1, D): each width group attends its own query heads (GQA
+        head h // (Hq / H)) in one launch."""
+        from .fused_attention import mixed_tier_decode_attention
+        Hq = query.shape[1]
+        g = Hq // self.H
+        out = torch.empty_like(query)
+        for bits, heads, a in self.groups:
+            qi = self._index(("q", bits, g), [h * g + i for h in heads for i in range(g)])
+            ki = self._index(("kv", bits), heads)
+            o = mixed_tier_decode_attention(query.index_select(1, qi), hot_keys.index_select(1, ki),
+                                            hot_values.index_select(1, ki), a, sm_scale=sm_scale)
+            out.index_copy_(1, qi, o)
+        return out

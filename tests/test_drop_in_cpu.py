@@ -185,3 +185,22 @@ def test_vllm_engine_config_and_no_cpu_fallback():
             c.recent_tokens_protected, c.importance_decay) == (1024, 4096, 8192, 4, 2, 128, 0.9, 64, 4, 32, 0.95)
     with pytest.raises(RuntimeError):
         AdaptiveCacheEngine(c, num_layers=1, num_heads=2, head_dim=128, device="cpu")
+
+
+def test_from_calibration_applies_per_head_bits(tmp_path):
+    """AKVCache.from_calibration (reference drop_in.py:1281-1313) on a report
+    JSON: protect window, layer count, warm bits from the average, and the
+    per-(layer, head) widths handed to each layer."""
+    import json
+    rep = {"recommended_protect_first": 1, "recommended_protect_last": 0, "num_layers": 3,
+           "recommended_average_bits": 3.2, "recommended_preset": "balanced",
+           "per_head_bits": {"1": [2, 4], "2": [4, 4]}}
+    path = tmp_path / "calib.json"
+    path.write_text(json.dumps(rep))
+    cache = AKVCache.from_calibration(str(path), hot_budget=64)
+    assert cache.warm_bits == 3 and cache.hot_budget == 64 and cache.num_hidden_layers == 3
+    x = torch.zeros(1, 2, 4, 128, dtype=torch.float16)
+    for i in range(3):
+        cache.update(x, x, i)
+    assert cache.layers[0].protect and cache.layers[0].per_head_bits is None
+    assert cache.layers[1].per_head_bits == [2, 4] and cache.layers[2].per_head_bits == [4, 4]

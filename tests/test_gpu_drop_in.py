@@ -147,3 +147,42 @@ def test_generate_under_demotion_and_beam_ops():
     assert layer._hot_keys.shape[0] == 2 and layer._warm.B == 2 and layer._warm_keys_fp16.shape[0] == 2
     cache.batch_select_indices(torch.tensor([1], device=DEV))
     assert layer._hot_keys.shape[0] == 1 and layer._warm.buf.shape[0] == 1
+
+
+@pytest.mark.parametrize("frac", [0.0, 0.05])
+def test_per_head_bits_match_reference_per_head_quantisation(frac):
+    """per_head_bits (reference drop_in.py:315-374): head h is quantised on
+    its own at per_head_bits[h] (K and V), outlier channels from that head
+    alone.  The warm copy must equal the oracle's per-head quantiser calls
+    bit for bit; the fused decode over the per-width arenas must match SDPA
+    over the chronological view."""
+    from akv import AKVLayer
+    from oracle import akv_oracle as O
+    bits = [2, 4, 3, 4]
+    g = torch.Generator(device=DEV).manual_seed(11)
+    k = torch.randn(1, 4, 100, 128, generator=g, device=DEV)
+    k[..., 9] *= 12
+    k, v = k.half(), torch.randn(1, 4, 100, 128, generator=g, device=DEV).half()
+    layer = AKVLayer(warm_bits=3, hot_budget=40, enable_promotion=False, enable_promotion_proxy=False,
+                     per_head_bits=bits, outlier_fraction=frac)
+    layer.update(k, v)
+    pos = layer._warm_positions.tolist()
+    assert len(pos) == 60
+    kn, vn = k.cpu().numpy(), v.cpu().numpy()
+    for h, b in enumerate(bits):
+        rk = O.dequantize_keys(O.quantize_keys(kn[0, h:h + 1][:, pos], b, frac))
+        rv = O.dequantize_values(O.quantize_values(vn[0, h:h + 1][:, pos], b, frac))
+        np.testing.assert_array_equal(layer._warm_keys_fp16[0, h:h + 1].cpu().numpy().view(np.uint16), rk.view(np.uint16))
+        np.testing.assert_array_equal(layer._warm_values_fp16[0, h:h + 1].cpu().numpy().view(np.uint16), rv.view(np.uint16))
+    pw = {2: 32, 3: 48, 4: 64}
+    assert layer.memory_usage_bytes()["warm_bytes_packed"] == sum(2 * 60 * pw[b] + 4 * 128 + 4 * 60 for b in bits)
+    # one decode step through the per-width arenas
+    k1 = torch.randn(1, 4, 1, 128, generator=g, device=DEV).half()
+    layer.update(k1, k1.clone())
+    q = torch.randn(1, 8, 1, 128, generator=g, device=DEV).half()
+    out = layer.decode_attention(q, 128 ** -0.5).float()
+    fk, fv = layer.full_view()
+    K, V = fk.float().repeat_interleave(2, 1), fv.float().repeat_interleave(2, 1)
+    p = torch.softmax(torch.einsum("bhqd,bhnd->bhqn", q.float(), K) / 128 ** 0.5, -1)
+    ref = torch.einsum("bhqn,bhnd->bhqd", p, V)
+    assert (out - ref).abs().max().item() <= 2e-3
