@@ -162,10 +162,12 @@ AKV_DEV bool fast_coef(__half s, __half& m, __half& ns, __half& r) {
   return true;
 }
 
-template <int BITS>
+// UNIT: every multiplier m of the group is 1 (all scales >= 1/8), so d needs no rescale.
+template <int BITS, bool UNIT = false>
 AKV_DEV uint32_t encode_pair16(uint32_t x2, uint32_t z2, uint32_t m2, uint32_t ns2, uint32_t r2) {
   constexpr uint32_t top = kMagic2 + ((1u << BITS) - 1) * 0x00010001u;
-  const __half2 d = __hmul2_rn(__hsub2_rn(u32_as_h2(x2), u32_as_h2(z2)), u32_as_h2(m2));
+  const __half2 x_z = __hsub2_rn(u32_as_h2(x2), u32_as_h2(z2));
+  const __half2 d = UNIT ? x_z : __hmul2_rn(x_z, u32_as_h2(m2));
   const __half2 q0 = __hmul2_rn(d, u32_as_h2(r2));
   const __half2 q = __hfma2(__hfma2(u32_as_h2(ns2), q0, d), u32_as_h2(r2), q0);
   return h2_as_u32(__hmin2(__hadd2_rn(q, u32_as_h2(kMagic2)), u32_as_h2(top)));
@@ -546,6 +548,7 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
   }
 
   bool all_fast = true;  // every scale of the group takes the fp16 path
+  bool all_unit = true;  // ... and needs no power-of-two rescale (m = 1)
   if constexpr (IS_KEY) {
     // ---- keys: scale per (head, channel pair); 1/scale for the encoder; the
     //      scale / zero rows of every block record the group covers
@@ -575,6 +578,7 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
         all_fast = false;
       }
       km[w] = h2_as_u32(__halves2half2(m0, m1));
+      all_unit = all_unit && km[w] == 0x3C003C00u;
       kns[w] = h2_as_u32(__halves2half2(n0, n1));
       kr[w] = h2_as_u32(__halves2half2(r0, r1));
       if (p.dst.pair_order) {  // warm records: each 32-channel chunk in the decode pair order
@@ -627,6 +631,7 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
         fm = fns = fr = __ushort_as_half(0);
         all_fast = false;
       }
+      all_unit = all_unit && __half_as_ushort(fm) == 0x3C00u;
       vco[r] = make_uint4(__half_as_ushort(lo) | (static_cast<uint32_t>(__half_as_ushort(fm)) << 16),
                           __half_as_ushort(fns) | (static_cast<uint32_t>(__half_as_ushort(fr)) << 16),
                           __float_as_uint(-se), __float_as_uint(rc));
@@ -644,6 +649,7 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
     }
   }
   all_fast = __syncthreads_and(all_fast);
+  all_unit = __syncthreads_and(all_unit) && all_fast;
 
   // ---- encode + pack: a work item is 8 channels of one head; its threads walk
   //      the tokens.  Keys keep the 8 channels' coefficients in registers and
@@ -672,7 +678,15 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
 #pragma unroll
           for (int i = 0; i < 4; ++i) fast = fast && (m2[i] & 0x7FFFu) && (m2[i] & 0x7FFF0000u);
         }
-        if (fast) {
+        if (all_unit) {
+          walk_tokens(sub, nt, tpc, xcol, D, cbase, cv, [&](const __half* x, char* c, int) {
+            uint32_t x2[4], mm[4];
+            lds_u32x4(x, x2);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) mm[i] = encode_pair16<BITS, true>(x2[i], z2[i], m2[i], ns2[i], r2[i]);
+            if (c) store_packed8<BITS>(c, pack8<BITS>(mm));
+          });
+        } else if (fast) {
           walk_tokens(sub, nt, tpc, xcol, D, cbase, cv, [&](const __half* x, char* c, int) {
             uint32_t x2[4], mm[4];
             lds_u32x4(x, x2);
@@ -698,6 +712,18 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
             if (c) store_packed8<BITS>(c, pack8<BITS>(mm));
           });
         }
+      } else if (all_unit) {
+        const uint4* vrow = vco + h * nt;
+        walk_tokens(sub, nt, tpc, xcol, D, cbase, cv, [&](const __half* x, char* c, int t) {
+          const uint2 rec = *reinterpret_cast<const uint2*>(vrow + t);
+          uint32_t x2[4], mm[4];
+          lds_u32x4(x, x2);
+          const uint32_t z2 = prmt(rec.x, rec.x, 0x1010);
+          const uint32_t ns2 = prmt(rec.y, rec.y, 0x1010), r2 = prmt(rec.y, rec.y, 0x3232);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) mm[i] = encode_pair16<BITS, true>(x2[i], z2, 0u, ns2, r2);
+          if (c) store_packed8<BITS>(c, pack8<BITS>(mm));
+        });
       } else if (all_fast) {
         const uint4* vrow = vco + h * nt;
         walk_tokens(sub, nt, tpc, xcol, D, cbase, cv, [&](const __half* x, char* c, int t) {
