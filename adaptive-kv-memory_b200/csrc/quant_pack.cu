@@ -557,6 +557,9 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
     for (int w = tid; w < H * D2; w += kQuantThreads) {
       const int h = w / D2, dp = w - h * D2;
       __half2 lo, sc;
+      // zero-range columns (max == min, the zeroed outlier channels among
+      // them): x - zero is 0 for every token, so any multiplier encodes them
+      bool flat0 = false, flat1 = false;
       if constexpr (MODE == kQuantEncode) {
         const size_t o = ((static_cast<size_t>(b) * p.n_groups + grp) * p.H + h0 + h) * D2 + dp;
         lo = reinterpret_cast<const __half2*>(p.ws_zero)[o];
@@ -564,7 +567,10 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
         reinterpret_cast<__half2*>(cz)[w] = lo;
       } else {
         lo = reinterpret_cast<const __half2*>(cz)[w];
-        sc = affine_scale2<BITS>(lo, reinterpret_cast<const __half2*>(cs)[w]);
+        const __half2 hi = reinterpret_cast<const __half2*>(cs)[w];
+        sc = affine_scale2<BITS>(lo, hi);
+        flat0 = __half2float(__low2half(hi)) == __half2float(__low2half(lo));
+        flat1 = __half2float(__high2half(hi)) == __half2float(__high2half(lo));
       }
       reinterpret_cast<__half2*>(cs)[w] = sc;
       if (!dq2_scale_ok(__low2half(sc)) || !dq2_scale_ok(__high2half(sc))) flg[h * nblk] = 1u;
@@ -578,7 +584,7 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
         all_fast = false;
       }
       km[w] = h2_as_u32(__halves2half2(m0, m1));
-      all_unit = all_unit && km[w] == 0x3C003C00u;
+      all_unit = all_unit && ((km[w] & 0xFFFFu) == 0x3C00u || flat0) && ((km[w] >> 16) == 0x3C00u || flat1);
       kns[w] = h2_as_u32(__halves2half2(n0, n1));
       kr[w] = h2_as_u32(__halves2half2(r0, r1));
       if (p.dst.pair_order) {  // warm records: each 32-channel chunk in the decode pair order
