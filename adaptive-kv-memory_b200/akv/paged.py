@@ -73,7 +73,9 @@ class PagedWarmPool:
         if run:
             target, base = None, self.buf[pages[0]].data_ptr()
         else:
-            target = torch.empty(nblk, H, self.rec, dtype=torch.uint8, device=self.device)
+            # zeroed: the unused slots of a partial block must decode to finite
+            # values (their weight is 0, and 0 * NaN would poison the output)
+            target = torch.zeros(nblk, H, self.rec, dtype=torch.uint8, device=self.device)
             base = target.data_ptr()
         sp = None if status is None else status.data_ptr()
         for x, is_key, bits in ((k, True, self.key_bits), (v, False, self.value_bits)):

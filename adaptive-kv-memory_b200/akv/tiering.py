@@ -34,6 +34,9 @@ def fused_importance_update(attention_weights: torch.Tensor, scores: torch.Tenso
     return scores
 
 
+_select_ws: dict = {}  # device -> selection workspace (histograms, threshold state, per-CTA counts)
+
+
 def select_bottomk(scores: torch.Tensor, k: int, protect_first: int = 4, protect_last: int = 16) -> torch.Tensor:
     """Ascending int64 indices of the k lowest scores, protected ends excluded; ties lowest index first."""
     _C.require_cuda(scores)
@@ -42,8 +45,13 @@ def select_bottomk(scores: torch.Tensor, k: int, protect_first: int = 4, protect
     out = torch.empty(k, dtype=torch.int64, device=s.device)
     if k == 0:
         return out
+    need = _C.workspace_bytes("akv_select_workspace_bytes", n)
+    key = (s.device.type, s.device.index)
+    ws = _select_ws.get(key)
+    if ws is None or ws.numel() < need:
+        ws = _select_ws[key] = torch.empty(need, dtype=torch.uint8, device=s.device)
     _C.check(_C.load().akv_select_bottomk(s.data_ptr(), n, k, protect_first, protect_last, out.data_ptr(),
-                                          None, 0, _C.stream_of(s)), "akv_select_bottomk")
+                                          ws.data_ptr(), ws.numel(), _C.stream_of(s)), "akv_select_bottomk")
     return out
 
 

@@ -69,7 +69,27 @@ __global__ void migrator_reduce_kernel(const float* __restrict__ scores, const i
   __shared__ float smax[32], rmax[32];
   __shared__ float amin[32];
   float a = -INFINITY, r = -INFINITY, t = INFINITY;
-  for (int i = threadIdx.x; i < N; i += blockDim.x) {
+  // four positions per thread and trip with 16-byte loads when all three
+  // arrays are 16-byte aligned (several loads in flight per thread), the
+  // rest one by one
+  const bool vec = ((reinterpret_cast<uintptr_t>(scores) | reinterpret_cast<uintptr_t>(retrieval) |
+                     reinterpret_cast<uintptr_t>(access)) & 15u) == 0;
+  int done = 0;
+  if (vec) {
+    const int ng = N / 4;
+    for (int g = threadIdx.x; g < ng; g += blockDim.x) {
+      const float4 sv = __ldg(reinterpret_cast<const float4*>(scores) + g);
+      const float4 rv = __ldg(reinterpret_cast<const float4*>(retrieval) + g);
+      const longlong2 a0 = __ldg(reinterpret_cast<const longlong2*>(access) + 2 * g);
+      const longlong2 a1 = __ldg(reinterpret_cast<const longlong2*>(access) + 2 * g + 1);
+      a = fmaxf(fmaxf(a, fmaxf(sv.x, sv.y)), fmaxf(sv.z, sv.w));
+      r = fmaxf(fmaxf(r, fmaxf(rv.x, rv.y)), fmaxf(rv.z, rv.w));
+      t = fminf(fminf(t, fminf(static_cast<float>(a0.x), static_cast<float>(a0.y))),
+                fminf(static_cast<float>(a1.x), static_cast<float>(a1.y)));
+    }
+    done = 4 * ng;
+  }
+  for (int i = done + threadIdx.x; i < N; i += blockDim.x) {
     a = fmaxf(a, scores[i]);
     r = fmaxf(r, retrieval[i]);
     t = fminf(t, static_cast<float>(access[i]));  // access.float().min()
@@ -127,102 +147,223 @@ __global__ void migrator_importance_kernel(const float* __restrict__ scores, con
 // bottom-k selection with protected ends (akv/drop_in.py:392-413)
 //
 // Scores map to order-preserving u32 keys; protected positions get the key
-// of +inf.  A single CTA finds the k-th smallest key by an 8-bit radix select
-// (4 passes of a 256-bin histogram), then a stable compaction emits, in
-// ascending index order, every position below the threshold key plus the
-// first (k - count_below) positions equal to it.
+// of +inf.  The k-th smallest key is found by an 8-bit radix select (four
+// passes, most significant byte first), then a stable compaction emits, in
+// ascending index order, every position below that key plus the first
+// (k - count_below) positions equal to it.  Every step is a short launch
+// over the whole GPU (no CTA waits on another):
+//   per pass: sel_hist_kernel (per-CTA shared histograms of the keys that
+//   match the prefix so far, lanes of a warp that hit one bin adding with a
+//   single atomic, then added into the pass's global histogram) and
+//   sel_pick_kernel (one CTA: the bin holding the k-th key extends the prefix);
+//   then sel_count_kernel (per-CTA counts of keys below / equal to the
+//   threshold) and sel_compact_kernel (each CTA places its contiguous slice
+//   after the lower CTAs' counts and writes it in index order).
+// Workspace (u32): hist[4][256] (zeroed first), state {prefix, mask,
+// remaining}, counts[grid][2].
 // ---------------------------------------------------------------------------
-constexpr int kSelThreads = 1024;
+constexpr int kSelThreads = 256;
+constexpr int kSelWarps = kSelThreads / 32;
+constexpr int kSelMaxCtas = 2 * 148;
+constexpr size_t kSelWsWords = 4 * 256 + 4 + 2 * kSelMaxCtas;
 
 AKV_DEV uint32_t order_key(float f) {
   uint32_t u = __float_as_uint(f);
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-AKV_DEV uint32_t sel_key(const float* s, int i, int n, int pf, int pl) {
-  if (i < pf || i >= n - pl) return order_key(INFINITY);
-  return order_key(s[i]);
+// keys of positions 4g .. 4g+3 (beyond n: key 0, valid false); one 16-byte
+// load when the scores are 16-byte aligned
+AKV_DEV void sel_keys4(const float* s, bool vec, int g, int n, int pf, int pl, uint32_t (&key)[4], bool (&valid)[4]) {
+  const int i0 = 4 * g;
+  float v[4];
+  if (vec && i0 + 3 < n) {
+    const float4 f = __ldg(reinterpret_cast<const float4*>(s) + g);
+    v[0] = f.x;
+    v[1] = f.y;
+    v[2] = f.z;
+    v[3] = f.w;
+  } else {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) v[e] = i0 + e < n ? __ldg(s + i0 + e) : 0.f;
+  }
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const int i = i0 + e;
+    valid[e] = i < n;
+    key[e] = !valid[e] ? 0u : ((i < pf || i >= n - pl) ? order_key(INFINITY) : order_key(v[e]));
+  }
 }
 
-__global__ void __launch_bounds__(kSelThreads) select_bottomk_kernel(const float* __restrict__ scores, int n, int k,
-                                                                     int pf, int pl, int64_t* __restrict__ out) {
+struct SelArgs {
+  const float* scores;
+  int n, k, pf, pl, vec;
+  int ng, per_cta;  // 4-position groups in total / per CTA slice (multiple of 32)
+  uint32_t* ws;
+  int64_t* out;
+};
+
+AKV_DEV uint32_t* sel_hist(const SelArgs& a, int pass) { return a.ws + pass * 256; }
+AKV_DEV uint32_t* sel_state(const SelArgs& a) { return a.ws + 4 * 256; }
+AKV_DEV uint32_t* sel_counts(const SelArgs& a) { return a.ws + 4 * 256 + 4; }
+
+__global__ void __launch_bounds__(kSelThreads) sel_hist_kernel(const SelArgs a, int pass) {
   __shared__ uint32_t hist[256];
-  __shared__ uint32_t s_prefix, s_mask, s_remaining;
-  __shared__ uint32_t warp_cnt[kSelThreads / 32];
+  const int tid = threadIdx.x, lane = tid & 31;
+  hist[tid] = 0;
+  const uint32_t prefix = pass ? sel_state(a)[0] : 0u, mask = pass ? sel_state(a)[1] : 0u;
+  const int shift = 24 - 8 * pass;
+  __syncthreads();
+  const int g0 = blockIdx.x * a.per_cta, g1 = g0 + a.per_cta;
+  for (int g = g0 + tid; g < g1; g += kSelThreads) {  // per_cta is a multiple of 32: whole warps every trip
+    uint32_t key[4];
+    bool valid[4];
+    sel_keys4(a.scores, a.vec, g, a.n, a.pf, a.pl, key, valid);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const bool hit = valid[e] && (key[e] & mask) == prefix;
+      const uint32_t bin = (key[e] >> shift) & 255u;
+      const uint32_t voters = __ballot_sync(0xffffffffu, hit);
+      if (hit) {
+        const uint32_t peers = __match_any_sync(voters, bin);
+        if ((peers & ((1u << lane) - 1u)) == 0) atomicAdd(&hist[bin], __popc(peers));
+      }
+    }
+  }
+  __syncthreads();
+  const uint32_t c = hist[tid];
+  if (c) atomicAdd(&sel_hist(a, pass)[tid], c);
+}
+
+__global__ void sel_pick_kernel(const SelArgs a, int pass) {
+  if (threadIdx.x != 0) return;
+  uint32_t* st = sel_state(a);
+  const uint32_t prefix = pass ? st[0] : 0u, mask = pass ? st[1] : 0u;
+  const uint32_t rem = pass ? st[2] : static_cast<uint32_t>(a.k);
+  const uint32_t* h = sel_hist(a, pass);
+  const int shift = 24 - 8 * pass;
+  uint32_t acc = 0;
+  int bin = 0;
+  for (; bin < 255; ++bin) {
+    if (acc + h[bin] >= rem) break;
+    acc += h[bin];
+  }
+  st[0] = prefix | (static_cast<uint32_t>(bin) << shift);
+  st[1] = mask | (255u << shift);
+  st[2] = rem - acc;
+}
+
+// keys below / equal to the threshold in this CTA's slice
+__global__ void __launch_bounds__(kSelThreads) sel_count_kernel(const SelArgs a) {
+  __shared__ uint32_t wl[kSelWarps], we[kSelWarps];
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const uint32_t thr = sel_state(a)[0];
+  uint32_t c_lt = 0, c_eq = 0;
+  const int g0 = blockIdx.x * a.per_cta, g1 = g0 + a.per_cta;
+  for (int g = g0 + tid; g < g1; g += kSelThreads) {
+    uint32_t key[4];
+    bool valid[4];
+    sel_keys4(a.scores, a.vec, g, a.n, a.pf, a.pl, key, valid);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      c_lt += valid[e] && key[e] < thr;
+      c_eq += valid[e] && key[e] == thr;
+    }
+  }
+  c_lt = __reduce_add_sync(0xffffffffu, c_lt);
+  c_eq = __reduce_add_sync(0xffffffffu, c_eq);
+  if (lane == 0) {
+    wl[wid] = c_lt;
+    we[wid] = c_eq;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    uint32_t tl = 0, te = 0;
+    for (int w = 0; w < kSelWarps; ++w) {
+      tl += wl[w];
+      te += we[w];
+    }
+    sel_counts(a)[2 * blockIdx.x] = tl;
+    sel_counts(a)[2 * blockIdx.x + 1] = te;
+  }
+}
+
+// stable compaction of this CTA's slice: warp w of the CTA owns the
+// contiguous groups [g0 + w*wt, g0 + (w+1)*wt); lane l holds positions
+// 4l .. 4l+3 of each 128-position trip
+__global__ void __launch_bounds__(kSelThreads) sel_compact_kernel(const SelArgs a) {
+  __shared__ uint32_t wl[kSelWarps], we[kSelWarps];
   __shared__ uint32_t s_base_lt, s_base_eq;
-  const int tid = threadIdx.x;
-  if (tid == 0) {
-    s_prefix = 0;
-    s_mask = 0;
-    s_remaining = static_cast<uint32_t>(k);
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const uint32_t thr = sel_state(a)[0], take_eq = sel_state(a)[2];
+  if (tid < 32) {  // entries of the lower CTAs
+    uint32_t bl = 0, be = 0;
+    for (int c = lane; c < static_cast<int>(blockIdx.x); c += 32) {
+      bl += sel_counts(a)[2 * c];
+      be += sel_counts(a)[2 * c + 1];
+    }
+    bl = __reduce_add_sync(0xffffffffu, bl);
+    be = __reduce_add_sync(0xffffffffu, be);
+    if (lane == 0) {
+      s_base_lt = bl;
+      s_base_eq = be;
+    }
+  }
+  const int wt = a.per_cta / kSelWarps;  // multiple of 32 (per_cta is a multiple of 32 * kSelWarps)
+  const int g_begin = blockIdx.x * a.per_cta + wid * wt, g_end = g_begin + wt;
+  uint32_t c_lt = 0, c_eq = 0;
+  for (int g = g_begin + lane; g < g_end; g += 32) {
+    uint32_t key[4];
+    bool valid[4];
+    sel_keys4(a.scores, a.vec, g, a.n, a.pf, a.pl, key, valid);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      c_lt += valid[e] && key[e] < thr;
+      c_eq += valid[e] && key[e] == thr;
+    }
+  }
+  c_lt = __reduce_add_sync(0xffffffffu, c_lt);
+  c_eq = __reduce_add_sync(0xffffffffu, c_eq);
+  if (lane == 0) {
+    wl[wid] = c_lt;
+    we[wid] = c_eq;
   }
   __syncthreads();
-  // radix select of the k-th smallest key, most significant byte first
-  for (int shift = 24; shift >= 0; shift -= 8) {
-    for (int i = tid; i < 256; i += kSelThreads) hist[i] = 0;
-    __syncthreads();
-    const uint32_t prefix = s_prefix, mask = s_mask;
-    for (int i = tid; i < n; i += kSelThreads) {
-      const uint32_t key = sel_key(scores, i, n, pf, pl);
-      if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
-    }
-    __syncthreads();
-    if (tid == 0) {
-      uint32_t rem = s_remaining, acc = 0;
-      int bin = 0;
-      for (; bin < 256; ++bin) {
-        if (acc + hist[bin] >= rem) break;
-        acc += hist[bin];
-      }
-      s_remaining = rem - acc;
-      s_prefix = prefix | (static_cast<uint32_t>(bin) << shift);
-      s_mask = mask | (255u << shift);
-    }
-    __syncthreads();
+  uint32_t base_lt = s_base_lt, base_eq = s_base_eq;
+  for (int w = 0; w < wid; ++w) {
+    base_lt += wl[w];
+    base_eq += we[w];
   }
-  const uint32_t thr = s_prefix;       // key of the k-th smallest
-  const uint32_t take_eq = s_remaining;  // how many keys == thr to take (lowest indices first)
-  // stable compaction in index order, chunk by chunk
-  if (tid == 0) {
-    s_base_lt = 0;
-    s_base_eq = 0;
-  }
-  __syncthreads();
-  const int lane = tid & 31, wid = tid >> 5;
-  for (int base = 0; base < n; base += kSelThreads) {
-    const int i = base + tid;
-    uint32_t key = i < n ? sel_key(scores, i, n, pf, pl) : 0xffffffffu;
-    const bool lt = i < n && key < thr;
-    const bool eq = i < n && key == thr;
-    // ranks of `eq` entries in index order
-    const uint32_t beq = __ballot_sync(0xffffffffu, eq);
-    const uint32_t blt = __ballot_sync(0xffffffffu, lt);
-    if (lane == 0) warp_cnt[wid] = (__popc(blt) << 16) | __popc(beq);
-    __syncthreads();
-    uint32_t pre_lt = 0, pre_eq = 0, tot_lt = 0, tot_eq = 0;
-    for (int w = 0; w < kSelThreads / 32; ++w) {
-      const uint32_t c = warp_cnt[w];
-      if (w < wid) {
-        pre_lt += c >> 16;
-        pre_eq += c & 0xffffu;
-      }
-      tot_lt += c >> 16;
-      tot_eq += c & 0xffffu;
+  if (base_lt + min(base_eq, take_eq) >= static_cast<uint32_t>(a.k)) return;  // everything selected lies before
+  const uint32_t below = (1u << lane) - 1u;
+  for (int g = g_begin + lane; g < g_end; g += 32) {
+    uint32_t key[4];
+    bool valid[4];
+    sel_keys4(a.scores, a.vec, g, a.n, a.pf, a.pl, key, valid);
+    uint32_t blt[4], beq[4], lanes_lt = 0, lanes_eq = 0;  // entries of lower lanes
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      blt[e] = __ballot_sync(0xffffffffu, valid[e] && key[e] < thr);
+      beq[e] = __ballot_sync(0xffffffffu, valid[e] && key[e] == thr);
+      lanes_lt += __popc(blt[e] & below);
+      lanes_eq += __popc(beq[e] & below);
     }
-    const uint32_t my_lt = s_base_lt + pre_lt + __popc(blt & ((1u << lane) - 1u));
-    const uint32_t my_eq = s_base_eq + pre_eq + __popc(beq & ((1u << lane) - 1u));
-    // output position = number of selected entries with smaller index
-    // selected = lt, or eq with rank < take_eq
-    if (lt || (eq && my_eq < take_eq)) {
-      const uint32_t eq_before = min(my_eq, take_eq);
-      out[my_lt + eq_before] = i;
+    uint32_t my_lt = base_lt + lanes_lt, my_eq = base_eq + lanes_eq;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const bool lt = valid[e] && key[e] < thr;
+      const bool eq = valid[e] && key[e] == thr;
+      // output position = number of selected entries with a smaller index;
+      // selected = lt, or eq with rank < take_eq
+      if (lt || (eq && my_eq < take_eq)) a.out[my_lt + min(my_eq, take_eq)] = 4 * g + e;
+      my_lt += lt;
+      my_eq += eq;
     }
-    __syncthreads();
-    if (tid == 0) {
-      s_base_lt += tot_lt;
-      s_base_eq += tot_eq;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      base_lt += __popc(blt[e]);
+      base_eq += __popc(beq[e]);
     }
-    __syncthreads();
   }
 }
 
@@ -304,19 +445,38 @@ extern "C" int akv_importance_update(const float* attn, int B, int H, int M, int
   return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_LAUNCH;
 }
 
-extern "C" size_t akv_select_workspace_bytes(int n) { return n >= 0 ? 16 : 0; }
+extern "C" size_t akv_select_workspace_bytes(int n) { return n >= 0 ? kSelWsWords * sizeof(uint32_t) : 0; }
 
 extern "C" int akv_select_bottomk(const float* scores, int n, int k, int protect_first, int protect_last,
                                   int64_t* idx_out, void* workspace, size_t workspace_bytes, void* stream) {
-  (void)workspace;
-  (void)workspace_bytes;
   if (!scores || !idx_out) return AKV_ERR_NULL;
   if (n < 0 || k < 0 || k > n || protect_first < 0 || protect_last < 0) return AKV_ERR_SHAPE;
   if (k == 0) return AKV_OK;
-  if (protect_first > n) protect_first = n;
-  if (protect_last > n) protect_last = n;
-  select_bottomk_kernel<<<1, kSelThreads, 0, static_cast<cudaStream_t>(stream)>>>(scores, n, k, protect_first,
-                                                                                 protect_last, idx_out);
+  if (!workspace || workspace_bytes < kSelWsWords * sizeof(uint32_t)) return AKV_ERR_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(workspace) % 16) return AKV_ERR_ALIGN;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  SelArgs a{};
+  a.scores = scores;
+  a.n = n;
+  a.k = k;
+  a.pf = std::min(protect_first, n);
+  a.pl = std::min(protect_last, n);
+  a.vec = (reinterpret_cast<uintptr_t>(scores) % 16) == 0;
+  a.ng = (n + 3) / 4;
+  // slices of whole warp tiles (32 groups per warp per trip, kSelWarps warps)
+  constexpr int unit = 32 * kSelWarps;
+  const int ctas = std::max(1, std::min(kSelMaxCtas, (a.ng + unit - 1) / unit));
+  a.per_cta = (a.ng + ctas * unit - 1) / (ctas * unit) * unit;
+  const int grid = (a.ng + a.per_cta - 1) / a.per_cta;
+  a.ws = static_cast<uint32_t*>(workspace);
+  a.out = idx_out;
+  if (cudaMemsetAsync(workspace, 0, 4 * 256 * sizeof(uint32_t), st) != cudaSuccess) return AKV_ERR_LAUNCH;
+  for (int pass = 0; pass < 4; ++pass) {
+    sel_hist_kernel<<<grid, kSelThreads, 0, st>>>(a, pass);
+    sel_pick_kernel<<<1, 32, 0, st>>>(a, pass);
+  }
+  sel_count_kernel<<<grid, kSelThreads, 0, st>>>(a);
+  sel_compact_kernel<<<grid, kSelThreads, 0, st>>>(a);
   return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_LAUNCH;
 }
 

@@ -88,3 +88,26 @@ def test_cold_copy_roundtrip():
     ev = tiering.cold_restore_blocks(host, dst, 2, stream=side)
     ev.synchronize()
     np.testing.assert_array_equal(_np(dst[:, :, 2:5]), _np(src[:, :, 5:8]))
+
+
+@pytest.mark.parametrize("n,k,pf,pl,levels", [(131072, 64, 4, 32, 0), (131072, 640, 4, 32, 50),
+                                              (100003, 1000, 0, 0, 7), (4097, 4097, 3, 5, 3), (37, 5, 2, 2, 0)])
+def test_select_bottomk_large_ties_unaligned(n, k, pf, pl, levels):
+    """Multi-CTA selection against a stable CPU ordering (value, then index;
+    protected ends rank as +inf): many CTAs, ties spanning CTA slices, and an
+    unaligned score pointer (the scalar-load path)."""
+    from akv import tiering
+    rng = np.random.default_rng(n + k)
+    vals = rng.random(n + 1).astype(np.float32)
+    if levels:
+        vals = np.floor(vals * levels).astype(np.float32) / levels  # heavy ties
+    for offset in (0, 1):
+        base = torch.from_numpy(vals).to(DEV)
+        s = base[offset:offset + n]
+        got = tiering.select_bottomk(s, k, pf, pl).cpu().numpy()
+        keys = vals[offset:offset + n].astype(np.float64).copy()
+        keys[:pf] = np.inf
+        if pl:
+            keys[n - pl:] = np.inf
+        want = np.sort(np.lexsort((np.arange(n), keys))[:k])
+        np.testing.assert_array_equal(got, want)
