@@ -187,7 +187,7 @@ class AKVLayer(_LayerBase):
         idx_dev = _to_device(demote_idx, hk.device)
         blk0 = arena.append(hk, hv, group=n, tok_idx=idx_dev)
         slots = torch.arange(blk0 * BLOCK, blk0 * BLOCK + n, dtype=torch.int64, device=hk.device)
-        self._warm_slots = slots if self._warm_slots is None else torch.cat([self._warm_slots, slots])
+        self._append_1d("_warm_slots", slots)
         # the reference's measure_packed_bytes of this event's K and V dicts (drop_in.py:331-336)
         if isinstance(arena, HeadGroupArena):  # one K and one V dict per head, at that head's width
             self._warm_bytes_packed += B * sum(2 * n * packed_width(D, b) + 4 * D + 4 * n for b in self.per_head_bits)
@@ -211,6 +211,26 @@ class AKVLayer(_LayerBase):
         if self._warm_keys_fp16 is not None or self._warm is None or self._warm_slots is None:
             return self._warm_keys_fp16, self._warm_values_fp16
         return self._warm.dequantize(tok_idx=self._warm_slots)
+
+    def _append_1d(self, name: str, new: torch.Tensor) -> None:
+        """``self.<name> = cat([self.<name>, new])`` for the warm tier's
+        per-token vectors (positions on the host, record slots on the device),
+        amortised: the vector is the front of a capacity buffer and an append
+        that fits writes only the new entries.  A vector rebuilt elsewhere
+        (promotion) is moved into a new buffer first."""
+        cur = getattr(self, name)
+        bufs = self.__dict__.setdefault("_vec_bufs", {})
+        buf = bufs.get(name)
+        n_old = 0 if cur is None else cur.shape[0]
+        n = n_old + new.shape[0]
+        in_buf = cur is None or (buf is not None and cur.data_ptr() == buf.data_ptr() and cur.device == buf.device)
+        if buf is None or not in_buf or n > buf.shape[0] or buf.device != new.device or buf.dtype != new.dtype:
+            nb = torch.empty(max(2 * n, 64), dtype=new.dtype, device=new.device)
+            if n_old:
+                nb[:n_old].copy_(cur)
+            bufs[name] = buf = nb
+        buf[n_old:n].copy_(new)
+        setattr(self, name, buf[:n])
 
     def _append_warm_fp16(self, dk: torch.Tensor, dv: torch.Tensor) -> None:
         """Append dequantised warm rows to the FP16 working copy.
@@ -371,8 +391,7 @@ class AKVLayer(_LayerBase):
             demote_idx = self._select_demote_indices(n_demote, hot_len)
             demote_positions = self._hot_positions[demote_idx]
             self._demote(demote_idx)
-            self._warm_positions = (demote_positions if self._warm_positions is None
-                                    else torch.cat([self._warm_positions, demote_positions]))
+            self._append_1d("_warm_positions", demote_positions)
             self._warm_len += n_demote
             if self._proxy_score is not None:
                 pad = torch.zeros(n_demote, dtype=self._proxy_score.dtype, device=self._warm_keys_fp16.device)
