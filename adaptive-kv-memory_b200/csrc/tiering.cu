@@ -12,23 +12,68 @@ namespace akv {
 // importance update (akv/triton_ops.py:604-650, CPU branch semantics)
 //   imp[n]    = sum_m ( sum_{b,h} attn[b,h,m,n] / (B*H) )
 //   scores[n] = fl(fl(scores[n] * decay) + imp[n])
-// One thread per column n; the (b,h) sum runs in order, like a sequential
-// reduction of the reference's mean over dims (0, 1).
+// Per column n the (b,h) sum runs in order, like a sequential reduction of
+// the reference's mean over dims (0, 1).
 // ---------------------------------------------------------------------------
+// attention received by positions n0 .. n0+W-1:
+//   imp[w] = sum_m fl(fl(sum_{bh} attn[bh, m, n0+w]) / (B*H)), the (b,h) sum in
+// order.  W = 4: 16-byte loads (n0 a multiple of 4, rows 16-byte aligned);
+// eight (b,h) rows are loaded before they are added, so a thread keeps
+// several loads in flight while the additions keep their order.
+template <int W>
+AKV_DEV void attn_received(const float* __restrict__ attn, int BH, int M, int Na, int n0, float (&imp)[W]) {
+  const float cnt = static_cast<float>(BH);
+#pragma unroll
+  for (int w = 0; w < W; ++w) imp[w] = 0.f;
+  for (int m = 0; m < M; ++m) {
+    float s[W];
+#pragma unroll
+    for (int w = 0; w < W; ++w) s[w] = 0.f;
+    const float* col = attn + static_cast<int64_t>(m) * Na + n0;
+    const int64_t rs = static_cast<int64_t>(M) * Na;  // stride between (b,h) rows
+    int bh = 0;
+    for (; bh + 8 <= BH; bh += 8) {
+      float v[8][W];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if constexpr (W == 4) {
+          const float4 f = __ldg(reinterpret_cast<const float4*>(col + (bh + j) * rs));
+          v[j][0] = f.x;
+          v[j][1] = f.y;
+          v[j][2] = f.z;
+          v[j][3] = f.w;
+        } else {
+          v[j][0] = __ldg(col + (bh + j) * rs);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+#pragma unroll
+        for (int w = 0; w < W; ++w) s[w] = __fadd_rn(s[w], v[j][w]);
+    }
+    for (; bh < BH; ++bh)
+#pragma unroll
+      for (int w = 0; w < W; ++w) s[w] = __fadd_rn(s[w], __ldg(col + bh * rs + w));
+#pragma unroll
+    for (int w = 0; w < W; ++w) imp[w] = __fadd_rn(imp[w], __fdiv_rn(s[w], cnt));
+  }
+}
+
+// W positions per thread (W = 4 when Na % 4 == 0 and the rows are 16-byte aligned)
+template <int W>
 __global__ void importance_update_kernel(const float* __restrict__ attn, int B, int H, int M, int Na,
                                          float* __restrict__ scores, int N, float decay) {
-  const int n = blockIdx.x * blockDim.x + threadIdx.x;
-  if (n >= N) return;
-  float imp = 0.f;
-  if (n < Na) {
-    const float inv = static_cast<float>(B * H);
-    for (int m = 0; m < M; ++m) {
-      float s = 0.f;
-      for (int bh = 0; bh < B * H; ++bh) s = __fadd_rn(s, attn[(static_cast<int64_t>(bh) * M + m) * Na + n]);
-      imp = __fadd_rn(imp, __fdiv_rn(s, inv));
-    }
+  const int n0 = (blockIdx.x * blockDim.x + threadIdx.x) * W;
+  if (n0 >= N) return;
+  float imp[W];
+#pragma unroll
+  for (int w = 0; w < W; ++w) imp[w] = 0.f;
+  if (n0 < Na) attn_received<W>(attn, B * H, M, Na, n0, imp);  // W = 4 only when Na % 4 == 0
+#pragma unroll
+  for (int w = 0; w < W; ++w) {
+    const int n = n0 + w;
+    if (n < N) scores[n] = __fadd_rn(__fmul_rn(scores[n], decay), n < Na ? imp[w] : 0.f);
   }
-  scores[n] = __fadd_rn(__fmul_rn(scores[n], decay), imp);
 }
 
 // ---------------------------------------------------------------------------
@@ -40,26 +85,26 @@ __global__ void importance_update_kernel(const float* __restrict__ attn, int B, 
 // scores = fl(fl(scores*decay) + received); last access = step where
 // received > 0.01.
 // ---------------------------------------------------------------------------
+template <int W>
 __global__ void migrator_update_kernel(const float* __restrict__ attn, int B, int H, int M, int Na,
                                        float* __restrict__ scores, int64_t* __restrict__ access,
                                        float* __restrict__ retrieval, int n_prev, int64_t step, float decay) {
-  const int n = blockIdx.x * blockDim.x + threadIdx.x;
-  if (n >= Na) return;
-  const float cnt = static_cast<float>(B * H);
-  float imp = 0.f;
-  for (int m = 0; m < M; ++m) {
-    float s = 0.f;
-    for (int bh = 0; bh < B * H; ++bh) s = __fadd_rn(s, attn[(static_cast<int64_t>(bh) * M + m) * Na + n]);
-    imp = __fadd_rn(imp, __fdiv_rn(s, cnt));
+  const int n0 = (blockIdx.x * blockDim.x + threadIdx.x) * W;
+  if (n0 >= Na) return;
+  float imp[W];
+  attn_received<W>(attn, B * H, M, Na, n0, imp);
+#pragma unroll
+  for (int w = 0; w < W; ++w) {
+    const int n = n0 + w;
+    float sc = scores[n];
+    if (n >= n_prev) {
+      sc = 0.f;
+      access[n] = step;
+      retrieval[n] = 0.f;
+    }
+    scores[n] = __fadd_rn(__fmul_rn(sc, decay), imp[w]);
+    if (imp[w] > 0.01f) access[n] = step;
   }
-  float sc = scores[n];
-  if (n >= n_prev) {
-    sc = 0.f;
-    access[n] = step;
-    retrieval[n] = 0.f;
-  }
-  scores[n] = __fadd_rn(__fmul_rn(sc, decay), imp);
-  if (imp > 0.01f) access[n] = step;
 }
 
 // compute_importance (:175-219), step 1: max of scores, min of last access,
@@ -440,8 +485,11 @@ extern "C" int akv_importance_update(const float* attn, int B, int H, int M, int
   if (!scores || (!attn && Na > 0)) return AKV_ERR_NULL;
   if (B <= 0 || H <= 0 || M <= 0 || Na < 0 || N < 0) return AKV_ERR_SHAPE;
   if (N == 0) return AKV_OK;
-  importance_update_kernel<<<(N + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(attn, B, H, M, Na,
-                                                                                          scores, N, decay);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (Na % 4 == 0 && N % 4 == 0 && (reinterpret_cast<uintptr_t>(attn) % 16) == 0)
+    importance_update_kernel<4><<<(N / 4 + 255) / 256, 256, 0, st>>>(attn, B, H, M, Na, scores, N, decay);
+  else
+    importance_update_kernel<1><<<(N + 255) / 256, 256, 0, st>>>(attn, B, H, M, Na, scores, N, decay);
   return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_LAUNCH;
 }
 
@@ -518,8 +566,13 @@ extern "C" int akv_migrator_update(const float* attn, int B, int H, int M, int N
   if (!attn || !scores || !last_access || !retrieval) return AKV_ERR_NULL;
   if (B <= 0 || H <= 0 || M <= 0 || Na < 0 || n_prev < 0) return AKV_ERR_SHAPE;
   if (Na == 0) return AKV_OK;
-  migrator_update_kernel<<<(Na + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      attn, B, H, M, Na, scores, last_access, retrieval, n_prev, step, decay);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (Na % 4 == 0 && (reinterpret_cast<uintptr_t>(attn) % 16) == 0)
+    migrator_update_kernel<4><<<(Na / 4 + 255) / 256, 256, 0, st>>>(attn, B, H, M, Na, scores, last_access,
+                                                                    retrieval, n_prev, step, decay);
+  else
+    migrator_update_kernel<1><<<(Na + 255) / 256, 256, 0, st>>>(attn, B, H, M, Na, scores, last_access, retrieval,
+                                                                n_prev, step, decay);
   return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_LAUNCH;
 }
 
