@@ -186,3 +186,28 @@ def test_per_head_bits_match_reference_per_head_quantisation(frac):
     p = torch.softmax(torch.einsum("bhqd,bhnd->bhqn", q.float(), K) / 128 ** 0.5, -1)
     ref = torch.einsum("bhqn,bhnd->bhqd", p, V)
     assert (out - ref).abs().max().item() <= 2e-3
+
+
+def test_per_head_bits_fallback_and_calibrated_layers():
+    """Ported from the reference's tests/test_per_head_bits.py (:28-69): the
+    per-head path demotes with one arena per distinct width; a width list that
+    does not match the head count falls back to the layer's widths; only
+    calibrated layers get per-head widths."""
+    from akv import AKVCache, AKVLayer
+    from akv.packed_layout import HeadGroupArena, WarmArena
+    g = torch.Generator(device=DEV).manual_seed(12)
+    x = torch.randn(1, 2, 4, 128, generator=g, device=DEV).half()
+    layer = AKVLayer(warm_bits=3, hot_budget=2, per_head_bits=[2, 3, 4, 2])  # 4 widths, 2 heads
+    layer.update(x, x.clone())
+    assert isinstance(layer._warm, WarmArena) and layer._warm_keys_fp16.shape[2] == 2
+    layer = AKVLayer(warm_bits=4, hot_budget=2, per_head_bits=[2, 3])
+    layer.update(x, x.clone())
+    assert isinstance(layer._warm, HeadGroupArena) and layer._warm_keys_fp16.shape[2] == 2
+    assert sorted(b for b, _, _ in layer._warm.groups) == [2, 3]
+    cache = AKVCache(warm_bits=3, hot_budget=4)
+    cache._calibration_per_head_bits = {0: [2, 4]}
+    y = torch.randn(1, 2, 6, 128, generator=g, device=DEV).half()
+    cache.update(y, y.clone(), layer_idx=0)
+    cache.update(y, y.clone(), layer_idx=1)
+    assert cache.layers[0].per_head_bits == [2, 4] and isinstance(cache.layers[0]._warm, HeadGroupArena)
+    assert cache.layers[1].per_head_bits is None and isinstance(cache.layers[1]._warm, WarmArena)
