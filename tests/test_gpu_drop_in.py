@@ -211,3 +211,32 @@ def test_per_head_bits_fallback_and_calibrated_layers():
     cache.update(y, y.clone(), layer_idx=1)
     assert cache.layers[0].per_head_bits == [2, 4] and isinstance(cache.layers[0]._warm, HeadGroupArena)
     assert cache.layers[1].per_head_bits is None and isinstance(cache.layers[1]._warm, WarmArena)
+
+
+def test_byte_accounting_ported_from_reference():
+    """Ported from the reference's tests/test_packed_bytes.py (:95-125) and
+    tests/test_memory_alignment.py (:140-168): after demotion the measured
+    packed bytes are positive, below the FP16 working copy and the FP16
+    equivalent, ``warm_bytes`` aliases them, and the cache aggregate exposes
+    every key."""
+    from akv import AKVCache, AKVLayer
+    g = torch.Generator(device=DEV).manual_seed(13)
+    layer = AKVLayer(warm_bits=4, hot_budget=4, group_size=32)
+    k = torch.randn(1, 2, 8, 128, generator=g, device=DEV).half()
+    v = torch.randn(1, 2, 8, 128, generator=g, device=DEV).half()
+    layer.update(k, v)
+    layer.update(k, v)
+    st = layer.memory_usage_bytes()
+    for key in ("warm_bytes_live", "warm_bytes_packed", "warm_bytes_formula"):
+        assert key in st
+    assert 0 < st["warm_bytes_packed"] < st["warm_bytes_live"]
+    assert st["warm_bytes_packed"] < st["fp16_equivalent_bytes"]
+    assert st["warm_bytes"] == st["warm_bytes_packed"]
+    cache = AKVCache(warm_bits=4, hot_budget=4, num_hidden_layers=1)
+    cache.update(torch.randn(1, 2, 16, 128, generator=g, device=DEV).half(),
+                 torch.randn(1, 2, 16, 128, generator=g, device=DEV).half(), layer_idx=0)
+    stats = cache.memory_usage()
+    for key in ("hot_bytes", "warm_bytes", "warm_bytes_live", "warm_bytes_packed", "warm_bytes_formula",
+                "total_bytes", "fp16_equivalent_bytes", "savings_ratio", "num_layers"):
+        assert key in stats
+    assert stats["warm_bytes"] == stats["warm_bytes_packed"] <= stats["warm_bytes_live"]
