@@ -1022,9 +1022,19 @@ static void split_shares(int per_unit, int n_warm_blocks, int nhb, double wbytes
 // to stream, and the split partials the combine reads stay few.
 constexpr int kMinBlocksPerSplit = 16;
 
+// Waves of resident CTAs the split count aims for: three when there are many
+// units (config 3's 128: the smaller CTAs even out the tail), one when there
+// are at most kFewUnits (a KV-head shard on 2-8 GPUs, batch 1 at 64 heads),
+// where a three-wave target cuts every unit into short splits whose per-CTA
+// set-up dominates (per layer, 1-wave vs 3-wave target: 8-GPU config-3 shard
+// 29.4 vs 34.9 us, 4-GPU 52.1 vs 59.4, 2-GPU 91.4 vs 94.6, config-5b shard
+// 30.9 vs 37.5; the full config-3 layer is 1.9 % slower with one wave).
+constexpr int kFewUnits = 64;
+
 // candidate split counts per unit: [lo, hi]; unit_blocks = warm + hot blocks of one unit
 static void per_unit_range(int units, int unit_blocks, int& lo, int& hi) {
-  lo = max(1, (3 * kDecodeSlots + units - 1) / units);
+  const int waves = units <= kFewUnits ? 1 : 3;
+  lo = max(1, (waves * kDecodeSlots + units - 1) / units);
   hi = lo + max(8, lo);
   const int cap = max(1, unit_blocks / kMinBlocksPerSplit);
   if (hi > cap) {

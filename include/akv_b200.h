@@ -332,7 +332,8 @@ int akv_migrator_importance(const float* scores, const int64_t* last_access, con
  * (akv/vmm.py:221-242): the k lowest scores with the first `protect_first`
  * and last `protect_last` positions excluded (treated as +inf), returned as
  * ascending int64 indices.  Equal scores are taken lowest index first.
- * workspace >= akv_select_workspace_bytes(n).
+ * workspace >= akv_select_workspace_bytes(n) bytes, 16-byte aligned
+ * (AKV_ERR_ALIGN otherwise); the call is several short launches on `stream`.
  * ---------------------------------------------------------------------- */
 size_t akv_select_workspace_bytes(int n);
 int akv_select_bottomk(const float* scores, int n, int k, int protect_first, int protect_last,
