@@ -263,3 +263,29 @@ def test_reference_int4_layout_golden(golden_dir, gs):
         ref = z[f"{t}/{tag}"].astype(np.float32)
         err = np.abs(_np(out).astype(np.float32) - ref)
         assert (err <= tolerance(ref)).all(), (tag, err.max())
+
+
+def test_few_units_long_context():
+    """Config-5b shard shape (B1, 64 Q / 8 KV heads, 61,440 warm k4v4 + 4,096
+    hot): 8 units, so the planner's one-wave target gives each CTA ~28 blocks
+    and each warp several stage refills.  Reference: fp32 attention over the
+    arena's dequantised tiers."""
+    import akv
+    B, Hq, Hkv, D, nw, nh = 1, 64, 8, 128, 61440, 4096
+    g = torch.Generator(device=DEV).manual_seed(9)
+    wk = torch.randn(B, Hkv, nw, D, generator=g, device=DEV).half()
+    wv = torch.randn(B, Hkv, nw, D, generator=g, device=DEV).half()
+    arena = akv.WarmArena(B, Hkv, D, 4, 4, 0.0, max_blocks=nw // 32, device=DEV)
+    arena.append(wk, wv, group=32)
+    hk = torch.randn(B, Hkv, nh, D, generator=g, device=DEV).half()
+    hv = torch.randn(B, Hkv, nh, D, generator=g, device=DEV).half()
+    q = torch.randn(B, Hq, D, generator=g, device=DEV).half()
+    out = akv.mixed_tier_decode_attention(q, hk, hv, arena).float()
+    kd, vd = arena.dequantize()
+    K = torch.cat([kd[0], hk[0]], 1).float().repeat_interleave(Hq // Hkv, 0)
+    V = torch.cat([vd[0], hv[0]], 1).float().repeat_interleave(Hq // Hkv, 0)
+    p = torch.softmax(torch.einsum("hd,hnd->hn", q[0].float(), K) / D ** 0.5, -1)
+    ref = torch.einsum("hn,hnd->hd", p, V)
+    err = (out[0] - ref).abs().max().item()
+    print(f"[decode err] few units, long context: {err:.3e}")
+    assert err <= ATOL
