@@ -34,6 +34,7 @@ from __future__ import annotations
 import logging
 from typing import Any, Optional, Tuple
 
+import numpy as np
 import torch
 
 from . import _C
@@ -150,8 +151,10 @@ class AKVLayer(_LayerBase):
         """Recency importance on the CPU (drop_in.py:376-390)."""
         if self._importance is None or self._importance.shape[0] != hot_len - n_new:
             self._importance = torch.ones(hot_len, dtype=torch.float32)
-        else:
-            self._importance = torch.cat([self._importance * self._decay, torch.ones(n_new, dtype=torch.float32)])
+        else:  # host bookkeeping in numpy: the same float32 multiply, far less dispatch
+            imp = self._importance.numpy()
+            self._importance = torch.from_numpy(
+                np.concatenate([imp * np.float32(self._decay), np.ones(n_new, dtype=np.float32)]))
 
     def _select_demote_indices(self, n_demote: int, hot_len: int) -> torch.Tensor:
         """Lowest importance, first 4 / last min(16, budget//4) protected, ascending (drop_in.py:392-413)."""
@@ -159,16 +162,16 @@ class AKVLayer(_LayerBase):
         protect_recent = min(16, self.hot_budget // 4)
         if self._importance is None or self._importance.shape[0] != hot_len:
             return torch.arange(n_demote)
-        scores = self._importance.clone()
-        scores[:protect_initial] = float("inf")
-        scores[max(0, hot_len - protect_recent):] = float("inf")
-        _, idx = scores.topk(n_demote, largest=False)
-        idx, _ = idx.sort()
-        return idx
+        scores = self._importance.numpy().copy()
+        scores[:protect_initial] = np.inf
+        scores[max(0, hot_len - protect_recent):] = np.inf
+        _, idx = torch.from_numpy(scores).topk(n_demote, largest=False)  # torch's tie order, as the reference
+        return torch.from_numpy(np.sort(idx.numpy()))
 
     # ------------------------------------------------------------------ warm tier
-    def _demote(self, demote_idx: torch.Tensor) -> None:
-        """Quantise the selected hot rows into new warm records (one scale group per batch row)."""
+    def _demote(self, demote_idx: torch.Tensor, idx_dev: Optional[torch.Tensor] = None) -> None:
+        """Quantise the selected hot rows into new warm records (one scale group per batch row).
+        ``idx_dev``: the same indices already on the device."""
         hk, hv = self._hot_keys, self._hot_values
         _C.require_cuda(hk, hv)
         B, H, _, D = hk.shape
@@ -184,7 +187,8 @@ class AKVLayer(_LayerBase):
         arena = self._warm
         nblk = (n + BLOCK - 1) // BLOCK
         arena.grow(arena.n_blocks + nblk)
-        idx_dev = _to_device(demote_idx, hk.device)
+        if idx_dev is None:
+            idx_dev = _to_device(demote_idx, hk.device)
         blk0 = arena.append(hk, hv, group=n, tok_idx=idx_dev)
         slots = torch.arange(blk0 * BLOCK, blk0 * BLOCK + n, dtype=torch.int64, device=hk.device)
         self._append_1d("_warm_slots", slots)
@@ -359,13 +363,14 @@ class AKVLayer(_LayerBase):
                cache_kwargs: Optional[dict] = None) -> Tuple[torch.Tensor, torch.Tensor]:
         """Append, migrate, return the chronological full view (drop_in.py:591-787)."""
         N = key_states.shape[2]
-        new_positions = torch.arange(self._total_len, self._total_len + N, dtype=torch.long)
+        new_positions = np.arange(self._total_len, self._total_len + N, dtype=np.int64)
         if self._hot_keys is None:
-            self._hot_keys, self._hot_values, self._hot_positions = key_states, value_states, new_positions
+            self._hot_keys, self._hot_values = key_states, value_states
+            self._hot_positions = torch.from_numpy(new_positions)
         else:
             self._hot_keys = torch.cat([self._hot_keys, key_states], dim=2)
             self._hot_values = torch.cat([self._hot_values, value_states], dim=2)
-            self._hot_positions = torch.cat([self._hot_positions, new_positions])
+            self._hot_positions = torch.from_numpy(np.concatenate([self._hot_positions.numpy(), new_positions]))
         self._total_len += N
         if self.protect:
             return self._publish(self._hot_keys, self._hot_values)
@@ -389,21 +394,27 @@ class AKVLayer(_LayerBase):
         if hot_len > budget:
             n_demote = hot_len - budget
             demote_idx = self._select_demote_indices(n_demote, hot_len)
-            demote_positions = self._hot_positions[demote_idx]
-            self._demote(demote_idx)
+            d_np = demote_idx.numpy()
+            kept_np = np.delete(np.arange(hot_len, dtype=np.int64), d_np)
+            hp = self._hot_positions.numpy()
+            demote_positions = torch.from_numpy(hp[d_np])
+            idx_dev, kept_dev = None, None
+            if self._hot_keys.device.type == "cuda":  # demote and keep indices in one host-to-device copy
+                both = _to_device(torch.from_numpy(np.concatenate([d_np, kept_np])), self._hot_keys.device)
+                idx_dev, kept_dev = both[:n_demote], both[n_demote:]
+            self._demote(demote_idx, idx_dev)
             self._append_1d("_warm_positions", demote_positions)
             self._warm_len += n_demote
             if self._proxy_score is not None:
                 pad = torch.zeros(n_demote, dtype=self._proxy_score.dtype, device=self._warm_keys_fp16.device)
                 self._proxy_score = torch.cat([self._proxy_score.to(pad.device), pad])
-            keep = torch.ones(hot_len, dtype=torch.bool)
-            keep[demote_idx] = False
-            kept_dev = _to_device(keep.nonzero().squeeze(1), self._hot_keys.device)
+            if kept_dev is None:
+                kept_dev = _to_device(torch.from_numpy(kept_np), self._hot_keys.device)
             self._hot_keys = self._hot_keys.index_select(2, kept_dev)
             self._hot_values = self._hot_values.index_select(2, kept_dev)
-            self._hot_positions = self._hot_positions[keep]
+            self._hot_positions = torch.from_numpy(hp[kept_np])
             if self._importance is not None:
-                self._importance = self._importance[keep]
+                self._importance = torch.from_numpy(self._importance.numpy()[kept_np])
 
         if self.fused_decode and N == 1 and self._warm is not None:
             return self._publish(*self._placeholder())
