@@ -40,8 +40,10 @@ from .paged import PagedWarmPool, paged_decode_attention
 from .packed_layout import BLOCK
 
 
-def _pinned_to(x: list, dtype, device) -> torch.Tensor:
-    return torch.tensor(x, dtype=dtype).pin_memory().to(device, non_blocking=True)
+def _pinned(values: list, dtype) -> torch.Tensor:
+    """Host values staged in pinned memory, so their copy to the device is
+    asynchronous (a copy from pageable memory waits for the stream)."""
+    return torch.tensor(values, dtype=dtype).pin_memory()
 
 
 @dataclass
@@ -89,9 +91,9 @@ class _LayerState:
         self.warm_len_dev = torch.zeros(S, dtype=torch.int32, device=device)
 
     def sync_lengths(self, slot: int) -> None:
-        self.hot_len_dev[slot:slot + 1].copy_(_pinned_to([self.hot_len[slot]], torch.int32, "cpu"),
+        self.hot_len_dev[slot:slot + 1].copy_(_pinned([self.hot_len[slot]], torch.int32),
                                               non_blocking=True)
-        self.warm_len_dev[slot:slot + 1].copy_(_pinned_to([len(self.pages[slot])], torch.int32, "cpu"),
+        self.warm_len_dev[slot:slot + 1].copy_(_pinned([len(self.pages[slot])], torch.int32),
                                                non_blocking=True)
 
     def reset(self, slot: int) -> None:
@@ -181,7 +183,7 @@ class AdaptiveCacheEngine:
             pages = L.pool.alloc(nblk)
             L.pool.write(ck[None, :, init:init + n_dem], cv[None, :, init:init + n_dem], pages, group=BLOCK)
             first = len(L.pages[slot])
-            L.table[slot, first:first + nblk].copy_(_pinned_to(pages, torch.int32, "cpu"), non_blocking=True)
+            L.table[slot, first:first + nblk].copy_(_pinned(pages, torch.int32), non_blocking=True)
             L.pages[slot].extend(pages)
             L.events[slot].append((first, n_dem))
             keep = total - n_dem
@@ -250,12 +252,12 @@ class AdaptiveAttentionBackend:
         else:
             rows = max(slots) + 1
             q = torch.zeros(rows, *query.shape[1:], dtype=query.dtype, device=query.device)
-            idx = _pinned_to(slots, torch.int64, query.device)
+            idx = _pinned(slots, torch.int64).to(query.device, non_blocking=True)
             q.index_copy_(0, idx, query)
         out = paged_decode_attention(q, L.hot_k[:rows], L.hot_v[:rows], L.hot_len_dev[:rows], L.pool,
                                      L.table[:rows], L.warm_len_dev[:rows], sm_scale=sm_scale)
         if rows != S or slots != list(range(S)):
-            out = out.index_select(0, _pinned_to(slots, torch.int64, query.device))
+            out = out.index_select(0, _pinned(slots, torch.int64).to(query.device, non_blocking=True))
         return out
 
     def forward(self, query: torch.Tensor, seq_id: int, layer_idx: int,
