@@ -204,3 +204,33 @@ def test_from_calibration_applies_per_head_bits(tmp_path):
         cache.update(x, x, i)
     assert cache.layers[0].protect and cache.layers[0].per_head_bits is None
     assert cache.layers[1].per_head_bits == [2, 4] and cache.layers[2].per_head_bits == [4, 4]
+
+
+def test_paged_pool_allocator_on_cpu():
+    """PagedWarmPool page bookkeeping (host logic, no kernels): pages come out
+    ascending from a fresh pool, exhaustion raises, released pages are reused."""
+    from akv.paged import PagedWarmPool
+    pool = PagedWarmPool(8, 2, 128, 4, 2, 0.01, device="cpu")
+    assert pool.buf.shape == (8, 2, pool.rec) and pool.free_pages == 8
+    a = pool.alloc(3)
+    b = pool.alloc(2)
+    assert a == [0, 1, 2] and b == [3, 4] and pool.free_pages == 3
+    with pytest.raises(RuntimeError):
+        pool.alloc(4)
+    pool.release(a)
+    assert pool.free_pages == 6
+    c = pool.alloc(4)
+    assert sorted(c) == [0, 1, 2, 5] and c[:3] == [0, 1, 2]  # released pages first, ascending
+
+
+def test_head_group_arena_grouping_on_cpu():
+    """HeadGroupArena (per-head widths, reference drop_in.py:315-374): one
+    arena per distinct width over that width's heads, in head order."""
+    from akv.packed_layout import HeadGroupArena
+    arena = HeadGroupArena(2, [4, 2, 3, 2, 4], 128, 0.0, max_blocks=4, device="cpu")
+    groups = [(bits, heads, a.H, a.key_bits, a.value_bits) for bits, heads, a in arena.groups]
+    assert groups == [(2, [1, 3], 2, 2, 2), (3, [2], 1, 3, 3), (4, [0, 4], 2, 4, 4)]
+    assert arena.H == 5 and arena.B == 2 and arena.n_blocks == 0
+    arena.grow(9)
+    assert all(a.max_blocks >= 9 for _, _, a in arena.groups) and arena.max_blocks >= 9
+    assert arena.resident_bytes() == sum(a.buf.numel() for _, _, a in arena.groups)
