@@ -326,6 +326,50 @@ def make_drop_in_traces(ref_path: str):
     print("drop-in traces written to", HERE)
 
 
+def make_per_head_trace(ref_path: str):
+    """AKVCache update trace of the reference with calibrated per-head bit
+    widths on layer 0 (drop_in.py:315-374: each head quantised on its own at
+    its width, outlier channels from that head alone): positions after every
+    update, the final chronological K/V view, byte accounting."""
+    import torch
+    torch.set_num_threads(1)
+    sys.path.insert(0, ref_path)
+    from akv.drop_in import AKVCache
+    out = {}
+    H, D, name = 2, 64, "d"
+    steps = [200] + [1] * 20 + [40] + [1] * 10
+    g = torch.Generator().manual_seed(ord(name))
+    cache = AKVCache(num_hidden_layers=1, warm_bits=3, hot_budget=64, outlier_fraction=0.05,
+                     enable_promotion=False, enable_promotion_proxy=False)
+    cache._calibration_per_head_bits = {0: [2, 4]}
+    warm_pos, hot_pos, ks, vs = [], [], [], []
+    for n in steps:
+        k = make_kv(g, H, n, D, outlier_ch=(7,)).unsqueeze(0)
+        v = make_kv(g, H, n, D).unsqueeze(0)
+        full_k, full_v = cache.update(k, v, 0)
+        layer = cache.layers[0]
+        assert layer.per_head_bits == [2, 4]
+        warm_pos.append(np.array([] if layer._warm_positions is None else layer._warm_positions.tolist(),
+                                 dtype=np.int64))
+        hot_pos.append(layer._hot_positions.numpy().astype(np.int64))
+        ks.append(k.numpy())
+        vs.append(v.numpy())
+    out[f"{name}/steps"] = np.array(steps, dtype=np.int64)
+    out[f"{name}/k_in"] = np.concatenate(ks, axis=2)
+    out[f"{name}/v_in"] = np.concatenate(vs, axis=2)
+    out[f"{name}/warm_pos"] = np.concatenate(warm_pos)
+    out[f"{name}/warm_len"] = np.array([len(w) for w in warm_pos], dtype=np.int64)
+    out[f"{name}/hot_pos"] = np.concatenate(hot_pos)
+    out[f"{name}/hot_len"] = np.array([len(h) for h in hot_pos], dtype=np.int64)
+    out[f"{name}/full_k"] = full_k.numpy()
+    out[f"{name}/full_v"] = full_v.numpy()
+    mu = cache.memory_usage()
+    for key in ("hot_bytes", "warm_bytes_packed", "warm_bytes_live", "fp16_equivalent_bytes", "total_bytes"):
+        out[f"{name}/mem/{key}"] = np.array(mu[key], dtype=np.int64)
+    np.savez_compressed(os.path.join(HERE, "drop_in_per_head.npz"), **out)
+    print("per-head trace written to", HERE)
+
+
 def make_migrator_trace(ref_path: str):
     """ImportanceBasedMigrator (akv/vmm.py:113-245) of the reference driven by
     seeded attention: importance and eviction candidates after some steps.
@@ -366,7 +410,10 @@ if __name__ == "__main__":
         sys.exit(0)
     if len(sys.argv) > 2 and sys.argv[2] == "drop_in":
         make_drop_in_traces(sys.argv[1])
+    elif len(sys.argv) > 2 and sys.argv[2] == "per_head":
+        make_per_head_trace(sys.argv[1])
     else:
         main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
         make_drop_in_traces(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
         make_migrator_trace(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+        make_per_head_trace(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")

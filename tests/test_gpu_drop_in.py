@@ -21,7 +21,9 @@ DEV = "cuda:0"
 
 
 def _traces(golden_dir):
-    return np.load(os.path.join(golden_dir, "drop_in.npz"))
+    z = dict(np.load(os.path.join(golden_dir, "drop_in.npz")))
+    z.update(np.load(os.path.join(golden_dir, "drop_in_per_head.npz")))  # case "d"
+    return z
 
 
 CASES = {
@@ -30,16 +32,21 @@ CASES = {
               promotion_threshold=0.3),
     "c": dict(warm_bits=2, hot_budget=32, adaptive_hot_frac=0.25, enable_promotion=False,
               enable_promotion_proxy=False),
+    # calibrated per-head widths (2 and 4 bits) on layer 0, 5 % outlier channels per head
+    "d": dict(warm_bits=3, hot_budget=64, outlier_fraction=0.05, enable_promotion=False,
+              enable_promotion_proxy=False),
 }
 
 
-@pytest.mark.parametrize("name", ["a", "b", "c"])
+@pytest.mark.parametrize("name", ["a", "b", "c", "d"])
 def test_update_trace_matches_reference(name, golden_dir):
     from akv import AKVCache
     z = _traces(golden_dir)
     cache = AKVCache(num_hidden_layers=1, **CASES[name])
     if name == "b":
         cache.hot_budget = 48
+    if name == "d":
+        cache._calibration_per_head_bits = {0: [2, 4]}
     steps = z[f"{name}/steps"]
     k_in = torch.from_numpy(z[f"{name}/k_in"]).to(DEV)
     v_in = torch.from_numpy(z[f"{name}/v_in"]).to(DEV)
