@@ -48,21 +48,22 @@ SIGNATURES = {
     "akv_warm_layout_init": (c_int, [c_int, c_int, c_int, c_int, POINTER(WarmLayout)]),
     "akv_pack_codes": (c_int, [c_void_p, c_int64, c_int, c_int, c_void_p, c_void_p]),
     "akv_unpack_codes": (c_int, [c_void_p, c_int64, c_int, c_int, c_void_p, c_void_p]),
-    "akv_quantize": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64,
+    "akv_quantize": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64,
                              c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                              POINTER(QDest), c_void_p, c_void_p]),
     "akv_quantize_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int, c_int, c_int]),
-    "akv_quantize_ws": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64,
+    "akv_quantize_ws": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64,
                                 c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                                 POINTER(QDest), c_void_p, c_size_t, c_void_p, c_void_p]),
     "akv_outlier_norm_sums_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
-    "akv_outlier_norm_sums": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64,
-                                      c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_size_t, c_void_p]),
-    "akv_quantize_ext": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64,
+    "akv_outlier_norm_sums": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64,
+                                      c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_size_t, c_void_p,
+                                      c_void_p]),
+    "akv_quantize_ext": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64,
                                  c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                                  POINTER(QDest), c_void_p, c_int, c_void_p, c_size_t, c_void_p, c_void_p]),
-    "akv_dequantize": (c_int, [POINTER(QDest), c_void_p, c_int64, c_int, c_int, c_int, c_int, c_int, c_int,
-                               c_int, c_void_p, c_int64, c_int64, c_int64, c_void_p]),
+    "akv_dequantize": (c_int, [POINTER(QDest), c_void_p, c_int64, c_int64, c_int, c_int, c_int, c_int, c_int,
+                               c_int, c_int, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p]),
     "akv_int4_group_dequant": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int64,
                                        c_int, c_int, c_int, c_int, c_void_p, c_int64, c_int64, c_void_p]),
     "akv_decode_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int, c_int]),
@@ -94,8 +95,8 @@ SIGNATURES = {
                                         c_int, c_int, c_void_p, c_void_p, c_size_t, c_void_p]),
     "akv_select_workspace_bytes": (c_size_t, [c_int]),
     "akv_select_bottomk": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_size_t, c_void_p]),
-    "akv_gather_rows": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int, c_int, c_int, c_int64,
-                                c_void_p, c_int64, c_int64, c_int64, c_void_p]),
+    "akv_gather_rows": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p, c_int, c_int, c_int,
+                                c_int64, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p]),
     "akv_cold_copy": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int64, c_int, c_void_p, c_void_p]),
 }
 
@@ -173,21 +174,24 @@ def workspace_bytes(name: str, *args) -> int:
 
 def quantize(x_ptr: int, sb: int, sh: int, sn: int, tok_ptr, tok_sb: int, B: int, H: int, N: int, D: int,
              bits: int, is_key: bool, group: int, n_out: int, dest: QDest, status_ptr, device,
-             score_sum=None, score_heads: int = 0) -> None:
+             score_sum=None, score_heads: int = 0, n_src: int = 0) -> None:
     """akv_quantize_ext with a workspace from torch's allocator when the shape needs one
-    (``score_sum``: all-reduced outlier norm sums when heads are sharded over GPUs)."""
+    (``score_sum``: all-reduced outlier norm sums when heads are sharded over GPUs; ``n_src``:
+    rows the source holds, the bound the kernel checks each ``tok_ptr`` index against)."""
     import torch
     lib = load()
     need = workspace_bytes("akv_quantize_workspace_bytes", B, H, N, D, group, n_out, int(is_key))
     ws = torch.empty(need + 256, dtype=torch.uint8, device=device) if need else None
     wp = None if ws is None else (ws.data_ptr() + 255) // 256 * 256
-    rc = lib.akv_quantize_ext(x_ptr, sb, sh, sn, tok_ptr, tok_sb, B, H, N, D, bits, int(is_key), group, n_out,
+    if tok_ptr is not None and n_src <= 0:
+        raise ValueError("akv_quantize: a token index list needs the source row count n_src")
+    rc = lib.akv_quantize_ext(x_ptr, sb, sh, sn, tok_ptr, tok_sb, n_src, B, H, N, D, bits, int(is_key), group, n_out,
                               ctypes.byref(dest), None if score_sum is None else score_sum.data_ptr(), score_heads,
                               wp, need, status_ptr, torch.cuda.current_stream(device).cuda_stream)
     check(rc, "akv_quantize")
 
 
-def outlier_norm_sums(x, tok_idx, N: int, group: int):
+def outlier_norm_sums(x, tok_idx, N: int, group: int, status=None):
     """(B, n_groups, D) fp32: per scale group, the sum over x's heads of the per-(head, channel) L2 norms."""
     import torch
     lib = load()
@@ -200,7 +204,8 @@ def outlier_norm_sums(x, tok_idx, N: int, group: int):
     ti = None if tok_idx is None else tok_idx.contiguous()
     rc = lib.akv_outlier_norm_sums(x.data_ptr(), x.stride(0), x.stride(1), x.stride(2),
                                    None if ti is None else ti.data_ptr(), 0 if ti is None or ti.dim() == 1 else ti.stride(0),
-                                   B, H, N, D, group, out.data_ptr(), wp, need,
+                                   x.shape[2], B, H, N, D, group, out.data_ptr(), wp, need,
+                                   None if status is None else status.data_ptr(),
                                    torch.cuda.current_stream(x.device).cuda_stream)
     check(rc, "akv_outlier_norm_sums")
     return out

@@ -112,8 +112,8 @@ class AffineQuantizer:
         oi = q["outlier_idx"].to(torch.int16).contiguous() if n else None
         src = dict_dest(codes, scale, zero, od, oi, N, D, bits, n, is_key)
         out = torch.empty(H, N, D, dtype=torch.float16, device=codes.device)
-        rc = _C.load().akv_dequantize(ctypes.byref(src), None, 0, 1, H, N, D, bits, int(is_key), n,
-                                      out.data_ptr(), 0, N * D, D, _C.stream_of(codes))
+        rc = _C.load().akv_dequantize(ctypes.byref(src), None, 0, 0, 1, H, N, D, bits, int(is_key), n,
+                                      out.data_ptr(), 0, N * D, D, None, _C.stream_of(codes))
         _C.check(rc, "akv_dequantize")
         return out
 

@@ -162,12 +162,16 @@ class WarmArena:
             _C.quantize(x.data_ptr(), x.stride(0), x.stride(1), x.stride(2),
                         None if ti is None else ti.data_ptr(), tsb,
                         B, H, N, D, bits, is_key, min(group, N), self.n_out, dest, sp, x.device,
-                        score_sum=ss, score_heads=score_heads)
+                        score_sum=ss, score_heads=score_heads, n_src=x.shape[2])
         self.n_blocks += nblk
         return blk0
 
-    def dequantize(self, tok_idx: torch.Tensor | None = None, n_tokens: int | None = None) -> tuple:
-        """FP16 (B, H, N, D) K and V of warm token slots (``tok_idx`` = slot = blk*32 + s)."""
+    def dequantize(self, tok_idx: torch.Tensor | None = None, n_tokens: int | None = None,
+                   status: torch.Tensor | None = None) -> tuple:
+        """FP16 (B, H, N, D) K and V of warm token slots (``tok_idx`` = slot = blk*32 + s).
+
+        A slot outside the arena's written blocks records AKV_ERR_SHAPE in
+        ``status`` (an int32 device word, when given) and reads slot 0."""
         lib = _C.load()
         N = tok_idx.shape[-1] if tok_idx is not None else (n_tokens if n_tokens is not None
                                                             else self.n_blocks * BLOCK)
@@ -177,9 +181,10 @@ class WarmArena:
             src = self.dest(is_key, 0)
             rc = lib.akv_dequantize(ctypes.byref(src), None if tok_idx is None else tok_idx.data_ptr(),
                                     0 if tok_idx is None or tok_idx.dim() == 1 else tok_idx.stride(0),
+                                    max(self.n_blocks, 1) * BLOCK,
                                     self.B, self.H, N, self.D, bits, int(is_key), self.n_out,
                                     out.data_ptr(), out.stride(0), out.stride(1), out.stride(2),
-                                    _C.stream_of(self.buf))
+                                    _C.ptr(status), _C.stream_of(self.buf))
             _C.check(rc, "akv_dequantize")
             outs.append(out)
         return tuple(outs)
@@ -209,7 +214,8 @@ class WarmArena:
             dest = record_dest(self.layout, self._base(blk0) + dst_head * sh, sb, sh, rec, is_key)
             _C.quantize(xh.data_ptr(), xh.stride(0), xh.stride(1), xh.stride(2),
                         None if ti is None else ti.data_ptr(), tsb,
-                        B, 1, N, D, bits, is_key, min(group, N), self.n_out, dest, None, x.device)
+                        B, 1, N, D, bits, is_key, min(group, N), self.n_out, dest, None, x.device,
+                        n_src=x.shape[2])
 
     def drop_slots(self, slots: torch.Tensor) -> None:
         """Drop warm tokens (slot = blk*32 + s, int64 on the device) from every

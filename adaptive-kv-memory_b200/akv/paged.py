@@ -107,9 +107,9 @@ class PagedWarmPool:
             for o, (is_key, bits) in zip(outs, ((True, self.key_bits), (False, self.value_bits))):
                 src = record_dest(self.layout, base, 0, self.rec, self.H * self.rec, is_key)
                 view = o[:, :, t0:t1]
-                rc = lib.akv_dequantize(ctypes.byref(src), None, 0, 1, self.H, t1 - t0, self.D, bits, int(is_key),
-                                        self.n_out, view.data_ptr(), view.stride(0), view.stride(1), view.stride(2),
-                                        _C.stream_of(self.buf))
+                rc = lib.akv_dequantize(ctypes.byref(src), None, 0, 0, 1, self.H, t1 - t0, self.D, bits,
+                                        int(is_key), self.n_out, view.data_ptr(), view.stride(0), view.stride(1),
+                                        view.stride(2), None, _C.stream_of(self.buf))
                 _C.check(rc, "akv_dequantize")
             t0 = t1
         return tuple(outs)

@@ -61,8 +61,12 @@ def select_demote_indices(scores: torch.Tensor, n_demote: int, hot_budget: int,
     return select_bottomk(scores, n_demote, protect_initial, min(16, hot_budget // 4))
 
 
-def gather_rows(x: torch.Tensor, idx: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
-    """out[b, h, i] = x[b, h, idx[i]] for (B, H, N, D) tensors (rows of D elements)."""
+def gather_rows(x: torch.Tensor, idx: torch.Tensor, out: torch.Tensor | None = None,
+                status: torch.Tensor | None = None) -> torch.Tensor:
+    """out[b, h, i] = x[b, h, idx[i]] for (B, H, N, D) tensors (rows of D elements).
+
+    An index outside [0, N) records AKV_ERR_SHAPE in ``status`` (an int32
+    device word, when given) and copies row 0 instead."""
     _C.require_cuda(x, idx)
     B, H, N, D = x.shape
     n = idx.shape[0]
@@ -72,10 +76,10 @@ def gather_rows(x: torch.Tensor, idx: torch.Tensor, out: torch.Tensor | None = N
     if x.stride(-1) != 1 or out.stride(-1) != 1:
         raise ValueError("rows must be contiguous")
     i64 = idx.to(torch.int64).contiguous()
-    _C.check(_C.load().akv_gather_rows(x.data_ptr(), x.stride(0) * es, x.stride(1) * es, x.stride(2) * es,
+    _C.check(_C.load().akv_gather_rows(x.data_ptr(), x.stride(0) * es, x.stride(1) * es, x.stride(2) * es, N,
                                        i64.data_ptr(), n, B, H, D * es,
                                        out.data_ptr(), out.stride(0) * es, out.stride(1) * es, out.stride(2) * es,
-                                       _C.stream_of(x)), "akv_gather_rows")
+                                       _C.ptr(status), _C.stream_of(x)), "akv_gather_rows")
     return out
 
 

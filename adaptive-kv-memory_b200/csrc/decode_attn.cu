@@ -25,6 +25,7 @@
 #include <algorithm>
 #include <cfloat>
 #include <cmath>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -1271,7 +1272,11 @@ namespace akv {
 constexpr size_t kNoAllocScratchBytes = static_cast<size_t>(8) << 20;  // AKV_NOALLOC_SCRATCH_BYTES
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 constexpr int kMaxDevices = 64;
-static void* g_noalloc_ptr[kMaxDevices];  // device address of g_noalloc_scratch, per device
+// Device address of g_noalloc_scratch per device, looked up once per device
+// under a std::once_flag, so first calls from several host threads are safe.
+static void* g_noalloc_ptr[kMaxDevices];
+static int g_noalloc_rc[kMaxDevices];
+static std::once_flag g_noalloc_once[kMaxDevices];
 }  // namespace akv
 
 extern "C" int akv_mixed_decode_noalloc(const uint16_t* q, int64_t q_sb, int64_t q_sh, const uint16_t* hot_k,
@@ -1285,13 +1290,15 @@ extern "C" int akv_mixed_decode_noalloc(const uint16_t* q, int64_t q_sb, int64_t
   if (need > kNoAllocScratchBytes) return AKV_ERR_WORKSPACE;  // beyond the fixed scratch array
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return AKV_ERR_LAUNCH;
-  if (!g_noalloc_ptr[dev]) {
-    // one-time set-up per device, with that device current: the host-side name
-    // g_noalloc_scratch is not a device address, so ask the runtime for it
+  // one-time set-up per device, with that device current: the host-side name
+  // g_noalloc_scratch is not a device address, so ask the runtime for it
+  std::call_once(g_noalloc_once[dev], [dev] {
     void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return AKV_ERR_LAUNCH;
-    g_noalloc_ptr[dev] = p;
-  }
+    const bool ok = cudaGetSymbolAddress(&p, g_noalloc_scratch) == cudaSuccess && p;
+    g_noalloc_ptr[dev] = ok ? p : nullptr;
+    g_noalloc_rc[dev] = ok ? AKV_OK : AKV_ERR_LAUNCH;
+  });
+  if (g_noalloc_rc[dev] != AKV_OK) return g_noalloc_rc[dev];
   return akv_mixed_decode(q, q_sb, q_sh, hot_k, hot_v, h_sb, h_sh, h_sn, n_hot, hot_len, warm, w_sb, w_sh, layout,
                           n_warm_blocks, warm_len, B, Hq, Hkv, D, sm_scale, out, o_sb, o_sh, lse, partial_out,
                           g_noalloc_ptr[dev], kNoAllocScratchBytes, status, stream);

@@ -15,7 +15,10 @@
 // one pass over the columns yields the outlier norms and the key min/max, a
 // pass over the rows yields the value min/max, and the encode pass turns 8
 // channels of one token into BITS packed bytes per work item.  The division
-// is exact without a divide: with r = RN(1/s) precomputed per scale,
+// is exact without a divide, by Markstein's FMA remainder correction of a
+// quotient estimate (P. Markstein, "Computation of elementary functions on
+// the IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990): with
+// r = RN(1/s) precomputed per scale,
 //   q0 = x*r,  e = fma(-s, q0, x),  q = fma(e, r, q0)   (packed fp32x2 ops)
 // equals RN(x/s) for every pair of non-negative finite fp16 x and s (checked
 // exhaustively against double division, all 2^30 pairs).  fp16(q) + 1024 in
@@ -34,6 +37,7 @@ struct QuantParams {
   int64_t sb, sh, sn;
   const int64_t* tok_idx;
   int64_t tok_sb;
+  int64_t n_src;  // rows in the source: a tok_idx entry outside [0, n_src) records AKV_ERR_SHAPE, reads row 0
   int B, H, N, D, bits, is_key, group, n_out;
   akv_qdest dst;
   int* status;
@@ -87,8 +91,9 @@ AKV_DEV uint64_t div_exact2(uint64_t x2, uint64_t ns2, uint64_t r2) {
   return f2_fma(f2_fma(ns2, q0, x2), r2, q0);
 }
 
-// RN(1/s) for s an fp16 value or kZeroScale: one Newton step from the
-// hardware approximation (within 1 ulp) lands on the correctly rounded
+// RN(1/s) for s an fp16 value or kZeroScale: one Newton-Raphson step
+// y' = y + y*(1 - s*y) (residual by FMA, as in Markstein's method above) from
+// the hardware approximation (within 1 ulp) lands on the correctly rounded
 // reciprocal for every such s (checked exhaustively from starts up to 3 ulp off).
 AKV_DEV float rcp_exact(float s) {
   float y;
@@ -393,7 +398,11 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
     } else {
       for (int r = tid; r < rows; r += 32) {
         const int t = r % nt, h = r / nt;
-        const int64_t row = p.tok_idx ? p.tok_idx[b * p.tok_sb + t0 + t] : static_cast<int64_t>(t0 + t);
+        int64_t row = p.tok_idx ? p.tok_idx[b * p.tok_sb + t0 + t] : static_cast<int64_t>(t0 + t);
+        if (p.tok_idx && static_cast<uint64_t>(row) >= static_cast<uint64_t>(p.n_src)) {
+          set_status(p.status, AKV_ERR_SHAPE);
+          row = 0;
+        }
         tma_load_1d(xs + r * D, p.src + b * p.sb + (h0 + h) * p.sh + row * p.sn, D * 2, &stage_bar);
       }
     }
@@ -883,9 +892,11 @@ struct DequantParams {
   akv_qdest src;
   const int64_t* tok_idx;
   int64_t tok_sb;
+  int64_t n_src;  // tokens in the source: a tok_idx entry outside [0, n_src) records AKV_ERR_SHAPE, reads token 0
   int B, H, N, D, n_out;
   __half* out;
   int64_t osb, osh, osn;
+  int* status;
 };
 
 template <int BITS, bool IS_KEY>
@@ -900,7 +911,11 @@ __global__ void dequantize_kernel(const DequantParams p) {
     r /= p.N;
     const int h = static_cast<int>(r % p.H);
     const int b = static_cast<int>(r / p.H);
-    const int64_t tok = p.tok_idx ? p.tok_idx[b * p.tok_sb + n] : n;
+    int64_t tok = p.tok_idx ? p.tok_idx[b * p.tok_sb + n] : n;
+    if (p.tok_idx && static_cast<uint64_t>(tok) >= static_cast<uint64_t>(p.n_src)) {
+      set_status(p.status, AKV_ERR_SHAPE);
+      tok = 0;
+    }
     const int blk = static_cast<int>(tok / kBlockTokens), slot = static_cast<int>(tok % kBlockTokens);
     uint32_t wds[BITS];
     load_words<BITS>(vaddr(p.src.codes, b, h, blk, slot) + su * 4 * BITS, wds);
@@ -1150,27 +1165,28 @@ extern "C" size_t akv_quantize_workspace_bytes(int B, int H, int N, int D, int g
 }
 
 extern "C" int akv_quantize(const uint16_t* src, int64_t src_sb, int64_t src_sh, int64_t src_sn,
-                            const int64_t* tok_idx, int64_t tok_sb, int B, int H, int N, int D, int bits,
-                            int is_key, int group, int n_outlier, const akv_qdest* dst, int* status,
+                            const int64_t* tok_idx, int64_t tok_sb, int64_t n_src, int B, int H, int N, int D,
+                            int bits, int is_key, int group, int n_outlier, const akv_qdest* dst, int* status,
                             void* stream) {
-  return akv_quantize_ws(src, src_sb, src_sh, src_sn, tok_idx, tok_sb, B, H, N, D, bits, is_key, group, n_outlier,
-                         dst, nullptr, 0, status, stream);
+  return akv_quantize_ws(src, src_sb, src_sh, src_sn, tok_idx, tok_sb, n_src, B, H, N, D, bits, is_key, group,
+                         n_outlier, dst, nullptr, 0, status, stream);
 }
 
 extern "C" int akv_quantize_ws(const uint16_t* src, int64_t src_sb, int64_t src_sh, int64_t src_sn,
-                               const int64_t* tok_idx, int64_t tok_sb, int B, int H, int N, int D, int bits,
-                               int is_key, int group, int n_outlier, const akv_qdest* dst, void* workspace,
-                               size_t workspace_bytes, int* status, void* stream) {
-  return akv_quantize_ext(src, src_sb, src_sh, src_sn, tok_idx, tok_sb, B, H, N, D, bits, is_key, group,
+                               const int64_t* tok_idx, int64_t tok_sb, int64_t n_src, int B, int H, int N, int D,
+                               int bits, int is_key, int group, int n_outlier, const akv_qdest* dst,
+                               void* workspace, size_t workspace_bytes, int* status, void* stream) {
+  return akv_quantize_ext(src, src_sb, src_sh, src_sn, tok_idx, tok_sb, n_src, B, H, N, D, bits, is_key, group,
                           n_outlier, dst, nullptr, 0, workspace, workspace_bytes, status, stream);
 }
 
 extern "C" int akv_quantize_ext(const uint16_t* src, int64_t src_sb, int64_t src_sh, int64_t src_sn,
-                                const int64_t* tok_idx, int64_t tok_sb, int B, int H, int N, int D, int bits,
-                                int is_key, int group, int n_outlier, const akv_qdest* dst,
+                                const int64_t* tok_idx, int64_t tok_sb, int64_t n_src, int B, int H, int N, int D,
+                                int bits, int is_key, int group, int n_outlier, const akv_qdest* dst,
                                 const float* score_sum, int score_heads, void* workspace, size_t workspace_bytes,
                                 int* status, void* stream) {
   if (!src || !dst) return AKV_ERR_NULL;
+  if (tok_idx && n_src <= 0) return AKV_ERR_SHAPE;
   if (score_sum && score_heads <= 0) return AKV_ERR_SHAPE;
   if (bits < 2 || bits > 4) return AKV_ERR_BITS;
   if (B <= 0 || H <= 0 || N <= 0 || D <= 0 || D % 32 != 0 || D > 256) return AKV_ERR_SHAPE;
@@ -1200,6 +1216,7 @@ extern "C" int akv_quantize_ext(const uint16_t* src, int64_t src_sb, int64_t src
   p.sn = src_sn;
   p.tok_idx = tok_idx;
   p.tok_sb = tok_sb;
+  p.n_src = n_src;
   p.B = B;
   p.H = H;
   p.N = N;
@@ -1223,10 +1240,11 @@ extern "C" int akv_quantize_ext(const uint16_t* src, int64_t src_sb, int64_t src
   }
 }
 
-extern "C" int akv_dequantize(const akv_qdest* src, const int64_t* tok_idx, int64_t tok_sb, int B, int H, int N,
-                              int D, int bits, int is_key, int n_outlier, uint16_t* out, int64_t out_sb,
-                              int64_t out_sh, int64_t out_sn, void* stream) {
+extern "C" int akv_dequantize(const akv_qdest* src, const int64_t* tok_idx, int64_t tok_sb, int64_t n_src, int B,
+                              int H, int N, int D, int bits, int is_key, int n_outlier, uint16_t* out,
+                              int64_t out_sb, int64_t out_sh, int64_t out_sn, int* status, void* stream) {
   if (!src || !out || !src->codes.ptr || !src->scale.ptr || !src->zero.ptr) return AKV_ERR_NULL;
+  if (tok_idx && n_src <= 0) return AKV_ERR_SHAPE;
   if (n_outlier > 0 && (!src->out_idx.ptr || !src->out_data.ptr)) return AKV_ERR_NULL;
   if (bits < 2 || bits > 4) return AKV_ERR_BITS;
   if (B <= 0 || H <= 0 || N < 0 || D <= 0 || D % 32 != 0 || D > 256) return AKV_ERR_SHAPE;
@@ -1235,8 +1253,8 @@ extern "C" int akv_dequantize(const akv_qdest* src, const int64_t* tok_idx, int6
   if (!aligned(src->codes.ptr, 4) || src->codes.sb % 4 || src->codes.sh % 4 || src->codes.sblk % 4 ||
       src->codes.sslot % 4)
     return AKV_ERR_ALIGN;
-  DequantParams p{*src, tok_idx, tok_sb, B, H, N, D, n_outlier, reinterpret_cast<__half*>(out),
-                  out_sb, out_sh, out_sn};
+  DequantParams p{*src, tok_idx, tok_sb, n_src, B, H, N, D, n_outlier, reinterpret_cast<__half*>(out),
+                  out_sb, out_sh, out_sn, status};
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   switch (bits * 2 + (is_key ? 1 : 0)) {
     case 5: return launch_dequant<2, true>(p, st);
@@ -1308,9 +1326,11 @@ extern "C" size_t akv_outlier_norm_sums_workspace_bytes(int B, int H, int N, int
 }
 
 extern "C" int akv_outlier_norm_sums(const uint16_t* src, int64_t src_sb, int64_t src_sh, int64_t src_sn,
-                                     const int64_t* tok_idx, int64_t tok_sb, int B, int H, int N, int D, int group,
-                                     float* out, void* workspace, size_t workspace_bytes, void* stream) {
+                                     const int64_t* tok_idx, int64_t tok_sb, int64_t n_src, int B, int H, int N,
+                                     int D, int group, float* out, void* workspace, size_t workspace_bytes,
+                                     int* status, void* stream) {
   if (!src || !out) return AKV_ERR_NULL;
+  if (tok_idx && n_src <= 0) return AKV_ERR_SHAPE;
   if (B <= 0 || H <= 0 || N <= 0 || D <= 0 || D % 32 != 0 || D > 256) return AKV_ERR_SHAPE;
   if (group <= 0 || group > N) group = N;
   if (N > group && group % kBlockTokens != 0) return AKV_ERR_SHAPE;
@@ -1325,6 +1345,8 @@ extern "C" int akv_outlier_norm_sums(const uint16_t* src, int64_t src_sb, int64_
   p.sn = src_sn;
   p.tok_idx = tok_idx;
   p.tok_sb = tok_sb;
+  p.n_src = n_src;
+  p.status = status;
   p.B = B;
   p.H = H;
   p.N = N;

@@ -416,8 +416,9 @@ __global__ void __launch_bounds__(kSelThreads) sel_compact_kernel(const SelArgs 
 // row gather: 16-byte vectors, one (b, h, row) per warp-stride
 // ---------------------------------------------------------------------------
 __global__ void gather_rows_kernel(const char* __restrict__ src, int64_t s_sb, int64_t s_sh, int64_t s_sn,
-                                   const int64_t* __restrict__ idx, int n, int B, int H, int64_t row_bytes,
-                                   char* __restrict__ dst, int64_t d_sb, int64_t d_sh, int64_t d_sn) {
+                                   int64_t n_src, const int64_t* __restrict__ idx, int n, int B, int H,
+                                   int64_t row_bytes, char* __restrict__ dst, int64_t d_sb, int64_t d_sh,
+                                   int64_t d_sn, int* status) {
   const int64_t vpr = row_bytes / 16;
   const int64_t total = static_cast<int64_t>(B) * H * n * vpr;
   for (int64_t w = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; w < total;
@@ -428,7 +429,12 @@ __global__ void gather_rows_kernel(const char* __restrict__ src, int64_t s_sb, i
     r /= n;
     const int h = static_cast<int>(r % H);
     const int b = static_cast<int>(r / H);
-    const uint4 x = ldg_nc_v4(src + b * s_sb + h * s_sh + idx[i] * s_sn + v * 16);
+    int64_t row = idx[i];
+    if (static_cast<uint64_t>(row) >= static_cast<uint64_t>(n_src)) {  // out of range: flag it, read row 0
+      set_status(status, AKV_ERR_SHAPE);
+      row = 0;
+    }
+    const uint4 x = ldg_nc_v4(src + b * s_sb + h * s_sh + row * s_sn + v * 16);
     *reinterpret_cast<uint4*>(dst + b * d_sb + h * d_sh + i * d_sn + v * 16) = x;
   }
 }
@@ -528,11 +534,11 @@ extern "C" int akv_select_bottomk(const float* scores, int n, int k, int protect
   return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_LAUNCH;
 }
 
-extern "C" int akv_gather_rows(const void* src, int64_t s_sb, int64_t s_sh, int64_t s_sn, const int64_t* idx, int n,
-                               int B, int H, int64_t row_bytes, void* dst, int64_t d_sb, int64_t d_sh, int64_t d_sn,
-                               void* stream) {
+extern "C" int akv_gather_rows(const void* src, int64_t s_sb, int64_t s_sh, int64_t s_sn, int64_t n_src,
+                               const int64_t* idx, int n, int B, int H, int64_t row_bytes, void* dst, int64_t d_sb,
+                               int64_t d_sh, int64_t d_sn, int* status, void* stream) {
   if (!src || !dst || (!idx && n > 0)) return AKV_ERR_NULL;
-  if (n < 0 || B <= 0 || H <= 0 || row_bytes <= 0) return AKV_ERR_SHAPE;
+  if (n < 0 || B <= 0 || H <= 0 || row_bytes <= 0 || n_src <= 0) return AKV_ERR_SHAPE;
   if (n == 0) return AKV_OK;
   auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) % 16) == 0; };
   if (row_bytes % 16 || !al(src) || !al(dst) || s_sb % 16 || s_sh % 16 || s_sn % 16 || d_sb % 16 || d_sh % 16 ||
@@ -541,8 +547,8 @@ extern "C" int akv_gather_rows(const void* src, int64_t s_sb, int64_t s_sh, int6
   const int64_t total = static_cast<int64_t>(B) * H * n * (row_bytes / 16);
   const int64_t blocks = std::min<int64_t>((total + 255) / 256, 148 * 16);
   gather_rows_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const char*>(src), s_sb, s_sh, s_sn, idx, n, B, H, row_bytes, static_cast<char*>(dst), d_sb,
-      d_sh, d_sn);
+      static_cast<const char*>(src), s_sb, s_sh, s_sn, n_src, idx, n, B, H, row_bytes, static_cast<char*>(dst),
+      d_sb, d_sh, d_sn, status);
   return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_LAUNCH;
 }
 

@@ -1,8 +1,8 @@
 #!/usr/bin/env python
 """Benchmark of the AKV warm-tier hot path on B200.
 
-Workload (the configuration the north-star targets are
-quoted on): Llama-3-8B-shaped KV cache at 32K context, batch 16, 32 layers,
+Workload (config 3, the configuration the decode and quantise+pack targets
+are quoted on): Llama-3-8B-shaped KV cache at 32K context, batch 16, 32 layers,
 32 query / 8 KV heads, head_dim 128, fp16; k4v2 warm tier (4-bit K, 2-bit V)
 with outlier_fraction 0.01; 2048-token FP16 hot window + 30720 warm tokens
 (960 block records per (row, KV head)).  Synthetic seeded N(0,1) K/V with
@@ -20,9 +20,10 @@ Multi-GPU: KV heads are sharded across ranks (no collective on the data
 path); the timed region is bracketed by barriers and the max over ranks is
 reported (strong scaling: total work fixed).
 
---impl reference: the reference's CPU path (the numpy oracle restatement of
-AffineQuantizer dequantise + fp32 attention) on the host cores, on a bounded
-sample of units, extrapolated to the full step.
+--impl reference: the reference's CPU decode recipe (unpack, AffineQuantizer
+dequantise, cat, fp32 matmul / softmax / matmul) restated in torch and run with
+torch's CPU kernels on every host core, on a bounded sample of units,
+extrapolated to the full step.
 """
 from __future__ import annotations
 
@@ -201,7 +202,7 @@ DECODE_SHAPES = {
 
 def decode_shapes_bench(torch, akv, dev, reps: int = 20) -> dict:
     """Per-layer device time of one decode launch (decode + combine) at the
-    other BASELINE shapes.  Each shape cycles through enough layer copies
+    other configurations' shapes.  Each shape cycles through enough layer copies
     that the working set is >= 256 MB (twice the L2), inside one CUDA graph
     replayed `reps` times; algorithmic bytes as for the headline metric."""
     out = {}
@@ -622,67 +623,70 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
-# ---------------------------------------------------------------------------- CPU (oracle) arm
-def _oracle_unit(seed: int) -> float:
-    """Time the reference CPU decode path for one (row, KV head) unit of one layer:
-    dequantise the 30720 warm tokens (960 quantiser groups) and run fp32 attention
-    for the 4 query heads over [warm; hot].  Returns seconds (quantisation itself untimed)."""
-    import numpy as np
-    from oracle import akv_oracle as O
+# ---------------------------------------------------------------------------- CPU (reference path) arm
+def _cpu_shape() -> dict:
     c = CFG
-    rng = np.random.default_rng(seed)
-    n_warm, n_hot, D = c["ctx"] - c["hot"], c["hot"], c["D"]
-    g = c["Hq"] // c["Hkv"]
-    k = rng.standard_normal((1, 1, n_warm, D)).astype(np.float16)
-    v = rng.standard_normal((1, 1, n_warm, D)).astype(np.float16)
-    gk = O.quantize_groups(k, c["key_bits"], 32, True, c["outlier_fraction"])
-    gv = O.quantize_groups(v, c["value_bits"], 32, False, c["outlier_fraction"])
-    hk = rng.standard_normal((1, 1, n_hot, D)).astype(np.float16)
-    hv = rng.standard_normal((1, 1, n_hot, D)).astype(np.float16)
-    q = rng.standard_normal((1, g, D)).astype(np.float16)
-    t = time.perf_counter()
-    dk = O.dequantize_groups(gk)
-    dv = O.dequantize_groups(gv)
-    O.decode_attention(q, np.concatenate([dk, hk], 2), np.concatenate([dv, hv], 2))
-    return time.perf_counter() - t
+    return dict(n_warm=c["ctx"] - c["hot"], n_hot=c["hot"], D=c["D"], g=c["Hq"] // c["Hkv"],
+                key_bits=c["key_bits"], value_bits=c["value_bits"], outlier_fraction=c["outlier_fraction"])
+
+
+def _cpu_sample(units: int, threads: int):
+    """Build `units` seeded (row, KV head) units once (untimed); return a
+    function that times one pass of the reference's CPU decode path over them
+    and returns the per-step estimate in µs (mean per unit x units per step)."""
+    from oracle import akv_torch_ref as R
+    import torch
+    torch.set_num_threads(threads)
+    shape = _cpu_shape()
+    inputs = [R.unit_inputs(s, **shape) for s in range(units)]
+    total_units = CFG["B"] * CFG["Hkv"] * CFG["layers"]
+
+    def one_pass() -> float:
+        t = time.perf_counter()
+        for a in inputs:
+            R.decode_unit(*a)
+        return (time.perf_counter() - t) / len(inputs) * total_units * 1e6
+
+    one_pass()  # first touch
+    return one_pass, total_units
+
+
+def _cpu_desc(units: int, total_units: int, threads: int) -> str:
+    from oracle import akv_torch_ref as R
+    return (f"{units} of {total_units} (row, KV head, layer) units per step, extrapolated linearly to the full "
+            f"step: the reference's CPU decode recipe in torch (unpack + dequantise_keys/values of the 30720 "
+            f"warm tokens, cat with the 2048 hot, fp32 matmul-softmax-matmul for 4 query heads), "
+            f"torch.set_num_threads({threads}) on {R.cpu_model()}")
 
 
 def cpu_baseline(units: int, world: int) -> dict:
-    """Single-core oracle timing on `units` sampled units, extrapolated to the full step."""
-    c = CFG
-    total_units = c["B"] * c["Hkv"] * c["layers"]
-    per_unit = statistics.mean(_oracle_unit(s) for s in range(units))
-    us_step = per_unit * total_units * 1e6
-    return {"value": round(us_step, 1), "unit": "µs/step", "cores": 1, "kind": "port",
-            "sample": f"{units} of {total_units} (row, KV head, layer) units of one decode step "
-                      f"(dequantise 30720 warm tokens + fp32 attention over 32768 tokens, 4 query heads), "
-                      f"extrapolated linearly to the full step"}
+    """The reference's CPU decode path on all host cores, a bounded sample of units."""
+    threads = os.cpu_count() or 1
+    one_pass, total_units = _cpu_sample(units, threads)
+    v = statistics.median(one_pass() for _ in range(3))
+    return {"value": round(v, 1), "unit": "µs/step", "cores": threads, "kind": "port",
+            "sample": _cpu_desc(units, total_units, threads)}
 
 
 def run_reference(args):
-    """Time the reference's CPU path (oracle port) on all host cores, one bounded sample per step."""
+    """Time the reference's CPU path on the host cores (rank 0 only), one bounded sample per step."""
     world, rank, local = dist_setup()
     if rank != 0:
         return
-    import multiprocessing as mp
-    c = CFG
-    procs = os.cpu_count() or 1
-    total_units = c["B"] * c["Hkv"] * c["layers"]
+    threads = os.cpu_count() or 1
+    one_pass, total_units = _cpu_sample(args.cpu_units, threads)
     vals = []
-    with mp.get_context("spawn").Pool(procs) as pool:
-        for i in range(args.warmup + args.steps):
-            t = pool.map(_oracle_unit, range(i * procs, (i + 1) * procs))
-            if i >= args.warmup:
-                vals.append(statistics.mean(t) * total_units / procs * 1e6)
+    for i in range(args.warmup + args.steps):
+        v = one_pass()
+        if i >= args.warmup:
+            vals.append(v)
     v = statistics.mean(vals)
-    sample = (f"{procs} of {total_units} (row, KV head, layer) units per step, one per core "
-              f"(dequantise 30720 warm tokens + fp32 attention over 32768 tokens, 4 query heads), "
-              f"extrapolated linearly to the full step")
+    sample = _cpu_desc(args.cpu_units, total_units, threads)
     res = {"metric": METRIC, "impl": "reference", "value": round(v, 1), "unit": "µs/step",
            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(v / 1e3, 3),
            "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "f16 in, f32 acc",
            "data": "synthetic (seeded N(0,1) K/V)", "config": workload_config(1),
-           "cpu_baseline": {"value": round(v, 1), "unit": "µs/step", "cores": procs, "kind": "port",
+           "cpu_baseline": {"value": round(v, 1), "unit": "µs/step", "cores": threads, "kind": "port",
                             "sample": sample},
            "e2e": {"value": round(v, 1), "unit": "µs/step", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(res), flush=True)
@@ -695,7 +699,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=CFG["layers"])
-    ap.add_argument("--cpu-units", type=int, default=8)
+    ap.add_argument("--cpu-units", type=int, default=4, help="(row, KV head) units timed per CPU-arm step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-migration", action="store_true")
     ap.add_argument("--no-shapes", action="store_true", help="skip the per-layer decode timings of configs 1, 2, 5")

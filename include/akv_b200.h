@@ -14,8 +14,10 @@
  *     a negative AKV_ERR_* code without launching anything on error.
  *   - Work is enqueued asynchronously on `stream`; no call synchronises.
  *   - `status` (nullable) is a device int that kernels set to a negative
- *     AKV_ERR_* code when a bounded device-side wait runs out; callers read it
- *     after synchronising.  It is never cleared by the library.
+ *     AKV_ERR_* code when a bounded device-side wait runs out (AKV_ERR_TIMEOUT)
+ *     or an index read from device memory is out of range (AKV_ERR_SHAPE; the
+ *     access is redirected to element 0, never made out of bounds); callers
+ *     read it after synchronising.  It is never cleared by the library.
  *   - The library never allocates device memory: scratch comes from the
  *     caller as `workspace`.
  *   - fp16 = IEEE binary16 stored as uint16_t.
@@ -30,7 +32,7 @@
 extern "C" {
 #endif
 
-#define AKV_ABI_VERSION 2
+#define AKV_ABI_VERSION 3
 #define AKV_BLOCK_TOKENS 32 /* tokens per warm block record */
 
 enum {
@@ -135,6 +137,9 @@ int akv_unpack_codes(const uint8_t* packed, int64_t rows, int dim, int bits, uin
  *                (d contiguous, rows 16-byte aligned)
  *   tok_idx      optional int64 row indices: token t of the call reads row
  *                tok_idx[b*tok_sb + t] (fused gather for demotion); NULL = rows 0..N-1
+ *   n_src        rows the source holds (used with tok_idx; ignored when it is NULL):
+ *                an index outside [0, n_src) records AKV_ERR_SHAPE in *status and
+ *                reads row 0 instead, so a bad index list never reads out of bounds
  *   B, H, N, D   batch rows, heads, tokens in the call, head dim (D % 32 == 0, D <= 256)
  *   group        tokens per scale group (K min/max and outlier selection run
  *                per group of `group` consecutive tokens; N = one reference call)
@@ -142,7 +147,7 @@ int akv_unpack_codes(const uint8_t* packed, int64_t rows, int dim, int bits, uin
  *                max(1, int(D*outlier_fraction))
  * ---------------------------------------------------------------------- */
 int akv_quantize(const uint16_t* src, int64_t src_sb, int64_t src_sh, int64_t src_sn,
-                 const int64_t* tok_idx, int64_t tok_sb,
+                 const int64_t* tok_idx, int64_t tok_sb, int64_t n_src,
                  int B, int H, int N, int D, int bits, int is_key, int group, int n_outlier,
                  const akv_qdest* dst, int* status, void* stream);
 
@@ -157,7 +162,7 @@ size_t akv_quantize_workspace_bytes(int B, int H, int N, int D, int group, int n
  * akv_quantize_workspace_bytes); identical results.  Without enough
  * workspace a shape that needs the chunked path returns AKV_ERR_WORKSPACE. */
 int akv_quantize_ws(const uint16_t* src, int64_t src_sb, int64_t src_sh, int64_t src_sn,
-                    const int64_t* tok_idx, int64_t tok_sb,
+                    const int64_t* tok_idx, int64_t tok_sb, int64_t n_src,
                     int B, int H, int N, int D, int bits, int is_key, int group, int n_outlier,
                     const akv_qdest* dst, void* workspace, size_t workspace_bytes, int* status, void* stream);
 
@@ -170,13 +175,14 @@ int akv_quantize_ws(const uint16_t* src, int64_t src_sb, int64_t src_sh, int64_t
  * akv_outlier_norm_sums_workspace_bytes (256-byte aligned). */
 size_t akv_outlier_norm_sums_workspace_bytes(int B, int H, int N, int D, int group);
 int akv_outlier_norm_sums(const uint16_t* src, int64_t src_sb, int64_t src_sh, int64_t src_sn,
-                          const int64_t* tok_idx, int64_t tok_sb, int B, int H, int N, int D, int group,
-                          float* out, void* workspace, size_t workspace_bytes, void* stream);
+                          const int64_t* tok_idx, int64_t tok_sb, int64_t n_src, int B, int H, int N, int D,
+                          int group, float* out, void* workspace, size_t workspace_bytes, int* status,
+                          void* stream);
 
 /* akv_quantize_ws with outlier scores from outside: score_sum [B][n_groups][D]
  * (NULL = from this call's heads), score = score_sum / score_heads. */
 int akv_quantize_ext(const uint16_t* src, int64_t src_sb, int64_t src_sh, int64_t src_sn,
-                     const int64_t* tok_idx, int64_t tok_sb,
+                     const int64_t* tok_idx, int64_t tok_sb, int64_t n_src,
                      int B, int H, int N, int D, int bits, int is_key, int group, int n_outlier,
                      const akv_qdest* dst, const float* score_sum, int score_heads,
                      void* workspace, size_t workspace_bytes, int* status, void* stream);
@@ -188,11 +194,14 @@ int akv_quantize_ext(const uint16_t* src, int64_t src_sb, int64_t src_sh, int64_
  *   src          the same view struct the quantiser wrote (mask ignored)
  *   tok_idx      optional int64 token indices into the source token space
  *                (token p lives in blk p/32, slot p%32); NULL = tokens 0..N-1
+ *   n_src        tokens the source holds (used with tok_idx): an index outside
+ *                [0, n_src) records AKV_ERR_SHAPE in *status (nullable) and
+ *                reads token 0 instead
  *   out          fp16 (b, h, n, d) at out + b*out_sb + h*out_sh + n*out_sn + d
  * ---------------------------------------------------------------------- */
-int akv_dequantize(const akv_qdest* src, const int64_t* tok_idx, int64_t tok_sb,
+int akv_dequantize(const akv_qdest* src, const int64_t* tok_idx, int64_t tok_sb, int64_t n_src,
                    int B, int H, int N, int D, int bits, int is_key, int n_outlier,
-                   uint16_t* out, int64_t out_sb, int64_t out_sh, int64_t out_sn, void* stream);
+                   uint16_t* out, int64_t out_sb, int64_t out_sh, int64_t out_sn, int* status, void* stream);
 
 /* ------------------------------------------------------------------------
  * Dequantise the reference's INT4 per-token, per-D-group layout
@@ -276,7 +285,9 @@ int akv_mixed_decode_paged(const uint16_t* q, int64_t q_sb, int64_t q_sh,
  * the process exits.  Shapes whose akv_decode_workspace_bytes exceeds it are
  * rejected with AKV_ERR_WORKSPACE before anything is launched.  The first call
  * on a device looks up the array's device address (cudaGetSymbolAddress) with
- * that device current; make that first call before any stream capture.  All
+ * that device current, once per device even when several host threads make
+ * their first call at the same time; make that first call before any stream
+ * capture.  All
  * calls on a device share the one array, so calls that overlap on the GPU
  * (different streams, no ordering between them) race and must not be issued. */
 #define AKV_NOALLOC_SCRATCH_BYTES (8u << 20)
@@ -342,10 +353,12 @@ int akv_select_bottomk(const float* scores, int n, int k, int protect_first, int
 /* Row gather/compaction for tier moves (drop_in.py:684-685 gather,
  * :739-751 keep-mask compaction, :474-475 promote-prepend).
  * Copies `n` rows of `row_bytes` (multiple of 16) for every (b, h):
- *   dst + b*d_sb + h*d_sh + i*d_sn  <-  src + b*s_sb + h*s_sh + idx[i]*s_sn   */
-int akv_gather_rows(const void* src, int64_t s_sb, int64_t s_sh, int64_t s_sn,
+ *   dst + b*d_sb + h*d_sh + i*d_sn  <-  src + b*s_sb + h*s_sh + idx[i]*s_sn
+ * The source holds n_src rows: an idx entry outside [0, n_src) records
+ * AKV_ERR_SHAPE in *status (nullable) and copies row 0 instead. */
+int akv_gather_rows(const void* src, int64_t s_sb, int64_t s_sh, int64_t s_sn, int64_t n_src,
                     const int64_t* idx, int n, int B, int H, int64_t row_bytes,
-                    void* dst, int64_t d_sb, int64_t d_sh, int64_t d_sn, void* stream);
+                    void* dst, int64_t d_sb, int64_t d_sh, int64_t d_sn, int* status, void* stream);
 
 /* ------------------------------------------------------------------------
  * A8: cold tier copies.  Replaces AsyncMigrator._do_warm_to_cold /

@@ -149,7 +149,7 @@ def main(ref_path: str):
     np.savez_compressed(os.path.join(HERE, "affine.npz"), **out)
 
     # ---------------- config-1 slice: 32-token groups ----------------
-    # BASELINE config 1 shapes (B1, 2 KV heads, D128, 3-bit), first 8 groups.
+    # config 1 shapes (B1, 2 KV heads, D128, 3-bit), first 8 groups.
     g = torch.Generator().manual_seed(0)
     H, N, D = 2, 256, 128
     kout = list(range(0, D, 100))  # one planted outlier channel at D=128
@@ -404,6 +404,15 @@ def make_migrator_trace(ref_path: str):
     print("migrator trace written to", HERE, snaps, "snapshots")
 
 
+def _reference_path() -> str:
+    """The reference source tree: the first argument, else $AKV_REFERENCE."""
+    path = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("AKV_REFERENCE", "")
+    if not path:
+        sys.exit("usage: make_golden.py <reference source path> [migrator|drop_in|per_head] "
+                 "(or set AKV_REFERENCE)")
+    return path
+
+
 if __name__ == "__main__":
     if len(sys.argv) > 2 and sys.argv[2] == "migrator":
         make_migrator_trace(sys.argv[1])
@@ -413,7 +422,8 @@ if __name__ == "__main__":
     elif len(sys.argv) > 2 and sys.argv[2] == "per_head":
         make_per_head_trace(sys.argv[1])
     else:
-        main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
-        make_drop_in_traces(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
-        make_migrator_trace(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
-        make_per_head_trace(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+        ref = _reference_path()
+        main(ref)
+        make_drop_in_traces(ref)
+        make_migrator_trace(ref)
+        make_per_head_trace(ref)

@@ -40,7 +40,7 @@ def test_ctypes_table_matches_header():
 def test_version_and_strerror():
     from akv import _C
     lib = _C.load()
-    assert lib.akv_abi_version() == 2
+    assert lib.akv_abi_version() == 3
     assert _C.strerror(0) == "ok"
     for code in range(-1, -9, -1):
         assert _C.strerror(code) != "unknown status"
@@ -67,13 +67,18 @@ def test_host_validation_without_gpu():
     assert lib.akv_warm_layout_init(128, 5, 3, 0, ctypes.byref(_C.WarmLayout())) == -2
     assert lib.akv_warm_layout_init(100, 3, 3, 0, ctypes.byref(_C.WarmLayout())) == -1
     d = _C.QDest()
-    assert lib.akv_quantize(None, 0, 0, 0, None, 0, 1, 1, 1, 128, 3, 1, 32, 0, ctypes.byref(d), None, None) == -7
-    assert lib.akv_quantize(16, 0, 0, 0, None, 0, 1, 1, 1, 128, 9, 1, 32, 0, ctypes.byref(d), None, None) == -2
-    assert lib.akv_quantize(16, 0, 0, 0, None, 0, 1, 1, 1, 100, 3, 1, 32, 0, ctypes.byref(d), None, None) == -1
-    assert lib.akv_quantize(8, 0, 0, 0, None, 0, 1, 1, 1, 128, 3, 1, 32, 0, ctypes.byref(d), None, None) == -3
+    assert lib.akv_quantize(None, 0, 0, 0, None, 0, 0, 1, 1, 1, 128, 3, 1, 32, 0, ctypes.byref(d), None, None) == -7
+    assert lib.akv_quantize(16, 0, 0, 0, None, 0, 0, 1, 1, 1, 128, 9, 1, 32, 0, ctypes.byref(d), None, None) == -2
+    assert lib.akv_quantize(16, 0, 0, 0, None, 0, 0, 1, 1, 1, 100, 3, 1, 32, 0, ctypes.byref(d), None, None) == -1
+    assert lib.akv_quantize(8, 0, 0, 0, None, 0, 0, 1, 1, 1, 128, 3, 1, 32, 0, ctypes.byref(d), None, None) == -3
     assert lib.akv_mixed_decode(16, 0, 0, None, None, 0, 0, 0, 0, None, None, 0, 0, None, 0, None,
                                 1, 8, 2, 64, 1.0, 16, 0, 0, None, None, None, 0, None, None) == -4
     assert lib.akv_decode_workspace_bytes(1, 12, 2, 128, 512, 112) > 0
     assert lib.akv_decode_workspace_bytes(1, 12, 5, 128, 512, 112) == 0
     assert lib.akv_select_bottomk(None, 10, 3, 0, 0, None, None, 0, None) == -7
     assert lib.akv_cold_copy(16, 8, 16, 16, 16, 1, 0, None, None) == -1
+    # an index list needs the source length it is checked against (n_src > 0)
+    assert lib.akv_quantize(16, 0, 0, 0, 16, 0, 0, 1, 1, 1, 128, 3, 1, 32, 0, ctypes.byref(d), None, None) == -1
+    assert lib.akv_dequantize(ctypes.byref(d), 16, 0, 0, 1, 1, 1, 128, 3, 1, 0, 16, 0, 0, 0, None, None) == -7
+    assert lib.akv_gather_rows(16, 0, 0, 16, 0, 16, 1, 1, 1, 16, 16, 0, 0, 16, None, None) == -1
+    assert lib.akv_abi_version() == 3

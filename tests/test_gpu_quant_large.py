@@ -121,10 +121,10 @@ def test_chunked_shape_needs_workspace():
     od = torch.empty(H, N, 1, dtype=torch.float16, device=DEV)
     oi = torch.empty(1, dtype=torch.int16, device=DEV)
     dest = akv.affine_quantizer.dict_dest(codes, scale, zero, od, oi, N, D, 4, 1, True)
-    rc = lib.akv_quantize(x.data_ptr(), 0, N * D, D, None, 0, 1, H, N, D, 4, 1, N, 1, ctypes.byref(dest), None,
+    rc = lib.akv_quantize(x.data_ptr(), 0, N * D, D, None, 0, 0, 1, H, N, D, 4, 1, N, 1, ctypes.byref(dest), None,
                           torch.cuda.current_stream().cuda_stream)
     assert rc == -8  # AKV_ERR_WORKSPACE
     ws = torch.empty(need - 256, dtype=torch.uint8, device=DEV)
-    rc = lib.akv_quantize_ws(x.data_ptr(), 0, N * D, D, None, 0, 1, H, N, D, 4, 1, N, 1, ctypes.byref(dest),
+    rc = lib.akv_quantize_ws(x.data_ptr(), 0, N * D, D, None, 0, 0, 1, H, N, D, 4, 1, N, 1, ctypes.byref(dest),
                              ws.data_ptr(), need - 256, None, torch.cuda.current_stream().cuda_stream)
     assert rc == -8
