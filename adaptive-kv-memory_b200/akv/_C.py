@@ -86,6 +86,11 @@ SIGNATURES = {
                                          c_int, c_int, c_int, c_int, c_float,
                                          c_void_p, c_int64, c_int64, c_void_p, c_void_p,
                                          c_void_p, c_void_p]),
+    "akv_prefill_attention": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int,
+                                      c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int, c_void_p, c_int64,
+                                      c_void_p, c_int64, c_int64, POINTER(WarmLayout), c_int, c_void_p, c_int64,
+                                      c_int, c_int, c_int, c_int, c_float,
+                                      c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p]),
     "akv_lse_combine": (c_int, [c_void_p, c_int64, c_int64, c_int, c_int, c_int, c_void_p, c_int64, c_void_p,
                                 c_void_p, c_void_p]),
     "akv_importance_update": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int, c_float, c_void_p]),

@@ -1,7 +1,8 @@
 """akv — B200-native warm tier of Adaptive KV Memory.
 
 Block-affine quantise + bit-pack, packed warm block records, mixed-tier
-(FP16 hot + packed warm) split-K decode attention, importance update and
+(FP16 hot + packed warm) split-K decode attention and tensor-core prefill
+attention, importance update and
 demote/promote, behind the reference package's Python API.  Every op runs in
 the sm_100a library ``akv/_lib/libakv_sm100.so``; there is no CPU fallback.
 """
@@ -9,7 +10,7 @@ from . import _C
 from .affine_quantizer import AffineQuantConfig, AffineQuantizer
 from .bitpack import pack, unpack, packed_bytes
 from .fused_attention import (fused_int4_decode_attention, int4_group_dequant, mixed_precision_decode_attention,
-                              mixed_tier_decode_attention)
+                              mixed_tier_decode_attention, prefill_attention)
 from .packed_layout import WarmArena, measure_packed_bytes
 from .drop_in import AKVCache, AKVLayer, recommend_preset
 
@@ -19,6 +20,6 @@ __all__ = [
     "AKVCache", "AKVLayer", "recommend_preset",
     "AffineQuantConfig", "AffineQuantizer", "WarmArena", "measure_packed_bytes",
     "mixed_tier_decode_attention", "mixed_precision_decode_attention", "fused_int4_decode_attention",
-    "int4_group_dequant",
+    "int4_group_dequant", "prefill_attention",
     "pack", "unpack", "packed_bytes",
 ]

@@ -213,3 +213,67 @@ def mixed_precision_decode_attention(query, hot_keys, hot_values,
     _int4_partials(q, warm_k_packed, warm_k_scales, warm_k_zeros, warm_v_packed, warm_v_scales, warm_v_zeros,
                    group_size, sm_scale, warm_k_packed.shape[1], parts)
     return _combine(parts, B, H, Dp, q.device)[..., :D].unsqueeze(2)
+
+
+def prefill_attention(query: torch.Tensor, q_pos: torch.Tensor,
+                      hot_keys: Optional[torch.Tensor] = None, hot_values: Optional[torch.Tensor] = None,
+                      hot_pos: Optional[torch.Tensor] = None, warm=None, warm_pos: Optional[torch.Tensor] = None,
+                      sm_scale: Optional[float] = None, out: Optional[torch.Tensor] = None,
+                      return_lse: bool = False, status: Optional[torch.Tensor] = None):
+    """Causal attention of many query tokens over the FP16 hot tier and the packed warm tier.
+
+    The prefill attention the reference runs with SDPA over ``AKVLayer``'s
+    chronological FP16 view (akv/drop_in.py:753-787), on the tcgen05 tensor
+    cores (``akv_prefill_attention``): query token m sees key token j iff
+    ``pos(j) <= q_pos[m]``; warm records are dequantised exactly like the
+    reference inside the kernel, never written back to memory.
+
+    query:      (B, Hq, M, D) fp16, D = 128
+    q_pos:      (B, M) or (M,) int32 query positions
+    hot_keys:   (B, Hkv, N_hot, D) fp16 and hot_pos (B, N_hot) or (N_hot,) int32
+    warm:       a ``WarmArena``; warm_pos (B, n_blocks*32) or (n_blocks*32,) int32
+                positions of the record slots (slots with a clear mask bit are skipped)
+    Returns (B, Hq, M, D) fp16 (and the natural-log LSE (B, Hq, M) fp32).
+    """
+    _C.require_cuda(query, hot_keys, hot_values)
+    B, Hq, M, D = query.shape
+    if query.stride(-1) != 1:
+        query = query.contiguous()
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    dev = query.device
+
+    def pos2(p, n):
+        p = p.to(device=dev, dtype=torch.int32)
+        p = p.unsqueeze(0).expand(B, n) if p.dim() == 1 else p
+        if p.stride(-1) != 1:
+            p = p.contiguous()
+        return p
+
+    qp = pos2(q_pos, M)
+    nh = 0 if hot_keys is None else hot_keys.shape[2]
+    if nh:
+        Hkv = hot_keys.shape[1]
+        if hot_keys.stride() != hot_values.stride() or hot_keys.stride(-1) != 1:
+            raise ValueError("hot keys / values need equal strides and a contiguous last dim")
+        hp = pos2(hot_pos, nh)
+    else:
+        Hkv = warm.H if warm is not None else Hq
+        hp = None
+    nwb = warm.n_blocks if warm is not None else 0
+    wp = pos2(warm_pos, nwb * _C.BLOCK_TOKENS) if nwb else None
+    if warm is not None and (warm.B != B or warm.H != Hkv or warm.D != D):
+        raise ValueError("warm arena shape does not match the query / hot tier")
+    o = out if out is not None else torch.empty(B, Hq, M, D, dtype=torch.float16, device=dev)
+    lse = torch.empty(B, Hq, M, dtype=torch.float32, device=dev) if return_lse else None
+    hs = hot_keys.stride() if nh else (0, 0, 0, 1)
+    rc = _C.load().akv_prefill_attention(
+        query.data_ptr(), query.stride(0), query.stride(1), query.stride(2), qp.data_ptr(), qp.stride(0), M,
+        hot_keys.data_ptr() if nh else None, hot_values.data_ptr() if nh else None, hs[0], hs[1], hs[2], nh,
+        hp.data_ptr() if nh else None, hp.stride(0) if nh else 0,
+        warm.buf.data_ptr() if nwb else None, warm.buf.stride(0) if nwb else 0, warm.buf.stride(1) if nwb else 0,
+        ctypes.byref(warm.layout) if nwb else None, nwb, wp.data_ptr() if nwb else None, wp.stride(0) if nwb else 0,
+        B, Hq, Hkv, D, float(sm_scale), o.data_ptr(), o.stride(0), o.stride(1), o.stride(2), _C.ptr(lse),
+        _C.ptr(status), _C.stream_of(query))
+    _C.check(rc, "akv_prefill_attention")
+    return (o, lse) if return_lse else o

@@ -300,6 +300,39 @@ int akv_mixed_decode_noalloc(const uint16_t* q, int64_t q_sb, int64_t q_sh,
                              uint16_t* out, int64_t o_sb, int64_t o_sh, float* lse, float* partial_out,
                              int* status, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Mixed-tier prefill attention (many query tokens, causal by position) on
+ * the tcgen05 tensor cores.  Replaces the prefill attention the reference
+ * runs with SDPA over AKVLayer's chronological FP16 view
+ * (akv/drop_in.py:753-787, the view built at :762-775): query token m of row b
+ * sees key token j iff pos(j) <= q_pos[b*qp_sb + m], over the FP16 hot tier
+ * and the packed warm records (dequantised exactly like the reference,
+ * never materialised in HBM).  fp16 operands, fp32 accumulation, softmax
+ * probabilities rounded to fp16 before the P.V product.
+ *
+ *   q            fp16 (b, hq, m, d) at q + b*q_sb + hq*q_sh + m*q_sm + d, m < M
+ *   q_pos        int32 query positions, q_pos[b*qp_sb + m]
+ *   hot_k/hot_v  fp16 (b, hkv, t, d) at p + b*h_sb + h*h_sh + t*h_sn + d, t < n_hot
+ *   hot_pos      int32 hot-token positions, hot_pos[b*hp_sb + t]
+ *   warm         block records, record j of (b, hkv) at warm + b*w_sb + h*w_sh + j*layout.bytes;
+ *                slot s of record j holds the token at warm_pos[b*wp_sb + 32*j + s]
+ *                (slots whose mask bit is clear are skipped)
+ *   out          fp16 (b, hq, m, d) at out + b*o_sb + hq*o_sh + m*o_sm + d
+ *   lse          optional fp32 [(b*Hq + hq)*M + m], natural-log LSE of the
+ *                scaled logits (-inf for a row that sees no key)
+ * D == 128; q, hot and out bases 16-byte aligned with strides multiples of 8
+ * elements (tensor TMA).  A query row that sees no key gets a zero output row.
+ * ---------------------------------------------------------------------- */
+int akv_prefill_attention(const uint16_t* q, int64_t q_sb, int64_t q_sh, int64_t q_sm,
+                          const int32_t* q_pos, int64_t qp_sb, int M,
+                          const uint16_t* hot_k, const uint16_t* hot_v, int64_t h_sb, int64_t h_sh, int64_t h_sn,
+                          int n_hot, const int32_t* hot_pos, int64_t hp_sb,
+                          const uint8_t* warm, int64_t w_sb, int64_t w_sh, const akv_warm_layout* layout,
+                          int n_warm_blocks, const int32_t* warm_pos, int64_t wp_sb,
+                          int B, int Hq, int Hkv, int D, float sm_scale,
+                          uint16_t* out, int64_t o_sb, int64_t o_sh, int64_t o_sm, float* lse,
+                          int* status, void* stream);
+
 /* Log-sum-exp combine of partial records (acc[D], m, l) — the split-K merge
  * inside one GPU and the merge of a sequence split across GPUs.  Record of
  * row r, split s at part + s*part_ss + r*part_sr (floats).  Writes any of:

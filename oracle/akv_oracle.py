@@ -327,6 +327,41 @@ def decode_attention(q: np.ndarray, keys: np.ndarray, values: np.ndarray,
 
 
 
+def prefill_attention(q: np.ndarray, q_pos: np.ndarray, keys: np.ndarray, values: np.ndarray,
+                      key_pos: np.ndarray, sm_scale: float | None = None) -> np.ndarray:
+    """Causal attention by position in fp32: the SDPA the reference runs over
+    AKVLayer's chronological FP16 view during prefill (akv/drop_in.py:753-787;
+    the view holds every token once, in position order, so the causal mask of
+    query i is "key position <= position of i").
+
+    q: (B, Hq, M, D); q_pos: (B, M); keys/values: (B, Hkv, N, D) fp16 (the
+    dequantised warm tokens and the hot tokens in any order); key_pos: (B, N)
+    (a key with position > every query position is never seen).  GQA as in
+    decode_attention.  A row that sees no key is zero.  Returns fp32 (B, Hq, M, D).
+    """
+    q = _f(q)
+    B, Hq, M, D = q.shape
+    Hkv = keys.shape[1]
+    g = Hq // Hkv
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    kf = _f(keys)
+    vf = _f(values)
+    out = np.zeros((B, Hq, M, D), F32)
+    for b in range(B):
+        vis = key_pos[b][None, :] <= q_pos[b][:, None]  # (M, N)
+        for h in range(Hq):
+            kv = h // g
+            s = (q[b, h] @ kf[b, kv].T).astype(F32) * F32(sm_scale)
+            s = np.where(vis, s, -np.inf)
+            m = s.max(axis=1, keepdims=True)
+            m = np.where(np.isfinite(m), m, 0.0).astype(F32)
+            p = np.exp(s - m)
+            l = p.sum(axis=1, keepdims=True, dtype=F32)
+            out[b, h] = np.where(l > 0, (p @ vf[b, kv]) / np.where(l > 0, l, 1.0), 0.0)
+    return out
+
+
 LOG2E = 1.4426950408889634
 
 
