@@ -135,6 +135,10 @@ class AKVLayer(_LayerBase):
         self._nan: Optional[torch.Tensor] = None  # one-element source of the fused-decode placeholder
         self._warm: Optional[WarmArena] = None  # packed warm block records (source of truth)
         self._warm_slots: Optional[torch.Tensor] = None  # arena slot (blk*32 + s) of each warm token
+        # int32 position of the token in each arena slot (device), read by the
+        # prefill kernel; slots a demote event leaves empty are never read
+        # (their record mask bit is clear)
+        self._slot_pos: Optional[torch.Tensor] = None
         self._warm_len = 0
         self._total_len = 0
         self._warm_bytes_packed = 0
@@ -169,9 +173,11 @@ class AKVLayer(_LayerBase):
         return torch.from_numpy(np.sort(idx.numpy()))
 
     # ------------------------------------------------------------------ warm tier
-    def _demote(self, demote_idx: torch.Tensor, idx_dev: Optional[torch.Tensor] = None) -> None:
+    def _demote(self, demote_idx: torch.Tensor, idx_dev: Optional[torch.Tensor] = None,
+                pos_dev: Optional[torch.Tensor] = None) -> None:
         """Quantise the selected hot rows into new warm records (one scale group per batch row).
-        ``idx_dev``: the same indices already on the device."""
+        ``idx_dev``: the same indices already on the device; ``pos_dev``: the
+        demoted tokens' positions on the device (recorded per arena slot)."""
         hk, hv = self._hot_keys, self._hot_values
         _C.require_cuda(hk, hv)
         B, H, _, D = hk.shape
@@ -192,6 +198,8 @@ class AKVLayer(_LayerBase):
         blk0 = arena.append(hk, hv, group=n, tok_idx=idx_dev)
         slots = torch.arange(blk0 * BLOCK, blk0 * BLOCK + n, dtype=torch.int64, device=hk.device)
         self._append_1d("_warm_slots", slots)
+        if pos_dev is not None:
+            self._record_slot_pos(blk0 * BLOCK, pos_dev)
         # the reference's measure_packed_bytes of this event's K and V dicts (drop_in.py:331-336)
         if isinstance(arena, HeadGroupArena):  # one K and one V dict per head, at that head's width
             self._warm_bytes_packed += B * sum(2 * n * packed_width(D, b) + 4 * D + 4 * n for b in self.per_head_bits)
@@ -201,6 +209,17 @@ class AKVLayer(_LayerBase):
                                             + 4 * H * n)
         if not self._no_fp16_copy:
             self._append_warm_fp16(*arena.dequantize(tok_idx=slots))
+
+    def _record_slot_pos(self, slot0: int, pos_dev: torch.Tensor) -> None:
+        """Positions of the tokens written at arena slots slot0 .. slot0 + n - 1."""
+        need = self._warm.max_blocks * BLOCK
+        buf = self._slot_pos
+        if buf is None or buf.shape[0] < need or buf.device != pos_dev.device:
+            nb = torch.zeros(need, dtype=torch.int32, device=pos_dev.device)
+            if buf is not None:
+                nb[:buf.shape[0]].copy_(buf[:need])
+            self._slot_pos = buf = nb
+        buf[slot0:slot0 + pos_dev.shape[0]].copy_(pos_dev)
 
     @property
     def _no_fp16_copy(self) -> bool:
@@ -398,11 +417,13 @@ class AKVLayer(_LayerBase):
             kept_np = np.delete(np.arange(hot_len, dtype=np.int64), d_np)
             hp = self._hot_positions.numpy()
             demote_positions = torch.from_numpy(hp[d_np])
-            idx_dev, kept_dev = None, None
-            if self._hot_keys.device.type == "cuda":  # demote and keep indices in one host-to-device copy
-                both = _to_device(torch.from_numpy(np.concatenate([d_np, kept_np])), self._hot_keys.device)
-                idx_dev, kept_dev = both[:n_demote], both[n_demote:]
-            self._demote(demote_idx, idx_dev)
+            idx_dev, kept_dev, pos_dev = None, None, None
+            if self._hot_keys.device.type == "cuda":  # demote / keep indices and positions in one copy
+                both = _to_device(torch.from_numpy(np.concatenate([d_np, kept_np, hp[d_np]])),
+                                  self._hot_keys.device)
+                idx_dev, kept_dev = both[:n_demote], both[n_demote:hot_len]
+                pos_dev = both[hot_len:]
+            self._demote(demote_idx, idx_dev, pos_dev)
             self._append_1d("_warm_positions", demote_positions)
             self._warm_len += n_demote
             if self._proxy_score is not None:
@@ -416,7 +437,7 @@ class AKVLayer(_LayerBase):
             if self._importance is not None:
                 self._importance = torch.from_numpy(self._importance.numpy()[kept_np])
 
-        if self.fused_decode and N == 1 and self._warm is not None:
+        if self.fused_decode and self._warm is not None:
             return self._publish(*self._placeholder())
         return self._publish(*self.full_view())
 
@@ -444,6 +465,25 @@ class AKVLayer(_LayerBase):
         v = self._nan.expand(B, H, n, D)
         k._akv_layer = self
         return k, v
+
+    def can_prefill_fused(self) -> bool:
+        """Prefill attention can read this layer's tiers in place (one bit
+        width for every head, and a position recorded for every warm slot)."""
+        return (self._warm is not None and not isinstance(self._warm, HeadGroupArena)
+                and self._slot_pos is not None and self._hot_keys is not None)
+
+    def prefill_attention(self, query: torch.Tensor, sm_scale: Optional[float] = None) -> torch.Tensor:
+        """The newest q_len tokens' queries (B, Hq, q_len, D), causal by
+        position over the packed warm records and the FP16 hot tier in place
+        (akv_prefill_attention) -- the SDPA over the chronological view of the
+        reference's prefill (drop_in.py:753-787).  Returns (B, Hq, q_len, D)."""
+        from .fused_attention import prefill_attention
+        M = query.shape[2]
+        dev = query.device
+        q_pos = torch.arange(self._total_len - M, self._total_len, dtype=torch.int32, device=dev)
+        hot_pos = _to_device(self._hot_positions.to(torch.int32), dev)
+        return prefill_attention(query, q_pos, self._hot_keys, self._hot_values, hot_pos, self._warm,
+                                 self._slot_pos[: self._warm.n_blocks * BLOCK], sm_scale=sm_scale)
 
     def decode_attention(self, query: torch.Tensor, sm_scale: Optional[float] = None) -> torch.Tensor:
         """One decode query (B, Hq, 1, D) over the packed warm records and the

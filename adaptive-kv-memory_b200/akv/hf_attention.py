@@ -1,4 +1,4 @@
-"""HuggingFace attention hook: decode steps attend over the packed warm tier.
+"""HuggingFace attention hook: decode and prefill attend over the packed warm tier.
 
 The reference's ``AKVLayer.update`` returns the chronologically sorted
 [dequantised warm; hot] FP16 view and the model's attention runs over it
@@ -9,9 +9,12 @@ builder under the same name).  With ``AKVCache(fused_decode=True)``:
 * a decode step (one query token, no padding mask, no sliding window) calls
   the sm_100a mixed-tier decode kernel on the layer's packed warm block
   records and FP16 hot tier in place; no FP16 view is built or read;
-* everything else (prefill, chunked prefill, padded batches, layers without
-  a warm tier, caches that are not fused) goes to torch's SDPA over the view,
-  as the reference does.
+* a prefill with no padding mask (HF passes none for a plain causal prompt)
+  calls the tcgen05 prefill kernel on the same tiers, causal by token
+  position;
+* everything else (masked or padded batches, sliding windows, per-head bit
+  widths at prefill, layers without a warm tier, caches that are not fused)
+  goes to torch's SDPA over the view, as the reference does.
 
 Softmax attention of a single query does not depend on the order of the
 keys, so attending over [warm records; hot] equals attending over the
@@ -45,9 +48,13 @@ def akv_attention_forward(module: torch.nn.Module, query: torch.Tensor, key: tor
 
     layer = getattr(key, "_akv_layer", None)
     if layer is not None:
-        if (query.shape[2] == 1 and attention_mask is None and not dropout
-                and kwargs.get("sliding_window") is None and query.shape[-1] == KERNEL_HEAD_DIM):
+        plain = (attention_mask is None and not dropout and kwargs.get("sliding_window") is None
+                 and query.shape[-1] == KERNEL_HEAD_DIM)
+        if plain and query.shape[2] == 1:
             out = layer.decode_attention(query, scaling)  # (B, Hq, 1, D)
+            return out.transpose(1, 2), None
+        if plain and is_causal is not False and layer.can_prefill_fused():
+            out = layer.prefill_attention(query, scaling)  # (B, Hq, q_len, D), causal by position
             return out.transpose(1, 2), None
         key, value = layer.full_view()
     return sdpa_attention_forward(module, query, key, value, attention_mask, dropout=dropout, scaling=scaling,

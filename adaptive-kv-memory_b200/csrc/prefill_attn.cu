@@ -170,6 +170,15 @@ AKV_DEV void tmem_st32u(uint32_t taddr, const uint32_t (&v)[32]) {
       : "memory");
 }
 
+AKV_DEV void tmem_st16u(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+
 AKV_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 AKV_DEV void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -187,103 +196,214 @@ AKV_DEV uint32_t tile_off(int r, int c) {
   return static_cast<uint32_t>((r & 7) * 16 + (r >> 3) * 128 + (c >> 3) * 2048 + (c & 7) * 2);
 }
 
-// ------------------------------------------------------------------ warm tile dequantisation
-// Thread t dequantises token t of the tile (record t / 32, slot t % 32) into
-// row t of the K and V tiles, exactly like the reference: for each channel
-// pair fp16(fp16(c * s) + z) with both roundings (__hmul2_rn, __hadd2_rn).
-// K scales / zeros come per channel (staged in natural channel order in
-// kscale / kzero by the record's warp), V scale / zero per token.  Invalid
-// slots (mask bit clear, or beyond the written records) get zero rows, so
-// their (zero) softmax weight never meets a non-finite value.
+// ------------------------------------------------------------------ warm tile rows
+// Thread t handles token t of a warm tile (record t / 32, slot t % 32).  Its
+// packed K and V code rows, its V scale / zero and its outlier originals are
+// fetched into registers one visible tile ahead (16-byte loads, all in flight
+// together); lane l of the record's warp also fetches bytes 8l..8l+7 of the
+// record's K scales and zeros (stored in the decode pair order).  So the
+// global-memory latency of the next tile hides behind the tensor-core work and
+// the softmax of the current one.
+constexpr int kPrefetchOut = 2;  // outlier channels kept in registers (more: read at dequantisation)
+
 template <int KB, int VB>
-AKV_DEV void dequant_row(const uint8_t* rec, const akv_warm_layout& L, int slot, bool valid, const __half* ks,
-                         const __half* kz, unsigned char* ktile, unsigned char* vtile, int t) {
-  constexpr int kp = kD * KB / 8, vp = kD * VB / 8;
-  const uint8_t* kc = rec + L.kc + slot * kp;
-  const uint8_t* vc = rec + L.vc + slot * vp;
-  const __half vs = valid ? *reinterpret_cast<const __half*>(rec + L.vs + 2 * slot) : __float2half_rn(0.f);
-  const __half vz = valid ? *reinterpret_cast<const __half*>(rec + L.vz + 2 * slot) : __float2half_rn(0.f);
-  const __half2 vs2 = __halves2half2(vs, vs), vz2 = __halves2half2(vz, vz);
-  const int n_out = L.n_outlier;
-#pragma unroll 1
-  for (int cb = 0; cb < kD / 8; ++cb) {  // 8 channels per 16-byte column block
-    uint32_t kw[KB], vw[VB];             // the block's codes: 8*KB bits of K, 8*VB bits of V
-    uint32_t kcodes[8], vcodes[8];
-    if (valid) {
-      // 8 codes of KB bits = KB bytes starting at byte cb*KB (byte-aligned for any KB)
+struct WarmRow {
+  uint4 k[KB];          // K codes: 128 * KB / 8 bytes
+  uint4 v[VB];          // V codes
+  uint2 ks2, kz2;       // this lane's K scale / zero pair words 2l, 2l+1 of its record
+  uint2 ids;            // outlier ids: K at bytes 2j, V at bytes 2n + 2j (n <= 2)
+  uint32_t vsz;         // V scale (low half) and zero (high half) of this token
+  __half ko[kPrefetchOut], vo[kPrefetchOut];
+  const uint8_t* rec;   // nullptr: beyond the written blocks
+  int kp;               // the token's position (INT_MAX: empty slot)
+  bool valid;           // slot holds a token (mask bit set)
+};
+
+template <int KB, int VB>
+AKV_DEV void load_warm_row(const Params& p, int b, int kvh, int tile, int t, WarmRow<KB, VB>& w) {
+  const int blk = tile * 4 + (t >> 5), slot = t & 31;
+  w.valid = false;
+  w.rec = nullptr;
+  w.kp = INT_MAX;
+  if (blk >= p.n_warm_blocks) return;
+  const uint8_t* rec = p.warm + b * p.w_sb + kvh * p.w_sh + static_cast<int64_t>(blk) * p.L.bytes;
+  w.rec = rec;
+  const int n = p.L.n_outlier;
+  w.ks2 = __ldg(reinterpret_cast<const uint2*>(rec + p.L.ks) + slot);
+  w.kz2 = __ldg(reinterpret_cast<const uint2*>(rec + p.L.kz) + slot);
+  w.ids = n > 0 ? __ldg(reinterpret_cast<const uint2*>(rec + p.L.ki)) : make_uint2(0u, 0u);
+  const uint32_t mask = __ldg(reinterpret_cast<const uint32_t*>(rec + p.L.mask));
+  w.valid = (mask >> slot) & 1u;
+  const int kp = __ldg(p.warm_pos + b * p.wp_sb + blk * 32 + slot);
+  w.kp = w.valid ? kp : INT_MAX;
+  const uint4* kr = reinterpret_cast<const uint4*>(rec + p.L.kc + slot * (kD * KB / 8));
+  const uint4* vr = reinterpret_cast<const uint4*>(rec + p.L.vc + slot * (kD * VB / 8));
 #pragma unroll
-      for (int i = 0; i < KB; ++i) kw[i] = kc[cb * KB + i];
+  for (int i = 0; i < KB; ++i) w.k[i] = __ldg(kr + i);
 #pragma unroll
-      for (int i = 0; i < VB; ++i) vw[i] = vc[cb * VB + i];
-      if constexpr (KB == 4) {
+  for (int i = 0; i < VB; ++i) w.v[i] = __ldg(vr + i);
+  w.vsz = static_cast<uint32_t>(__half_as_ushort(__ldg(reinterpret_cast<const __half*>(rec + p.L.vs) + slot))) |
+          (static_cast<uint32_t>(__half_as_ushort(__ldg(reinterpret_cast<const __half*>(rec + p.L.vz) + slot))) << 16);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          kcodes[2 * i] = kw[i] >> 4;
-          kcodes[2 * i + 1] = kw[i] & 15u;
-        }
-      } else if constexpr (KB == 2) {
-#pragma unroll
-        for (int i = 0; i < 2; ++i)
-#pragma unroll
-          for (int j = 0; j < 4; ++j) kcodes[4 * i + j] = (kw[i] >> (6 - 2 * j)) & 3u;
-      } else {
-        const uint32_t w = (kw[0] << 16) | (kw[1] << 8) | kw[2];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) kcodes[j] = (w >> (21 - 3 * j)) & 7u;
-      }
-      if constexpr (VB == 4) {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          vcodes[2 * i] = vw[i] >> 4;
-          vcodes[2 * i + 1] = vw[i] & 15u;
-        }
-      } else if constexpr (VB == 2) {
-#pragma unroll
-        for (int i = 0; i < 2; ++i)
-#pragma unroll
-          for (int j = 0; j < 4; ++j) vcodes[4 * i + j] = (vw[i] >> (6 - 2 * j)) & 3u;
-      } else {
-        const uint32_t w = (vw[0] << 16) | (vw[1] << 8) | vw[2];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) vcodes[j] = (w >> (21 - 3 * j)) & 7u;
-      }
-    }
-    __align__(16) __half2 ko[4], vo[4];
-    const uint4 s4 = *reinterpret_cast<const uint4*>(ks + cb * 8);
-    const uint4 z4 = *reinterpret_cast<const uint4*>(kz + cb * 8);
-    const __half2* s2 = reinterpret_cast<const __half2*>(&s4);
-    const __half2* z2 = reinterpret_cast<const __half2*>(&z4);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      if (valid) {
-        const __half2 ck = __halves2half2(__uint2half_rn(kcodes[2 * i]), __uint2half_rn(kcodes[2 * i + 1]));
-        const __half2 cv = __halves2half2(__uint2half_rn(vcodes[2 * i]), __uint2half_rn(vcodes[2 * i + 1]));
-        ko[i] = __hadd2_rn(__hmul2_rn(ck, s2[i]), z2[i]);
-        vo[i] = __hadd2_rn(__hmul2_rn(cv, vs2), vz2);
-      } else {
-        ko[i] = vo[i] = __float2half2_rn(0.f);
-      }
-    }
-    if (valid && n_out > 0) {  // outlier channels: the fp16 originals replace the dequantised values
-      const int16_t* kid = reinterpret_cast<const int16_t*>(rec + L.ki);
-      const int16_t* vid = reinterpret_cast<const int16_t*>(rec + L.vi);
-      const __half* kov = reinterpret_cast<const __half*>(rec + L.ko) + slot * n_out;
-      const __half* vov = reinterpret_cast<const __half*>(rec + L.vo) + slot * n_out;
-      __half* kh = reinterpret_cast<__half*>(ko);
-      __half* vh = reinterpret_cast<__half*>(vo);
-      for (int j = 0; j < n_out; ++j) {
-        const int kch = kid[j] - cb * 8, vch = vid[j] - cb * 8;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          if (kch == e) kh[e] = kov[j];
-          if (vch == e) vh[e] = vov[j];
-        }
-      }
-    }
-    *reinterpret_cast<uint4*>(ktile + tile_off(t, cb * 8)) = *reinterpret_cast<const uint4*>(ko);
-    *reinterpret_cast<uint4*>(vtile + tile_off(t, cb * 8)) = *reinterpret_cast<const uint4*>(vo);
+  for (int j = 0; j < kPrefetchOut; ++j) {
+    w.ko[j] = j < n ? __ldg(reinterpret_cast<const __half*>(rec + p.L.ko) + slot * n + j) : __float2half_rn(0.f);
+    w.vo[j] = j < n ? __ldg(reinterpret_cast<const __half*>(rec + p.L.vo) + slot * n + j) : __float2half_rn(0.f);
   }
 }
+
+// K scales / zeros of this warp's record in natural channel order: pair word
+// wi holds channels key_pair(KB, wi % 16) of 32-channel chunk wi / 16.
+template <int KB, int VB>
+AKV_DEV void stage_kscale(const WarmRow<KB, VB>& w, int lane, __half* ks, __half* kz) {
+  const uint32_t sw[2] = {w.ks2.x, w.ks2.y}, zw[2] = {w.kz2.x, w.kz2.y};
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int wi = 2 * lane + j;
+    const PairIdx pi = key_pair(KB, wi & 15);
+    const int c0 = 32 * (wi >> 4);
+    const bool have = w.rec != nullptr;
+    ks[c0 + pi.a] = __ushort_as_half(have ? static_cast<unsigned short>(sw[j] & 0xFFFFu) : 0);
+    ks[c0 + pi.b] = __ushort_as_half(have ? static_cast<unsigned short>(sw[j] >> 16) : 0);
+    kz[c0 + pi.a] = __ushort_as_half(have ? static_cast<unsigned short>(zw[j] & 0xFFFFu) : 0);
+    kz[c0 + pi.b] = __ushort_as_half(have ? static_cast<unsigned short>(zw[j] >> 16) : 0);
+  }
+}
+
+// code of channel C in a packed row held as 32-bit words (akv/bitpack.py
+// layouts: 4 bits even channel in the high nibble, 2 bits MSB first, 3 bits
+// 24-bit big-endian groups); C is a template argument, so every shift and
+// word index is a constant
+template <int BITS, int C, int NW>
+AKV_DEV uint32_t code_of(const uint32_t (&w)[NW]) {
+  if constexpr (BITS == 4) {
+    constexpr int by = C >> 1;
+    return (w[by >> 2] >> (8 * (by & 3) + ((C & 1) ? 0 : 4))) & 15u;
+  } else if constexpr (BITS == 2) {
+    constexpr int by = C >> 2;
+    return (w[by >> 2] >> (8 * (by & 3) + 6 - 2 * (C & 3))) & 3u;
+  } else {
+    constexpr int b0 = 3 * (C >> 3);       // bytes b0..b0+2 form a big-endian 24-bit word
+    constexpr int bit = 21 - 3 * (C & 7);  // code j of the group at bits 21-3j .. 23-3j
+    const uint32_t w24 = (((w[b0 >> 2] >> (8 * (b0 & 3))) & 0xFFu) << 16) |
+                         (((w[(b0 + 1) >> 2] >> (8 * ((b0 + 1) & 3))) & 0xFFu) << 8) |
+                         ((w[(b0 + 2) >> 2] >> (8 * ((b0 + 2) & 3))) & 0xFFu);
+    return (w24 >> bit) & 7u;
+  }
+}
+
+// channels (C, C+1) (C even) as exact fp16 codes.  4 and 2 bits: the byte
+// holding both codes is copied into both 16-bit halves (PRMT), one LOP3 keeps
+// each half's code bits in place and ORs in the exponent of 1024, giving
+// (1024 + M0*c0, 1024 + M1*c1) with power-of-two M, and one HFMA2
+// x * (1/M0, 1/M1) - (1024/M0, 1024/M1) gives (c0, c1) exactly.  3 bits:
+// the codes are extracted and (1024 + code) - 1024 is formed directly.
+template <int BITS, int C, int NW>
+AKV_DEV __half2 code_pair_h2(const uint32_t (&w)[NW]) {
+  if constexpr (BITS == 4 || BITS == 2) {
+    constexpr int by = BITS == 4 ? C >> 1 : C >> 2;  // byte of the row holding channels C and C+1
+    constexpr uint32_t k = by & 3;
+    const uint32_t y = prmt(w[by >> 2], 0u, k | (4u << 4) | (k << 8) | (4u << 12));  // (byte, byte)
+    // code masks in the byte (even channel first) and their multipliers
+    constexpr uint32_t m0 = BITS == 4 ? 0xF0u : ((C & 2) ? 0x0Cu : 0xC0u);
+    constexpr uint32_t m1 = BITS == 4 ? 0x0Fu : ((C & 2) ? 0x03u : 0x30u);
+    constexpr int e0 = BITS == 4 ? 4 : ((C & 2) ? 2 : 6), e1 = BITS == 4 ? 0 : ((C & 2) ? 0 : 4);
+    uint32_t x;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(x) : "r"(y), "n"(m0 | (m1 << 16)), "n"(0x64006400u));
+    constexpr uint32_t inv = fp16_pow2_bits(-e0, false) | (fp16_pow2_bits(-e1, false) << 16);
+    constexpr uint32_t off = fp16_pow2_bits(10 - e0, true) | (fp16_pow2_bits(10 - e1, true) << 16);
+    uint32_t r;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(x), "r"(inv), "r"(off));
+    return u32_as_h2(r);
+  } else {
+    const uint32_t u = code_of<BITS, C>(w) | (code_of<BITS, C + 1>(w) << 16) | 0x64006400u;
+    return __hsub2(u32_as_h2(u), u32_as_h2(0x64006400u));
+  }
+}
+
+// one 8-channel column block CB of the K row (per-channel scale / zero) or
+// of the V row (per-token scale / zero), exactly dequantised
+template <int BITS, bool IS_KEY, int CB, int NW>
+AKV_DEV void dq_block(const uint32_t (&w)[NW], const __half* ks, const __half* kz, __half2 vs2, __half2 vz2,
+                      bool valid, unsigned char* tile, int t) {
+  if constexpr (CB < kD / 8) {
+    uint4 o = make_uint4(0u, 0u, 0u, 0u);
+    if (valid) {
+      __half2 s[4], z[4];
+      if constexpr (IS_KEY) {
+        const uint4 s4 = *reinterpret_cast<const uint4*>(ks + CB * 8);
+        const uint4 z4 = *reinterpret_cast<const uint4*>(kz + CB * 8);
+        s[0] = u32_as_h2(s4.x), s[1] = u32_as_h2(s4.y), s[2] = u32_as_h2(s4.z), s[3] = u32_as_h2(s4.w);
+        z[0] = u32_as_h2(z4.x), z[1] = u32_as_h2(z4.y), z[2] = u32_as_h2(z4.z), z[3] = u32_as_h2(z4.w);
+      } else {
+        s[0] = s[1] = s[2] = s[3] = vs2;
+        z[0] = z[1] = z[2] = z[3] = vz2;
+      }
+      o.x = h2_as_u32(__hadd2_rn(__hmul2_rn(code_pair_h2<BITS, 8 * CB>(w), s[0]), z[0]));
+      o.y = h2_as_u32(__hadd2_rn(__hmul2_rn(code_pair_h2<BITS, 8 * CB + 2>(w), s[1]), z[1]));
+      o.z = h2_as_u32(__hadd2_rn(__hmul2_rn(code_pair_h2<BITS, 8 * CB + 4>(w), s[2]), z[2]));
+      o.w = h2_as_u32(__hadd2_rn(__hmul2_rn(code_pair_h2<BITS, 8 * CB + 6>(w), s[3]), z[3]));
+    }
+    *reinterpret_cast<uint4*>(tile + tile_off(t, CB * 8)) = o;
+    dq_block<BITS, IS_KEY, CB + 1>(w, ks, kz, vs2, vz2, valid, tile, t);
+  }
+}
+
+// Row t of the K (IS_KEY) or V tile from the prefetched registers, exactly
+// like the reference: fp16(fp16(code * scale) + zero) per element
+// (__hmul2_rn then __hadd2_rn), outlier channels then overwritten with their
+// fp16 originals.  Invalid slots get zero rows (their softmax weight is 0
+// and must not meet a non-finite value).
+template <int KB, int VB, bool IS_KEY>
+AKV_DEV void dequant_row(const WarmRow<KB, VB>& w, const Params& p, const __half* ks, const __half* kz,
+                         unsigned char* tile, int t) {
+  constexpr int BITS = IS_KEY ? KB : VB;
+  uint32_t cw[4 * BITS];
+#pragma unroll
+  for (int i = 0; i < BITS; ++i) {
+    const uint4 q = IS_KEY ? w.k[i] : w.v[i < VB ? i : 0];
+    cw[4 * i] = q.x;
+    cw[4 * i + 1] = q.y;
+    cw[4 * i + 2] = q.z;
+    cw[4 * i + 3] = q.w;
+  }
+  const __half2 vs2 = u32_as_h2((w.vsz & 0xFFFFu) * 0x10001u), vz2 = u32_as_h2((w.vsz >> 16) * 0x10001u);
+  dq_block<BITS, IS_KEY, 0>(cw, ks, kz, vs2, vz2, w.valid, tile, t);
+  const int n = p.L.n_outlier;
+  if (w.valid && n > 0) {  // outlier channels: the fp16 originals replace the dequantised values
+    const int slot = t & 31;
+    for (int j = 0; j < n; ++j) {
+      int ch;
+      __half val;
+      if (n <= kPrefetchOut) {  // ids: K at 16-bit word j, V at word n + j of the 8 prefetched bytes
+        const int q = IS_KEY ? j : n + j;
+        const uint32_t wd = q < 2 ? w.ids.x : w.ids.y;
+        ch = static_cast<int16_t>((wd >> (16 * (q & 1))) & 0xFFFFu);
+        val = IS_KEY ? (j == 0 ? w.ko[0] : w.ko[1]) : (j == 0 ? w.vo[0] : w.vo[1]);
+      } else {
+        ch = reinterpret_cast<const int16_t*>(w.rec + (IS_KEY ? p.L.ki : p.L.vi))[j];
+        val = reinterpret_cast<const __half*>(w.rec + (IS_KEY ? p.L.ko : p.L.vo))[slot * n + j];
+      }
+      *reinterpret_cast<__half*>(tile + tile_off(t, ch)) = val;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ tile visibility
+// Key position of thread t's key in tile `tile` (INT_MAX: no key there, or
+// an empty warm slot).
+AKV_DEV int key_pos(const Params& p, int b, int kvh, int n_wtiles, int tile, int t) {
+  if (tile < n_wtiles) {
+    const int blk = tile * 4 + (t >> 5), slot = t & 31;
+    if (blk >= p.n_warm_blocks) return INT_MAX;
+    const uint8_t* rec = p.warm + b * p.w_sb + kvh * p.w_sh + static_cast<int64_t>(blk) * p.L.bytes;
+    const uint32_t mask = __ldg(reinterpret_cast<const uint32_t*>(rec + p.L.mask));
+    return ((mask >> slot) & 1u) ? __ldg(p.warm_pos + b * p.wp_sb + blk * 32 + slot) : INT_MAX;
+  }
+  const int j = (tile - n_wtiles) * kTile + t;
+  return j < p.n_hot ? __ldg(p.hot_pos + b * p.hp_sb + j) : INT_MAX;
+}
+
+constexpr int kScanTiles = 32;  // tiles whose visibility one scan step decides
 
 // ------------------------------------------------------------------ the kernel
 struct Maps {
@@ -297,11 +417,13 @@ __global__ void __launch_bounds__(kThreads, 2) prefill_kernel(const Params p, co
   unsigned char* ktile = smem + kTileBytes;       // K
   unsigned char* vtile = smem + 2 * kTileBytes;   // V
   unsigned char* aux = smem + 3 * kTileBytes;
-  __half* kscale = reinterpret_cast<__half*>(aux);         // [4][128] natural channel order
-  __half* kzero = kscale + 4 * kD;                          // [4][128]
+  __half* kscale = reinterpret_cast<__half*>(aux);             // [4][128] natural channel order
+  __half* kzero = kscale + 4 * kD;                              // [4][128]
   int32_t* kpos = reinterpret_cast<int32_t*>(kzero + 4 * kD);  // [128] key positions (INT_MAX: invisible)
   uint64_t* bars = reinterpret_cast<uint64_t*>(kpos + kTile);  // load, s, o
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4);
+  __shared__ uint32_t s_vis, s_notfull;  // the current scan window: bit j = tile c0 + j visible / not fully visible
+  __shared__ int s_qmax[4], s_qmin[4];
 
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const int m0 = blockIdx.x * kTile;
@@ -324,32 +446,33 @@ __global__ void __launch_bounds__(kThreads, 2) prefill_kernel(const Params p, co
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
+  const int mrow = m0 + t;
+  const bool row_ok = mrow < p.M;
+  const int qpos = row_ok ? __ldg(p.q_pos + b * p.qp_sb + mrow) : INT_MIN;
+  {
+    const int qmx = __reduce_max_sync(0xffffffffu, qpos);
+    const int qmn = __reduce_min_sync(0xffffffffu, row_ok ? qpos : INT_MAX);
+    if (lane == 0) {
+      s_qmax[warp] = qmx;
+      s_qmin[warp] = qmn;
+    }
+  }
+  // ---- Q tile: 16 column blocks by tensor TMA (rows beyond M read as zeros)
+  if (t == 0) {
+    mbar_arrive_expect_tx(bar_load, kTileBytes);
+    for (int cb = 0; cb < kD / 8; ++cb) tma_load_4d(qtile + cb * 2048, &maps.q, cb * 8, m0, h, b, bar_load);
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t tS = tmem, tO = tmem + kTile;
   const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;  // this warp's TMEM lanes
-
-  const int mrow = m0 + t;
-  const bool row_ok = mrow < p.M;
-  const int qpos = row_ok ? p.q_pos[b * p.qp_sb + mrow] : INT_MIN;
-  int qmax = qpos;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) qmax = max(qmax, __shfl_xor_sync(0xffffffffu, qmax, o));
-  __shared__ int s_qmax[4];
-  if (lane == 0) s_qmax[warp] = qmax;
+  const int cta_qmax = max(max(s_qmax[0], s_qmax[1]), max(s_qmax[2], s_qmax[3]));
+  const int cta_qmin = min(min(s_qmin[0], s_qmin[1]), min(s_qmin[2], s_qmin[3]));
 
   uint32_t ph_load = 0, ph_s = 0, ph_o = 0;
   bool ok = true;  // no bounded wait has run out
-
-  // ---- Q tile: 16 column blocks by tensor TMA (rows beyond M read as zeros)
-  if (t == 0) {
-    mbar_arrive_expect_tx(bar_load, kTileBytes);
-    for (int cb = 0; cb < kD / 8; ++cb) tma_load_4d(qtile + cb * 2048, &maps.q, cb * 8, m0, h, b, bar_load);
-  }
-  __syncthreads();
-  const int cta_qmax = max(max(s_qmax[0], s_qmax[1]), max(s_qmax[2], s_qmax[3]));
   if (!mbar_wait(bar_load, ph_load, p.status)) {
     mbar_wait(bar_load, ph_load, p.status);
     ok = false;
@@ -361,40 +484,67 @@ __global__ void __launch_bounds__(kThreads, 2) prefill_kernel(const Params p, co
   const uint32_t idesc_o = instr_desc(kTile, kD, 1);     // O = P V:   B (= V) MN-major
   const uint32_t q_addr = smem_u32(qtile), k_addr = smem_u32(ktile), v_addr = smem_u32(vtile);
 
+  const int n_wtiles = (p.n_warm_blocks + 3) / 4;
+  const int n_tiles = n_wtiles + (p.n_hot + kTile - 1) / kTile;
+
+  // visibility of tiles [c0, c0 + 32): one scan step reads every key position
+  // of the window (32 loads per thread in flight) and ORs the per-tile flags
+  int win = -1;
+  auto scan = [&](int c0) {
+    if (t == 0) s_vis = s_notfull = 0u;
+    __syncthreads();
+    int kp[kScanTiles];
+#pragma unroll
+    for (int j = 0; j < kScanTiles; ++j) kp[j] = c0 + j < n_tiles ? key_pos(p, b, kvh, n_wtiles, c0 + j, t) : INT_MAX;
+    uint32_t vis = 0u, nf = 0u;
+#pragma unroll
+    for (int j = 0; j < kScanTiles; ++j) {
+      vis |= static_cast<uint32_t>(kp[j] <= cta_qmax) << j;
+      nf |= static_cast<uint32_t>(kp[j] > cta_qmin) << j;
+    }
+    vis = __reduce_or_sync(0xffffffffu, vis);
+    nf = __reduce_or_sync(0xffffffffu, nf);
+    if (lane == 0) {
+      atomicOr(&s_vis, vis);
+      atomicOr(&s_notfull, nf);
+    }
+    __syncthreads();
+    win = c0;
+  };
+  // first visible tile at or after `from` (n_tiles: none); uniform over the CTA
+  auto next_visible = [&](int from) {
+    while (from < n_tiles) {
+      const int c0 = from - from % kScanTiles;
+      if (win != c0) scan(c0);
+      const uint32_t bits = s_vis >> (from - c0);
+      if (bits) return from + __ffs(bits) - 1;
+      from = c0 + kScanTiles;
+    }
+    return n_tiles;
+  };
+
   float m_run = -INFINITY;  // running max of this row's scaled logits (log2 units)
   float l_run = 0.f;        // running sum of 2^(s - m_run)
   bool o_live = false;      // O holds accumulated values (a P.V has been issued)
-  bool pv_pending = false;  // a P.V MMA may still read the K/P and V tiles
+  bool pv_pending = false;  // a P.V MMA may still read the V tile and the P columns
 
-  const int n_wtiles = (p.n_warm_blocks + 3) / 4;
-  const int n_htiles = (p.n_hot + kTile - 1) / kTile;
-  const int rec = p.L.bytes;
-  for (int tile = 0; tile < n_wtiles + n_htiles && ok; ++tile) {
-    const bool warm_tile = tile < n_wtiles;
-    // -- key positions of the tile (INT_MAX: no such key / invalid slot)
-    int kp_t = INT_MAX;
-    bool valid = false;
-    const uint8_t* recp = nullptr;
-    int slot = t & 31;
+  WarmRow<KB, VB> wr;
+  int cur = next_visible(0);
+  if (cur < n_wtiles) load_warm_row<KB, VB>(p, b, kvh, cur, t, wr);
+  while (cur < n_tiles && ok) {
+    const bool warm_tile = cur < n_wtiles;
+    const bool full = !((s_notfull >> (cur - win)) & 1u);  // every key valid and visible to every row
+    const int nxt = next_visible(cur + 1);                  // (may rescan: uniform)
+
+    // -- the previous tile's P.V reads V and the P columns; S of the previous
+    // tile is complete, so a warm tile's K rows are dequantised first, while
+    // that P.V may still run
     if (warm_tile) {
-      const int blk = tile * 4 + (t >> 5);
-      if (blk < p.n_warm_blocks) {
-        recp = p.warm + b * p.w_sb + kvh * p.w_sh + static_cast<int64_t>(blk) * rec;
-        const uint32_t mask = *reinterpret_cast<const uint32_t*>(recp + p.L.mask);
-        valid = (mask >> slot) & 1u;
-        if (valid) kp_t = p.warm_pos[b * p.wp_sb + blk * 32 + slot];
-      }
-    } else {
-      const int j = (tile - n_wtiles) * kTile + t;
-      if (j < p.n_hot) {
-        valid = true;
-        kp_t = p.hot_pos[b * p.hp_sb + j];
-      }
+      kpos[t] = wr.kp;
+      stage_kscale<KB, VB>(wr, lane, kscale + warp * kD, kzero + warp * kD);
+      __syncwarp();
+      dequant_row<KB, VB, true>(wr, p, kscale + warp * kD, kzero + warp * kD, ktile, t);
     }
-    // skip a tile no query row of this CTA can see
-    if (!__syncthreads_or(valid && kp_t <= cta_qmax)) continue;
-
-    // -- the previous tile's P.V must be done before K/P and V are overwritten
     if (pv_pending) {
       if (!mbar_wait(bar_o, ph_o, p.status)) {
         mbar_wait(bar_o, ph_o, p.status);
@@ -405,28 +555,15 @@ __global__ void __launch_bounds__(kThreads, 2) prefill_kernel(const Params p, co
       tc_fence_after();
     }
     if (__syncthreads_or(!ok)) break;
-    kpos[t] = kp_t;
 
     if (warm_tile) {
-      // stage the K scales / zeros of this warp's record in natural channel order
-      if (recp) {
-        const __half* ks = reinterpret_cast<const __half*>(recp + p.L.ks);
-        const __half* kz = reinterpret_cast<const __half*>(recp + p.L.kz);
-        for (int c = lane; c < kD; c += 32) {
-          const int s = (c & ~31) + key_pair_slot(KB, c & 31);
-          kscale[warp * kD + c] = ks[s];
-          kzero[warp * kD + c] = kz[s];
-        }
-      } else {
-        for (int c = lane; c < kD; c += 32) kscale[warp * kD + c] = kzero[warp * kD + c] = __float2half_rn(0.f);
-      }
-      __syncwarp();
-      dequant_row<KB, VB>(recp ? recp : p.warm, p.L, slot, valid && recp, kscale + warp * kD, kzero + warp * kD,
-                          ktile, vtile, t);
+      dequant_row<KB, VB, false>(wr, p, nullptr, nullptr, vtile, t);
       fence_proxy_async_shared();  // generic-proxy tile writes -> visible to the tensor cores
+      if (nxt < n_wtiles) load_warm_row<KB, VB>(p, b, kvh, nxt, t, wr);  // next tile's rows in flight
     } else {
+      kpos[t] = key_pos(p, b, kvh, n_wtiles, cur, t);
       if (t == 0) {
-        const int j0 = (tile - n_wtiles) * kTile;
+        const int j0 = (cur - n_wtiles) * kTile;
         mbar_arrive_expect_tx(bar_load, 2 * kTileBytes);
         for (int cb = 0; cb < kD / 8; ++cb) {
           tma_load_4d(ktile + cb * 2048, &maps.hk, cb * 8, j0, kvh, b, bar_load);
@@ -461,20 +598,30 @@ __global__ void __launch_bounds__(kThreads, 2) prefill_kernel(const Params p, co
     tc_fence_after();
     if (__syncthreads_or(!ok)) break;
 
-    // -- softmax over this row's 128 logits
-    float s[4][32];
-#pragma unroll
-    for (int c = 0; c < 4; ++c) tmem_ld32(tS + lane_base + c * 32, s[c]);
-    tmem_wait_ld();
+    // -- softmax, pass 1: this row's max over the tile (S read 32 columns at a time)
+    const float sl2 = p.scale_log2;
     float mx = -INFINITY;
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      float sv[32];
+      tmem_ld32(tS + lane_base + c * 32, sv);
+      tmem_wait_ld();
+      if (full) {
 #pragma unroll
-    for (int c = 0; c < 4; ++c)
+        for (int i = 0; i < 32; ++i) mx = fmaxf(mx, sv[i]);
+      } else {
+        const int4* kp4 = reinterpret_cast<const int4*>(kpos + c * 32);
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const bool vis = kpos[c * 32 + i] <= qpos;
-        s[c][i] = vis ? s[c][i] * p.scale_log2 : -INFINITY;
-        mx = fmaxf(mx, s[c][i]);
+        for (int i = 0; i < 8; ++i) {
+          const int4 k4 = kp4[i];
+          mx = fmaxf(mx, k4.x <= qpos ? sv[4 * i] : -INFINITY);
+          mx = fmaxf(mx, k4.y <= qpos ? sv[4 * i + 1] : -INFINITY);
+          mx = fmaxf(mx, k4.z <= qpos ? sv[4 * i + 2] : -INFINITY);
+          mx = fmaxf(mx, k4.w <= qpos ? sv[4 * i + 3] : -INFINITY);
+        }
       }
+    }
+    mx = mx * sl2;  // scale_log2 > 0: the max of the scaled logits
     const bool move = mx > m_run + kLazy;
     float alpha = 1.f;
     if (move) {
@@ -494,26 +641,36 @@ __global__ void __launch_bounds__(kThreads, 2) prefill_kernel(const Params p, co
       }
       tmem_wait_st();
     }
-    // P = 2^(s - m) as an exact-to-2^-22 pair of fp16 terms, hi = fp16(P) and
-    // lo = fp16(P - hi), written over this row's S columns of tensor memory
-    // (hi: keys 2c, 2c+1 in column c; lo: in column 64 + c), so P.V runs as
-    // two MMAs with A read from tensor memory
+    // -- pass 2: P = 2^(s - m) as an exact-to-2^-22 pair of fp16 terms, hi =
+    // fp16(P) and lo = fp16(P - hi), written over the S columns just read:
+    // keys 32c .. 32c+31 -> hi in columns 32c .. 32c+15, lo in 32c+16 .. 32c+31
+    // (two keys per column), so P.V runs as two MMAs with A in tensor memory
     const float mb = (m_run == -INFINITY) ? 0.f : m_run;
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      float sv[32];
+      tmem_ld32(tS + lane_base + c * 32, sv);
+      tmem_wait_ld();
+      const int4* kp4 = reinterpret_cast<const int4*>(kpos + c * 32);
+      uint32_t hi[16], lo[16];
 #pragma unroll
-    for (int c2 = 0; c2 < 2; ++c2) {  // keys 64*c2 .. 64*c2 + 63
-      uint32_t hi[32], lo[32];
+      for (int i = 0; i < 8; ++i) {
+        const int4 k4 = full ? make_int4(INT_MIN, INT_MIN, INT_MIN, INT_MIN) : kp4[i];
+        const int kk[4] = {k4.x, k4.y, k4.z, k4.w};
+        float pr[4];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int k = 64 * c2 + 2 * i;
-        const float p0 = exp2f(s[k >> 5][k & 31] - mb), p1 = exp2f(s[k >> 5][(k & 31) + 1] - mb);
-        const __half2 h = __floats2half2_rn(p0, p1);
-        const float2 hf = __half22float2(h);
-        hi[i] = h2_as_u32(h);
-        lo[i] = h2_as_u32(__floats2half2_rn(p0 - hf.x, p1 - hf.y));
-        l_run += p0 + p1;
+        for (int e = 0; e < 4; ++e) pr[e] = kk[e] <= qpos ? fast_exp2(fmaf(sv[4 * i + e], sl2, -mb)) : 0.f;
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const __half2 hh = __floats2half2_rn(pr[2 * e], pr[2 * e + 1]);
+          const float2 hf = __half22float2(hh);
+          hi[2 * i + e] = h2_as_u32(hh);
+          lo[2 * i + e] = h2_as_u32(__floats2half2_rn(pr[2 * e] - hf.x, pr[2 * e + 1] - hf.y));
+          l_run += pr[2 * e] + pr[2 * e + 1];
+        }
       }
-      tmem_st32u(tS + lane_base + 32 * c2, hi);
-      tmem_st32u(tS + lane_base + 64 + 32 * c2, lo);
+      tmem_st16u(tS + lane_base + 32 * c, hi);
+      tmem_st16u(tS + lane_base + 32 * c + 16, lo);
     }
     tmem_wait_st();
     tc_fence_before();
@@ -525,13 +682,15 @@ __global__ void __launch_bounds__(kThreads, 2) prefill_kernel(const Params p, co
 #pragma unroll
       for (int ks = 0; ks < kTile / 16; ++ks) {
         const uint64_t bd = smem_desc(v_addr + ks * 256, 128, 2048);  // V: MN-major (keys = K, channels = N)
-        umma_f16_ts(tO, tS + 8 * ks, bd, idesc_o, (o_live || ks > 0) ? 1u : 0u);
-        umma_f16_ts(tO, tS + 64 + 8 * ks, bd, idesc_o, 1u);
+        const uint32_t col = 32 * (ks >> 1) + 8 * (ks & 1);
+        umma_f16_ts(tO, tS + col, bd, idesc_o, (o_live || ks > 0) ? 1u : 0u);
+        umma_f16_ts(tO, tS + col + 16, bd, idesc_o, 1u);
       }
       umma_commit(bar_o);
     }
     o_live = true;
     pv_pending = true;
+    cur = nxt;
   }
 
   // ---- epilogue: O / l -> fp16 rows

@@ -113,8 +113,9 @@ def peaks() -> dict:
     if os.path.exists(p):
         with open(p) as f:
             d = json.load(f)
-        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
-    return {"hbm_gbs": 6650.0, "source": "fallback"}
+        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured", "bf16_tflops": d.get("bf16_tflops"),
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained")}
+    return {"hbm_gbs": 6650.0, "source": "fallback", "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
 def make_kv(torch, gen, shape, device, outlier_ch=(3, 77)):
@@ -323,6 +324,59 @@ def paged_bench(torch, akv, dev, n_seqs: int = 64, reps: int = 20) -> dict:
     res = {"workload": f"{n_seqs} sequences, warm 1,024-30,720 tokens (seeded), 512 hot each, 32/8 heads, "
                        "k4v2 + 1% outliers, shuffled pages", "total_warm_tokens": sum(lens), **res}
     del pool, hk, hv
+    torch.cuda.empty_cache()
+    return res
+
+
+# ---------------------------------------------------------------------------- prefill (config 3)
+def prefill_bench(torch, akv, dev, arena, hot_k, hot_v, reps: int = 2) -> dict:
+    """Config-3 prefill attention of one layer on the tcgen05 kernel: B16, 32
+    query / 8 KV heads, a 32,768-token prompt after its prefill demotion
+    (30,720 warm tokens in packed k4v2 records at sorted positions drawn at
+    random, as the demotion picks them, and 2,048 FP16 hot tokens), every
+    query attending causally by position.  Device time per layer launch (CUDA
+    events, median of `reps` after one warm-up); FLOPs = 4 * D * (visible
+    query-key pairs) * B * Hq, the causal attention's algorithmic work."""
+    B, Hkv, _, D = hot_k.shape
+    Hq = CFG["Hq"] * Hkv // CFG["Hkv"]
+    N = CFG["ctx"]
+    n_warm = arena.n_blocks * 32
+    g = torch.Generator().manual_seed(31)
+    perm = torch.randperm(N, generator=g)
+    wpos = perm[:n_warm].sort().values.to(torch.int32).to(dev)
+    hpos = perm[n_warm:].sort().values.to(torch.int32).to(dev)
+    gd = torch.Generator(device=dev).manual_seed(32)
+    q = torch.randn(B, Hq, N, D, generator=gd, device=dev).half()
+    qpos = torch.arange(N, dtype=torch.int32, device=dev)
+    out = torch.empty_like(q)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def run():
+        akv.prefill_attention(q, qpos, hot_k, hot_v, hpos, arena, wpos, out=out, status=status)
+
+    run()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        run()
+        e1.record()
+        e1.synchronize()
+        ts.append(e0.elapsed_time(e1) * 1e3)
+    if int(status.item()) != 0:
+        raise SystemExit(f"prefill device status {int(status.item())}")
+    us = statistics.median(ts)
+    flops = 4.0 * D * (N * (N + 1) / 2) * B * Hq
+    tf = flops / (us * 1e-6) / 1e12
+    pk = peaks()
+    res = {"workload": f"config 3 prefill, one layer: B{B}, {Hq}/{Hkv} heads, {N}-token prompt causal, "
+                       f"{n_warm} warm (k4v2 records) + {N - n_warm} hot",
+           "layer_us": round(us, 1), "causal_flops": flops, "tflops": round(tf, 1)}
+    if pk.get("bf16_tflops_sustained"):
+        res["frac_of_bf16_sustained"] = round(tf / pk["bf16_tflops_sustained"], 4)
+        res["frac_of_bf16_burst"] = round(tf / pk["bf16_tflops"], 4)
+    del q, out
     torch.cuda.empty_cache()
     return res
 
@@ -604,6 +658,8 @@ def run_ours(args):
             "gpu_launches": 2 * L * args.steps,
             "clocks": clocks,
         }
+        if world == 1 and not args.no_prefill:
+            res["prefill"] = prefill_bench(torch, akv, dev, arenas[0], hot_k[0], hot_v[0])
         if world == 1 and not args.no_migration:
             res["migration"] = migration_bench(torch, akv, dev)
         if world == 1 and (not args.no_shapes or args.hf_tokens > 0):
@@ -702,6 +758,7 @@ def main():
     ap.add_argument("--cpu-units", type=int, default=4, help="(row, KV head) units timed per CPU-arm step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-migration", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the config-3 prefill attention timing")
     ap.add_argument("--no-shapes", action="store_true", help="skip the per-layer decode timings of configs 1, 2, 5")
     ap.add_argument("--hf-tokens", type=int, default=256,
                     help="config-2 HF greedy decoding length (0: skip the end-to-end model run)")

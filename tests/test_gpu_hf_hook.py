@@ -1,12 +1,13 @@
 """GPU: the "akv" HuggingFace attention hook over AKVCache(fused_decode=True).
 
-A decode step of a fused cache attends over the packed warm records and the
-hot tier in place (akv.hf_attention).  Checked against the reference data
+A decode step or a causal prefill of a fused cache attends over the packed
+warm records and the hot tier in place (akv.hf_attention).  Checked against the reference data
 flow (drop_in.py:753-787): SDPA over the chronological [dequantised warm;
 hot] FP16 view that a non-fused AKVCache returns.
 
-* per call: on every decode step of a Qwen2-shaped model, the hook's output
-  equals SDPA over the same layer's full view within the attention bar;
+* per call: on the prefill and every decode step of a Qwen2-shaped model, the
+  hook's output equals SDPA over the same layer's full view within the
+  attention bar;
 * end to end: teacher-forced decoding through the fused cache gives the same
   logits as the view cache, within a tolerance that allows each layer's
   attention to differ by the attention bar.
@@ -60,17 +61,21 @@ def test_hook_matches_sdpa_over_view_each_step(policy, monkeypatch):
     }[policy]
     model = _model()
     model.config._attn_implementation = "akv"
-    errs, calls = [], [0]
+    errs, calls, prefills = [], [0], [0]
     real = hook.akv_attention_forward
 
     def checked(module, query, key, value, attention_mask, **k2):
         out, w = real(module, query, key, value, attention_mask, **k2)
         layer = getattr(key, "_akv_layer", None)
-        if layer is not None and query.shape[2] == 1 and attention_mask is None:
-            calls[0] += 1
+        if layer is not None and attention_mask is None:
+            causal = query.shape[2] > 1  # a prefill: the tcgen05 kernel, causal by position
+            if causal:
+                prefills[0] += 1
+            else:
+                calls[0] += 1
             fk, fv = layer.full_view()
             ref, _ = sdpa_attention_forward(module, query.float(), fk.float(), fv.float(), None,
-                                            scaling=k2.get("scaling"))
+                                            scaling=k2.get("scaling"), is_causal=causal)
             errs.append(((out.float() - ref).abs().max().item(), _excess(out.float(), ref)))
         return out, w
 
@@ -88,6 +93,7 @@ def test_hook_matches_sdpa_over_view_each_step(policy, monkeypatch):
     finally:
         AttentionInterface.register("akv", real)
     assert calls[0] == 2 * 24, calls
+    assert prefills[0] == 2, prefills  # the 200-token prompt of both layers went through the prefill kernel
     print(f"[hf hook {policy}] max |fused - sdpa(view)| = {max(e[0] for e in errs):.2e}")
     assert max(e[1] for e in errs) <= 0.0
     layer = cache.layers[0]
@@ -99,17 +105,34 @@ def test_hook_matches_sdpa_over_view_each_step(policy, monkeypatch):
         assert live == layer._warm_keys_fp16.shape[2]
 
 
+def _fp32_attention(module, query, key, value, attention_mask, dropout=0.0, scaling=None, is_causal=None, **kw):
+    """SDPA in fp32 over the (real, non-fused) view: the exact-attention arm."""
+    from transformers.integrations.sdpa_attention import sdpa_attention_forward
+    out, w = sdpa_attention_forward(module, query.float(), key.float(), value.float(), attention_mask,
+                                    dropout=dropout, scaling=scaling, is_causal=is_causal, **kw)
+    return out.to(query.dtype), w
+
+
 def test_fused_decoding_logits_match_view_cache():
-    """Teacher-forced decoding: fused cache + "akv" hook against a view cache + SDPA."""
+    """Teacher-forced decoding: the fused cache + "akv" hook (prefill and
+    decode kernels) against the reference data flow (view cache + fp16 SDPA),
+    both measured against fp32 attention over the same view.  Every attention
+    call of either arm differs from fp32 attention by fp16 rounding, and the
+    model amplifies that through its layers; the fused arm must stay as close
+    to the fp32 arm as the reference flow is."""
     import akv
+    from transformers import AttentionInterface
+    from transformers.masking_utils import AttentionMaskInterface, sdpa_mask
+    AttentionInterface.register("akv_fp32", _fp32_attention)
+    AttentionMaskInterface.register("akv_fp32", sdpa_mask)
     model = _model()
     g = torch.Generator(device=DEV).manual_seed(2)
     prompt = torch.randint(1, 1000, (1, 300), generator=g, device=DEV)
     toks = torch.randint(1, 1000, (1, 32), generator=g, device=DEV)
     kw = dict(warm_bits=3, hot_budget=64, enable_promotion=False, enable_promotion_proxy=False, num_hidden_layers=2)
     logits = {}
-    for mode in ("view", "fused"):
-        model.config._attn_implementation = "sdpa" if mode == "view" else "akv"
+    for mode, impl in (("view", "sdpa"), ("fused", "akv"), ("fp32", "akv_fp32")):
+        model.config._attn_implementation = impl
         cache = akv.AKVCache(fused_decode=(mode == "fused"), **kw)
         rows = []
         with torch.no_grad():
@@ -119,13 +142,16 @@ def test_fused_decoding_logits_match_view_cache():
         logits[mode] = torch.cat(rows)
         assert cache.layers[1]._warm is not None
     model.config._attn_implementation = "sdpa"
-    a, b = logits["view"], logits["fused"]
-    err = (a - b).abs().max().item()
-    scale = a.abs().max().item()
-    print(f"[hf hook e2e] max |logits fused - view| = {err:.3e} (max |logit| {scale:.2f})")
-    assert torch.isfinite(b).all()
-    assert err <= 2e-2 * max(scale, 1.0)
-    assert (a.argmax(-1) == b.argmax(-1)).float().mean().item() >= 0.9
+    ref, view, fused = logits["fp32"], logits["view"], logits["fused"]
+    e_view = (view - ref).abs().max().item()
+    e_fused = (fused - ref).abs().max().item()
+    scale = ref.abs().max().item()
+    print(f"[hf hook e2e] max |logits - fp32 arm|: fused {e_fused:.3e}, view+SDPA {e_view:.3e} "
+          f"(max |logit| {scale:.2f})")
+    assert torch.isfinite(fused).all()
+    assert e_fused <= max(1.5 * e_view, 2e-2 * max(scale, 1.0))
+    agree = lambda a: (a.argmax(-1) == ref.argmax(-1)).float().mean().item()  # noqa: E731
+    assert agree(fused) >= agree(view) - 0.05
 
 
 def test_generate_with_hook_and_beam_ops():

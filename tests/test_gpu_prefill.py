@@ -157,3 +157,42 @@ def test_prefill_gqa_strided_query():
     qs = q.transpose(1, 2).contiguous().transpose(1, 2)  # same values, head stride D, token stride Hq*D
     out, _ = _run((qs, qpos, hk, hv, hpos, arena, wpos))
     check(out, _oracle(q, qpos, hk, hv, hpos, arena, wpos))
+
+
+def test_prefill_config3_scale_vs_torch_fp32():
+    """Config-3 shape per KV head: a 32K prompt after its prefill demotion
+    (30,720 warm tokens at k4v2 with one outlier channel, at sorted positions
+    drawn at random; 2,048 hot), every one of the 32,768 queries of 4 query
+    heads, causal.  Reference: fp32 softmax attention in torch on the GPU over
+    the exactly dequantised warm tier (the akv dequantiser, pinned bit-exact
+    to the oracle elsewhere) and the hot tier, in query chunks."""
+    import akv
+    g = torch.Generator(device=DEV).manual_seed(9)
+    B, Hq, Hkv, D, N, n_hot = 1, 4, 1, 128, 32768, 2048
+    n_warm = N - n_hot
+    perm = torch.randperm(N, generator=torch.Generator().manual_seed(9))
+    wpos = perm[:n_warm].sort().values.to(torch.int32)
+    hpos = perm[n_warm:].sort().values.to(torch.int32)
+    arena = akv.WarmArena(B, Hkv, D, 4, 2, outlier_fraction=0.01, max_blocks=n_warm // 32, device=DEV)
+    arena.append(_kv(g, (B, Hkv, n_warm, D)), _kv(g, (B, Hkv, n_warm, D), (5,)), group=32)
+    hk, hv = _kv(g, (B, Hkv, n_hot, D)), _kv(g, (B, Hkv, n_hot, D), (5,))
+    q = torch.randn(B, Hq, N, D, generator=g, device=DEV).half()
+    qpos = torch.arange(N, dtype=torch.int32, device=DEV)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    out = akv.prefill_attention(q, qpos, hk, hv, hpos.to(DEV), arena, wpos.to(DEV), status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    dk, dv = arena.dequantize(n_tokens=n_warm)
+    K = torch.cat([dk, hk], 2)[0, 0].float()
+    V = torch.cat([dv, hv], 2)[0, 0].float()
+    kp = torch.cat([wpos, hpos]).to(DEV)
+    worst = 0.0
+    for m0 in range(0, N, 2048):
+        qc = q[0, :, m0:m0 + 2048].float()
+        s = torch.einsum("hmd,nd->hmn", qc, K) / np.sqrt(D)
+        vis = kp[None, None, :] <= qpos[m0:m0 + 2048][None, :, None]
+        p = torch.softmax(s.masked_fill(~vis, float("-inf")), -1)
+        ref = (p @ V).cpu().numpy()
+        check(out[0, :, m0:m0 + 2048], ref)
+        worst = max(worst, float(np.abs(out[0, :, m0:m0 + 2048].float().cpu().numpy() - ref).max()))
+    assert worst < 0.05
