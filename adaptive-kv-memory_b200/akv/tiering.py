@@ -167,6 +167,17 @@ class ImportanceMigrator:
         if st is not None and indices.numel() > 0:
             st[2][indices.to(self.device)] = 1.0
 
+    def compact(self, layer_idx: int, keep: torch.Tensor) -> None:
+        """Keep only positions ``keep`` (ascending int64 on the device), in that
+        order: the tier manager's hot compaction after a demotion."""
+        st = self._state.get(layer_idx)
+        if st is None:
+            return
+        m = keep.numel()
+        for i in range(3):
+            st[i][:m] = st[i][keep]
+        st[3] = m
+
     def advance_step(self) -> None:
         self._step += 1
         for st in self._state.values():

@@ -183,12 +183,121 @@ def migration_bench(torch, akv, dev) -> dict:
     def h2d():
         tiering.cold_restore_blocks(host, cold_src, 0, stream=side).synchronize()
     t_d2h, t_h2d = timed(d2h, 10), timed(h2d, 10)
-    return {"workload": "config 4 shape: batch 8, 8 KV heads, 128K tokens, 2-bit warm, pinned cold tier",
+    res = {"workload": "config 4 shape: batch 8, 8 KV heads, 128K tokens, 2-bit warm, pinned cold tier",
             "importance_update_us": round(t_upd, 2), "importance_update_gbs": round(upd_bytes / (t_upd * 1e3), 1),
             "evict_select_us": round(t_sel, 2),
             "demote_pass_us": round(t_dem, 2), "demote_tokens": 64,
             "cold_d2h_gbs": round(cb / (t_d2h * 1e3), 1), "cold_h2d_gbs": round(cb / (t_h2d * 1e3), 1),
             "cold_bytes": cb}
+    del arena, hk, hv, cold_src, host
+    torch.cuda.empty_cache()
+    res["tier_manager"] = tier_manager_bench(torch, akv, dev)
+    return res
+
+
+def tier_manager_bench(torch, akv, dev, steps: int = 4096, every: int = 64) -> dict:
+    """Config 4 at shape through the three-tier manager (akv.migration.TierManager):
+    batch 8, 8 KV heads (32 query heads), head_dim 128, a 128K context held as
+    28,672 cold tokens (INT2 records in pinned host memory), 98,304 warm tokens
+    (2-bit records, the compact preset) and 4,096 FP16 hot tokens; then
+    `steps` decode steps, each appending one token, folding a synthetic
+    attention row (5 % of the hot tokens carry 80 % of the mass) into the
+    importance scores and attending over hot + warm; every `every` steps a pass
+    demotes 64 hot tokens to warm, restores 2 cold blocks and evicts the oldest
+    warm blocks back to the warm budget.  Timed with CUDA events around the
+    whole loop (host work included); afterwards every position must sit in
+    exactly one tier and the last attention is checked against fp32 attention
+    over the dequantised warm tier and the hot tier (torch on the GPU)."""
+    from akv.migration import TierManager
+    B, H, Hq, D = 8, 8, 32, 128
+    n_cold, n_warm, n_hot = 28672, 98304, 4096
+    warm_budget = n_warm // 32
+    tm = TierManager(B, H, D, hot_capacity=n_hot + every, warm_blocks=(n_cold + n_warm) // 32 + 64,
+                     cold_blocks=n_cold // 32 + 64, key_bits=2, value_bits=2, importance_decay=0.9, device=dev)
+    g = torch.Generator(device=dev).manual_seed(41)
+    for t0 in range(0, n_cold + n_warm, 8192):
+        n = min(8192, n_cold + n_warm - t0)
+        tm.load_warm(0, make_kv(torch, g, (B, H, n, D), dev), make_kv(torch, g, (B, H, n, D), dev))
+    tm.evict(0, n_cold // 32)  # the oldest blocks go to the cold tier
+    tm.append(0, make_kv(torch, g, (B, H, n_hot, D), dev), make_kv(torch, g, (B, H, n_hot, D), dev))
+    new_k = [make_kv(torch, g, (B, H, 1, D), dev) for _ in range(64)]
+    new_v = [make_kv(torch, g, (B, H, 1, D), dev) for _ in range(64)]
+    qs = [torch.randn(B, Hq, D, generator=g, device=dev).half() for _ in range(8)]
+    attn = []
+    for i in range(4):
+        n = n_hot + every
+        k = max(1, n // 20)
+        idx = torch.randperm(n, generator=g, device=dev)[:k]
+        p = torch.rand(B, H, 1, n, generator=g, device=dev)
+        p[..., idx] = 0.0
+        p = p / p.sum(-1, keepdim=True) * 0.2
+        p[..., idx] += 0.8 / k
+        attn.append(p)
+    out = torch.empty(B, Hq, D, dtype=torch.float16, device=dev)
+    pass_ms = []
+
+    def step(i):
+        tm.append(0, new_k[i % 64], new_v[i % 64])
+        tm.update_importance(0, attn[i % 4][..., :tm.hot_len(0)])
+        tm.advance_step()
+        tm.attend(0, qs[i % 8], out=out)
+        if (i + 1) % every == 0:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            tm.demote(0, every)
+            tm.restore(0, 2)
+            over = tm.warm_len_blocks(0) - warm_budget
+            if over > 0:
+                tm.evict(0, over)
+            tm.end_pass()
+            e1.record()
+            pass_ms.append((e0, e1))
+
+    for i in range(every):  # warm-up: one full pass
+        step(i)
+    torch.cuda.synchronize()
+    pass_ms.clear()
+    d2h0, h2d0 = tm.stats.cold_bytes_d2h, tm.stats.cold_bytes_h2d
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for i in range(steps):
+        step(i)
+    t1.record()
+    torch.cuda.synchronize()
+    total_ms = t0.elapsed_time(t1)
+    passes = [a.elapsed_time(b) for a, b in pass_ms]
+    # checks: tiers partition the positions; attention against fp32 (torch, GPU)
+    pos = tm.positions(0)
+    allpos = torch.from_numpy(__import__("numpy").sort(__import__("numpy").concatenate(
+        [pos["hot"], pos["warm"], pos["cold"]])))
+    partition_ok = bool(torch.equal(allpos, torch.arange(tm.layers[0].next_pos)))
+    lay = tm.layers[0]
+    q = qs[0]
+    o = tm.attend(0, q)
+    nb = lay.arena.n_blocks
+    masks = lay.arena.masks()[0, 0]
+    valid = ((masks[:, None] >> torch.arange(32, device=dev)) & 1).bool().reshape(-1)
+    slots = torch.arange(nb * 32, device=dev)[valid]
+    wk, wv = lay.arena.dequantize(tok_idx=slots)
+    K = torch.cat([wk, lay.hot_k[:, :, :lay.hot_len]], 2).float()
+    V = torch.cat([wv, lay.hot_v[:, :, :lay.hot_len]], 2).float()
+    qf = q.float().reshape(B, H, Hq // H, D)
+    sc = torch.einsum("bhgd,bhnd->bhgn", qf, K) / (D ** 0.5)
+    ref = torch.einsum("bhgn,bhnd->bhgd", torch.softmax(sc, -1), V).reshape(B, Hq, D)
+    max_err = float((o.float() - ref).abs().max().item())
+    del K, V, wk, wv, sc
+    res = {"workload": f"config 4 through the tier manager: B{B}, {H} KV / {Hq} Q heads, 128K context "
+                       f"({n_cold} cold INT2 in pinned host memory, {n_warm} warm 2-bit, {n_hot} hot), {steps} decode "
+                       f"steps, demote 64 / restore 2 cold blocks / evict oldest warm every {every}",
+           "us_per_step": round(total_ms * 1e3 / steps, 2), "pass_us": round(statistics.median(passes) * 1e3, 1),
+           "passes": len(passes), "cold_gb_moved": round((tm.stats.cold_bytes_d2h - d2h0 + tm.stats.cold_bytes_h2d
+                                                          - h2d0) / 1e9, 3),
+           "final_tiers_tokens": {"hot": int(pos["hot"].size), "warm": int(pos["warm"].size),
+                                  "cold": int(pos["cold"].size)},
+           "partition_ok": partition_ok, "max_err": max_err}
+    del tm
+    torch.cuda.empty_cache()
+    return res
 
 
 # ---------------------------------------------------------------------------- other decode shapes
@@ -324,6 +433,108 @@ def paged_bench(torch, akv, dev, n_seqs: int = 64, reps: int = 20) -> dict:
     res = {"workload": f"{n_seqs} sequences, warm 1,024-30,720 tokens (seeded), 512 hot each, 32/8 heads, "
                        "k4v2 + 1% outliers, shuffled pages", "total_warm_tokens": sum(lens), **res}
     del pool, hk, hv
+    torch.cuda.empty_cache()
+    return res
+
+
+# ---------------------------------------------------------------------------- sequence split (config 5b)
+def seq_split_bench(torch, akv, dev, world: int, rank: int, reps: int = 20) -> dict:
+    """Config 5b across the ranks: batch 1, 64 query / 8 KV heads, a 512K
+    context (520,192 warm tokens in k4v4 records + 4,096 FP16 hot on rank 0)
+    whose warm blocks are split contiguously over the ranks.  Per layer: each
+    rank's decode writes the split partial (acc, m, l) of its tokens, an NCCL
+    all-gather collects the (64, 130) partials over NVLink, and the LSE combine
+    kernel merges them.  Each component is timed with CUDA events on the rank
+    (median of `reps`), the max over ranks is reported.  Rank 0 also rebuilds
+    the whole sequence and checks the split result against one single-GPU
+    decode of all tokens (max_err).  Every rank quantises shard r from seed
+    400 + r, so the records are identical either way."""
+    import torch.distributed as dist
+    from akv import parallel as P
+    B, Hq, Hkv, D = 1, 64, 8, 128
+    n_hot = 4096
+    nblk = (512 * 1024 - n_hot) // 32
+    spans = [P.ShardPlan("sequence", world, r).span(nblk) for r in range(world)]
+
+    def shard(r, arena):
+        lo, hi = spans[r]
+        g = torch.Generator(device=dev).manual_seed(400 + r)
+        for b0 in range(lo, hi, 4096):  # bounded temporaries
+            n = min(4096, hi - b0) * 32
+            arena.append(make_kv(torch, g, (B, Hkv, n, D), dev), make_kv(torch, g, (B, Hkv, n, D), dev), group=32)
+
+    lo, hi = spans[rank]
+    mine = akv.WarmArena(B, Hkv, D, 4, 4, 0.0, max_blocks=hi - lo, device=dev)
+    shard(rank, mine)
+    gh = torch.Generator(device=dev).manual_seed(399)
+    hk = make_kv(torch, gh, (B, Hkv, n_hot, D), dev)
+    hv = make_kv(torch, gh, (B, Hkv, n_hot, D), dev)
+    q = torch.randn(B, Hq, D, generator=gh, device=dev).half()
+    # layer copies so each rank's working set exceeds the L2 between repetitions
+    shard_bytes = mine.buf.numel() + (2 * hk.numel() * 2 if rank == 0 else 0)
+    copies = max(1, -(-(256 << 20) // shard_bytes))
+    arenas = [mine]
+    for _ in range(copies - 1):
+        a = akv.WarmArena(B, Hkv, D, 4, 4, 0.0, max_blocks=hi - lo, device=dev)
+        a.buf.copy_(mine.buf)
+        a.n_blocks = mine.n_blocks
+        arenas.append(a)
+    rows = B * Hq
+    gathered = torch.empty(world, rows, D + 2, dtype=torch.float32, device=dev)
+    out = torch.empty(rows, D, dtype=torch.float16, device=dev)
+    hot = (hk, hv) if rank == 0 else (None, None)
+
+    def layer(i):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        ev[0].record()
+        p = P.local_partial(q, hot[0], hot[1], arenas[i % copies])
+        ev[1].record()
+        dist.all_gather_into_tensor(gathered, p)
+        ev[2].record()
+        part = gathered.permute(1, 0, 2).contiguous()
+        _C_combine(part, out)
+        ev[3].record()
+        return ev
+
+    from akv import _C
+
+    def _C_combine(part, o):
+        _C.check(_C.load().akv_lse_combine(part.data_ptr(), D + 2, part.stride(0), rows, world, D, o.data_ptr(), D,
+                                           None, None, _C.stream_of(part)), "akv_lse_combine")
+
+    for i in range(3):
+        layer(i)
+    torch.cuda.synchronize()
+    dist.barrier()
+    t = {"decode": [], "all_gather": [], "combine": [], "layer": []}
+    for i in range(reps):
+        ev = layer(i)
+        ev[3].synchronize()
+        t["decode"].append(ev[0].elapsed_time(ev[1]) * 1e3)
+        t["all_gather"].append(ev[1].elapsed_time(ev[2]) * 1e3)
+        t["combine"].append(ev[2].elapsed_time(ev[3]) * 1e3)
+        t["layer"].append(ev[0].elapsed_time(ev[3]) * 1e3)
+    med = torch.tensor([statistics.median(t[k]) for k in ("decode", "all_gather", "combine", "layer")],
+                       dtype=torch.float64, device=dev)
+    dist.all_reduce(med, op=dist.ReduceOp.MAX)
+    split_out = out.clone()
+    max_err = None
+    if rank == 0:  # the whole sequence on this GPU
+        full = akv.WarmArena(B, Hkv, D, 4, 4, 0.0, max_blocks=nblk, device=dev)
+        for r in range(world):
+            shard(r, full)
+        ref = akv.mixed_tier_decode_attention(q, hk, hv, full)
+        max_err = float((split_out.float() - ref.reshape(rows, D).float()).abs().max().item())
+        del full
+    dist.barrier()
+    d, g_, c_, l_ = [round(float(x), 2) for x in med.tolist()]
+    res = {"workload": f"config 5b: B1, 64/8 heads, 512K context (520,192 warm k4v4 + 4,096 hot on rank 0), "
+                       f"warm blocks split over {world} GPUs, NCCL all-gather + LSE combine",
+           "decode_us": d, "all_gather_us": g_, "combine_us": c_, "layer_us": l_,
+           "warm_blocks_per_rank": hi - lo, "layer_copies": copies,
+           "limiter": max((("decode", d), ("all_gather", g_), ("combine", c_)), key=lambda x: x[1])[0],
+           "max_err": max_err}
+    del arenas, mine
     torch.cuda.empty_cache()
     return res
 
@@ -639,6 +850,10 @@ def run_ours(args):
         # shapes scale it by the (row, KV head) units they process
         traffic = int(tr["bytes_per_launch"] * (B * hkv) / (CFG["B"] * CFG["Hkv"]))
 
+    seq_split = None
+    if world > 1 and not args.no_seq_split:  # every rank takes part (collectives)
+        seq_split = seq_split_bench(torch, akv, dev, world, rank)
+
     if rank == 0:
         res = {
             "metric": METRIC, "value": round(ms_step * 1e3, 2), "unit": "µs/step",
@@ -658,6 +873,8 @@ def run_ours(args):
             "gpu_launches": 2 * L * args.steps,
             "clocks": clocks,
         }
+        if seq_split is not None:
+            res["seq_split_5b"] = seq_split
         if world == 1 and not args.no_prefill:
             res["prefill"] = prefill_bench(torch, akv, dev, arenas[0], hot_k[0], hot_v[0])
         if world == 1 and not args.no_migration:
@@ -759,6 +976,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-migration", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-3 prefill attention timing")
+    ap.add_argument("--no-seq-split", action="store_true", help="skip the config-5b sequence split (N > 1)")
     ap.add_argument("--no-shapes", action="store_true", help="skip the per-layer decode timings of configs 1, 2, 5")
     ap.add_argument("--hf-tokens", type=int, default=256,
                     help="config-2 HF greedy decoding length (0: skip the end-to-end model run)")
