@@ -124,8 +124,16 @@ class AKVLayer(_LayerBase):
         # tier in place
         self.fused_decode = fused_decode
 
-        self._hot_keys: Optional[torch.Tensor] = None
-        self._hot_values: Optional[torch.Tensor] = None
+        # hot tier storage: ring buffers (B, H, cap, D) whose rows [0, _hn) are
+        # the live tokens; _phys maps logical hot order (arrival order, promoted
+        # tokens first) to buffer rows (None: identity).  A decode step writes
+        # its token into the row its demoted token leaves, so no step copies
+        # the hot tier; the logical-order tensors (_hot_keys / _hot_values) are
+        # rebuilt only where order matters (the view, promotion, batch ops).
+        self._hk: Optional[torch.Tensor] = None
+        self._hv: Optional[torch.Tensor] = None
+        self._hn = 0
+        self._phys: Optional[np.ndarray] = None
         self._warm_keys_fp16: Optional[torch.Tensor] = None  # exact dequantisation of the warm records
         self._warm_values_fp16: Optional[torch.Tensor] = None
         # capacity buffers behind the two tensors above: appends write in place
@@ -134,11 +142,16 @@ class AKVLayer(_LayerBase):
         self._warm_vbuf: Optional[torch.Tensor] = None
         self._nan: Optional[torch.Tensor] = None  # one-element source of the fused-decode placeholder
         self._warm: Optional[WarmArena] = None  # packed warm block records (source of truth)
-        self._warm_slots: Optional[torch.Tensor] = None  # arena slot (blk*32 + s) of each warm token
-        # int32 position of the token in each arena slot (device), read by the
-        # prefill kernel; slots a demote event leaves empty are never read
-        # (their record mask bit is clear)
-        self._slot_pos: Optional[torch.Tensor] = None
+        # arena slot (blk*32 + s) of each warm token, in warm order (host; the
+        # device copy _warm_slots is built when a dequantisation needs it)
+        self._wslots_buf = np.zeros(64, dtype=np.int64)
+        self._wslots_n = 0
+        self._wslots_dev: Optional[torch.Tensor] = None
+        # int32 position of the token in each arena slot (host mirror; uploaded
+        # for the prefill kernel); slots a demote event leaves empty are never
+        # read (their record mask bit is clear)
+        self._slot_pos_np: Optional[np.ndarray] = None
+        self._slot_pos_dev: Optional[torch.Tensor] = None
         self._warm_len = 0
         self._total_len = 0
         self._warm_bytes_packed = 0
@@ -149,6 +162,124 @@ class AKVLayer(_LayerBase):
         self._decay = 0.3
         self._n_anchors = 16
         self._step = 0
+
+    # ------------------------------------------------------------------ hot ring
+    def _hot_view(self, buf: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
+        if buf is None:
+            return None
+        if self._phys is None:
+            return buf[:, :, :self._hn]
+        return buf.index_select(2, _to_device(torch.from_numpy(self._phys), buf.device))
+
+    @property
+    def _hot_keys(self) -> Optional[torch.Tensor]:
+        """Hot keys (B, H, hot_len, D) in logical order (a view when rows are in order)."""
+        return self._hot_view(self._hk)
+
+    @property
+    def _hot_values(self) -> Optional[torch.Tensor]:
+        return self._hot_view(self._hv)
+
+    def _set_hot(self, which: int, x: Optional[torch.Tensor]) -> None:
+        """Replace the keys (0) or values (1) with logical-order tensor x; the
+        other buffer is first rewritten in logical order, so the two stay aligned."""
+        if self._phys is not None:
+            other = self._hv if which == 0 else self._hk
+            if other is not None:
+                o = self._hot_view(other)
+                if which == 0:
+                    self._hv = o.contiguous()
+                else:
+                    self._hk = o.contiguous()
+            self._phys = None
+        if x is None:
+            if which == 0:
+                self._hk = None
+            else:
+                self._hv = None
+            self._hn = 0
+            return
+        buf = x.contiguous() if x.stride(-1) != 1 else x
+        if which == 0:
+            self._hk = buf
+        else:
+            self._hv = buf
+        self._hn = x.shape[2]
+
+    @_hot_keys.setter
+    def _hot_keys(self, x: Optional[torch.Tensor]) -> None:
+        self._set_hot(0, x)
+
+    @_hot_values.setter
+    def _hot_values(self, x: Optional[torch.Tensor]) -> None:
+        self._set_hot(1, x)
+
+    def _hot_reserve(self, n: int) -> None:
+        """Room for n live rows (capacity doubles; live rows are copied)."""
+        cap = self._hk.shape[2]
+        if n <= cap and self._hk.stride(2) == self._hk.shape[3] and self._hk.is_contiguous():
+            return
+        new_cap = max(n, 2 * cap, self.hot_budget + 64)
+        B, H, _, D = self._hk.shape
+        for name in ("_hk", "_hv"):
+            old = getattr(self, name)
+            nb = torch.empty(B, H, new_cap, D, dtype=old.dtype, device=old.device)
+            nb[:, :, :self._hn].copy_(old[:, :, :self._hn])
+            setattr(self, name, nb)
+
+    def _hot_append(self, k: torch.Tensor, v: torch.Tensor) -> None:
+        """Append new tokens at the end of the logical order (rows _hn .. _hn + N)."""
+        N = k.shape[2]
+        if self._hk is None:
+            self._hk, self._hv, self._hn, self._phys = k, v, 0, None
+            self._hk = None
+            B, H, _, D = k.shape
+            cap = max(N, self.hot_budget) + 64
+            self._hk = torch.empty(B, H, cap, D, dtype=k.dtype, device=k.device)
+            self._hv = torch.empty(B, H, cap, D, dtype=v.dtype, device=v.device)
+        self._hot_reserve(self._hn + N)
+        self._hk[:, :, self._hn:self._hn + N].copy_(k)
+        self._hv[:, :, self._hn:self._hn + N].copy_(v)
+        if self._phys is not None:
+            self._phys = np.concatenate([self._phys, np.arange(self._hn, self._hn + N, dtype=np.int64)])
+        self._hn += N
+
+    def _hot_remove(self, rows: np.ndarray, kept_logical: np.ndarray) -> None:
+        """Drop buffer rows ``rows``; the live rows of the tail move into the
+        holes, and the logical order becomes the kept logical indices."""
+        phys = self._phys if self._phys is not None else np.arange(self._hn, dtype=np.int64)
+        new_n = self._hn - rows.size
+        gone = np.zeros(self._hn, dtype=bool)
+        gone[rows] = True
+        holes = rows[rows < new_n]
+        movers = np.nonzero(~gone[new_n:])[0] + new_n  # live rows past the new end
+        if holes.size:
+            dev = self._hk.device
+            if holes.size == 1:
+                h, m = int(holes[0]), int(movers[0])
+                self._hk[:, :, h].copy_(self._hk[:, :, m])
+                self._hv[:, :, h].copy_(self._hv[:, :, m])
+            else:
+                idx = _to_device(torch.from_numpy(np.concatenate([movers, holes])), dev)
+                src, dst = idx[:movers.size], idx[movers.size:]
+                self._hk.index_copy_(2, dst, self._hk.index_select(2, src))
+                self._hv.index_copy_(2, dst, self._hv.index_select(2, src))
+            remap = np.arange(self._hn, dtype=np.int64)
+            remap[movers] = holes
+            new_phys = remap[phys[kept_logical]]
+        else:
+            new_phys = phys[kept_logical]
+        self._hn = new_n
+        self._phys = None if np.array_equal(new_phys, np.arange(new_n)) else new_phys
+
+    def _hot_phys_positions(self) -> np.ndarray:
+        """Position of the token in each buffer row [0, _hn)."""
+        hp = self._hot_positions.numpy()
+        if self._phys is None:
+            return hp
+        out = np.empty(self._hn, dtype=hp.dtype)
+        out[self._phys] = hp
+        return out
 
     # ------------------------------------------------------------------ importance / selection
     def _update_importance(self, n_new: int, hot_len: int) -> None:
@@ -173,15 +304,15 @@ class AKVLayer(_LayerBase):
         return torch.from_numpy(np.sort(idx.numpy()))
 
     # ------------------------------------------------------------------ warm tier
-    def _demote(self, demote_idx: torch.Tensor, idx_dev: Optional[torch.Tensor] = None,
-                pos_dev: Optional[torch.Tensor] = None) -> None:
-        """Quantise the selected hot rows into new warm records (one scale group per batch row).
-        ``idx_dev``: the same indices already on the device; ``pos_dev``: the
-        demoted tokens' positions on the device (recorded per arena slot)."""
-        hk, hv = self._hot_keys, self._hot_values
+    def _demote(self, rows: np.ndarray, positions: np.ndarray) -> None:
+        """Quantise hot buffer rows ``rows`` (the demote event, in logical
+        order) into new warm records, one scale group per batch row, reading
+        the rows in place (a single row by pointer, several through the fused
+        gather); ``positions`` are the demoted tokens' positions."""
+        hk, hv = self._hk[:, :, :self._hn], self._hv[:, :, :self._hn]
         _C.require_cuda(hk, hv)
         B, H, _, D = hk.shape
-        n = int(demote_idx.numel())
+        n = int(rows.size)
         if self._warm is None:
             cap = max(4, (n + BLOCK - 1) // BLOCK)
             if self.per_head_bits is not None and len(self.per_head_bits) == H:
@@ -193,13 +324,14 @@ class AKVLayer(_LayerBase):
         arena = self._warm
         nblk = (n + BLOCK - 1) // BLOCK
         arena.grow(arena.n_blocks + nblk)
-        if idx_dev is None:
-            idx_dev = _to_device(demote_idx, hk.device)
-        blk0 = arena.append(hk, hv, group=n, tok_idx=idx_dev)
-        slots = torch.arange(blk0 * BLOCK, blk0 * BLOCK + n, dtype=torch.int64, device=hk.device)
-        self._append_1d("_warm_slots", slots)
-        if pos_dev is not None:
-            self._record_slot_pos(blk0 * BLOCK, pos_dev)
+        if n == 1:
+            r = int(rows[0])
+            blk0 = arena.append(hk[:, :, r:r + 1], hv[:, :, r:r + 1], group=1)
+        else:
+            blk0 = arena.append(hk, hv, group=n, tok_idx=_to_device(torch.from_numpy(rows), hk.device))
+        slots = np.arange(blk0 * BLOCK, blk0 * BLOCK + n, dtype=np.int64)
+        self._wslots_append(slots)
+        self._record_slot_pos(blk0 * BLOCK, positions)
         # the reference's measure_packed_bytes of this event's K and V dicts (drop_in.py:331-336)
         if isinstance(arena, HeadGroupArena):  # one K and one V dict per head, at that head's width
             self._warm_bytes_packed += B * sum(2 * n * packed_width(D, b) + 4 * D + 4 * n for b in self.per_head_bits)
@@ -208,18 +340,58 @@ class AKVLayer(_LayerBase):
             self._warm_bytes_packed += B * (H * n * packed_width(D, kb) + 4 * H * D + H * n * packed_width(D, vb)
                                             + 4 * H * n)
         if not self._no_fp16_copy:
-            self._append_warm_fp16(*arena.dequantize(tok_idx=slots))
+            self._append_warm_fp16(*arena.dequantize(tok_idx=_to_device(torch.from_numpy(slots), hk.device)))
 
-    def _record_slot_pos(self, slot0: int, pos_dev: torch.Tensor) -> None:
+    @property
+    def _wslots(self) -> np.ndarray:
+        return self._wslots_buf[:self._wslots_n]
+
+    @_wslots.setter
+    def _wslots(self, arr: np.ndarray) -> None:
+        self._wslots_buf = np.array(arr, dtype=np.int64)
+        self._wslots_n = self._wslots_buf.shape[0]
+        self._wslots_dev = None
+
+    def _wslots_append(self, slots: np.ndarray) -> None:
+        """Amortised append: the slot list is the front of a capacity buffer."""
+        n = self._wslots_n + slots.shape[0]
+        if n > self._wslots_buf.shape[0]:
+            nb = np.empty(max(2 * n, 64), dtype=np.int64)
+            nb[:self._wslots_n] = self._wslots_buf[:self._wslots_n]
+            self._wslots_buf = nb
+        self._wslots_buf[self._wslots_n:n] = slots
+        self._wslots_n = n
+        self._wslots_dev = None
+
+    @property
+    def _warm_slots(self) -> Optional[torch.Tensor]:
+        """Device copy of the warm tokens' arena slots (built when needed)."""
+        if self._warm is None:
+            return None
+        if self._wslots_dev is None or self._wslots_dev.shape[0] != self._wslots.shape[0]:
+            self._wslots_dev = _to_device(torch.from_numpy(self._wslots), self._warm.device)
+        return self._wslots_dev
+
+    def _record_slot_pos(self, slot0: int, positions: np.ndarray) -> None:
         """Positions of the tokens written at arena slots slot0 .. slot0 + n - 1."""
         need = self._warm.max_blocks * BLOCK
-        buf = self._slot_pos
-        if buf is None or buf.shape[0] < need or buf.device != pos_dev.device:
-            nb = torch.zeros(need, dtype=torch.int32, device=pos_dev.device)
+        buf = self._slot_pos_np
+        if buf is None or buf.shape[0] < need:
+            nb = np.zeros(need, dtype=np.int32)
             if buf is not None:
-                nb[:buf.shape[0]].copy_(buf[:need])
-            self._slot_pos = buf = nb
-        buf[slot0:slot0 + pos_dev.shape[0]].copy_(pos_dev)
+                nb[:buf.shape[0]] = buf
+            self._slot_pos_np = buf = nb
+        buf[slot0:slot0 + positions.shape[0]] = positions
+        self._slot_pos_dev = None
+
+    @property
+    def _slot_pos(self) -> Optional[torch.Tensor]:
+        """Device int32 slot positions for the prefill kernel (uploaded when they changed)."""
+        if self._slot_pos_np is None or self._warm is None:
+            return None
+        if self._slot_pos_dev is None:
+            self._slot_pos_dev = _to_device(torch.from_numpy(self._slot_pos_np.copy()), self._warm.device)
+        return self._slot_pos_dev
 
     @property
     def _no_fp16_copy(self) -> bool:
@@ -285,12 +457,13 @@ class AKVLayer(_LayerBase):
     def _remove_warm(self, promote_mask: torch.Tensor, n_promote: int, warm_len: int) -> None:
         """Drop promoted tokens from the warm tier (records keep the bytes, mask bits cleared)."""
         keep = ~promote_mask
-        gone = self._warm_slots[promote_mask.to(self._warm_slots.device)]
-        if self._warm is not None and gone.numel():
-            self._warm.drop_slots(gone)
+        pm = promote_mask.detach().cpu().numpy()
+        gone = self._wslots[pm]
+        if self._warm is not None and gone.size:
+            self._warm.drop_slots(_to_device(torch.from_numpy(gone), self._warm.device))
         self._warm_keys_fp16 = self._warm_keys_fp16[:, :, keep, :]
         self._warm_values_fp16 = self._warm_values_fp16[:, :, keep, :]
-        self._warm_slots = self._warm_slots[keep.to(self._warm_slots.device)]
+        self._wslots = self._wslots[~pm]
         if self._warm_positions is not None:
             self._warm_positions = self._warm_positions[keep.detach().to("cpu")]
         if warm_len > 0:
@@ -312,8 +485,9 @@ class AKVLayer(_LayerBase):
         if filter_proxy:
             self._proxy_score = self._proxy_score[~promote_mask]
         self._remove_warm(promote_mask, n_promote, warm_len)
-        self._hot_keys = torch.cat([promoted_k, self._hot_keys], dim=2)
-        self._hot_values = torch.cat([promoted_v, self._hot_values], dim=2)
+        nk = torch.cat([promoted_k, self._hot_keys], dim=2)
+        nv = torch.cat([promoted_v, self._hot_values], dim=2)
+        self._hot_keys, self._hot_values = nk, nv
         if promoted_pos is not None and self._hot_positions is not None:
             self._hot_positions = torch.cat([promoted_pos, self._hot_positions])
         if self._importance is not None:
@@ -331,10 +505,10 @@ class AKVLayer(_LayerBase):
 
     def _promote_from_warm(self, attention_weights: torch.Tensor) -> None:
         """Promotion by mean attention to warm tokens (drop_in.py:415-484)."""
-        if self._warm_keys_fp16 is None or self._warm_keys_fp16.shape[2] == 0 or self._hot_keys is None:
+        if self._warm_keys_fp16 is None or self._warm_keys_fp16.shape[2] == 0 or self._hk is None:
             return
         warm_len = self._warm_keys_fp16.shape[2]
-        hot_len = self._hot_keys.shape[2]
+        hot_len = self._hn
         if attention_weights.dim() == 4 and attention_weights.shape[-1] >= warm_len + hot_len:
             warm_attn = attention_weights[:, :, :, :warm_len].mean(dim=(0, 1, 2))
             promote_mask = warm_attn > self.promotion_threshold
@@ -361,7 +535,7 @@ class AKVLayer(_LayerBase):
     def _promote_from_proxy(self) -> None:
         """Attention-free promotion (drop_in.py:527-589)."""
         if (self._proxy_score is None or self._warm_keys_fp16 is None or self._warm_keys_fp16.shape[2] == 0
-                or self._hot_keys is None):
+                or self._hk is None):
             return
         if self._proxy_score.shape[0] != self._warm_keys_fp16.shape[2]:
             return
@@ -383,59 +557,67 @@ class AKVLayer(_LayerBase):
         """Append, migrate, return the chronological full view (drop_in.py:591-787)."""
         N = key_states.shape[2]
         new_positions = np.arange(self._total_len, self._total_len + N, dtype=np.int64)
-        if self._hot_keys is None:
-            self._hot_keys, self._hot_values = key_states, value_states
+        first = self._hk is None
+        budget = self.hot_budget
+        if self.adaptive_hot_frac > 0.0:
+            budget = max(self.hot_budget, int(self.adaptive_hot_frac * (self._total_len + N)))
+        # a decode step of a layer that demotes one token and promotes nothing:
+        # its token goes straight into the row the demoted token leaves
+        fast = (N == 1 and not first and not self.protect and not self.enable_promotion
+                and not self.enable_promotion_proxy and self._hn + 1 - budget == 1 and key_states.is_cuda)
+        if first:
+            self._hot_append(key_states, value_states)
             self._hot_positions = torch.from_numpy(new_positions)
         else:
-            self._hot_keys = torch.cat([self._hot_keys, key_states], dim=2)
-            self._hot_values = torch.cat([self._hot_values, value_states], dim=2)
+            if not fast:
+                self._hot_append(key_states, value_states)
             self._hot_positions = torch.from_numpy(np.concatenate([self._hot_positions.numpy(), new_positions]))
         self._total_len += N
         if self.protect:
             return self._publish(self._hot_keys, self._hot_values)
         self._step += 1
 
-        hot_len = self._hot_keys.shape[2]
+        hot_len = self._hn + (1 if fast else 0)
         self._update_importance(N, hot_len)
         if self.enable_promotion_proxy:
             self._update_proxy_score(key_states)
         if self.enable_promotion and cache_kwargs and "attention_weights" in cache_kwargs:
             self._promote_from_warm(cache_kwargs["attention_weights"])
-            hot_len = self._hot_keys.shape[2]
+            hot_len = self._hn
         elif self.enable_promotion and self.enable_promotion_proxy:
             self._promote_from_proxy()
-            hot_len = self._hot_keys.shape[2]
-
-        budget = self.hot_budget
-        if self.adaptive_hot_frac > 0.0:
-            budget = max(self.hot_budget, int(self.adaptive_hot_frac * self._total_len))
+            hot_len = self._hn
 
         if hot_len > budget:
             n_demote = hot_len - budget
-            demote_idx = self._select_demote_indices(n_demote, hot_len)
-            d_np = demote_idx.numpy()
+            d_np = self._select_demote_indices(n_demote, hot_len).numpy()
             kept_np = np.delete(np.arange(hot_len, dtype=np.int64), d_np)
             hp = self._hot_positions.numpy()
-            demote_positions = torch.from_numpy(hp[d_np])
-            idx_dev, kept_dev, pos_dev = None, None, None
-            if self._hot_keys.device.type == "cuda":  # demote / keep indices and positions in one copy
-                both = _to_device(torch.from_numpy(np.concatenate([d_np, kept_np, hp[d_np]])),
-                                  self._hot_keys.device)
-                idx_dev, kept_dev = both[:n_demote], both[n_demote:hot_len]
-                pos_dev = both[hot_len:]
-            self._demote(demote_idx, idx_dev, pos_dev)
-            self._append_1d("_warm_positions", demote_positions)
+            phys = self._phys if self._phys is not None else np.arange(self._hn, dtype=np.int64)
+            if fast and int(d_np[0]) == hot_len - 1:  # the new token itself: append it, then demote
+                self._hot_append(key_states, value_states)
+                phys = self._phys if self._phys is not None else np.arange(self._hn, dtype=np.int64)
+                fast = False
+            rows = phys[d_np]
+            self._demote(rows, hp[d_np])
+            self._append_1d("_warm_positions", torch.from_numpy(hp[d_np]))
             self._warm_len += n_demote
             if self._proxy_score is not None:
                 pad = torch.zeros(n_demote, dtype=self._proxy_score.dtype, device=self._warm_keys_fp16.device)
                 self._proxy_score = torch.cat([self._proxy_score.to(pad.device), pad])
-            if kept_dev is None:
-                kept_dev = _to_device(torch.from_numpy(kept_np), self._hot_keys.device)
-            self._hot_keys = self._hot_keys.index_select(2, kept_dev)
-            self._hot_values = self._hot_values.index_select(2, kept_dev)
+            if fast:  # the new token takes the demoted token's row
+                r = int(rows[0])
+                self._hk[:, :, r:r + 1].copy_(key_states)
+                self._hv[:, :, r:r + 1].copy_(value_states)
+                new_phys = np.append(np.delete(phys, d_np), r)
+                self._phys = None if np.array_equal(new_phys, np.arange(self._hn)) else new_phys
+            else:
+                self._hot_remove(rows, kept_np)
             self._hot_positions = torch.from_numpy(hp[kept_np])
             if self._importance is not None:
                 self._importance = torch.from_numpy(self._importance.numpy()[kept_np])
+        elif fast:  # nothing to demote after all (a promotion path made room): append normally
+            self._hot_append(key_states, value_states)
 
         if self.fused_decode and self._warm is not None:
             return self._publish(*self._placeholder())
@@ -456,11 +638,11 @@ class AKVLayer(_LayerBase):
         zero-stride tensors of the view's shape, the key tagged with this
         layer.  Only the "akv" attention function reads the tag; any other
         attention over them produces NaN, never a silently wrong result."""
-        hk = self._hot_keys
+        hk = self._hk
         if self._nan is None or self._nan.dtype != hk.dtype or self._nan.device != hk.device:
             self._nan = torch.full((1, 1, 1, 1), float("nan"), dtype=hk.dtype, device=hk.device)
         B, H, _, D = hk.shape
-        n = hk.shape[2] + self._warm_len
+        n = self._hn + self._warm_len
         k = self._nan.expand(B, H, n, D)
         v = self._nan.expand(B, H, n, D)
         k._akv_layer = self
@@ -470,7 +652,7 @@ class AKVLayer(_LayerBase):
         """Prefill attention can read this layer's tiers in place (one bit
         width for every head, and a position recorded for every warm slot)."""
         return (self._warm is not None and not isinstance(self._warm, HeadGroupArena)
-                and self._slot_pos is not None and self._hot_keys is not None)
+                and self._slot_pos_np is not None and self._hk is not None)
 
     def prefill_attention(self, query: torch.Tensor, sm_scale: Optional[float] = None) -> torch.Tensor:
         """The newest q_len tokens' queries (B, Hq, q_len, D), causal by
@@ -481,27 +663,29 @@ class AKVLayer(_LayerBase):
         M = query.shape[2]
         dev = query.device
         q_pos = torch.arange(self._total_len - M, self._total_len, dtype=torch.int32, device=dev)
-        hot_pos = _to_device(self._hot_positions.to(torch.int32), dev)
-        return prefill_attention(query, q_pos, self._hot_keys, self._hot_values, hot_pos, self._warm,
+        # the hot rows in buffer order, each with its token's position (order does not matter)
+        hot_pos = _to_device(torch.from_numpy(self._hot_phys_positions().astype(np.int32)), dev)
+        hn = self._hn
+        return prefill_attention(query, q_pos, self._hk[:, :, :hn], self._hv[:, :, :hn], hot_pos, self._warm,
                                  self._slot_pos[: self._warm.n_blocks * BLOCK], sm_scale=sm_scale)
 
     def decode_attention(self, query: torch.Tensor, sm_scale: Optional[float] = None) -> torch.Tensor:
         """One decode query (B, Hq, 1, D) over the packed warm records and the
         FP16 hot tier, in place (akv_mixed_decode).  Returns (B, Hq, 1, D)."""
         from .fused_attention import mixed_tier_decode_attention
+        hk, hv = self._hk[:, :, :self._hn], self._hv[:, :, :self._hn]  # buffer order: attention is order-free
         if isinstance(self._warm, HeadGroupArena):
-            return self._warm.decode(query, self._hot_keys, self._hot_values, sm_scale=sm_scale)
-        return mixed_tier_decode_attention(query, self._hot_keys, self._hot_values, self._warm, sm_scale=sm_scale)
+            return self._warm.decode(query, hk, hv, sm_scale=sm_scale)
+        return mixed_tier_decode_attention(query, hk, hv, self._warm, sm_scale=sm_scale)
 
     # ------------------------------------------------------------------ accounting
     def memory_usage_bytes(self) -> dict:
         """Per-layer byte accounting with the reference's keys (drop_in.py:794-878)."""
         H, D = 1, 128
         hot = 0
-        if self._hot_keys is not None:
-            hot = (self._hot_keys.element_size() * self._hot_keys.numel()
-                   + self._hot_values.element_size() * self._hot_values.numel())
-            H, D = self._hot_keys.shape[1], self._hot_keys.shape[3]
+        if self._hk is not None:
+            B_, H, _, D = self._hk.shape
+            hot = 2 * self._hk.element_size() * B_ * H * self._hn * D
         live = 0
         if self._warm_keys_fp16 is not None:
             live = (self._warm_keys_fp16.element_size() * self._warm_keys_fp16.numel()
@@ -520,7 +704,7 @@ class AKVLayer(_LayerBase):
 
     # ------------------------------------------------------------------ batch ops
     def _select_batch(self, fn) -> None:
-        if self._hot_keys is not None:
+        if self._hk is not None:
             self._hot_keys, self._hot_values = fn(self._hot_keys), fn(self._hot_values)
         if self._warm_keys_fp16 is not None:
             self._warm_keys_fp16, self._warm_values_fp16 = fn(self._warm_keys_fp16), fn(self._warm_values_fp16)
@@ -663,7 +847,7 @@ class AKVCache(_CacheBase):
             layer._select_batch(fn)
             if layer._warm is not None and arena_index is not None:
                 layer._warm.select_batch(arena_index)
-            if layer.keys is not None and layer._hot_keys is not None:
+            if layer.keys is not None and layer._hk is not None:
                 if getattr(layer.keys, "_akv_layer", None) is not None:
                     layer.keys, layer.values = layer._placeholder()
                 else:
@@ -674,8 +858,8 @@ class AKVCache(_CacheBase):
 
     def batch_repeat_interleave(self, repeats: int):
         idx = None
-        if self.layers and self.layers[0]._hot_keys is not None:
-            B = self.layers[0]._hot_keys.shape[0]
+        if self.layers and self.layers[0]._hk is not None:
+            B = self.layers[0]._hk.shape[0]
             idx = torch.arange(B).repeat_interleave(repeats)
         self._each_batch(lambda t: t.repeat_interleave(repeats, dim=0), idx)
         return self
@@ -687,12 +871,12 @@ class AKVCache(_CacheBase):
     def crop(self, max_length: int):
         """Trim the hot tier from the end (drop_in.py:1231-1243)."""
         for layer in self.layers:
-            if layer._hot_keys is not None:
-                cur = layer._hot_keys.shape[2] + layer._warm_len
+            if layer._hk is not None:
+                cur = layer._hn + layer._warm_len
                 if cur > max_length:
-                    keep = max(0, layer._hot_keys.shape[2] - (cur - max_length))
-                    layer._hot_keys = layer._hot_keys[:, :, :keep, :]
-                    layer._hot_values = layer._hot_values[:, :, :keep, :]
+                    keep = max(0, layer._hn - (cur - max_length))
+                    nk, nv = layer._hot_keys[:, :, :keep, :], layer._hot_values[:, :, :keep, :]
+                    layer._hot_keys, layer._hot_values = nk, nv
                     layer._total_len = max_length
 
     def reset(self):
@@ -726,7 +910,7 @@ class AKVCache(_CacheBase):
     def __getitem__(self, layer_idx: int):
         if layer_idx < len(self.layers):
             layer = self.layers[layer_idx]
-            if layer._hot_keys is not None:
+            if layer._hk is not None:
                 wk, wv = layer.warm_fp16()
                 if wk is not None:
                     return (torch.cat([wk, layer._hot_keys], dim=2), torch.cat([wv, layer._hot_values], dim=2))

@@ -383,13 +383,19 @@ AKV_DEV void flush_vout(WarpState& s, int g8, int q4) {
 }
 
 // x[mt][4]: raw logits q.k of this thread's 4 tokens x 2 heads (-inf =
-// masked); p = 2^(x * scale_log2 + nb) overwrites x.  Lazy rescaling: the
-// running max moves (warp-wide max, rescale of acc and l) only when some logit
-// of the block exceeds it by more than lazy_raw = kLazyMax / scale_log2;
-// otherwise p <= 2^kLazyMax, far inside fp16 and fp32 range, and the block
-// costs no shuffles.  acc / l and -nb + log2(l) do not depend on which
-// offset was used.  scale_log2 > 0, so a masked -inf logit gives p = 0.
-constexpr float kLazyMax = 8.f;
+// masked); p = 2^(x * scale_log2 + nb) overwrites x.  The running max moves
+// (warp-wide max, rescale of acc and l) whenever some logit of the block
+// exceeds it by more than lazy_raw = kLazyMax / scale_log2, otherwise the
+// block costs no shuffles.  kLazyMax = 0: the offset is always the exact
+// running max, so the largest weight so far is exactly 1 when P is rounded to
+// fp16 for the P.V product.  A lazy offset (weights up to 2^8) saves ~3 % of
+// the config-3 step but rounds the dominant weight too, and where one key
+// carries a row that rounding (2^-11 relative) shows in the output: measured
+// 2.2e-3 against fp32 attention on a random-init model's decode, twice the
+// error of flash attention over the same fp16 view, which keeps the exact
+// max.  acc / l and -nb + log2(l) do not depend on which offset was used.
+// scale_log2 > 0, so a masked -inf logit gives p = 0.
+constexpr float kLazyMax = 0.f;
 
 AKV_DEV void online_softmax(WarpState& s, float (&x)[2][4], float sl2, float lazy_raw) {
   float mx[2];
@@ -921,6 +927,9 @@ __global__ void __launch_bounds__(kCombineThreads) lse_combine_kernel(const floa
   __shared__ float w[kCombineMaxSplits];
   __shared__ float acc[kCombineGroups][kCombineChunk];
   __shared__ float sM, sL;
+  // launched as a programmatic dependent of the decode kernel: wait until that
+  // grid has completed and its partials are visible (a no-op otherwise)
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int r = blockIdx.x;
   if (r >= rows) return;
   const float* base = part + static_cast<int64_t>(r) * sr;
@@ -981,6 +990,27 @@ __global__ void __launch_bounds__(kCombineThreads) lse_combine_kernel(const floa
 }
 
 static dim3 combine_grid(int rows, int D) { return dim3(rows, (D + kCombineChunk - 1) / kCombineChunk); }
+
+// The split merge of a decode launch, as a programmatic dependent launch: the
+// GPU processes its launch while the decode kernel is still running, and its
+// griddepcontrol.wait holds it until the decode grid's partials are complete.
+static int launch_combine_dependent(const float* part, int64_t ss, int64_t sr, int rows, int splits, int D,
+                                    __half* out, int64_t o_sr, float* lse, float* merged, cudaStream_t st) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = combine_grid(rows, D);
+  cfg.blockDim = dim3(kCombineThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, lse_combine_kernel, part, ss, sr, rows, splits, D, out, o_sr, lse, merged) ==
+                 cudaSuccess
+             ? AKV_OK
+             : AKV_ERR_LAUNCH;
+}
 
 // ------------------------------------------------------------------ host side
 struct DecodePlan {
@@ -1216,9 +1246,8 @@ static int decode_impl(const uint16_t* q, int64_t q_sb, int64_t q_sh, const uint
     default: rc = launch_decode<4, 4>(p, st); break;
   }
   if (rc != AKV_OK) return rc;
-  lse_combine_kernel<<<combine_grid(B * Hq, D), kCombineThreads, 0, st>>>(ws, D + 2, static_cast<int64_t>(pl.splits) * (D + 2), B * Hq,
-                                             pl.splits, D, outh, o_sh, lse, partial_out);
-  return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_LAUNCH;
+  return launch_combine_dependent(ws, D + 2, static_cast<int64_t>(pl.splits) * (D + 2), B * Hq, pl.splits, D, outh,
+                                  o_sh, lse, partial_out, st);
 }
 
 extern "C" int akv_mixed_decode(const uint16_t* q, int64_t q_sb, int64_t q_sh, const uint16_t* hot_k,

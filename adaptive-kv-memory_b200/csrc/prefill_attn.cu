@@ -491,6 +491,7 @@ __global__ void __launch_bounds__(kThreads, 2) prefill_kernel(const Params p, co
   // of the window (32 loads per thread in flight) and ORs the per-tile flags
   int win = -1;
   auto scan = [&](int c0) {
+    __syncthreads();  // every thread has read the previous window's flags before they are cleared
     if (t == 0) s_vis = s_notfull = 0u;
     __syncthreads();
     int kp[kScanTiles];

@@ -668,10 +668,78 @@ def hf_decode_bench(torch, akv, dev, new_tokens: int = 256, prompt: int = 32768)
         res[f"{mode}_prefill_ms"] = round(pre_ms, 1)
     model.config._attn_implementation = "sdpa"
     res["greedy_match_fused_vs_view"] = round((toks["view"] == toks["fused"]).float().mean().item(), 4)
+    res["teacher_forced"] = hf_parity_leg(torch, akv, model, ids, toks, make_cache, sdpa_backends)
     res["speedup_fused_vs_view"] = round(res["fused_tok_s"] / res["view_tok_s"], 3)
     res = {"workload": f"qwen2.5-1.5b-shaped random-init decoder, prompt {prompt}, greedy {new_tokens} tokens, "
                        "batch 1, AKVCache 3-bit warm + 1024 hot (promotion off)", **res}
     del model
+    torch.cuda.empty_cache()
+    return res
+
+
+def hf_parity_leg(torch, akv, model, ids, toks, make_cache, sdpa_backends) -> dict:
+    """Teacher-forced decoding of the view arm's greedy tokens through the view
+    (reference data flow) and fused arms: the max logit difference over the
+    steps; the first step where the two greedy runs diverged, with the view
+    arm's top-1 / top-2 logit margin there and the fused arm's logit error at
+    that step; and, at that step, each layer's max attention error against
+    fp32 SDPA over the same layer's chronological view, for both arms."""
+    from torch.nn.attention import sdpa_kernel
+    from transformers import AttentionInterface
+    from transformers.integrations.sdpa_attention import sdpa_attention_forward
+    import akv.hf_attention as hook
+    forced = toks["view"]
+    diff = (toks["view"] != toks["fused"]).nonzero()
+    first = int(diff[0, 1].item()) if diff.numel() else None
+    probe = {"step": first, "errs": {}, "on": False}
+
+    def checked(mode):
+        def fn(module, query, key, value, attention_mask, **kw):
+            if mode == "fused":
+                out, w = hook.akv_attention_forward(module, query, key, value, attention_mask, **kw)
+            else:
+                out, w = sdpa_attention_forward(module, query, key, value, attention_mask, **kw)
+            if probe["on"] and query.shape[2] == 1:
+                layer = getattr(key, "_akv_layer", None)
+                fk, fv = layer.full_view() if layer is not None else (key, value)
+                ref, _ = sdpa_attention_forward(module, query.float(), fk.float(), fv.float(), None,
+                                                scaling=kw.get("scaling"))
+                e = (out.float() - ref).abs().max().item()
+                probe["errs"].setdefault(mode, []).append(e)
+            return out, w
+        return fn
+
+    from transformers.masking_utils import AttentionMaskInterface, sdpa_mask
+    AttentionMaskInterface.register("akv_parity", sdpa_mask)
+    logits = {}
+    for mode in ("view", "fused"):
+        AttentionInterface.register("akv_parity", checked(mode))
+        cache = make_cache(mode)
+        model.config._attn_implementation = "akv_parity"  # (make_cache picks the arm's own implementation)
+        rows = []
+        with torch.no_grad(), sdpa_kernel(sdpa_backends):
+            out = model(input_ids=ids, past_key_values=cache, use_cache=True, logits_to_keep=1)
+            rows.append(out.logits[:, -1].float())
+            for i in range(forced.shape[1] - 1):
+                probe["on"] = first is not None and i + 1 == first  # logits of step i+1 predict token i+1
+                out = model(input_ids=forced[:, i:i + 1], past_key_values=cache, use_cache=True, logits_to_keep=1)
+                probe["on"] = False
+                rows.append(out.logits[:, -1].float())
+        logits[mode] = torch.cat(rows)
+        del cache
+    AttentionInterface.register("akv_parity", hook.akv_attention_forward)
+    model.config._attn_implementation = "sdpa"
+    lv, lf = logits["view"], logits["fused"]
+    res = {"forced_tokens": int(forced.shape[1]), "max_logit_diff": round((lv - lf).abs().max().item(), 4),
+           "max_abs_logit": round(lv.abs().max().item(), 3), "first_divergence_step": first}
+    if first is not None:
+        top2 = lv[first].topk(2).values
+        res["view_top2_margin_at_divergence"] = round((top2[0] - top2[1]).item(), 5)
+        res["logit_diff_at_divergence"] = round((lv[first] - lf[first]).abs().max().item(), 5)
+        for mode in ("view", "fused"):
+            e = probe["errs"].get(mode, [])
+            res[f"{mode}_layer_attn_err_vs_fp32_max"] = round(max(e), 6) if e else None
+        res["layers_probed"] = len(probe["errs"].get("fused", []))
     torch.cuda.empty_cache()
     return res
 
