@@ -157,7 +157,10 @@ class AKVLayer(_LayerBase):
         self._warm_bytes_packed = 0
         self._proxy_score: Optional[torch.Tensor] = None
         self._hot_positions: Optional[torch.Tensor] = None
-        self._warm_positions: Optional[torch.Tensor] = None
+        # positions of the warm tokens in warm order: the front of a host
+        # capacity buffer (an append writes only the new entries)
+        self._wpos_buf = np.zeros(64, dtype=np.int64)
+        self._wpos_n = 0
         self._importance: Optional[torch.Tensor] = None
         self._decay = 0.3
         self._n_anchors = 16
@@ -341,6 +344,27 @@ class AKVLayer(_LayerBase):
                                             + 4 * H * n)
         if not self._no_fp16_copy:
             self._append_warm_fp16(*arena.dequantize(tok_idx=_to_device(torch.from_numpy(slots), hk.device)))
+
+    @property
+    def _warm_positions(self) -> Optional[torch.Tensor]:
+        """Positions of the warm tokens in warm order (CPU int64, a view of the host buffer)."""
+        return torch.from_numpy(self._wpos_buf[:self._wpos_n]) if self._wpos_n else None
+
+    @_warm_positions.setter
+    def _warm_positions(self, t: Optional[torch.Tensor]) -> None:
+        arr = np.zeros(0, np.int64) if t is None else np.asarray(t.numpy() if isinstance(t, torch.Tensor) else t,
+                                                                  dtype=np.int64)
+        self._wpos_buf = np.array(arr, dtype=np.int64)
+        self._wpos_n = arr.shape[0]
+
+    def _wpos_append(self, pos: np.ndarray) -> None:
+        n = self._wpos_n + pos.shape[0]
+        if n > self._wpos_buf.shape[0]:
+            nb = np.empty(max(2 * n, 64), dtype=np.int64)
+            nb[:self._wpos_n] = self._wpos_buf[:self._wpos_n]
+            self._wpos_buf = nb
+        self._wpos_buf[self._wpos_n:n] = pos
+        self._wpos_n = n
 
     @property
     def _wslots(self) -> np.ndarray:
@@ -591,7 +615,11 @@ class AKVLayer(_LayerBase):
         if hot_len > budget:
             n_demote = hot_len - budget
             d_np = self._select_demote_indices(n_demote, hot_len).numpy()
-            kept_np = np.delete(np.arange(hot_len, dtype=np.int64), d_np)
+            if n_demote == 1:  # one index: two slices are much cheaper than np.delete
+                v0 = int(d_np[0])
+                kept_np = np.concatenate((np.arange(v0, dtype=np.int64), np.arange(v0 + 1, hot_len, dtype=np.int64)))
+            else:
+                kept_np = np.delete(np.arange(hot_len, dtype=np.int64), d_np)
             hp = self._hot_positions.numpy()
             phys = self._phys if self._phys is not None else np.arange(self._hn, dtype=np.int64)
             if fast and int(d_np[0]) == hot_len - 1:  # the new token itself: append it, then demote
@@ -600,7 +628,7 @@ class AKVLayer(_LayerBase):
                 fast = False
             rows = phys[d_np]
             self._demote(rows, hp[d_np])
-            self._append_1d("_warm_positions", torch.from_numpy(hp[d_np]))
+            self._wpos_append(hp[d_np])
             self._warm_len += n_demote
             if self._proxy_score is not None:
                 pad = torch.zeros(n_demote, dtype=self._proxy_score.dtype, device=self._warm_keys_fp16.device)
@@ -609,13 +637,19 @@ class AKVLayer(_LayerBase):
                 r = int(rows[0])
                 self._hk[:, :, r:r + 1].copy_(key_states)
                 self._hv[:, :, r:r + 1].copy_(value_states)
-                new_phys = np.append(np.delete(phys, d_np), r)
+                new_phys = np.concatenate((phys[:v0], phys[v0 + 1:], np.array([r], dtype=np.int64)))
                 self._phys = None if np.array_equal(new_phys, np.arange(self._hn)) else new_phys
             else:
                 self._hot_remove(rows, kept_np)
-            self._hot_positions = torch.from_numpy(hp[kept_np])
-            if self._importance is not None:
-                self._importance = torch.from_numpy(self._importance.numpy()[kept_np])
+            if n_demote == 1:
+                self._hot_positions = torch.from_numpy(np.concatenate((hp[:v0], hp[v0 + 1:])))
+                if self._importance is not None:
+                    imp = self._importance.numpy()
+                    self._importance = torch.from_numpy(np.concatenate((imp[:v0], imp[v0 + 1:])))
+            else:
+                self._hot_positions = torch.from_numpy(hp[kept_np])
+                if self._importance is not None:
+                    self._importance = torch.from_numpy(self._importance.numpy()[kept_np])
         elif fast:  # nothing to demote after all (a promotion path made room): append normally
             self._hot_append(key_states, value_states)
 
