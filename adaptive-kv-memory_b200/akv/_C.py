@@ -66,6 +66,13 @@ SIGNATURES = {
                                c_int, c_int, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p]),
     "akv_int4_group_dequant": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int64,
                                        c_int, c_int, c_int, c_int, c_void_p, c_int64, c_int64, c_void_p]),
+    "akv_group_dequant": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int64,
+                                  c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int64, c_int64, c_void_p]),
+    "akv_group_quantize": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int, c_int, c_int, c_int, c_void_p,
+                                   c_int64, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "akv_attention_probs": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64, c_int64,
+                                    c_void_p, c_int, c_int, c_int, c_int, c_int, c_float, c_void_p, c_int64,
+                                    c_int64, c_int64, c_int, c_void_p]),
     "akv_decode_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int, c_int]),
     "akv_mixed_decode": (c_int, [c_void_p, c_int64, c_int64,
                                  c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int, c_void_p,
@@ -93,6 +100,7 @@ SIGNATURES = {
                                       c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p]),
     "akv_lse_combine": (c_int, [c_void_p, c_int64, c_int64, c_int, c_int, c_int, c_void_p, c_int64, c_void_p,
                                 c_void_p, c_void_p]),
+    "akv_set_reduction_width": (c_int, [c_int]),
     "akv_importance_update": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int, c_float, c_void_p]),
     "akv_migrator_update": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int,
                                     c_int64, c_float, c_void_p]),
@@ -102,6 +110,9 @@ SIGNATURES = {
     "akv_select_bottomk": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_size_t, c_void_p]),
     "akv_gather_rows": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p, c_int, c_int, c_int,
                                 c_int64, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p]),
+    "akv_scatter_rows": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int, c_int,
+                                 c_int, c_int64, c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p]),
+    "akv_selftest_wait": (c_int, [c_int, c_int64, c_void_p, c_void_p, c_void_p]),
     "akv_cold_copy": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int64, c_int, c_void_p, c_void_p]),
 }
 
@@ -127,8 +138,21 @@ def load():
         fn = getattr(lib, name)
         fn.restype = res
         fn.argtypes = args
+    lib.akv_set_reduction_width(cpu_reduction_width())
     _lib = lib
     return lib
+
+
+def cpu_reduction_width() -> int:
+    """Floats per SIMD register torch's CPU kernels use on this host (16 with
+    AVX-512, 8 otherwise): the importance sums follow the reference's torch
+    CPU reduction order on the same machine."""
+    import torch
+    try:
+        cap = torch.backends.cpu.get_cpu_capability()
+    except Exception:
+        cap = ""
+    return 16 if "AVX512" in str(cap).upper() else 8
 
 
 def strerror(rc: int) -> str:

@@ -40,6 +40,7 @@ import torch
 from . import _C
 from .bitpack import packed_width
 from .packed_layout import BLOCK, HeadGroupArena, WarmArena
+from .tiering import gather_rows, scatter_rows
 
 logger = logging.getLogger(__name__)
 
@@ -264,9 +265,7 @@ class AKVLayer(_LayerBase):
                 self._hv[:, :, h].copy_(self._hv[:, :, m])
             else:
                 idx = _to_device(torch.from_numpy(np.concatenate([movers, holes])), dev)
-                src, dst = idx[:movers.size], idx[movers.size:]
-                self._hk.index_copy_(2, dst, self._hk.index_select(2, src))
-                self._hv.index_copy_(2, dst, self._hv.index_select(2, src))
+                self._move_rows(idx[:movers.size], idx[movers.size:])
             remap = np.arange(self._hn, dtype=np.int64)
             remap[movers] = holes
             new_phys = remap[phys[kept_logical]]
@@ -274,6 +273,15 @@ class AKVLayer(_LayerBase):
             new_phys = phys[kept_logical]
         self._hn = new_n
         self._phys = None if np.array_equal(new_phys, np.arange(new_n)) else new_phys
+
+    def _move_rows(self, src: torch.Tensor, dst: torch.Tensor) -> None:
+        """Ring rows src -> rows dst (disjoint sets) in both buffers, one row-scatter launch each."""
+        if self._hk.stride(-1) == 1 and (self._hk.shape[-1] * self._hk.element_size()) % 16 == 0:
+            scatter_rows(self._hk, self._hk, dst, src)
+            scatter_rows(self._hv, self._hv, dst, src)
+        else:
+            self._hk.index_copy_(2, dst, self._hk.index_select(2, src))
+            self._hv.index_copy_(2, dst, self._hv.index_select(2, src))
 
     def _hot_phys_positions(self) -> np.ndarray:
         """Position of the token in each buffer row [0, _hn)."""
@@ -503,15 +511,27 @@ class AKVLayer(_LayerBase):
         proxy update then restarts the EMA on the length mismatch)."""
         warm_len = self._warm_keys_fp16.shape[2]
         promote_idx = promote_mask.nonzero(as_tuple=True)[0]
-        promoted_k = self._warm_keys_fp16[:, :, promote_idx, :]
-        promoted_v = self._warm_values_fp16[:, :, promote_idx, :]
         promoted_pos = self._warm_positions[promote_idx.detach().to("cpu")] if self._warm_positions is not None else None
+        wk = self._warm_keys_fp16
+        if self._hk is not None and wk.stride(-1) == 1 and (wk.shape[-1] * wk.element_size()) % 16 == 0:
+            # promoted rows go to free ring rows [hn, hn + n) by the row
+            # gather and to the front of the logical order
+            hn = self._hn
+            self._hot_reserve(hn + n_promote)
+            gather_rows(self._warm_keys_fp16, promote_idx, out=self._hk[:, :, hn:hn + n_promote])
+            gather_rows(self._warm_values_fp16, promote_idx, out=self._hv[:, :, hn:hn + n_promote])
+            old = self._phys if self._phys is not None else np.arange(hn, dtype=np.int64)
+            self._phys = np.concatenate([np.arange(hn, hn + n_promote, dtype=np.int64), old])
+            self._hn = hn + n_promote
+        else:
+            promoted_k = self._warm_keys_fp16[:, :, promote_idx, :]
+            promoted_v = self._warm_values_fp16[:, :, promote_idx, :]
+            nk = torch.cat([promoted_k, self._hot_keys], dim=2)
+            nv = torch.cat([promoted_v, self._hot_values], dim=2)
+            self._hot_keys, self._hot_values = nk, nv
         if filter_proxy:
             self._proxy_score = self._proxy_score[~promote_mask]
         self._remove_warm(promote_mask, n_promote, warm_len)
-        nk = torch.cat([promoted_k, self._hot_keys], dim=2)
-        nv = torch.cat([promoted_v, self._hot_values], dim=2)
-        self._hot_keys, self._hot_values = nk, nv
         if promoted_pos is not None and self._hot_positions is not None:
             self._hot_positions = torch.cat([promoted_pos, self._hot_positions])
         if self._importance is not None:

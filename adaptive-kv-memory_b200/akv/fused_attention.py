@@ -277,3 +277,45 @@ def prefill_attention(query: torch.Tensor, q_pos: torch.Tensor,
         _C.ptr(status), _C.stream_of(query))
     _C.check(rc, "akv_prefill_attention")
     return (o, lse) if return_lse else o
+
+
+# ---------------------------------------------------------------------------- compatibility entry points
+def _dequantize_any(qt, quantizer) -> torch.Tensor:
+    """A group-format quantised tensor (the reference's ``QuantizedTensor``
+    fields: data, scales, zeros, shape, bits, group_size) dequantised by the
+    CUDA kernel; anything else through ``quantizer.dequantize``."""
+    fields = ("data", "scales", "zeros", "shape", "bits", "group_size")
+    if all(hasattr(qt, f) for f in fields) and qt.data.is_cuda:
+        from .group_format import group_dequantize
+        shape = tuple(qt.shape)
+        rows = int(math.prod(shape[:-1]))
+        return group_dequantize(qt.data, qt.scales, qt.zeros, qt.bits, qt.group_size, rows, shape[-1]).reshape(shape)
+    return quantizer.dequantize(qt)
+
+
+def fused_decode_attention(query: torch.Tensor, keys_quantized, values_quantized, quantizer) -> torch.Tensor:
+    """Reference compatibility wrapper (akv/fused_attention.py:373-390):
+    decode attention of (B, H, 1, D) queries over quantised K / V of shape
+    (B, H, N, D).  The tiers are dequantised (on CUDA for the group format)
+    and attended by the decode kernel as one FP16 tier."""
+    k = _dequantize_any(keys_quantized, quantizer).to(torch.float16)
+    v = _dequantize_any(values_quantized, quantizer).to(torch.float16)
+    B, H, _, D = query.shape
+    if k.stride(-1) != 1 or k.stride() != v.stride():
+        k, v = k.contiguous(), v.contiguous()
+    out = mixed_tier_decode_attention(query.to(torch.float16), k, v, sm_scale=1.0 / math.sqrt(D))
+    return out.to(query.dtype)
+
+
+def fused_quantize_evict(keys: torch.Tensor, values: torch.Tensor, scores, evict_mask: torch.Tensor, quantizer):
+    """Reference compatibility wrapper (akv/fused_attention.py:393-401): the
+    tokens (dim 2 of (B, H, N, D) keys / values) where ``evict_mask`` is True,
+    gathered by the row-gather kernel and passed to ``quantizer.quantize``.
+    Returns (quantised keys, quantised values), or (None, None)."""
+    from .tiering import gather_rows
+    idx = evict_mask.nonzero(as_tuple=True)[0]
+    if idx.numel() == 0:
+        return None, None
+    k_evict = gather_rows(keys, idx)
+    v_evict = gather_rows(values, idx)
+    return quantizer.quantize(k_evict), quantizer.quantize(v_evict)

@@ -111,22 +111,35 @@ def local_partial(query: torch.Tensor, hot_keys: Optional[torch.Tensor], hot_val
     return p
 
 
-def combine_partials(part: torch.Tensor) -> torch.Tensor:
-    """(rows, splits, D+2) partial records -> (rows, D) fp16 via the LSE combine kernel."""
+def combine_partials(part: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """(rows, splits, D+2) partial records -> (rows, D) fp16 via the LSE combine kernel.
+
+    Any row / split strides with a contiguous last dim are read in place, so
+    the all-gather's (world, rows, D+2) buffer passes as
+    ``gathered.permute(1, 0, 2)`` without a copy."""
     _C.require_cuda(part)
-    part = part.contiguous()
+    if part.stride(-1) != 1:
+        part = part.contiguous()
     rows, splits, D2 = part.shape
     D = D2 - 2
-    out = torch.empty(rows, D, dtype=torch.float16, device=part.device)
-    _C.check(_C.load().akv_lse_combine(part.data_ptr(), D2, part.stride(0), rows, splits, D, out.data_ptr(), D,
-                                       None, None, _C.stream_of(part)), "akv_lse_combine")
+    if out is None:
+        out = torch.empty(rows, D, dtype=torch.float16, device=part.device)
+    _C.check(_C.load().akv_lse_combine(part.data_ptr(), part.stride(1), part.stride(0), rows, splits, D,
+                                       out.data_ptr(), out.stride(0), None, None, _C.stream_of(part)),
+             "akv_lse_combine")
     return out
 
 
 def _all_gather(t: torch.Tensor, world: int, group=None) -> torch.Tensor:
+    """(world, *t.shape): one all_gather_into_tensor on NCCL, a list all_gather elsewhere."""
     import torch.distributed as dist
+    t = t.contiguous()
+    if t.is_cuda:
+        out = torch.empty((world,) + tuple(t.shape), dtype=t.dtype, device=t.device)
+        dist.all_gather_into_tensor(out, t, group=group)
+        return out
     outs = [torch.empty_like(t) for _ in range(world)]
-    dist.all_gather(outs, t.contiguous(), group=group)
+    dist.all_gather(outs, t, group=group)
     return torch.stack(outs)
 
 
@@ -144,7 +157,7 @@ def sequence_split_decode(query: torch.Tensor, hot_keys: Optional[torch.Tensor],
     all_gather = all_gather or (lambda t: _all_gather(t, world, process_group))
     combine = combine or combine_partials
     p = partial(query, hot_keys, hot_values, warm, sm_scale)
-    gathered = all_gather(p)                       # (world, rows, D+2)
-    part = gathered.permute(1, 0, 2).contiguous()  # (rows, world, D+2)
+    gathered = all_gather(p)           # (world, rows, D+2)
+    part = gathered.permute(1, 0, 2)   # (rows, world, D+2), a strided view
     q3 = query.reshape(query.shape[0], query.shape[1], query.shape[-1])
     return combine(part).reshape(q3.shape)

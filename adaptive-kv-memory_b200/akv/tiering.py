@@ -83,6 +83,32 @@ def gather_rows(x: torch.Tensor, idx: torch.Tensor, out: torch.Tensor | None = N
     return out
 
 
+def scatter_rows(src: torch.Tensor, dst: torch.Tensor, dst_idx: torch.Tensor, src_idx: torch.Tensor | None = None,
+                 status: torch.Tensor | None = None) -> torch.Tensor:
+    """dst[b, h, dst_idx[i]] = src[b, h, src_idx[i] if given else i] for (B, H, N, D) tensors.
+
+    Rows read and rows written must not overlap (src may be dst).  An index
+    outside its tensor's rows records AKV_ERR_SHAPE in ``status`` and uses
+    row 0."""
+    _C.require_cuda(src, dst, dst_idx, src_idx)
+    B, H, n_src, D = src.shape
+    if dst.shape[:2] != (B, H) or dst.shape[3] != D or dst.dtype != src.dtype:
+        raise ValueError("src and dst need the same (B, H, *, D) shape and dtype")
+    if src.stride(-1) != 1 or dst.stride(-1) != 1:
+        raise ValueError("rows must be contiguous")
+    es = src.element_size()
+    di = dst_idx.to(torch.int64).contiguous()
+    si = src_idx.to(torch.int64).contiguous() if src_idx is not None else None
+    n = di.shape[0]
+    if si is not None and si.shape[0] != n:
+        raise ValueError("src_idx and dst_idx lengths differ")
+    _C.check(_C.load().akv_scatter_rows(src.data_ptr(), src.stride(0) * es, src.stride(1) * es, src.stride(2) * es,
+                                        n_src, _C.ptr(si), di.data_ptr(), n, B, H, D * es, dst.data_ptr(),
+                                        dst.stride(0) * es, dst.stride(1) * es, dst.stride(2) * es, dst.shape[2],
+                                        _C.ptr(status), _C.stream_of(src)), "akv_scatter_rows")
+    return dst
+
+
 def cold_copy_blocks(arena_buf: torch.Tensor, blk0: int, nblk: int, host: torch.Tensor,
                      stream: torch.cuda.Stream | None = None) -> torch.cuda.Event:
     """Copy warm records [blk0, blk0+nblk) of every (b, h) to a pinned host buffer (B, H, nblk, rec)."""

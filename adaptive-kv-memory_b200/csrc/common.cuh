@@ -136,12 +136,13 @@ AKV_DEV uint64_t global_timer_ns() {
 }
 
 // Bounded wait: returns false (and records a timeout) if the phase does not
-// complete within kWaitLimitNs.
-AKV_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int* status) {
+// complete within limit_ns (kWaitLimitNs in every kernel; the self-test entry
+// akv_selftest_wait passes a short one).
+AKV_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   while (!mbar_try_wait(bar, parity)) {
-    if (global_timer_ns() - t0 > kWaitLimitNs) {
+    if (global_timer_ns() - t0 > limit_ns) {
       set_status(status, AKV_ERR_TIMEOUT);
       return false;
     }
@@ -154,7 +155,7 @@ AKV_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int* status) {
 AKV_DEV void fence_proxy_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // 1-D bulk TMA copy global -> shared, completion counted on an mbarrier.
-// dst/src 16-byte aligned, bytes a multiple of 16.  No multicast.
+// dst/src 16-byte aligned, bytes a multiple of 16.  One CTA only.
 AKV_DEV void tma_load_1d(void* dst_smem, const void* src_gmem, uint32_t bytes, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(

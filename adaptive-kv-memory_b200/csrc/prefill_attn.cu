@@ -21,7 +21,7 @@
 //                 memory, V read MN-major from shared memory, O accumulated in
 //                 tensor memory
 // Q and hot K/V tiles arrive by tensor TMA (cp.async.bulk.tensor, this GPU's
-// memory only, no multicast); warm tiles are dequantised by the CTA's threads.
+// memory only, one CTA per copy); warm tiles are dequantised by the CTA's threads.
 // Two CTAs fit on an SM (96 KB of tiles, 256 TMEM columns each), so one CTA's
 // MMAs overlap the other's softmax and dequantisation.
 //

@@ -958,39 +958,6 @@ __global__ void dequantize_kernel(const DequantParams p) {
 }
 
 // ---------------------------------------------------------------------------
-// INT4 per-token, per-D-group affine layout of the reference's
-// fused_int4_decode_attention / mixed_precision_decode_attention
-// (akv/fused_attention.py:293-317): byte j of a row holds channel 2j in the
-// high nibble and 2j+1 in the low one; value = fp16(fp32(fp32(c*s) + z)) with
-// (s, z) of group d / group_size.  One thread per 8 channels of one token.
-// ---------------------------------------------------------------------------
-__global__ void int4_group_dequant_kernel(const uint8_t* packed, int64_t p_sh, int64_t p_sn, const __half* sc,
-                                          const __half* zr, int64_t s_sh, int64_t s_sn, int H, int N, int D,
-                                          int gsize, __half* out, int64_t o_sh, int64_t o_sn) {
-  const int nc = D / 8;
-  const int64_t total = static_cast<int64_t>(H) * N * nc;
-  for (int64_t w = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; w < total;
-       w += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int c8 = static_cast<int>(w % nc);
-    const int64_t r = w / nc;
-    const int n = static_cast<int>(r % N), h = static_cast<int>(r / N);
-    const uint32_t word = *reinterpret_cast<const uint32_t*>(packed + h * p_sh + n * p_sn + 4 * c8);
-    const __half* srow = sc + h * s_sh + n * s_sn;
-    const __half* zrow = zr + h * s_sh + n * s_sn;
-    __align__(16) __half o[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int d = 8 * c8 + i;
-      const uint32_t byte = (word >> (8 * (i / 2))) & 0xFFu;
-      const float c = static_cast<float>((i & 1) ? (byte & 15u) : (byte >> 4));
-      const int g = d / gsize;
-      o[i] = __float2half_rn(__fadd_rn(__fmul_rn(c, __half2float(srow[g])), __half2float(zrow[g])));
-    }
-    *reinterpret_cast<uint4*>(out + h * o_sh + n * o_sn + 8 * c8) = *reinterpret_cast<const uint4*>(o);
-  }
-}
-
-// ---------------------------------------------------------------------------
 // standalone bit packing (akv/bitpack.py), any row width, zero right-padding
 // ---------------------------------------------------------------------------
 __global__ void pack_codes_kernel(const uint8_t* codes, int64_t rows, int dim, int bits, uint8_t* out) {
@@ -1291,21 +1258,6 @@ extern "C" int akv_unpack_codes(const uint8_t* packed, int64_t rows, int dim, in
   const int64_t blocks = std::min<int64_t>((total + 255) / 256, 148 * 16);
   unpack_codes_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       packed, rows, dim, bits, codes);
-  return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_LAUNCH;
-}
-
-extern "C" int akv_int4_group_dequant(const uint8_t* packed, int64_t p_sh, int64_t p_sn, const uint16_t* scales,
-                                      const uint16_t* zeros, int64_t s_sh, int64_t s_sn, int H, int N, int D,
-                                      int group_size, uint16_t* out, int64_t o_sh, int64_t o_sn, void* stream) {
-  if (!packed || !scales || !zeros || !out) return AKV_ERR_NULL;
-  if (H <= 0 || N < 0 || D <= 0 || D % 8 != 0 || group_size <= 0) return AKV_ERR_SHAPE;
-  if (N == 0) return AKV_OK;
-  if (!aligned(packed, 4) || p_sh % 4 || p_sn % 4 || !aligned(out, 16) || o_sh % 8 || o_sn % 8) return AKV_ERR_ALIGN;
-  const int64_t total = static_cast<int64_t>(H) * N * (D / 8);
-  const int64_t blocks = std::min<int64_t>((total + 255) / 256, 148 * 16);
-  int4_group_dequant_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      packed, p_sh, p_sn, reinterpret_cast<const __half*>(scales), reinterpret_cast<const __half*>(zeros), s_sh,
-      s_sn, H, N, D, group_size, reinterpret_cast<__half*>(out), o_sh, o_sn);
   return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_LAUNCH;
 }
 

@@ -12,68 +12,160 @@ namespace akv {
 // importance update (akv/triton_ops.py:604-650, CPU branch semantics)
 //   imp[n]    = sum_m ( sum_{b,h} attn[b,h,m,n] / (B*H) )
 //   scores[n] = fl(fl(scores[n] * decay) + imp[n])
-// Per column n the (b,h) sum runs in order, like a sequential reduction of
-// the reference's mean over dims (0, 1).
+//
+// Both sums add in the order of torch's CPU reduction of a contiguous tensor
+// over its outer dimension (the reference's attention_weights.float()
+// .mean(dim=(0, 1)).sum(dim=0); the restated ordering is PyTorch's
+// cascade_sum / multi_row_sum / row_sum in aten/src/ATen/native/cpu/
+// SumKernel.cpp, BSD licence):
+//  * a column whose index lies below the last multiple of twice the CPU
+//    vector width `vw` (floats per SIMD register of the machine running the
+//    reference: 16 with AVX-512, 8 with AVX2; torch sums those columns in
+//    blocks of four and two registers) sums its R rows in "cascade"
+//    order: with lp = max(4, ceil(log2(R)) / 4), the rows are added one by
+//    one to level 0; after every 2^lp rows level 0 is added to level 1 (and
+//    cleared), level 1 to level 2 when the row count is a multiple of 2^(2lp),
+//    level 2 to level 3 at multiples of 2^(3lp); at the end the levels are
+//    added in order 0 + 1 + 2 + 3;
+//  * the remaining columns (one register's worth and the scalar tail) sum
+//    four interleaved cascades (rows
+//    4i + k, i < R/4) with the last R % 4 rows added to cascade 0, then
+//    cascades 1, 2, 3 added to it in order.
+// The mean divides the (b, h) sum by B*H (sum, then a true division, as
+// torch's CPU mean does).  The flattened (m, n) column index decides the
+// order of the (b, h) sum, n alone that of the sum over m.
 // ---------------------------------------------------------------------------
-// attention received by positions n0 .. n0+W-1:
-//   imp[w] = sum_m fl(fl(sum_{bh} attn[bh, m, n0+w]) / (B*H)), the (b,h) sum in
-// order.  W = 4: 16-byte loads (n0 a multiple of 4, rows 16-byte aligned);
-// eight (b,h) rows are loaded before they are added, so a thread keeps
-// several loads in flight while the additions keep their order.
-template <int W>
-AKV_DEV void attn_received(const float* __restrict__ attn, int BH, int M, int Na, int n0, float (&imp)[W]) {
-  const float cnt = static_cast<float>(BH);
-#pragma unroll
-  for (int w = 0; w < W; ++w) imp[w] = 0.f;
-  for (int m = 0; m < M; ++m) {
-    float s[W];
-#pragma unroll
-    for (int w = 0; w < W; ++w) s[w] = 0.f;
-    const float* col = attn + static_cast<int64_t>(m) * Na + n0;
-    const int64_t rs = static_cast<int64_t>(M) * Na;  // stride between (b,h) rows
-    int bh = 0;
-    for (; bh + 8 <= BH; bh += 8) {
-      float v[8][W];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        if constexpr (W == 4) {
-          const float4 f = __ldg(reinterpret_cast<const float4*>(col + (bh + j) * rs));
-          v[j][0] = f.x;
-          v[j][1] = f.y;
-          v[j][2] = f.z;
-          v[j][3] = f.w;
-        } else {
-          v[j][0] = __ldg(col + (bh + j) * rs);
+struct TorchCascade {
+  float acc[4];
+  int i, lp, mask;
+  AKV_DEV void init(int size) {
+    int cl = 0;
+    while ((1 << cl) < size) ++cl;  // ceil(log2(size)), 0 for size <= 1
+    lp = cl / 4 > 4 ? cl / 4 : 4;
+    mask = (1 << lp) - 1;
+    i = 0;
+    acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+  }
+  AKV_DEV void push(float v) {
+    acc[0] = __fadd_rn(acc[0], v);
+    if ((++i & mask) == 0) {  // a full step of 2^lp rows
+      acc[1] = __fadd_rn(acc[1], acc[0]);
+      acc[0] = 0.f;
+      if ((i & (mask << lp)) == 0) {
+        acc[2] = __fadd_rn(acc[2], acc[1]);
+        acc[1] = 0.f;
+        if ((i & (mask << (2 * lp))) == 0) {
+          acc[3] = __fadd_rn(acc[3], acc[2]);
+          acc[2] = 0.f;
         }
       }
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-#pragma unroll
-        for (int w = 0; w < W; ++w) s[w] = __fadd_rn(s[w], v[j][w]);
     }
-    for (; bh < BH; ++bh)
+  }
+  AKV_DEV float result() const {
+    return __fadd_rn(__fadd_rn(__fadd_rn(acc[0], acc[1]), acc[2]), acc[3]);
+  }
+};
+
+// torch-order sum of the BH rows of one column (row stride rs).  Rows are
+// loaded eight at a time so a thread keeps several loads in flight while the
+// additions keep their order; ILP selects the four-interleaved-cascade form.
+template <bool ILP>
+AKV_DEV float bh_column_sum(const float* __restrict__ col, int64_t rs, int BH) {
+  if constexpr (!ILP) {
+    TorchCascade c;
+    c.init(BH);
+    int bh = 0;
+    for (; bh + 8 <= BH; bh += 8) {
+      float v[8];
 #pragma unroll
-      for (int w = 0; w < W; ++w) s[w] = __fadd_rn(s[w], __ldg(col + bh * rs + w));
+      for (int j = 0; j < 8; ++j) v[j] = __ldg(col + (bh + j) * rs);
 #pragma unroll
-    for (int w = 0; w < W; ++w) imp[w] = __fadd_rn(imp[w], __fdiv_rn(s[w], cnt));
+      for (int j = 0; j < 8; ++j) c.push(v[j]);
+    }
+    for (; bh < BH; ++bh) c.push(__ldg(col + bh * rs));
+    return c.result();
+  } else {
+    TorchCascade c0, c1, c2, c3;
+    c0.init(BH / 4);
+    c1.init(BH / 4);
+    c2.init(BH / 4);
+    c3.init(BH / 4);
+    const int full = BH / 4 * 4;
+    int bh = 0;
+    for (; bh + 8 <= full; bh += 8) {
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = __ldg(col + (bh + j) * rs);
+      c0.push(v[0]);
+      c1.push(v[1]);
+      c2.push(v[2]);
+      c3.push(v[3]);
+      c0.push(v[4]);
+      c1.push(v[5]);
+      c2.push(v[6]);
+      c3.push(v[7]);
+    }
+    if (bh < full) {  // one group of four left
+      c0.push(__ldg(col + bh * rs));
+      c1.push(__ldg(col + (bh + 1) * rs));
+      c2.push(__ldg(col + (bh + 2) * rs));
+      c3.push(__ldg(col + (bh + 3) * rs));
+      bh += 4;
+    }
+    float s = c0.result();
+    for (; bh < BH; ++bh) s = __fadd_rn(s, __ldg(col + bh * rs));  // the last BH % 4 rows go into cascade 0
+    s = __fadd_rn(s, c1.result());
+    s = __fadd_rn(s, c2.result());
+    return __fadd_rn(s, c3.result());
   }
 }
 
-// W positions per thread (W = 4 when Na % 4 == 0 and the rows are 16-byte aligned)
-template <int W>
-__global__ void importance_update_kernel(const float* __restrict__ attn, int B, int H, int M, int Na,
-                                         float* __restrict__ scores, int N, float decay) {
-  const int n0 = (blockIdx.x * blockDim.x + threadIdx.x) * W;
-  if (n0 >= N) return;
-  float imp[W];
-#pragma unroll
-  for (int w = 0; w < W; ++w) imp[w] = 0.f;
-  if (n0 < Na) attn_received<W>(attn, B * H, M, Na, n0, imp);  // W = 4 only when Na % 4 == 0
-#pragma unroll
-  for (int w = 0; w < W; ++w) {
-    const int n = n0 + w;
-    if (n < N) scores[n] = __fadd_rn(__fmul_rn(scores[n], decay), n < Na ? imp[w] : 0.f);
+// attention received by position n: imp = torch-order sum over m of
+// fl(torch-order sum over (b, h) of attn[bh, m, n] / (B*H)).
+AKV_DEV float attn_received_col(const float* __restrict__ attn, int BH, int M, int Na, int n, int vw) {
+  const float cnt = static_cast<float>(BH);
+  const int64_t rs = static_cast<int64_t>(M) * Na;  // stride between (b,h) rows = columns of the (b,h) sum
+  const int64_t jv1 = rs / (2 * vw) * (2 * vw);
+  const int jv2 = Na / (2 * vw) * (2 * vw);
+  auto avg_of = [&](int m) {
+    const float* col = attn + static_cast<int64_t>(m) * Na + n;
+    const float s = static_cast<int64_t>(m) * Na + n >= jv1 ? bh_column_sum<true>(col, rs, BH)
+                                                              : bh_column_sum<false>(col, rs, BH);
+    return __fdiv_rn(s, cnt);
+  };
+  if (M == 1) return avg_of(0);
+  if (n < jv2) {
+    TorchCascade c;
+    c.init(M);
+    for (int m = 0; m < M; ++m) c.push(avg_of(m));
+    return c.result();
   }
+  TorchCascade c0, c1, c2, c3;
+  c0.init(M / 4);
+  c1.init(M / 4);
+  c2.init(M / 4);
+  c3.init(M / 4);
+  const int full = M / 4 * 4;
+  int m = 0;
+  for (; m < full; m += 4) {
+    c0.push(avg_of(m));
+    c1.push(avg_of(m + 1));
+    c2.push(avg_of(m + 2));
+    c3.push(avg_of(m + 3));
+  }
+  float imp = c0.result();
+  for (; m < M; ++m) imp = __fadd_rn(imp, avg_of(m));
+  imp = __fadd_rn(imp, c1.result());
+  imp = __fadd_rn(imp, c2.result());
+  return __fadd_rn(imp, c3.result());
+}
+
+__global__ void importance_update_kernel(const float* __restrict__ attn, int B, int H, int M, int Na,
+                                         float* __restrict__ scores, int N, float decay, int vw) {
+  const int n = blockIdx.x * blockDim.x + threadIdx.x;
+  if (n >= N) return;
+  const float imp = n < Na ? attn_received_col(attn, B * H, M, Na, n, vw) : 0.f;
+  scores[n] = __fadd_rn(__fmul_rn(scores[n], decay), imp);
 }
 
 // ---------------------------------------------------------------------------
@@ -85,26 +177,20 @@ __global__ void importance_update_kernel(const float* __restrict__ attn, int B, 
 // scores = fl(fl(scores*decay) + received); last access = step where
 // received > 0.01.
 // ---------------------------------------------------------------------------
-template <int W>
 __global__ void migrator_update_kernel(const float* __restrict__ attn, int B, int H, int M, int Na,
                                        float* __restrict__ scores, int64_t* __restrict__ access,
-                                       float* __restrict__ retrieval, int n_prev, int64_t step, float decay) {
-  const int n0 = (blockIdx.x * blockDim.x + threadIdx.x) * W;
-  if (n0 >= Na) return;
-  float imp[W];
-  attn_received<W>(attn, B * H, M, Na, n0, imp);
-#pragma unroll
-  for (int w = 0; w < W; ++w) {
-    const int n = n0 + w;
-    float sc = scores[n];
-    if (n >= n_prev) {
-      sc = 0.f;
-      access[n] = step;
-      retrieval[n] = 0.f;
-    }
-    scores[n] = __fadd_rn(__fmul_rn(sc, decay), imp[w]);
-    if (imp[w] > 0.01f) access[n] = step;
+                                       float* __restrict__ retrieval, int n_prev, int64_t step, float decay, int vw) {
+  const int n = blockIdx.x * blockDim.x + threadIdx.x;
+  if (n >= Na) return;
+  const float imp = attn_received_col(attn, B * H, M, Na, n, vw);
+  float sc = scores[n];
+  if (n >= n_prev) {
+    sc = 0.f;
+    access[n] = step;
+    retrieval[n] = 0.f;
   }
+  scores[n] = __fadd_rn(__fmul_rn(sc, decay), imp);
+  if (imp > 0.01f) access[n] = step;
 }
 
 // compute_importance (:175-219), step 1: max of scores, min of last access,
@@ -439,6 +525,58 @@ __global__ void gather_rows_kernel(const char* __restrict__ src, int64_t s_sb, i
   }
 }
 
+// dst[b, h, dst_idx[i]] <- src[b, h, src_idx ? src_idx[i] : i]; indices
+// outside their tier record AKV_ERR_SHAPE and read / write row 0.
+__global__ void scatter_rows_kernel(const char* __restrict__ src, int64_t s_sb, int64_t s_sh, int64_t s_sn,
+                                    int64_t n_src, const int64_t* __restrict__ src_idx,
+                                    const int64_t* __restrict__ dst_idx, int n, int B, int H, int64_t row_bytes,
+                                    char* __restrict__ dst, int64_t d_sb, int64_t d_sh, int64_t d_sn, int64_t n_dst,
+                                    int* status) {
+  const int64_t vpr = row_bytes / 16;
+  const int64_t total = static_cast<int64_t>(B) * H * n * vpr;
+  for (int64_t w = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; w < total;
+       w += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t v = w % vpr;
+    int64_t r = w / vpr;
+    const int i = static_cast<int>(r % n);
+    r /= n;
+    const int h = static_cast<int>(r % H);
+    const int b = static_cast<int>(r / H);
+    int64_t sr = src_idx ? src_idx[i] : i;
+    int64_t dr = dst_idx[i];
+    if (static_cast<uint64_t>(sr) >= static_cast<uint64_t>(n_src)) {
+      set_status(status, AKV_ERR_SHAPE);
+      sr = 0;
+    }
+    if (static_cast<uint64_t>(dr) >= static_cast<uint64_t>(n_dst)) {
+      set_status(status, AKV_ERR_SHAPE);
+      dr = 0;
+    }
+    const uint4 x = *reinterpret_cast<const uint4*>(src + b * s_sb + h * s_sh + sr * s_sn + v * 16);
+    *reinterpret_cast<uint4*>(dst + b * d_sb + h * d_sh + dr * d_sn + v * 16) = x;
+  }
+}
+
+// Self-test of the bounded mbarrier wait every kernel uses: one CTA waits on
+// phase 0 of a barrier with arrival count 1.  arrive = 1: thread 0 arrives
+// first and the wait completes; arrive = 0: nothing arrives, the wait runs out
+// after limit_ns, records AKV_ERR_TIMEOUT in *status and the kernel returns.
+// result[0] = 1 when every thread's wait completed, 2 when it ran out.
+__global__ void selftest_wait_kernel(int arrive, uint64_t limit_ns, int* status, int* result) {
+  __shared__ uint64_t bar;
+  __shared__ int ran_out;
+  if (threadIdx.x == 0) {
+    ran_out = 0;
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (arrive && threadIdx.x == 0) mbar_arrive(&bar);
+  if (!mbar_wait(&bar, 0, status, limit_ns)) atomicExch(&ran_out, 1);
+  __syncthreads();
+  if (threadIdx.x == 0) result[0] = ran_out ? 2 : 1;
+}
+
 }  // namespace akv
 
 using namespace akv;
@@ -486,16 +624,23 @@ extern "C" int akv_warm_layout_init(int D, int kb, int vb, int n, akv_warm_layou
   return AKV_OK;
 }
 
+// Floats per SIMD register of the CPU whose torch reduction order the
+// importance sums follow (16: AVX-512, 8: AVX2 / default builds).
+static int g_reduction_width = 16;
+
+extern "C" int akv_set_reduction_width(int floats) {
+  if (floats != 4 && floats != 8 && floats != 16) return AKV_ERR_SHAPE;
+  g_reduction_width = floats;
+  return AKV_OK;
+}
+
 extern "C" int akv_importance_update(const float* attn, int B, int H, int M, int Na, float* scores, int N,
                                      float decay, void* stream) {
   if (!scores || (!attn && Na > 0)) return AKV_ERR_NULL;
   if (B <= 0 || H <= 0 || M <= 0 || Na < 0 || N < 0) return AKV_ERR_SHAPE;
   if (N == 0) return AKV_OK;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (Na % 4 == 0 && N % 4 == 0 && (reinterpret_cast<uintptr_t>(attn) % 16) == 0)
-    importance_update_kernel<4><<<(N / 4 + 255) / 256, 256, 0, st>>>(attn, B, H, M, Na, scores, N, decay);
-  else
-    importance_update_kernel<1><<<(N + 255) / 256, 256, 0, st>>>(attn, B, H, M, Na, scores, N, decay);
+  importance_update_kernel<<<(N + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      attn, B, H, M, Na, scores, N, decay, g_reduction_width);
   return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_LAUNCH;
 }
 
@@ -552,6 +697,33 @@ extern "C" int akv_gather_rows(const void* src, int64_t s_sb, int64_t s_sh, int6
   return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_LAUNCH;
 }
 
+extern "C" int akv_scatter_rows(const void* src, int64_t s_sb, int64_t s_sh, int64_t s_sn, int64_t n_src,
+                                const int64_t* src_idx, const int64_t* dst_idx, int n, int B, int H,
+                                int64_t row_bytes, void* dst, int64_t d_sb, int64_t d_sh, int64_t d_sn, int64_t n_dst,
+                                int* status, void* stream) {
+  if (!src || !dst || !dst_idx) return AKV_ERR_NULL;
+  if (n < 0 || B <= 0 || H <= 0 || row_bytes <= 0 || row_bytes % 16 || n_src <= 0 || n_dst <= 0)
+    return AKV_ERR_SHAPE;
+  if (n == 0) return AKV_OK;
+  if (reinterpret_cast<uintptr_t>(src) % 16 || reinterpret_cast<uintptr_t>(dst) % 16 || s_sb % 16 || s_sh % 16 ||
+      s_sn % 16 || d_sb % 16 || d_sh % 16 || d_sn % 16)
+    return AKV_ERR_ALIGN;
+  const int64_t total = static_cast<int64_t>(B) * H * n * (row_bytes / 16);
+  const int64_t blocks = std::min<int64_t>((total + 255) / 256, 148 * 16);
+  scatter_rows_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const char*>(src), s_sb, s_sh, s_sn, n_src, src_idx, dst_idx, n, B, H, row_bytes,
+      static_cast<char*>(dst), d_sb, d_sh, d_sn, n_dst, status);
+  return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_LAUNCH;
+}
+
+extern "C" int akv_selftest_wait(int arrive, int64_t limit_ns, int* status, int* result, void* stream) {
+  if (!status || !result) return AKV_ERR_NULL;
+  if (limit_ns <= 0 || limit_ns > static_cast<int64_t>(kWaitLimitNs)) return AKV_ERR_SHAPE;
+  selftest_wait_kernel<<<1, 64, 0, static_cast<cudaStream_t>(stream)>>>(arrive, static_cast<uint64_t>(limit_ns),
+                                                                         status, result);
+  return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_LAUNCH;
+}
+
 extern "C" int akv_cold_copy(void* dst, int64_t dst_stride, const void* src, int64_t src_stride, int64_t chunk_bytes,
                              int64_t count, int dir, void* stream, void* event) {
   if (!dst || !src) return AKV_ERR_NULL;
@@ -572,13 +744,8 @@ extern "C" int akv_migrator_update(const float* attn, int B, int H, int M, int N
   if (!attn || !scores || !last_access || !retrieval) return AKV_ERR_NULL;
   if (B <= 0 || H <= 0 || M <= 0 || Na < 0 || n_prev < 0) return AKV_ERR_SHAPE;
   if (Na == 0) return AKV_OK;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (Na % 4 == 0 && (reinterpret_cast<uintptr_t>(attn) % 16) == 0)
-    migrator_update_kernel<4><<<(Na / 4 + 255) / 256, 256, 0, st>>>(attn, B, H, M, Na, scores, last_access,
-                                                                    retrieval, n_prev, step, decay);
-  else
-    migrator_update_kernel<1><<<(Na + 255) / 256, 256, 0, st>>>(attn, B, H, M, Na, scores, last_access, retrieval,
-                                                                n_prev, step, decay);
+  migrator_update_kernel<<<(Na + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      attn, B, H, M, Na, scores, last_access, retrieval, n_prev, step, decay, g_reduction_width);
   return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_LAUNCH;
 }
 

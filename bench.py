@@ -484,32 +484,31 @@ def seq_split_bench(torch, akv, dev, world: int, rank: int, reps: int = 20) -> d
     out = torch.empty(rows, D, dtype=torch.float16, device=dev)
     hot = (hk, hv) if rank == 0 else (None, None)
 
-    def layer(i):
-        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    def layer(i, ev):
         ev[0].record()
         p = P.local_partial(q, hot[0], hot[1], arenas[i % copies])
         ev[1].record()
         dist.all_gather_into_tensor(gathered, p)
         ev[2].record()
-        part = gathered.permute(1, 0, 2).contiguous()
-        _C_combine(part, out)
+        P.combine_partials(gathered.permute(1, 0, 2), out=out)  # strided read, no copy
         ev[3].record()
-        return ev
 
-    from akv import _C
-
-    def _C_combine(part, o):
-        _C.check(_C.load().akv_lse_combine(part.data_ptr(), D + 2, part.stride(0), rows, world, D, o.data_ptr(), D,
-                                           None, None, _C.stream_of(part)), "akv_lse_combine")
+    def new_events():
+        return [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(reps)]
 
     for i in range(3):
-        layer(i)
+        layer(i, new_events()[0])
     torch.cuda.synchronize()
     dist.barrier()
-    t = {"decode": [], "all_gather": [], "combine": [], "layer": []}
+    evs = new_events()
+    # The GPU sleeps ~10 ms while the host enqueues every repetition, so the
+    # events time the device work, not the host's per-call Python.
+    torch.cuda._sleep(20_000_000)
     for i in range(reps):
-        ev = layer(i)
-        ev[3].synchronize()
+        layer(i, evs[i])
+    torch.cuda.synchronize()
+    t = {"decode": [], "all_gather": [], "combine": [], "layer": []}
+    for ev in evs:
         t["decode"].append(ev[0].elapsed_time(ev[1]) * 1e3)
         t["all_gather"].append(ev[1].elapsed_time(ev[2]) * 1e3)
         t["combine"].append(ev[2].elapsed_time(ev[3]) * 1e3)
@@ -518,13 +517,21 @@ def seq_split_bench(torch, akv, dev, world: int, rank: int, reps: int = 20) -> d
                        dtype=torch.float64, device=dev)
     dist.all_reduce(med, op=dist.ReduceOp.MAX)
     split_out = out.clone()
-    max_err = None
+    max_err = single_us = None
     if rank == 0:  # the whole sequence on this GPU
         full = akv.WarmArena(B, Hkv, D, 4, 4, 0.0, max_blocks=nblk, device=dev)
         for r in range(world):
             shard(r, full)
         ref = akv.mixed_tier_decode_attention(q, hk, hv, full)
         max_err = float((split_out.float() - ref.reshape(rows, D).float()).abs().max().item())
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+        torch.cuda._sleep(20_000_000)
+        for i in range(5):  # the whole context is ~690 MB, far above the L2
+            e[i].record()
+            akv.mixed_tier_decode_attention(q, hk, hv, full)
+        e[5].record()
+        torch.cuda.synchronize()
+        single_us = statistics.median(e[i].elapsed_time(e[i + 1]) * 1e3 for i in range(5))
         del full
     dist.barrier()
     d, g_, c_, l_ = [round(float(x), 2) for x in med.tolist()]
@@ -533,7 +540,10 @@ def seq_split_bench(torch, akv, dev, world: int, rank: int, reps: int = 20) -> d
            "decode_us": d, "all_gather_us": g_, "combine_us": c_, "layer_us": l_,
            "warm_blocks_per_rank": hi - lo, "layer_copies": copies,
            "limiter": max((("decode", d), ("all_gather", g_), ("combine", c_)), key=lambda x: x[1])[0],
-           "max_err": max_err}
+           "max_err": max_err,
+           "single_gpu_layer_us": None if single_us is None else round(single_us, 2)}
+    if single_us:
+        res["speedup_vs_single_gpu"] = round(single_us / l_, 3)
     del arenas, mine
     torch.cuda.empty_cache()
     return res
@@ -867,6 +877,8 @@ def run_ours(args):
     ev_in = [torch.cuda.Event() for _ in range(L)]
     ev_out = [torch.cuda.Event() for _ in range(L)]
 
+    e2e_status = torch.zeros(1, dtype=torch.int32, device=dev)
+
     def e2e_step():
         s_in.wait_stream(st)  # uploads may overwrite q_in only after the previous step read it
         with torch.cuda.stream(s_in):
@@ -875,7 +887,8 @@ def run_ours(args):
                 ev_in[l].record(s_in)
         for l in range(L):
             st.wait_event(ev_in[l])
-            akv.mixed_tier_decode_attention(q_in[l], hot_k[l], hot_v[l], arenas[l], out=o_dev[l])
+            akv.mixed_tier_decode_attention(q_in[l], hot_k[l], hot_v[l], arenas[l], out=o_dev[l],
+                                            status=e2e_status)
             ev_out[l].record(st)
             s_out.wait_event(ev_out[l])
             with torch.cuda.stream(s_out):
@@ -894,6 +907,8 @@ def run_ours(args):
     torch.cuda.synchronize()
     barrier()
     e2e_ms = max_over_ranks(t0.elapsed_time(t1) / args.steps)
+    if int(e2e_status.item()) != 0:
+        raise SystemExit(f"device status {int(e2e_status.item())} on the e2e path")
 
     # ---- roofline of the dominant kernel (per layer launch)
     # algorithmic bytes per layer launch, per (batch row, KV head): warm codes

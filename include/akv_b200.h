@@ -38,7 +38,7 @@ extern "C" {
 enum {
   AKV_OK = 0,
   AKV_ERR_SHAPE = -1,       /* bad or unsupported shape / length */
-  AKV_ERR_BITS = -2,        /* bit width not in {2,3,4} */
+  AKV_ERR_BITS = -2,        /* unsupported bit width ({2,3,4}; {2,4,8} for the group format) */
   AKV_ERR_ALIGN = -3,       /* pointer or stride alignment */
   AKV_ERR_UNSUPPORTED = -4, /* valid request this build does not handle */
   AKV_ERR_LAUNCH = -5,      /* kernel launch / CUDA runtime error */
@@ -219,6 +219,48 @@ int akv_int4_group_dequant(const uint8_t* packed, int64_t p_sh, int64_t p_sn,
                            uint16_t* out, int64_t o_sh, int64_t o_sn, void* stream);
 
 /* ------------------------------------------------------------------------
+ * The same per-token, per-D-group ("group format") layout at 2, 4 or 8 bits,
+ * as the reference's triton_ops._dequantize_packed (akv/triton_ops.py:657-715)
+ * reads it for fused_quantized_attention (:330-376),
+ * fused_mixed_precision_attention (:466-515) and
+ * triton_kernels.fused_decode_attention (akv/triton_kernels.py:281-423):
+ * 8 bits one code per byte; 4 bits channel 2j in the high nibble of byte j;
+ * 2 bits channel 4j in bits 7..6 of byte j, then 5..4, 3..2, 1..0.
+ * `symmetric` (device int, nullable = 0) selects (code - max/2)*scale, the
+ * reference's branch for an all-zero zeros tensor; otherwise
+ * fp32(code*scale) + zero.  Both rounded once more to fp16.  D % 8 == 0.
+ * ---------------------------------------------------------------------- */
+int akv_group_dequant(const uint8_t* packed, int64_t p_sh, int64_t p_sn,
+                      const uint16_t* scales, const uint16_t* zeros, int64_t s_sh, int64_t s_sn,
+                      int H, int N, int D, int group_size, int bits, const int32_t* symmetric,
+                      uint16_t* out, int64_t o_sh, int64_t o_sn, void* stream);
+
+/* Group-format quantisation of fp16 rows, the arithmetic of the reference's
+ * triton_kernels.fused_quantize_evict (akv/triton_kernels.py:426-500): rows
+ * padded with zeros to whole groups; per group min / max, scale =
+ * fp16(fp16(max - min) / (2^bits - 1)), zero = min, code = clamp(round-half-
+ * even(fp16(fp16(x - zero) / scale)), 0, 2^bits - 1) (0 where that is NaN:
+ * a constant group), every half op a float op rounded to fp16 as torch does.
+ * Row r of the output reads source row row_idx[r] (nullable = r) at
+ * src + row*s_sn; an index outside [0, n_src) records AKV_ERR_SHAPE in
+ * *status (nullable) and reads row 0.  Writes packed[n][row_bytes] and fp16
+ * scales / zeros [n][ceil(D/group_size)], contiguous. */
+int akv_group_quantize(const uint16_t* src, int64_t s_sn, const int64_t* row_idx, int64_t n_src, int n, int D,
+                       int group_size, int bits, uint8_t* packed, int64_t row_bytes,
+                       uint16_t* scales, uint16_t* zeros, int* status, void* stream);
+
+/* Softmax weights of one key tier for the attention-weight output of
+ * triton_ops.fused_mixed_precision_attention (akv/triton_ops.py:466-515):
+ * out[b][h][m][col0 + n] = exp(sm_scale * q[b,h,m,:] . k[b,h,n,:] - lse[b,h,m])
+ * with lse (B*H*M, contiguous, natural log) the log-sum-exp over every tier
+ * (0 where lse is -inf).  Element strides; k strides may be 0 (a tier shared
+ * by the batch or the heads).  D <= 256. */
+int akv_attention_probs(const uint16_t* q, int64_t q_sb, int64_t q_sh, int64_t q_sm,
+                        const uint16_t* k, int64_t k_sb, int64_t k_sh, int64_t k_sn, const float* lse,
+                        int B, int H, int M, int N, int D, float sm_scale,
+                        float* out, int64_t o_sb, int64_t o_sh, int64_t o_sm, int col0, void* stream);
+
+/* ------------------------------------------------------------------------
  * A5: mixed-tier decode attention (one query token per sequence).
  * Replaces the reference's decode paths that attend over [warm; hot]:
  * fused_attention.mixed_precision_decode_attention (akv/fused_attention.py:324-366),
@@ -351,6 +393,16 @@ int akv_lse_combine(const float* part, int64_t part_ss, int64_t part_sr, int row
 int akv_importance_update(const float* attn, int B, int H, int M, int Na, float* scores, int N, float decay,
                           void* stream);
 
+/* The order of the two sums above (and in akv_migrator_update) is torch's
+ * CPU reduction order for a contiguous tensor reduced over its outer
+ * dimension, which depends on the CPU's SIMD width: columns below the last
+ * multiple of 2*`floats` (floats per vector register: 16 with AVX-512, 8 with
+ * AVX2) add their rows in torch's multi-level cascade, the rest in four
+ * interleaved cascades.  Set it to the width of the machine whose reference
+ * results are to be matched (default 16); process-wide, not per stream.
+ * AKV_ERR_SHAPE unless floats is 4, 8 or 16. */
+int akv_set_reduction_width(int floats);
+
 /* ------------------------------------------------------------------------
  * A6: ImportanceBasedMigrator (akv/vmm.py:113-245) state on the GPU: fp32
  * scores, int64 last-access steps and fp32 retrieval flags per position.
@@ -392,6 +444,28 @@ int akv_select_bottomk(const float* scores, int n, int k, int protect_first, int
 int akv_gather_rows(const void* src, int64_t s_sb, int64_t s_sh, int64_t s_sn, int64_t n_src,
                     const int64_t* idx, int n, int B, int H, int64_t row_bytes,
                     void* dst, int64_t d_sb, int64_t d_sh, int64_t d_sn, int* status, void* stream);
+
+/* Row scatter, the counterpart of akv_gather_rows for tier moves that write
+ * into given rows (the hot ring's hole refill after a demotion, promoted rows
+ * into free ring rows; the reference's :474-475 prepend and :739-751 keep-mask
+ * compaction rewrite whole tensors instead):
+ *   dst + b*d_sb + h*d_sh + dst_idx[i]*d_sn  <-  src + b*s_sb + h*s_sh + s*s_sn,
+ *   s = src_idx ? src_idx[i] : i
+ * Indices outside [0, n_src) / [0, n_dst) record AKV_ERR_SHAPE in *status
+ * (nullable) and use row 0.  Rows read and rows written must not overlap
+ * (src and dst may be the same buffer).  row_bytes, pointers and strides
+ * multiples of 16. */
+int akv_scatter_rows(const void* src, int64_t s_sb, int64_t s_sh, int64_t s_sn, int64_t n_src,
+                     const int64_t* src_idx, const int64_t* dst_idx, int n, int B, int H, int64_t row_bytes,
+                     void* dst, int64_t d_sb, int64_t d_sh, int64_t d_sn, int64_t n_dst, int* status, void* stream);
+
+/* Self-test of the bounded device-side wait (the mbarrier wait every kernel
+ * of this library uses, with its limit shortened to limit_ns, at most the
+ * kernels' own 2 s): one CTA waits on a barrier phase that, with arrive = 0,
+ * nothing completes.  The wait runs out, *status receives AKV_ERR_TIMEOUT,
+ * result[0] = 2 and the kernel returns: the context stays usable.  With
+ * arrive = 1 a thread completes the phase first and result[0] = 1. */
+int akv_selftest_wait(int arrive, int64_t limit_ns, int* status, int* result, void* stream);
 
 /* ------------------------------------------------------------------------
  * A8: cold tier copies.  Replaces AsyncMigrator._do_warm_to_cold /

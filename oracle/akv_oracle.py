@@ -422,19 +422,157 @@ def int4_group_dequant(packed: np.ndarray, scales: np.ndarray, zeros: np.ndarray
 
 
 # ---------------------------------------------------------------------------
+# Group format: per token, per D-group, packed bytes (the kernel API of
+# triton_ops / triton_kernels and KVQuantizer's QuantizedTensor)
+# ---------------------------------------------------------------------------
+
+def group_unpack(packed: np.ndarray, bits: int, count: int) -> np.ndarray:
+    """triton_ops.py:672-686 / quantizer.py:221-243 — codes of a flat byte stream (MSB first)."""
+    p = np.asarray(packed).astype(np.uint8).reshape(-1)
+    if bits == 8:
+        c = p
+    elif bits == 4:
+        c = np.stack([(p >> 4) & 15, p & 15], -1).reshape(-1)
+    elif bits == 2:
+        c = np.stack([(p >> 6) & 3, (p >> 4) & 3, (p >> 2) & 3, p & 3], -1).reshape(-1)
+    else:
+        raise ValueError(f"Unsupported bits: {bits}")
+    return c[:count]
+
+
+def group_pack(codes: np.ndarray, bits: int) -> np.ndarray:
+    """quantizer.py:193-219 — flat codes -> bytes (MSB first, zero padded)."""
+    c = np.asarray(codes).astype(np.uint8).reshape(-1)
+    per = 8 // bits
+    c = np.concatenate([c, np.zeros((-c.size) % per, np.uint8)]).reshape(-1, per)
+    out = np.zeros(c.shape[0], np.uint8)
+    for t in range(per):
+        out |= (c[:, t] << (8 - bits * (t + 1))).astype(np.uint8)
+    return out
+
+
+def group_dequantize(packed: np.ndarray, scales: np.ndarray, zeros: np.ndarray, bits: int, group_size: int,
+                     N: int, D: int) -> np.ndarray:
+    """triton_ops.py:657-715 (``_dequantize_packed``) — (N, D) fp16.
+
+    Rows are padded to whole groups; fp32 arithmetic: ``codes*s + z`` (two
+    roundings) or, when every zero is 0, ``(codes - max//2) * s``; one
+    rounding to fp16 at the end."""
+    Dp = -(-D // group_size) * group_size
+    c = group_unpack(packed, bits, N * Dp).astype(F32).reshape(N, -1, group_size)
+    s = _f(scales).reshape(N, -1)[..., None]
+    z = _f(zeros).reshape(N, -1)[..., None]
+    if np.all(z == 0):
+        out = ((c - F32(((1 << bits) - 1) // 2)) * s).astype(F32)
+    else:
+        out = ((c * s).astype(F32) + z).astype(F32)
+    return _h(out.reshape(N, -1)[:, :D])
+
+
+def group_quantize_fp16(x: np.ndarray, bits: int, group_size: int):
+    """triton_kernels.py:470-500 (``fused_quantize_evict``'s quantiser) on
+    fp16 rows (n, D): every half op is a float op rounded to fp16.  The
+    ``clamp(min=1e-8)`` on the fp16 scale changes nothing (every positive
+    fp16 exceeds 1e-8 and fp16(1e-8) is 0); a zero scale makes 0/0 = NaN,
+    whose uint8 cast the reference leaves to the platform: 0 here.
+    Returns (packed (n, Dp*bits/8), scales (n, ng) fp16, zeros (n, ng) fp16)."""
+    x = np.asarray(x, F16)
+    n, d = x.shape
+    Dp = -(-d // group_size) * group_size
+    xp = np.zeros((n, Dp), F16)
+    xp[:, :d] = x
+    g = xp.reshape(n, -1, group_size)
+    mn, mx = g.min(-1), g.max(-1)
+    maxint = (1 << bits) - 1
+    scale = _h(_f(_h(_f(mx) - _f(mn))) / F32(maxint))
+    with np.errstate(invalid="ignore", divide="ignore"):
+        q = _f(_h(_f(_h(_f(g) - _f(mn)[..., None])) / _f(scale)[..., None]))
+    q = np.rint(q)
+    q = np.where(np.isnan(q), 0, np.clip(q, 0, maxint)).astype(np.uint8)
+    packed = np.stack([group_pack(q[r], bits) for r in range(n)]) if n else np.zeros((0, Dp * bits // 8), np.uint8)
+    return packed, scale, mn.astype(F16)
+
+
+# ---------------------------------------------------------------------------
 # Importance update and demote selection
 # ---------------------------------------------------------------------------
 
-def importance_update(attn: np.ndarray, scores: np.ndarray, decay: float) -> np.ndarray:
+def _cascade(rows: np.ndarray) -> np.ndarray:
+    """Sum over axis 0 in torch's CPU cascade order (PyTorch
+    aten/src/ATen/native/cpu/SumKernel.cpp, multi_row_sum): with
+    lp = max(4, ceil(log2(R)) // 4) rows go one by one into level 0; after
+    every 2^lp rows level 0 moves into level 1, at multiples of 2^(2lp) level
+    1 into 2, at 2^(3lp) level 2 into 3; then levels 0 + 1 + 2 + 3."""
+    R = rows.shape[0]
+    lp = max(4, (int(math.ceil(math.log2(R))) if R > 1 else 0) // 4)
+    step, mask = 1 << lp, (1 << lp) - 1
+    acc = np.zeros((4,) + rows.shape[1:], F32)
+    i = 0
+    while i + step <= R:
+        for _ in range(step):
+            acc[0] = acc[0] + rows[i]
+            i += 1
+        for j in range(1, 4):
+            acc[j] = acc[j] + acc[j - 1]
+            acc[j - 1] = 0
+            if i & (mask << (j * lp)):
+                break
+    while i < R:
+        acc[0] = acc[0] + rows[i]
+        i += 1
+    out = acc[0]
+    for j in range(1, 4):
+        out = (out + acc[j]).astype(F32)
+    return out.astype(F32)
+
+
+def _cascade_ilp4(rows: np.ndarray) -> np.ndarray:
+    """torch's row_sum: four interleaved cascades (rows 4i + k), the last
+    R % 4 rows added to cascade 0, then cascades 1, 2, 3 added in order."""
+    R = rows.shape[0]
+    s = R // 4
+    if s:
+        p = np.stack([_cascade(rows[k:4 * s:4]) for k in range(4)])
+    else:
+        p = np.zeros((4,) + rows.shape[1:], F32)
+    out = p[0]
+    for i in range(4 * s, R):
+        out = (out + rows[i]).astype(F32)
+    for k in range(1, 4):
+        out = (out + p[k]).astype(F32)
+    return out
+
+
+def torch_outer_sum(x: np.ndarray, vec_width: int = 16) -> np.ndarray:
+    """torch.sum(x, dim=0) on the CPU for a contiguous fp32 (R, C) array,
+    bit for bit: columns below the last multiple of 2*vec_width (torch sums
+    them in blocks of four and two vector registers) in cascade order, the
+    rest (one register's worth and the scalar tail) in the interleaved form.
+    vec_width = floats per SIMD register (16 with AVX-512, 8 with AVX2)."""
+    x = np.asarray(x, F32)
+    R, C = x.shape
+    jv = C // (2 * vec_width) * (2 * vec_width)
+    out = np.empty(C, F32)
+    if jv:
+        out[:jv] = _cascade(x[:, :jv])
+    if jv < C:
+        out[jv:] = _cascade_ilp4(x[:, jv:])
+    return out
+
+
+def importance_update(attn: np.ndarray, scores: np.ndarray, decay: float, vec_width: int = 16) -> np.ndarray:
     """triton_ops.py:604-650 (CPU branch): scores*decay + sum_M mean_{B,H} attn.
 
-    Two roundings (``mul_`` then ``add_``); the importance vector is truncated
-    or zero-padded to len(scores) (:627-633).
+    ``attention_weights.float().mean(dim=(0, 1)).sum(dim=0)`` in torch's CPU
+    reduction order (``torch_outer_sum``; the mean is the sum divided by
+    B*H), then two roundings (``mul_`` then ``add_``); the importance vector
+    is truncated or zero-padded to len(scores) (:627-633).
     """
     a = _f(attn)
     B, H, M, N = a.shape
-    avg = (np.sum(a, axis=(0, 1), dtype=F32) / F32(B * H)).astype(F32)
-    imp = np.sum(avg, axis=0, dtype=F32).astype(F32)
+    tot = torch_outer_sum(a.reshape(B * H, M * N), vec_width).reshape(M, N)
+    avg = (tot / F32(B * H)).astype(F32)
+    imp = torch_outer_sum(avg, vec_width) if M > 1 else avg[0]
     n = scores.shape[0]
     if imp.shape[0] > n:
         imp = imp[:n]

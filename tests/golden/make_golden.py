@@ -404,11 +404,76 @@ def make_migrator_trace(ref_path: str):
     print("migrator trace written to", HERE, snaps, "snapshots")
 
 
+def make_group_format(ref_path: str):
+    """The reference's group-format tier (per token, per D-group, packed
+    bytes): KVQuantizer quantise / dequantise (akv/quantizer.py:71-191), the
+    dequantiser of the kernel API (triton_ops._dequantize_packed,
+    akv/triton_ops.py:657-715), triton_kernels.fused_quantize_evict
+    (akv/triton_kernels.py:426-500) in fp16, and fp32 attention over hot +
+    dequantised warm with its softmax weights (the recipe of
+    triton_kernels._fused_decode_attention_dispatch :350-390 and
+    triton_ops._fused_mixed_attention_torch :518-551, in fp32)."""
+    import torch
+    torch.set_num_threads(1)
+    sys.path.insert(0, ref_path)
+    from akv.quantizer import KVQuantizer, QuantConfig
+    from akv import triton_ops, triton_kernels
+    g = torch.Generator().manual_seed(21)
+    out = {}
+    cases = [(40, 128, 32), (33, 72, 32), (16, 64, 64), (24, 128, 128)]
+    for bits in (2, 4, 8):
+        for ci, (N, D, gs) in enumerate(cases):
+            x = torch.randn(N, D, generator=g)
+            x[:, 5] *= 12.0
+            x[3] = 0.75  # a constant row: zero range in every group
+            x = x.half()
+            tag = f"b{bits}_c{ci}"
+            out[f"x_{tag}"] = x.numpy()
+            for sym in (False, True):
+                qz = KVQuantizer(QuantConfig(bits=bits, group_size=gs, symmetric=sym))
+                qt = qz.quantize(x)
+                st = f"{tag}_{'s' if sym else 'a'}"
+                out[f"data_{st}"] = qt.data.numpy()
+                out[f"scales_{st}"] = qt.scales.numpy()
+                out[f"zeros_{st}"] = qt.zeros.numpy()
+                out[f"deq_{st}"] = qz.dequantize(qt).numpy()
+                out[f"dp_{st}"] = triton_ops._dequantize_packed(qt.data, qt.scales, qt.zeros, bits, gs, N, D,
+                                                                 "cpu", torch.float16).numpy()
+            v = torch.randn(N, D, generator=g).half()
+            mask = torch.rand(N, generator=g) < 0.5
+            mask[3] = True
+            out[f"v_{tag}"] = v.numpy()
+            out[f"mask_{tag}"] = mask.numpy()
+            res = triton_kernels.fused_quantize_evict(x, v, mask, bits=bits, group_size=gs)
+            for name, t in zip(("kp", "ks", "kz", "vp", "vs", "vz"), res):
+                out[f"qe_{name}_{tag}"] = t.numpy()
+    # attention over hot (B, H, N_hot, D) + a 4-bit group-format warm tier (N_warm, D)
+    B, H, M, D, n_hot, n_warm, gs = 2, 3, 2, 128, 20, 70, 32
+    q = torch.randn(B, H, M, D, generator=g).half()
+    hk = torch.randn(B, H, n_hot, D, generator=g).half()
+    hv = torch.randn(B, H, n_hot, D, generator=g).half()
+    wk = torch.randn(n_warm, D, generator=g).half()
+    wv = torch.randn(n_warm, D, generator=g).half()
+    qz = KVQuantizer(QuantConfig(bits=4, group_size=gs))
+    kq, vq = qz.quantize(wk), qz.quantize(wv)
+    dk = triton_ops._dequantize_packed(kq.data, kq.scales, kq.zeros, 4, gs, n_warm, D, "cpu", torch.float16)
+    dv = triton_ops._dequantize_packed(vq.data, vq.scales, vq.zeros, 4, gs, n_warm, D, "cpu", torch.float16)
+    keys = torch.cat([hk, dk.expand(B, H, -1, -1)], 2).float()
+    vals = torch.cat([hv, dv.expand(B, H, -1, -1)], 2).float()
+    w = torch.softmax(torch.matmul(q.float(), keys.transpose(-2, -1)) / math.sqrt(D), dim=-1)
+    out.update(att_q=q.numpy(), att_hk=hk.numpy(), att_hv=hv.numpy(), att_kd=kq.data.numpy(),
+               att_ks=kq.scales.numpy(), att_kz=kq.zeros.numpy(), att_vd=vq.data.numpy(), att_vs=vq.scales.numpy(),
+               att_vz=vq.zeros.numpy(), att_gs=np.int64(gs), att_out=torch.matmul(w, vals).numpy(),
+               att_w=w.numpy())
+    np.savez_compressed(os.path.join(HERE, "group_format.npz"), **out)
+    print("group-format fixtures written to", HERE)
+
+
 def _reference_path() -> str:
     """The reference source tree: the first argument, else $AKV_REFERENCE."""
     path = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("AKV_REFERENCE", "")
     if not path:
-        sys.exit("usage: make_golden.py <reference source path> [migrator|drop_in|per_head] "
+        sys.exit("usage: make_golden.py <reference source path> [migrator|drop_in|per_head|group_format] "
                  "(or set AKV_REFERENCE)")
     return path
 
@@ -421,9 +486,12 @@ if __name__ == "__main__":
         make_drop_in_traces(sys.argv[1])
     elif len(sys.argv) > 2 and sys.argv[2] == "per_head":
         make_per_head_trace(sys.argv[1])
+    elif len(sys.argv) > 2 and sys.argv[2] == "group_format":
+        make_group_format(sys.argv[1])
     else:
         ref = _reference_path()
         main(ref)
         make_drop_in_traces(ref)
         make_migrator_trace(ref)
         make_per_head_trace(ref)
+        make_group_format(ref)

@@ -25,7 +25,7 @@ def test_importance_update_golden(golden_dir):
         scores = torch.from_numpy(z[f"{t}/scores_in"]).to(DEV)
         out = tiering.fused_importance_update(attn, scores, decay=float(z[f"{t}/decay"]))
         assert out.data_ptr() == scores.data_ptr()  # in place, like the reference
-        np.testing.assert_allclose(_np(out), z[f"{t}/scores_out"], rtol=2e-6, atol=1e-7)
+        np.testing.assert_array_equal(_np(out), z[f"{t}/scores_out"])
     s = torch.ones(32, device=DEV)
     out = tiering.fused_importance_update(torch.zeros(1, 1, 1, 32, device=DEV), s, decay=0.5)
     np.testing.assert_array_equal(_np(out), z["imp_zero/scores_out"])
@@ -37,9 +37,35 @@ def test_importance_update_pad_and_truncate():
     for na, n in ((40, 64), (100, 64)):
         attn = rng.random((2, 3, 2, na)).astype(np.float32)
         scores = rng.random(n).astype(np.float32)
-        ref = O.importance_update(attn, scores, 0.9)
+        ref = O.importance_update(attn, scores, 0.9, vec_width=_C_width())
         out = tiering.fused_importance_update(torch.from_numpy(attn).to(DEV), torch.from_numpy(scores).to(DEV), 0.9)
-        np.testing.assert_allclose(_np(out), ref, rtol=2e-6, atol=1e-7)
+        np.testing.assert_array_equal(_np(out), ref)
+
+
+def _C_width():
+    from akv import _C
+    return _C.cpu_reduction_width()
+
+
+@pytest.mark.parametrize("width", [8, 16])
+@pytest.mark.parametrize("shape", [(8, 8, 1, 512), (16, 32, 1, 1000), (4, 8, 2, 3000), (3, 5, 17, 100),
+                                   (5, 7, 3, 33), (32, 16, 1, 2000), (8, 8, 1, 131072), (2, 8, 64, 300)])
+def test_importance_update_torch_order(shape, width):
+    """Bit-exact against the oracle's restatement of torch's CPU reduction
+    order (pinned to torch itself on the CPU) at both SIMD widths: every
+    cascade level, block, single-register and scalar-tail column path."""
+    from akv import _C, tiering
+    rng = np.random.default_rng(sum(shape) + width)
+    a = rng.random(shape).astype(np.float32)
+    a /= a.sum(-1, keepdims=True)
+    s = rng.random(shape[-1]).astype(np.float32)
+    lib = _C.load()
+    try:
+        assert lib.akv_set_reduction_width(width) == 0
+        out = tiering.fused_importance_update(torch.from_numpy(a).to(DEV), torch.from_numpy(s).to(DEV), 0.9)
+        np.testing.assert_array_equal(_np(out), O.importance_update(a, s, 0.9, vec_width=width))
+    finally:
+        lib.akv_set_reduction_width(_C.cpu_reduction_width())
 
 
 def test_select_golden(golden_dir):

@@ -115,7 +115,7 @@ def test_importance_golden(golden_dir):
     for (B, H, M, N) in ((1, 4, 1, 64), (2, 8, 3, 257), (8, 8, 1, 512)):
         t = f"imp_B{B}_H{H}_M{M}_N{N}"
         s = O.importance_update(z[f"{t}/attn"], z[f"{t}/scores_in"], float(z[f"{t}/decay"]))
-        np.testing.assert_allclose(s, z[f"{t}/scores_out"], rtol=2e-6, atol=1e-7)
+        np.testing.assert_array_equal(s, z[f"{t}/scores_out"])
     s = O.importance_update(np.zeros((1, 1, 1, 32), np.float32), np.ones(32, np.float32), 0.5)
     np.testing.assert_array_equal(s, z["imp_zero/scores_out"])
     for key in [k for k in z.files if k.startswith("sel_") and k.endswith("/meta")]:
@@ -123,3 +123,45 @@ def test_importance_golden(golden_dir):
         hot_len, budget, n_dem = (int(x) for x in z[key])
         idx = O.select_demote(z[f"{t}/scores"], n_dem, budget)
         np.testing.assert_array_equal(idx, z[f"{t}/idx"], err_msg=t)
+
+
+# ---------------------------------------------------------------------------- group format
+def test_group_format_oracle_matches_reference(golden_dir):
+    """The group-format dequantiser (triton_ops._dequantize_packed, also
+    KVQuantizer.dequantize) and fused_quantize_evict's fp16 quantiser against
+    the reference's own outputs, bit for bit."""
+    f = _load(golden_dir, "group_format.npz")
+    cases = [(40, 128, 32), (33, 72, 32), (16, 64, 64), (24, 128, 128)]
+    for bits in (2, 4, 8):
+        for ci, (N, D, gs) in enumerate(cases):
+            tag = f"b{bits}_c{ci}"
+            for st in ("a", "s"):
+                k = f"{tag}_{st}"
+                d = O.group_dequantize(f[f"data_{k}"], f[f"scales_{k}"], f[f"zeros_{k}"], bits, gs, N, D)
+                np.testing.assert_array_equal(d.view(np.uint16), f[f"dp_{k}"].view(np.uint16))
+                np.testing.assert_array_equal(d.view(np.uint16), f[f"deq_{k}"].view(np.uint16))
+            x, mask = f[f"x_{tag}"], f[f"mask_{tag}"]
+            for src, pre in ((x, "k"), (f[f"v_{tag}"], "v")):
+                p, s, z = O.group_quantize_fp16(src[mask], bits, gs)
+                np.testing.assert_array_equal(p, f[f"qe_{pre}p_{tag}"])
+                np.testing.assert_array_equal(s.view(np.uint16), f[f"qe_{pre}s_{tag}"].view(np.uint16))
+                np.testing.assert_array_equal(z.view(np.uint16), f[f"qe_{pre}z_{tag}"].view(np.uint16))
+
+
+@pytest.mark.parametrize("shape", [(1, 4, 1, 64), (2, 8, 3, 257), (8, 8, 1, 512), (16, 32, 1, 1000), (4, 8, 2, 3000),
+                                   (8, 8, 1, 4099), (3, 5, 17, 100), (2, 2, 1, 5), (5, 7, 3, 33), (32, 16, 1, 2000)])
+def test_importance_order_is_torch_cpu_order(shape):
+    """The oracle's reduction order equals torch's own CPU result on this
+    host, bit for bit, across column counts that exercise every path (whole
+    blocks, one register, scalar tail) and row counts that exercise every
+    cascade level."""
+    import torch
+    from akv import _C
+    torch.set_num_threads(1)
+    rng = np.random.default_rng(sum(shape))
+    a = rng.random(shape).astype(np.float32)
+    a /= a.sum(-1, keepdims=True)
+    s = rng.random(shape[-1]).astype(np.float32)
+    ref = (torch.from_numpy(s) * 0.9 + torch.from_numpy(a).mean(dim=(0, 1)).sum(dim=0)).numpy()
+    out = O.importance_update(a, s, 0.9, vec_width=_C.cpu_reduction_width())
+    np.testing.assert_array_equal(out, ref)
