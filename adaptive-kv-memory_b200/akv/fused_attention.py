@@ -23,11 +23,23 @@ import torch
 from . import _C
 
 _workspaces: dict = {}
-KERNEL_HEAD_DIM = 128  # head dim of the decode kernel; smaller hot-only inputs are zero-padded to it
+KERNEL_HEAD_DIMS = (64, 128, 256)  # head dims the decode kernel is built for
+KERNEL_HEAD_DIM = 128  # the prefill kernel's head dim
 
 
-def _pad_dim(x: torch.Tensor, d: int = KERNEL_HEAD_DIM) -> torch.Tensor:
-    """Zero-pad the last dim to d: padded channels add 0 to every q.k and give all-zero output columns."""
+def kernel_head_dim(D: int) -> int:
+    """The smallest decode-kernel head dim >= D (0 when D is larger than all)."""
+    for d in KERNEL_HEAD_DIMS:
+        if D <= d:
+            return d
+    return 0
+
+
+def _pad_dim(x: torch.Tensor, d: Optional[int] = None) -> torch.Tensor:
+    """Zero-pad the last dim to d (default: the next decode-kernel head dim):
+    padded channels add 0 to every q.k and give all-zero output columns."""
+    if d is None:
+        d = kernel_head_dim(x.shape[-1]) or x.shape[-1]
     if x.shape[-1] == d:
         return x
     out = torch.zeros(*x.shape[:-1], d, dtype=x.dtype, device=x.device)
@@ -75,7 +87,8 @@ def mixed_tier_decode_attention(query: torch.Tensor,
     B, Hq, D = q3.shape
     if sm_scale is None:
         sm_scale = 1.0 / math.sqrt(D)
-    if D < KERNEL_HEAD_DIM and D % 8 == 0 and warm is None and partial_out is None and out is None:
+    if (D not in KERNEL_HEAD_DIMS and kernel_head_dim(D) and D % 8 == 0 and warm is None and partial_out is None
+            and out is None):
         nh = hot_keys.shape[2] if n_hot is None else int(n_hot)
         res = mixed_tier_decode_attention(_pad_dim(q3), _pad_dim(hot_keys[:, :, :nh]), _pad_dim(hot_values[:, :, :nh]),
                                           None, nh, sm_scale, hot_len, None, return_lse, None, status, None)

@@ -24,7 +24,7 @@ from typing import Optional
 import torch
 
 from . import _C
-from .fused_attention import KERNEL_HEAD_DIM, _pad_dim, mixed_tier_decode_attention
+from .fused_attention import _pad_dim, kernel_head_dim, mixed_tier_decode_attention
 
 
 def padded_dim(D: int, group_size: int) -> int:
@@ -120,8 +120,8 @@ def group_attention(query: torch.Tensor, hot_k: Optional[torch.Tensor], hot_v: O
     the (B, H, M, N_hot + N_warm) fp32 softmax weights in [hot; warm] order."""
     _C.require_cuda(query, hot_k, hot_v, warm_k, warm_v)
     B, H, M, D = query.shape
-    if D > KERNEL_HEAD_DIM or D % 8:
-        raise ValueError(f"head_dim {D} unsupported (multiple of 8, at most {KERNEL_HEAD_DIM})")
+    if not kernel_head_dim(D) or D % 8:
+        raise ValueError(f"head_dim {D} unsupported (multiple of 8, at most 256)")
     if sm_scale is None:
         sm_scale = 1.0 / math.sqrt(D)
     dev = query.device

@@ -6,12 +6,13 @@ The reference's ``AKVLayer.update`` returns the chronologically sorted
 ``"akv"`` to ``transformers.AttentionInterface`` (with the SDPA mask
 builder under the same name).  With ``AKVCache(fused_decode=True)``:
 
-* a decode step (one query token, no padding mask, no sliding window) calls
-  the sm_100a mixed-tier decode kernel on the layer's packed warm block
-  records and FP16 hot tier in place; no FP16 view is built or read;
+* a decode step (one query token, no padding mask, no sliding window, head
+  dim 64, 128 or 256) calls the sm_100a mixed-tier decode kernel on the
+  layer's packed warm block records and FP16 hot tier in place; no FP16
+  view is built or read;
 * a prefill with no padding mask (HF passes none for a plain causal prompt)
-  calls the tcgen05 prefill kernel on the same tiers, causal by token
-  position;
+  at head dim 128 calls the tcgen05 prefill kernel on the same tiers,
+  causal by token position;
 * everything else (masked or padded batches, sliding windows, per-head bit
   widths at prefill, layers without a warm tier, caches that are not fused)
   goes to torch's SDPA over the view, as the reference does.
@@ -34,7 +35,7 @@ from typing import Optional
 
 import torch
 
-from .fused_attention import KERNEL_HEAD_DIM
+from .fused_attention import KERNEL_HEAD_DIM, KERNEL_HEAD_DIMS
 
 NAME = "akv"
 
@@ -48,12 +49,11 @@ def akv_attention_forward(module: torch.nn.Module, query: torch.Tensor, key: tor
 
     layer = getattr(key, "_akv_layer", None)
     if layer is not None:
-        plain = (attention_mask is None and not dropout and kwargs.get("sliding_window") is None
-                 and query.shape[-1] == KERNEL_HEAD_DIM)
-        if plain and query.shape[2] == 1:
+        plain = attention_mask is None and not dropout and kwargs.get("sliding_window") is None
+        if plain and query.shape[2] == 1 and query.shape[-1] in KERNEL_HEAD_DIMS:
             out = layer.decode_attention(query, scaling)  # (B, Hq, 1, D)
             return out.transpose(1, 2), None
-        if plain and is_causal is not False and layer.can_prefill_fused():
+        if plain and query.shape[-1] == KERNEL_HEAD_DIM and is_causal is not False and layer.can_prefill_fused():
             out = layer.prefill_attention(query, scaling)  # (B, Hq, q_len, D), causal by position
             return out.transpose(1, 2), None
         key, value = layer.full_view()

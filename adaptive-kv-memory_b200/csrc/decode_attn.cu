@@ -31,7 +31,12 @@
 
 namespace akv {
 
-constexpr int kHeadDim = 128;
+// head dims the decode kernel is built for (template parameter D): the K side
+// gives each of a warp's four thread columns q4 the channels
+// [q4*D/4, (q4+1)*D/4) (D/128 whole 32-channel record chunks, or half a chunk
+// at D = 64), the V side gives each of its eight thread rows g8 the channels
+// [g8*D/8, (g8+1)*D/8) (D/16 m-tiles of the P.V product)
+constexpr bool decode_head_dim_ok(int D) { return D == 64 || D == 128 || D == 256; }
 constexpr int kConsumerWarps = 4;
 constexpr int kDecodeThreads = kConsumerWarps * 32;
 constexpr int kStagesPerWarp = 2;                          // blocks each warp keeps in flight
@@ -154,6 +159,30 @@ AKV_DEV KWords<KB> k_words(const uint8_t* row, int q4) {
   return r;
 }
 
+// D = 64: thread q4 owns half h = q4 & 1 of chunk q4 >> 1 (16 channels,
+// pairs 8h .. 8h+7 of the chunk, which repeat the pattern of pairs 0..7 with
+// channels + 16), moved into the words pairs 0..7 read.
+template <int KB>
+AKV_DEV KWords<KB> k_words_half(const uint8_t* row, int q4) {
+  KWords<KB> r;
+  if constexpr (KB == 4) {
+    const uint2 v = lds_v2(row + 8 * q4);
+    r.w[0] = v.x;
+    r.w[1] = v.y;
+    r.w[2] = r.w[3] = 0u;
+  } else if constexpr (KB == 2) {
+    r.w[0] = lds_u32(row + 4 * q4);
+    r.w[1] = 0u;
+  } else {
+    const KWords<3> c = k_words<3>(row, q4 >> 1);
+    const bool hi = q4 & 1;
+    r.w[0] = hi ? c.w[2] : c.w[0];
+    r.w[1] = hi ? c.w[3] : c.w[1];
+    r.w[2] = r.w[3] = 0u;
+  }
+  return r;
+}
+
 // Magic pair I (codes kPairs*[I], multiplier kMult*[I]) of a K row chunk.
 template <int KB, int I>
 AKV_DEV uint32_t k_raw(const KWords<KB>& kw) {
@@ -194,12 +223,14 @@ AKV_DEV uint32_t k_raw(const KWords<KB>& kw) {
   }
 }
 
-template <int KB, int I = 0>
-AKV_DEV void q_pairs(const __half (&qv)[32], uint32_t (&qp)[16]) {
-  if constexpr (I < 16) {
+// query pairs of NP pairs (16 for a whole 32-channel chunk, 8 for a half)
+// starting at channel BASE of the thread's query channels, in the K pair order
+template <int KB, int NP, int BASE, int NQ, int I = 0>
+AKV_DEV void q_pairs(const __half (&qv)[NQ], uint32_t (&qp)[NP]) {
+  if constexpr (I < NP) {
     constexpr PairIdx pi = kpair<KB>(I);
-    qp[I] = h2_as_u32(__halves2half2(qv[pi.a], qv[pi.b]));
-    q_pairs<KB, I + 1>(qv, qp);
+    qp[I] = h2_as_u32(__halves2half2(qv[BASE + pi.a], qv[BASE + pi.b]));
+    q_pairs<KB, NP, BASE, NQ, I + 1>(qv, qp);
   }
 }
 
@@ -207,8 +238,8 @@ AKV_DEV void q_pairs(const __half (&qv)[32], uint32_t (&qp)[16]) {
 // dequantised exactly, into the two m-tile accumulators.  ks2 / kz2 point at
 // this thread's chunk of the record's K scale / zero (decode pair order), so
 // each step reads its two (scale, zero) pairs with two 8-byte loads.
-template <int KB, bool FAST, int KS, int KEND>
-AKV_DEV void qk_steps(const KWords<KB> (&W)[2][2], const uint2* ks2, const uint2* kz2, const uint32_t (&qp)[16],
+template <int KB, bool FAST, int KS, int KEND, int QO, int NQP>
+AKV_DEV void qk_steps(const KWords<KB> (&W)[2][2], const uint2* ks2, const uint2* kz2, const uint32_t (&qp)[NQP],
                       float (&c)[2][4]) {
   if constexpr (KS < KEND) {
     constexpr int I0 = 2 * KS, I1 = 2 * KS + 1;
@@ -222,29 +253,43 @@ AKV_DEV void qk_steps(const KWords<KB> (&W)[2][2], const uint2* ks2, const uint2
       const uint32_t a1 = dqx<M0, FAST>(k_raw<KB, I0>(W[mt][1]), s0, b0, z0);
       const uint32_t a2 = dqx<M1, FAST>(k_raw<KB, I1>(W[mt][0]), s1, b1, z1);
       const uint32_t a3 = dqx<M1, FAST>(k_raw<KB, I1>(W[mt][1]), s1, b1, z1);
-      mma_16816(c[mt], a0, a1, a2, a3, qp[I0], qp[I1]);
+      mma_16816(c[mt], a0, a1, a2, a3, qp[QO + I0], qp[QO + I1]);
     }
-    qk_steps<KB, FAST, KS + 1, KEND>(W, ks2, kz2, qp, c);
+    qk_steps<KB, FAST, KS + 1, KEND, QO, NQP>(W, ks2, kz2, qp, c);
   }
 }
 
-// ---- V token pair (ta, tb) of thread group g8 (channels 16*g8 .. +15)
+// ---- V token pair (ta, tb) of 16 channels ch0 .. ch0+15 (ch0 % 16 == 0) of
+// thread group g8; EIGHT: only channels ch0 .. ch0+7 (head dim 64)
 template <int VB>
 struct VRow {
   uint32_t w[VB == 2 ? 1 : 2];
 };
 
-template <int VB>
-AKV_DEV VRow<VB> v_row_load(const uint8_t* row, int g8) {
+template <int VB, bool EIGHT = false>
+AKV_DEV VRow<VB> v_row_load(const uint8_t* row, int ch0) {
   VRow<VB> r;
-  if constexpr (VB == 4) {
-    const uint2 w = lds_v2(row + 8 * g8);
+  if constexpr (EIGHT) {
+    if constexpr (VB == 4) {
+      r.w[0] = lds_u32(row + ch0 / 2);
+      r.w[1] = 0u;
+    } else if constexpr (VB == 2) {
+      r.w[0] = *reinterpret_cast<const uint16_t*>(row + ch0 / 4);
+    } else {
+      const int base = ch0 * 3 / 8;  // 3 bytes: one 24-bit group
+      const uint8_t* p = row + (base & ~3);
+      const uint32_t v0 = __funnelshift_r(lds_u32(p), lds_u32(p + 4), (base & 3) * 8);
+      r.w[0] = prmt(v0, 0u, 0x4012);
+      r.w[1] = 0u;
+    }
+  } else if constexpr (VB == 4) {
+    const uint2 w = lds_v2(row + ch0 / 2);
     r.w[0] = w.x;
     r.w[1] = w.y;
   } else if constexpr (VB == 2) {
-    r.w[0] = lds_u32(row + 4 * g8);
+    r.w[0] = lds_u32(row + ch0 / 4);
   } else {
-    const int base = 6 * g8;
+    const int base = ch0 * 3 / 8;
     const uint8_t* p = row + (base & ~3);
     const uint32_t lo = lds_u32(p), hi = lds_u32(p + 4);
     const int sh = (base & 3) * 8;
@@ -332,8 +377,9 @@ __host__ __device__ constexpr int vmult(int ci) {
 }
 
 // ------------------------------------------------------------------ shared softmax/PV state
+template <int D>
 struct WarpState {
-  float acc[8][4];  // O^T: tile mt rows (g8 -> d=16*g8+2mt, g8+8 -> d+1), cols heads (2q4, 2q4+1)
+  float acc[D / 16][4];  // O^T: tile mt rows (g8 -> d=(D/8)*g8+2mt, g8+8 -> d+1), cols heads (2q4, 2q4+1)
   float mr[2];      // running max of the raw logits q.k for heads 2q4, 2q4+1 (-inf: none yet)
   float nb[2];      // -mr * scale_log2: the exponent offset in use (0 while mr = -inf)
   float l[2];       // partial row sums (this thread's tokens only)
@@ -344,9 +390,10 @@ struct WarpState {
   int vch;
 };
 
-AKV_DEV void state_init(WarpState& s) {
+template <int D>
+AKV_DEV void state_init(WarpState<D>& s) {
 #pragma unroll
-  for (int i = 0; i < 8; ++i)
+  for (int i = 0; i < D / 16; ++i)
 #pragma unroll
     for (int j = 0; j < 4; ++j) s.acc[i][j] = 0.f;
   s.mr[0] = s.mr[1] = -INFINITY;
@@ -359,14 +406,16 @@ AKV_DEV void state_init(WarpState& s) {
 
 // Add the side tile's correction sum_t p_t (original_t - vd_t) into O^T row
 // vch and clear it.  Every lane takes part (shuffles); vch is warp-uniform.
-AKV_DEV void flush_vout(WarpState& s, int g8, int q4) {
+template <int D>
+AKV_DEV void flush_vout(WarpState<D>& s, int g8, int q4) {
+  constexpr int kVpt = D / 8;  // V channels per thread row g8
   const float v0 = __shfl_sync(0xffffffffu, s.vo_acc[0] + s.vo_acc[2], q4);
   const float v1 = __shfl_sync(0xffffffffu, s.vo_acc[1] + s.vo_acc[3], q4);
   const int ch = s.vch;
-  if (ch >= 0 && (ch >> 4) == g8) {
-    const int mt = (ch & 15) >> 1;
+  if (ch >= 0 && ch / kVpt == g8) {
+    const int mt = (ch % kVpt) >> 1;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
+    for (int i = 0; i < D / 16; ++i) {
       if (i == mt) {
         if (ch & 1) {
           s.acc[i][2] += v0;
@@ -397,7 +446,8 @@ AKV_DEV void flush_vout(WarpState& s, int g8, int q4) {
 // scale_log2 > 0, so a masked -inf logit gives p = 0.
 constexpr float kLazyMax = 0.f;
 
-AKV_DEV void online_softmax(WarpState& s, float (&x)[2][4], float sl2, float lazy_raw) {
+template <int D>
+AKV_DEV void online_softmax(WarpState<D>& s, float (&x)[2][4], float sl2, float lazy_raw) {
   float mx[2];
   mx[0] = fmaxf(fmaxf(x[0][0], x[0][2]), fmaxf(x[1][0], x[1][2]));
   mx[1] = fmaxf(fmaxf(x[0][1], x[0][3]), fmaxf(x[1][1], x[1][3]));
@@ -422,7 +472,7 @@ AKV_DEV void online_softmax(WarpState& s, float (&x)[2][4], float sl2, float laz
     s.vo_acc[2] *= alpha[0];
     s.vo_acc[3] *= alpha[1];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
+    for (int i = 0; i < D / 16; ++i) {
       s.acc[i][0] *= alpha[0];
       s.acc[i][1] *= alpha[1];
       s.acc[i][2] *= alpha[0];
@@ -446,19 +496,20 @@ AKV_DEV void p_fragments(const float (&x)[2][4], uint32_t (&pb)[2][2]) {
     for (int r = 0; r < 2; ++r) pb[mt][r] = movmatrix_trans(pack_h2(x[mt][2 * r], x[mt][2 * r + 1]));
 }
 
-// P.V k-step over 16 tokens: for each of the 8 m-tiles (channel pairs 2mt,
-// 2mt+1 of this thread group), the two token pairs, dequantised exactly.
-template <int VB, bool FAST, int MT>
-AKV_DEV void pv_tiles(WarpState& st, const VPair<VB>& v0, const VPair<VB>& v1, uint32_t s0, uint32_t b0,
+// P.V k-step over 16 tokens: m-tiles MT .. MEND-1 (channel pairs 2(mt%8),
+// 2(mt%8)+1 of the 16-channel group the token-pair codes v0 / v1 hold), the
+// two token pairs, dequantised exactly.
+template <int VB, bool FAST, int MT, int MEND, int D>
+AKV_DEV void pv_tiles(WarpState<D>& st, const VPair<VB>& v0, const VPair<VB>& v1, uint32_t s0, uint32_t b0,
                       uint32_t z0, uint32_t s1, uint32_t b1, uint32_t z1, const uint32_t (&pb)[2]) {
-  if constexpr (MT < 8) {
-    constexpr int C0 = 2 * MT, C1 = 2 * MT + 1;
+  if constexpr (MT < MEND) {
+    constexpr int C0 = 2 * (MT % 8), C1 = 2 * (MT % 8) + 1;
     const uint32_t a0 = dqx<vmult<VB>(C0), FAST>(v_raw<VB, C0>(v0), s0, b0, z0);
     const uint32_t a1 = dqx<vmult<VB>(C1), FAST>(v_raw<VB, C1>(v0), s0, b0, z0);
     const uint32_t a2 = dqx<vmult<VB>(C0), FAST>(v_raw<VB, C0>(v1), s1, b1, z1);
     const uint32_t a3 = dqx<vmult<VB>(C1), FAST>(v_raw<VB, C1>(v1), s1, b1, z1);
     mma_16816(st.acc[MT], a0, a1, a2, a3, pb[0], pb[1]);
-    pv_tiles<VB, FAST, MT + 1>(st, v0, v1, s0, b0, z0, s1, b1, z1, pb);
+    pv_tiles<VB, FAST, MT + 1, MEND, D>(st, v0, v1, s0, b0, z0, s1, b1, z1, pb);
   }
 }
 
@@ -468,42 +519,42 @@ AKV_DEV void pv_tiles(WarpState& st, const VPair<VB>& v0, const VPair<VB>& v1, u
 // fp16) whose A operand is zero except row ch.  ch is the same for the whole
 // warp, so the target tile MT = (ch & 15) / 2 is a warp-uniform switch and
 // every accumulator index stays a compile-time constant.
-template <int MT>
-AKV_DEV void outlier_tile(WarpState& st, const uint32_t (&ao)[4], const uint32_t (&an)[4], const uint32_t (&pb)[2]) {
+template <int MT, int D>
+AKV_DEV void outlier_tile(WarpState<D>& st, const uint32_t (&ao)[4], const uint32_t (&an)[4],
+                          const uint32_t (&pb)[2]) {
   mma_16816(st.acc[MT], ao[0], ao[1], ao[2], ao[3], pb[0], pb[1]);
   mma_16816(st.acc[MT], an[0], an[1], an[2], an[3], pb[0], pb[1]);
 }
 
-AKV_DEV void outlier_mma(WarpState& st, int mt, const uint32_t (&ao)[4], const uint32_t (&an)[4],
+// tile mt (warp-uniform) as a chain of compile-time cases
+template <int D, int MT = 0>
+AKV_DEV void outlier_mma(WarpState<D>& st, int mt, const uint32_t (&ao)[4], const uint32_t (&an)[4],
                          const uint32_t (&pb)[2]) {
-  switch (mt) {
-    case 0: outlier_tile<0>(st, ao, an, pb); break;
-    case 1: outlier_tile<1>(st, ao, an, pb); break;
-    case 2: outlier_tile<2>(st, ao, an, pb); break;
-    case 3: outlier_tile<3>(st, ao, an, pb); break;
-    case 4: outlier_tile<4>(st, ao, an, pb); break;
-    case 5: outlier_tile<5>(st, ao, an, pb); break;
-    case 6: outlier_tile<6>(st, ao, an, pb); break;
-    default: outlier_tile<7>(st, ao, an, pb); break;
+  if constexpr (MT + 1 < D / 16) {
+    if (mt == MT) outlier_tile<MT, D>(st, ao, an, pb);
+    else outlier_mma<D, MT + 1>(st, mt, ao, an, pb);
+  } else {
+    outlier_tile<MT, D>(st, ao, an, pb);
   }
 }
 
 // ------------------------------------------------------------------ epilogue
 // Reduce the per-thread partials of one warp and park them in shared memory:
 // red[h][d] (fp32, natural channel order), rm[h], rl[h].
-AKV_DEV void warp_to_smem(WarpState& s, int lane, float* red, float* rm, float* rl) {
+template <int D>
+AKV_DEV void warp_to_smem(WarpState<D>& s, int lane, float* red, float* rm, float* rl) {
   const int g8 = lane >> 2, q4 = lane & 3;
 #pragma unroll
   for (int h = 0; h < 2; ++h)
 #pragma unroll
     for (int o = 4; o < 32; o <<= 1) s.l[h] += __shfl_xor_sync(0xffffffffu, s.l[h], o);
 #pragma unroll
-  for (int mt = 0; mt < 8; ++mt) {
-    const int d = 16 * g8 + 2 * mt;
-    red[(2 * q4) * kHeadDim + d] = s.acc[mt][0];
-    red[(2 * q4 + 1) * kHeadDim + d] = s.acc[mt][1];
-    red[(2 * q4) * kHeadDim + d + 1] = s.acc[mt][2];
-    red[(2 * q4 + 1) * kHeadDim + d + 1] = s.acc[mt][3];
+  for (int mt = 0; mt < D / 16; ++mt) {
+    const int d = (D / 8) * g8 + 2 * mt;
+    red[(2 * q4) * D + d] = s.acc[mt][0];
+    red[(2 * q4 + 1) * D + d] = s.acc[mt][1];
+    red[(2 * q4) * D + d + 1] = s.acc[mt][2];
+    red[(2 * q4 + 1) * D + d + 1] = s.acc[mt][3];
   }
   if (g8 == 0) {  // partial (acc, m, l) with acc and l relative to 2^m, m = -nb (log2 units)
     rm[2 * q4] = s.l[0] == 0.f ? -INFINITY : -s.nb[0];
@@ -514,11 +565,12 @@ AKV_DEV void warp_to_smem(WarpState& s, int lane, float* red, float* rm, float* 
 }
 
 // Merge the consumer warps' partials and write this CTA's split partial.
+template <int D>
 AKV_DEV void cta_write_partial(const DecodeParams& p, float* red, float* rm, float* rl, int b, int kvh, int hg,
                                int split) {
   const int nh = min(8, p.g - hg * 8);
-  for (int i = threadIdx.x; i < nh * kHeadDim; i += blockDim.x) {
-    const int h = i / kHeadDim, d = i % kHeadDim;
+  for (int i = threadIdx.x; i < nh * D; i += blockDim.x) {
+    const int h = i / D, d = i % D;
     float M = -INFINITY;
 #pragma unroll
     for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, rm[w * 8 + h]);
@@ -527,15 +579,15 @@ AKV_DEV void cta_write_partial(const DecodeParams& p, float* red, float* rm, flo
 #pragma unroll
     for (int w = 0; w < kConsumerWarps; ++w) {
       const float f = fast_exp2(rm[w * 8 + h] - base);
-      acc += f * red[(w * 8 + h) * kHeadDim + d];
+      acc += f * red[(w * 8 + h) * D + d];
       L += f * rl[w * 8 + h];
     }
     const int hq = kvh * p.g + hg * 8 + h;
-    float* part = p.ws + ((static_cast<int64_t>(b) * p.Hq + hq) * p.splits + split) * (kHeadDim + 2);
+    float* part = p.ws + ((static_cast<int64_t>(b) * p.Hq + hq) * p.splits + split) * (D + 2);
     part[d] = acc;
     if (d == 0) {
-      part[kHeadDim] = M;
-      part[kHeadDim + 1] = L;
+      part[D] = M;
+      part[D + 1] = L;
     }
   }
 }
@@ -549,12 +601,13 @@ AKV_DEV void cta_write_partial(const DecodeParams& p, float* red, float* rm, flo
 // NOUT: 0 = no outlier channels; 1 = one (K: q[ch] * original added to the
 // logits with FFMAs, V: the side tile of WarpState); 2 = any n_out <= 8
 // (extra MMAs per channel).
-template <int KB, int VB, int NOUT, bool FAST>
-AKV_DEV void warm_block(WarpState& st, const uint8_t* r, uint32_t mask, const uint32_t (&qp)[16], const float* qs,
-                        int n_out, float sl2, float lazy_raw, int g8, int q4) {
-  constexpr RecLayout R = rec_layout(kHeadDim, KB, VB, 0);
-  constexpr RecLayout R1 = rec_layout(kHeadDim, KB, VB, 1);
-  constexpr int kp = kHeadDim * KB / 8, vp = kHeadDim * VB / 8;
+template <int D, int KB, int VB, int NOUT, bool FAST>
+AKV_DEV void warm_block(WarpState<D>& st, const uint8_t* r, uint32_t mask, const uint32_t (&qp)[D / 8],
+                        const float* qs, int n_out, float sl2, float lazy_raw, int g8, int q4) {
+  constexpr RecLayout R = rec_layout(D, KB, VB, 0);
+  constexpr RecLayout R1 = rec_layout(D, KB, VB, 1);
+  constexpr int kp = D * KB / 8, vp = D * VB / 8;
+  constexpr int kVpt = D / 8;  // V channels of thread row g8: [kVpt*g8, kVpt*(g8+1))
 
   // one outlier channel: fetch its ids, the query at the K channel and the K
   // originals of this thread's tokens before the main work
@@ -562,8 +615,8 @@ AKV_DEV void warm_block(WarpState& st, const uint8_t* r, uint32_t mask, const ui
   if constexpr (NOUT == 1) {
     const int kch = *reinterpret_cast<const int16_t*>(r + R1.ki);
     const int vch = *reinterpret_cast<const int16_t*>(r + R1.vi);
-    qk1[0] = qs[(2 * q4) * kHeadDim + kch];
-    qk1[1] = qs[(2 * q4 + 1) * kHeadDim + kch];
+    qk1[0] = qs[(2 * q4) * D + kch];
+    qk1[1] = qs[(2 * q4 + 1) * D + kch];
     const __half* ko = reinterpret_cast<const __half*>(r + R1.ko);
 #pragma unroll
     for (int mt = 0; mt < 2; ++mt)
@@ -575,15 +628,39 @@ AKV_DEV void warm_block(WarpState& st, const uint8_t* r, uint32_t mask, const ui
     }
   }
 
-  // ---- S^T = K^ q  (tokens x heads): rows 16mt + 8rr + g8, k-steps over channel pairs
-  KWords<KB> W[2][2];
-#pragma unroll
-  for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-    for (int rr = 0; rr < 2; ++rr) W[mt][rr] = k_words<KB>(r + R.kc + (16 * mt + 8 * rr + g8) * kp, q4);
+  // ---- S^T = K^ q  (tokens x heads): rows 16mt + 8rr + g8, k-steps over channel pairs;
+  // one pass of 8 k-steps per 32-channel chunk of the thread (4 k-steps over half a chunk at D = 64)
   float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-  qk_steps<KB, FAST, 0, 8>(W, reinterpret_cast<const uint2*>(r + R.ks) + 8 * q4,
-                           reinterpret_cast<const uint2*>(r + R.kz) + 8 * q4, qp, c);
+  const uint2* ks2 = reinterpret_cast<const uint2*>(r + R.ks);
+  const uint2* kz2 = reinterpret_cast<const uint2*>(r + R.kz);
+  if constexpr (D == 64) {
+    KWords<KB> W[2][2];
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) W[mt][rr] = k_words_half<KB>(r + R.kc + (16 * mt + 8 * rr + g8) * kp, q4);
+    qk_steps<KB, FAST, 0, 4, 0, D / 8>(W, ks2 + 4 * q4, kz2 + 4 * q4, qp, c);
+  } else {
+    constexpr int kCh = D / 128;  // 32-channel chunks per thread
+    {
+      const int ch = kCh * q4;
+      KWords<KB> W[2][2];
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) W[mt][rr] = k_words<KB>(r + R.kc + (16 * mt + 8 * rr + g8) * kp, ch);
+      qk_steps<KB, FAST, 0, 8, 0, D / 8>(W, ks2 + 8 * ch, kz2 + 8 * ch, qp, c);
+    }
+    if constexpr (kCh == 2) {
+      const int ch = kCh * q4 + 1;
+      KWords<KB> W[2][2];
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) W[mt][rr] = k_words<KB>(r + R.kc + (16 * mt + 8 * rr + g8) * kp, ch);
+      qk_steps<KB, FAST, 0, 8, 16, D / 8>(W, ks2 + 8 * ch, kz2 + 8 * ch, qp, c);
+    }
+  }
   // K outlier channels: their dequantised value is 0 (scale = zero = 0) and the
   // reference puts the fp16 original there.  One channel: + q[ch] * original
   // per logit.  General: one more MMA whose k slots 2q4, 2q4+1 are outliers
@@ -601,8 +678,8 @@ AKV_DEV void warm_block(WarpState& st, const uint8_t* r, uint32_t mask, const ui
     const int16_t* kid = reinterpret_cast<const int16_t*>(r + R.ki);
     const int j0 = 2 * q4, j1 = 2 * q4 + 1;
     const __half hz = __float2half_rn(0.f);
-    const __half qa = j0 < n_out ? __float2half_rn(qs[g8 * kHeadDim + kid[j0]]) : hz;
-    const __half qb = j1 < n_out ? __float2half_rn(qs[g8 * kHeadDim + kid[j1]]) : hz;
+    const __half qa = j0 < n_out ? __float2half_rn(qs[g8 * D + kid[j0]]) : hz;
+    const __half qb = j1 < n_out ? __float2half_rn(qs[g8 * D + kid[j1]]) : hz;
     const uint32_t bq = h2_as_u32(__halves2half2(qa, qb));
 #pragma unroll
     for (int mt = 0; mt < 2; ++mt) {
@@ -639,12 +716,21 @@ AKV_DEV void warm_block(WarpState& st, const uint8_t* r, uint32_t mask, const ui
   for (int ks = 0; ks < 2; ++ks) {
     const int ta = 16 * ks + 2 * q4;
     const uint8_t* vc = r + R.vc;
-    const VPair<VB> v0 = v_pair<VB>(v_row_load<VB>(vc + ta * vp, g8), v_row_load<VB>(vc + (ta + 1) * vp, g8));
-    const VPair<VB> v1 = v_pair<VB>(v_row_load<VB>(vc + (ta + 8) * vp, g8), v_row_load<VB>(vc + (ta + 9) * vp, g8));
     const uint32_t s0 = lds_u32(vsc + ta), z0 = lds_u32(vzr + ta);
     const uint32_t s1 = lds_u32(vsc + ta + 8), z1 = lds_u32(vzr + ta + 8);
     const uint32_t b0 = FAST ? neg1024(s0) : 0u, b1 = FAST ? neg1024(s1) : 0u;
-    pv_tiles<VB, FAST, 0>(st, v0, v1, s0, b0, z0, s1, b1, z1, pb[ks]);
+    constexpr bool kEight = D == 64;  // 8 V channels per thread row: half a 16-channel group
+#pragma unroll
+    for (int j = 0; j < (kEight ? 1 : kVpt / 16); ++j) {  // 16-channel groups of the thread row
+      const int ch0 = kVpt * g8 + 16 * j;
+      const VPair<VB> v0 = v_pair<VB>(v_row_load<VB, kEight>(vc + ta * vp, ch0),
+                                      v_row_load<VB, kEight>(vc + (ta + 1) * vp, ch0));
+      const VPair<VB> v1 = v_pair<VB>(v_row_load<VB, kEight>(vc + (ta + 8) * vp, ch0),
+                                      v_row_load<VB, kEight>(vc + (ta + 9) * vp, ch0));
+      if (j == 0) pv_tiles<VB, FAST, 0, (kEight ? 4 : 8), D>(st, v0, v1, s0, b0, z0, s1, b1, z1, pb[ks]);
+      if constexpr (kVpt / 16 == 2)
+        if (j == 1) pv_tiles<VB, FAST, 8, 16, D>(st, v0, v1, s0, b0, z0, s1, b1, z1, pb[ks]);
+    }
   }
 
   // ---- V outlier channels: O^T row ch += sum_t p_t (original_t - vd_t).
@@ -670,7 +756,7 @@ AKV_DEV void warm_block(WarpState& st, const uint8_t* r, uint32_t mask, const ui
     const int16_t* vid = reinterpret_cast<const int16_t*>(r + R.ki + 2 * n_out);
     for (int j = 0; j < n_out; ++j) {
       const int ch = vid[j];
-      const bool own = (ch >> 4) == g8;
+      const bool own = ch / kVpt == g8;
       const int hf = ch & 1;
 #pragma unroll
       for (int ks = 0; ks < 2; ++ks) {
@@ -684,7 +770,7 @@ AKV_DEV void warm_block(WarpState& st, const uint8_t* r, uint32_t mask, const ui
         const uint32_t ao[4] = {o0 & m0, o0 & m1, o1 & m0, o1 & m1};
         const uint32_t an[4] = {(d0 ^ 0x80008000u) & m0, (d0 ^ 0x80008000u) & m1, (d1 ^ 0x80008000u) & m0,
                                 (d1 ^ 0x80008000u) & m1};
-        outlier_mma(st, (ch & 15) >> 1, ao, an, pb[ks]);
+        outlier_mma<D>(st, (ch % kVpt) >> 1, ao, an, pb[ks]);
       }
     }
   }
@@ -693,9 +779,16 @@ AKV_DEV void warm_block(WarpState& st, const uint8_t* r, uint32_t mask, const ui
 // PAGED: warm records are found through the block table (p.btab), else row
 // b's records are contiguous; a compile-time choice, so the contiguous kernel
 // carries no table logic.
-template <int KB, int VB, int NOUT, bool PAGED>
-__global__ void __launch_bounds__(kDecodeThreads, 4) mixed_decode_kernel(const DecodeParams p) {
-  constexpr RecLayout R = rec_layout(kHeadDim, KB, VB, 0);
+// resident CTAs per SM the kernel is built for: head dim 256 keeps twice the
+// O^T accumulators and query pairs per thread, so it gets more registers
+__host__ __device__ constexpr int decode_ctas_per_sm(int D) { return D == 256 ? 2 : 4; }
+
+template <int D, int KB, int VB, int NOUT, bool PAGED>
+__global__ void __launch_bounds__(kDecodeThreads, decode_ctas_per_sm(D)) mixed_decode_kernel(const DecodeParams p) {
+  static_assert(decode_head_dim_ok(D), "head dim 64, 128 or 256");
+  constexpr RecLayout R = rec_layout(D, KB, VB, 0);
+  constexpr int kCpt = D / 4;  // K-side query channels of thread column q4: [kCpt*q4, kCpt*(q4+1))
+  constexpr int kVpt = D / 8;  // V-side channels of thread row g8
   extern __shared__ __align__(128) unsigned char smem[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g8 = lane >> 2, q4 = lane & 3;
@@ -707,18 +800,18 @@ __global__ void __launch_bounds__(kDecodeThreads, 4) mixed_decode_kernel(const D
   // shared memory map
   const int rec = p.L.bytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);        // [kStages], 96 bytes
-  float* qs = reinterpret_cast<float*>(smem + 256);               // [8][128] query (fp32) for outliers
-  unsigned char* stage0 = smem + 256 + 8 * kHeadDim * 4;          // [kStages][rec]
+  float* qs = reinterpret_cast<float*>(smem + 256);               // [8][D] query (fp32) for outliers
+  unsigned char* stage0 = smem + 256 + 8 * D * 4;                 // [kStages][rec]
   // epilogue buffers alias the stages once the main loop is over
-  float* red = reinterpret_cast<float*>(stage0);                  // [warps][8][128]
-  float* rm = red + kConsumerWarps * 8 * kHeadDim;                // [warps][8]
+  float* red = reinterpret_cast<float*>(stage0);                  // [warps][8][D]
+  float* rm = red + kConsumerWarps * 8 * D;                       // [warps][8]
   float* rl = rm + kConsumerWarps * 8;
 
   const int nh = min(8, p.g - hg * 8);
   const int qh_base = kvh * p.g + hg * 8;
   const float sl2 = p.scale_log2, lazy_raw = p.lazy_raw;
 
-  WarpState st;
+  WarpState<D> st;
   state_init(st);
 
   // warm CTAs: every warp initialises its own stage barriers and puts its
@@ -770,12 +863,12 @@ __global__ void __launch_bounds__(kDecodeThreads, 4) mixed_decode_kernel(const D
   // this thread's query column (head g8 of the head group; zero padding beyond nh);
   // a negative softmax scale is applied as -q (exact) with scale |sm_scale|
   const uint32_t qflip = p.q_neg ? 0x80008000u : 0u;
-  __half qv[32];
+  __half qv[kCpt];
   {
     const bool have = g8 < nh;
-    const __half* qrow = p.q + b * p.q_sb + (qh_base + (have ? g8 : 0)) * p.q_sh + 32 * q4;
+    const __half* qrow = p.q + b * p.q_sb + (qh_base + (have ? g8 : 0)) * p.q_sh + kCpt * q4;
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
+    for (int k = 0; k < kCpt / 8; ++k) {
       uint4 v = have ? ldg_nc_v4(qrow + 8 * k) : make_uint4(0, 0, 0, 0);
       v.x ^= qflip;
       v.y ^= qflip;
@@ -786,17 +879,31 @@ __global__ void __launch_bounds__(kDecodeThreads, 4) mixed_decode_kernel(const D
   }
   if (warp == 0) {  // fp32 copy of the head group's queries for the outlier terms
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
+    for (int k = 0; k < kCpt / 4; ++k) {
       const float4 f = make_float4(__half2float(qv[4 * k]), __half2float(qv[4 * k + 1]), __half2float(qv[4 * k + 2]),
                                    __half2float(qv[4 * k + 3]));
-      *reinterpret_cast<float4*>(qs + g8 * kHeadDim + 32 * q4 + 4 * k) = f;
+      *reinterpret_cast<float4*>(qs + g8 * D + kCpt * q4 + 4 * k) = f;
     }
   }
   __syncthreads();
 
   if (warm_cta) {
-    uint32_t qp[16];
-    q_pairs<KB>(qv, qp);
+    // query pairs in the K pair order: 16 per 32-channel chunk (8 for the half chunk at D = 64)
+    uint32_t qp[D / 8];
+    if constexpr (D == 64) {
+      q_pairs<KB, 8, 0, kCpt>(qv, qp);
+    } else {
+      uint32_t q0[16];
+      q_pairs<KB, 16, 0, kCpt>(qv, q0);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) qp[i] = q0[i];
+      if constexpr (D == 256) {
+        uint32_t q1[16];
+        q_pairs<KB, 16, 32, kCpt>(qv, q1);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) qp[16 + i] = q1[i];
+      }
+    }
     const int n_out = p.L.n_outlier;
 
     int waited = 0;  // blocks whose copy this warp has seen land
@@ -807,9 +914,9 @@ __global__ void __launch_bounds__(kDecodeThreads, 4) mixed_decode_kernel(const D
       const uint8_t* r = wstage + s * rec;
       const uint2 mf = lds_v2(r + R.mask);  // valid-slot mask, decode flags
       if ((mf.y & 0xFFFFu) == 0x0101u)
-        warm_block<KB, VB, NOUT, true>(st, r, mf.x, qp, qs, n_out, sl2, lazy_raw, g8, q4);
+        warm_block<D, KB, VB, NOUT, true>(st, r, mf.x, qp, qs, n_out, sl2, lazy_raw, g8, q4);
       else
-        warm_block<KB, VB, NOUT, false>(st, r, mf.x, qp, qs, n_out, sl2, lazy_raw, g8, q4);
+        warm_block<D, KB, VB, NOUT, false>(st, r, mf.x, qp, qs, n_out, sl2, lazy_raw, g8, q4);
       // refill this stage with the warp's block li+3 once every lane is done reading it
       __syncwarp();
       if (lane == 0 && li + kStagesPerWarp < nmine) {
@@ -834,9 +941,12 @@ __global__ void __launch_bounds__(kDecodeThreads, 4) mixed_decode_kernel(const D
     const int nhb = (nhot_b + 31) / 32;
     const int blo = hs * p.hbps;
     const int bhi = min(nhb, blo + p.hbps);
-    uint32_t qn[16];
+    // K rows in passes of up to 32 channels (16 words, 8 k-steps) of the thread's kCpt
+    constexpr int kPassCh = kCpt < 32 ? kCpt : 32;
+    constexpr int kPasses = kCpt / kPassCh;
+    uint32_t qn[kCpt / 2];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) qn[i] = h2_as_u32(__halves2half2(qv[2 * i], qv[2 * i + 1]));
+    for (int i = 0; i < kCpt / 2; ++i) qn[i] = h2_as_u32(__halves2half2(qv[2 * i], qv[2 * i + 1]));
     const __half* kb = p.hk + b * p.h_sb + kvh * p.h_sh;
     const __half* vb = p.hv + b * p.h_sb + kvh * p.h_sh;
     for (int blk = blo + warp; blk < bhi; blk += kConsumerWarps) {
@@ -845,26 +955,31 @@ __global__ void __launch_bounds__(kDecodeThreads, 4) mixed_decode_kernel(const D
       bool valid[2][2];
 #pragma unroll
       for (int mt = 0; mt < 2; ++mt) {
-        uint32_t e0[16], e1[16];
-#pragma unroll
-        for (int rr = 0; rr < 2; ++rr) {
-          const int t = t0 + 16 * mt + 8 * rr + g8;
-          valid[mt][rr] = t < nhot_b;
-          uint32_t* e = rr ? e1 : e0;
-          const __half* row = kb + static_cast<int64_t>(valid[mt][rr] ? t : 0) * p.h_sn + 32 * q4;
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const uint4 v = valid[mt][rr] ? ldg_nc_v4(row + 8 * k) : make_uint4(0, 0, 0, 0);
-            e[4 * k + 0] = v.x;
-            e[4 * k + 1] = v.y;
-            e[4 * k + 2] = v.z;
-            e[4 * k + 3] = v.w;
-          }
-        }
         float c[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks)
-          mma_16816(c, e0[2 * ks], e1[2 * ks], e0[2 * ks + 1], e1[2 * ks + 1], qn[2 * ks], qn[2 * ks + 1]);
+        for (int pass = 0; pass < kPasses; ++pass) {
+          uint32_t e0[kPassCh / 2], e1[kPassCh / 2];
+#pragma unroll
+          for (int rr = 0; rr < 2; ++rr) {
+            const int t = t0 + 16 * mt + 8 * rr + g8;
+            valid[mt][rr] = t < nhot_b;
+            uint32_t* e = rr ? e1 : e0;
+            const __half* row =
+                kb + static_cast<int64_t>(valid[mt][rr] ? t : 0) * p.h_sn + kCpt * q4 + kPassCh * pass;
+#pragma unroll
+            for (int k = 0; k < kPassCh / 8; ++k) {
+              const uint4 v = valid[mt][rr] ? ldg_nc_v4(row + 8 * k) : make_uint4(0, 0, 0, 0);
+              e[4 * k + 0] = v.x;
+              e[4 * k + 1] = v.y;
+              e[4 * k + 2] = v.z;
+              e[4 * k + 3] = v.w;
+            }
+          }
+#pragma unroll
+          for (int ks = 0; ks < kPassCh / 4; ++ks)
+            mma_16816(c, e0[2 * ks], e1[2 * ks], e0[2 * ks + 1], e1[2 * ks + 1], qn[kPassCh / 2 * pass + 2 * ks],
+                      qn[kPassCh / 2 * pass + 2 * ks + 1]);
+        }
 #pragma unroll
         for (int j = 0; j < 4; ++j) x[mt][j] = valid[mt][j >> 1] ? c[j] : -INFINITY;
       }
@@ -873,25 +988,34 @@ __global__ void __launch_bounds__(kDecodeThreads, 4) mixed_decode_kernel(const D
       p_fragments(x, pb);
 #pragma unroll
       for (int ks = 0; ks < 2; ++ks) {
-        uint32_t va[4][8];
+        // the thread row's V channels in groups of 16 (8 at D = 64): m-tiles 8j .. 8j + kW - 1
+        constexpr int kW = D == 64 ? 4 : 8;  // words (channel pairs) per group
 #pragma unroll
-        for (int tt = 0; tt < 4; ++tt) {
-          const int t = t0 + 16 * ks + 2 * q4 + (tt & 1) + 8 * (tt >> 1);
-          const bool ok = t < nhot_b;
-          const __half* row = vb + static_cast<int64_t>(ok ? t : 0) * p.h_sn + 16 * g8;
-          const uint4 v0 = ok ? ldg_nc_v4(row) : make_uint4(0, 0, 0, 0);
-          const uint4 v1 = ok ? ldg_nc_v4(row + 8) : make_uint4(0, 0, 0, 0);
-          va[tt][0] = v0.x; va[tt][1] = v0.y; va[tt][2] = v0.z; va[tt][3] = v0.w;
-          va[tt][4] = v1.x; va[tt][5] = v1.y; va[tt][6] = v1.z; va[tt][7] = v1.w;
-        }
+        for (int j = 0; j < kVpt / (2 * kW); ++j) {
+          uint32_t va[4][kW];
 #pragma unroll
-        for (int mt = 0; mt < 8; ++mt) {
-          // channel pair (2mt, 2mt+1) of this thread group's chunk lives in word mt
-          const uint32_t a0 = prmt(va[0][mt], va[1][mt], 0x5410);  // (ta, tb) at channel 2mt
-          const uint32_t a1 = prmt(va[0][mt], va[1][mt], 0x7632);  // (ta, tb) at channel 2mt+1
-          const uint32_t a2 = prmt(va[2][mt], va[3][mt], 0x5410);
-          const uint32_t a3 = prmt(va[2][mt], va[3][mt], 0x7632);
-          mma_16816(st.acc[mt], a0, a1, a2, a3, pb[ks][0], pb[ks][1]);
+          for (int tt = 0; tt < 4; ++tt) {
+            const int t = t0 + 16 * ks + 2 * q4 + (tt & 1) + 8 * (tt >> 1);
+            const bool ok = t < nhot_b;
+            const __half* row = vb + static_cast<int64_t>(ok ? t : 0) * p.h_sn + kVpt * g8 + 2 * kW * j;
+#pragma unroll
+            for (int k = 0; k < kW / 4; ++k) {
+              const uint4 v = ok ? ldg_nc_v4(row + 8 * k) : make_uint4(0, 0, 0, 0);
+              va[tt][4 * k + 0] = v.x;
+              va[tt][4 * k + 1] = v.y;
+              va[tt][4 * k + 2] = v.z;
+              va[tt][4 * k + 3] = v.w;
+            }
+          }
+#pragma unroll
+          for (int m = 0; m < kW; ++m) {
+            // channel pair (2mt, 2mt+1) of this thread row's channels lives in word m of group j
+            const uint32_t a0 = prmt(va[0][m], va[1][m], 0x5410);  // (ta, tb) at channel 2mt
+            const uint32_t a1 = prmt(va[0][m], va[1][m], 0x7632);  // (ta, tb) at channel 2mt+1
+            const uint32_t a2 = prmt(va[2][m], va[3][m], 0x5410);
+            const uint32_t a3 = prmt(va[2][m], va[3][m], 0x7632);
+            mma_16816(st.acc[kW * j + m], a0, a1, a2, a3, pb[ks][0], pb[ks][1]);
+          }
         }
       }
     }
@@ -900,9 +1024,9 @@ __global__ void __launch_bounds__(kDecodeThreads, 4) mixed_decode_kernel(const D
   // ---------------- epilogue: merge consumer warps, write the split partial
   if constexpr (NOUT == 1) flush_vout(st, g8, q4);
   __syncthreads();
-  warp_to_smem(st, lane, red + warp * 8 * kHeadDim, rm + warp * 8, rl + warp * 8);
+  warp_to_smem(st, lane, red + warp * 8 * D, rm + warp * 8, rl + warp * 8);
   __syncthreads();
-  cta_write_partial(p, red, rm, rl, b, kvh, hg, split);
+  cta_write_partial<D>(p, red, rm, rl, b, kvh, hg, split);
 }
 
 // ------------------------------------------------------------------ LSE combine
@@ -1020,10 +1144,12 @@ struct DecodePlan {
 // Split-K plan.  A unit is one (batch row, KV head, <= 8 query heads); its
 // tokens are split into warm and hot splits in proportion to their bytes.
 // The split count per unit is chosen so that the grid fills its last wave of
-// kDecodeSlots resident CTAs well, from at least ~3 waves (a half-empty last
+// decode_slots(D) resident CTAs well, from at least ~3 waves (a half-empty last
 // wave leaves SMs idle at the end of the launch); config 3 (128 units) gets
 // 18 splits: 2,304 CTAs, 3.9 waves.
-constexpr int kDecodeSlots = 148 * 4;  // 148 SMs x 4 resident decode CTAs
+constexpr int kSms = 148;
+// resident decode CTAs of the whole GPU at head dim D
+static int decode_slots(int D) { return kSms * decode_ctas_per_sm(D); }
 // Device time per byte of a hot CTA relative to a warm one: a hot warp streams
 // plain fp16 rows (16 KB per 32-token block, two DRAM round trips, little
 // arithmetic) while a warm warp dequantises ~3.9 KB records, so hot splits
@@ -1063,9 +1189,9 @@ constexpr int kMinBlocksPerSplit = 16;
 constexpr int kFewUnits = 64;
 
 // candidate split counts per unit: [lo, hi]; unit_blocks = warm + hot blocks of one unit
-static void per_unit_range(int units, int unit_blocks, int& lo, int& hi) {
+static void per_unit_range(int units, int unit_blocks, int slots, int& lo, int& hi) {
   const int waves = units <= kFewUnits ? 1 : 3;
-  lo = max(1, (waves * kDecodeSlots + units - 1) / units);
+  lo = max(1, (waves * slots + units - 1) / units);
   hi = lo + max(8, lo);
   const int cap = max(1, unit_blocks / kMinBlocksPerSplit);
   if (hi > cap) {
@@ -1074,23 +1200,24 @@ static void per_unit_range(int units, int unit_blocks, int& lo, int& hi) {
   }
 }
 
-static DecodePlan plan_decode(int B, int Hq, int Hkv, int n_hot, int n_warm_blocks, int rec_bytes) {
+static DecodePlan plan_decode(int B, int Hq, int Hkv, int D, int n_hot, int n_warm_blocks, int rec_bytes) {
   DecodePlan pl{};
   const int g = Hq / Hkv;
   pl.n_hg = (g + 7) / 8;
   const int units = B * Hkv * pl.n_hg;
   const int nhb = (n_hot + 31) / 32;
   const double wbytes = static_cast<double>(n_warm_blocks) * rec_bytes;
-  const double hbytes = static_cast<double>(nhb) * 32 * kHeadDim * 4 * kHotCost;
+  const double hbytes = static_cast<double>(nhb) * 32 * D * 4 * kHotCost;
+  const int slots = decode_slots(D);
   int lo, hi;
-  per_unit_range(units, n_warm_blocks + nhb, lo, hi);
+  per_unit_range(units, n_warm_blocks + nhb, slots, lo, hi);
   double best = -1.0;
   DecodePlan cand = pl;
   for (int pu = lo; pu <= hi; ++pu) {
     split_shares(pu, n_warm_blocks, nhb, wbytes, hbytes, cand);
     const int64_t ctas = static_cast<int64_t>(units) * cand.splits;
-    const int64_t waves = (ctas + kDecodeSlots - 1) / kDecodeSlots;
-    const double fill = static_cast<double>(ctas) / static_cast<double>(waves * kDecodeSlots);
+    const int64_t waves = (ctas + slots - 1) / slots;
+    const double fill = static_cast<double>(ctas) / static_cast<double>(waves * slots);
     if (fill > best + 0.03) {  // more splits only for a clearly fuller last wave
       best = fill;
       pl.warm_splits = cand.warm_splits;
@@ -1103,16 +1230,16 @@ static DecodePlan plan_decode(int B, int Hq, int Hkv, int n_hot, int n_warm_bloc
   return pl;
 }
 
-static size_t decode_smem_bytes(int rec_bytes) {
+static size_t decode_smem_bytes(int rec_bytes, int D) {
   const size_t ring = static_cast<size_t>(kStages) * rec_bytes;
-  const size_t epi = static_cast<size_t>(kConsumerWarps) * 8 * kHeadDim * 4 + kConsumerWarps * 8 * 8;
-  return 256 + 8 * kHeadDim * 4 + (ring > epi ? ring : epi);
+  const size_t epi = static_cast<size_t>(kConsumerWarps) * 8 * D * 4 + kConsumerWarps * 8 * 8;
+  return 256 + 8 * D * 4 + (ring > epi ? ring : epi);
 }
 
-template <int KB, int VB, int NOUT>
+template <int D, int KB, int VB, int NOUT>
 static int launch_decode3(const DecodeParams& p, cudaStream_t st) {
-  const size_t smem = decode_smem_bytes(p.L.bytes);
-  auto kern = p.btab ? mixed_decode_kernel<KB, VB, NOUT, true> : mixed_decode_kernel<KB, VB, NOUT, false>;
+  const size_t smem = decode_smem_bytes(p.L.bytes, D);
+  auto kern = p.btab ? mixed_decode_kernel<D, KB, VB, NOUT, true> : mixed_decode_kernel<D, KB, VB, NOUT, false>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
       cudaSuccess)
     return AKV_ERR_LAUNCH;
@@ -1120,12 +1247,27 @@ static int launch_decode3(const DecodeParams& p, cudaStream_t st) {
   return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_LAUNCH;
 }
 
-template <int KB, int VB>
+template <int D, int KB, int VB>
 static int launch_decode(const DecodeParams& p, cudaStream_t st) {
   const int n = p.n_warm_blocks > 0 ? p.L.n_outlier : 0;
-  if (n == 0) return launch_decode3<KB, VB, 0>(p, st);
-  if (n == 1) return launch_decode3<KB, VB, 1>(p, st);
-  return launch_decode3<KB, VB, 2>(p, st);
+  if (n == 0) return launch_decode3<D, KB, VB, 0>(p, st);
+  if (n == 1) return launch_decode3<D, KB, VB, 1>(p, st);
+  return launch_decode3<D, KB, VB, 2>(p, st);
+}
+
+template <int D>
+static int launch_decode_bits(const DecodeParams& p, int kb, int vb, cudaStream_t st) {
+  switch (kb * 10 + vb) {
+    case 22: return launch_decode<D, 2, 2>(p, st);
+    case 23: return launch_decode<D, 2, 3>(p, st);
+    case 24: return launch_decode<D, 2, 4>(p, st);
+    case 32: return launch_decode<D, 3, 2>(p, st);
+    case 33: return launch_decode<D, 3, 3>(p, st);
+    case 34: return launch_decode<D, 3, 4>(p, st);
+    case 42: return launch_decode<D, 4, 2>(p, st);
+    case 43: return launch_decode<D, 4, 3>(p, st);
+    default: return launch_decode<D, 4, 4>(p, st);
+  }
 }
 
 }  // namespace akv
@@ -1134,18 +1276,19 @@ using namespace akv;
 
 // Upper bound on the split count of plan_decode for any record size: the warm
 // and hot shares of the largest candidate round to at most hi + 1 splits.
-static int max_splits(int B, int Hq, int Hkv, int n_hot, int n_warm_blocks) {
+static int max_splits(int B, int Hq, int Hkv, int D, int n_hot, int n_warm_blocks) {
   const int g = Hq / Hkv;
   const int units = B * Hkv * ((g + 7) / 8);
   int lo, hi;
-  per_unit_range(units, n_warm_blocks + (n_hot + 31) / 32, lo, hi);
+  per_unit_range(units, n_warm_blocks + (n_hot + 31) / 32, decode_slots(D), lo, hi);
   const int cap = n_warm_blocks + (n_hot + 31) / 32;
   return max(1, min(hi + 2, cap));
 }
 
 extern "C" size_t akv_decode_workspace_bytes(int B, int Hq, int Hkv, int D, int n_hot, int n_warm_blocks) {
-  if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || D != kHeadDim || n_hot < 0 || n_warm_blocks < 0) return 0;
-  return static_cast<size_t>(B) * Hq * max_splits(B, Hq, Hkv, n_hot, n_warm_blocks) * (D + 2) * sizeof(float);
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || !decode_head_dim_ok(D) || n_hot < 0 || n_warm_blocks < 0)
+    return 0;
+  return static_cast<size_t>(B) * Hq * max_splits(B, Hq, Hkv, D, n_hot, n_warm_blocks) * (D + 2) * sizeof(float);
 }
 
 // Shared body of akv_mixed_decode (btab == nullptr: row b's records are
@@ -1160,7 +1303,7 @@ static int decode_impl(const uint16_t* q, int64_t q_sb, int64_t q_sh, const uint
                        void* stream) {
   if (!q || (!out && !partial_out)) return AKV_ERR_NULL;
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || n_hot < 0 || n_warm_blocks < 0) return AKV_ERR_SHAPE;
-  if (D != kHeadDim) return AKV_ERR_UNSUPPORTED;
+  if (!decode_head_dim_ok(D)) return AKV_ERR_UNSUPPORTED;
   if (n_hot > 0 && (!hot_k || !hot_v)) return AKV_ERR_NULL;
   if (n_warm_blocks > 0 && (!warm || !layout)) return AKV_ERR_NULL;
   auto al = [](const void* ptr, int a) { return (reinterpret_cast<uintptr_t>(ptr) % a) == 0; };
@@ -1183,9 +1326,9 @@ static int decode_impl(const uint16_t* q, int64_t q_sb, int64_t q_sh, const uint
       return AKV_ERR_UNSUPPORTED;
   }
   if (!workspace) return AKV_ERR_NULL;
-  const DecodePlan pl = plan_decode(B, Hq, Hkv, n_hot, n_warm_blocks, n_warm_blocks > 0 ? L.bytes : 1);
+  const DecodePlan pl = plan_decode(B, Hq, Hkv, D, n_hot, n_warm_blocks, n_warm_blocks > 0 ? L.bytes : 1);
   const int splits = max(pl.splits, 1);
-  if (splits > max_splits(B, Hq, Hkv, n_hot, n_warm_blocks)) return AKV_ERR_UNSUPPORTED;  // planner invariant
+  if (splits > max_splits(B, Hq, Hkv, D, n_hot, n_warm_blocks)) return AKV_ERR_UNSUPPORTED;  // planner invariant
   const size_t need = static_cast<size_t>(B) * Hq * splits * (D + 2) * sizeof(float);
   if (workspace_bytes < need || !al(workspace, 16)) return AKV_ERR_WORKSPACE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -1234,17 +1377,9 @@ static int decode_impl(const uint16_t* q, int64_t q_sb, int64_t q_sh, const uint
   p.status = status;
   int rc;
   const int kb = n_warm_blocks > 0 ? L.key_bits : 4, vb = n_warm_blocks > 0 ? L.value_bits : 4;
-  switch (kb * 10 + vb) {
-    case 22: rc = launch_decode<2, 2>(p, st); break;
-    case 23: rc = launch_decode<2, 3>(p, st); break;
-    case 24: rc = launch_decode<2, 4>(p, st); break;
-    case 32: rc = launch_decode<3, 2>(p, st); break;
-    case 33: rc = launch_decode<3, 3>(p, st); break;
-    case 34: rc = launch_decode<3, 4>(p, st); break;
-    case 42: rc = launch_decode<4, 2>(p, st); break;
-    case 43: rc = launch_decode<4, 3>(p, st); break;
-    default: rc = launch_decode<4, 4>(p, st); break;
-  }
+  if (D == 64) rc = launch_decode_bits<64>(p, kb, vb, st);
+  else if (D == 256) rc = launch_decode_bits<256>(p, kb, vb, st);
+  else rc = launch_decode_bits<128>(p, kb, vb, st);
   if (rc != AKV_OK) return rc;
   return launch_combine_dependent(ws, D + 2, static_cast<int64_t>(pl.splits) * (D + 2), B * Hq, pl.splits, D, outh,
                                   o_sh, lse, partial_out, st);
@@ -1315,7 +1450,7 @@ extern "C" int akv_mixed_decode_noalloc(const uint16_t* q, int64_t q_sb, int64_t
                                         int B, int Hq, int Hkv, int D, float sm_scale, uint16_t* out, int64_t o_sb,
                                         int64_t o_sh, float* lse, float* partial_out, int* status, void* stream) {
   const size_t need = akv_decode_workspace_bytes(B, Hq, Hkv, D, n_hot, n_warm_blocks);
-  if (need == 0) return D != kHeadDim ? AKV_ERR_UNSUPPORTED : AKV_ERR_SHAPE;
+  if (need == 0) return !decode_head_dim_ok(D) ? AKV_ERR_UNSUPPORTED : AKV_ERR_SHAPE;
   if (need > kNoAllocScratchBytes) return AKV_ERR_WORKSPACE;  // beyond the fixed scratch array
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return AKV_ERR_LAUNCH;

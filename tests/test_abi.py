@@ -72,7 +72,7 @@ def test_host_validation_without_gpu():
     assert lib.akv_quantize(16, 0, 0, 0, None, 0, 0, 1, 1, 1, 100, 3, 1, 32, 0, ctypes.byref(d), None, None) == -1
     assert lib.akv_quantize(8, 0, 0, 0, None, 0, 0, 1, 1, 1, 128, 3, 1, 32, 0, ctypes.byref(d), None, None) == -3
     assert lib.akv_mixed_decode(16, 0, 0, None, None, 0, 0, 0, 0, None, None, 0, 0, None, 0, None,
-                                1, 8, 2, 64, 1.0, 16, 0, 0, None, None, None, 0, None, None) == -4
+                                1, 8, 2, 96, 1.0, 16, 0, 0, None, None, None, 0, None, None) == -4
     assert lib.akv_decode_workspace_bytes(1, 12, 2, 128, 512, 112) > 0
     assert lib.akv_decode_workspace_bytes(1, 12, 5, 128, 512, 112) == 0
     assert lib.akv_select_bottomk(None, 10, 3, 0, 0, None, None, 0, None) == -7

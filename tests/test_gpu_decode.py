@@ -289,3 +289,41 @@ def test_few_units_long_context():
     err = (out[0] - ref).abs().max().item()
     print(f"[decode err] few units, long context: {err:.3e}")
     assert err <= ATOL
+
+
+# ---------------------------------------------------------------------------- head dims 64 and 256
+@pytest.mark.parametrize("D", [64, 256])
+@pytest.mark.parametrize("kb,vb", [(2, 2), (3, 3), (4, 4), (4, 2), (2, 3), (3, 4)])
+def test_head_dims_bit_pairs(D, kb, vb):
+    """The decode kernel built for head dim 64 (half a 32-channel record
+    chunk per K thread column, 8 V channels per thread row) and 256 (two
+    chunks, two 16-channel V groups), warm + hot, against the oracle."""
+    check(60 + D + 3 * kb + vb, 2, 8, 2, 32 * 6 + 9, 45, kb, vb, 0.0, D=D, outlier_ch=(5,))
+
+
+@pytest.mark.parametrize("D", [64, 256])
+@pytest.mark.parametrize("n_out", [1, 3, 8])
+def test_head_dims_outliers(D, n_out):
+    """One outlier channel (the side-tile path) and several, up to the
+    kernel's eight (the extra-MMA path), at head dims 64 and 256, channels at
+    both ends of the row."""
+    f = (n_out + 0.5) / D
+    check(70 + D, 1, 16, 4, 32 * 9 + 17, 33, 4, 2, f, D=D, outlier_ch=(1, D // 2 + 3, D - 1))
+
+
+@pytest.mark.parametrize("D", [64, 256])
+def test_head_dims_hot_only_ragged(D):
+    check(80 + D, 3, 12, 4, 0, 150, 4, 4, 0.0, D=D, hot_len=[150, 1, 77])
+    check(81 + D, 3, 12, 4, 32 * 7, 40, 3, 2, 0.0, D=D, hot_len=[40, 0, 13], warm_blocks=[7, 2, 0])
+
+
+def test_head_dim_64_tinyllama_shape():
+    """The paper's ITL model shape (TinyLlama: 32 query / 4 KV heads, head
+    dim 64) at a 4K context: 3,584 warm tokens at k4v2 with 1 % outliers,
+    512 hot."""
+    check(90, 1, 32, 4, 3584, 512, 4, 2, 0.01, D=64, outlier_ch=(9,))
+
+
+def test_head_dim_256_gqa_groups():
+    """Head dim 256 with 16 query heads per KV head (two head groups per CTA row)."""
+    check(91, 2, 32, 2, 32 * 12, 64, 3, 3, 0.0, D=256, outlier_ch=(200,))

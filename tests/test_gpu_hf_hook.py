@@ -31,13 +31,15 @@ def _excess(out, ref):
     return ((out - ref).abs() - tol).max().item()
 
 
-def _model(layers=2, vocab=1000):
+def _model(layers=2, vocab=1000, head_dim=128):
     from transformers import Qwen2Config, Qwen2ForCausalLM
     import akv.hf_attention as hook
     hook.register()
     torch.manual_seed(0)
-    cfg = Qwen2Config(vocab_size=vocab, hidden_size=512, intermediate_size=1024, num_hidden_layers=layers,
-                      num_attention_heads=4, num_key_value_heads=2, max_position_embeddings=4096,
+    heads = 512 // head_dim if head_dim <= 128 else 4
+    cfg = Qwen2Config(vocab_size=vocab, hidden_size=heads * head_dim, intermediate_size=1024,
+                      num_hidden_layers=layers, num_attention_heads=heads, num_key_value_heads=2,
+                      max_position_embeddings=4096,
                       rms_norm_eps=1e-6, initializer_range=0.08)
     return Qwen2ForCausalLM(cfg).eval().half().to(DEV)
 
@@ -47,9 +49,13 @@ def _step(model, cache, ids):
     return out.logits[:, -1].float()
 
 
-@pytest.mark.parametrize("policy", ["recency", "proxy_promotion", "k4v2_outliers"])
-def test_hook_matches_sdpa_over_view_each_step(policy, monkeypatch):
-    """Every fused decode call against SDPA over that layer's full view."""
+@pytest.mark.parametrize("policy,head_dim", [("recency", 128), ("proxy_promotion", 128), ("k4v2_outliers", 128),
+                                             ("recency", 64), ("k4v2_outliers", 64), ("recency", 256),
+                                             ("k4v2_outliers", 256)])
+def test_hook_matches_sdpa_over_view_each_step(policy, head_dim, monkeypatch):
+    """Every fused decode call against SDPA over that layer's full view, on
+    models with head dim 128 (Llama / Qwen), 64 (TinyLlama-like: 8 query /
+    2 KV heads) and 256 (Gemma-like)."""
     import akv
     import akv.hf_attention as hook
     from transformers.integrations.sdpa_attention import sdpa_attention_forward
@@ -60,7 +66,7 @@ def test_hook_matches_sdpa_over_view_each_step(policy, monkeypatch):
         "k4v2_outliers": dict(warm_key_bits=4, warm_value_bits=2, warm_bits=4, hot_budget=40,
                               outlier_fraction=0.02, enable_promotion=False, enable_promotion_proxy=False),
     }[policy]
-    model = _model()
+    model = _model(head_dim=head_dim)
     model.config._attn_implementation = "akv"
     errs, calls, prefills = [], [0], [0]
     real = hook.akv_attention_forward
