@@ -13,6 +13,7 @@ from .fused_attention import (fused_int4_decode_attention, int4_group_dequant, m
                               mixed_tier_decode_attention, prefill_attention)
 from .packed_layout import WarmArena, measure_packed_bytes
 from .drop_in import AKVCache, AKVLayer, recommend_preset
+from .graphs import DecodeGraph
 from .tiering import fused_importance_update
 from .triton_ops import HAS_TRITON, fused_mixed_precision_attention, fused_quantized_attention
 from .triton_kernels import fused_decode_attention, fused_quantize_evict
@@ -20,7 +21,7 @@ from .triton_kernels import fused_decode_attention, fused_quantize_evict
 __version__ = "0.1.0"
 
 __all__ = [
-    "AKVCache", "AKVLayer", "recommend_preset",
+    "AKVCache", "AKVLayer", "recommend_preset", "DecodeGraph",
     "AffineQuantConfig", "AffineQuantizer", "WarmArena", "measure_packed_bytes",
     "mixed_tier_decode_attention", "mixed_precision_decode_attention", "fused_int4_decode_attention",
     "int4_group_dequant", "prefill_attention",

@@ -880,29 +880,41 @@ def run_ours(args):
     e2e_status = torch.zeros(1, dtype=torch.int32, device=dev)
 
     def e2e_step():
-        s_in.wait_stream(st)  # uploads may overwrite q_in only after the previous step read it
+        cur = torch.cuda.current_stream()
+        s_in.wait_stream(cur)  # uploads may overwrite q_in only after the previous step read it
         with torch.cuda.stream(s_in):
             for l in range(L):
                 q_in[l].copy_(q_host[l], non_blocking=True)
                 ev_in[l].record(s_in)
         for l in range(L):
-            st.wait_event(ev_in[l])
+            cur.wait_event(ev_in[l])
             akv.mixed_tier_decode_attention(q_in[l], hot_k[l], hot_v[l], arenas[l], out=o_dev[l],
                                             status=e2e_status)
-            ev_out[l].record(st)
+            ev_out[l].record(cur)
             s_out.wait_event(ev_out[l])
             with torch.cuda.stream(s_out):
                 o_host[l].copy_(o_dev[l], non_blocking=True)
-        st.wait_stream(s_out)
+        cur.wait_stream(s_out)
 
+    # The step (uploads, 32 layers, downloads, with their stream fork / join)
+    # is captured once as a DecodeGraph, the public API a serving loop uses to
+    # replay a fixed step; where capture is refused the step runs eagerly.
+    e2e_mode = "graph"
+    try:
+        e2e_graph = akv.DecodeGraph(e2e_step, warmup=max(args.warmup, 3))
+        run_e2e = e2e_graph.replay
+    except Exception as exc:  # noqa: BLE001 - report and fall back to eager issue
+        e2e_mode = f"eager ({type(exc).__name__})"
+        torch.cuda.synchronize()
+        run_e2e = e2e_step
     for _ in range(max(args.warmup, 3)):
-        e2e_step()
+        run_e2e()
     torch.cuda.synchronize()
     barrier()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record(st)
     for _ in range(args.steps):
-        e2e_step()
+        run_e2e()
     t1.record(st)
     torch.cuda.synchronize()
     barrier()
@@ -951,7 +963,7 @@ def run_ours(args):
                          "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": traffic,
                          "kernel": "mixed_decode_kernel (+ lse_combine_kernel in the same per-layer time)",
                          "algorithmic_bytes_per_launch": alg_bytes_layer, "peak_source": pk["source"]},
-            "e2e": {"value": round(e2e_ms * 1e3, 2), "unit": "µs/step",
+            "e2e": {"value": round(e2e_ms * 1e3, 2), "unit": "µs/step", "mode": e2e_mode,
                     "h2d_bytes_per_step": L * B * hq * D * 2, "d2h_bytes_per_step": L * B * hq * D * 2},
             "gpu_launches": 2 * L * args.steps,
             "clocks": clocks,
