@@ -755,10 +755,46 @@ def hf_parity_leg(torch, akv, model, ids, toks, make_cache, sdpa_backends) -> di
 
 
 # ---------------------------------------------------------------------------- our arm
+def prefill_case(args) -> None:
+    """A small prefill case for profiler captures (one GPU): batch 1, 32/8
+    heads, an `--prefill-case N`-token prompt (N - N/8 warm k4v2 tokens at
+    random sorted positions, N/8 hot), three launches; prints each launch's
+    time and TFLOP/s."""
+    import torch
+    import akv
+    dev = torch.device("cuda", 0)
+    B, Hq, Hkv, D, N = 1, 32, 8, 128, args.prefill_case
+    n_hot = max(128, N // 8)
+    n_warm = (N - n_hot) // 32 * 32
+    N = n_warm + n_hot
+    g = torch.Generator(device=dev).manual_seed(0)
+    perm = torch.randperm(N, generator=torch.Generator().manual_seed(0))
+    wpos = perm[:n_warm].sort().values.to(torch.int32).to(dev)
+    hpos = perm[n_warm:].sort().values.to(torch.int32).to(dev)
+    arena = akv.WarmArena(B, Hkv, D, 4, 2, 0.01, max_blocks=n_warm // 32, device=dev)
+    arena.append(make_kv(torch, g, (B, Hkv, n_warm, D), dev), make_kv(torch, g, (B, Hkv, n_warm, D), dev), group=32)
+    hk, hv = make_kv(torch, g, (B, Hkv, n_hot, D), dev), make_kv(torch, g, (B, Hkv, n_hot, D), dev)
+    q = torch.randn(B, Hq, N, D, generator=g, device=dev).half()
+    qpos = torch.arange(N, dtype=torch.int32, device=dev)
+    st = torch.zeros(1, dtype=torch.int32, device=dev)
+    flops = 4.0 * D * N * (N + 1) / 2 * B * Hq
+    for _ in range(3):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        akv.prefill_attention(q, qpos, hk, hv, hpos, arena, wpos, status=st)
+        e1.record()
+        e1.synchronize()
+        ms = e0.elapsed_time(e1)
+        print(json.dumps({"prefill_case": N, "ms": round(ms, 3), "tflops": round(flops / ms / 1e9, 1),
+                          "status": int(st.item())}))
+
+
 def run_ours(args):
     import torch
     import akv
 
+    if args.prefill_case:
+        return prefill_case(args)
     world, rank, local = dist_setup()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -1075,6 +1111,8 @@ def main():
     ap.add_argument("--no-shapes", action="store_true", help="skip the per-layer decode timings of configs 1, 2, 5")
     ap.add_argument("--hf-tokens", type=int, default=256,
                     help="config-2 HF greedy decoding length (0: skip the end-to-end model run)")
+    ap.add_argument("--prefill-case", type=int, default=0,
+                    help="only run a small prefill case of this prompt length (profiler captures)")
     ap.add_argument("--batch", type=int, default=CFG["B"],
                     help="batch rows (default: config 3's 16; smaller only for profiler captures)")
     args = ap.parse_args()
