@@ -64,6 +64,10 @@ SIGNATURES = {
                                  POINTER(QDest), c_void_p, c_int, c_void_p, c_size_t, c_void_p, c_void_p]),
     "akv_dequantize": (c_int, [POINTER(QDest), c_void_p, c_int64, c_int64, c_int, c_int, c_int, c_int, c_int,
                                c_int, c_int, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p]),
+    "akv_warm_append_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int, c_int]),
+    "akv_warm_append": (c_int, [c_void_p, c_int64, c_int64, POINTER(WarmLayout), c_int, c_void_p, c_int64, c_int64,
+                                c_int64, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64, c_int,
+                                c_int, c_int, c_int, c_void_p, c_size_t, c_void_p, c_void_p]),
     "akv_int4_group_dequant": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int64,
                                        c_int, c_int, c_int, c_int, c_void_p, c_int64, c_int64, c_void_p]),
     "akv_group_dequant": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int64,

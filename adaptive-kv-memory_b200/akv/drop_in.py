@@ -74,6 +74,48 @@ def _to_device(t: torch.Tensor, device: torch.device) -> torch.Tensor:
 
 
 # presets of the reference (drop_in.py:89-126)
+class _GapVec:
+    """A host vector kept as the live slice [lo, hi) of a larger numpy
+    buffer: removing the element at logical index i moves the shorter side
+    (O(min(i, n - i))), appending writes one slot (amortised O(1)).  The hot
+    tier's logical-order vectors (positions, importance, buffer rows) live
+    here, so a decode step that demotes a token near the front and appends
+    one at the end rewrites neither vector."""
+
+    __slots__ = ("buf", "lo", "hi")
+
+    def __init__(self, arr, dtype):
+        a = np.asarray(arr, dtype=dtype).reshape(-1)
+        n = a.shape[0]
+        self.buf = np.empty(max(2 * n, 64), dtype=dtype)
+        self.buf[:n] = a
+        self.lo, self.hi = 0, n
+
+    def __len__(self) -> int:
+        return self.hi - self.lo
+
+    def view(self) -> np.ndarray:
+        return self.buf[self.lo:self.hi]
+
+    def remove(self, i: int) -> None:
+        lo, hi, b = self.lo, self.hi, self.buf
+        if i < (hi - lo) // 2:
+            b[lo + 1:lo + 1 + i] = b[lo:lo + i].copy()
+            self.lo = lo + 1
+        else:
+            b[lo + i:hi - 1] = b[lo + i + 1:hi].copy()
+            self.hi = hi - 1
+
+    def append(self, x) -> None:
+        if self.hi == self.buf.shape[0]:
+            n = self.hi - self.lo
+            nb = np.empty(max(2 * (n + 1), 64), dtype=self.buf.dtype)
+            nb[:n] = self.buf[self.lo:self.hi]
+            self.buf, self.lo, self.hi = nb, 0, n
+        self.buf[self.hi] = x
+        self.hi += 1
+
+
 _PRESETS = {
     "quality": {"warm_bits": 4, "hot_budget": 256, "description": "Near-lossless 4-bit. +1-2% PPL."},
     "balanced": {"warm_bits": 3, "hot_budget": 128, "description": "Block-affine 3-bit. +3.3% PPL, 5x compression."},
@@ -166,6 +208,40 @@ class AKVLayer(_LayerBase):
         self._decay = 0.3
         self._n_anchors = 16
         self._step = 0
+
+    # ------------------------------------------------------------------ hot-tier order vectors
+    # Logical-order (arrival order, promoted tokens first) host vectors of the
+    # hot tier, kept in _GapVec buffers.  Reads return copies (numpy / CPU
+    # torch, as before); assignments replace the vector.
+    @property
+    def _phys(self) -> Optional[np.ndarray]:
+        """Buffer row of each logical hot token (None: identity)."""
+        g = self.__dict__.get("_phys_g")
+        return None if g is None else g.view().copy()
+
+    @_phys.setter
+    def _phys(self, a) -> None:
+        self.__dict__["_phys_g"] = None if a is None else _GapVec(a, np.int64)
+
+    @property
+    def _hot_positions(self) -> Optional[torch.Tensor]:
+        g = self.__dict__.get("_hpos_g")
+        return None if g is None else torch.from_numpy(g.view().copy())
+
+    @_hot_positions.setter
+    def _hot_positions(self, t) -> None:
+        self.__dict__["_hpos_g"] = None if t is None else _GapVec(
+            t.numpy() if isinstance(t, torch.Tensor) else t, np.int64)
+
+    @property
+    def _importance(self) -> Optional[torch.Tensor]:
+        g = self.__dict__.get("_imp_g")
+        return None if g is None else torch.from_numpy(g.view().copy())
+
+    @_importance.setter
+    def _importance(self, t) -> None:
+        self.__dict__["_imp_g"] = None if t is None else _GapVec(
+            t.numpy() if isinstance(t, torch.Tensor) else t, np.float32)
 
     # ------------------------------------------------------------------ hot ring
     def _hot_view(self, buf: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
@@ -599,6 +675,10 @@ class AKVLayer(_LayerBase):
     def update(self, key_states: torch.Tensor, value_states: torch.Tensor,
                cache_kwargs: Optional[dict] = None) -> Tuple[torch.Tensor, torch.Tensor]:
         """Append, migrate, return the chronological full view (drop_in.py:591-787)."""
+        if self._steady_decode_step(key_states, value_states):
+            if self.fused_decode and self._warm is not None:
+                return self._publish(*self._placeholder())
+            return self._publish(*self.full_view())
         N = key_states.shape[2]
         new_positions = np.arange(self._total_len, self._total_len + N, dtype=np.int64)
         first = self._hk is None
@@ -676,6 +756,56 @@ class AKVLayer(_LayerBase):
         if self.fused_decode and self._warm is not None:
             return self._publish(*self._placeholder())
         return self._publish(*self.full_view())
+
+    def _steady_decode_step(self, key_states: torch.Tensor, value_states: torch.Tensor) -> bool:
+        """The steady-state decode step (one new token, hot tier full, recency
+        importance, no promotion) in O(1) host work; False when it does not
+        apply (update() then runs the general path).
+
+        Same result as the general path: the recency update imp * 0.3 (fp32)
+        with 1.0 for the new token (drop_in.py:376-390), the demoted token is
+        the reference's torch.topk(1, largest=False) over the scores with the
+        first 4 and last min(16, budget // 4) positions protected
+        (drop_in.py:392-413) — for 64 or more scores torch's CPU top-1 is the
+        first index of the minimum, which np.argmin returns — then that
+        token's row is quantised into a new warm record and the new token is
+        written into the row it leaves."""
+        if (key_states.shape[2] != 1 or self.protect or self.enable_promotion or self.enable_promotion_proxy
+                or self.adaptive_hot_frac > 0.0 or self._hk is None or not key_states.is_cuda):
+            return False
+        d = self.__dict__
+        ig, hg = d.get("_imp_g"), d.get("_hpos_g")
+        hn = self._hn
+        pr = min(16, self.hot_budget // 4)
+        hot_len = hn + 1
+        if (hn != self.hot_budget or hot_len < 64 or ig is None or hg is None or len(ig) != hn or len(hg) != hn
+                or hot_len - pr <= 4):
+            return False
+        pg = d.get("_phys_g")
+        if pg is None:
+            pg = d["_phys_g"] = _GapVec(np.arange(hn, dtype=np.int64), np.int64)
+        # recency importance and the new token's position
+        imp = ig.view()
+        imp *= np.float32(self._decay)
+        ig.append(1.0)
+        hg.append(self._total_len)
+        self._total_len += 1
+        self._step += 1
+        # the demoted token: first minimum of the unprotected scores
+        v0 = 4 + int(np.argmin(ig.view()[4:hot_len - pr]))
+        r = int(pg.view()[v0])
+        pos = np.array([hg.view()[v0]], dtype=np.int64)
+        self._demote(np.array([r], dtype=np.int64), pos)
+        self._wpos_append(pos)
+        self._warm_len += 1
+        # the new token takes the demoted token's buffer row
+        self._hk[:, :, r:r + 1].copy_(key_states)
+        self._hv[:, :, r:r + 1].copy_(value_states)
+        ig.remove(v0)
+        hg.remove(v0)
+        pg.remove(v0)
+        pg.append(r)
+        return True
 
     def full_view(self) -> Tuple[torch.Tensor, torch.Tensor]:
         """The chronologically sorted [warm; hot] FP16 K/V (drop_in.py:753-787)."""

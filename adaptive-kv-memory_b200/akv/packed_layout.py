@@ -154,6 +154,24 @@ class WarmArena:
         ti = None if tok_idx is None else tok_idx.contiguous()
         tsb = 0 if ti is None or ti.dim() == 1 else ti.stride(0)
         sp = None if status is None else status.data_ptr()
+        if score_sums is None and k.shape == v.shape:  # both fields in one call (akv_warm_append)
+            kx = k if k.stride(-1) == 1 else k.contiguous()
+            vx = v if v.stride(-1) == 1 else v.contiguous()
+            g = min(group, N)
+            lib = _C.load()
+            needs = self.__dict__.setdefault("_append_ws", {})
+            need = needs.get((N, g))
+            if need is None:
+                need = needs[(N, g)] = lib.akv_warm_append_workspace_bytes(B, H, N, D, g, self.n_out)
+            ws = torch.empty(need + 256, dtype=torch.uint8, device=kx.device) if need else None
+            wp = None if ws is None else (ws.data_ptr() + 255) // 256 * 256
+            _C.check(lib.akv_warm_append(self.buf.data_ptr(), self.buf.stride(0), self.buf.stride(1),
+                                         ctypes.byref(self.layout), blk0, kx.data_ptr(), kx.stride(0), kx.stride(1),
+                                         kx.stride(2), vx.data_ptr(), vx.stride(0), vx.stride(1), vx.stride(2),
+                                         None if ti is None else ti.data_ptr(), tsb, kx.shape[2], B, H, N, g, wp,
+                                         need, sp, _C.stream_of(kx)), "akv_warm_append")
+            self.n_blocks += nblk
+            return blk0
         for i, (x, is_key, bits) in enumerate(((k, True, self.key_bits), (v, False, self.value_bits))):
             if x.stride(-1) != 1:
                 x = x.contiguous()

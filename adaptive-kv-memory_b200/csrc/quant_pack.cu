@@ -1320,3 +1320,62 @@ extern "C" int akv_outlier_norm_sums(const uint16_t* src, int64_t src_sb, int64_
   reduce<<<dim3(pl.n_groups, B), kQuantThreads, pl.reduce_smem, st>>>(p);
   return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_LAUNCH;
 }
+
+// ---------------------------------------------------------------------------
+// One demotion event into new warm block records: the K and V destinations
+// (the record fields akv_warm_layout describes) are built here, and the two
+// quantiser launches issued back to back, so a caller appending to an arena
+// makes one call per event.
+// ---------------------------------------------------------------------------
+static akv_qdest record_qdest(uint8_t* base, int64_t sb, int64_t sh, const akv_warm_layout& L, bool is_key) {
+  akv_qdest d{};
+  const int64_t sblk = L.bytes;
+  const int n = L.n_outlier;
+  auto view = [&](int off, int64_t sslot) { return akv_view{base + off, sb, sh, sblk, sslot}; };
+  if (is_key) {
+    d.pair_order = 1;  // records keep K scale / zero in the decode pair order
+    d.codes = view(L.kc, L.head_dim * L.key_bits / 8);
+    d.scale = view(L.ks, 0);
+    d.zero = view(L.kz, 0);
+    if (n) {
+      d.out_data = view(L.ko, 2 * n);
+      d.out_idx = view(L.ki, 0);
+    }
+  } else {
+    d.codes = view(L.vc, L.head_dim * L.value_bits / 8);
+    d.scale = view(L.vs, 2);
+    d.zero = view(L.vz, 2);
+    if (n) {
+      d.out_data = view(L.vo, 2 * n);
+      d.out_idx = view(L.vi, 0);
+      d.out_vdq = view(L.vd, 2 * n);
+    }
+  }
+  d.mask = view(L.mask, 0);
+  d.flags = view(L.flags + (is_key ? 0 : 1), 0);
+  return d;
+}
+
+extern "C" size_t akv_warm_append_workspace_bytes(int B, int H, int N, int D, int group, int n_outlier) {
+  const size_t k = akv_quantize_workspace_bytes(B, H, N, D, group, n_outlier, 1);
+  const size_t v = akv_quantize_workspace_bytes(B, H, N, D, group, n_outlier, 0);
+  return k > v ? k : v;
+}
+
+extern "C" int akv_warm_append(uint8_t* arena, int64_t a_sb, int64_t a_sh, const akv_warm_layout* layout, int blk0,
+                               const uint16_t* k, int64_t k_sb, int64_t k_sh, int64_t k_sn, const uint16_t* v,
+                               int64_t v_sb, int64_t v_sh, int64_t v_sn, const int64_t* tok_idx, int64_t tok_sb,
+                               int64_t n_src, int B, int H, int N, int group, void* workspace,
+                               size_t workspace_bytes, int* status, void* stream) {
+  if (!arena || !layout || !k || !v) return AKV_ERR_NULL;
+  if (blk0 < 0) return AKV_ERR_SHAPE;
+  const akv_warm_layout L = *layout;
+  uint8_t* base = arena + static_cast<int64_t>(blk0) * L.bytes;
+  const akv_qdest dk = record_qdest(base, a_sb, a_sh, L, true);
+  const akv_qdest dv = record_qdest(base, a_sb, a_sh, L, false);
+  int rc = akv_quantize_ext(k, k_sb, k_sh, k_sn, tok_idx, tok_sb, n_src, B, H, N, L.head_dim, L.key_bits, 1, group,
+                            L.n_outlier, &dk, nullptr, 0, workspace, workspace_bytes, status, stream);
+  if (rc != AKV_OK) return rc;
+  return akv_quantize_ext(v, v_sb, v_sh, v_sn, tok_idx, tok_sb, n_src, B, H, N, L.head_dim, L.value_bits, 0, group,
+                          L.n_outlier, &dv, nullptr, 0, workspace, workspace_bytes, status, stream);
+}

@@ -187,6 +187,21 @@ int akv_quantize_ext(const uint16_t* src, int64_t src_sb, int64_t src_sh, int64_
                      const akv_qdest* dst, const float* score_sum, int score_heads,
                      void* workspace, size_t workspace_bytes, int* status, void* stream);
 
+/* One demotion event into new warm block records of an arena (the K and V
+ * fields akv_warm_layout describes; the record of (b, h, blk) starts at
+ * arena + b*a_sb + h*a_sh + blk*layout->bytes; blocks blk0 ..
+ * blk0 + ceil(N/32) - 1 are written): akv_quantize_ext for the keys, then
+ * the values, of the same N rows (same tok_idx, n_src and group), in one
+ * call.  Replaces the reference's per-event quantize_keys / quantize_values
+ * pair of AKVLayer._demote (akv/drop_in.py:684-701).  Workspace: at least
+ * akv_warm_append_workspace_bytes(...) (NULL when that is 0). */
+size_t akv_warm_append_workspace_bytes(int B, int H, int N, int D, int group, int n_outlier);
+int akv_warm_append(uint8_t* arena, int64_t a_sb, int64_t a_sh, const akv_warm_layout* layout, int blk0,
+                    const uint16_t* k, int64_t k_sb, int64_t k_sh, int64_t k_sn,
+                    const uint16_t* v, int64_t v_sb, int64_t v_sh, int64_t v_sn,
+                    const int64_t* tok_idx, int64_t tok_sb, int64_t n_src, int B, int H, int N, int group,
+                    void* workspace, size_t workspace_bytes, int* status, void* stream);
+
 /* ------------------------------------------------------------------------
  * A4: unpack + dequantise to fp16.
  * Replaces AffineQuantizer.dequantize_keys/values (akv/affine_quantizer.py:112-124,
