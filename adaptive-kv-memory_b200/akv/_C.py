@@ -31,6 +31,7 @@ class QDest(ctypes.Structure):
         [("pair_order", c_int32)]
 
 
+
 class WarmLayout(ctypes.Structure):
     """akv_warm_layout: byte offsets inside one 32-token warm block record."""
     _fields_ = [(n, c_int32) for n in ("head_dim", "key_bits", "value_bits", "n_outlier", "kc", "vc", "ks",
@@ -39,6 +40,19 @@ class WarmLayout(ctypes.Structure):
 
     def as_dict(self) -> dict:
         return {n: getattr(self, n) for n, _ in self._fields_}
+
+class LayerStep(ctypes.Structure):
+    """akv_layer_step (include/akv_b200.h): one AKVLayer's steady decode-step state."""
+    _fields_ = [("hot_k", c_void_p), ("hot_v", c_void_p), ("h_sb", c_int64), ("h_sh", c_int64), ("h_sn", c_int64),
+                ("hot_rows", c_int64), ("arena", c_void_p), ("a_sb", c_int64), ("a_sh", c_int64),
+                ("layout", WarmLayout), ("B", c_int32), ("H", c_int32), ("n_blocks", c_int32),
+                ("max_blocks", c_int32), ("phys", c_void_p), ("hpos", c_void_p), ("imp", c_void_p),
+                ("lo", c_int64), ("hi", c_int64), ("cap", c_int64), ("wslots", c_void_p), ("wpos", c_void_p),
+                ("slot_pos", c_void_p), ("n_wslots", c_int64), ("cap_wslots", c_int64), ("n_wpos", c_int64),
+                ("cap_wpos", c_int64), ("cap_slot_pos", c_int64), ("protect_first", c_int32),
+                ("protect_recent", c_int32), ("decay", c_float), ("total_len", c_int64), ("step", c_int64),
+                ("warm_len", c_int64), ("warm_bytes_packed", c_int64), ("bytes_per_event", c_int64),
+                ("status", c_void_p)]
 
 
 # name -> (restype, argtypes); must list every function declared in akv_b200.h
@@ -68,6 +82,8 @@ SIGNATURES = {
     "akv_warm_append": (c_int, [c_void_p, c_int64, c_int64, POINTER(WarmLayout), c_int, c_void_p, c_int64, c_int64,
                                 c_int64, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64, c_int,
                                 c_int, c_int, c_int, c_void_p, c_size_t, c_void_p, c_void_p]),
+    "akv_layer_decode_step": (c_int, [POINTER(LayerStep), c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64,
+                                      c_void_p]),
     "akv_int4_group_dequant": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int64,
                                        c_int, c_int, c_int, c_int, c_void_p, c_int64, c_int64, c_void_p]),
     "akv_group_dequant": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int64,

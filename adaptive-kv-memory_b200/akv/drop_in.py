@@ -31,6 +31,7 @@ reference.
 """
 from __future__ import annotations
 
+import ctypes
 import logging
 from typing import Any, Optional, Tuple
 
@@ -784,6 +785,9 @@ class AKVLayer(_LayerBase):
         pg = d.get("_phys_g")
         if pg is None:
             pg = d["_phys_g"] = _GapVec(np.arange(hn, dtype=np.int64), np.int64)
+        if (type(self._warm) is WarmArena and self._no_fp16_copy and key_states.dtype == torch.float16
+                and self._native_decode_step(key_states, value_states, ig, hg, pg, pr)):
+            return True
         # recency importance and the new token's position
         imp = ig.view()
         imp *= np.float32(self._decay)
@@ -805,6 +809,73 @@ class AKVLayer(_LayerBase):
         hg.remove(v0)
         pg.remove(v0)
         pg.append(r)
+        return True
+
+    def _native_decode_step(self, key_states, value_states, ig: "_GapVec", hg: "_GapVec", pg: "_GapVec",
+                            pr: int) -> bool:
+        """_steady_decode_step in one library call (akv_layer_decode_step): the
+        host vectors are handed over by pointer, the launches issued there.
+        The three hot order vectors share one buffer capacity and [lo, hi)."""
+        arena = self._warm
+        hn = self._hn
+        # one capacity and window for the three order vectors, room for one more entry
+        if not (ig.lo == hg.lo == pg.lo and ig.hi == hg.hi == pg.hi and ig.hi < ig.buf.shape[0]
+                and ig.buf.shape[0] == hg.buf.shape[0] == pg.buf.shape[0]):
+            cap = max(2 * (hn + 1), 64)
+            for g in (ig, hg, pg):
+                nb = np.empty(cap, dtype=g.buf.dtype)
+                nb[:hn] = g.view()
+                g.buf, g.lo, g.hi = nb, 0, hn
+        if arena.n_blocks + 1 > arena.max_blocks:
+            arena.grow(arena.n_blocks + 1)
+        if self._wslots_n + 1 > self._wslots_buf.shape[0]:
+            nb = np.empty(max(2 * (self._wslots_n + 1), 64), dtype=np.int64)
+            nb[:self._wslots_n] = self._wslots_buf[:self._wslots_n]
+            self._wslots_buf = nb
+        if self._wpos_n + 1 > self._wpos_buf.shape[0]:
+            nb = np.empty(max(2 * (self._wpos_n + 1), 64), dtype=np.int64)
+            nb[:self._wpos_n] = self._wpos_buf[:self._wpos_n]
+            self._wpos_buf = nb
+        if self._slot_pos_np is None or self._slot_pos_np.shape[0] < arena.max_blocks * BLOCK:
+            self._record_slot_pos(0, np.zeros(0, dtype=np.int64))
+        hk, hv = self._hk, self._hv
+        if hk.stride() != hv.stride() or hk.stride(-1) != 1 or key_states.stride(-1) != 1 \
+                or value_states.stride(-1) != 1:
+            return False
+        c = self.__dict__.get("_step_ctx")
+        if c is None:
+            c = self.__dict__["_step_ctx"] = _C.LayerStep()
+            kb, vb, D, H, B = self.warm_key_bits, self.warm_value_bits, arena.D, arena.H, arena.B
+            c.layout = arena.layout
+            c.B, c.H = B, H
+            c.protect_first, c.protect_recent = 4, pr
+            c.decay = self._decay
+            c.bytes_per_event = B * (H * packed_width(D, kb) + 4 * H * D + H * packed_width(D, vb) + 4 * H)
+        c.hot_k, c.hot_v = hk.data_ptr(), hv.data_ptr()
+        c.h_sb, c.h_sh, c.h_sn = hk.stride(0), hk.stride(1), hk.stride(2)
+        c.hot_rows = hk.shape[2]
+        buf = arena.buf
+        c.arena, c.a_sb, c.a_sh = buf.data_ptr(), buf.stride(0), buf.stride(1)
+        c.n_blocks, c.max_blocks = arena.n_blocks, arena.max_blocks
+        c.phys, c.hpos, c.imp = pg.buf.ctypes.data, hg.buf.ctypes.data, ig.buf.ctypes.data
+        c.lo, c.hi, c.cap = ig.lo, ig.hi, ig.buf.shape[0]
+        c.wslots, c.n_wslots, c.cap_wslots = self._wslots_buf.ctypes.data, self._wslots_n, self._wslots_buf.shape[0]
+        c.wpos, c.n_wpos, c.cap_wpos = self._wpos_buf.ctypes.data, self._wpos_n, self._wpos_buf.shape[0]
+        c.slot_pos, c.cap_slot_pos = self._slot_pos_np.ctypes.data, self._slot_pos_np.shape[0]
+        c.total_len, c.step, c.warm_len = self._total_len, self._step, self._warm_len
+        c.warm_bytes_packed = self._warm_bytes_packed
+        ks, vs = key_states.stride(), value_states.stride()
+        _C.check(_C.load().akv_layer_decode_step(ctypes.byref(c), key_states.data_ptr(), ks[0], ks[1],
+                                                 value_states.data_ptr(), vs[0], vs[1], _C.stream_of(hk)),
+                 "akv_layer_decode_step")
+        for g in (ig, hg, pg):
+            g.lo, g.hi = c.lo, c.hi
+        arena.n_blocks = c.n_blocks
+        self._wslots_n, self._wpos_n = c.n_wslots, c.n_wpos
+        self._wslots_dev = None
+        self._slot_pos_dev = None
+        self._total_len, self._step, self._warm_len = c.total_len, c.step, c.warm_len
+        self._warm_bytes_packed = c.warm_bytes_packed
         return True
 
     def full_view(self) -> Tuple[torch.Tensor, torch.Tensor]:

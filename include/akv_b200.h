@@ -483,6 +483,50 @@ int akv_scatter_rows(const void* src, int64_t s_sb, int64_t s_sh, int64_t s_sn, 
 int akv_selftest_wait(int arrive, int64_t limit_ns, int* status, int* result, void* stream);
 
 /* ------------------------------------------------------------------------
+ * AKVLayer's steady decode step in one call.  Replaces, for a layer whose hot
+ * tier is full and whose importance is the recency form with no promotion,
+ * AKVLayer.update's per-step work (akv/drop_in.py:591-787: _update_importance
+ * :376-390, _select_demote_indices :392-413, the demotion :684-701 and the
+ * append of the new token):
+ *   imp[lo..hi) *= decay (fp32), the new token gets importance 1.0 and
+ *   position total_len; the demoted token is the first minimum of the scores
+ *   at logical indices [protect_first, n + 1 - protect_recent) (torch's CPU
+ *   top-1 for 64 or more scores); its hot row phys[lo + v0] is quantised into
+ *   warm block n_blocks (akv_warm_append, one token), the new token's K / V
+ *   rows (B, H, 1, D; element strides nk_sb / nk_sh) are copied into that hot
+ *   row after it, the warm slot / position vectors get one entry, and entry
+ *   v0 leaves the hot order vectors (the new token's row appended last).
+ * Host vectors are caller-owned arrays; the caller guarantees the
+ * capacities below (checked: AKV_ERR_SHAPE, nothing done).  Hot tier and
+ * arena are device memory; element strides for the hot tier, bytes for the
+ * arena. */
+typedef struct {
+  uint16_t* hot_k;
+  uint16_t* hot_v;
+  int64_t h_sb, h_sh, h_sn; /* elements */
+  int64_t hot_rows;         /* rows allocated per (b, h) */
+  uint8_t* arena;
+  int64_t a_sb, a_sh;       /* bytes */
+  akv_warm_layout layout;
+  int32_t B, H, n_blocks, max_blocks;
+  int64_t* phys;            /* hot order vectors: logical entry i at [lo + i], i < hi - lo */
+  int64_t* hpos;
+  float* imp;
+  int64_t lo, hi, cap;      /* shared by the three; cap >= hi + 1 */
+  int64_t* wslots;          /* warm slot of each warm token, in warm order */
+  int64_t* wpos;            /* position of each warm token, in warm order */
+  int32_t* slot_pos;        /* position per arena slot */
+  int64_t n_wslots, cap_wslots, n_wpos, cap_wpos, cap_slot_pos;
+  int32_t protect_first, protect_recent;
+  float decay;
+  int64_t total_len, step, warm_len, warm_bytes_packed, bytes_per_event;
+  int* status;              /* device, nullable */
+} akv_layer_step;
+
+int akv_layer_decode_step(akv_layer_step* ctx, const uint16_t* new_k, int64_t nk_sb, int64_t nk_sh,
+                          const uint16_t* new_v, int64_t nv_sb, int64_t nv_sh, void* stream);
+
+/* ------------------------------------------------------------------------
  * A8: cold tier copies.  Replaces AsyncMigrator._do_warm_to_cold /
  * _do_cold_to_warm (akv/async_migration.py:303-349): warm block records move
  * byte-for-byte between HBM and a pinned host arena with cudaMemcpy2DAsync

@@ -82,3 +82,23 @@ def test_host_validation_without_gpu():
     assert lib.akv_dequantize(ctypes.byref(d), 16, 0, 0, 1, 1, 1, 128, 3, 1, 0, 16, 0, 0, 0, None, None) == -7
     assert lib.akv_gather_rows(16, 0, 0, 16, 0, 16, 1, 1, 1, 16, 16, 0, 0, 16, None, None) == -1
     assert lib.akv_abi_version() == 3
+
+
+def test_layer_step_struct_matches_header(tmp_path):
+    """The ctypes mirror of akv_layer_step has the header's size and field offsets."""
+    import shutil
+    import subprocess
+    from akv import _C
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    fields = [f[0] for f in _C.LayerStep._fields_]
+    src = tmp_path / "sz.c"
+    src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "akv_b200.h"\nint main(void){\n'
+                   + 'printf("%zu\\n", sizeof(akv_layer_step));\n'
+                   + "".join(f'printf("%zu\\n", offsetof(akv_layer_step, {f}));\n' for f in fields) + "return 0;}\n")
+    exe = tmp_path / "sz"
+    subprocess.run([cc, "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
+    out = [int(x) for x in subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split()]
+    assert out[0] == ctypes.sizeof(_C.LayerStep)
+    assert out[1:] == [getattr(_C.LayerStep, f).offset for f in fields]
