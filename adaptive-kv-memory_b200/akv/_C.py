@@ -13,6 +13,7 @@ from ctypes import POINTER, c_float, c_int, c_int32, c_int64, c_size_t, c_void_p
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "libakv_sm100.so")
 
 AKV_OK = 0
+AKV_ERR_WORKSPACE = -8
 BLOCK_TOKENS = 32
 ERRORS = {
     -1: "AKV_ERR_SHAPE", -2: "AKV_ERR_BITS", -3: "AKV_ERR_ALIGN", -4: "AKV_ERR_UNSUPPORTED",
@@ -40,6 +41,17 @@ class WarmLayout(ctypes.Structure):
 
     def as_dict(self) -> dict:
         return {n: getattr(self, n) for n, _ in self._fields_}
+
+class DecodeArgs(ctypes.Structure):
+    """akv_decode_args (include/akv_b200.h)."""
+    _fields_ = [("q", c_void_p), ("q_sb", c_int64), ("q_sh", c_int64), ("hot_k", c_void_p), ("hot_v", c_void_p),
+                ("h_sb", c_int64), ("h_sh", c_int64), ("h_sn", c_int64), ("n_hot", c_int32), ("hot_len", c_void_p),
+                ("warm", c_void_p), ("w_sb", c_int64), ("w_sh", c_int64), ("layout", c_void_p),
+                ("n_warm_blocks", c_int32), ("warm_len", c_void_p), ("B", c_int32), ("Hq", c_int32),
+                ("Hkv", c_int32), ("D", c_int32), ("sm_scale", c_float), ("out", c_void_p), ("o_sb", c_int64),
+                ("o_sh", c_int64), ("lse", c_void_p), ("partial_out", c_void_p), ("workspace", c_void_p),
+                ("workspace_bytes", c_size_t), ("workspace_need", c_void_p), ("status", c_void_p)]
+
 
 class LayerStep(ctypes.Structure):
     """akv_layer_step (include/akv_b200.h): one AKVLayer's steady decode-step state."""
@@ -82,6 +94,7 @@ SIGNATURES = {
     "akv_warm_append": (c_int, [c_void_p, c_int64, c_int64, POINTER(WarmLayout), c_int, c_void_p, c_int64, c_int64,
                                 c_int64, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64, c_int,
                                 c_int, c_int, c_int, c_void_p, c_size_t, c_void_p, c_void_p]),
+    "akv_mixed_decode_args": (c_int, [POINTER(DecodeArgs), c_void_p]),
     "akv_layer_decode_step": (c_int, [POINTER(LayerStep), c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64,
                                       c_void_p]),
     "akv_int4_group_dequant": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int64,

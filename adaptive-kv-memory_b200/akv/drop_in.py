@@ -33,6 +33,7 @@ from __future__ import annotations
 
 import ctypes
 import logging
+import math
 from typing import Any, Optional, Tuple
 
 import numpy as np
@@ -927,11 +928,54 @@ class AKVLayer(_LayerBase):
     def decode_attention(self, query: torch.Tensor, sm_scale: Optional[float] = None) -> torch.Tensor:
         """One decode query (B, Hq, 1, D) over the packed warm records and the
         FP16 hot tier, in place (akv_mixed_decode).  Returns (B, Hq, 1, D)."""
-        from .fused_attention import mixed_tier_decode_attention
+        from .fused_attention import KERNEL_HEAD_DIMS, mixed_tier_decode_attention
         hk, hv = self._hk[:, :, :self._hn], self._hv[:, :, :self._hn]  # buffer order: attention is order-free
-        if isinstance(self._warm, HeadGroupArena):
-            return self._warm.decode(query, hk, hv, sm_scale=sm_scale)
-        return mixed_tier_decode_attention(query, hk, hv, self._warm, sm_scale=sm_scale)
+        warm = self._warm
+        if isinstance(warm, HeadGroupArena):
+            return warm.decode(query, hk, hv, sm_scale=sm_scale)
+        D = query.shape[-1]
+        if (warm is not None and query.dtype == torch.float16 and query.dim() == 4 and query.stride(-1) == 1
+                and D in KERNEL_HEAD_DIMS and hk.stride() == hv.stride() and self._hn > 0):
+            return self._decode_args_call(query, hk, hv, warm, sm_scale)
+        return mixed_tier_decode_attention(query, hk, hv, warm, sm_scale=sm_scale)
+
+    def _decode_args_call(self, query, hk, hv, warm, sm_scale) -> torch.Tensor:
+        """mixed_tier_decode_attention through akv_mixed_decode_args: the
+        layer keeps the argument struct and its workspace, a step updates
+        the pointers and lengths that moved."""
+        B, Hq, _, D = query.shape
+        d = self.__dict__
+        a = d.get("_dec_args")
+        if a is None:
+            a = d["_dec_args"] = _C.DecodeArgs()
+            d["_dec_need"] = ctypes.c_size_t(0)
+            a.workspace_need = ctypes.addressof(d["_dec_need"])
+            d["_dec_ws"] = None
+        a.q, a.q_sb, a.q_sh = query.data_ptr(), query.stride(0), query.stride(1)
+        a.hot_k, a.hot_v = hk.data_ptr(), hv.data_ptr()
+        a.h_sb, a.h_sh, a.h_sn = hk.stride(0), hk.stride(1), hk.stride(2)
+        a.n_hot = self._hn
+        buf = warm.buf
+        a.warm, a.w_sb, a.w_sh = buf.data_ptr(), buf.stride(0), buf.stride(1)
+        if d.get("_dec_layout") is not warm.layout:
+            d["_dec_layout"] = warm.layout
+            a.layout = ctypes.addressof(warm.layout)
+        a.n_warm_blocks = warm.n_blocks
+        a.B, a.Hq, a.Hkv, a.D = B, Hq, warm.H, D
+        a.sm_scale = (1.0 / math.sqrt(D)) if sm_scale is None else float(sm_scale)
+        out = torch.empty(B, Hq, 1, D, dtype=torch.float16, device=query.device)
+        a.out, a.o_sb, a.o_sh = out.data_ptr(), Hq * D, D
+        lib = _C.load()
+        stream = _C.stream_of(query)
+        rc = lib.akv_mixed_decode_args(ctypes.byref(a), stream)
+        if rc == _C.AKV_ERR_WORKSPACE:  # first call or a longer context: a larger workspace, then again
+            need = int(d["_dec_need"].value)
+            ws = torch.empty(max(2 * need, 1 << 20), dtype=torch.uint8, device=query.device)
+            d["_dec_ws"] = ws
+            a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+            rc = lib.akv_mixed_decode_args(ctypes.byref(a), stream)
+        _C.check(rc, "akv_mixed_decode")
+        return out
 
     # ------------------------------------------------------------------ accounting
     def memory_usage_bytes(self) -> dict:

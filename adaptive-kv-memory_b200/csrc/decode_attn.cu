@@ -1397,6 +1397,20 @@ extern "C" int akv_mixed_decode(const uint16_t* q, int64_t q_sb, int64_t q_sh, c
                      workspace, workspace_bytes, status, stream);
 }
 
+extern "C" int akv_mixed_decode_args(const akv_decode_args* a, void* stream) {
+  if (!a) return AKV_ERR_NULL;
+  const size_t need = akv_decode_workspace_bytes(a->B, a->Hq, a->Hkv, a->D, a->n_hot, a->n_warm_blocks);
+  if (need == 0) return decode_head_dim_ok(a->D) ? AKV_ERR_SHAPE : AKV_ERR_UNSUPPORTED;
+  if (a->workspace_bytes < need) {
+    if (a->workspace_need) *a->workspace_need = need;
+    return AKV_ERR_WORKSPACE;
+  }
+  return akv_mixed_decode(a->q, a->q_sb, a->q_sh, a->hot_k, a->hot_v, a->h_sb, a->h_sh, a->h_sn, a->n_hot, a->hot_len,
+                          a->warm, a->w_sb, a->w_sh, a->layout, a->n_warm_blocks, a->warm_len, a->B, a->Hq, a->Hkv,
+                          a->D, a->sm_scale, a->out, a->o_sb, a->o_sh, a->lse, a->partial_out, a->workspace,
+                          a->workspace_bytes, a->status, stream);
+}
+
 extern "C" int akv_mixed_decode_paged(const uint16_t* q, int64_t q_sb, int64_t q_sh, const uint16_t* hot_k,
                                       const uint16_t* hot_v, int64_t h_sb, int64_t h_sh, int64_t h_sn, int n_hot,
                                       const int32_t* hot_len, const uint8_t* pool, int n_pages,

@@ -670,11 +670,19 @@ def hf_decode_bench(torch, akv, dev, new_tokens: int = 256, prompt: int = 32768)
     modes = ("dynamic", "view", "fused")
     for mode in modes:  # warm-up: kernels, allocator pools, HF's first-call paths
         decode(mode, ids[:, :4096], 4)
-    res, toks = {}, {}
-    for mode in modes:
+    # two timed runs per arm in mirrored order (dynamic, view, fused, fused,
+    # view, dynamic): the loops are host-bound, so the shared host's load
+    # moves single runs by 10 %; each arm reports its better run and both
+    res, toks, runs = {}, {}, {m: [] for m in modes}
+    for mode in modes + modes[::-1]:
         pre_ms, ms, toks[mode] = decode(mode, ids, new_tokens)
+        runs[mode].append((pre_ms, ms))
+    for mode in modes:
+        pre_ms = min(r[0] for r in runs[mode])
+        ms = min(r[1] for r in runs[mode])
         res[f"{mode}_tok_s"] = round(new_tokens / (ms * 1e-3), 1)
         res[f"{mode}_ms_per_token"] = round(ms / new_tokens, 3)
+        res[f"{mode}_ms_per_token_runs"] = [round(r[1] / new_tokens, 3) for r in runs[mode]]
         res[f"{mode}_prefill_ms"] = round(pre_ms, 1)
     model.config._attn_implementation = "sdpa"
     res["greedy_match_fused_vs_view"] = round((toks["view"] == toks["fused"]).float().mean().item(), 4)

@@ -310,6 +310,39 @@ int akv_mixed_decode(const uint16_t* q, int64_t q_sb, int64_t q_sh,
                      uint16_t* out, int64_t o_sb, int64_t o_sh, float* lse, float* partial_out,
                      void* workspace, size_t workspace_bytes, int* status, void* stream);
 
+/* The same call with its arguments in one struct, for callers that issue it
+ * every decode step with most arguments unchanged (an attention hook keeps
+ * one per layer and updates q, out and the warm length): the fields mean
+ * what the parameters of akv_mixed_decode mean.  When workspace_bytes is too
+ * small the call returns AKV_ERR_WORKSPACE and writes the bytes it needs to
+ * *workspace_need (nullable); nothing is launched. */
+typedef struct {
+  const uint16_t* q;
+  int64_t q_sb, q_sh;
+  const uint16_t* hot_k;
+  const uint16_t* hot_v;
+  int64_t h_sb, h_sh, h_sn;
+  int32_t n_hot;
+  const int32_t* hot_len;
+  const uint8_t* warm;
+  int64_t w_sb, w_sh;
+  const akv_warm_layout* layout;
+  int32_t n_warm_blocks;
+  const int32_t* warm_len;
+  int32_t B, Hq, Hkv, D;
+  float sm_scale;
+  uint16_t* out;
+  int64_t o_sb, o_sh;
+  float* lse;
+  float* partial_out;
+  void* workspace;
+  size_t workspace_bytes;
+  size_t* workspace_need;
+  int* status;
+} akv_decode_args;
+
+int akv_mixed_decode_args(const akv_decode_args* a, void* stream);
+
 /* Paged form of akv_mixed_decode for a pool of block records shared by many
  * sequences (continuous batching).  Replaces the attention call of the
  * reference's vLLM backend, AdaptiveAttentionBackend.forward

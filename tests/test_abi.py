@@ -102,3 +102,22 @@ def test_layer_step_struct_matches_header(tmp_path):
     out = [int(x) for x in subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split()]
     assert out[0] == ctypes.sizeof(_C.LayerStep)
     assert out[1:] == [getattr(_C.LayerStep, f).offset for f in fields]
+
+
+def test_decode_args_struct_matches_header(tmp_path):
+    import shutil
+    import subprocess
+    from akv import _C
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    fields = [f[0] for f in _C.DecodeArgs._fields_]
+    src = tmp_path / "da.c"
+    src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "akv_b200.h"\nint main(void){\n'
+                   + 'printf("%zu\\n", sizeof(akv_decode_args));\n'
+                   + "".join(f'printf("%zu\\n", offsetof(akv_decode_args, {f}));\n' for f in fields) + "return 0;}\n")
+    exe = tmp_path / "da"
+    subprocess.run([cc, "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
+    out = [int(x) for x in subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split()]
+    assert out[0] == ctypes.sizeof(_C.DecodeArgs)
+    assert out[1:] == [getattr(_C.DecodeArgs, f).offset for f in fields]
