@@ -844,6 +844,31 @@ class AKVLayer(_LayerBase):
                 or value_states.stride(-1) != 1:
             return False
         c = self.__dict__.get("_step_ctx")
+        key = self.__dict__.get("_step_key")
+        fresh = (c is not None and key is not None and key[0] is hk and key[1] is arena.buf and key[2] is ig.buf
+                 and key[3] is self._wslots_buf and key[4] is self._wpos_buf and key[5] is self._slot_pos_np
+                 and c.lo == ig.lo and c.hi == ig.hi and c.n_blocks == arena.n_blocks
+                 and c.n_wslots == self._wslots_n and c.n_wpos == self._wpos_n and c.total_len == self._total_len
+                 and c.step == self._step and c.warm_len == self._warm_len
+                 and c.warm_bytes_packed == self._warm_bytes_packed and key[6] is hg.buf and key[7] is pg.buf)
+        if not fresh:
+            c = self._refresh_step_ctx(c, hk, hv, arena, ig, hg, pg, pr)
+        ks, vs = key_states.stride(), value_states.stride()
+        _C.check(_C.load().akv_layer_decode_step(ctypes.byref(c), key_states.data_ptr(), ks[0], ks[1],
+                                                 value_states.data_ptr(), vs[0], vs[1], _C.stream_of(hk)),
+                 "akv_layer_decode_step")
+        for g in (ig, hg, pg):
+            g.lo, g.hi = c.lo, c.hi
+        arena.n_blocks = c.n_blocks
+        self._wslots_n, self._wpos_n = c.n_wslots, c.n_wpos
+        self._wslots_dev = None
+        self._slot_pos_dev = None
+        self._total_len, self._step, self._warm_len = c.total_len, c.step, c.warm_len
+        self._warm_bytes_packed = c.warm_bytes_packed
+        return True
+
+    def _refresh_step_ctx(self, c, hk, hv, arena, ig, hg, pg, pr):
+        """(Re)fill the akv_layer_step struct from the layer's current state."""
         if c is None:
             c = self.__dict__["_step_ctx"] = _C.LayerStep()
             kb, vb, D, H, B = self.warm_key_bits, self.warm_value_bits, arena.D, arena.H, arena.B
@@ -865,19 +890,9 @@ class AKVLayer(_LayerBase):
         c.slot_pos, c.cap_slot_pos = self._slot_pos_np.ctypes.data, self._slot_pos_np.shape[0]
         c.total_len, c.step, c.warm_len = self._total_len, self._step, self._warm_len
         c.warm_bytes_packed = self._warm_bytes_packed
-        ks, vs = key_states.stride(), value_states.stride()
-        _C.check(_C.load().akv_layer_decode_step(ctypes.byref(c), key_states.data_ptr(), ks[0], ks[1],
-                                                 value_states.data_ptr(), vs[0], vs[1], _C.stream_of(hk)),
-                 "akv_layer_decode_step")
-        for g in (ig, hg, pg):
-            g.lo, g.hi = c.lo, c.hi
-        arena.n_blocks = c.n_blocks
-        self._wslots_n, self._wpos_n = c.n_wslots, c.n_wpos
-        self._wslots_dev = None
-        self._slot_pos_dev = None
-        self._total_len, self._step, self._warm_len = c.total_len, c.step, c.warm_len
-        self._warm_bytes_packed = c.warm_bytes_packed
-        return True
+        self.__dict__["_step_key"] = (hk, buf, ig.buf, self._wslots_buf, self._wpos_buf, self._slot_pos_np, hg.buf,
+                                      pg.buf)
+        return c
 
     def full_view(self) -> Tuple[torch.Tensor, torch.Tensor]:
         """The chronologically sorted [warm; hot] FP16 K/V (drop_in.py:753-787)."""

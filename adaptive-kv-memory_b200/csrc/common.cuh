@@ -11,6 +11,8 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "akv_b200.h"
 
 #define AKV_DEV __device__ __forceinline__
@@ -86,7 +88,31 @@ __host__ __device__ constexpr RecLayout rec_layout(int D, int kb, int vb, int n)
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 constexpr uint32_t kSuspendHintNs = 1000000u;     // 1 ms
 
-// ---------------------------------------------------------------- status
+// ---------------------------------------------------------------- launch set-up
+// Dynamic shared memory above 48 KB needs a per-function attribute; setting
+// it costs a driver call, so each kernel instance (template argument) keeps
+// the largest size it has been given per device and sets it only when a
+// larger one is asked for.
+template <auto Kern>
+inline bool ensure_dynamic_smem(size_t smem) {
+  if (smem <= 48 * 1024) return true;
+  constexpr int kDevices = 64;
+  static std::atomic<int> have[kDevices];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  if (dev < 0 || dev >= kDevices)
+    return cudaFuncSetAttribute(Kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) ==
+           cudaSuccess;
+  int cur = have[dev].load(std::memory_order_acquire);
+  if (cur >= static_cast<int>(smem)) return true;
+  if (cudaFuncSetAttribute(Kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
+    return false;
+  while (cur < static_cast<int>(smem) && !have[dev].compare_exchange_weak(cur, static_cast<int>(smem))) {
+  }
+  return true;
+}
+
+// ---------------------------------------------------------------- status// ---------------------------------------------------------------- status
 AKV_DEV void set_status(int* status, int code) {
   if (status) atomicCAS(status, 0, code);
 }

@@ -1240,9 +1240,9 @@ template <int D, int KB, int VB, int NOUT>
 static int launch_decode3(const DecodeParams& p, cudaStream_t st) {
   const size_t smem = decode_smem_bytes(p.L.bytes, D);
   auto kern = p.btab ? mixed_decode_kernel<D, KB, VB, NOUT, true> : mixed_decode_kernel<D, KB, VB, NOUT, false>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
-      cudaSuccess)
-    return AKV_ERR_LAUNCH;
+  const bool ok = p.btab ? ensure_dynamic_smem<mixed_decode_kernel<D, KB, VB, NOUT, true>>(smem)
+                         : ensure_dynamic_smem<mixed_decode_kernel<D, KB, VB, NOUT, false>>(smem);
+  if (!ok) return AKV_ERR_LAUNCH;
   kern<<<dim3(p.splits, p.Hkv * p.n_hg, p.B), kDecodeThreads, smem, st>>>(p);
   return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_LAUNCH;
 }
