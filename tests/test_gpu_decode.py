@@ -109,7 +109,8 @@ def check(seed, B, Hq, Hkv, n_warm, n_hot, kb, vb, frac, D=128, outlier_ch=(7,),
 
 
 def test_config1_full():
-    """B1, 12 Q / 2 KV heads, D128, 512 hot + 3584 warm at 3 bits, 32-token groups,
+    """Config 1 (the reference's small benchmark case): B1, 12 Q / 2 KV heads, D128, 512 hot + 3584 warm
+    at 3 bits, 32-token groups,
     1% of K channels x12 outliers, RoPE on K."""
     check(0, 1, 12, 2, 3584, 512, 3, 3, 0.0, outlier_ch=(100,))
 
@@ -178,7 +179,7 @@ def test_extreme_magnitudes(q_mul, k_mul):
 
 
 def test_config3_full_context():
-    """BASELINE config 3 at full size (B16, 32 Q / 8 KV heads, 30,720 warm k4v2
+    """Config 3 (the headline decode shape) at full size (B16, 32 Q / 8 KV heads, 30,720 warm k4v2
     tokens with 1 % outliers + 2,048 hot): every warp streams a dozen records
     through its stage ring, refilling each stage.  Reference: fp32 attention
     over the arena's dequantised tiers (the dequantisation itself is checked
