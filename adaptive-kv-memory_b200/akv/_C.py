@@ -97,6 +97,15 @@ SIGNATURES = {
     "akv_mixed_decode_args": (c_int, [POINTER(DecodeArgs), c_void_p]),
     "akv_layer_decode_step": (c_int, [POINTER(LayerStep), c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64,
                                       c_void_p]),
+    "akv_peer_alloc": (c_int, [c_size_t, c_void_p]),
+    "akv_peer_free": (c_int, [c_void_p]),
+    "akv_ipc_export": (c_int, [c_void_p, c_void_p]),
+    "akv_ipc_open": (c_int, [c_void_p, c_void_p]),
+    "akv_ipc_close": (c_int, [c_void_p]),
+    "akv_peer_publish": (c_int, [c_void_p, c_int64, c_int, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p,
+                                 c_void_p]),
+    "akv_peer_combine": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int64, c_void_p,
+                                 c_void_p, c_void_p]),
     "akv_int4_group_dequant": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int64,
                                        c_int, c_int, c_int, c_int, c_void_p, c_int64, c_int64, c_void_p]),
     "akv_group_dequant": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int64,

@@ -143,17 +143,110 @@ def _all_gather(t: torch.Tensor, world: int, group=None) -> torch.Tensor:
     return torch.stack(outs)
 
 
+class PeerExchange:
+    """The cross-GPU step of a sequence split over NVLink peer memory.
+
+    Every rank allocates one exchange buffer (``akv_peer_alloc``: a gather
+    area for two epochs of the world's merged partial records, a flag per
+    rank, a counter), exports it as a CUDA IPC handle, and maps every other
+    rank's buffer (handles exchanged once with ``all_gather_object``).  Then
+    ``exchange(part)`` per decode step: ``akv_peer_publish`` stores this
+    rank's records into every rank's buffer and raises its flag there,
+    ``akv_peer_combine`` waits for the world's flags of the step in local
+    memory and merges — no collective call on the data path.  Every rank
+    calls ``exchange`` the same number of times, in the same order.
+    ``close()`` is collective too."""
+
+    HANDLE_BYTES = 64
+
+    def __init__(self, rows: int, D: int, group=None, device=None):
+        import ctypes
+        import torch.distributed as dist
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.rows, self.D = rows, D
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        lib = _C.load()
+        rec = D + 2
+        self.n_gather = 2 * self.world * rows * rec
+        nbytes = 4 * self.n_gather + 4 * self.world + 8
+        p = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            _C.check(lib.akv_peer_alloc(nbytes, ctypes.byref(p)), "akv_peer_alloc")
+            self.base = p.value
+            h = ctypes.create_string_buffer(self.HANDLE_BYTES)
+            _C.check(lib.akv_ipc_export(self.base, h), "akv_ipc_export")
+            handles = [None] * self.world
+            dist.all_gather_object(handles, h.raw, group=group)
+            self._opened = []
+            bases = []
+            for r, hb in enumerate(handles):
+                if r == self.rank:
+                    bases.append(self.base)
+                    continue
+                q = ctypes.c_void_p()
+                _C.check(lib.akv_ipc_open(ctypes.create_string_buffer(hb, self.HANDLE_BYTES), ctypes.byref(q)),
+                         "akv_ipc_open")
+                self._opened.append(q.value)
+                bases.append(q.value)
+        self.flags = self.base + 4 * self.n_gather
+        self.counter = self.flags + 4 * self.world
+        self.peer_gather = torch.tensor(bases, dtype=torch.int64, device=self.device)
+        self.peer_flags = torch.tensor([b + 4 * self.n_gather for b in bases], dtype=torch.int64, device=self.device)
+        self.epoch = 0
+        dist.barrier(group=group)  # every rank has mapped every buffer before the first publish
+
+    def exchange(self, part: torch.Tensor, out: Optional[torch.Tensor] = None, lse: Optional[torch.Tensor] = None,
+                 status: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Merge this rank's (rows, D+2) partial records with every other rank's: (rows, D) fp16."""
+        if part.shape != (self.rows, self.D + 2) or part.dtype != torch.float32 or part.stride(-1) != 1:
+            raise ValueError("partial records must be fp32 (rows, D+2) with a contiguous last dim")
+        if out is None:
+            out = torch.empty(self.rows, self.D, dtype=torch.float16, device=part.device)
+        lib = _C.load()
+        st = _C.stream_of(part)
+        self.epoch += 1
+        _C.check(lib.akv_peer_publish(part.data_ptr(), part.stride(0), self.rows, self.D, self.peer_gather.data_ptr(),
+                                      self.peer_flags.data_ptr(), self.world, self.rank, self.epoch, self.counter, st),
+                 "akv_peer_publish")
+        _C.check(lib.akv_peer_combine(self.base, self.flags, self.rows, self.D, self.world, self.epoch,
+                                      out.data_ptr(), out.stride(0), _C.ptr(lse), _C.ptr(status), st),
+                 "akv_peer_combine")
+        return out
+
+    def close(self) -> None:
+        """Collective: after every rank's work is done, unmap the peers' buffers and free this one."""
+        import torch.distributed as dist
+        if self.base is None:
+            return
+        lib = _C.load()
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)  # nobody still stores into a buffer about to go
+        with torch.cuda.device(self.device):
+            for q in self._opened:
+                lib.akv_ipc_close(q)
+            dist.barrier(group=self.group)
+            lib.akv_peer_free(self.base)
+        self.base = None
+
+
 def sequence_split_decode(query: torch.Tensor, hot_keys: Optional[torch.Tensor],
                           hot_values: Optional[torch.Tensor], warm, world: int,
                           sm_scale: Optional[float] = None, process_group=None,
                           partial: Optional[Callable] = None, all_gather: Optional[Callable] = None,
-                          combine: Optional[Callable] = None) -> torch.Tensor:
+                          combine: Optional[Callable] = None,
+                          exchange: Optional[PeerExchange] = None) -> torch.Tensor:
     """Decode attention of one sequence whose tokens are spread over ``world`` GPUs.
 
     Each GPU passes the tokens it holds (its contiguous share of warm blocks,
     and the hot window on whichever GPU keeps it; others pass None).  Returns
     (B, Hq, D) fp16 on every GPU."""
     partial = partial or local_partial
+    if exchange is not None:  # NVLink peer memory: publish + wait-and-merge, no collective call
+        p = partial(query, hot_keys, hot_values, warm, sm_scale)
+        q3 = query.reshape(query.shape[0], query.shape[1], query.shape[-1])
+        return exchange.exchange(p).reshape(q3.shape)
     all_gather = all_gather or (lambda t: _all_gather(t, world, process_group))
     combine = combine or combine_partials
     p = partial(query, hot_keys, hot_values, warm, sm_scale)

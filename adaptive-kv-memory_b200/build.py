@@ -20,7 +20,7 @@ CSRC = os.path.join(HERE, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
 OUT_DIR = os.path.join(HERE, "akv", "_lib")
 LIB = os.path.join(OUT_DIR, "libakv_sm100.so")
-SOURCES = ["quant_pack.cu", "decode_attn.cu", "tiering.cu", "prefill_attn.cu", "group_format.cu", "layer_step.cu"]
+SOURCES = ["quant_pack.cu", "decode_attn.cu", "tiering.cu", "prefill_attn.cu", "group_format.cu", "layer_step.cu", "peer_exchange.cu"]
 
 
 def nvcc() -> str:

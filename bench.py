@@ -517,13 +517,42 @@ def seq_split_bench(torch, akv, dev, world: int, rank: int, reps: int = 20) -> d
                        dtype=torch.float64, device=dev)
     dist.all_reduce(med, op=dist.ReduceOp.MAX)
     split_out = out.clone()
-    max_err = single_us = None
+
+    # the same layer with the cross-GPU step over NVLink peer memory
+    # (akv_peer_publish + akv_peer_combine: no collective call)
+    ex = P.PeerExchange(rows, D, device=dev)
+    out_peer = torch.empty(rows, D, dtype=torch.float16, device=dev)
+
+    def layer_peer(i, ev):
+        ev[0].record()
+        p = P.local_partial(q, hot[0], hot[1], arenas[i % copies])
+        ev[1].record()
+        ex.exchange(p, out=out_peer)
+        ev[2].record()
+
+    for i in range(3):
+        layer_peer(i, new_events()[0])
+    torch.cuda.synchronize()
+    dist.barrier()
+    evs = new_events()
+    torch.cuda._sleep(20_000_000)
+    for i in range(reps):
+        layer_peer(i, evs[i])
+    torch.cuda.synchronize()
+    tp = torch.tensor([statistics.median(ev[1].elapsed_time(ev[2]) * 1e3 for ev in evs),
+                       statistics.median(ev[0].elapsed_time(ev[2]) * 1e3 for ev in evs)],
+                      dtype=torch.float64, device=dev)
+    dist.all_reduce(tp, op=dist.ReduceOp.MAX)
+    peer_out = out_peer.clone()
+    ex.close()
+    max_err = single_us = peer_err = None
     if rank == 0:  # the whole sequence on this GPU
         full = akv.WarmArena(B, Hkv, D, 4, 4, 0.0, max_blocks=nblk, device=dev)
         for r in range(world):
             shard(r, full)
         ref = akv.mixed_tier_decode_attention(q, hk, hv, full)
         max_err = float((split_out.float() - ref.reshape(rows, D).float()).abs().max().item())
+        peer_err = float((peer_out.float() - ref.reshape(rows, D).float()).abs().max().item())
         e = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
         torch.cuda._sleep(20_000_000)
         for i in range(5):  # the whole context is ~690 MB, far above the L2
@@ -541,7 +570,11 @@ def seq_split_bench(torch, akv, dev, world: int, rank: int, reps: int = 20) -> d
            "warm_blocks_per_rank": hi - lo, "layer_copies": copies,
            "limiter": max((("decode", d), ("all_gather", g_), ("combine", c_)), key=lambda x: x[1])[0],
            "max_err": max_err,
-           "single_gpu_layer_us": None if single_us is None else round(single_us, 2)}
+           "single_gpu_layer_us": None if single_us is None else round(single_us, 2),
+           "peer": {"how": "the cross-GPU step over NVLink peer memory: akv_peer_publish (P2P stores of the "
+                           "merged records + flags) and akv_peer_combine (bounded wait, merge)",
+                    "exchange_us": round(float(tp[0]), 2), "layer_us": round(float(tp[1]), 2),
+                    "max_err": peer_err}}
     if single_us:
         res["speedup_vs_single_gpu"] = round(single_us / l_, 3)
     del arenas, mine

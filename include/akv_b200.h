@@ -560,6 +560,43 @@ int akv_layer_decode_step(akv_layer_step* ctx, const uint16_t* new_k, int64_t nk
                           const uint16_t* new_v, int64_t nv_sb, int64_t nv_sh, void* stream);
 
 /* ------------------------------------------------------------------------
+ * (e) Sequence split across GPUs over NVLink peer memory: the cross-GPU step
+ * of a batch-1, very-long-context decode whose warm blocks are spread over
+ * the GPUs (the reference attends over one GPU's whole cache; this replaces
+ * an all-gather of the partial records followed by akv_lse_combine).
+ *
+ * Each GPU owns one exchange buffer (akv_peer_alloc, zeroed; the explicit
+ * exception to "the library never allocates": it must be an allocation base
+ * for CUDA IPC) laid out as
+ *   gather [2][world][rows][D+2] floats, then flags [world] int32, then a
+ *   counter [2] int32,
+ * exported with akv_ipc_export (64-byte handle) and mapped by every other
+ * GPU's process with akv_ipc_open (lazy peer access).  Per step (epoch
+ * 1, 2, ..., the same on every GPU):
+ *   akv_peer_publish  this GPU's merged partial records part[rows][D+2] (row
+ *                     stride part_sr floats, e.g. akv_mixed_decode's
+ *                     partial_out) into slot [epoch & 1][rank] of every GPU's
+ *                     gather (P2P stores; peer_gather: device array of the
+ *                     world gather bases as mapped here), then flag `rank` of
+ *                     every GPU (peer_flags: device array of the world flag
+ *                     arrays) set to epoch after system-scope fences
+ *   akv_peer_combine  waits until every flag of this GPU's array reaches
+ *                     epoch (bounded, 2 s: AKV_ERR_TIMEOUT in *status, zero
+ *                     output), then merges the world records into fp16 out
+ *                     (row stride o_sr) and natural-log lse (nullable)
+ * Free an exchange only after every GPU has synchronised and closed its
+ * mappings (akv_ipc_close). */
+int akv_peer_alloc(size_t bytes, void** dev_ptr_out);
+int akv_peer_free(void* dev_ptr);
+int akv_ipc_export(const void* dev_ptr, void* handle_out);
+int akv_ipc_open(const void* handle, void** dev_ptr_out);
+int akv_ipc_close(void* dev_ptr);
+int akv_peer_publish(const float* part, int64_t part_sr, int rows, int D, float* const* peer_gather,
+                     int* const* peer_flags, int world, int rank, int epoch, int* counter, void* stream);
+int akv_peer_combine(const float* gather, const int* flags, int rows, int D, int world, int epoch,
+                     uint16_t* out, int64_t o_sr, float* lse, int* status, void* stream);
+
+/* ------------------------------------------------------------------------
  * A8: cold tier copies.  Replaces AsyncMigrator._do_warm_to_cold /
  * _do_cold_to_warm (akv/async_migration.py:303-349): warm block records move
  * byte-for-byte between HBM and a pinned host arena with cudaMemcpy2DAsync

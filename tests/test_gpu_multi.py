@@ -65,6 +65,28 @@ def _worker(rank, world, port, errfile):
         assert err <= 2e-3, f"sequence split err {err}"
         torch.cuda.synchronize()
         dist.barrier()
+        # the same split with the cross-GPU step over NVLink peer memory, five
+        # steps (both gather halves, several epochs), new queries each step
+        ex = P.PeerExchange(Hq, D, device=dev)
+        try:
+            st = torch.zeros(1, dtype=torch.int32, device=dev)
+            for step in range(5):
+                qs = torch.from_numpy(np.random.default_rng(50 + step).standard_normal((1, Hq, D))
+                                      .astype(np.float16)).to(dev)
+                if step % 2:
+                    out_p = P.sequence_split_decode(qs, hk if rank == 0 else None, hv if rank == 0 else None, part,
+                                                    world, exchange=ex)
+                else:
+                    p = P.local_partial(qs, hk if rank == 0 else None, hv if rank == 0 else None, part)
+                    out_p = ex.exchange(p, status=st).reshape(qs.shape)
+                ref_p = akv.mixed_tier_decode_attention(qs, hk, hv, whole)
+                torch.cuda.synchronize()
+                e = (out_p.float() - ref_p.float()).abs().max().item()
+                assert e <= 2e-3, f"peer sequence split err {e} at step {step}"
+            assert int(st.item()) == 0
+        finally:
+            ex.close()
+        dist.barrier()
     except Exception as e:  # report to the parent; every rank still leaves the group
         with open(f"{errfile}.{rank}", "w") as f:
             f.write(repr(e))
