@@ -46,16 +46,25 @@ def build(verbose: bool = False, force: bool = False) -> str:
         lib_t = os.path.getmtime(LIB)
         if all(os.path.getmtime(d) <= lib_t for d in deps):
             return LIB
-    objs = []
-    for s in srcs:
+    # the sources compile side by side, and each splits its device-code
+    # optimisation over the host's cores (the decode kernel's many template
+    # instances dominate the build)
+    from concurrent.futures import ThreadPoolExecutor
+
+    def compile_one(s):
         o = os.path.join(OUT_DIR, os.path.basename(s) + ".o")
-        cmd = [nvcc(), "-c", s, "-o", o] + flags(verbose)
+        cmd = [nvcc(), "-c", s, "-o", o, f"--split-compile={os.cpu_count() or 1}"] + flags(verbose)
         r = subprocess.run(cmd, capture_output=True, text=True)
-        if verbose or r.returncode:
-            sys.stderr.write(r.stdout + r.stderr)
-        if r.returncode:
-            raise RuntimeError(f"nvcc failed on {s}")
-        objs.append(o)
+        return s, o, r
+
+    objs = []
+    with ThreadPoolExecutor(max_workers=len(srcs)) as ex:
+        for s, o, r in ex.map(compile_one, srcs):
+            if verbose or r.returncode:
+                sys.stderr.write(r.stdout + r.stderr)
+            if r.returncode:
+                raise RuntimeError(f"nvcc failed on {s}")
+            objs.append(o)
     tmp = LIB + ".tmp"
     cmd = [nvcc(), "-shared", "-o", tmp] + objs + ["-gencode", "arch=compute_100a,code=sm_100a",
                                                  "-Xcompiler", "-fPIC", "-lcudart"]
