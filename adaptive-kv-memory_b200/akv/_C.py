@@ -94,6 +94,9 @@ SIGNATURES = {
     "akv_warm_append": (c_int, [c_void_p, c_int64, c_int64, POINTER(WarmLayout), c_int, c_void_p, c_int64, c_int64,
                                 c_int64, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64, c_int,
                                 c_int, c_int, c_int, c_void_p, c_size_t, c_void_p, c_void_p]),
+    "akv_warm_demote_install": (c_int, [c_void_p, c_int64, c_int64, POINTER(WarmLayout), c_int, c_void_p, c_int64,
+                                        c_int64, c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p,
+                                        c_int64, c_int64, c_int, c_int, c_void_p, c_void_p]),
     "akv_mixed_decode_args": (c_int, [POINTER(DecodeArgs), c_void_p]),
     "akv_layer_decode_step": (c_int, [POINTER(LayerStep), c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64,
                                       c_void_p]),

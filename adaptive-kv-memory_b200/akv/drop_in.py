@@ -42,6 +42,7 @@ import torch
 from . import _C
 from .bitpack import packed_width
 from .packed_layout import BLOCK, HeadGroupArena, WarmArena
+from .fused_attention import KERNEL_HEAD_DIMS as _KERNEL_HEAD_DIMS
 from .tiering import gather_rows, scatter_rows
 
 logger = logging.getLogger(__name__)
@@ -940,24 +941,29 @@ class AKVLayer(_LayerBase):
         return prefill_attention(query, q_pos, self._hk[:, :, :hn], self._hv[:, :, :hn], hot_pos, self._warm,
                                  self._slot_pos[: self._warm.n_blocks * BLOCK], sm_scale=sm_scale)
 
-    def decode_attention(self, query: torch.Tensor, sm_scale: Optional[float] = None) -> torch.Tensor:
+    def decode_attention(self, query: torch.Tensor, sm_scale: Optional[float] = None,
+                         reuse_out: bool = False) -> torch.Tensor:
         """One decode query (B, Hq, 1, D) over the packed warm records and the
-        FP16 hot tier, in place (akv_mixed_decode).  Returns (B, Hq, 1, D)."""
-        from .fused_attention import KERNEL_HEAD_DIMS, mixed_tier_decode_attention
-        hk, hv = self._hk[:, :, :self._hn], self._hv[:, :, :self._hn]  # buffer order: attention is order-free
+        FP16 hot tier, in place (akv_mixed_decode).  Returns (B, Hq, 1, D).
+        reuse_out: write into a buffer the layer keeps and reuses at its next
+        step (for a caller that consumes the result before then)."""
         warm = self._warm
+        hk_all = self._hk
+        if (type(warm) is WarmArena and self._hn > 0 and query.dtype == torch.float16 and query.dim() == 4
+                and query.stride(-1) == 1 and query.shape[-1] in _KERNEL_HEAD_DIMS
+                and hk_all.stride() == self._hv.stride()):
+            return self._decode_args_call(query, hk_all, self._hv, warm, sm_scale, reuse_out)
+        from .fused_attention import mixed_tier_decode_attention
+        hk, hv = hk_all[:, :, :self._hn], self._hv[:, :, :self._hn]  # buffer order: attention is order-free
         if isinstance(warm, HeadGroupArena):
             return warm.decode(query, hk, hv, sm_scale=sm_scale)
-        D = query.shape[-1]
-        if (warm is not None and query.dtype == torch.float16 and query.dim() == 4 and query.stride(-1) == 1
-                and D in KERNEL_HEAD_DIMS and hk.stride() == hv.stride() and self._hn > 0):
-            return self._decode_args_call(query, hk, hv, warm, sm_scale)
         return mixed_tier_decode_attention(query, hk, hv, warm, sm_scale=sm_scale)
 
-    def _decode_args_call(self, query, hk, hv, warm, sm_scale) -> torch.Tensor:
+    def _decode_args_call(self, query, hk, hv, warm, sm_scale, reuse_out: bool = False) -> torch.Tensor:
         """mixed_tier_decode_attention through akv_mixed_decode_args: the
-        layer keeps the argument struct and its workspace, a step updates
-        the pointers and lengths that moved."""
+        layer keeps the argument struct and its workspace; a step rewrites
+        the query pointer and the lengths, the rest only when the tensors
+        behind it (hot buffer, warm arena, query shape, scale) changed."""
         B, Hq, _, D = query.shape
         d = self.__dict__
         a = d.get("_dec_args")
@@ -966,20 +972,32 @@ class AKVLayer(_LayerBase):
             d["_dec_need"] = ctypes.c_size_t(0)
             a.workspace_need = ctypes.addressof(d["_dec_need"])
             d["_dec_ws"] = None
-        a.q, a.q_sb, a.q_sh = query.data_ptr(), query.stride(0), query.stride(1)
-        a.hot_k, a.hot_v = hk.data_ptr(), hv.data_ptr()
-        a.h_sb, a.h_sh, a.h_sn = hk.stride(0), hk.stride(1), hk.stride(2)
-        a.n_hot = self._hn
+            d["_dec_key"] = None
         buf = warm.buf
-        a.warm, a.w_sb, a.w_sh = buf.data_ptr(), buf.stride(0), buf.stride(1)
-        if d.get("_dec_layout") is not warm.layout:
-            d["_dec_layout"] = warm.layout
+        qs = query.stride()
+        objs, vals = (hk, hv, buf, warm.layout), (B, Hq, D, qs[0], qs[1], sm_scale)
+        old = d["_dec_key"]
+        if old is None or any(x is not y for x, y in zip(objs, old[0])) or vals != old[1]:
+            d["_dec_key"] = (objs, vals)
+            a.q_sb, a.q_sh = qs[0], qs[1]
+            a.hot_k, a.hot_v = hk.data_ptr(), hv.data_ptr()
+            a.h_sb, a.h_sh, a.h_sn = hk.stride(0), hk.stride(1), hk.stride(2)
+            a.warm, a.w_sb, a.w_sh = buf.data_ptr(), buf.stride(0), buf.stride(1)
             a.layout = ctypes.addressof(warm.layout)
+            a.B, a.Hq, a.Hkv, a.D = B, Hq, warm.H, D
+            a.sm_scale = (1.0 / math.sqrt(D)) if sm_scale is None else float(sm_scale)
+            d["_dec_out"] = None
+        a.q = query.data_ptr()
+        a.n_hot = self._hn
         a.n_warm_blocks = warm.n_blocks
-        a.B, a.Hq, a.Hkv, a.D = B, Hq, warm.H, D
-        a.sm_scale = (1.0 / math.sqrt(D)) if sm_scale is None else float(sm_scale)
-        out = torch.empty(B, Hq, 1, D, dtype=torch.float16, device=query.device)
-        a.out, a.o_sb, a.o_sh = out.data_ptr(), Hq * D, D
+        out = d["_dec_out"] if reuse_out else None
+        if out is None or out.device != query.device:
+            out = torch.empty(B, Hq, 1, D, dtype=torch.float16, device=query.device)
+            if reuse_out:
+                d["_dec_out"] = out
+            a.out, a.o_sb, a.o_sh = out.data_ptr(), Hq * D, D
+        elif a.out != out.data_ptr():
+            a.out, a.o_sb, a.o_sh = out.data_ptr(), Hq * D, D
         lib = _C.load()
         stream = _C.stream_of(query)
         rc = lib.akv_mixed_decode_args(ctypes.byref(a), stream)

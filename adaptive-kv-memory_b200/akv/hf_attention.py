@@ -45,18 +45,19 @@ def akv_attention_forward(module: torch.nn.Module, query: torch.Tensor, key: tor
                           scaling: Optional[float] = None, is_causal: Optional[bool] = None, **kwargs):
     """The ``AttentionInterface`` signature: query (B, Hq, q_len, D), key /
     value (B, Hkv, kv_len, D); returns ((B, q_len, Hq, D), None)."""
-    from transformers.integrations.sdpa_attention import sdpa_attention_forward
-
     layer = getattr(key, "_akv_layer", None)
     if layer is not None:
         plain = attention_mask is None and not dropout and kwargs.get("sliding_window") is None
         if plain and query.shape[2] == 1 and query.shape[-1] in KERNEL_HEAD_DIMS:
-            out = layer.decode_attention(query, scaling)  # (B, Hq, 1, D)
+            # the output buffer is the layer's own, rewritten at its next decode
+            # step; the caller's o_proj has consumed it by then (stream order)
+            out = layer.decode_attention(query, scaling, reuse_out=True)  # (B, Hq, 1, D)
             return out.transpose(1, 2), None
         if plain and query.shape[-1] == KERNEL_HEAD_DIM and is_causal is not False and layer.can_prefill_fused():
             out = layer.prefill_attention(query, scaling)  # (B, Hq, q_len, D), causal by position
             return out.transpose(1, 2), None
         key, value = layer.full_view()
+    from transformers.integrations.sdpa_attention import sdpa_attention_forward
     return sdpa_attention_forward(module, query, key, value, attention_mask, dropout=dropout, scaling=scaling,
                                   is_causal=is_causal, **kwargs)
 

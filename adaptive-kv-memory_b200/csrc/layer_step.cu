@@ -49,23 +49,16 @@ extern "C" int akv_layer_decode_step(akv_layer_step* c, const uint16_t* new_k, i
   const int64_t vpos = pos[lo + v0];
   if (r < 0 || r >= c->hot_rows) return AKV_ERR_SHAPE;
 
-  // its K / V rows into a new record (one group of one token)
+  // its K / V rows into a new record (one group of one token), and the new
+  // token written over them in ring row r: one launch (the record is read
+  // before the row is overwritten inside each CTA)
   const int blk = c->n_blocks;
-  const uint16_t* kr = c->hot_k + r * c->h_sn;
-  const uint16_t* vr = c->hot_v + r * c->h_sn;
-  int rc = akv_warm_append(c->arena, c->a_sb, c->a_sh, &c->layout, blk, kr, c->h_sb, c->h_sh, c->h_sn, vr, c->h_sb,
-                           c->h_sh, c->h_sn, nullptr, 0, 0, c->B, c->H, 1, 1, nullptr, 0, c->status, stream);
+  uint16_t* kr = c->hot_k + r * c->h_sn;
+  uint16_t* vr = c->hot_v + r * c->h_sn;
+  const int rc = akv_warm_demote_install(c->arena, c->a_sb, c->a_sh, &c->layout, blk, kr, c->h_sb, c->h_sh, vr,
+                                         c->h_sb, c->h_sh, new_k, nk_sb, nk_sh, new_v, nv_sb, nv_sh, c->B, c->H,
+                                         c->status, stream);
   if (rc != AKV_OK) return rc;
-  // the new token into row r (after the quantiser read it: same stream)
-  const size_t row_bytes = static_cast<size_t>(c->layout.head_dim) * 2;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  for (int b = 0; b < c->B; ++b) {
-    if (cudaMemcpy2DAsync(c->hot_k + b * c->h_sb + r * c->h_sn, c->h_sh * 2, new_k + b * nk_sb, nk_sh * 2, row_bytes,
-                          c->H, cudaMemcpyDeviceToDevice, st) != cudaSuccess ||
-        cudaMemcpy2DAsync(c->hot_v + b * c->h_sb + r * c->h_sn, c->h_sh * 2, new_v + b * nv_sb, nv_sh * 2, row_bytes,
-                          c->H, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
-      return AKV_ERR_LAUNCH;
-  }
 
   // warm-side host vectors
   c->wslots[c->n_wslots++] = static_cast<int64_t>(blk) * AKV_BLOCK_TOKENS;

@@ -350,15 +350,18 @@ __host__ __device__ inline QuantSmem quant_smem_layout(int H, int nt, int D, int
 // channels and key scales, and MODE kQuantEncode (same grid) encodes each
 // chunk with them.
 // ---------------------------------------------------------------------------
+// The CTA body, with its grid coordinates as arguments so that a fused
+// kernel can run it for more than one tensor (demote_install_kernel).
+// Returns false when the staging copy timed out (status set, nothing written).
 template <int BITS, bool IS_KEY, int MODE>
-__global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group_kernel(const QuantParams p) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
+__device__ __forceinline__ bool quantize_group_body(const QuantParams& p, int bx, int by, int bz,
+                                                    unsigned char* smem_raw) {
   const int tid = threadIdx.x;
-  const int b = blockIdx.y;
-  const int t0 = MODE == kQuantFull ? blockIdx.x * p.group : blockIdx.x * kBlockTokens;  // multiple of 32, or 0
-  const int chunk = blockIdx.x;
+  const int b = by;
+  const int t0 = MODE == kQuantFull ? bx * p.group : bx * kBlockTokens;  // multiple of 32, or 0
+  const int chunk = bx;
   const int grp = t0 / p.group;
-  const int h0 = MODE == kQuantFull ? 0 : blockIdx.z * p.heads_per_cta;  // first head of this CTA
+  const int h0 = MODE == kQuantFull ? 0 : bz * p.heads_per_cta;  // first head of this CTA
   const int blk0 = t0 / kBlockTokens;
   const int nt = MODE == kQuantFull ? min(p.group, p.N - t0) : min(kBlockTokens, p.N - t0);
   const int nblk = (nt + kBlockTokens - 1) / kBlockTokens;
@@ -411,7 +414,7 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
     const bool ok = mbar_wait(&stage_bar, 0, p.status);
     if (__syncthreads_or(!ok)) {  // timed out: let the copies land (bounded), then give up
       if (!ok) mbar_wait(&stage_bar, 0, p.status);
-      return;
+      return false;
     }
   }
 
@@ -487,7 +490,7 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
     }
     __syncthreads();
   }
-  if constexpr (MODE == kQuantStats) return;
+  if constexpr (MODE == kQuantStats) return true;
 
   // ---- outlier channels: score = mean over heads of the norms, top-n
   //      (chunked path: the reduction kernel chose them for the whole group)
@@ -790,7 +793,58 @@ __global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group
       }
     }
   }
+  return true;
 }
+
+template <int BITS, bool IS_KEY, int MODE>
+__global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_group_kernel(const QuantParams p) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  quantize_group_body<BITS, IS_KEY, MODE>(p, blockIdx.x, blockIdx.y, blockIdx.z, smem_raw);
+}
+
+// One demote event of a single token per batch row that also puts the new
+// token in the freed slot: grid (1, B, 2), z = 0 quantises row b's K source
+// row (all heads) into its record and z = 1 the V row, then the CTA writes
+// the new token's K (or V) rows over the source row it has just staged (the
+// staging wait orders the read before the overwrite; no other CTA reads that
+// row).  One launch for what is otherwise two quantiser launches and two
+// row copies per decode step.
+struct InstallRows {
+  const __half* nk;
+  int64_t nk_sb, nk_sh;
+  const __half* nv;
+  int64_t nv_sb, nv_sh;
+  int vec16;  // sources and destinations 16-byte aligned with strides in 8-half units
+};
+
+template <int KBITS, int VBITS>
+__global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) demote_install_kernel(const QuantParams pk,
+                                                                                         const QuantParams pv,
+                                                                                         const InstallRows ins) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const bool key = blockIdx.z == 0;
+  const bool ok = key ? quantize_group_body<KBITS, true, kQuantFull>(pk, 0, blockIdx.y, 0, smem_raw)
+                      : quantize_group_body<VBITS, false, kQuantFull>(pv, 0, blockIdx.y, 0, smem_raw);
+  if (!ok) return;
+  const QuantParams& p = key ? pk : pv;
+  const int b = blockIdx.y, D = p.D;
+  const __half* src = key ? ins.nk + b * ins.nk_sb : ins.nv + b * ins.nv_sb;
+  const int64_t s_sh = key ? ins.nk_sh : ins.nv_sh;
+  __half* dst = const_cast<__half*>(p.src) + b * p.sb;
+  if (ins.vec16) {
+    const int per_row = D / 8;
+    for (int i = threadIdx.x; i < p.H * per_row; i += blockDim.x) {
+      const int h = i / per_row, c = (i % per_row) * 8;
+      *reinterpret_cast<uint4*>(dst + h * p.sh + c) = *reinterpret_cast<const uint4*>(src + h * s_sh + c);
+    }
+  } else {
+    for (int i = threadIdx.x; i < p.H * D; i += blockDim.x) {
+      const int h = i / D, c = i % D;
+      dst[h * p.sh + c] = src[h * s_sh + c];
+    }
+  }
+}
+
 
 // ---------------------------------------------------------------------------
 // chunked path, step 2: one CTA per (group, b) folds the chunk partials in
@@ -1147,11 +1201,12 @@ extern "C" int akv_quantize_ws(const uint16_t* src, int64_t src_sb, int64_t src_
                           n_outlier, dst, nullptr, 0, workspace, workspace_bytes, status, stream);
 }
 
-extern "C" int akv_quantize_ext(const uint16_t* src, int64_t src_sb, int64_t src_sh, int64_t src_sn,
-                                const int64_t* tok_idx, int64_t tok_sb, int64_t n_src, int B, int H, int N, int D,
-                                int bits, int is_key, int group, int n_outlier, const akv_qdest* dst,
-                                const float* score_sum, int score_heads, void* workspace, size_t workspace_bytes,
-                                int* status, void* stream) {
+// Checks of one quantiser call and its parameter block (akv_quantize_ext and
+// the fused single-token demotion share them).
+static int prepare_quant(const uint16_t* src, int64_t src_sb, int64_t src_sh, int64_t src_sn, const int64_t* tok_idx,
+                         int64_t tok_sb, int64_t n_src, int B, int H, int N, int D, int bits, int is_key, int group,
+                         int n_outlier, const akv_qdest* dst, const float* score_sum, int score_heads, int* status,
+                         QuantParams& p, QuantPlan& pl) {
   if (!src || !dst) return AKV_ERR_NULL;
   if (tok_idx && n_src <= 0) return AKV_ERR_SHAPE;
   if (score_sum && score_heads <= 0) return AKV_ERR_SHAPE;
@@ -1173,10 +1228,9 @@ extern "C" int akv_quantize_ext(const uint16_t* src, int64_t src_sb, int64_t src
     return AKV_ERR_ALIGN;
   if (dst->mask.ptr && !aligned(dst->mask.ptr, 4)) return AKV_ERR_ALIGN;
   if (dst->out_vdq.ptr && (!aligned(dst->out_vdq.ptr, 2) || dst->out_vdq.sslot % 2)) return AKV_ERR_ALIGN;
-  const QuantPlan pl = plan_quant(B, H, N, D, group, n_outlier, is_key != 0);
+  pl = plan_quant(B, H, N, D, group, n_outlier, is_key != 0);
   if (pl.smem > kQuantSmemLimit) return AKV_ERR_UNSUPPORTED;
-  if (pl.chunked && (!workspace || workspace_bytes < pl.ws_bytes || !aligned(workspace, 256))) return AKV_ERR_WORKSPACE;
-  QuantParams p{};
+  p = QuantParams{};
   p.src = reinterpret_cast<const __half*>(src);
   p.sb = src_sb;
   p.sh = src_sh;
@@ -1196,6 +1250,21 @@ extern "C" int akv_quantize_ext(const uint16_t* src, int64_t src_sb, int64_t src
   p.status = status;
   p.score_sum = score_sum;
   p.score_heads = score_heads;
+  p.n_groups = pl.n_groups;
+  return AKV_OK;
+}
+
+extern "C" int akv_quantize_ext(const uint16_t* src, int64_t src_sb, int64_t src_sh, int64_t src_sn,
+                                const int64_t* tok_idx, int64_t tok_sb, int64_t n_src, int B, int H, int N, int D,
+                                int bits, int is_key, int group, int n_outlier, const akv_qdest* dst,
+                                const float* score_sum, int score_heads, void* workspace, size_t workspace_bytes,
+                                int* status, void* stream) {
+  QuantParams p;
+  QuantPlan pl;
+  const int rc = prepare_quant(src, src_sb, src_sh, src_sn, tok_idx, tok_sb, n_src, B, H, N, D, bits, is_key, group,
+                               n_outlier, dst, score_sum, score_heads, status, p, pl);
+  if (rc != AKV_OK) return rc;
+  if (pl.chunked && (!workspace || workspace_bytes < pl.ws_bytes || !aligned(workspace, 256))) return AKV_ERR_WORKSPACE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   switch (bits * 2 + (is_key ? 1 : 0)) {
     case 5: return launch_quant<2, true>(p, pl, workspace, st);
@@ -1378,4 +1447,54 @@ extern "C" int akv_warm_append(uint8_t* arena, int64_t a_sb, int64_t a_sh, const
   if (rc != AKV_OK) return rc;
   return akv_quantize_ext(v, v_sb, v_sh, v_sn, tok_idx, tok_sb, n_src, B, H, N, L.head_dim, L.value_bits, 0, group,
                           L.n_outlier, &dv, nullptr, 0, workspace, workspace_bytes, status, stream);
+}
+
+template <int KBITS, int VBITS>
+static int launch_demote_install(const QuantParams& pk, const QuantParams& pv, const InstallRows& ins, size_t smem,
+                                 int B, cudaStream_t st) {
+  auto kern = demote_install_kernel<KBITS, VBITS>;
+  if (!set_smem(kern, smem)) return AKV_ERR_LAUNCH;
+  kern<<<dim3(1, B, 2), kQuantThreads, smem, st>>>(pk, pv, ins);
+  return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_LAUNCH;
+}
+
+extern "C" int akv_warm_demote_install(uint8_t* arena, int64_t a_sb, int64_t a_sh, const akv_warm_layout* layout,
+                                       int blk0, uint16_t* k, int64_t k_sb, int64_t k_sh, uint16_t* v, int64_t v_sb,
+                                       int64_t v_sh, const uint16_t* nk, int64_t nk_sb, int64_t nk_sh,
+                                       const uint16_t* nv, int64_t nv_sb, int64_t nv_sh, int B, int H, int* status,
+                                       void* stream) {
+  if (!arena || !layout || !k || !v || !nk || !nv) return AKV_ERR_NULL;
+  if (blk0 < 0) return AKV_ERR_SHAPE;
+  const akv_warm_layout L = *layout;
+  const int D = L.head_dim;
+  uint8_t* base = arena + static_cast<int64_t>(blk0) * L.bytes;
+  const akv_qdest dk = record_qdest(base, a_sb, a_sh, L, true);
+  const akv_qdest dv = record_qdest(base, a_sb, a_sh, L, false);
+  QuantParams pk, pv;
+  QuantPlan lk, lv;
+  int rc = prepare_quant(k, k_sb, k_sh, D, nullptr, 0, 0, B, H, 1, D, L.key_bits, 1, 1, L.n_outlier, &dk, nullptr, 0,
+                         status, pk, lk);
+  if (rc != AKV_OK) return rc;
+  rc = prepare_quant(v, v_sb, v_sh, D, nullptr, 0, 0, B, H, 1, D, L.value_bits, 0, 1, L.n_outlier, &dv, nullptr, 0,
+                     status, pv, lv);
+  if (rc != AKV_OK) return rc;
+  if (lk.chunked || lv.chunked) return AKV_ERR_UNSUPPORTED;  // one token never is
+  InstallRows ins{reinterpret_cast<const __half*>(nk), nk_sb, nk_sh, reinterpret_cast<const __half*>(nv), nv_sb,
+                  nv_sh, 0};
+  ins.vec16 = aligned(nk, 16) && aligned(nv, 16) && nk_sb % 8 == 0 && nk_sh % 8 == 0 && nv_sb % 8 == 0 &&
+              nv_sh % 8 == 0;  // the destinations passed the quantiser's 16-byte checks
+  const size_t smem = std::max(lk.smem, lv.smem);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (L.key_bits * 8 + L.value_bits) {
+    case 18: return launch_demote_install<2, 2>(pk, pv, ins, smem, B, st);
+    case 19: return launch_demote_install<2, 3>(pk, pv, ins, smem, B, st);
+    case 20: return launch_demote_install<2, 4>(pk, pv, ins, smem, B, st);
+    case 26: return launch_demote_install<3, 2>(pk, pv, ins, smem, B, st);
+    case 27: return launch_demote_install<3, 3>(pk, pv, ins, smem, B, st);
+    case 28: return launch_demote_install<3, 4>(pk, pv, ins, smem, B, st);
+    case 34: return launch_demote_install<4, 2>(pk, pv, ins, smem, B, st);
+    case 35: return launch_demote_install<4, 3>(pk, pv, ins, smem, B, st);
+    case 36: return launch_demote_install<4, 4>(pk, pv, ins, smem, B, st);
+    default: return AKV_ERR_BITS;
+  }
 }

@@ -202,6 +202,20 @@ int akv_warm_append(uint8_t* arena, int64_t a_sb, int64_t a_sh, const akv_warm_l
                     const int64_t* tok_idx, int64_t tok_sb, int64_t n_src, int B, int H, int N, int group,
                     void* workspace, size_t workspace_bytes, int* status, void* stream);
 
+/* akv_warm_append of ONE token per batch row (group 1, no index), whose K / V
+ * source rows (k, v: row b at k + b*k_sb, head h at + h*k_sh, D contiguous
+ * halves) are then overwritten by a new token's rows (nk / nv, same layout
+ * with their own strides): one launch for the demote + insert of a decode
+ * step whose hot window is full (the reference's AKVLayer._demote of the
+ * evicted token followed by the new token's torch.cat into the hot tier,
+ * akv/drop_in.py:684-701 and :360-372).  The record written is bit-identical
+ * to akv_warm_append's. */
+int akv_warm_demote_install(uint8_t* arena, int64_t a_sb, int64_t a_sh, const akv_warm_layout* layout, int blk0,
+                            uint16_t* k, int64_t k_sb, int64_t k_sh, uint16_t* v, int64_t v_sb, int64_t v_sh,
+                            const uint16_t* nk, int64_t nk_sb, int64_t nk_sh,
+                            const uint16_t* nv, int64_t nv_sb, int64_t nv_sh, int B, int H,
+                            int* status, void* stream);
+
 /* ------------------------------------------------------------------------
  * A4: unpack + dequantise to fp16.
  * Replaces AffineQuantizer.dequantize_keys/values (akv/affine_quantizer.py:112-124,

@@ -203,3 +203,38 @@ def test_warm_arena_event_mode_and_gather():
     rv = O._dequant(O.quantize_values(hot_v[0][:, idx], 3))
     np.testing.assert_array_equal(_bits16(_np(dk[0])), _bits16(rk))
     np.testing.assert_array_equal(_bits16(_np(dv[0])), _bits16(rv))
+
+
+@pytest.mark.parametrize("kb,vb,frac,B", [(3, 3, 0.0, 1), (4, 2, 0.01, 2), (2, 4, 0.05, 1), (4, 4, 0.02, 3)])
+def test_warm_demote_install_matches_append_then_copy(kb, vb, frac, B):
+    """akv_warm_demote_install: the one-token record equals akv_warm_append's
+    byte for byte, and the source ring row ends up holding the new token."""
+    import ctypes
+    akv = _akv()
+    from akv import _C
+    H, cap, D, r = 4, 96, 128, 37
+    g = torch.Generator(device=DEV).manual_seed(kb * 7 + vb + B)
+    ring = torch.randn(2, B, H, cap, D, generator=g, device=DEV).half()
+    ring[..., 5] *= 12
+    new = torch.randn(2, B, H, 1, D, generator=g, device=DEV).half()
+    a = akv.WarmArena(B, H, D, kb, vb, outlier_fraction=frac, max_blocks=3, device=DEV)
+    b = akv.WarmArena(B, H, D, kb, vb, outlier_fraction=frac, max_blocks=3, device=DEV)
+    for ar in (a, b):  # one ordinary block first, so the records land at blk 1
+        ar.append(ring[0, :, :, :32].contiguous(), ring[1, :, :, :32].contiguous(), group=32)
+    a.append(ring[0, :, :, r:r + 1], ring[1, :, :, r:r + 1], group=1)
+    expect = ring.clone()
+    expect[:, :, :, r] = new[:, :, :, 0]
+    work = ring.clone()
+    st = torch.zeros(1, dtype=torch.int32, device=DEV)
+    kr, vr = work[0, :, :, r], work[1, :, :, r]
+    nk, nv = new[0, :, :, 0], new[1, :, :, 0]
+    rc = _C.load().akv_warm_demote_install(
+        b.buf.data_ptr(), b.buf.stride(0), b.buf.stride(1), ctypes.byref(b.layout), 1,
+        kr.data_ptr(), kr.stride(0), kr.stride(1), vr.data_ptr(), vr.stride(0), vr.stride(1),
+        nk.data_ptr(), nk.stride(0), nk.stride(1), nv.data_ptr(), nv.stride(0), nv.stride(1), B, H,
+        st.data_ptr(), _C.stream_of(work))
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert int(st.item()) == 0
+    assert torch.equal(a.buf[:, :, :2], b.buf[:, :, :2])
+    assert torch.equal(work, expect)
