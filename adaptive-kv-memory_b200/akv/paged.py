@@ -60,12 +60,18 @@ class PagedWarmPool:
         self._free.extend(sorted(pages, reverse=True))
 
     def write(self, k: torch.Tensor, v: torch.Tensor, pages: Sequence[int], group: int = BLOCK,
-              status: Optional[torch.Tensor] = None) -> None:
+              status: Optional[torch.Tensor] = None, tok_idx: Optional[torch.Tensor] = None) -> None:
         """Quantise (1, H, N, D) fp16 K/V (any strides, last dim contiguous)
         into ``pages`` (ceil(N / 32) of them, block j -> pages[j]); ``group``
-        tokens share one K scale (32: one per block)."""
+        tokens share one K scale (32: one per block).  ``tok_idx`` (int64
+        device, n entries): the rows of k / v to take, in that order (the
+        quantiser gathers them; N is then n and k / v's third dim is the
+        source's row count)."""
         _C.require_cuda(k, v)
         _, H, N, D = k.shape
+        n_src = N
+        if tok_idx is not None:
+            N = tok_idx.numel()
         nblk = (N + BLOCK - 1) // BLOCK
         if (H, D) != (self.H, self.D) or len(pages) != nblk or k.shape[0] != 1:
             raise ValueError("K/V shape or page count does not match the pool")
@@ -82,8 +88,10 @@ class PagedWarmPool:
             if x.stride(-1) != 1:
                 x = x.contiguous()
             dest = record_dest(self.layout, base, 0, self.rec, H * self.rec, is_key)
-            _C.quantize(x.data_ptr(), x.stride(0), x.stride(1), x.stride(2), None, 0,
-                        1, H, N, D, bits, is_key, min(group, N), self.n_out, dest, sp, x.device)
+            _C.quantize(x.data_ptr(), x.stride(0), x.stride(1), x.stride(2),
+                        None if tok_idx is None else tok_idx.data_ptr(), 0,
+                        1, H, N, D, bits, is_key, min(group, N), self.n_out, dest, sp, x.device,
+                        n_src=n_src if tok_idx is not None else 0)
         if target is not None:
             idx = torch.tensor(pages, dtype=torch.int64).pin_memory().to(self.device, non_blocking=True)
             self.buf.index_copy_(0, idx, target)

@@ -20,7 +20,12 @@ hot window would exceed ``hot_budget_per_seq``, its oldest tokens after the
 ``initial_tokens_protected`` first ones are demoted, at least
 ``eviction_batch_size`` at a time (as many as the recent-token protection
 allows), quantised into freshly allocated pages with one K scale per
-32-token block.  Warm pages per sequence are bounded by
+32-token block.  The hot rows of a slot are kept in any order (attention
+over them is order-free) with each row's token position on the host: a
+demotion quantises the oldest rows straight from the hot pool (the
+quantiser gathers them by index) and moves only as many of the newest rows
+into the freed rows, so the valid rows stay a prefix; nothing else of the
+window is copied.  The first ``initial_tokens_protected`` rows never move.  Warm pages per sequence are bounded by
 ``warm_budget_per_seq``; this engine has no cold tier (the INT2 cold tier of
 ``akv.tiering`` serves ``AKVCache``), so a sequence that outgrows its warm
 budget raises.  ``AdaptiveKVLLM`` / ``patch_vllm_model_runner`` of the
@@ -33,9 +38,11 @@ import math
 from dataclasses import dataclass
 from typing import Optional, Sequence
 
+import numpy as np
 import torch
 
 from . import _C
+from .fused_attention import KERNEL_HEAD_DIM, prefill_attention
 from .paged import PagedWarmPool, paged_decode_attention
 from .packed_layout import BLOCK
 
@@ -84,6 +91,8 @@ class _LayerState:
         self.hot_k = torch.zeros(S, kv_heads, cfg.hot_budget_per_seq, head_dim, dtype=dtype, device=device)
         self.hot_v = torch.zeros_like(self.hot_k)
         self.hot_len = [0] * S
+        self.row_pos = np.zeros((S, cfg.hot_budget_per_seq), dtype=np.int64)  # token position of each hot row
+        self.seen = [0] * S                      # tokens fed so far (the next position)
         self.pages = [[] for _ in range(S)]      # block table rows (host)
         self.events = [[] for _ in range(S)]     # (first block, tokens) of each demote event
         self.table = torch.zeros(S, self.max_blocks, dtype=torch.int32, device=device)
@@ -98,8 +107,13 @@ class _LayerState:
 
     def reset(self, slot: int) -> None:
         self.pool.release(self.pages[slot])
-        self.pages[slot], self.events[slot], self.hot_len[slot] = [], [], 0
+        self.pages[slot], self.events[slot], self.hot_len[slot], self.seen[slot] = [], [], 0, 0
         self.sync_lengths(slot)
+
+    def chronological(self, slot: int) -> np.ndarray:
+        """The slot's hot rows in token order."""
+        h = self.hot_len[slot]
+        return np.argsort(self.row_pos[slot, :h], kind="stable")
 
 
 class AdaptiveCacheEngine:
@@ -156,7 +170,8 @@ class AdaptiveCacheEngine:
                attention_weights: Optional[torch.Tensor] = None):
         """Append (1, Hkv, N, D) K/V of one sequence at one layer and demote
         beyond the hot budget.  Returns the sequence's hot window (1, Hkv,
-        hot_len, D) K and V; its warm tokens stay packed in the pool."""
+        hot_len, D) K and V, its rows in pool order (not token order); its
+        warm tokens stay packed in the pool."""
         _C.require_cuda(key_states, value_states)
         if seq_id not in self._slot:
             self.allocate(seq_id)
@@ -166,32 +181,63 @@ class AdaptiveCacheEngine:
         h, N = L.hot_len[slot], key_states.shape[2]
         total = h + N
         budget = cfg.hot_budget_per_seq
+        pos0 = L.seen[slot]
+        L.seen[slot] = pos0 + N
         if total <= budget:
             L.hot_k[slot, :, h:total] = key_states[0]
             L.hot_v[slot, :, h:total] = value_states[0]
+            L.row_pos[slot, h:total] = np.arange(pos0, pos0 + N)
             L.hot_len[slot] = total
         else:
             init = min(cfg.initial_tokens_protected, budget)
             movable = max(0, total - init - cfg.recent_tokens_protected)
             n_dem = min(max(total - budget, cfg.eviction_batch_size), max(movable, total - budget))
-            ck = torch.cat([L.hot_k[slot, :, :h], key_states[0]], dim=1)
-            cv = torch.cat([L.hot_v[slot, :, :h], value_states[0]], dim=1)
             nblk = (n_dem + BLOCK - 1) // BLOCK
             if len(L.pages[slot]) + nblk > L.max_blocks:
                 raise RuntimeError(f"sequence {seq_id} exceeds its warm budget of "
                                    f"{cfg.warm_budget_per_seq} tokens at layer {layer_idx}")
             pages = L.pool.alloc(nblk)
-            L.pool.write(ck[None, :, init:init + n_dem], cv[None, :, init:init + n_dem], pages, group=BLOCK)
+            dev = L.hot_k.device
+            if n_dem <= h - init:  # the demoted tokens are all in the window: gather, no copy of it
+                pos = L.row_pos[slot]
+                cand = np.argpartition(pos[init:h], n_dem - 1)[:n_dem] + init if n_dem < h - init \
+                    else np.arange(init, h)
+                dem = cand[np.argsort(pos[cand], kind="stable")]  # the n_dem oldest rows, in token order
+                L.pool.write(L.hot_k[slot:slot + 1], L.hot_v[slot:slot + 1], pages, group=BLOCK,
+                             tok_idx=_pinned(dem.tolist(), torch.int64).to(dev, non_blocking=True))
+                new_h = h - n_dem
+                is_dem = np.zeros(h, dtype=bool)
+                is_dem[dem] = True
+                holes = dem[dem < new_h]
+                movers = np.nonzero(~is_dem[new_h:h])[0] + new_h
+                if holes.size:
+                    both = _pinned(np.concatenate([movers, holes]).tolist(), torch.int64).to(dev, non_blocking=True)
+                    src, dst = both[:holes.size], both[holes.size:]
+                    for buf in (L.hot_k, L.hot_v):
+                        buf[slot].index_copy_(1, dst, buf[slot].index_select(1, src))
+                    pos[holes] = pos[movers]
+                L.hot_k[slot, :, new_h:new_h + N] = key_states[0]
+                L.hot_v[slot, :, new_h:new_h + N] = value_states[0]
+                pos[new_h:new_h + N] = np.arange(pos0, pos0 + N)
+                L.hot_len[slot] = new_h + N
+            else:  # a prompt chunk longer than the window: some new tokens go straight to the warm tier
+                order = _pinned(L.chronological(slot).tolist(), torch.int64).to(dev, non_blocking=True)
+                ck = torch.cat([L.hot_k[slot, :, :h].index_select(1, order), key_states[0]], dim=1)
+                cv = torch.cat([L.hot_v[slot, :, :h].index_select(1, order), value_states[0]], dim=1)
+                cpos = np.concatenate([np.sort(L.row_pos[slot, :h]), np.arange(pos0, pos0 + N)])
+                L.pool.write(ck[None, :, init:init + n_dem], cv[None, :, init:init + n_dem], pages, group=BLOCK)
+                keep = total - n_dem
+                L.hot_k[slot, :, :init] = ck[:, :init]
+                L.hot_v[slot, :, :init] = cv[:, :init]
+                L.hot_k[slot, :, init:keep] = ck[:, init + n_dem:]
+                L.hot_v[slot, :, init:keep] = cv[:, init + n_dem:]
+                L.row_pos[slot, :init] = cpos[:init]
+                L.row_pos[slot, init:keep] = cpos[init + n_dem:]
+                L.hot_len[slot] = keep
             first = len(L.pages[slot])
             L.table[slot, first:first + nblk].copy_(_pinned(pages, torch.int32), non_blocking=True)
             L.pages[slot].extend(pages)
             L.events[slot].append((first, n_dem))
-            keep = total - n_dem
-            L.hot_k[slot, :, :init] = ck[:, :init]
-            L.hot_v[slot, :, :init] = cv[:, :init]
-            L.hot_k[slot, :, init:keep] = ck[:, init + n_dem:]
-            L.hot_v[slot, :, init:keep] = cv[:, init + n_dem:]
-            L.hot_len[slot] = keep
             self._total_migrations += 1
         L.sync_lengths(slot)
         return L.hot_k[slot:slot + 1, :, :L.hot_len[slot]], L.hot_v[slot:slot + 1, :, :L.hot_len[slot]]
@@ -205,14 +251,16 @@ class AdaptiveCacheEngine:
         L = self._layers[layer_idx]
         init = min(self.config.initial_tokens_protected, self.config.hot_budget_per_seq)
         hl = L.hot_len[slot]
-        ks, vs = [L.hot_k[slot:slot + 1, :, :min(init, hl)]], [L.hot_v[slot:slot + 1, :, :min(init, hl)]]
+        order = torch.from_numpy(L.chronological(slot)).to(L.hot_k.device)
+        hk, hv = L.hot_k[slot:slot + 1].index_select(2, order), L.hot_v[slot:slot + 1].index_select(2, order)
+        ks, vs = [hk[:, :, :min(init, hl)]], [hv[:, :, :min(init, hl)]]
         for first, n in L.events[slot]:
             nb = (n + BLOCK - 1) // BLOCK
             k, v = L.pool.dequantize(L.pages[slot][first:first + nb], n_tokens=n)
             ks.append(k)
             vs.append(v)
-        ks.append(L.hot_k[slot:slot + 1, :, min(init, hl):hl])
-        vs.append(L.hot_v[slot:slot + 1, :, min(init, hl):hl])
+        ks.append(hk[:, :, min(init, hl):hl])
+        vs.append(hv[:, :, min(init, hl):hl])
         return torch.cat(ks, 2), torch.cat(vs, 2)
 
     # ------------------------------------------------------------------ accounting
@@ -264,13 +312,20 @@ class AdaptiveAttentionBackend:
                 sm_scale: Optional[float] = None) -> torch.Tensor:
         """Reference signature: query (1, Hq, M, D) -> (1, Hq, M, D).  M = 1
         runs the paged decode kernel; M > 1 attends every query over the
-        sequence's full K/V without a mask, as the reference's fallback does."""
+        sequence's full K/V without a mask, as the reference's fallback does
+        (vllm_integration.py:331-343): the tcgen05 prefill kernel with every
+        key visible to every query at head dim 128, else fp32 torch."""
         eng = self.cache_engine
         if eng.get_cache(seq_id) is None:
             raise ValueError(f"No cache for seq_id={seq_id}")
         if query.shape[2] == 1:
             return self.forward_batch(query[:, :, 0], [seq_id], layer_idx, sm_scale).unsqueeze(2)
         k, v = eng.get_kv_for_attention(seq_id, layer_idx)
+        if query.shape[-1] == KERNEL_HEAD_DIM and query.dtype == torch.float16:
+            M, T = query.shape[2], k.shape[2]
+            q_pos = torch.full((M,), T, dtype=torch.int32, device=query.device)  # sees keys 0 .. T
+            k_pos = torch.arange(T, dtype=torch.int32, device=query.device)
+            return prefill_attention(query, q_pos, k, v, k_pos, sm_scale=sm_scale)
         g = query.shape[1] // k.shape[1]
         k, v = k.repeat_interleave(g, dim=1), v.repeat_interleave(g, dim=1)
         if sm_scale is None:

@@ -158,7 +158,7 @@ def test_engine_batched_decode_and_slot_reuse():
             k, v = _kv(g, (1, 2, n, 128)), _kv(g, (1, 2, n, 128))
             eng.update(s, k, v, layer)
             feeds[(s, layer)] = [k]
-    for _ in range(5):
+    for _ in range(150):  # two or three demotions per sequence with the rows out of token order
         for s in (10, 11, 12):
             for layer in range(2):
                 k, v = _kv(g, (1, 2, 1, 128)), _kv(g, (1, 2, 1, 128))
@@ -197,6 +197,11 @@ def test_engine_batched_decode_and_slot_reuse():
     q1 = torch.randn(1, 8, 1, 128, generator=g, device=DEV).half()
     assert backend.forward(q1, 20, 0).shape == (1, 8, 1, 128)
     q4 = torch.randn(1, 8, 4, 128, generator=g, device=DEV).half()
-    assert backend.forward(q4, 20, 1).shape == (1, 8, 4, 128)
+    o4 = backend.forward(q4, 20, 1)
+    assert o4.shape == (1, 8, 4, 128)
+    k, v = eng.get_kv_for_attention(20, 1)  # M > 1: every query over every key, no mask
+    K, V = k.float().repeat_interleave(4, 1), v.float().repeat_interleave(4, 1)
+    ref = torch.softmax(q4.float() @ K.transpose(-2, -1) / 128 ** 0.5, -1) @ V
+    assert (o4.float() - ref).abs().max().item() <= 2e-3
     with pytest.raises(ValueError):
         backend.forward(q1, 99, 0)
