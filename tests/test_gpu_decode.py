@@ -292,6 +292,38 @@ def test_few_units_long_context():
     assert err <= ATOL
 
 
+def test_config5a_full_shape():
+    """Config 5a at its full shape (B32, 64 Q / 8 KV heads, 61,440 warm k4v4
+    tokens + 4,096 hot, ~10 GB of fp16 inputs): every row against fp32
+    attention over the arena's dequantised tiers (GQA groups, no repeat)."""
+    import akv
+    B, Hq, Hkv, D, nw, nh = 32, 64, 8, 128, 61440, 4096
+    g = torch.Generator(device=DEV).manual_seed(5)
+    arena = akv.WarmArena(B, Hkv, D, 4, 4, 0.0, max_blocks=nw // 32, device=DEV)
+    wk = torch.randn(B, Hkv, nw, D, generator=g, device=DEV).half()
+    wv = torch.randn(B, Hkv, nw, D, generator=g, device=DEV).half()
+    arena.append(wk, wv, group=32)
+    del wk, wv
+    hk = torch.randn(B, Hkv, nh, D, generator=g, device=DEV).half()
+    hv = torch.randn(B, Hkv, nh, D, generator=g, device=DEV).half()
+    q = torch.randn(B, Hq, D, generator=g, device=DEV).half()
+    out = akv.mixed_tier_decode_attention(q, hk, hv, arena).float()
+    gq = Hq // Hkv
+    worst = 0.0
+    kd, vd = arena.dequantize()
+    for b in range(B):
+        K = torch.cat([kd[b], hk[b]], 1).float()  # (Hkv, N, D)
+        V = torch.cat([vd[b], hv[b]], 1).float()
+        qb = q[b].float().view(Hkv, gq, D)
+        p = torch.softmax(torch.einsum("hgd,hnd->hgn", qb, K) / D ** 0.5, -1)
+        ref = torch.einsum("hgn,hnd->hgd", p, V).reshape(Hq, D)
+        worst = max(worst, (out[b] - ref).abs().max().item())
+    print(f"[decode err] config 5a full shape: {worst:.3e}")
+    assert worst <= ATOL
+    del arena, kd, vd
+    torch.cuda.empty_cache()
+
+
 # ---------------------------------------------------------------------------- head dims 64 and 256
 @pytest.mark.parametrize("D", [64, 256])
 @pytest.mark.parametrize("kb,vb", [(2, 2), (3, 3), (4, 4), (4, 2), (2, 3), (3, 4)])
