@@ -67,20 +67,22 @@ struct TorchCascade {
 };
 
 // torch-order sum of the BH rows of one column (row stride rs).  Rows are
-// loaded eight at a time so a thread keeps several loads in flight while the
-// additions keep their order; ILP selects the four-interleaved-cascade form.
+// loaded kRowsInFlight at a time so a thread keeps several loads in flight
+// while the additions keep their order; ILP selects the four-interleaved-
+// cascade form.
+constexpr int kRowsInFlight = 16;
 template <bool ILP>
 AKV_DEV float bh_column_sum(const float* __restrict__ col, int64_t rs, int BH) {
   if constexpr (!ILP) {
     TorchCascade c;
     c.init(BH);
     int bh = 0;
-    for (; bh + 8 <= BH; bh += 8) {
-      float v[8];
+    for (; bh + kRowsInFlight <= BH; bh += kRowsInFlight) {
+      float v[kRowsInFlight];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = __ldg(col + (bh + j) * rs);
+      for (int j = 0; j < kRowsInFlight; ++j) v[j] = __ldg(col + (bh + j) * rs);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) c.push(v[j]);
+      for (int j = 0; j < kRowsInFlight; ++j) c.push(v[j]);
     }
     for (; bh < BH; ++bh) c.push(__ldg(col + bh * rs));
     return c.result();
@@ -92,25 +94,23 @@ AKV_DEV float bh_column_sum(const float* __restrict__ col, int64_t rs, int BH) {
     c3.init(BH / 4);
     const int full = BH / 4 * 4;
     int bh = 0;
-    for (; bh + 8 <= full; bh += 8) {
-      float v[8];
+    for (; bh + kRowsInFlight <= full; bh += kRowsInFlight) {
+      float v[kRowsInFlight];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = __ldg(col + (bh + j) * rs);
-      c0.push(v[0]);
-      c1.push(v[1]);
-      c2.push(v[2]);
-      c3.push(v[3]);
-      c0.push(v[4]);
-      c1.push(v[5]);
-      c2.push(v[6]);
-      c3.push(v[7]);
+      for (int j = 0; j < kRowsInFlight; ++j) v[j] = __ldg(col + (bh + j) * rs);
+#pragma unroll
+      for (int j = 0; j < kRowsInFlight; j += 4) {
+        c0.push(v[j]);
+        c1.push(v[j + 1]);
+        c2.push(v[j + 2]);
+        c3.push(v[j + 3]);
+      }
     }
-    if (bh < full) {  // one group of four left
+    for (; bh + 4 <= full; bh += 4) {  // groups of four left
       c0.push(__ldg(col + bh * rs));
       c1.push(__ldg(col + (bh + 1) * rs));
       c2.push(__ldg(col + (bh + 2) * rs));
       c3.push(__ldg(col + (bh + 3) * rs));
-      bh += 4;
     }
     float s = c0.result();
     for (; bh < BH; ++bh) s = __fadd_rn(s, __ldg(col + bh * rs));  // the last BH % 4 rows go into cascade 0
