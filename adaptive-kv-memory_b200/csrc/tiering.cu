@@ -193,10 +193,21 @@ __global__ void migrator_update_kernel(const float* __restrict__ attn, int B, in
   if (imp > 0.01f) access[n] = step;
 }
 
+// Order-preserving u32 key of a float and back (for max / min by integer
+// atomics); a min is kept as the max of the complemented key, so zeroed words
+// are the identity of all three reductions.
+AKV_DEV uint32_t mig_key(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+AKV_DEV float mig_unkey(uint32_t k) { return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k); }
+
 // compute_importance (:175-219), step 1: max of scores, min of last access,
-// max of retrieval over [0, N) -> red[0..2] (one CTA)
+// max of retrieval over [0, N) -> red[0..2] as keys (zeroed before the
+// launch); every CTA reduces a grid-stride share, then folds it in with one
+// atomic per quantity (max and min do not depend on the order)
 __global__ void migrator_reduce_kernel(const float* __restrict__ scores, const int64_t* __restrict__ access,
-                                       const float* __restrict__ retrieval, int N, float* red) {
+                                       const float* __restrict__ retrieval, int N, uint32_t* red) {
   __shared__ float smax[32], rmax[32];
   __shared__ float amin[32];
   float a = -INFINITY, r = -INFINITY, t = INFINITY;
@@ -208,7 +219,7 @@ __global__ void migrator_reduce_kernel(const float* __restrict__ scores, const i
   int done = 0;
   if (vec) {
     const int ng = N / 4;
-    for (int g = threadIdx.x; g < ng; g += blockDim.x) {
+    for (int g = blockIdx.x * blockDim.x + threadIdx.x; g < ng; g += gridDim.x * blockDim.x) {
       const float4 sv = __ldg(reinterpret_cast<const float4*>(scores) + g);
       const float4 rv = __ldg(reinterpret_cast<const float4*>(retrieval) + g);
       const longlong2 a0 = __ldg(reinterpret_cast<const longlong2*>(access) + 2 * g);
@@ -220,7 +231,7 @@ __global__ void migrator_reduce_kernel(const float* __restrict__ scores, const i
     }
     done = 4 * ng;
   }
-  for (int i = done + threadIdx.x; i < N; i += blockDim.x) {
+  for (int i = done + blockIdx.x * blockDim.x + threadIdx.x; i < N; i += gridDim.x * blockDim.x) {
     a = fmaxf(a, scores[i]);
     r = fmaxf(r, retrieval[i]);
     t = fminf(t, static_cast<float>(access[i]));  // access.float().min()
@@ -248,9 +259,9 @@ __global__ void migrator_reduce_kernel(const float* __restrict__ scores, const i
       t = fminf(t, __shfl_xor_sync(0xffffffffu, t, o));
     }
     if (lane == 0) {
-      red[0] = a;
-      red[1] = t;
-      red[2] = r;
+      atomicMax(red, mig_key(a));
+      atomicMax(red + 1, ~mig_key(t));
+      atomicMax(red + 2, mig_key(r));
     }
   }
 }
@@ -259,11 +270,11 @@ __global__ void migrator_reduce_kernel(const float* __restrict__ scores, const i
 // rounded like torch's, protected ends at +inf
 __global__ void migrator_importance_kernel(const float* __restrict__ scores, const int64_t* __restrict__ access,
                                            const float* __restrict__ retrieval, int N, int64_t step,
-                                           const float* __restrict__ red, float w_a, float w_r, float w_t,
+                                           const uint32_t* __restrict__ red, float w_a, float w_r, float w_t,
                                            int n_first, int n_last, float* __restrict__ out) {
   const int n = blockIdx.x * blockDim.x + threadIdx.x;
   if (n >= N) return;
-  const float smax = red[0], amin = red[1], rmax = red[2];
+  const float smax = mig_unkey(red[0]), amin = mig_unkey(~red[1]), rmax = mig_unkey(red[2]);
   const float attn_norm = __fdiv_rn(scores[n], fmaxf(smax, 1e-10f));
   // max(1.0, step - access.min()) is Python double arithmetic, then a float32 divisor
   const double den = fmax(1.0, static_cast<double>(step) - static_cast<double>(amin));
@@ -285,18 +296,19 @@ __global__ void migrator_importance_kernel(const float* __restrict__ scores, con
 // over the whole GPU (no CTA waits on another):
 //   per pass: sel_hist_kernel (per-CTA shared histograms of the keys that
 //   match the prefix so far, lanes of a warp that hit one bin adding with a
-//   single atomic, then added into the pass's global histogram) and
-//   sel_pick_kernel (one CTA: the bin holding the k-th key extends the prefix);
-//   then sel_count_kernel (per-CTA counts of keys below / equal to the
-//   threshold) and sel_compact_kernel (each CTA places its contiguous slice
-//   after the lower CTAs' counts and writes it in index order).
-// Workspace (u32): hist[4][256] (zeroed first), state {prefix, mask,
-// remaining}, counts[grid][2].
+//   single atomic, then added into the pass's global histogram; the last CTA
+//   to arrive scans that histogram and extends the prefix by the byte of the
+//   k-th key); then sel_count_kernel (per-CTA counts of keys below / equal to
+//   the threshold) and sel_compact_kernel (each CTA places its contiguous
+//   slice after the lower CTAs' counts and writes it in index order).
+// Workspace (u32): hist[4][256] and the per-pass arrival counters done[4]
+// (zeroed first), state {prefix, mask, remaining}, counts[grid][2].
 // ---------------------------------------------------------------------------
 constexpr int kSelThreads = 256;
 constexpr int kSelWarps = kSelThreads / 32;
 constexpr int kSelMaxCtas = 2 * 148;
-constexpr size_t kSelWsWords = 4 * 256 + 4 + 2 * kSelMaxCtas;
+constexpr size_t kSelWsWords = 4 * 256 + 4 + 4 + 2 * kSelMaxCtas;
+constexpr size_t kSelZeroWords = 4 * 256 + 4;  // histograms and per-pass arrival counters, zeroed per call
 
 AKV_DEV uint32_t order_key(float f) {
   uint32_t u = __float_as_uint(f);
@@ -335,8 +347,51 @@ struct SelArgs {
 };
 
 AKV_DEV uint32_t* sel_hist(const SelArgs& a, int pass) { return a.ws + pass * 256; }
-AKV_DEV uint32_t* sel_state(const SelArgs& a) { return a.ws + 4 * 256; }
-AKV_DEV uint32_t* sel_counts(const SelArgs& a) { return a.ws + 4 * 256 + 4; }
+AKV_DEV uint32_t* sel_done(const SelArgs& a) { return a.ws + 4 * 256; }
+AKV_DEV uint32_t* sel_state(const SelArgs& a) { return a.ws + 4 * 256 + 4; }
+AKV_DEV uint32_t* sel_counts(const SelArgs& a) { return a.ws + 4 * 256 + 8; }
+
+// The whole CTA (256 threads, one bin each): the bin holding the rem-th
+// smallest key of this pass is the first whose inclusive count reaches rem
+// (bin 255 if none of the first 255 does), found with a block-wide scan of
+// the histogram; the threshold state moves on by one byte.
+AKV_DEV void sel_pick(const SelArgs& a, int pass) {
+  static_assert(kSelThreads == 256, "one thread per histogram bin");
+  __shared__ uint32_t wsum[8];
+  __shared__ uint32_t s_bin, s_below;
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  uint32_t* st = sel_state(a);
+  const uint32_t prefix = pass ? __ldcg(st) : 0u, mask = pass ? __ldcg(st + 1) : 0u;
+  const uint32_t rem = pass ? __ldcg(st + 2) : static_cast<uint32_t>(a.k);
+  const uint32_t v = __ldcg(sel_hist(a, pass) + tid);
+  uint32_t x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) wsum[w] = x;
+  __syncthreads();
+  uint32_t off = 0;
+  for (int i = 0; i < w; ++i) off += wsum[i];
+  const uint32_t incl = x + off, excl = incl - v;
+  if (tid == 255) {  // the fallback: bin 255 after everything below it
+    s_bin = 255u;
+    s_below = excl;
+  }
+  __syncthreads();
+  if (tid < 255 && excl < rem && incl >= rem) {  // exactly one bin, the first reaching rem
+    s_bin = static_cast<uint32_t>(tid);
+    s_below = excl;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    const int shift = 24 - 8 * pass;
+    st[0] = prefix | (s_bin << shift);
+    st[1] = mask | (255u << shift);
+    st[2] = rem - s_below;
+  }
+}
 
 __global__ void __launch_bounds__(kSelThreads) sel_hist_kernel(const SelArgs a, int pass) {
   __shared__ uint32_t hist[256];
@@ -364,24 +419,16 @@ __global__ void __launch_bounds__(kSelThreads) sel_hist_kernel(const SelArgs a, 
   __syncthreads();
   const uint32_t c = hist[tid];
   if (c) atomicAdd(&sel_hist(a, pass)[tid], c);
-}
-
-__global__ void sel_pick_kernel(const SelArgs a, int pass) {
-  if (threadIdx.x != 0) return;
-  uint32_t* st = sel_state(a);
-  const uint32_t prefix = pass ? st[0] : 0u, mask = pass ? st[1] : 0u;
-  const uint32_t rem = pass ? st[2] : static_cast<uint32_t>(a.k);
-  const uint32_t* h = sel_hist(a, pass);
-  const int shift = 24 - 8 * pass;
-  uint32_t acc = 0;
-  int bin = 0;
-  for (; bin < 255; ++bin) {
-    if (acc + h[bin] >= rem) break;
-    acc += h[bin];
+  // the last CTA to finish the pass picks the next threshold byte
+  __threadfence();
+  __syncthreads();
+  __shared__ bool last;
+  if (tid == 0) last = atomicAdd(sel_done(a) + pass, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (last) {
+    __threadfence();
+    sel_pick(a, pass);
   }
-  st[0] = prefix | (static_cast<uint32_t>(bin) << shift);
-  st[1] = mask | (255u << shift);
-  st[2] = rem - acc;
 }
 
 // keys below / equal to the threshold in this CTA's slice
@@ -669,11 +716,8 @@ extern "C" int akv_select_bottomk(const float* scores, int n, int k, int protect
   const int grid = (a.ng + a.per_cta - 1) / a.per_cta;
   a.ws = static_cast<uint32_t*>(workspace);
   a.out = idx_out;
-  if (cudaMemsetAsync(workspace, 0, 4 * 256 * sizeof(uint32_t), st) != cudaSuccess) return AKV_ERR_LAUNCH;
-  for (int pass = 0; pass < 4; ++pass) {
-    sel_hist_kernel<<<grid, kSelThreads, 0, st>>>(a, pass);
-    sel_pick_kernel<<<1, 32, 0, st>>>(a, pass);
-  }
+  if (cudaMemsetAsync(workspace, 0, kSelZeroWords * sizeof(uint32_t), st) != cudaSuccess) return AKV_ERR_LAUNCH;
+  for (int pass = 0; pass < 4; ++pass) sel_hist_kernel<<<grid, kSelThreads, 0, st>>>(a, pass);
   sel_count_kernel<<<grid, kSelThreads, 0, st>>>(a);
   sel_compact_kernel<<<grid, kSelThreads, 0, st>>>(a);
   return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_LAUNCH;
@@ -758,8 +802,10 @@ extern "C" int akv_migrator_importance(const float* scores, const int64_t* last_
   if (N == 0) return AKV_OK;
   if (!workspace || workspace_bytes < 16) return AKV_ERR_WORKSPACE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  float* red = static_cast<float*>(workspace);
-  migrator_reduce_kernel<<<1, 1024, 0, st>>>(scores, last_access, retrieval, N, red);
+  uint32_t* red = static_cast<uint32_t*>(workspace);
+  if (cudaMemsetAsync(red, 0, 3 * sizeof(uint32_t), st) != cudaSuccess) return AKV_ERR_LAUNCH;
+  const int ctas = std::max(1, std::min(2 * 148, (N + 4 * 1024 - 1) / (4 * 1024)));
+  migrator_reduce_kernel<<<ctas, 1024, 0, st>>>(scores, last_access, retrieval, N, red);
   migrator_importance_kernel<<<(N + 255) / 256, 256, 0, st>>>(scores, last_access, retrieval, N, step, red, w_attn,
                                                                w_recency, w_retrieval, std::min(protect_first, N),
                                                                std::min(protect_last, N), out);
