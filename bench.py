@@ -310,6 +310,45 @@ DECODE_SHAPES = {
 }
 
 
+def host_call_bench(torch, akv, dev, calls: int = 300) -> dict:
+    """Host time per eager decode call (config 1's shape, B1, 12/2 heads,
+    3,584 warm k3v3 + 512 hot): the enqueue loop is timed on the host with no
+    synchronize inside (the launch queue does not fill), so the figure is the
+    Python + ctypes + launch cost of one call, not device time.  Two entry
+    points: the public mixed_tier_decode_attention (argument checks, a cached
+    workspace, one akv_mixed_decode call) and AKVLayer's cached argument
+    struct (akv_mixed_decode_args), the HF hook's path."""
+    import time
+    from akv.drop_in import AKVLayer
+    gen = torch.Generator(device=dev).manual_seed(3)
+    B, Hq, Hkv, D, n_hot, n_warm = 1, 12, 2, 128, 512, 3584
+    arena = akv.WarmArena(B, Hkv, D, 3, 3, 0.0, max_blocks=n_warm // 32, device=dev)
+    arena.append(make_kv(torch, gen, (B, Hkv, n_warm, D), dev), make_kv(torch, gen, (B, Hkv, n_warm, D), dev),
+                 group=32)
+    hk = make_kv(torch, gen, (B, Hkv, n_hot, D), dev)
+    hv = make_kv(torch, gen, (B, Hkv, n_hot, D), dev)
+    q = torch.randn(B, Hq, 1, D, generator=gen, device=dev).half()
+    layer = AKVLayer(warm_bits=3, hot_budget=n_hot, enable_promotion=False, enable_promotion_proxy=False,
+                     fused_decode=True)
+    layer.update(make_kv(torch, gen, (B, Hkv, n_hot + n_warm, D), dev),
+                 make_kv(torch, gen, (B, Hkv, n_hot + n_warm, D), dev))  # a prompt: 512 hot, the rest demoted
+
+    def per_call(fn):
+        for _ in range(20):
+            fn()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(calls):
+            fn()
+        t1 = time.perf_counter()
+        torch.cuda.synchronize()
+        return round((t1 - t0) / calls * 1e6, 2)
+
+    return {"workload": "config 1 shape, eager calls, host enqueue time per call",
+            "mixed_tier_decode_attention_us": per_call(lambda: akv.mixed_tier_decode_attention(q, hk, hv, arena)),
+            "akv_layer_decode_attention_us": per_call(lambda: layer.decode_attention(q, reuse_out=True))}
+
+
 def decode_shapes_bench(torch, akv, dev, reps: int = 20) -> dict:
     """Per-layer device time of one decode launch (decode + combine) at the
     other configurations' shapes.  Each shape cycles through enough layer copies
@@ -1056,6 +1095,7 @@ def run_ours(args):
             torch.cuda.empty_cache()
         if world == 1 and not args.no_shapes:
             res["decode_shapes"] = decode_shapes_bench(torch, akv, dev)
+            res["host_call"] = host_call_bench(torch, akv, dev)
             res["paged_decode"] = paged_bench(torch, akv, dev)
         if world == 1 and args.hf_tokens > 0:
             res["hf_decode"] = hf_decode_bench(torch, akv, dev, new_tokens=args.hf_tokens)
